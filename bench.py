@@ -1,0 +1,538 @@
+#!/usr/bin/env python
+"""IVF search throughput on B200: QPS at recall@10 >= 0.95 (dim 1024) and the
+list scan's HBM bandwidth.
+
+Workload (one step = one search batch): 1M fp32 unit-norm vectors, dim 1024,
+from a 1,000-component Gaussian mixture (component means N(0, I) normalised,
+per-point noise sigma = 0.3 in norm, renormalised; seeded synthetic data, no
+dataset), inner-product metric, nlist = 4096 lists trained by k-means on the
+GPU (10 iterations, seeded random init), nprobe = 32, k = 10, 10 batches of
+1,024 queries from the same mixture, one batch per step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (under torchrun): the lists are partitioned over the ranks (largest
+first onto the least-loaded rank); every rank holds all centroids, scans only
+its own lists for the same query batch, the per-rank top-k go through one NCCL
+all-gather, and the engine's merge kernel forms the answer.
+
+--impl reference times the reference's own CPU implementation of the path
+(IVFIndex::search_nprobe built from its sources, oracle/_ref) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_VEC = 1_000_000
+DIM = 1024
+NCOMP = 1000
+SIGMA = 0.3
+NLIST = 4096
+NPROBE = 32
+K = 10
+BATCH = 1024
+NBATCH = 10
+KMEANS_ITERS = 10
+SEED = 0
+METRIC_IP = 1
+WORKLOAD = (f"ivf-search: {N_VEC // 1_000_000}M x {DIM} fp32 unit-norm mixture({NCOMP}), "
+            f"IP, nlist {NLIST}, nprobe {NPROBE}, k {K}, batch {BATCH}")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def make_data():
+    from m3_memory_b200 import synthetic as S
+
+    rng = np.random.default_rng(SEED)
+    means = S.mixture_means(NCOMP, DIM, rng)
+    X, _ = S.gaussian_mixture(N_VEC, means, SIGMA, rng)
+    Q, _ = S.gaussian_mixture(BATCH * NBATCH, means, SIGMA, rng)
+    return X, Q.reshape(NBATCH, BATCH, DIM)
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: str):
+        self.gpu = gpu
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", self.gpu], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.f.flush()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in Path(self.f.name).read_text().splitlines():
+                p = [x.strip() for x in line.split(",")]
+                if len(p) >= 9:
+                    rows.append(p)
+        finally:
+            os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def gpu_selector(dev):
+    import torch
+
+    try:
+        u = torch.cuda.get_device_properties(dev).uuid
+        return "GPU-" + str(u)
+    except Exception:
+        return str(dev)
+
+
+# ---------------------------------------------------------------- helpers
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def scan_traffic_per_launch():
+    """dram bytes of one scan launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "list_scan_traffic.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return d.get("dram_bytes_per_launch")
+    return None
+
+
+def exact_topk_ip(X_dev, Q_dev, k):
+    """Exact top-k by inner product (fp32 matmul, TF32 off), chunked over X."""
+    import torch
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    best_s = best_i = None
+    step = 1 << 17
+    for b in range(0, X_dev.shape[0], step):
+        s = Q_dev @ X_dev[b:b + step].T
+        v, i = torch.topk(s, k, dim=1)
+        i = i + b
+        if best_s is None:
+            best_s, best_i = v, i
+        else:
+            cs, ci = torch.cat([best_s, v], 1), torch.cat([best_i, i], 1)
+            best_s, o = torch.topk(cs, k, dim=1)
+            best_i = torch.gather(ci, 1, o)
+    return best_i
+
+
+def recall_at_k(found_ids, exact_ids, k):
+    hit = 0
+    for a, b in zip(found_ids, exact_ids):
+        hit += len(set(a[:k].tolist()) & set(b[:k].tolist()))
+    return hit / (len(found_ids) * k)
+
+
+def shard_lists(sizes, world):
+    """Greedy balancing: largest list first onto the least-loaded rank."""
+    load = [0] * world
+    owner = np.empty(len(sizes), np.int32)
+    for l in np.argsort(-np.asarray(sizes), kind="stable"):
+        r = int(np.argmin(load))
+        owner[l] = r
+        load[r] += int(sizes[l])
+    return owner
+
+
+def cpu_reference_qps(C, X, assign, Q_all, threads, target_s=12.0, warm_q=None):
+    """The reference core's IVFIndex::search_nprobe on the host: returns
+    (qps, sample description)."""
+    from oracle import oracle as O
+
+    ref = O.RefIndex(DIM, METRIC_IP, False)
+    ref.set_centroids(C)
+    order = np.argsort(assign, kind="stable")
+    bounds = np.searchsorted(assign[order], np.arange(NLIST + 1))
+    ids = np.arange(len(X), dtype=np.int64)
+    for c in range(NLIST):
+        b, e = bounds[c], bounds[c + 1]
+        if e > b:
+            rows = order[b:e]
+            ref.rebuild_cluster(c, ids[rows], X[rows])
+    Qf = Q_all.reshape(-1, DIM)
+    probe = Qf[: max(threads, 1) * 2]
+    t0 = time.perf_counter()
+    ref.search_nprobe(probe, K, NPROBE, threads=threads)
+    rate = len(probe) / max(time.perf_counter() - t0, 1e-6)
+    n = int(min(len(Qf), max(threads, rate * target_s)))
+    t0 = time.perf_counter()
+    ref.search_nprobe(Qf[:n], K, NPROBE, threads=threads)
+    dt = time.perf_counter() - t0
+    return n / dt, f"{n} of the {len(Qf)} queries, search_nprobe split over {threads} threads"
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    if not O.have_ref():
+        try:
+            O.build(ref=None)
+        except Exception:
+            pass
+    if not O.have_ref():
+        print(json.dumps({"impl": "reference",
+                          "unavailable": "oracle/_ref/liboracle_ref.so (the reference core) "
+                                         "was not built on this box"}))
+        return
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    X, Qb = make_data()
+    # Index for the reference arm, built on the host without the GPU engine:
+    # k-means init rows (the same seeded sampler), 2 Lloyd rounds with BLAS.
+    C = X[O.sample_rows(SEED, N_VEC, NLIST)].copy()
+    step = 1 << 16
+
+    def assign_of(C):
+        a = np.empty(N_VEC, np.int32)
+        for b in range(0, N_VEC, step):
+            a[b:b + step] = np.argmax(X[b:b + step] @ C.T, axis=1)
+        return a
+
+    from scipy import sparse
+
+    for _ in range(2):
+        a = assign_of(C)
+        onehot = sparse.csr_matrix((np.ones(N_VEC, np.float32), (a, np.arange(N_VEC))),
+                                   shape=(NLIST, N_VEC))
+        sums = np.asarray(onehot @ X)
+        cnt = np.bincount(a, minlength=NLIST)
+        nz = cnt > 0
+        C[nz] = (sums[nz] / cnt[nz, None]).astype(np.float32)
+    a = assign_of(C)
+    ref = O.RefIndex(DIM, METRIC_IP, False)
+    ref.set_centroids(C)
+    order = np.argsort(a, kind="stable")
+    bounds = np.searchsorted(a[order], np.arange(NLIST + 1))
+    ids = np.arange(N_VEC, dtype=np.int64)
+    for c in range(NLIST):
+        b, e = bounds[c], bounds[c + 1]
+        if e > b:
+            rows = order[b:e]
+            ref.rebuild_cluster(c, ids[rows], X[rows])
+    Qf = Qb.reshape(-1, DIM)
+    per_step = max(threads * 4, 16)
+    pos = 0
+
+    def one_step():
+        nonlocal pos
+        q = np.take(Qf, np.arange(pos, pos + per_step) % len(Qf), axis=0)
+        pos += per_step
+        ref.search_nprobe(q, K, NPROBE, threads=threads)
+
+    for _ in range(args.warmup):
+        one_step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_step()
+    dt = time.perf_counter() - t0
+    qps = per_step * args.steps / dt
+    sample = f"{per_step} queries per step over {threads} host threads"
+    print(json.dumps({
+        "impl": "reference", "metric": "search QPS at recall@10>=0.95 (IVF, dim 1024)",
+        "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "nq_per_step": per_step,
+                   "index": "host k-means (2 Lloyd rounds, BLAS) -- setup only"},
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads,
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from m3_memory_b200 import cabi
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    t_setup = time.perf_counter()
+    X, Qb = make_data()
+    log(f"[rank {rank}] data ready in {time.perf_counter() - t_setup:.1f}s")
+    eng = cabi.Engine()
+    ids = np.arange(N_VEC, dtype=np.int64)
+    t0 = time.perf_counter()
+    C, assign = eng.kmeans(X, NLIST, KMEANS_ITERS, SEED, METRIC_IP, False)
+    log(f"[rank {rank}] k-means {KMEANS_ITERS} it on the GPU: {time.perf_counter() - t0:.1f}s")
+    sizes = np.bincount(assign, minlength=NLIST)
+    owner = shard_lists(sizes, world) if world > 1 else np.zeros(NLIST, np.int32)
+    eng.create_ivf(1, DIM, METRIC_IP, False, C)
+    order = np.argsort(assign, kind="stable")
+    bounds = np.searchsorted(assign[order], np.arange(NLIST + 1))
+    local_rows = 0
+    for c in range(NLIST):
+        b, e = bounds[c], bounds[c + 1]
+        if e > b and owner[c] == rank:
+            rows = order[b:e]
+            eng.load_cluster(1, c, ids[rows], X[rows])
+            local_rows += e - b
+    log(f"[rank {rank}] index loaded ({local_rows} rows local) "
+        f"after {time.perf_counter() - t_setup:.1f}s")
+
+    Qd = torch.from_numpy(Qb).to(dev)  # [NBATCH, BATCH, DIM]
+    out_ids = torch.empty((BATCH, K), dtype=torch.int64, device=dev)
+    out_sc = torch.empty((BATCH, K), dtype=torch.float32, device=dev)
+    out_cnt = torch.empty((BATCH,), dtype=torch.int32, device=dev)
+    g_ids = torch.empty((world, BATCH, K), dtype=torch.int64, device=dev)
+    g_sc = torch.empty((world, BATCH, K), dtype=torch.float32, device=dev)
+    m_ids = torch.empty((BATCH, K), dtype=torch.int64, device=dev)
+    m_sc = torch.empty((BATCH, K), dtype=torch.float32, device=dev)
+    m_cnt = torch.empty((BATCH,), dtype=torch.int32, device=dev)
+
+    def step(b, nprobe):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        eng.search_device(1, Qd[b].data_ptr(), BATCH, K, nprobe, out_ids.data_ptr(),
+                          out_sc.data_ptr(), out_cnt.data_ptr(), stream)
+        if world == 1:
+            return out_ids, out_sc
+        dist.all_gather_into_tensor(g_sc, out_sc)
+        dist.all_gather_into_tensor(g_ids, out_ids)
+        eng.merge_shards_device(g_sc.data_ptr(), g_ids.data_ptr(), world, BATCH, K,
+                                m_ids.data_ptr(), m_sc.data_ptr(), m_cnt.data_ptr(), stream)
+        return m_ids, m_sc
+
+    # ---- recall@10 against exact search (untimed); pick nprobe
+    nprobe = NPROBE
+    recall = None
+    if rank == 0:
+        Xd = torch.from_numpy(X).to(dev)
+        exact = exact_topk_ip(Xd, Qd[0], K).cpu().numpy()
+        del Xd
+        torch.cuda.empty_cache()
+    sweep = {}
+    for p in (NPROBE, 48, 64, 96, 128, 256):
+        found, _ = step(0, p)
+        torch.cuda.synchronize()
+        eng.sync_errors()
+        r = recall_at_k(found.cpu().numpy(), exact, K) if rank == 0 else 0.0
+        if world > 1:
+            t = torch.tensor([r], device=dev)
+            dist.broadcast(t, 0)
+            r = float(t.item())
+        sweep[p] = r
+        if r >= 0.95:
+            nprobe, recall = p, r
+            break
+    if recall is None:
+        nprobe, recall = max(sweep, key=sweep.get), max(sweep.values())
+    log(f"[rank {rank}] recall@10 sweep {sweep} -> nprobe {nprobe}")
+
+    # ---- device-resident timing
+    for w in range(args.warmup):
+        step(w % NBATCH, nprobe)
+    torch.cuda.synchronize()
+    eng.sync_errors()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_selector(local_rank)) as clk:
+        ev0.record()
+        for i in range(args.steps):
+            step(i % NBATCH, nprobe)
+        ev1.record()
+        torch.cuda.synchronize()
+    eng.sync_errors()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    qps = BATCH * args.steps / (ms / 1e3)
+    clocks = clk.summary()
+
+    # ---- end to end through the C ABI with host buffers (H2D + D2H inside)
+    pinned = torch.from_numpy(Qb).pin_memory()
+    h_ids = torch.empty((BATCH, K), dtype=torch.int64).pin_memory()
+    h_sc = torch.empty((BATCH, K), dtype=torch.float32).pin_memory()
+    h_cnt = torch.empty((BATCH,), dtype=torch.int32).pin_memory()
+    scan_ms, scan_bytes, launches = [], [], 0
+    if world == 1:
+        lib = cabi.lib()
+
+        def e2e_step(b):
+            cabi.check(lib.m3g_search(eng.h, 1, pinned[b].data_ptr(), BATCH, K, nprobe,
+                                      h_ids.data_ptr(), h_sc.data_ptr(), h_cnt.data_ptr()))
+
+        eng.set_profiling(True)
+        for w in range(args.warmup):
+            e2e_step(w % NBATCH)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            e2e_step(i % NBATCH)
+            p = eng.last_profile()
+            scan_ms.append(p["ms_scan"])
+            scan_bytes.append(p["scan_bytes"])
+            launches += p["kernel_launches"]
+        e2e_s = time.perf_counter() - t0
+        eng.set_profiling(False)
+    else:
+        stream = torch.cuda.current_stream(dev)
+        qdev = torch.empty((BATCH, DIM), dtype=torch.float32, device=dev)
+
+        def e2e_step(b):
+            qdev.copy_(pinned[b], non_blocking=True)
+            s = stream.cuda_stream
+            eng.search_device(1, qdev.data_ptr(), BATCH, K, nprobe, out_ids.data_ptr(),
+                              out_sc.data_ptr(), out_cnt.data_ptr(), s)
+            dist.all_gather_into_tensor(g_sc, out_sc)
+            dist.all_gather_into_tensor(g_ids, out_ids)
+            eng.merge_shards_device(g_sc.data_ptr(), g_ids.data_ptr(), world, BATCH, K,
+                                    m_ids.data_ptr(), m_sc.data_ptr(), m_cnt.data_ptr(), s)
+            h_ids.copy_(m_ids, non_blocking=True)
+            h_sc.copy_(m_sc, non_blocking=True)
+            h_cnt.copy_(m_cnt, non_blocking=True)
+            torch.cuda.synchronize()
+
+        for w in range(args.warmup):
+            e2e_step(w % NBATCH)
+        dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            e2e_step(i % NBATCH)
+        e2e_s = time.perf_counter() - t0
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_qps = BATCH * args.steps / e2e_s
+
+    if rank != 0:
+        return
+    per_step_launches = (launches / args.steps) if launches else (
+        8 if world == 1 else 9)
+    peak, peak_kind = peaks()
+    roofline = None
+    if scan_ms:
+        avg_ms = statistics.mean(scan_ms)
+        avg_bytes = statistics.mean(scan_bytes)
+        achieved = avg_bytes / (avg_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": scan_traffic_per_launch(),
+                    "kernel": "list_scan_kernel",
+                    "bytes_per_launch": avg_bytes, "ms_per_launch": avg_ms,
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                    if peak_kind == "measured" else "fallback 6650 GB/s"}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+
+        if O.have_ref():
+            threads = len(os.sched_getaffinity(0))
+            v, sample = cpu_reference_qps(C, X, assign, Qb, threads)
+            cpu = {"value": v, "unit": "queries/s", "cores": threads, "kind": "reference",
+                   "sample": sample}
+    line = {
+        "metric": "search QPS at recall@10>=0.95 (IVF, dim 1024)",
+        "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture; no dataset)",
+        "config": {"workload": WORKLOAD, "n_vectors": N_VEC, "dim": DIM, "nlist": NLIST,
+                   "nprobe": nprobe, "k": K, "batch": BATCH, "recall_at_10": recall,
+                   "recall_sweep": {str(k): v for k, v in sweep.items()},
+                   "kmeans_iters": KMEANS_ITERS,
+                   "l2_flush": "not needed: each step streams ~4 GB of lists (> 126 MB L2)",
+                   "parallelism": f"lists sharded over {world} GPU(s)" if world > 1 else "1 GPU"},
+        "gpu_launches": int(round(per_step_launches * args.steps)),
+        "clocks": clocks,
+        "e2e": {"value": e2e_qps, "unit": "queries/s",
+                "h2d_bytes_per_step": BATCH * DIM * 4,
+                "d2h_bytes_per_step": BATCH * K * 12 + BATCH * 4,
+                "path": "m3g_search (C ABI, pinned host buffers)" if world == 1
+                else "H2D + m3g_search_device + NCCL all-gather + m3g_merge_shards_device + D2H"},
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch.distributed as dist
+
+    if world > 1:
+        import datetime
+
+        import torch
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

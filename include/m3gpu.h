@@ -1,0 +1,203 @@
+/* m3gpu.h -- C ABI of libm3gpu, the B200 (sm_100a) engine for the M3 IVF index
+ * hot path of AgentMemory's `m3` backend (Leo9660/M3_memory).
+ *
+ * Each entry point replaces one method of the reference's m3::AsyncEngine
+ * (AgentMemory/M3/include/m3_async.h:63-169, bound to Python by
+ * AgentMemory/M3/src/bindings_async.cpp:153-588); the citation beside each
+ * declaration names the reference interface it stands for.  Only plain
+ * pointers, sizes and ints cross this boundary.
+ *
+ * Conventions
+ *   - Every function returns an m3g_status (0 = ok).  On failure the calling
+ *     thread's m3g_last_error() holds a message.  The status codes map onto the
+ *     reference's C++ exception types: M3G_EINVAL = std::invalid_argument,
+ *     M3G_ERANGE = std::out_of_range, M3G_ERUNTIME = std::runtime_error.
+ *   - Host pointers are plain host memory (pinned or pageable); functions named
+ *     *_device take device pointers of the engine's CUDA device.
+ *   - Vectors are row-major float32 [n, dim]; ids are int64.
+ *   - Search results are written padded: out_ids[nq*k] / out_scores[nq*k] with
+ *     -1 / +inf in unused slots, out_counts[nq] = valid results per query
+ *     (the reference returns ragged lists after dropping -1 slots,
+ *     AgentMemory/M3/src/m3_index.cpp:444-475).
+ *   - Scores are the reference's unified "smaller is better" score
+ *     (AgentMemory/M3/include/base.h:22-31): squared L2, -dot, 1-dot, or
+ *     1-cosine.
+ */
+#ifndef M3GPU_H
+#define M3GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct m3g_engine m3g_engine;
+
+typedef enum {
+    M3G_OK = 0,
+    M3G_EINVAL = 1,       /* std::invalid_argument */
+    M3G_ERANGE = 2,       /* std::out_of_range */
+    M3G_ERUNTIME = 3,     /* std::runtime_error */
+    M3G_ECUDA = 4,        /* a CUDA runtime / driver call failed */
+    M3G_ENCCL = 5,        /* a collective failed */
+    M3G_ETIMEOUT = 6,     /* a bounded device wait ran out */
+    M3G_EUNSUPPORTED = 7  /* valid request outside this engine's limits */
+} m3g_status;
+
+/* m3::Metric, AgentMemory/M3/include/base.h:10 */
+typedef enum { M3G_L2 = 0, M3G_IP = 1, M3G_COSINE = 2 } m3g_metric;
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* m3g_last_error(void);
+/* ABI version (major * 10000 + minor * 100 + patch). */
+int m3g_version(void);
+
+/* AsyncEngine::AsyncEngine / ~AsyncEngine (AgentMemory/M3/src/m3_async.cpp:14-32).
+ * The engine binds to the CUDA device current on the calling thread. */
+int m3g_engine_create(m3g_engine** out);
+int m3g_engine_destroy(m3g_engine* e);
+/* Rebind to CUDA device `device` (before any index is created). */
+int m3g_set_device(m3g_engine* e, int device);
+
+/* AsyncEngine::start / stop (m3_async.cpp:53-105). */
+int m3g_start(m3g_engine* e, int writer_threads, int maintenance_threads);
+int m3g_stop(m3g_engine* e);
+
+/* AsyncEngine::set_*_policy (m3_async.cpp:109-119; AsyncQueuePolicy,
+ * AsyncSearchPolicy, AsyncMaintenancePolicy at m3_async.h:44-59).  auto_split
+ * has no counterpart: when nonzero the maintenance pass also splits lists
+ * larger than split_threshold rows (the reference leaves this as a TODO,
+ * m3_index.cpp:304-311); 0 keeps the reference's behaviour. */
+int m3g_set_queue_policy(m3g_engine* e, size_t capacity, size_t pop_batch_max,
+                         int block_on_full);
+int m3g_set_search_policy(m3g_engine* e, int default_nprobe, int parallel_queries);
+int m3g_set_maintenance_policy(m3g_engine* e, double period_sec, size_t split_threshold,
+                               double compact_ratio, int auto_split);
+
+/* AsyncEngine::create_ivf (m3_async.cpp:36-49 -> IVFIndex::set_centroids,
+ * m3_index.cpp:98-131).  centroids: [nlist, dim]; nlist may be 0.  Replaces
+ * an existing index of the same id. */
+int m3g_create_ivf(m3g_engine* e, int index_id, int dim, int metric, int normalized,
+                   const float* centroids, int64_t nlist);
+
+/* AsyncEngine::load_cluster (m3_async.cpp:237-260 -> Cluster::rebuild_from,
+ * cluster.cpp:152-178): synchronous full replace of one list. */
+int m3g_load_cluster(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
+                     const float* vecs, int64_t n);
+
+/* AsyncEngine::enqueue_insert / enqueue_update / enqueue_delete
+ * (m3_async.cpp:123-187; applied by writer threads as Cluster::add_batch /
+ * update_batch / erase_batch, cluster.cpp:55-150).  *accepted = 0 when the
+ * engine is stopped or the queue is full with block_on_full = 0. */
+int m3g_enqueue_insert(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
+                       const float* vecs, int64_t n, int* accepted);
+int m3g_enqueue_update(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
+                       const float* vecs, int64_t n, int insert_if_absent, int* accepted);
+int m3g_enqueue_delete(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
+                       int64_t n, int* accepted);
+
+/* AsyncEngine::enqueue_insert_auto (m3_async.cpp:262-313): rows are routed to
+ * their nearest centroid on the GPU (bit-exact with IVFIndex::nearest_clusters,
+ * m3_index.cpp:243-264) and enqueued as one insert per cluster. */
+int m3g_enqueue_insert_auto(m3g_engine* e, int index_id, const int64_t* ids, const float* vecs,
+                            int64_t n, int* accepted);
+
+/* AsyncEngine::flush (m3_async.cpp:191-201).  Also reports (and clears) the
+ * first error a writer thread hit since the last flush; the reference
+ * terminates the process in that case instead. */
+int m3g_flush(m3g_engine* e);
+
+/* AsyncEngine::search (m3_async.cpp:205-235 -> IVFIndex::search_nprobe,
+ * m3_index.cpp:368-483).  nprobe <= 0 uses the search policy's default_nprobe.
+ * Host buffers; synchronous.  An unknown index_id yields empty results, as the
+ * reference core does (m3_async.cpp:218-222). */
+int m3g_search(m3g_engine* e, int index_id, const float* queries, int64_t nq, int k, int nprobe,
+               int64_t* out_ids, float* out_scores, int32_t* out_counts);
+
+/* The same search with device-resident queries and results (device pointers of
+ * the engine's device).  With stream == NULL the call is synchronous; with a
+ * cudaStream_t it is enqueued on that stream and returns at once (kernel-side
+ * errors then surface through m3g_sync_errors). */
+int m3g_search_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq, int k,
+                      int nprobe, int64_t* d_out_ids, float* d_out_scores, int32_t* d_out_counts,
+                      void* stream);
+/* Waits for the engine's outstanding device work and reports kernel errors. */
+int m3g_sync_errors(m3g_engine* e);
+
+/* IVFIndex::search_on (m3_index.cpp:314-366): search an explicit cluster list
+ * (no coarse step); every query probes cluster_ids in the given order. */
+int m3g_search_on(m3g_engine* e, int index_id, const int32_t* cluster_ids, int ncluster,
+                  const float* queries, int64_t nq, int k, int64_t* out_ids, float* out_scores,
+                  int32_t* out_counts);
+
+/* IVFIndex::nearest_clusters (m3_index.cpp:243-264): argmin of the unified
+ * score, lowest id on ties, -1 if the index has no lists.  Bit-exact. */
+int m3g_nearest_clusters(m3g_engine* e, int index_id, const float* vecs, int64_t n,
+                         int32_t* out_cluster);
+
+/* The top-nprobe centroid selection (IVFIndex::select_nprobe_for_query,
+ * m3_index.cpp:492-523) on its own: out_probes[nq, min(nprobe, nlist)]
+ * ascending by exact score (ties: lower id). */
+int m3g_select_probes(m3g_engine* e, int index_id, const float* queries, int64_t nq, int nprobe,
+                      int32_t* out_probes);
+
+/* AsyncEngine::dim_of / metric_of / normalized_of / nlist_of
+ * (m3_async.cpp:317-351); an unknown index gives dim 0, COSINE, 1, 0. */
+int m3g_info(m3g_engine* e, int index_id, int* dim, int* metric, int* normalized, int* nlist);
+
+/* Cluster::size / live_size (cluster.cpp:45-53). */
+int m3g_cluster_size(m3g_engine* e, int index_id, int cluster_id, int64_t* size, int64_t* live);
+/* The routing centroids [nlist, dim] (IVFIndex::centroid_ptr, m3_index.cpp:170-175). */
+int m3g_get_centroids(m3g_engine* e, int index_id, float* out);
+/* IVFIndex::add_cluster / set_centroid (m3_index.cpp:133-163). */
+int m3g_add_cluster(m3g_engine* e, int index_id, const float* centroid, int32_t* out_cluster_id);
+int m3g_set_centroid(m3g_engine* e, int index_id, int cluster_id, const float* centroid);
+/* IVFIndex::compact_cluster / maintenance_pass (m3_index.cpp:266-312). */
+int m3g_compact_cluster(m3g_engine* e, int index_id, int cluster_id);
+int m3g_maintenance_pass(m3g_engine* e, int index_id);
+
+/* k-means (no counterpart in the reference, whose centroids always come from
+ * the caller): nlist distinct seeded rows as the start, niter rounds of
+ * exact-assignment + fp64 mean update, assignment against the final centroids.
+ * Host buffers: X[n, dim] -> centroids[nlist, dim], assign[n] (nullable). */
+int m3g_kmeans(m3g_engine* e, const float* X, int64_t n, int dim, int metric, int normalized,
+               int nlist, int niter, uint64_t seed, float* out_centroids, int32_t* out_assign);
+/* Trains centroids on (ids, X) with m3g_kmeans, creates index_id with them
+ * (as create_ivf) and loads every row into its list in ascending row order. */
+int m3g_train_ivf(m3g_engine* e, int index_id, int dim, int metric, int normalized,
+                  const int64_t* ids, const float* X, int64_t n, int nlist, int niter,
+                  uint64_t seed, float* out_centroids);
+/* Splits one list by 2-means (niter rounds, seeded start rows) into itself and
+ * a new list: set_centroid(cluster_id, c0), add_cluster(c1), rows regrouped in
+ * list order.  *out_new_cluster = -1 when the list has fewer than 2 live rows. */
+int m3g_split_cluster(m3g_engine* e, int index_id, int cluster_id, int niter, uint64_t seed,
+                      int32_t* out_new_cluster);
+
+/* Final merge of a list-sharded search (one shard of the lists per GPU): each
+ * shard's answer [nq, k] (as m3g_search_device writes it) gathered into
+ * d_scores / d_ids [nshard, nq, k] -> the global top-k [nq, k].  Stands in for
+ * the ascending sort that ends IVFIndex::search_nprobe (m3_index.cpp:444-475)
+ * when the lists live on several GPUs.  Device pointers; enqueued on `stream`
+ * (NULL: synchronous). */
+int m3g_merge_shards_device(m3g_engine* e, const float* d_scores, const int64_t* d_ids,
+                            int nshard, int64_t nq, int k, int64_t* d_out_ids,
+                            float* d_out_scores, int32_t* d_out_counts, void* stream);
+
+/* Per-stage device time of the most recent search (profiling must be on). */
+typedef struct {
+    float ms_prep, ms_coarse_gemm, ms_select, ms_worklist, ms_scan, ms_merge, ms_total;
+    int64_t scan_bytes;     /* sum over distinct probed lists of rows * row bytes */
+    int64_t probed_pairs;   /* (query, list) pairs scanned */
+    int32_t kernel_launches;
+    int32_t nq, nprobe, k;
+} m3g_profile;
+int m3g_set_profiling(m3g_engine* e, int on);
+int m3g_last_profile(m3g_engine* e, m3g_profile* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M3GPU_H */

@@ -1,0 +1,332 @@
+// api.cpp -- the extern "C" surface of libm3gpu (declared in include/m3gpu.h).
+// Every entry point catches C++ exceptions and turns them into an m3g_status
+// plus the thread's last-error message.
+#include <cstring>
+#include <string>
+
+#include "engine.h"
+#include "m3gpu.h"
+
+struct m3g_engine {
+    m3g::Engine eng;
+};
+
+namespace {
+thread_local std::string g_last_error;
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        g_last_error.clear();
+        return M3G_OK;
+    } catch (const m3g::Error& e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "out of host memory";
+        return M3G_ERUNTIME;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return M3G_ERUNTIME;
+    } catch (...) {
+        g_last_error = "unknown error";
+        return M3G_ERUNTIME;
+    }
+}
+
+int bad_handle() {
+    g_last_error = "null engine handle";
+    return M3G_EINVAL;
+}
+}  // namespace
+
+#define M3G_ENGINE_OR_FAIL(e) \
+    if (!(e)) return bad_handle()
+
+extern "C" {
+
+const char* m3g_last_error(void) { return g_last_error.c_str(); }
+
+int m3g_version(void) { return 100; }
+
+int m3g_engine_create(m3g_engine** out) {
+    if (!out) return bad_handle();
+    return guarded([&] { *out = new m3g_engine(); });
+}
+
+int m3g_engine_destroy(m3g_engine* e) {
+    return guarded([&] { delete e; });
+}
+
+int m3g_set_device(m3g_engine* e, int device) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.set_device(device); });
+}
+
+int m3g_start(m3g_engine* e, int writer_threads, int maintenance_threads) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.start(writer_threads, maintenance_threads); });
+}
+
+int m3g_stop(m3g_engine* e) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.stop(); });
+}
+
+int m3g_set_queue_policy(m3g_engine* e, size_t capacity, size_t pop_batch_max, int block_on_full) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        m3g::QueuePolicy p;
+        p.capacity = capacity;
+        p.pop_batch_max = pop_batch_max;
+        p.block_on_full = block_on_full != 0;
+        e->eng.set_queue_policy(p);
+    });
+}
+
+int m3g_set_search_policy(m3g_engine* e, int default_nprobe, int parallel_queries) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        m3g::SearchPolicy p;
+        p.default_nprobe = default_nprobe;
+        p.parallel_queries = parallel_queries != 0;
+        e->eng.set_search_policy(p);
+    });
+}
+
+int m3g_set_maintenance_policy(m3g_engine* e, double period_sec, size_t split_threshold,
+                               double compact_ratio, int auto_split) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        m3g::MaintenancePolicy p;
+        p.period_sec = period_sec;
+        p.split_threshold = split_threshold;
+        p.compact_ratio = compact_ratio;
+        p.auto_split = auto_split != 0;
+        e->eng.set_maintenance_policy(p);
+    });
+}
+
+int m3g_create_ivf(m3g_engine* e, int index_id, int dim, int metric, int normalized,
+                   const float* centroids, int64_t nlist) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded(
+        [&] { e->eng.create_ivf(index_id, dim, metric, normalized != 0, centroids, nlist); });
+}
+
+int m3g_load_cluster(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
+                     const float* vecs, int64_t n) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.load_cluster(index_id, cluster_id, ids, vecs, n); });
+}
+
+namespace {
+int enqueue_op(m3g_engine* e, m3g::WriteOp::Kind kind, int index_id, int cluster_id,
+               const int64_t* ids, const float* vecs, int64_t n, bool insert_if_absent,
+               int* accepted) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (n < 0) m3g::fail(M3G_EINVAL, "enqueue: n < 0");
+        int dim = 0;
+        e->eng.info(index_id, &dim, nullptr, nullptr, nullptr);
+        if (kind != m3g::WriteOp::kDelete && dim <= 0)
+            m3g::fail(M3G_ERUNTIME, "enqueue: unknown index_id (call create_ivf first)");
+        m3g::WriteOp op;
+        op.kind = kind;
+        op.index_id = index_id;
+        op.cluster_id = cluster_id;
+        op.insert_if_absent = insert_if_absent;
+        if (n > 0) {
+            if (!ids) m3g::fail(M3G_EINVAL, "enqueue: ids missing");
+            op.ids.assign(ids, ids + n);
+            if (kind != m3g::WriteOp::kDelete) {
+                if (!vecs) m3g::fail(M3G_EINVAL, "enqueue: vectors missing");
+                op.vecs.assign(vecs, vecs + n * (int64_t)dim);
+            }
+        }
+        const bool ok = e->eng.enqueue(std::move(op));
+        if (accepted) *accepted = ok ? 1 : 0;
+    });
+}
+}  // namespace
+
+int m3g_enqueue_insert(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
+                       const float* vecs, int64_t n, int* accepted) {
+    return enqueue_op(e, m3g::WriteOp::kInsert, index_id, cluster_id, ids, vecs, n, false,
+                      accepted);
+}
+
+int m3g_enqueue_update(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
+                       const float* vecs, int64_t n, int insert_if_absent, int* accepted) {
+    return enqueue_op(e, m3g::WriteOp::kUpdate, index_id, cluster_id, ids, vecs, n,
+                      insert_if_absent != 0, accepted);
+}
+
+int m3g_enqueue_delete(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids, int64_t n,
+                       int* accepted) {
+    return enqueue_op(e, m3g::WriteOp::kDelete, index_id, cluster_id, ids, nullptr, n, false,
+                      accepted);
+}
+
+int m3g_enqueue_insert_auto(m3g_engine* e, int index_id, const int64_t* ids, const float* vecs,
+                            int64_t n, int* accepted) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        const bool ok = e->eng.enqueue_insert_auto(index_id, ids, vecs, n);
+        if (accepted) *accepted = ok ? 1 : 0;
+    });
+}
+
+int m3g_flush(m3g_engine* e) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.flush(); });
+}
+
+int m3g_search(m3g_engine* e, int index_id, const float* queries, int64_t nq, int k, int nprobe,
+               int64_t* out_ids, float* out_scores, int32_t* out_counts) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (nq > 0 && (!out_counts || (k > 0 && (!out_ids || !out_scores))))
+            m3g::fail(M3G_EINVAL, "search: output buffers missing");
+        e->eng.search(index_id, queries, nq, k, nprobe, false, out_ids, out_scores, out_counts,
+                      false, nullptr);
+    });
+}
+
+int m3g_search_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq, int k,
+                      int nprobe, int64_t* d_out_ids, float* d_out_scores, int32_t* d_out_counts,
+                      void* stream) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (nq > 0 && (!d_out_counts || (k > 0 && (!d_out_ids || !d_out_scores))))
+            m3g::fail(M3G_EINVAL, "search_device: output buffers missing");
+        e->eng.search(index_id, d_queries, nq, k, nprobe, true, d_out_ids, d_out_scores,
+                      d_out_counts, true, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int m3g_sync_errors(m3g_engine* e) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.sync_errors(); });
+}
+
+int m3g_search_on(m3g_engine* e, int index_id, const int32_t* cluster_ids, int ncluster,
+                  const float* queries, int64_t nq, int k, int64_t* out_ids, float* out_scores,
+                  int32_t* out_counts) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        e->eng.search_on(index_id, cluster_ids, ncluster, queries, nq, k, out_ids, out_scores,
+                         out_counts);
+    });
+}
+
+int m3g_nearest_clusters(m3g_engine* e, int index_id, const float* vecs, int64_t n,
+                         int32_t* out_cluster) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.nearest_clusters(index_id, vecs, n, out_cluster); });
+}
+
+int m3g_select_probes(m3g_engine* e, int index_id, const float* queries, int64_t nq, int nprobe,
+                      int32_t* out_probes) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.select_probes(index_id, queries, nq, nprobe, out_probes); });
+}
+
+int m3g_info(m3g_engine* e, int index_id, int* dim, int* metric, int* normalized, int* nlist) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.info(index_id, dim, metric, normalized, nlist); });
+}
+
+int m3g_cluster_size(m3g_engine* e, int index_id, int cluster_id, int64_t* size, int64_t* live) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.cluster_size(index_id, cluster_id, size, live); });
+}
+
+int m3g_get_centroids(m3g_engine* e, int index_id, float* out) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.get_centroids(index_id, out); });
+}
+
+int m3g_add_cluster(m3g_engine* e, int index_id, const float* centroid, int32_t* out_cluster_id) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        const int c = e->eng.add_cluster(index_id, centroid);
+        if (out_cluster_id) *out_cluster_id = c;
+    });
+}
+
+int m3g_set_centroid(m3g_engine* e, int index_id, int cluster_id, const float* centroid) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.set_centroid(index_id, cluster_id, centroid); });
+}
+
+int m3g_compact_cluster(m3g_engine* e, int index_id, int cluster_id) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.compact_cluster(index_id, cluster_id); });
+}
+
+int m3g_maintenance_pass(m3g_engine* e, int index_id) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.maintenance_pass(index_id); });
+}
+
+int m3g_kmeans(m3g_engine* e, const float* X, int64_t n, int dim, int metric, int normalized,
+               int nlist, int niter, uint64_t seed, float* out_centroids, int32_t* out_assign) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        e->eng.kmeans(X, n, dim, metric, normalized != 0, nlist, niter, seed, out_centroids,
+                      out_assign);
+    });
+}
+
+int m3g_train_ivf(m3g_engine* e, int index_id, int dim, int metric, int normalized,
+                  const int64_t* ids, const float* X, int64_t n, int nlist, int niter,
+                  uint64_t seed, float* out_centroids) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        e->eng.train_ivf(index_id, dim, metric, normalized != 0, ids, X, n, nlist, niter, seed,
+                         out_centroids);
+    });
+}
+
+int m3g_split_cluster(m3g_engine* e, int index_id, int cluster_id, int niter, uint64_t seed,
+                      int32_t* out_new_cluster) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        const int c = e->eng.split_cluster(index_id, cluster_id, niter, seed);
+        if (out_new_cluster) *out_new_cluster = c;
+    });
+}
+
+int m3g_merge_shards_device(m3g_engine* e, const float* d_scores, const int64_t* d_ids,
+                            int nshard, int64_t nq, int k, int64_t* d_out_ids,
+                            float* d_out_scores, int32_t* d_out_counts, void* stream) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (nshard <= 0 || nq < 0 || k < 0 || nq > INT32_MAX)
+            m3g::fail(M3G_EINVAL, "merge_shards: bad sizes");
+        if (nq > 0 && k > 0 && (!d_scores || !d_ids || !d_out_ids || !d_out_scores || !d_out_counts))
+            m3g::fail(M3G_EINVAL, "merge_shards: buffers missing");
+        m3g::DeviceGuard g(e->eng.device());
+        auto st = static_cast<cudaStream_t>(stream);
+        M3G_CK(m3g::launch_merge_shards(d_scores, d_ids, nshard, (int)nq, k, d_out_ids,
+                                        d_out_scores, d_out_counts, st));
+        if (!st) M3G_CK(cudaStreamSynchronize(st));
+    });
+}
+
+int m3g_set_profiling(m3g_engine* e, int on) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.set_profiling(on != 0); });
+}
+
+int m3g_last_profile(m3g_engine* e, m3g_profile* out) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (!out) m3g::fail(M3G_EINVAL, "last_profile: out missing");
+        *out = e->eng.last_profile();
+    });
+}
+
+}  // extern "C"

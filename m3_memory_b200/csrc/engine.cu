@@ -1,0 +1,1469 @@
+// engine.cu -- host implementation of the m3gpu engine (see engine.h).
+//
+// Reference behaviour mirrored here, by file:
+//   AgentMemory/M3/src/cluster.cpp   add/update/erase/rebuild/compact of one list
+//   AgentMemory/M3/src/m3_index.cpp  set_centroids, add_cluster, set_centroid,
+//                                    nearest_clusters, search_on, search_nprobe,
+//                                    maintenance_pass
+//   AgentMemory/M3/src/m3_async.cpp  create_ivf, start/stop, queue + writers,
+//                                    flush, search, load_cluster,
+//                                    enqueue_insert_auto, *_of
+#include "engine.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <unordered_set>
+
+#include "kernels_kmeans.h"
+
+namespace m3g {
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw Error(code, msg); }
+
+void check_cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(M3G_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+// Never throws (it also runs in destructors); a failed switch surfaces at the
+// next CUDA call, which does check.
+DeviceGuard::DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev_) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    if (prev_ != dev) {
+        if (cudaSetDevice(dev) == cudaSuccess) changed_ = true;
+        else cudaGetLastError();
+    }
+}
+DeviceGuard::~DeviceGuard() {
+    if (changed_) cudaSetDevice(prev_);
+}
+
+void sample_rows(uint64_t seed, int64_t n, int64_t m, int64_t* out) {
+    if (m < 0 || m > n) fail(M3G_EINVAL, "sample_rows: need 0 <= m <= n");
+    std::vector<int64_t> perm((size_t)n);
+    std::iota(perm.begin(), perm.end(), int64_t(0));
+    uint64_t st = seed;
+    auto next = [&st]() {
+        uint64_t z = (st += 0x9E3779B97F4A7C15ull);
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    for (int64_t i = 0; i < m; ++i) {
+        const int64_t j = i + (int64_t)(next() % (uint64_t)(n - i));
+        std::swap(perm[(size_t)i], perm[(size_t)j]);
+        out[i] = perm[(size_t)i];
+    }
+}
+
+namespace {
+
+constexpr int kDefaultNsm = 148;
+
+int round_up4(int d) { return (d + 3) & ~3; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D fp32 tensor map over [rows, dpad], box 32 x h, 128-byte swizzle.
+void make_row_map(CUtensorMap* m, const float* base, int64_t rows, int dpad, int h) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) fail(M3G_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t gdim[2] = {(cuuint64_t)dpad, (cuuint64_t)std::max<int64_t>(rows, 1)};
+    cuuint64_t gstride[1] = {(cuuint64_t)dpad * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)h};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstride,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(M3G_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+}
+
+void rebuild_maps(Index& ix) {
+    if (!ix.vecs.p) {
+        ix.maps_valid = false;
+        return;
+    }
+    make_row_map(&ix.maps.m64, ix.vecs.p, ix.arena_cap, ix.dpad, 64);
+    make_row_map(&ix.maps.m32, ix.vecs.p, ix.arena_cap, ix.dpad, 32);
+    make_row_map(&ix.maps.m16, ix.vecs.p, ix.arena_cap, ix.dpad, 16);
+    make_row_map(&ix.maps.m8, ix.vecs.p, ix.arena_cap, ix.dpad, 8);
+    ix.maps_valid = true;
+}
+
+// Copies n host rows of `dim` floats into device rows of `dpad` floats.
+void h2d_rows(float* dst, int dpad, const float* src, int dim, int64_t n, cudaStream_t st) {
+    if (n <= 0) return;
+    M3G_CK(cudaMemcpy2DAsync(dst, (size_t)dpad * 4, src, (size_t)dim * 4, (size_t)dim * 4,
+                             (size_t)n, cudaMemcpyHostToDevice, st));
+}
+
+// ---------------- index device state ----------------
+
+void ensure_centroid_cap(Index& ix, size_t need) {
+    if (need <= ix.c_cap && ix.C.p) return;
+    size_t cap = std::max<size_t>({need, ix.c_cap * 2, 16});
+    DBuf<float> C, cn, cn2;
+    DBuf<int64_t> off;
+    DBuf<int32_t> len, order;
+    C.alloc(cap * ix.dpad);
+    cn.alloc(cap);
+    cn2.alloc(cap);
+    off.alloc(cap);
+    len.alloc(cap);
+    order.alloc(cap);
+    M3G_CK(cudaMemsetAsync(C.p, 0, cap * ix.dpad * 4, ix.wstream));
+    if (ix.C.p && ix.c_cap) {
+        M3G_CK(cudaMemcpyAsync(C.p, ix.C.p, ix.c_cap * ix.dpad * 4, cudaMemcpyDeviceToDevice, ix.wstream));
+        M3G_CK(cudaMemcpyAsync(cn.p, ix.cn.p, ix.c_cap * 4, cudaMemcpyDeviceToDevice, ix.wstream));
+        M3G_CK(cudaMemcpyAsync(cn2.p, ix.cn2.p, ix.c_cap * 4, cudaMemcpyDeviceToDevice, ix.wstream));
+    }
+    M3G_CK(cudaStreamSynchronize(ix.wstream));
+    ix.C.swap(C);
+    ix.cn.swap(cn);
+    ix.cn2.swap(cn2);
+    ix.d_list_off.swap(off);
+    ix.d_list_len.swap(len);
+    ix.d_list_order.swap(order);
+    ix.c_cap = cap;
+}
+
+// Uploads centroids [c0, c0+n) from the host copy and recomputes their norms.
+void upload_centroids(Index& ix, int c0, int n) {
+    if (n <= 0) return;
+    h2d_rows(ix.C.p + (size_t)c0 * ix.dpad, ix.dpad, ix.centroids.data() + (size_t)c0 * ix.dim,
+             ix.dim, n, ix.wstream);
+    launch_row_norms(ix.C.p + (size_t)c0 * ix.dpad, ix.dpad, n, ix.dim, ix.cn.p + c0, ix.cn2.p + c0,
+                     ix.wstream);
+    M3G_CK(cudaGetLastError());
+}
+
+// Uploads per-list offsets / lengths and the longest-first order.
+void refresh_list_meta(Index& ix) {
+    const int L = ix.nlist();
+    if (L == 0) return;
+    std::vector<int64_t> off(L);
+    std::vector<int32_t> len(L), order(L);
+    for (int l = 0; l < L; ++l) {
+        off[l] = ix.lists[l].off;
+        len[l] = (int32_t)ix.lists[l].len;
+    }
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len[a] > len[b]; });
+    M3G_CK(cudaMemcpyAsync(ix.d_list_off.p, off.data(), L * 8, cudaMemcpyHostToDevice, ix.wstream));
+    M3G_CK(cudaMemcpyAsync(ix.d_list_len.p, len.data(), L * 4, cudaMemcpyHostToDevice, ix.wstream));
+    M3G_CK(cudaMemcpyAsync(ix.d_list_order.p, order.data(), L * 4, cudaMemcpyHostToDevice, ix.wstream));
+    M3G_CK(cudaStreamSynchronize(ix.wstream));
+}
+
+// Reallocates the arena with room for `extra` more rows, laying every list out
+// again contiguously (this also reclaims the holes relocations leave behind).
+void grow_arena(Index& ix, int64_t extra) {
+    int64_t used = 0;
+    for (auto& l : ix.lists) used += l.cap;
+    const int64_t cap = std::max<int64_t>({used + extra, ix.arena_cap + ix.arena_cap / 2, 1024});
+    DBuf<float> vecs, rn;
+    DBuf<int64_t> ids;
+    DBuf<uint8_t> alive;
+    vecs.alloc((size_t)cap * ix.dpad);
+    rn.alloc((size_t)cap);
+    ids.alloc((size_t)cap);
+    alive.alloc((size_t)cap);
+    M3G_CK(cudaMemsetAsync(vecs.p, 0, (size_t)cap * ix.dpad * 4, ix.wstream));
+    M3G_CK(cudaMemsetAsync(alive.p, 0, (size_t)cap, ix.wstream));
+    int64_t pos = 0;
+    for (auto& l : ix.lists) {
+        if (l.len > 0) {
+            M3G_CK(cudaMemcpyAsync(vecs.p + pos * ix.dpad, ix.vecs.p + l.off * ix.dpad,
+                                   (size_t)l.len * ix.dpad * 4, cudaMemcpyDeviceToDevice, ix.wstream));
+            M3G_CK(cudaMemcpyAsync(rn.p + pos, ix.rnorm2.p + l.off, (size_t)l.len * 4,
+                                   cudaMemcpyDeviceToDevice, ix.wstream));
+            M3G_CK(cudaMemcpyAsync(ids.p + pos, ix.ids.p + l.off, (size_t)l.len * 8,
+                                   cudaMemcpyDeviceToDevice, ix.wstream));
+            M3G_CK(cudaMemcpyAsync(alive.p + pos, ix.alive.p + l.off, (size_t)l.len,
+                                   cudaMemcpyDeviceToDevice, ix.wstream));
+        }
+        l.off = pos;
+        pos += l.cap;
+    }
+    M3G_CK(cudaStreamSynchronize(ix.wstream));
+    ix.vecs.swap(vecs);
+    ix.rnorm2.swap(rn);
+    ix.ids.swap(ids);
+    ix.alive.swap(alive);
+    ix.arena_cap = cap;
+    ix.arena_used = pos;
+    rebuild_maps(ix);
+}
+
+// Gives list l a fresh segment of `cap` rows, keeping its first `keep` rows.
+// When the arena is full it is rebuilt with every list laid out again, this
+// one already at its new capacity.
+void relocate(Index& ix, int l, int64_t cap, int64_t keep) {
+    ListMeta& L = ix.lists[l];
+    if (ix.arena_used + cap > ix.arena_cap) {
+        L.cap = cap;
+        grow_arena(ix, 0);
+        return;
+    }
+    const int64_t dst = ix.arena_used;
+    if (keep > 0) {
+        M3G_CK(cudaMemcpyAsync(ix.vecs.p + dst * ix.dpad, ix.vecs.p + L.off * ix.dpad,
+                               (size_t)keep * ix.dpad * 4, cudaMemcpyDeviceToDevice, ix.wstream));
+        M3G_CK(cudaMemcpyAsync(ix.rnorm2.p + dst, ix.rnorm2.p + L.off, (size_t)keep * 4,
+                               cudaMemcpyDeviceToDevice, ix.wstream));
+        M3G_CK(cudaMemcpyAsync(ix.ids.p + dst, ix.ids.p + L.off, (size_t)keep * 8,
+                               cudaMemcpyDeviceToDevice, ix.wstream));
+        M3G_CK(cudaMemcpyAsync(ix.alive.p + dst, ix.alive.p + L.off, (size_t)keep,
+                               cudaMemcpyDeviceToDevice, ix.wstream));
+    }
+    L.off = dst;
+    L.cap = cap;
+    ix.arena_used += cap;
+}
+
+void ensure_list_room(Index& ix, int l, int64_t need_len) {
+    ListMeta& L = ix.lists[l];
+    if (need_len <= L.cap) return;
+    const int64_t cap = std::max<int64_t>({need_len, L.cap * 2, 16});
+    relocate(ix, l, cap, L.len);
+}
+
+// Writes rows (ids, host vectors) at arena rows [row0, row0 + n) of list l.
+void write_rows(Index& ix, int64_t row0, const int64_t* ids, const float* vecs, int64_t n) {
+    if (n <= 0) return;
+    h2d_rows(ix.vecs.p + row0 * ix.dpad, ix.dpad, vecs, ix.dim, n, ix.wstream);
+    M3G_CK(cudaMemcpyAsync(ix.ids.p + row0, ids, (size_t)n * 8, cudaMemcpyHostToDevice, ix.wstream));
+    M3G_CK(cudaMemsetAsync(ix.alive.p + row0, 1, (size_t)n, ix.wstream));
+    launch_row_norms(ix.vecs.p + row0 * ix.dpad, ix.dpad, n, ix.dim, nullptr, ix.rnorm2.p + row0,
+                     ix.wstream);
+    M3G_CK(cudaGetLastError());
+}
+
+// Host-side staging of int64 index arrays for the scatter / gather kernels.
+struct DevIdx {
+    DBuf<int64_t> d;
+    void upload(const std::vector<int64_t>& v, cudaStream_t st) {
+        d.alloc(v.size());
+        if (!v.empty())
+            M3G_CK(cudaMemcpyAsync(d.p, v.data(), v.size() * 8, cudaMemcpyHostToDevice, st));
+    }
+};
+
+// Cluster::rebuild_from (cluster.cpp:152-178): full replace; later duplicates
+// of an id keep the first row in the map (unordered_map::emplace).
+void list_rebuild(Index& ix, int l, const int64_t* ids, const float* vecs, int64_t n) {
+    ListMeta& L = ix.lists[l];
+    if (n > L.cap) relocate(ix, l, std::max<int64_t>(n, 16), 0);
+    write_rows(ix, L.off, ids, vecs, n);
+    L.len = n;
+    L.live = n;
+    L.ids.assign(ids, ids + n);
+    L.alive.assign((size_t)n, 1);
+    L.id2row.clear();
+    L.id2row.reserve((size_t)n);
+    for (int64_t r = 0; r < n; ++r) L.id2row.emplace(ids[r], r);
+}
+
+// Cluster::add_batch (cluster.cpp:55-101).
+void list_add(Index& ix, int l, const int64_t* ids, const float* vecs, int64_t n) {
+    if (!ids || !vecs || n == 0) return;
+    ListMeta& L = ix.lists[l];
+    {
+        std::unordered_set<int64_t> seen;
+        seen.reserve((size_t)n * 2);
+        for (int64_t r = 0; r < n; ++r) {
+            if (!seen.insert(ids[r]).second)
+                fail(M3G_ERUNTIME, "Cluster::add_batch: duplicate id in batch");
+            if (L.id2row.count(ids[r])) fail(M3G_ERUNTIME, "Cluster::add_batch: duplicate id exists");
+        }
+    }
+    ensure_list_room(ix, l, L.len + n);
+    write_rows(ix, L.off + L.len, ids, vecs, n);
+    for (int64_t r = 0; r < n; ++r) {
+        L.id2row.emplace(ids[r], L.len + r);
+        L.ids.push_back(ids[r]);
+        L.alive.push_back(1);
+    }
+    L.len += n;
+    L.live += n;
+}
+
+// Cluster::update_batch (cluster.cpp:103-133): rows apply in order; a missing
+// id without insert_if_absent raises after the earlier rows were applied.
+void list_update(Index& ix, int l, const int64_t* ids, const float* vecs, int64_t n,
+                 bool insert_if_absent) {
+    if (!ids || !vecs || n == 0) return;
+    ListMeta& L = ix.lists[l];
+    std::unordered_map<int64_t, int64_t> dst_src;  // list row -> last source row
+    std::vector<int64_t> appended;                  // source rows appended, in order
+    bool missing = false;
+    int64_t r = 0;
+    for (; r < n; ++r) {
+        auto it = L.id2row.find(ids[r]);
+        if (it == L.id2row.end()) {
+            if (!insert_if_absent) {
+                missing = true;
+                break;
+            }
+            const int64_t row = L.len + (int64_t)appended.size();
+            appended.push_back(r);
+            L.id2row.emplace(ids[r], row);
+            dst_src[row] = r;
+        } else {
+            dst_src[it->second] = r;
+        }
+    }
+    const int64_t nappend = (int64_t)appended.size();
+    if (nappend) ensure_list_room(ix, l, L.len + nappend);
+    if (!dst_src.empty()) {
+        std::vector<int64_t> dst_rows;
+        std::vector<float> staging;
+        std::vector<int64_t> row_ids;
+        dst_rows.reserve(dst_src.size());
+        staging.reserve(dst_src.size() * ix.dim);
+        for (auto& kv : dst_src) {
+            dst_rows.push_back(L.off + kv.first);
+            staging.insert(staging.end(), vecs + kv.second * ix.dim, vecs + (kv.second + 1) * ix.dim);
+            row_ids.push_back(ids[kv.second]);
+        }
+        const int64_t m = (int64_t)dst_rows.size();
+        DBuf<float> d_src;
+        d_src.alloc((size_t)m * ix.dpad);
+        M3G_CK(cudaMemsetAsync(d_src.p, 0, (size_t)m * ix.dpad * 4, ix.wstream));
+        h2d_rows(d_src.p, ix.dpad, staging.data(), ix.dim, m, ix.wstream);
+        DevIdx di, dids;
+        di.upload(dst_rows, ix.wstream);
+        dids.upload(row_ids, ix.wstream);
+        M3G_CK(launch_scatter_rows(d_src.p, ix.dpad, di.d.p, m, ix.dpad, ix.vecs.p, ix.dpad, ix.wstream));
+        M3G_CK(launch_scatter_i64(dids.d.p, di.d.p, m, ix.ids.p, ix.wstream));
+        M3G_CK(launch_set_bytes(ix.alive.p, di.d.p, m, 1, ix.wstream));
+        // refresh the norms of the written rows
+        DBuf<float> nrm;
+        nrm.alloc((size_t)m);
+        launch_row_norms(d_src.p, ix.dpad, m, ix.dim, nullptr, nrm.p, ix.wstream);
+        M3G_CK(launch_scatter_rows(nrm.p, 1, di.d.p, m, 1, ix.rnorm2.p, 1, ix.wstream));
+        M3G_CK(cudaStreamSynchronize(ix.wstream));
+    }
+    for (int64_t i = 0; i < nappend; ++i) {
+        L.ids.push_back(ids[appended[i]]);
+        L.alive.push_back(1);
+    }
+    L.len += nappend;
+    L.live += nappend;
+    if (missing) fail(M3G_ERUNTIME, "Cluster::update_batch: id not found");
+}
+
+// Cluster::erase_batch (cluster.cpp:135-150).
+void list_erase(Index& ix, int l, const int64_t* ids, int64_t n) {
+    if (!ids || n == 0) return;
+    ListMeta& L = ix.lists[l];
+    std::vector<int64_t> rows;
+    for (int64_t r = 0; r < n; ++r) {
+        auto it = L.id2row.find(ids[r]);
+        if (it == L.id2row.end()) continue;
+        const int64_t row = it->second;
+        if (row < (int64_t)L.alive.size() && L.alive[row]) {
+            L.alive[row] = 0;
+            if (L.live > 0) --L.live;
+            rows.push_back(L.off + row);
+        }
+        L.id2row.erase(it);
+    }
+    if (!rows.empty()) {
+        DevIdx di;
+        di.upload(rows, ix.wstream);
+        M3G_CK(launch_set_bytes(ix.alive.p, di.d.p, (int64_t)rows.size(), 0, ix.wstream));
+        M3G_CK(cudaStreamSynchronize(ix.wstream));
+    }
+}
+
+// Moves the given rows of list l (list-relative, ascending) into a fresh
+// segment of list `dst_list` (which may be l itself), in that order.
+void regroup_rows(Index& ix, int l, const std::vector<int64_t>& rows, int dst_list) {
+    ListMeta& S = ix.lists[l];
+    const int64_t n = (int64_t)rows.size();
+    std::vector<int64_t> src_abs(rows.size());
+    for (size_t i = 0; i < rows.size(); ++i) src_abs[i] = S.off + rows[i];
+    std::vector<int64_t> new_ids(rows.size());
+    for (size_t i = 0; i < rows.size(); ++i) new_ids[i] = S.ids[rows[i]];
+    const int64_t cap = std::max<int64_t>(n, 16);
+    if (ix.arena_used + cap > ix.arena_cap) {
+        grow_arena(ix, cap);
+        for (size_t i = 0; i < rows.size(); ++i) src_abs[i] = ix.lists[l].off + rows[i];
+    }
+    const int64_t dst = ix.arena_used;
+    ix.arena_used += cap;
+    if (n > 0) {
+        DevIdx di;
+        di.upload(src_abs, ix.wstream);
+        M3G_CK(launch_gather_rows(ix.vecs.p, ix.dpad, di.d.p, n, ix.dpad, ix.vecs.p + dst * ix.dpad,
+                                  ix.dpad, ix.wstream));
+        M3G_CK(launch_gather_f32(ix.rnorm2.p, di.d.p, n, ix.rnorm2.p + dst, ix.wstream));
+        M3G_CK(launch_gather_i64(ix.ids.p, di.d.p, n, ix.ids.p + dst, ix.wstream));
+        M3G_CK(cudaMemsetAsync(ix.alive.p + dst, 1, (size_t)n, ix.wstream));
+        M3G_CK(cudaStreamSynchronize(ix.wstream));
+    }
+    ListMeta& D = ix.lists[dst_list];
+    D.off = dst;
+    D.cap = cap;
+    D.len = n;
+    D.live = n;
+    D.ids = std::move(new_ids);
+    D.alive.assign((size_t)n, 1);
+    D.id2row.clear();
+    for (int64_t r = 0; r < n; ++r) D.id2row.emplace(D.ids[r], r);
+}
+
+// Cluster::compact (cluster.cpp:276-309).
+void list_compact(Index& ix, int l) {
+    ListMeta& L = ix.lists[l];
+    if (L.len == 0 || L.live == L.len) return;
+    std::vector<int64_t> keep;
+    keep.reserve((size_t)L.live);
+    for (int64_t r = 0; r < L.len; ++r)
+        if (L.alive[r]) keep.push_back(r);
+    regroup_rows(ix, l, keep, l);
+}
+
+}  // namespace
+
+// ===================== Engine =====================
+
+Engine::Engine() {
+    cudaGetDevice(&device_);
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device_) == cudaSuccess && n > 0)
+        num_sms_ = n;
+    else
+        num_sms_ = kDefaultNsm;
+    cudaGetLastError();
+}
+
+Engine::~Engine() {
+    try {
+        stop();
+    } catch (...) {
+    }
+    DeviceGuard g(device_);
+    {
+        std::unique_lock lk(imu_);
+        indices_.clear();
+    }
+    if (ws_.stream) {
+        cudaStreamSynchronize(ws_.stream);
+        cudaStreamDestroy(ws_.stream);
+    }
+    if (ws_.done) cudaEventDestroy(ws_.done);
+    for (auto& e : ws_.ev)
+        if (e) cudaEventDestroy(e);
+    ws_.Q.release();
+    ws_.qn.release();
+    ws_.qn2.release();
+    ws_.S.release();
+    ws_.probes.release();
+    ws_.lcount.release();
+    ws_.lstart.release();
+    ws_.lcursor.release();
+    ws_.n_items.release();
+    ws_.item_counter.release();
+    ws_.pair_q.release();
+    ws_.pair_slot.release();
+    ws_.items.release();
+    ws_.part_score.release();
+    ws_.part_row.release();
+    ws_.out_ids.release();
+    ws_.out_scores.release();
+    ws_.out_counts.release();
+    ws_.err.release();
+    ws_.stats.release();
+}
+
+void Engine::set_device(int dev) {
+    int count = 0;
+    M3G_CK(cudaGetDeviceCount(&count));
+    if (dev < 0 || dev >= count) fail(M3G_EINVAL, "set_device: no such CUDA device");
+    std::shared_lock lk(imu_);
+    if (!indices_.empty() || ws_.stream) fail(M3G_ERUNTIME, "set_device: engine already in use");
+    device_ = dev;
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device_) == cudaSuccess && n > 0)
+        num_sms_ = n;
+}
+
+std::shared_ptr<Index> Engine::find(int index_id) const {
+    std::shared_lock lk(imu_);
+    auto it = indices_.find(index_id);
+    return it == indices_.end() ? nullptr : it->second;
+}
+
+std::shared_ptr<Index> Engine::get(int index_id, const char* who) const {
+    auto ix = find(index_id);
+    if (!ix) fail(M3G_ERANGE, std::string(who) + ": index not found");
+    return ix;
+}
+
+// ---------------- lifecycle: m3_async.cpp:53-105 ----------------
+
+void Engine::start(int writers, int maint) {
+    if (running_.exchange(true)) return;
+    for (int i = 0; i < writers; ++i) writers_.emplace_back([this] { writer_loop(); });
+    for (int i = 0; i < maint; ++i) maint_.emplace_back([this] { maintenance_loop(); });
+}
+
+void Engine::stop() {
+    if (!running_.exchange(false)) return;
+    {
+        std::lock_guard lk(qmu_);
+        q_not_empty_.notify_all();
+        q_not_full_.notify_all();
+    }
+    {
+        std::lock_guard lk(maint_mu_);
+        maint_cv_.notify_all();
+    }
+    for (auto& t : writers_) t.join();
+    writers_.clear();
+    for (auto& t : maint_) t.join();
+    maint_.clear();
+}
+
+// ---------------- index lifecycle ----------------
+
+void Engine::create_ivf(int index_id, int dim, int metric, bool normalized, const float* C,
+                        int64_t nlist) {
+    if (dim <= 0) fail(M3G_EINVAL, "IVFIndex: dim must be > 0");
+    if (metric < 0 || metric > 2) fail(M3G_EINVAL, "create_ivf: unknown metric");
+    if (nlist < 0 || (nlist > 0 && !C)) fail(M3G_EINVAL, "create_ivf: centroids missing");
+    if (nlist > (int64_t)INT32_MAX / 2) fail(M3G_EUNSUPPORTED, "create_ivf: too many lists");
+    DeviceGuard g(device_);
+    auto ix = std::make_shared<Index>();
+    ix->device = device_;
+    ix->dim = dim;
+    ix->dpad = round_up4(dim);
+    ix->metric = metric;
+    ix->normalized = normalized;
+    M3G_CK(cudaStreamCreateWithFlags(&ix->wstream, cudaStreamNonBlocking));
+    ix->centroids.assign(C, C + nlist * (int64_t)dim);
+    ix->lists.resize((size_t)nlist);
+    ensure_centroid_cap(*ix, (size_t)std::max<int64_t>(nlist, 1));
+    upload_centroids(*ix, 0, (int)nlist);
+    refresh_list_meta(*ix);
+    M3G_CK(cudaStreamSynchronize(ix->wstream));
+    std::shared_ptr<Index> old;
+    {
+        std::unique_lock lk(imu_);
+        auto& slot = indices_[index_id];
+        old = slot;
+        slot = ix;
+    }
+    if (old) {
+        std::unique_lock lk(old->mu);
+        if (ws_.done) cudaEventSynchronize(ws_.done);
+    }
+}
+
+void Engine::load_cluster(int index_id, int cid, const int64_t* ids, const float* vecs, int64_t n) {
+    auto ix = get(index_id, "AsyncEngine::load_cluster");
+    if (n < 0 || (n > 0 && (!ids || !vecs)))
+        fail(M3G_EINVAL, "AsyncEngine::load_cluster: vecs.size mismatch");
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (cid < 0 || cid >= ix->nlist())
+        fail(M3G_ERANGE, "IVFIndex::rebuild_cluster: invalid cluster_id");
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    list_rebuild(*ix, cid, ids, vecs, n);
+    refresh_list_meta(*ix);
+}
+
+// ---------------- queue: m3_async.cpp:123-201, 399-467 ----------------
+
+bool Engine::enqueue(WriteOp&& op) {
+    std::unique_lock lk(qmu_);
+    while (running_ && queue_.size() >= qpol_.capacity) {
+        if (!qpol_.block_on_full) return false;
+        q_not_full_.wait(lk);
+    }
+    if (!running_) return false;
+    queue_.emplace_back(std::move(op));
+    ++enqueued_;
+    q_not_empty_.notify_one();
+    return true;
+}
+
+void Engine::flush() {
+    {
+        std::unique_lock lk(qmu_);
+        while (running_ && (!queue_.empty() || applied_.load() < enqueued_.load()))
+            q_not_full_.wait(lk);
+    }
+    std::lock_guard lk(err_mu_);
+    if (first_error_code_) {
+        const int code = first_error_code_;
+        const std::string msg = first_error_;
+        first_error_code_ = 0;
+        first_error_.clear();
+        fail(code, "write failed in a writer thread: " + msg);
+    }
+}
+
+void Engine::record_error(const std::string& msg, int code) {
+    std::lock_guard lk(err_mu_);
+    if (!first_error_code_) {
+        first_error_code_ = code;
+        first_error_ = msg;
+    }
+}
+
+void Engine::apply(const WriteOp& op) {
+    auto ix = find(op.index_id);
+    if (!ix) fail(M3G_ERANGE, "writer: index " + std::to_string(op.index_id) + " not found");
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (op.cluster_id < 0 || op.cluster_id >= ix->nlist()) {
+        const char* w = op.kind == WriteOp::kInsert   ? "IVFIndex::add_batch: invalid cluster_id"
+                        : op.kind == WriteOp::kUpdate ? "IVFIndex::update_batch: invalid cluster_id"
+                                                      : "IVFIndex::erase_batch: invalid cluster_id";
+        fail(M3G_ERANGE, w);
+    }
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    const int64_t n = (int64_t)op.ids.size();
+    struct MetaRefresh {
+        Index& ix;
+        ~MetaRefresh() {
+            try {
+                refresh_list_meta(ix);
+            } catch (...) {
+            }
+        }
+    } refresh{*ix};
+    switch (op.kind) {
+        case WriteOp::kInsert:
+            list_add(*ix, op.cluster_id, op.ids.data(), op.vecs.data(), n);
+            break;
+        case WriteOp::kUpdate:
+            list_update(*ix, op.cluster_id, op.ids.data(), op.vecs.data(), n, op.insert_if_absent);
+            break;
+        case WriteOp::kDelete:
+            list_erase(*ix, op.cluster_id, op.ids.data(), n);
+            break;
+    }
+}
+
+void Engine::writer_loop() {
+    std::vector<WriteOp> batch;
+    while (running_) {
+        batch.clear();
+        {
+            std::unique_lock lk(qmu_);
+            while (queue_.empty() && running_) q_not_empty_.wait(lk);
+            if (!running_) break;
+            const size_t m = std::min(qpol_.pop_batch_max ? qpol_.pop_batch_max : 1, queue_.size());
+            for (size_t i = 0; i < m; ++i) {
+                batch.push_back(std::move(queue_.front()));
+                queue_.pop_front();
+            }
+            q_not_full_.notify_all();
+        }
+        for (auto& op : batch) {
+            try {
+                apply(op);
+            } catch (const Error& e) {
+                record_error(e.what(), e.code);
+            } catch (const std::exception& e) {
+                record_error(e.what(), M3G_ERUNTIME);
+            }
+            ++applied_;
+        }
+        std::lock_guard lk(qmu_);
+        q_not_full_.notify_all();
+    }
+}
+
+void Engine::maintenance_loop() {
+    while (running_) {
+        {
+            std::unique_lock lk(maint_mu_);
+            const double p = mpol_.period_sec > 0.0 ? mpol_.period_sec : 1.0;
+            maint_cv_.wait_for(lk, std::chrono::duration<double>(p), [this] { return !running_; });
+        }
+        if (!running_) break;
+        std::vector<int> ids;
+        {
+            std::shared_lock lk(imu_);
+            for (auto& kv : indices_) ids.push_back(kv.first);
+        }
+        for (int id : ids) {
+            try {
+                maintenance_pass(id);
+            } catch (const Error& e) {
+                record_error(e.what(), e.code);
+            } catch (const std::exception& e) {
+                record_error(e.what(), M3G_ERUNTIME);
+            }
+        }
+    }
+}
+
+// IVFIndex::maintenance_pass (m3_index.cpp:278-312): compact lists whose live
+// fraction fell below compact_ratio; optionally split oversized lists.
+void Engine::maintenance_pass(int index_id) {
+    auto ix = find(index_id);
+    if (!ix) return;
+    std::vector<int> to_split;
+    {
+        DeviceGuard g(device_);
+        std::unique_lock lk(ix->mu);
+        if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+        bool changed = false;
+        for (int l = 0; l < ix->nlist(); ++l) {
+            ListMeta& L = ix->lists[l];
+            if (L.len == 0) continue;
+            if ((double)L.live / (double)L.len < mpol_.compact_ratio) {
+                list_compact(*ix, l);
+                changed = true;
+            }
+            if (mpol_.auto_split && (size_t)L.live > mpol_.split_threshold) to_split.push_back(l);
+        }
+        if (changed) refresh_list_meta(*ix);
+    }
+    for (int l : to_split) split_cluster(index_id, l, 5, 0x5eed0000ull + (uint64_t)l);
+}
+
+void Engine::compact_cluster(int index_id, int cid) {
+    auto ix = find(index_id);
+    if (!ix) return;
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (cid < 0 || cid >= ix->nlist()) return;
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    list_compact(*ix, cid);
+    refresh_list_meta(*ix);
+}
+
+// ---------------- info ----------------
+
+void Engine::info(int index_id, int* dim, int* metric, int* normalized, int* nlist) {
+    auto ix = find(index_id);
+    if (!ix) {  // m3_async.cpp:317-351 defaults
+        if (dim) *dim = 0;
+        if (metric) *metric = M3G_COSINE;
+        if (normalized) *normalized = 1;
+        if (nlist) *nlist = 0;
+        return;
+    }
+    std::shared_lock lk(ix->mu);
+    if (dim) *dim = ix->dim;
+    if (metric) *metric = ix->metric;
+    if (normalized) *normalized = ix->normalized ? 1 : 0;
+    if (nlist) *nlist = ix->nlist();
+}
+
+void Engine::cluster_size(int index_id, int cid, int64_t* size, int64_t* live) {
+    auto ix = get(index_id, "cluster_size");
+    std::shared_lock lk(ix->mu);
+    if (cid < 0 || cid >= ix->nlist()) fail(M3G_ERANGE, "cluster_size: invalid cluster_id");
+    if (size) *size = ix->lists[cid].len;
+    if (live) *live = ix->lists[cid].live;
+}
+
+void Engine::get_centroids(int index_id, float* out) {
+    auto ix = get(index_id, "get_centroids");
+    std::shared_lock lk(ix->mu);
+    std::copy(ix->centroids.begin(), ix->centroids.end(), out);
+}
+
+int Engine::add_cluster(int index_id, const float* c) {
+    auto ix = get(index_id, "IVFIndex::add_cluster");
+    if (!c) fail(M3G_EINVAL, "IVFIndex::add_cluster: centroid dim mismatch");
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    const int cid = ix->nlist();
+    ensure_centroid_cap(*ix, (size_t)cid + 1);
+    ix->centroids.insert(ix->centroids.end(), c, c + ix->dim);
+    ix->lists.emplace_back();
+    upload_centroids(*ix, cid, 1);
+    refresh_list_meta(*ix);
+    return cid;
+}
+
+void Engine::set_centroid(int index_id, int cid, const float* c) {
+    auto ix = get(index_id, "IVFIndex::set_centroid");
+    if (!c) fail(M3G_EINVAL, "IVFIndex::set_centroid: centroid dim mismatch");
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (cid < 0 || cid >= ix->nlist()) fail(M3G_ERANGE, "IVFIndex::set_centroid: invalid cluster_id");
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    std::copy(c, c + ix->dim, ix->centroids.begin() + (size_t)cid * ix->dim);
+    upload_centroids(*ix, cid, 1);
+    M3G_CK(cudaStreamSynchronize(ix->wstream));
+}
+
+// ---------------- search pipeline ----------------
+
+namespace {
+constexpr int64_t kMaxChunkQueries = 8192;
+constexpr int64_t kMaxScoreEntries = int64_t(1) << 26;  // nq * L per chunk
+constexpr int64_t kMaxPartEntries = int64_t(1) << 25;   // nq * P * k per chunk
+constexpr int64_t kMaxAssignRows = int64_t(1) << 22;    // GEMM grid.y stays < 65536
+
+float gamma_of(int D) { return (float)(D + 4) * 5.9604645e-8f * 1.01f; }
+}  // namespace
+
+// Runs one query chunk whose queries (rows of dQ, stride ldq >= dpad, zero padded)
+// are on the device.  fixed_probes: if non-null, [nq, P] probe lists already on
+// the device (skips the coarse step).  Outputs [nq, k] / [nq] on the device.
+void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int k, int P,
+                        const int32_t* fixed_probes, int64_t* d_ids, float* d_scores,
+                        int32_t* d_counts, cudaStream_t st, bool profile) {
+    Workspace& w = ws_;
+    const int L = ix.nlist();
+    const int D = ix.dim;
+    cudaEvent_t* ev = w.ev;
+    if (profile) M3G_CK(cudaEventRecord(ev[0], st));
+    launch_row_norms(dQ, ldq, nq, D, w.qn.p, w.qn2.p, st);
+    M3G_CK(cudaGetLastError());
+    if (profile) M3G_CK(cudaEventRecord(ev[1], st));
+    const int32_t* probes = fixed_probes;
+    if (!probes) {
+        if (P >= L) {
+            M3G_CK(launch_iota_rows(w.probes.p, nq, P, st));
+            if (profile) M3G_CK(cudaEventRecord(ev[2], st));
+        } else {
+            launch_sgemm_nt(dQ, ldq, ix.C.p, ix.dpad, w.S.p, L, (int)nq, L, ix.dpad, st);
+            M3G_CK(cudaGetLastError());
+            if (profile) M3G_CK(cudaEventRecord(ev[2], st));
+            M3G_CK(launch_select_probes(w.S.p, L, dQ, ldq, ix.C.p, ix.dpad, w.qn.p, w.qn2.p, ix.cn.p,
+                                        ix.cn2.p, (int)nq, L, D, ix.metric, ix.normalized ? 1 : 0,
+                                        sgemm_error_beta(ix.dpad), gamma_of(D), P, 0, w.probes.p,
+                                        st));
+        }
+        probes = w.probes.p;
+    } else if (profile) {
+        M3G_CK(cudaEventRecord(ev[2], st));
+    }
+    if (profile) M3G_CK(cudaEventRecord(ev[3], st));
+    const int gmax = scan_gmax_for_dim(ix.dpad);
+    if (gmax <= 0) fail(M3G_EUNSUPPORTED, "search: dimension too large for the list scan");
+    M3G_CK(launch_build_worklist(probes, (int)nq, P, L, ix.d_list_order.p, gmax, w.lcount.p,
+                                 w.lstart.p, w.lcursor.p, w.items.p, w.n_items.p, w.pair_q.p,
+                                 w.pair_slot.p, st));
+    if (profile) {
+        M3G_CK(cudaMemsetAsync(w.stats.p, 0, 2 * sizeof(unsigned long long), st));
+        M3G_CK(launch_probed_rows(w.lcount.p, ix.d_list_len.p, L, w.stats.p, w.stats.p + 1, st));
+        M3G_CK(cudaEventRecord(ev[4], st));
+    }
+    M3G_CK(cudaMemsetAsync(w.item_counter.p, 0, sizeof(int32_t), st));
+    ScanArgs a{};
+    a.Q = dQ;
+    a.dpad = (int)ldq;
+    a.list_off = ix.d_list_off.p;
+    a.list_len = ix.d_list_len.p;
+    a.alive = ix.alive.p;
+    a.rnorm2 = ix.rnorm2.p;
+    a.qnorm2 = w.qn2.p;
+    a.items = w.items.p;
+    a.n_items = w.n_items.p;
+    a.item_counter = w.item_counter.p;
+    a.pair_q = w.pair_q.p;
+    a.pair_slot = w.pair_slot.p;
+    a.k = k;
+    a.P = P;
+    a.metric = ix.metric;
+    a.normalized = ix.normalized ? 1 : 0;
+    a.part_score = w.part_score.p;
+    a.part_row = w.part_row.p;
+    a.err = w.err.p;
+    const int grid = (int)std::min<int64_t>(num_sms_, std::max<int64_t>(1, nq * P));
+    if (ix.maps_valid) {
+        M3G_CK(launch_list_scan(ix.maps, a, gmax, grid, st));
+    } else {
+        // empty arena: every partial list is empty
+        M3G_CK(cudaMemsetAsync(w.part_row.p, 0xff, sizeof(int64_t) * (size_t)(nq * P * k), st));
+        std::vector<float> inf((size_t)(nq * P * k), INFINITY);
+        M3G_CK(cudaMemcpyAsync(w.part_score.p, inf.data(), inf.size() * 4, cudaMemcpyHostToDevice, st));
+        M3G_CK(cudaStreamSynchronize(st));
+    }
+    if (profile) M3G_CK(cudaEventRecord(ev[5], st));
+    M3G_CK(launch_merge_topk(w.part_score.p, w.part_row.p, ix.ids.p, (int)nq, P, k, d_ids, d_scores,
+                             d_counts, st));
+    if (profile) M3G_CK(cudaEventRecord(ev[6], st));
+    // kernels launched: norms, coarse (gemm + select, or iota), 3 work-list
+    // kernels, scan, merge (+ the byte counter when profiling)
+    int launches = 1 + (fixed_probes ? 0 : (P >= L ? 1 : 2)) + 3 + (ix.maps_valid ? 1 : 0) + 1;
+    if (profile) launches += 1;
+    last_launches_ += launches;
+}
+
+namespace {
+struct WsSizes {
+    int64_t nq, L, P, k, dpad;
+};
+template <class T>
+bool short_of(const DBuf<T>& b, int64_t n) {
+    return (size_t)n > b.n;
+}
+bool ws_needs_grow(const Workspace& w, const WsSizes& s) {
+    return !w.err.p || short_of(w.Q, s.nq * s.dpad) || short_of(w.qn, s.nq) ||
+           short_of(w.S, s.nq * s.L) || short_of(w.probes, s.nq * s.P) || short_of(w.lcount, s.L) ||
+           short_of(w.lstart, s.L) || short_of(w.lcursor, s.L) || short_of(w.pair_q, s.nq * s.P) ||
+           short_of(w.pair_slot, s.nq * s.P) || short_of(w.items, s.nq * s.P) ||
+           short_of(w.part_score, s.nq * s.P * s.k) || short_of(w.part_row, s.nq * s.P * s.k) ||
+           short_of(w.out_ids, s.nq * s.k) || short_of(w.out_scores, s.nq * s.k) ||
+           short_of(w.out_counts, s.nq);
+}
+void ensure_ws(Workspace& w, const WsSizes& s) {
+    if (!w.err.p) {
+        w.err.alloc(1);
+        M3G_CK(cudaMemset(w.err.p, 0, sizeof(int)));
+        w.stats.alloc(2);
+        w.n_items.alloc(1);
+        w.item_counter.alloc(1);
+    }
+    w.Q.ensure((size_t)(s.nq * s.dpad));
+    w.qn.ensure((size_t)s.nq);
+    w.qn2.ensure((size_t)s.nq);
+    w.S.ensure((size_t)(s.nq * s.L));
+    w.probes.ensure((size_t)(s.nq * s.P));
+    w.lcount.ensure((size_t)s.L);
+    w.lstart.ensure((size_t)s.L);
+    w.lcursor.ensure((size_t)s.L);
+    w.pair_q.ensure((size_t)(s.nq * s.P));
+    w.pair_slot.ensure((size_t)(s.nq * s.P));
+    w.items.ensure((size_t)(s.nq * s.P));
+    w.part_score.ensure((size_t)(s.nq * s.P * s.k));
+    w.part_row.ensure((size_t)(s.nq * s.P * s.k));
+    w.out_ids.ensure((size_t)(s.nq * s.k));
+    w.out_scores.ensure((size_t)(s.nq * s.k));
+    w.out_counts.ensure((size_t)s.nq);
+}
+
+int64_t chunk_queries(int64_t nq, int L, int P, int k) {
+    int64_t c = std::min<int64_t>(nq, kMaxChunkQueries);
+    c = std::min<int64_t>(c, std::max<int64_t>(1, kMaxScoreEntries / std::max(L, 1)));
+    c = std::min<int64_t>(c, std::max<int64_t>(1, kMaxPartEntries / std::max<int64_t>(1, (int64_t)P * k)));
+    return std::max<int64_t>(c, 1);
+}
+}  // namespace
+
+void Engine::acquire_ws(cudaStream_t st, int64_t nq, int64_t L, int64_t P, int64_t k,
+                        int64_t dpad) {
+    if (!ws_.stream) {
+        M3G_CK(cudaStreamCreateWithFlags(&ws_.stream, cudaStreamNonBlocking));
+        M3G_CK(cudaEventCreateWithFlags(&ws_.done, cudaEventDisableTiming));
+        for (auto& e : ws_.ev) M3G_CK(cudaEventCreate(&e));
+        M3G_CK(cudaEventRecord(ws_.done, ws_.stream));
+    }
+    if (!st) st = ws_.stream;
+    const WsSizes sz{nq, L, P, k, dpad};
+    if (ws_needs_grow(ws_, sz)) {
+        M3G_CK(cudaEventSynchronize(ws_.done));
+        ensure_ws(ws_, sz);
+    } else if (st != ws_.last_stream) {
+        M3G_CK(cudaStreamWaitEvent(st, ws_.done, 0));
+    }
+    ws_.last_stream = st;
+}
+
+void Engine::search(int index_id, const float* Q, int64_t nq, int k, int nprobe, bool q_dev,
+                    int64_t* out_ids, float* out_scores, int32_t* out_counts, bool out_dev,
+                    cudaStream_t ext_stream) {
+    if (nq < 0) fail(M3G_EINVAL, "search: nq < 0");
+    auto ix = find(index_id);
+    DeviceGuard g(device_);
+    // m3_async.cpp:224 then m3_index.cpp:372-388
+    int use_nprobe = nprobe > 0 ? nprobe : spol_.default_nprobe;
+    auto write_empty = [&](int64_t n) {
+        if (n <= 0 || k <= 0) {
+            if (n > 0) {
+                if (out_dev) M3G_CK(cudaMemsetAsync(out_counts, 0, n * 4, ext_stream));
+                else std::fill(out_counts, out_counts + n, 0);
+            }
+            return;
+        }
+        std::vector<int64_t> ids((size_t)(n * k), -1);
+        std::vector<float> sc((size_t)(n * k), INFINITY);
+        std::vector<int32_t> cn((size_t)n, 0);
+        if (out_dev) {
+            M3G_CK(cudaMemcpyAsync(out_ids, ids.data(), ids.size() * 8, cudaMemcpyHostToDevice, ext_stream));
+            M3G_CK(cudaMemcpyAsync(out_scores, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice, ext_stream));
+            M3G_CK(cudaMemcpyAsync(out_counts, cn.data(), cn.size() * 4, cudaMemcpyHostToDevice, ext_stream));
+            M3G_CK(cudaStreamSynchronize(ext_stream));
+        } else {
+            std::copy(ids.begin(), ids.end(), out_ids);
+            std::copy(sc.begin(), sc.end(), out_scores);
+            std::copy(cn.begin(), cn.end(), out_counts);
+        }
+    };
+    if (!ix || nq == 0 || k <= 0) {
+        write_empty(nq);
+        return;
+    }
+    if (!Q) fail(M3G_EINVAL, "search: queries missing");
+    if (k > scan_kmax())
+        fail(M3G_EUNSUPPORTED, "search: k > " + std::to_string(scan_kmax()) + " is not supported");
+    std::shared_lock lk(ix->mu);
+    const int L = ix->nlist();
+    if (L == 0) {
+        write_empty(nq);
+        return;
+    }
+    if (use_nprobe <= 0) use_nprobe = L;
+    const int P = std::min(use_nprobe, L);
+    const int64_t ch = chunk_queries(nq, L, P, k);
+    std::lock_guard wl(ws_.mu);
+    acquire_ws(ext_stream, ch, L, P, k, ix->dpad);
+    cudaStream_t st = ext_stream ? ext_stream : ws_.stream;
+    const bool profile = profiling_.load() && !ext_stream;
+    last_launches_ = 0;
+    const bool direct_q = q_dev && ix->dpad == ix->dim && (reinterpret_cast<uintptr_t>(Q) & 15u) == 0;
+    for (int64_t q0 = 0; q0 < nq; q0 += ch) {
+        const int64_t m = std::min(ch, nq - q0);
+        const float* dQ;
+        if (direct_q) {
+            dQ = Q + q0 * ix->dim;
+        } else {
+            if (ix->dpad != ix->dim)
+                M3G_CK(cudaMemsetAsync(ws_.Q.p, 0, (size_t)(m * ix->dpad) * 4, st));
+            M3G_CK(cudaMemcpy2DAsync(ws_.Q.p, (size_t)ix->dpad * 4, Q + q0 * ix->dim,
+                                     (size_t)ix->dim * 4, (size_t)ix->dim * 4, (size_t)m,
+                                     q_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+            dQ = ws_.Q.p;
+        }
+        int64_t* oi = out_dev ? out_ids + q0 * k : ws_.out_ids.p;
+        float* os = out_dev ? out_scores + q0 * k : ws_.out_scores.p;
+        int32_t* oc = out_dev ? out_counts + q0 : ws_.out_counts.p;
+        run_search(*ix, dQ, ix->dpad, m, k, P, nullptr, oi, os, oc, st, profile && q0 == 0 && m == nq);
+        if (!out_dev) {
+            M3G_CK(cudaMemcpyAsync(out_ids + q0 * k, oi, (size_t)(m * k) * 8, cudaMemcpyDeviceToHost, st));
+            M3G_CK(cudaMemcpyAsync(out_scores + q0 * k, os, (size_t)(m * k) * 4, cudaMemcpyDeviceToHost, st));
+            M3G_CK(cudaMemcpyAsync(out_counts + q0, oc, (size_t)m * 4, cudaMemcpyDeviceToHost, st));
+        }
+    }
+    M3G_CK(cudaEventRecord(ws_.done, st));
+    if (profile) {
+        prof_pending_ = true;
+        prof_.kernel_launches = last_launches_;
+        prof_row_bytes_ = (int64_t)ix->dim * 4;
+        prof_dim_ = ix->dim;
+        prof_.nq = (int32_t)nq;
+        prof_.nprobe = P;
+        prof_.k = k;
+    }
+    if (!ext_stream) {
+        M3G_CK(cudaStreamSynchronize(st));
+        int err = 0;
+        M3G_CK(cudaMemcpy(&err, ws_.err.p, sizeof(int), cudaMemcpyDeviceToHost));
+        if (err) {
+            M3G_CK(cudaMemset(ws_.err.p, 0, sizeof(int)));
+            fail(M3G_ETIMEOUT, "search: a device-side wait gave up (kernel error " + std::to_string(err) + ")");
+        }
+    }
+}
+
+void Engine::sync_errors() {
+    DeviceGuard g(device_);
+    std::lock_guard wl(ws_.mu);
+    if (!ws_.stream) return;
+    M3G_CK(cudaEventSynchronize(ws_.done));
+    int err = 0;
+    M3G_CK(cudaMemcpy(&err, ws_.err.p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) {
+        M3G_CK(cudaMemset(ws_.err.p, 0, sizeof(int)));
+        fail(M3G_ETIMEOUT, "search: a device-side wait gave up (kernel error " + std::to_string(err) + ")");
+    }
+}
+
+m3g_profile Engine::last_profile() {
+    DeviceGuard g(device_);
+    std::lock_guard wl(ws_.mu);
+    if (!prof_pending_) return prof_;
+    M3G_CK(cudaEventSynchronize(ws_.done));
+    float t[6];
+    for (int i = 0; i < 6; ++i) M3G_CK(cudaEventElapsedTime(&t[i], ws_.ev[i], ws_.ev[i + 1]));
+    prof_.ms_prep = t[0];
+    prof_.ms_coarse_gemm = t[1];
+    prof_.ms_select = t[2];
+    prof_.ms_worklist = t[3];
+    prof_.ms_scan = t[4];
+    prof_.ms_merge = t[5];
+    M3G_CK(cudaEventElapsedTime(&prof_.ms_total, ws_.ev[0], ws_.ev[6]));
+    unsigned long long st[2];
+    M3G_CK(cudaMemcpy(st, ws_.stats.p, sizeof(st), cudaMemcpyDeviceToHost));
+    // algorithmic bytes: every probed list read once, the queries, the results
+    prof_.scan_bytes = (int64_t)st[0] * prof_row_bytes_ + (int64_t)prof_.nq * prof_dim_ * 4 +
+                       (int64_t)prof_.nq * prof_.k * 12;
+    prof_.probed_pairs = (int64_t)st[1];
+    prof_pending_ = false;
+    return prof_;
+}
+
+void Engine::search_on(int index_id, const int32_t* cids, int ncids, const float* Q, int64_t nq,
+                       int k, int64_t* out_ids, float* out_scores, int32_t* out_counts) {
+    auto ix = find(index_id);
+    DeviceGuard g(device_);
+    if (!ix || nq <= 0 || k <= 0 || ncids <= 0) {
+        for (int64_t i = 0; i < nq; ++i) {
+            out_counts[i] = 0;
+            for (int j = 0; j < k; ++j) {
+                out_ids[i * k + j] = -1;
+                out_scores[i * k + j] = INFINITY;
+            }
+        }
+        return;
+    }
+    if (k > scan_kmax())
+        fail(M3G_EUNSUPPORTED, "search_on: k > " + std::to_string(scan_kmax()) + " is not supported");
+    std::shared_lock lk(ix->mu);
+    const int L = ix->nlist();
+    std::vector<int32_t> keep;  // m3_index.cpp:338-341: out-of-range ids are skipped
+    for (int i = 0; i < ncids; ++i)
+        if (cids[i] >= 0 && cids[i] < L) keep.push_back(cids[i]);
+    if (keep.empty()) {
+        for (int64_t i = 0; i < nq; ++i) {
+            out_counts[i] = 0;
+            for (int j = 0; j < k; ++j) {
+                out_ids[i * k + j] = -1;
+                out_scores[i * k + j] = INFINITY;
+            }
+        }
+        return;
+    }
+    const int P = (int)keep.size();
+    const int64_t ch = chunk_queries(nq, L, P, k);
+    std::lock_guard wl(ws_.mu);
+    acquire_ws(nullptr, ch, L, P, k, ix->dpad);
+    cudaStream_t st = ws_.stream;
+    DBuf<int32_t> row;
+    row.alloc((size_t)P);
+    M3G_CK(cudaMemcpyAsync(row.p, keep.data(), (size_t)P * 4, cudaMemcpyHostToDevice, st));
+    for (int64_t q0 = 0; q0 < nq; q0 += ch) {
+        const int64_t m = std::min(ch, nq - q0);
+        if (ix->dpad != ix->dim) M3G_CK(cudaMemsetAsync(ws_.Q.p, 0, (size_t)(m * ix->dpad) * 4, st));
+        M3G_CK(cudaMemcpy2DAsync(ws_.Q.p, (size_t)ix->dpad * 4, Q + q0 * ix->dim, (size_t)ix->dim * 4,
+                                 (size_t)ix->dim * 4, (size_t)m, cudaMemcpyHostToDevice, st));
+        M3G_CK(launch_broadcast_row(row.p, P, m, ws_.probes.p, st));
+        run_search(*ix, ws_.Q.p, ix->dpad, m, k, P, ws_.probes.p, ws_.out_ids.p, ws_.out_scores.p,
+                   ws_.out_counts.p, st, false);
+        M3G_CK(cudaMemcpyAsync(out_ids + q0 * k, ws_.out_ids.p, (size_t)(m * k) * 8, cudaMemcpyDeviceToHost, st));
+        M3G_CK(cudaMemcpyAsync(out_scores + q0 * k, ws_.out_scores.p, (size_t)(m * k) * 4, cudaMemcpyDeviceToHost, st));
+        M3G_CK(cudaMemcpyAsync(out_counts + q0, ws_.out_counts.p, (size_t)m * 4, cudaMemcpyDeviceToHost, st));
+    }
+    M3G_CK(cudaEventRecord(ws_.done, st));
+    M3G_CK(cudaStreamSynchronize(st));
+    int err = 0;
+    M3G_CK(cudaMemcpy(&err, ws_.err.p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) {
+        M3G_CK(cudaMemset(ws_.err.p, 0, sizeof(int)));
+        fail(M3G_ETIMEOUT, "search_on: a device-side wait gave up");
+    }
+}
+
+void Engine::select_probes(int index_id, const float* Q, int64_t nq, int nprobe, int32_t* out) {
+    auto ix = get(index_id, "select_probes");
+    DeviceGuard g(device_);
+    std::shared_lock lk(ix->mu);
+    const int L = ix->nlist();
+    if (nq <= 0 || L == 0 || nprobe == 0) return;
+    const int P = nprobe < 0 ? L : std::min(nprobe, L);
+    const int64_t ch = chunk_queries(nq, L, P, 1);
+    std::lock_guard wl(ws_.mu);
+    acquire_ws(nullptr, ch, L, P, 1, ix->dpad);
+    cudaStream_t st = ws_.stream;
+    for (int64_t q0 = 0; q0 < nq; q0 += ch) {
+        const int64_t m = std::min(ch, nq - q0);
+        if (ix->dpad != ix->dim) M3G_CK(cudaMemsetAsync(ws_.Q.p, 0, (size_t)(m * ix->dpad) * 4, st));
+        M3G_CK(cudaMemcpy2DAsync(ws_.Q.p, (size_t)ix->dpad * 4, Q + q0 * ix->dim, (size_t)ix->dim * 4,
+                                 (size_t)ix->dim * 4, (size_t)m, cudaMemcpyHostToDevice, st));
+        launch_row_norms(ws_.Q.p, ix->dpad, m, ix->dim, ws_.qn.p, ws_.qn2.p, st);
+        if (P >= L) {
+            M3G_CK(launch_iota_rows(ws_.probes.p, m, P, st));
+        } else {
+            launch_sgemm_nt(ws_.Q.p, ix->dpad, ix->C.p, ix->dpad, ws_.S.p, L, (int)m, L, ix->dpad, st);
+            M3G_CK(launch_select_probes(ws_.S.p, L, ws_.Q.p, ix->dpad, ix->C.p, ix->dpad, ws_.qn.p,
+                                        ws_.qn2.p, ix->cn.p, ix->cn2.p, (int)m, L, ix->dim,
+                                        ix->metric, ix->normalized ? 1 : 0,
+                                        sgemm_error_beta(ix->dpad), gamma_of(ix->dim), P, 0,
+                                        ws_.probes.p, st));
+        }
+        M3G_CK(cudaMemcpyAsync(out + q0 * P, ws_.probes.p, (size_t)(m * P) * 4, cudaMemcpyDeviceToHost, st));
+    }
+    M3G_CK(cudaEventRecord(ws_.done, st));
+    M3G_CK(cudaStreamSynchronize(st));
+}
+
+// Exact nearest-centroid assignment of n device rows (P = 1 selection).
+void Engine::assign_rows(Index& ix, const float* dX, int64_t ld, const float* xn, const float* xn2,
+                         int64_t n, int32_t* d_out, cudaStream_t st) {
+    const int L = ix.nlist();
+    const int64_t ch = std::max<int64_t>(
+        1, std::min<int64_t>({n, kMaxScoreEntries / std::max(L, 1), kMaxAssignRows}));
+    DBuf<float> S;
+    S.alloc((size_t)(std::min(ch, n) * L));
+    for (int64_t r0 = 0; r0 < n; r0 += ch) {
+        const int64_t m = std::min(ch, n - r0);
+        launch_sgemm_nt(dX + r0 * ld, ld, ix.C.p, ix.dpad, S.p, L, (int)m, L, ix.dpad, st);
+        M3G_CK(cudaGetLastError());
+        M3G_CK(launch_select_probes(S.p, L, dX + r0 * ld, ld, ix.C.p, ix.dpad, xn + r0, xn2 + r0,
+                                    ix.cn.p, ix.cn2.p, (int)m, L, ix.dim, ix.metric,
+                                    ix.normalized ? 1 : 0, sgemm_error_beta(ix.dpad),
+                                    gamma_of(ix.dim), 1, 1, d_out + r0, st));
+    }
+    M3G_CK(cudaStreamSynchronize(st));
+}
+
+void Engine::nearest_clusters(int index_id, const float* vecs, int64_t n, int32_t* out) {
+    auto ix = get(index_id, "nearest_clusters");
+    DeviceGuard g(device_);
+    if (n <= 0) return;
+    std::shared_lock lk(ix->mu);
+    const int L = ix->nlist();
+    if (L == 0) {
+        std::fill(out, out + n, -1);
+        return;
+    }
+    cudaStream_t st;
+    M3G_CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    struct StreamGuard {
+        cudaStream_t s;
+        ~StreamGuard() { cudaStreamDestroy(s); }
+    } sg{st};
+    DBuf<float> X, xn, xn2;
+    DBuf<int32_t> a;
+    X.alloc((size_t)(n * ix->dpad));
+    xn.alloc((size_t)n);
+    xn2.alloc((size_t)n);
+    a.alloc((size_t)n);
+    if (ix->dpad != ix->dim) M3G_CK(cudaMemsetAsync(X.p, 0, (size_t)(n * ix->dpad) * 4, st));
+    h2d_rows(X.p, ix->dpad, vecs, ix->dim, n, st);
+    launch_row_norms(X.p, ix->dpad, n, ix->dim, xn.p, xn2.p, st);
+    assign_rows(*ix, X.p, ix->dpad, xn.p, xn2.p, n, a.p, st);
+    M3G_CK(cudaMemcpyAsync(out, a.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    M3G_CK(cudaStreamSynchronize(st));
+}
+
+// m3_async.cpp:262-313, clusters enqueued in ascending id order.
+bool Engine::enqueue_insert_auto(int index_id, const int64_t* ids, const float* vecs, int64_t n) {
+    auto ix = get(index_id, "AsyncEngine::enqueue_insert_auto");
+    if (n == 0) return true;
+    if (n < 0 || !ids || !vecs)
+        fail(M3G_EINVAL, "AsyncEngine::enqueue_insert_auto: vecs size mismatch");
+    std::vector<int32_t> assign((size_t)n);
+    nearest_clusters(index_id, vecs, n, assign.data());
+    const int dim = ix->dim;
+    std::vector<int> order;
+    std::unordered_map<int, WriteOp> per;
+    for (int64_t i = 0; i < n; ++i) {
+        const int c = assign[(size_t)i];
+        if (c < 0) fail(M3G_ERUNTIME, "AsyncEngine::enqueue_insert_auto: unable to assign cluster");
+        auto [it, ins] = per.emplace(c, WriteOp{});
+        if (ins) {
+            it->second.kind = WriteOp::kInsert;
+            it->second.index_id = index_id;
+            it->second.cluster_id = c;
+            order.push_back(c);
+        }
+        it->second.ids.push_back(ids[i]);
+        it->second.vecs.insert(it->second.vecs.end(), vecs + i * dim, vecs + (i + 1) * dim);
+    }
+    std::sort(order.begin(), order.end());
+    bool ok = true;
+    for (int c : order)
+        if (!enqueue(std::move(per[c]))) ok = false;
+    return ok;
+}
+
+// ---------------- k-means / split ----------------
+
+namespace {
+// Device k-means over n rows of X (device, stride ld, zero padded to dpad).
+// C (device, [nlist, dpad]) holds the start centroids and returns the result.
+void kmeans_device(const float* X, int64_t ld, int64_t n, int dim, int dpad, int metric,
+                   bool normalized, int nlist, int niter, float* C, int32_t* assign,
+                   cudaStream_t st, int num_sms) {
+    (void)num_sms;
+    DBuf<float> xn, xn2, cn, cn2, S;
+    xn.alloc((size_t)n);
+    xn2.alloc((size_t)n);
+    cn.alloc((size_t)nlist);
+    cn2.alloc((size_t)nlist);
+    launch_row_norms(X, ld, n, dim, xn.p, xn2.p, st);
+    const int64_t ch = std::max<int64_t>(
+        1, std::min<int64_t>({n, kMaxScoreEntries / std::max(nlist, 1), kMaxAssignRows}));
+    S.alloc((size_t)(ch * nlist));
+    const int64_t chunk = sort_chunk_rows(n, nlist);
+    const int64_t nchunks = (n + chunk - 1) / chunk;
+    DBuf<int32_t> counts, totals;
+    DBuf<int64_t> start, perm;
+    counts.alloc((size_t)(nchunks * nlist));
+    totals.alloc((size_t)nlist);
+    start.alloc((size_t)nlist + 1);
+    perm.alloc((size_t)n);
+    const float beta = sgemm_error_beta(dpad);
+    const float gam = (float)(dim + 4) * 5.9604645e-8f * 1.01f;
+    auto assign_all = [&]() {
+        launch_row_norms(C, dpad, nlist, dim, cn.p, cn2.p, st);
+        for (int64_t r0 = 0; r0 < n; r0 += ch) {
+            const int64_t m = std::min(ch, n - r0);
+            launch_sgemm_nt(X + r0 * ld, ld, C, dpad, S.p, nlist, (int)m, nlist, dpad, st);
+            M3G_CK(cudaGetLastError());
+            M3G_CK(launch_select_probes(S.p, nlist, X + r0 * ld, ld, C, dpad, xn.p + r0, xn2.p + r0,
+                                        cn.p, cn2.p, (int)m, nlist, dim, metric, normalized ? 1 : 0,
+                                        beta, gam, 1, 1, assign + r0, st));
+        }
+    };
+    for (int it = 0; it < niter; ++it) {
+        assign_all();
+        M3G_CK(launch_stable_cluster_sort(assign, n, nlist, chunk, counts.p, totals.p, start.p,
+                                          perm.p, st));
+        M3G_CK(launch_centroid_update(X, ld, perm.p, start.p, nlist, dim, C, dpad, st));
+    }
+    assign_all();
+    M3G_CK(cudaStreamSynchronize(st));
+}
+}  // namespace
+
+void Engine::kmeans(const float* X, int64_t n, int dim, int metric, bool normalized, int nlist,
+                    int niter, uint64_t seed, float* C_out, int32_t* assign_out) {
+    if (dim <= 0) fail(M3G_EINVAL, "kmeans: dim must be > 0");
+    if (nlist <= 0 || nlist > n) fail(M3G_EINVAL, "kmeans: nlist must be in [1, n]");
+    if (niter < 0) fail(M3G_EINVAL, "kmeans: niter < 0");
+    if (!X || !C_out) fail(M3G_EINVAL, "kmeans: buffers missing");
+    DeviceGuard g(device_);
+    const int dpad = round_up4(dim);
+    cudaStream_t st;
+    M3G_CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    struct StreamGuard {
+        cudaStream_t s;
+        ~StreamGuard() { cudaStreamDestroy(s); }
+    } sg{st};
+    DBuf<float> dX, dC;
+    DBuf<int32_t> da;
+    dX.alloc((size_t)(n * dpad));
+    dC.alloc((size_t)nlist * dpad);
+    da.alloc((size_t)n);
+    if (dpad != dim) M3G_CK(cudaMemsetAsync(dX.p, 0, (size_t)(n * dpad) * 4, st));
+    h2d_rows(dX.p, dpad, X, dim, n, st);
+    std::vector<int64_t> init((size_t)nlist);
+    sample_rows(seed, n, nlist, init.data());
+    DevIdx di;
+    di.upload(init, st);
+    M3G_CK(launch_gather_rows(dX.p, dpad, di.d.p, nlist, dpad, dC.p, dpad, st));
+    kmeans_device(dX.p, dpad, n, dim, dpad, metric, normalized, nlist, niter, dC.p, da.p, st, num_sms_);
+    M3G_CK(cudaMemcpy2DAsync(C_out, (size_t)dim * 4, dC.p, (size_t)dpad * 4, (size_t)dim * 4,
+                             (size_t)nlist, cudaMemcpyDeviceToHost, st));
+    if (assign_out)
+        M3G_CK(cudaMemcpyAsync(assign_out, da.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    M3G_CK(cudaStreamSynchronize(st));
+}
+
+void Engine::train_ivf(int index_id, int dim, int metric, bool normalized, const int64_t* ids,
+                       const float* X, int64_t n, int nlist, int niter, uint64_t seed,
+                       float* C_out) {
+    if (!ids) fail(M3G_EINVAL, "train_ivf: ids missing");
+    std::vector<float> C((size_t)nlist * dim);
+    std::vector<int32_t> a((size_t)n);
+    kmeans(X, n, dim, metric, normalized, nlist, niter, seed, C.data(), a.data());
+    create_ivf(index_id, dim, metric, normalized, C.data(), nlist);
+    // stable grouping of rows by list, ascending row order
+    std::vector<int64_t> cnt((size_t)nlist + 1, 0);
+    for (int64_t i = 0; i < n; ++i) cnt[(size_t)a[(size_t)i] + 1]++;
+    for (int l = 0; l < nlist; ++l) cnt[(size_t)l + 1] += cnt[(size_t)l];
+    std::vector<int64_t> order((size_t)n);
+    {
+        std::vector<int64_t> cur(cnt.begin(), cnt.end() - 1);
+        for (int64_t i = 0; i < n; ++i) order[(size_t)cur[(size_t)a[(size_t)i]]++] = i;
+    }
+    std::vector<int64_t> lid;
+    std::vector<float> lv;
+    for (int l = 0; l < nlist; ++l) {
+        const int64_t b = cnt[(size_t)l], e = cnt[(size_t)l + 1];
+        if (b == e) continue;
+        lid.resize((size_t)(e - b));
+        lv.resize((size_t)(e - b) * dim);
+        for (int64_t i = b; i < e; ++i) {
+            lid[(size_t)(i - b)] = ids[order[(size_t)i]];
+            std::memcpy(&lv[(size_t)(i - b) * dim], X + order[(size_t)i] * dim, sizeof(float) * dim);
+        }
+        load_cluster(index_id, l, lid.data(), lv.data(), e - b);
+    }
+    if (C_out) std::copy(C.begin(), C.end(), C_out);
+}
+
+int Engine::split_cluster(int index_id, int cid, int niter, uint64_t seed) {
+    auto ix = get(index_id, "split_cluster");
+    if (niter < 0) fail(M3G_EINVAL, "split_cluster: niter < 0");
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (cid < 0 || cid >= ix->nlist()) fail(M3G_ERANGE, "split_cluster: invalid cluster_id");
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    list_compact(*ix, cid);
+    ListMeta& L = ix->lists[cid];
+    const int64_t n = L.len;
+    if (n < 2) {
+        refresh_list_meta(*ix);
+        return -1;
+    }
+    cudaStream_t st = ix->wstream;
+    const int dpad = ix->dpad;
+    DBuf<float> dC;
+    DBuf<int32_t> da;
+    dC.alloc((size_t)2 * dpad);
+    da.alloc((size_t)n);
+    int64_t init[2];
+    sample_rows(seed, n, 2, init);
+    std::vector<int64_t> init_abs = {L.off + init[0], L.off + init[1]};
+    DevIdx di;
+    di.upload(init_abs, st);
+    M3G_CK(launch_gather_rows(ix->vecs.p, dpad, di.d.p, 2, dpad, dC.p, dpad, st));
+    kmeans_device(ix->vecs.p + L.off * dpad, dpad, n, ix->dim, dpad, ix->metric, ix->normalized, 2,
+                  niter, dC.p, da.p, st, num_sms_);
+    std::vector<float> c2((size_t)2 * ix->dim);
+    M3G_CK(cudaMemcpy2DAsync(c2.data(), (size_t)ix->dim * 4, dC.p, (size_t)dpad * 4,
+                             (size_t)ix->dim * 4, 2, cudaMemcpyDeviceToHost, st));
+    std::vector<int32_t> a((size_t)n);
+    M3G_CK(cudaMemcpyAsync(a.data(), da.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    M3G_CK(cudaStreamSynchronize(st));
+    std::vector<int64_t> side0, side1;
+    for (int64_t r = 0; r < n; ++r) (a[(size_t)r] == 1 ? side1 : side0).push_back(r);
+    // set_centroid(cid, c0); add_cluster(c1)  (m3_index.cpp:133-163)
+    std::copy(c2.begin(), c2.begin() + ix->dim, ix->centroids.begin() + (size_t)cid * ix->dim);
+    upload_centroids(*ix, cid, 1);
+    const int nid = ix->nlist();
+    ensure_centroid_cap(*ix, (size_t)nid + 1);
+    ix->centroids.insert(ix->centroids.end(), c2.begin() + ix->dim, c2.end());
+    ix->lists.emplace_back();
+    upload_centroids(*ix, nid, 1);
+    // rows regrouped in list order: side 1 to the new list, side 0 stays
+    regroup_rows(*ix, cid, side1, nid);
+    regroup_rows(*ix, cid, side0, cid);
+    refresh_list_meta(*ix);
+    return nid;
+}
+
+}  // namespace m3g

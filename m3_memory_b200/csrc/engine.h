@@ -1,0 +1,264 @@
+// engine.h -- host-side engine of libm3gpu: indices with their device list
+// arenas, the asynchronous write queue, and the search pipeline.
+//
+// Mirrors the reference's three layers in one place:
+//   m3::Cluster  (AgentMemory/M3/src/cluster.cpp)     -> ListMeta + the arena rows
+//   m3::IVFIndex (AgentMemory/M3/src/m3_index.cpp)    -> Index
+//   m3::AsyncEngine (AgentMemory/M3/src/m3_async.cpp) -> Engine
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <condition_variable>
+#include <cstdint>
+#include <deque>
+#include <memory>
+#include <mutex>
+#include <shared_mutex>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "kernels.h"
+#include "m3gpu.h"
+
+namespace m3g {
+
+// An error with its ABI status code.
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+[[noreturn]] void fail(int code, const std::string& msg);
+void check_cuda(cudaError_t e, const char* what);
+#define M3G_CK(x) ::m3g::check_cuda((x), #x)
+
+// Sets a device for the scope and restores the caller's afterwards.
+class DeviceGuard {
+   public:
+    explicit DeviceGuard(int dev);
+    ~DeviceGuard();
+
+   private:
+    int prev_ = -1;
+    bool changed_ = false;
+};
+
+// Owning device allocation (contents are not preserved by alloc()).
+template <class T>
+struct DBuf {
+    T* p = nullptr;
+    size_t n = 0;
+    DBuf() = default;
+    DBuf(const DBuf&) = delete;
+    DBuf& operator=(const DBuf&) = delete;
+    ~DBuf() { release(); }
+    void alloc(size_t count) {
+        release();
+        if (count) M3G_CK(cudaMalloc(reinterpret_cast<void**>(&p), count * sizeof(T)));
+        n = count;
+    }
+    // Grows (discarding contents) when fewer than `count` elements are held.
+    void ensure(size_t count) {
+        if (count > n) alloc(count + count / 4 + 16);
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    void swap(DBuf& o) {
+        std::swap(p, o.p);
+        std::swap(n, o.n);
+    }
+};
+
+// One inverted list (m3::Cluster, AgentMemory/M3/include/cluster.h:18-87): its
+// segment [off, off + cap) of the arena, of which rows [off, off + len) are in
+// use, plus host mirrors of the ids and tombstones and the id -> row map.
+struct ListMeta {
+    int64_t off = 0, len = 0, cap = 0, live = 0;
+    std::vector<int64_t> ids;
+    std::vector<uint8_t> alive;
+    std::unordered_map<int64_t, int64_t> id2row;
+};
+
+struct Index {
+    int device = 0;
+    int dim = 0, dpad = 0, metric = 0;
+    bool normalized = false;
+    std::vector<float> centroids;  // [nlist, dim] host copy (routing centroids)
+    std::vector<ListMeta> lists;
+
+    // device: centroids and their norms
+    DBuf<float> C, cn, cn2;  // [cap, dpad], [cap], [cap]
+    size_t c_cap = 0;
+    // device: the list arena, [arena_cap, dpad] rows + per-row ids / tombstones / norms
+    DBuf<float> vecs, rnorm2;
+    DBuf<int64_t> ids;
+    DBuf<uint8_t> alive;
+    int64_t arena_cap = 0, arena_used = 0;
+    // device: per-list metadata, and the lists ordered longest first
+    DBuf<int64_t> d_list_off;
+    DBuf<int32_t> d_list_len, d_list_order;
+    RowMaps maps{};
+    bool maps_valid = false;
+
+    std::shared_mutex mu;  // shared: searches; exclusive: every mutation
+    cudaStream_t wstream = nullptr;
+
+    Index() = default;
+    Index(const Index&) = delete;
+    Index& operator=(const Index&) = delete;
+    ~Index() {
+        if (wstream) cudaStreamDestroy(wstream);
+    }
+    int nlist() const { return (int)lists.size(); }
+};
+
+struct QueuePolicy {
+    size_t capacity = 4096, pop_batch_max = 64;
+    bool block_on_full = true;
+};
+struct SearchPolicy {
+    int default_nprobe = 8;
+    bool parallel_queries = false;
+};
+struct MaintenancePolicy {
+    double period_sec = 1.0;
+    size_t split_threshold = 200000;
+    double compact_ratio = 0.7;
+    bool auto_split = false;
+};
+
+struct WriteOp {
+    enum Kind { kInsert, kUpdate, kDelete } kind = kInsert;
+    int index_id = 0, cluster_id = 0;
+    bool insert_if_absent = false;
+    std::vector<int64_t> ids;
+    std::vector<float> vecs;
+};
+
+// Scratch of the search pipeline, grown on demand and reused across calls.
+struct Workspace {
+    DBuf<float> Q, qn, qn2, S;
+    DBuf<int32_t> probes, lcount, lstart, lcursor, n_items, item_counter, pair_q, pair_slot;
+    DBuf<ScanItem> items;
+    DBuf<float> part_score;
+    DBuf<int64_t> part_row;
+    DBuf<int64_t> out_ids;
+    DBuf<float> out_scores;
+    DBuf<int32_t> out_counts;
+    DBuf<int> err;
+    DBuf<unsigned long long> stats;
+    cudaStream_t stream = nullptr;
+    cudaStream_t last_stream = nullptr;  // stream of the last user (ordered by `done`)
+    cudaEvent_t done = nullptr;
+    cudaEvent_t ev[8] = {};
+    std::mutex mu;
+};
+
+class Engine {
+   public:
+    Engine();
+    ~Engine();
+    void set_device(int dev);
+    int device() const { return device_; }
+
+    void start(int writers, int maint);
+    void stop();
+    void set_queue_policy(const QueuePolicy& p) { qpol_ = p; }
+    void set_search_policy(const SearchPolicy& p) { spol_ = p; }
+    void set_maintenance_policy(const MaintenancePolicy& p) { mpol_ = p; }
+
+    void create_ivf(int index_id, int dim, int metric, bool normalized, const float* C, int64_t nlist);
+    void load_cluster(int index_id, int cid, const int64_t* ids, const float* vecs, int64_t n);
+    bool enqueue(WriteOp&& op);
+    bool enqueue_insert_auto(int index_id, const int64_t* ids, const float* vecs, int64_t n);
+    void flush();
+
+    // Search entry points.  q_dev: queries are device pointers; out_dev: outputs
+    // are device pointers; ext_stream: enqueue on this stream and do not wait.
+    void search(int index_id, const float* Q, int64_t nq, int k, int nprobe, bool q_dev,
+                int64_t* out_ids, float* out_scores, int32_t* out_counts, bool out_dev,
+                cudaStream_t ext_stream);
+    void search_on(int index_id, const int32_t* cids, int ncids, const float* Q, int64_t nq, int k,
+                   int64_t* out_ids, float* out_scores, int32_t* out_counts);
+    void select_probes(int index_id, const float* Q, int64_t nq, int nprobe, int32_t* out);
+    void nearest_clusters(int index_id, const float* vecs, int64_t n, int32_t* out);
+    void sync_errors();
+
+    void info(int index_id, int* dim, int* metric, int* normalized, int* nlist);
+    void cluster_size(int index_id, int cid, int64_t* size, int64_t* live);
+    void get_centroids(int index_id, float* out);
+    int add_cluster(int index_id, const float* c);
+    void set_centroid(int index_id, int cid, const float* c);
+    void compact_cluster(int index_id, int cid);
+    void maintenance_pass(int index_id);
+
+    void kmeans(const float* X, int64_t n, int dim, int metric, bool normalized, int nlist,
+                int niter, uint64_t seed, float* C_out, int32_t* assign_out);
+    void train_ivf(int index_id, int dim, int metric, bool normalized, const int64_t* ids,
+                   const float* X, int64_t n, int nlist, int niter, uint64_t seed, float* C_out);
+    int split_cluster(int index_id, int cid, int niter, uint64_t seed);
+
+    void set_profiling(bool on) { profiling_ = on; }
+    m3g_profile last_profile();
+
+   private:
+    std::shared_ptr<Index> find(int index_id) const;
+    std::shared_ptr<Index> get(int index_id, const char* who) const;
+    void writer_loop();
+    void maintenance_loop();
+    void apply(const WriteOp& op);
+    void record_error(const std::string& msg, int code);
+
+    // device helpers (callers hold the right index lock)
+    void run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int k, int P,
+                    const int32_t* fixed_probes, int64_t* d_ids, float* d_scores,
+                    int32_t* d_counts, cudaStream_t st, bool profile);
+    void assign_rows(Index& ix, const float* dX, int64_t ld, const float* xn, const float* xn2,
+                     int64_t n, int32_t* d_out, cudaStream_t st);
+    // Creates the workspace stream / events on first use; then orders `st` after
+    // the previous user of the workspace (blocking only when buffers must grow).
+    void acquire_ws(cudaStream_t st, int64_t nq, int64_t L, int64_t P, int64_t k, int64_t dpad);
+
+    int device_ = 0;
+    int num_sms_ = 148;
+    std::unordered_map<int, std::shared_ptr<Index>> indices_;
+    mutable std::shared_mutex imu_;
+
+    std::mutex qmu_;
+    std::condition_variable q_not_empty_, q_not_full_;
+    std::deque<WriteOp> queue_;
+    QueuePolicy qpol_;
+    SearchPolicy spol_;
+    MaintenancePolicy mpol_;
+    std::vector<std::thread> writers_, maint_;
+    std::atomic<bool> running_{false};
+    std::atomic<uint64_t> enqueued_{0}, applied_{0};
+    std::mutex maint_mu_;
+    std::condition_variable maint_cv_;
+
+    std::mutex err_mu_;
+    std::string first_error_;
+    int first_error_code_ = 0;
+
+    Workspace ws_;
+    std::atomic<bool> profiling_{false};
+    m3g_profile prof_{};
+    bool prof_pending_ = false;
+    int64_t prof_row_bytes_ = 0, prof_dim_ = 0;
+    int32_t last_launches_ = 0;  // kernels the last search call launched
+    cudaStream_t prof_stream_ = nullptr;
+};
+
+// Seeded sampling shared with the oracle: m distinct indices of [0, n) by a
+// partial Fisher-Yates shuffle driven by splitmix64.
+void sample_rows(uint64_t seed, int64_t n, int64_t m, int64_t* out);
+
+}  // namespace m3g

@@ -1,0 +1,430 @@
+// k_coarse.cu -- coarse quantizer: row norms, the approximate query x centroid
+// inner-product matrix (SIMT fp32 variant; the tcgen05 variant lives in
+// k_gemm_tc.cu), and the exact top-nprobe / nearest-centroid selection.
+//
+// Selection contract (IVFIndex::select_nprobe_for_query,
+// AgentMemory/M3/src/m3_index.cpp:492-523, and IVFIndex::nearest_clusters,
+// :243-264): for each query, the P centroids with the smallest unified score as
+// the reference computes it (fp32, index-order sums, one rounding per op),
+// ascending.  Exact ties go to the lower cluster id (the reference leaves them
+// to nth_element / sort, or to its strict '<' scan, which is the same rule for
+// P = 1).
+//
+// Method: the approximate scores come with a rigorous error bound e_c, so
+// [a_c - e_c, a_c + e_c] holds the reference's value.  With T the P-th smallest
+// upper bound, no centroid whose lower bound exceeds T can be among the P
+// smallest.  The remaining candidates (normally P plus a handful) are rescored
+// in the reference's exact arithmetic and sorted by (score, id).
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "score.cuh"
+
+namespace m3g {
+
+// ---------------------------------------------------------------------------
+// Row norms: one warp per row, fp64 accumulation.  nrm_up[i] >= ||x_i|| (an
+// upper bound rounded up to fp32), nrm2[i] ~ ||x_i||^2 in fp32.
+// ---------------------------------------------------------------------------
+__global__ void row_norms_kernel(const float* __restrict__ X, int64_t ld, int64_t n, int d,
+                                 float* __restrict__ nrm_up, float* __restrict__ nrm2) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    const float* x = X + row * ld;
+    double acc = 0.0;
+    for (int i = lane; i < d; i += 32) {
+        double v = (double)x[i];
+        acc = fma(v, v, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+        if (nrm_up) nrm_up[row] = __double2float_ru(sqrt(acc) * (1.0 + 1e-12));
+        if (nrm2) nrm2[row] = (float)acc;
+    }
+}
+
+void launch_row_norms(const float* X, int64_t ld, int64_t n, int d, float* nrm_up, float* nrm2,
+                      cudaStream_t st) {
+    if (n <= 0) return;
+    const int rows_per_block = 8;
+    const int64_t grid = (n + rows_per_block - 1) / rows_per_block;
+    row_norms_kernel<<<(unsigned)grid, rows_per_block * 32, 0, st>>>(X, ld, n, d, nrm_up, nrm2);
+}
+
+// ---------------------------------------------------------------------------
+// SIMT fp32 GEMM, S[m][n] = sum_k A[m][k] * B[n][k] (both K-contiguous).
+// 128x128 tile, BK = 8, 256 threads, 8x8 outputs per thread.  Error bound for
+// any summation order with or without FMA: |S - exact| <= (K+2) 2^-24 sum|a b|.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int GB_M = 128, GB_N = 128, GB_K = 8;
+}
+
+__global__ void __launch_bounds__(256) sgemm_nt_kernel(const float* __restrict__ A, int64_t lda,
+                                                       const float* __restrict__ B, int64_t ldb,
+                                                       float* __restrict__ S, int64_t lds, int M,
+                                                       int N, int K) {
+    __shared__ __align__(16) float As[2][GB_K][GB_M];
+    __shared__ __align__(16) float Bs[2][GB_K][GB_N];
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.y * GB_M, n0 = blockIdx.x * GB_N;
+    // loader mapping: 128 rows x 8 k = 256 threads x float4
+    const int lr = tid >> 1, lk = (tid & 1) * 4;
+    const int tx = tid & 15, ty = tid >> 4;
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+    auto load = [&](int buf, int k0) {
+        float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int ar = m0 + lr, br = n0 + lr, kk = k0 + lk;
+        if (ar < M) {
+            const float* p = A + (int64_t)ar * lda + kk;
+            if (kk + 3 < K) va = *reinterpret_cast<const float4*>(p);
+            else {
+                if (kk < K) va.x = p[0];
+                if (kk + 1 < K) va.y = p[1];
+                if (kk + 2 < K) va.z = p[2];
+            }
+        }
+        if (br < N) {
+            const float* p = B + (int64_t)br * ldb + kk;
+            if (kk + 3 < K) vb = *reinterpret_cast<const float4*>(p);
+            else {
+                if (kk < K) vb.x = p[0];
+                if (kk + 1 < K) vb.y = p[1];
+                if (kk + 2 < K) vb.z = p[2];
+            }
+        }
+        As[buf][lk + 0][lr] = va.x;
+        As[buf][lk + 1][lr] = va.y;
+        As[buf][lk + 2][lr] = va.z;
+        As[buf][lk + 3][lr] = va.w;
+        Bs[buf][lk + 0][lr] = vb.x;
+        Bs[buf][lk + 1][lr] = vb.y;
+        Bs[buf][lk + 2][lr] = vb.z;
+        Bs[buf][lk + 3][lr] = vb.w;
+    };
+
+    load(0, 0);
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = 0; k0 < K; k0 += GB_K) {
+        if (k0 + GB_K < K) load(buf ^ 1, k0 + GB_K);
+#pragma unroll
+        for (int kk = 0; kk < GB_K; ++kk) {
+            float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+            float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+            float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+            float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+            float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+        buf ^= 1;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        if (r >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int c = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+            if (c < N) S[(int64_t)r * lds + c] = acc[i][j];
+        }
+    }
+}
+
+void launch_sgemm_nt(const float* A, int64_t lda, const float* B, int64_t ldb, float* S,
+                     int64_t lds, int M, int N, int K, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return;
+    dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M);
+    sgemm_nt_kernel<<<grid, 256, 0, st>>>(A, lda, B, ldb, S, lds, M, N, K);
+}
+
+float sgemm_error_beta(int K) { return (float)(K + 2) * 5.9604645e-8f * 1.01f; }
+
+// ---------------------------------------------------------------------------
+// Exact selection.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int SEL_BLOCK = 256;
+constexpr int SEL_CAP = 2048;        // candidates rescored and sorted in shared memory
+constexpr int SEL_KEYS_SMEM = 8192;  // upper-bound keys cached in shared memory up to this L
+constexpr int SEL_SORT_MAX = 1024;   // largest P whose selection is returned sorted
+
+struct SelShared {
+    unsigned hist[256];
+    unsigned prefix, remain, count, count2, m_less, tie_need, wtot[SEL_BLOCK / 32];
+};
+
+// Finds the rank-th smallest (1-based) of the keys produced by key_of(c),
+// c in [0, L), by 4 passes of an 8-bit radix select.  All threads return it.
+template <class KeyOf>
+__device__ uint32_t block_radix_select(KeyOf key_of, int L, unsigned rank, SelShared& sh) {
+    uint32_t prefix = 0, mask = 0;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int i = threadIdx.x; i < 256; i += SEL_BLOCK) sh.hist[i] = 0;
+        __syncthreads();
+        for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
+            const uint32_t k = key_of(c);
+            if ((k & mask) == prefix) atomicAdd(&sh.hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            // warp 0 scans the 256 bins: lane l owns bins 8l..8l+7
+            unsigned loc[8], s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                loc[j] = sh.hist[threadIdx.x * 8 + j];
+                s += loc[j];
+            }
+            unsigned incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+                if ((int)threadIdx.x >= o) incl += v;
+            }
+            const unsigned excl = incl - s;
+            if (excl < rank && rank <= incl) {
+                unsigned r = rank - excl;
+                int b = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (b == 0 && r <= loc[j]) b = j + 1;
+                    else if (b == 0) r -= loc[j];
+                }
+                sh.prefix = prefix | ((uint32_t)(threadIdx.x * 8 + b - 1) << shift);
+                sh.remain = r;
+            }
+        }
+        __syncthreads();
+        prefix = sh.prefix;
+        rank = sh.remain;
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    return prefix;
+}
+
+// Block-wide exclusive scan of one flag per thread; returns the thread's offset
+// and writes the block total to *total.
+__device__ unsigned block_flag_scan(bool flag, unsigned* total, SelShared& sh) {
+    const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const unsigned ball = __ballot_sync(0xffffffffu, flag);
+    const unsigned below = __popc(ball & ((1u << lane) - 1u));
+    if (lane == 0) sh.wtot[w] = __popc(ball);
+    __syncthreads();
+    unsigned base = 0, tot = 0;
+    for (unsigned i = 0; i < SEL_BLOCK / 32; ++i) {
+        if (i < w) base += sh.wtot[i];
+        tot += sh.wtot[i];
+    }
+    __syncthreads();
+    *total = tot;
+    return base + below;
+}
+
+__device__ void bitonic_sort_u64(unsigned long long* a, int n) {
+    // n is a power of two
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += SEL_BLOCK) {
+                const int p = i ^ j;
+                if (p > i) {
+                    const unsigned long long x = a[i], y = a[p];
+                    const bool up = (i & k) == 0;
+                    if ((x > y) == up) {
+                        a[i] = y;
+                        a[p] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+}  // namespace
+
+// One block per query.  S holds the approximate inner products (overwritten
+// with exact scores on the fallback path).  Writes P cluster ids per query into
+// probes (ascending by exact score when P <= 1024, else in ascending id order),
+// or -1 for the nearest-cluster form (P == 1, nan_is_none) when every score is NaN.
+__global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
+    float* __restrict__ S, int64_t lds, const float* __restrict__ Q, int64_t ldq,
+    const float* __restrict__ C, int64_t ldc, const float* __restrict__ qn,
+    const float* __restrict__ qn2, const float* __restrict__ cn, const float* __restrict__ cn2,
+    int L, int D, int metric, int normalized, float beta, float gamma, int P, int nan_is_none,
+    int32_t* __restrict__ probes) {
+    extern __shared__ __align__(16) unsigned char sel_smem[];
+    __shared__ SelShared sh;
+    const int q = blockIdx.x;
+    float* qs = reinterpret_cast<float*>(sel_smem);                               // D floats
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(qs + ((D + 3) & ~3));  // SEL_CAP
+    uint32_t* hkeys = reinterpret_cast<uint32_t*>(cand + SEL_CAP);               // L (if cached)
+    const bool cache = L <= SEL_KEYS_SMEM;
+
+    const float* qrow = Q + (int64_t)q * ldq;
+    for (int i = threadIdx.x; i < D; i += SEL_BLOCK) qs[i] = qrow[i];
+    float* srow = S + (int64_t)q * lds;
+    const float nq = qn[q], nq2 = qn2[q];
+    const bool nrm = normalized != 0;
+
+    auto bounds = [&](int c, float* lo, float* hi) {
+        approx_bounds(srow[c], nq, cn[c], nq2, cn2[c], beta, gamma, metric, nrm, lo, hi);
+    };
+    if (cache) {
+        for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
+            float lo, hi;
+            bounds(c, &lo, &hi);
+            hkeys[c] = float_key(hi);
+        }
+    }
+    __syncthreads();
+
+    const int PP = P < L ? P : L;
+    bool exact_all = PP > SEL_SORT_MAX;
+    if (!exact_all) {
+        // --- phase A: T = PP-th smallest upper bound
+        uint32_t tkey;
+        if (cache)
+            tkey = block_radix_select([&](int c) { return hkeys[c]; }, L, (unsigned)PP, sh);
+        else
+            tkey = block_radix_select(
+                [&](int c) {
+                    float lo, hi;
+                    bounds(c, &lo, &hi);
+                    return float_key(hi);
+                },
+                L, (unsigned)PP, sh);
+        // --- phase B: candidates whose lower bound is <= T (compared as keys,
+        // so a NaN bound, key 0xffffffff for hi / mapped low for lo, is kept)
+        if (threadIdx.x == 0) sh.count = 0;
+        __syncthreads();
+        for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
+            float lo, hi;
+            bounds(c, &lo, &hi);
+            if (float_key(lo) <= tkey || lo != lo) {
+                const unsigned slot = atomicAdd(&sh.count, 1u);
+                if (slot < (unsigned)SEL_CAP) cand[slot] = (unsigned long long)c;
+            }
+        }
+        __syncthreads();
+        const unsigned cnt = sh.count;
+        if (cnt > (unsigned)SEL_CAP) {
+            exact_all = true;
+        } else {
+            // --- phase C: rescore candidates exactly, sort by (score, id)
+            int n2 = 1;
+            while (n2 < (int)cnt) n2 <<= 1;
+            for (int i = threadIdx.x; i < n2; i += SEL_BLOCK) {
+                if (i < (int)cnt) {
+                    const int c = (int)cand[i];
+                    const float r = exact_score(qs, C + (int64_t)c * ldc, D, metric, nrm);
+                    cand[i] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
+                } else {
+                    cand[i] = ~0ull;
+                }
+            }
+            __syncthreads();
+            bitonic_sort_u64(cand, n2);
+            for (int j = threadIdx.x; j < PP; j += SEL_BLOCK) {
+                const unsigned long long kk = cand[j];
+                int32_t id = (int32_t)(kk & 0xffffffffu);
+                if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
+                probes[(int64_t)q * P + j] = id;
+            }
+            return;
+        }
+    }
+
+    // --- fallback: exact scores for every centroid, selection by (score, id)
+    __syncthreads();
+    for (int c = threadIdx.x; c < L; c += SEL_BLOCK)
+        srow[c] = exact_score(qs, C + (int64_t)c * ldc, D, metric, nrm);
+    __syncthreads();
+    const uint32_t kth =
+        block_radix_select([&](int c) { return float_key(srow[c]); }, L, (unsigned)PP, sh);
+    if (threadIdx.x == 0) {
+        sh.count = 0;
+        sh.count2 = 0;
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < L; c += SEL_BLOCK)
+        if (float_key(srow[c]) < kth) atomicAdd(&sh.count, 1u);
+    __syncthreads();
+    const unsigned m_less = sh.count;
+    const unsigned tie_need = (unsigned)PP - m_less;
+    // ordered compaction: keys < kth, then the first tie_need ids with key == kth
+    const bool sorted = PP <= SEL_SORT_MAX;
+    unsigned out_pos = 0, ties_taken = 0;
+    for (int c0 = 0; c0 < L; c0 += SEL_BLOCK) {
+        const int c = c0 + threadIdx.x;
+        const uint32_t k = c < L ? float_key(srow[c]) : 0xffffffffu;
+        const bool tie = c < L && k == kth;
+        unsigned tie_tot;
+        const unsigned tie_off = block_flag_scan(tie, &tie_tot, sh);
+        const bool take = c < L && (k < kth || (tie && ties_taken + tie_off < tie_need));
+        unsigned take_tot;
+        const unsigned off = block_flag_scan(take, &take_tot, sh);
+        if (take) {
+            if (sorted)
+                cand[out_pos + off] = ((unsigned long long)k << 32) | (unsigned)c;
+            else
+                probes[(int64_t)q * P + out_pos + off] = c;
+        }
+        out_pos += take_tot;
+        ties_taken += tie_tot;
+    }
+    __syncthreads();
+    if (sorted) {
+        int n2 = 1;
+        while (n2 < PP) n2 <<= 1;
+        for (int i = PP + threadIdx.x; i < n2; i += SEL_BLOCK) cand[i] = ~0ull;
+        __syncthreads();
+        bitonic_sort_u64(cand, n2);
+        for (int j = threadIdx.x; j < PP; j += SEL_BLOCK) {
+            const unsigned long long kk = cand[j];
+            int32_t id = (int32_t)(kk & 0xffffffffu);
+            if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
+            probes[(int64_t)q * P + j] = id;
+        }
+    }
+}
+
+size_t select_smem_bytes(int L, int D) {
+    size_t b = sizeof(float) * (size_t)((D + 3) & ~3) + sizeof(unsigned long long) * SEL_CAP;
+    if (L <= SEL_KEYS_SMEM) b += sizeof(uint32_t) * (size_t)L;
+    return b;
+}
+
+int select_max_dim() { return 8192; }
+
+cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t ldq, const float* C,
+                                 int64_t ldc, const float* qn, const float* qn2, const float* cn,
+                                 const float* cn2, int nq, int L, int D, int metric,
+                                 int normalized, float beta, float gamma, int P, int nan_is_none,
+                                 int32_t* probes, cudaStream_t st) {
+    if (nq <= 0) return cudaSuccess;
+    const size_t smem = select_smem_bytes(L, D);
+    cudaError_t e = cudaFuncSetAttribute(select_probes_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    select_probes_kernel<<<nq, SEL_BLOCK, smem, st>>>(S, lds, Q, ldq, C, ldc, qn, qn2, cn, cn2, L,
+                                                      D, metric, normalized, beta, gamma, P,
+                                                      nan_is_none, probes);
+    return cudaGetLastError();
+}
+
+}  // namespace m3g

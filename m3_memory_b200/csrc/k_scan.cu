@@ -1,0 +1,801 @@
+// k_scan.cu -- the inverted-list scan with per-query top-k (Cluster::search_into,
+// AgentMemory/M3/src/cluster.cpp:229-274, driven by IVFIndex::search_nprobe,
+// AgentMemory/M3/src/m3_index.cpp:368-483), reorganised list-centric for the GPU.
+//
+// The reference walks queries one by one and, for each, the probed lists.  Here a
+// search batch is turned around: the (query, probe) pairs are grouped by list, and
+// each work item is one list with up to `gmax` of the queries that probe it, so a
+// list is streamed from HBM once per item rather than once per query.
+//
+// Kernel shape (one persistent CTA per SM, warp-specialised):
+//   warp 8      producer: takes items from a global counter, bulk-copies the
+//               item's query rows into a double-buffered query area, and streams
+//               the list's rows through a ring of shared-memory stages with 2-D TMA
+//               (32 dims x up to 64 rows per stage, SWIZZLE_128B, no multicast).
+//   warps 0..7  consumers: split K -- warp w takes chunks w, w+8, ... of each
+//               64-row tile; each lane owns rows lane and lane+32 and keeps one fp32
+//               FMA accumulator per (row, query).  The eight partial sums are
+//               added in a fixed order, turned into the unified score, masked by
+//               tombstones, and each warp w < g folds the tile into the running
+//               top-k of query w.
+// Ordering: candidates are ranked by (score, probe slot, row in list), which is
+// the reference's visiting order; scores differ from the reference's only by
+// fp32 summation order.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace m3g {
+namespace {
+
+constexpr int KC = 32;          // dims per stage (128 bytes of fp32)
+constexpr int TR = 64;          // rows per tile
+constexpr int NCW = 8;          // consumer warps
+constexpr int NTHREADS = (NCW + 1) * 32;
+constexpr int GMAX = 8;         // queries per item (upper bound of the runtime gmax)
+constexpr int KMAX = 256;       // largest k the fused top-k keeps
+constexpr int STAGE_BYTES = TR * KC * 4;
+constexpr int MAX_STAGES = 12;
+constexpr int MIN_STAGES = 4;
+constexpr int PSTRIDE = GMAX + 1;  // partial-sum row stride (bank-conflict padding)
+constexpr int SMEM_LIMIT = 227 * 1024;
+
+struct ItemInfo {
+    int32_t list;      // -1: no more items
+    int32_t pad0;
+    int32_t npairs;
+    int32_t nrows;
+    int64_t off;       // first arena row of the list
+    int32_t q[GMAX];
+    int32_t slot[GMAX];
+};
+
+struct Layout {
+    int nstage;
+    int qstride;        // floats per query row in shared memory (multiple of 32)
+    int gmax;
+    uint32_t ring_off, q_off, part_off, sc_off, tks_off, tkr_off, info_off, bar_off, total;
+};
+
+__host__ __device__ inline int nchunks_of(int dpad) { return (dpad + KC - 1) / KC; }
+
+__host__ __device__ inline Layout make_layout(int dpad, int gmax, int nstage) {
+    Layout L;
+    L.gmax = gmax;
+    L.nstage = nstage;
+    L.qstride = nchunks_of(dpad) * KC;
+    uint32_t o = 0;
+    L.ring_off = o;
+    o += (uint32_t)nstage * STAGE_BYTES;
+    L.q_off = o;
+    o += 2u * (uint32_t)gmax * (uint32_t)L.qstride * 4u;
+    L.part_off = o;
+    o += (uint32_t)NCW * TR * PSTRIDE * 4u;
+    L.sc_off = o;
+    o += (uint32_t)GMAX * TR * 4u;
+    L.tks_off = o;
+    o += (uint32_t)GMAX * KMAX * 4u;
+    L.tkr_off = o;
+    o += (uint32_t)GMAX * KMAX * 4u;
+    L.info_off = o;
+    o += 2u * (uint32_t)sizeof(ItemInfo);
+    o = (o + 15u) & ~15u;
+    L.bar_off = o;
+    o += (uint32_t)(2 * MAX_STAGES + 4) * 8u;
+    L.total = o + 1024u;  // slack for aligning the ring to 1024 bytes
+    return L;
+}
+
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
+}
+
+// Producer side of the ring: waits until every stage it ever filled has landed
+// (used when a launch ends early on an error, so no copy is left in flight).
+__device__ void drain_stages(uint64_t* full, int nstage, uint32_t seq_end) {
+    const uint32_t first = seq_end > (uint32_t)nstage ? seq_end - nstage : 0u;
+    for (uint32_t s = first; s < seq_end; ++s) {
+        uint64_t* b = &full[s % nstage];
+        const uint32_t par = (s / nstage) & 1u;
+        for (uint32_t i = 0; i < kWaitSpinLimit; ++i) {
+            if (mbar_try_wait(b, par)) break;
+            __nanosleep(256);
+        }
+    }
+}
+
+template <int NQ, bool L2>
+__device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring,
+                                            const float* qbuf, uint64_t* full, uint64_t* empty,
+                                            uint32_t seq_tile, int nchunks, int warp, int lane,
+                                            float (&acc0)[GMAX], float (&acc1)[GMAX], int* err,
+                                            bool& ok) {
+#pragma unroll
+    for (int i = 0; i < GMAX; ++i) {
+        acc0[i] = 0.f;
+        acc1[i] = 0.f;
+    }
+    const int r0 = lane, r1 = lane + 32;
+    for (int c = warp; c < nchunks; c += NCW) {
+        const uint32_t s = seq_tile + (uint32_t)c;
+        const int stage = (int)(s % (uint32_t)L.nstage);
+        bool got = ok && mbar_wait(&full[stage], (s / (uint32_t)L.nstage) & 1u, err);
+        got = __all_sync(0xffffffffu, got);  // one decision per warp
+        if (!got) {
+            // Leave the tile's barrier structure intact; the launch ends at the
+            // next tile boundary with the error already recorded.
+            ok = false;
+            continue;
+        }
+        const uint32_t base = smem_u32(ring + (size_t)stage * STAGE_BYTES);
+        const float* qc = qbuf + c * KC;
+#pragma unroll
+        for (int j = 0; j < KC / 4; ++j) {
+            const float4 x0 = lds128(base + r0 * 128 + ((j ^ (r0 & 7)) << 4));
+            const float4 x1 = lds128(base + r1 * 128 + ((j ^ (r1 & 7)) << 4));
+#pragma unroll
+            for (int qi = 0; qi < NQ; ++qi) {
+                const float4 qv = *reinterpret_cast<const float4*>(qc + qi * L.qstride + j * 4);
+                if (L2) {
+                    float d;
+                    d = x0.x - qv.x; acc0[qi] = fmaf(d, d, acc0[qi]);
+                    d = x0.y - qv.y; acc0[qi] = fmaf(d, d, acc0[qi]);
+                    d = x0.z - qv.z; acc0[qi] = fmaf(d, d, acc0[qi]);
+                    d = x0.w - qv.w; acc0[qi] = fmaf(d, d, acc0[qi]);
+                    d = x1.x - qv.x; acc1[qi] = fmaf(d, d, acc1[qi]);
+                    d = x1.y - qv.y; acc1[qi] = fmaf(d, d, acc1[qi]);
+                    d = x1.z - qv.z; acc1[qi] = fmaf(d, d, acc1[qi]);
+                    d = x1.w - qv.w; acc1[qi] = fmaf(d, d, acc1[qi]);
+                } else {
+                    acc0[qi] = fmaf(x0.x, qv.x, acc0[qi]);
+                    acc0[qi] = fmaf(x0.y, qv.y, acc0[qi]);
+                    acc0[qi] = fmaf(x0.z, qv.z, acc0[qi]);
+                    acc0[qi] = fmaf(x0.w, qv.w, acc0[qi]);
+                    acc1[qi] = fmaf(x1.x, qv.x, acc1[qi]);
+                    acc1[qi] = fmaf(x1.y, qv.y, acc1[qi]);
+                    acc1[qi] = fmaf(x1.z, qv.z, acc1[qi]);
+                    acc1[qi] = fmaf(x1.w, qv.w, acc1[qi]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+    }
+}
+
+template <bool L2>
+__device__ __forceinline__ void tile_dispatch(int nq_rounded, const Layout& L, unsigned char* ring,
+                                              const float* qbuf, uint64_t* full, uint64_t* empty,
+                                              uint32_t seq_tile, int nchunks, int warp, int lane,
+                                              float (&acc0)[GMAX], float (&acc1)[GMAX], int* err,
+                                              bool& ok) {
+    switch (nq_rounded) {
+        case 1: tile_chunks<1, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+        case 2: tile_chunks<2, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+        case 4: tile_chunks<4, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+        default: tile_chunks<8, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+    }
+}
+
+// Folds up to 64 new (score, row) candidates (two per lane) into the sorted
+// top-k kept in shared memory (tks ascending by (score, row); rows of this tile
+// are larger than every row already held, so an equal score never displaces).
+__device__ __forceinline__ void topk_fold(float* tks, int32_t* tkr, int& cnt, int k, float s0,
+                                          int32_t row0, bool v0, float s1, int32_t row1, bool v1,
+                                          int lane) {
+    const float INF = __int_as_float(0x7f800000);
+    float tau = cnt == k ? tks[k - 1] : INF;
+    bool c0 = v0 && s0 < tau, c1 = v1 && s1 < tau;
+    while (__any_sync(0xffffffffu, c0 || c1)) {
+        // this lane's best candidate
+        unsigned long long mine = ~0ull;
+        if (c0) mine = ((unsigned long long)float_key(s0) << 32) | (uint32_t)row0;
+        if (c1) {
+            unsigned long long k1 = ((unsigned long long)float_key(s1) << 32) | (uint32_t)row1;
+            if (k1 < mine) mine = k1;
+        }
+        unsigned long long best = mine;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            if (other < best) best = other;
+        }
+        const float bs = key_float((uint32_t)(best >> 32));
+        const int32_t br = (int32_t)(best & 0xffffffffu);
+        // insertion position: entries with score <= bs stay in front
+        int pos = 0;
+        for (int i = lane; i < cnt; i += 32) pos += tks[i] <= bs ? 1 : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) pos += __shfl_xor_sync(0xffffffffu, pos, o);
+        const int last = cnt < k ? cnt : k - 1;  // entries [pos, last) move up by one
+        float ms[KMAX / 32];
+        int32_t mr[KMAX / 32];
+#pragma unroll
+        for (int m = 0; m < KMAX / 32; ++m) {
+            const int i = pos + lane + 32 * m;
+            if (i < last) {
+                ms[m] = tks[i];
+                mr[m] = tkr[i];
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int m = 0; m < KMAX / 32; ++m) {
+            const int i = pos + lane + 32 * m;
+            if (i < last) {
+                tks[i + 1] = ms[m];
+                tkr[i + 1] = mr[m];
+            }
+        }
+        if (lane == 0) {
+            tks[pos] = bs;
+            tkr[pos] = br;
+        }
+        __syncwarp();
+        cnt = cnt < k ? cnt + 1 : k;
+        if (c0 && s0 == bs && row0 == br) c0 = false;
+        if (c1 && s1 == bs && row1 == br) c1 = false;
+        tau = cnt == k ? tks[k - 1] : INF;
+        c0 = c0 && s0 < tau;
+        c1 = c1 && s1 < tau;
+    }
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    list_scan_kernel(const __grid_constant__ RowMaps maps, const ScanArgs a, const Layout L) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* ring = smem + L.ring_off;
+    float* qbase = reinterpret_cast<float*>(smem + L.q_off);
+    float* part = reinterpret_cast<float*>(smem + L.part_off);
+    float* sc = reinterpret_cast<float*>(smem + L.sc_off);
+    float* tks_all = reinterpret_cast<float*>(smem + L.tks_off);
+    int32_t* tkr_all = reinterpret_cast<int32_t*>(smem + L.tkr_off);
+    ItemInfo* info = reinterpret_cast<ItemInfo*>(smem + L.info_off);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+    uint64_t* empty = full + MAX_STAGES;
+    uint64_t* qfull = empty + MAX_STAGES;
+    uint64_t* qempty = qfull + 2;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nchunks = nchunks_of(a.dpad);
+    const int qbuf_floats = L.gmax * L.qstride;
+
+    // zero the query area once: its padding columns are never written again
+    for (int i = threadIdx.x; i < 2 * qbuf_floats; i += NTHREADS) qbase[i] = 0.f;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < L.nstage; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&qfull[b], 1);
+            mbar_init(&qempty[b], NCW);
+        }
+        fence_mbar_init();
+    }
+    if (warp == NCW && lane == 0) {
+        prefetch_tensormap(&maps.m64);
+        prefetch_tensormap(&maps.m32);
+        prefetch_tensormap(&maps.m16);
+        prefetch_tensormap(&maps.m8);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    if (warp == NCW) {
+        // ------------------------------ producer ------------------------------
+        uint32_t seq = 0;
+        const int nitems = *a.n_items;
+        bool ok = true;
+        int q_issued = 0;  // items whose query copies were issued
+        for (int it = 0; ok; ++it) {
+            const int qb = it & 1;
+            if (it >= 2 && !mbar_wait(&qempty[qb], ((it >> 1) - 1) & 1, a.err)) {
+                ok = false;
+                break;
+            }
+            int item = 0;
+            if (lane == 0) item = atomicAdd(a.item_counter, 1);
+            item = __shfl_sync(0xffffffffu, item, 0);
+            ItemInfo* inf = &info[qb];
+            if (item >= nitems) {
+                if (lane == 0) {
+                    inf->list = -1;
+                    mbar_arrive(&qfull[qb]);
+                }
+                break;
+            }
+            const ScanItem wi = a.items[item];
+            const int np = wi.npairs;
+            int nrows = 0;
+            int64_t off = 0;
+            if (wi.list >= 0) {
+                nrows = a.list_len[wi.list];
+                off = a.list_off[wi.list];
+            }
+            if (np < 1 || np > L.gmax || nrows < 0) {
+                if (lane == 0) atomicCAS(a.err, 0, (int)kErrBadItem);
+                if (lane == 0) {
+                    inf->list = -1;
+                    mbar_arrive(&qfull[qb]);
+                }
+                break;
+            }
+            int32_t myq = 0;
+            if (lane < np) {
+                myq = a.pair_q[wi.pair_begin + lane];
+                inf->q[lane] = myq;
+                inf->slot[lane] = a.pair_slot[wi.pair_begin + lane];
+            }
+            if (lane == 0) {
+                inf->list = wi.list;
+                inf->npairs = np;
+                inf->nrows = nrows;
+                inf->off = off;
+            }
+            __syncwarp();
+            float* qdst = qbase + qb * qbuf_floats;
+            if (lane == 0) mbar_arrive_expect_tx(&qfull[qb], (uint32_t)(np * a.dpad * 4));
+            __syncwarp();
+            if (lane < np)
+                bulk_g2s(qdst + lane * L.qstride, a.Q + (int64_t)myq * a.dpad,
+                         (uint32_t)(a.dpad * 4), &qfull[qb]);
+            q_issued = it + 1;
+            // stream the list: tiles of 64 rows, each as nchunks stages of 32 dims
+            const int ntiles = (nrows + TR - 1) / TR;
+            for (int t = 0; t < ntiles && ok; ++t) {
+                const int rows_here = min(TR, nrows - t * TR);
+                const int r8 = (rows_here + 7) & ~7;
+                const int y0 = (int)(off + (int64_t)t * TR);
+                for (int c = 0; c < nchunks; ++c) {
+                    const int stage = (int)(seq % (uint32_t)L.nstage);
+                    const uint32_t use = seq / (uint32_t)L.nstage;
+                    if (use >= 1 && !mbar_wait(&empty[stage], (use - 1) & 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    if (lane == 0) {
+                        unsigned char* dst = ring + (size_t)stage * STAGE_BYTES;
+                        mbar_arrive_expect_tx(&full[stage], (uint32_t)(r8 * 128));
+                        int r = 0;
+                        const int x = c * KC;
+                        if (r8 == 64) {
+                            tma_load_2d(dst, &maps.m64, x, y0, &full[stage]);
+                        } else {
+                            if (r8 - r >= 32) { tma_load_2d(dst + r * 128, &maps.m32, x, y0 + r, &full[stage]); r += 32; }
+                            if (r8 - r >= 16) { tma_load_2d(dst + r * 128, &maps.m16, x, y0 + r, &full[stage]); r += 16; }
+                            if (r8 - r >= 8) { tma_load_2d(dst + r * 128, &maps.m8, x, y0 + r, &full[stage]); r += 8; }
+                        }
+                    }
+                    ++seq;
+                }
+            }
+        }
+        if (!ok && lane == 0) {
+            drain_stages(full, L.nstage, seq);
+            if (q_issued > 0) {
+                const int lit = q_issued - 1;
+                for (uint32_t i = 0; i < kWaitSpinLimit; ++i) {
+                    if (mbar_try_wait(&qfull[lit & 1], (lit >> 1) & 1)) break;
+                    __nanosleep(256);
+                }
+            }
+        }
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    const int ctid = threadIdx.x;  // 0..255
+    uint32_t seq = 0;
+    float* tks = tks_all + warp * KMAX;
+    int32_t* tkr = tkr_all + warp * KMAX;
+    const float INF = __int_as_float(0x7f800000);
+    for (int it = 0;; ++it) {
+        const int qb = it & 1;
+        bool ok = __all_sync(0xffffffffu, mbar_wait(&qfull[qb], (it >> 1) & 1, a.err));
+        // every consumer warp takes the same exit decision here
+        if (named_bar_sync_or(1, NCW * 32, !ok)) return;
+        const ItemInfo* inf = &info[qb];
+        const int list = inf->list;
+        if (list < 0) return;
+        const int g = inf->npairs, nrows = inf->nrows;
+        const int64_t off = inf->off;
+        const int nqr = g <= 1 ? 1 : g <= 2 ? 2 : g <= 4 ? 4 : 8;
+        const float* qbuf = qbase + qb * qbuf_floats;
+        int cnt = 0;  // this warp's query (warp < g): entries held in tks/tkr
+        const int ntiles = (nrows + TR - 1) / TR;
+        for (int t = 0; t < ntiles; ++t) {
+            float acc0[GMAX], acc1[GMAX];
+            const uint32_t seq_tile = seq + (uint32_t)(t * nchunks);
+            if (a.metric == kL2)
+                tile_dispatch<true>(nqr, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, a.err, ok);
+            else
+                tile_dispatch<false>(nqr, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, a.err, ok);
+            float* pw = part + warp * TR * PSTRIDE;
+#pragma unroll
+            for (int qi = 0; qi < GMAX; ++qi) {
+                if (qi < nqr) {
+                    pw[lane * PSTRIDE + qi] = acc0[qi];
+                    pw[(lane + 32) * PSTRIDE + qi] = acc1[qi];
+                }
+            }
+            // uniform stop if any warp's wait gave up during this tile
+            if (named_bar_sync_or(1, NCW * 32, !ok)) return;
+            const int rows_here = min(TR, nrows - t * TR);
+            for (int e = ctid; e < TR * g; e += NCW * 32) {
+                const int r = e % TR, qi = e / TR;
+                float sum = 0.f;
+#pragma unroll
+                for (int w = 0; w < NCW; ++w) sum += part[(w * TR + r) * PSTRIDE + qi];
+                float s = INF;
+                if (r < rows_here) {
+                    const int64_t row = off + (int64_t)t * TR + r;
+                    if (a.alive[row]) {
+                        if (a.metric == kL2) s = sum;
+                        else if (a.metric == kIP) s = -sum;
+                        else if (a.normalized) s = 1.f - sum;
+                        else {
+                            const float na = a.qnorm2[inf->q[qi]], nb = a.rnorm2[row];
+                            s = (na == 0.f || nb == 0.f) ? 1.f : 1.f - sum / sqrtf(na * nb);
+                        }
+                    }
+                }
+                sc[qi * TR + r] = s;
+            }
+            named_bar_sync(1, NCW * 32);
+            if (warp < g) {
+                const int rbase = t * TR;
+                const float s0 = sc[warp * TR + lane], s1 = sc[warp * TR + lane + 32];
+                topk_fold(tks, tkr, cnt, a.k, s0, rbase + lane, score_valid(s0), s1,
+                          rbase + lane + 32, score_valid(s1), lane);
+            }
+        }
+        seq += (uint32_t)(ntiles * nchunks);
+        if (warp < g) {
+            const int64_t base = ((int64_t)inf->q[warp] * a.P + inf->slot[warp]) * a.k;
+            for (int j = lane; j < a.k; j += 32) {
+                a.part_score[base + j] = j < cnt ? tks[j] : INF;
+                a.part_row[base + j] = j < cnt ? off + tkr[j] : -1;
+            }
+        }
+        __syncwarp();
+        // releases the query buffer and the item record to the producer
+        if (lane == 0) mbar_arrive(&qempty[qb]);
+    }
+}
+
+Layout choose_layout(int dpad, int* gmax_out) {
+    for (int g = GMAX; g >= 1; g >>= 1) {
+        for (int ns = MAX_STAGES; ns >= MIN_STAGES; --ns) {
+            Layout L = make_layout(dpad, g, ns);
+            if (L.total <= (uint32_t)SMEM_LIMIT) {
+                *gmax_out = g;
+                return L;
+            }
+        }
+    }
+    *gmax_out = 0;
+    return make_layout(dpad, 1, MIN_STAGES);
+}
+
+}  // namespace
+
+int scan_kmax() { return KMAX; }
+
+int scan_gmax_for_dim(int dpad) {
+    int g = 0;
+    choose_layout(dpad, &g);
+    return g;
+}
+
+cudaError_t launch_list_scan(const RowMaps& maps, const ScanArgs& a, int gmax, int grid,
+                             cudaStream_t st) {
+    int g = 0;
+    Layout L = choose_layout(a.dpad, &g);
+    if (g == 0 || gmax > g || a.k > KMAX) return cudaErrorInvalidValue;
+    L = make_layout(a.dpad, gmax, L.nstage);
+    cudaError_t e = cudaFuncSetAttribute(list_scan_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    if (e != cudaSuccess) return e;
+    list_scan_kernel<<<grid, NTHREADS, L.total, st>>>(maps, a, L);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Work list.
+// ---------------------------------------------------------------------------
+namespace {
+
+__global__ void probe_hist_kernel(const int32_t* __restrict__ probes, int64_t n, int L,
+                                  int32_t* __restrict__ lcount) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int l = probes[i];
+        if (l >= 0 && l < L) atomicAdd(&lcount[l], 1);
+    }
+}
+
+constexpr int PLAN_THREADS = 1024;
+
+__device__ __forceinline__ int items_of(int c, int gmax) { return (c + gmax - 1) / gmax; }
+
+// One block: walks the clusters in list_order, assigns each its pair range and
+// its items (the pairs split into ceil(c / gmax) near-equal groups).
+__global__ void __launch_bounds__(PLAN_THREADS) plan_items_kernel(
+    const int32_t* __restrict__ lcount, const int32_t* __restrict__ order, int L, int gmax,
+    int32_t* __restrict__ lstart, ScanItem* __restrict__ items, int32_t* __restrict__ n_items) {
+    __shared__ int32_t sp[PLAN_THREADS], si[PLAN_THREADS];
+    const int t = threadIdx.x;
+    const int per = (L + PLAN_THREADS - 1) / PLAN_THREADS;
+    const int b = t * per, e = min(L, b + per);
+    int32_t np = 0, ni = 0;
+    for (int i = b; i < e; ++i) {
+        const int c = lcount[order[i]];
+        np += c;
+        ni += items_of(c, gmax);
+    }
+    sp[t] = np;
+    si[t] = ni;
+    __syncthreads();
+    for (int o = 1; o < PLAN_THREADS; o <<= 1) {
+        int32_t vp = t >= o ? sp[t - o] : 0, vi = t >= o ? si[t - o] : 0;
+        __syncthreads();
+        sp[t] += vp;
+        si[t] += vi;
+        __syncthreads();
+    }
+    int32_t pbase = sp[t] - np, ibase = si[t] - ni;
+    for (int i = b; i < e; ++i) {
+        const int l = order[i];
+        const int c = lcount[l];
+        lstart[l] = pbase;
+        const int n = items_of(c, gmax);
+        int pb = pbase;
+        for (int j = 0; j < n; ++j) {
+            const int sz = c / n + (j < c % n ? 1 : 0);
+            items[ibase + j] = ScanItem{l, pb, sz, 0};
+            pb += sz;
+        }
+        pbase += c;
+        ibase += n;
+    }
+    if (t == PLAN_THREADS - 1) *n_items = si[t];
+}
+
+__global__ void pair_scatter_kernel(const int32_t* __restrict__ probes, int nq, int P, int L,
+                                    const int32_t* __restrict__ lstart,
+                                    int32_t* __restrict__ lcursor, int32_t* __restrict__ pair_q,
+                                    int32_t* __restrict__ pair_slot) {
+    const int64_t n = (int64_t)nq * P;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int l = probes[i];
+        if (l < 0 || l >= L) continue;
+        const int pos = lstart[l] + atomicAdd(&lcursor[l], 1);
+        pair_q[pos] = (int32_t)(i / P);
+        pair_slot[pos] = (int32_t)(i % P);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
+                                  const int32_t* list_order, int gmax, int32_t* lcount,
+                                  int32_t* lstart, int32_t* lcursor, ScanItem* items,
+                                  int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
+                                  cudaStream_t st) {
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(lcount, 0, sizeof(int32_t) * (size_t)L, st)) != cudaSuccess) return e;
+    if ((e = cudaMemsetAsync(lcursor, 0, sizeof(int32_t) * (size_t)L, st)) != cudaSuccess) return e;
+    const int64_t n = (int64_t)nq * P;
+    const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
+    if (n > 0) probe_hist_kernel<<<blocks, 256, 0, st>>>(probes, n, L, lcount);
+    plan_items_kernel<<<1, PLAN_THREADS, 0, st>>>(lcount, list_order, L, gmax, lstart, items,
+                                                  n_items);
+    if (n > 0)
+        pair_scatter_kernel<<<blocks, 256, 0, st>>>(probes, nq, P, L, lstart, lcursor, pair_q,
+                                                    pair_slot);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Merge: per query, the k smallest of its P partial lists by (score, slot, j),
+// which is the order (score, probe rank, row in list).  The candidates are first
+// cut at tau = the smallest k-th score among full partial lists (every answer is
+// <= tau and at least k candidates are), then sorted in shared memory.  If more
+// than MCAP survive (massive ties), an exact radix selection over all candidates
+// decides instead.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int MRG_BLOCK = 256;
+constexpr int MCAP = 4096;
+
+__device__ void bitonic_u64(unsigned long long* a, int n) {
+    for (int k = 2; k <= n; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += MRG_BLOCK) {
+                const int p = i ^ j;
+                if (p > i) {
+                    const unsigned long long x = a[i], y = a[p];
+                    if ((x > y) == ((i & k) == 0)) {
+                        a[i] = y;
+                        a[p] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+}
+
+// rank-th smallest (1-based) 32-bit key among key_of(i), i < n.
+template <class F>
+__device__ uint32_t radix_select32(F key_of, int64_t n, unsigned rank, unsigned* hist,
+                                   unsigned* shv) {
+    uint32_t prefix = 0, mask = 0;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int i = threadIdx.x; i < 256; i += MRG_BLOCK) hist[i] = 0;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < n; i += MRG_BLOCK) {
+            const uint32_t k = key_of(i);
+            if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned r = rank;
+            int b = 0;
+            for (; b < 256; ++b) {
+                if (r <= hist[b]) break;
+                r -= hist[b];
+            }
+            shv[0] = prefix | ((uint32_t)b << shift);
+            shv[1] = r;
+        }
+        __syncthreads();
+        prefix = shv[0];
+        rank = shv[1];
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    return prefix;
+}
+
+// Candidate i = slot * k + j of query q lives at q * stride_q + slot * stride_slot
+// + j.  part_row holds arena rows mapped through row_ids, or, when row_ids is
+// null, the ids themselves.
+__global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
+    const float* __restrict__ part_score, const int64_t* __restrict__ part_row,
+    const int64_t* __restrict__ row_ids, int P, int k, int64_t stride_q, int64_t stride_slot,
+    int64_t* __restrict__ out_ids, float* __restrict__ out_scores,
+    int32_t* __restrict__ out_counts) {
+    __shared__ unsigned long long cand[MCAP];
+    __shared__ unsigned hist[256];
+    __shared__ unsigned shv[4];
+    __shared__ unsigned s_tau, s_cnt, s_valid;
+    const int q = blockIdx.x;
+    const int64_t n = (int64_t)P * k;
+    const float* ps = part_score + (int64_t)q * stride_q;
+    const int64_t* pr = part_row + (int64_t)q * stride_q;
+    const float INF = __int_as_float(0x7f800000);
+    auto at = [&](int64_t i) -> int64_t { return (i / k) * stride_slot + (i % k); };
+
+    // tau: smallest k-th score among full partial lists; count valid candidates
+    float tau = INF;
+    unsigned nvalid = 0;
+    for (int s = threadIdx.x; s < P; s += MRG_BLOCK) {
+        const float last = ps[(int64_t)s * stride_slot + k - 1];
+        if (score_valid(last)) tau = fminf(tau, last);
+    }
+    for (int64_t i = threadIdx.x; i < n; i += MRG_BLOCK) nvalid += score_valid(ps[at(i)]) ? 1u : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        tau = fminf(tau, __shfl_xor_sync(0xffffffffu, tau, o));
+        nvalid += __shfl_xor_sync(0xffffffffu, nvalid, o);
+    }
+    if (threadIdx.x == 0) {
+        s_tau = float_key(INF);
+        s_cnt = 0;
+        s_valid = 0;
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+        atomicMin(&s_tau, float_key(tau));
+        atomicAdd(&s_valid, nvalid);
+    }
+    __syncthreads();
+    tau = key_float(s_tau);
+    const unsigned total_valid = s_valid;
+    const int kk = (int)((unsigned)k < total_valid ? (unsigned)k : total_valid);
+    for (int64_t i = threadIdx.x; i < n; i += MRG_BLOCK) {
+        const float s = ps[at(i)];
+        if (score_valid(s) && s <= tau) {
+            const unsigned pos = atomicAdd(&s_cnt, 1u);
+            if (pos < (unsigned)MCAP)
+                cand[pos] = ((unsigned long long)float_key(s) << 32) | (uint32_t)i;
+        }
+    }
+    __syncthreads();
+    const unsigned cnt = s_cnt;
+    if (cnt <= (unsigned)MCAP) {
+        int n2 = 1;
+        while (n2 < (int)cnt) n2 <<= 1;
+        for (int i = (int)cnt + threadIdx.x; i < n2; i += MRG_BLOCK) cand[i] = ~0ull;
+        __syncthreads();
+        bitonic_u64(cand, n2);
+    } else {
+        // exact selection over all candidates (keys are unique: (score, index))
+        auto hi_key = [&](int64_t i) -> uint32_t {
+            const float s = ps[at(i)];
+            return score_valid(s) ? float_key(s) : 0xffffffffu;
+        };
+        const uint32_t kh = radix_select32(hi_key, n, (unsigned)kk, hist, shv);
+        // m = #candidates with a smaller score key
+        if (threadIdx.x == 0) s_cnt = 0;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < n; i += MRG_BLOCK)
+            if (hi_key(i) < kh) atomicAdd(&s_cnt, 1u);
+        __syncthreads();
+        const unsigned m = s_cnt;
+        auto lo_key = [&](int64_t i) -> uint32_t {
+            return hi_key(i) == kh ? (uint32_t)i : 0xffffffffu;
+        };
+        const uint32_t kl = radix_select32(lo_key, n, (unsigned)kk - m, hist, shv);
+        if (threadIdx.x == 0) s_cnt = 0;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < n; i += MRG_BLOCK) {
+            const uint32_t h = hi_key(i);
+            if (h < kh || (h == kh && (uint32_t)i <= kl)) {
+                const unsigned pos = atomicAdd(&s_cnt, 1u);
+                if (pos < (unsigned)MCAP) cand[pos] = ((unsigned long long)h << 32) | (uint32_t)i;
+            }
+        }
+        __syncthreads();
+        int n2 = 1;
+        while (n2 < kk) n2 <<= 1;
+        for (int i = kk + threadIdx.x; i < n2; i += MRG_BLOCK) cand[i] = ~0ull;
+        __syncthreads();
+        bitonic_u64(cand, n2);
+    }
+    for (int j = threadIdx.x; j < k; j += MRG_BLOCK) {
+        int64_t id = -1;
+        float s = INF;
+        if (j < kk) {
+            const unsigned long long c = cand[j];
+            const int64_t off = at((int64_t)(c & 0xffffffffu));
+            s = ps[off];
+            id = row_ids ? row_ids[pr[off]] : pr[off];
+        }
+        out_ids[(int64_t)q * k + j] = id;
+        out_scores[(int64_t)q * k + j] = s;
+    }
+    if (threadIdx.x == 0) out_counts[q] = kk;
+}
+}  // namespace
+
+cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
+                              const int64_t* row_ids, int nq, int P, int k, int64_t* out_ids,
+                              float* out_scores, int32_t* out_counts, cudaStream_t st) {
+    if (nq <= 0) return cudaSuccess;
+    merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(part_score, part_row, row_ids, P, k,
+                                                (int64_t)P * k, k, out_ids, out_scores,
+                                                out_counts);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_shards(const float* scores, const int64_t* ids, int nshard, int nq, int k,
+                                int64_t* out_ids, float* out_scores, int32_t* out_counts,
+                                cudaStream_t st) {
+    if (nq <= 0 || k <= 0) return cudaSuccess;
+    merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(scores, ids, nullptr, nshard, k, k,
+                                                (int64_t)nq * k, out_ids, out_scores, out_counts);
+    return cudaGetLastError();
+}
+
+}  // namespace m3g

@@ -1,0 +1,83 @@
+// kernels.h -- host-side launchers of the m3gpu CUDA kernels (internal to
+// libm3gpu; the public C ABI is include/m3gpu.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace m3g {
+
+// ---- coarse quantizer (k_coarse.cu) ----
+void launch_row_norms(const float* X, int64_t ld, int64_t n, int d, float* nrm_up, float* nrm2,
+                      cudaStream_t st);
+void launch_sgemm_nt(const float* A, int64_t lda, const float* B, int64_t ldb, float* S,
+                     int64_t lds, int M, int N, int K, cudaStream_t st);
+float sgemm_error_beta(int K);
+size_t select_smem_bytes(int L, int D);
+int select_max_dim();
+cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t ldq, const float* C,
+                                 int64_t ldc, const float* qn, const float* qn2, const float* cn,
+                                 const float* cn2, int nq, int L, int D, int metric,
+                                 int normalized, float beta, float gamma, int P, int nan_is_none,
+                                 int32_t* probes, cudaStream_t st);
+
+// ---- list scan (k_scan.cu) ----
+struct ScanItem {
+    int32_t list;        // cluster id
+    int32_t pair_begin;  // first (query, probe slot) pair of this item in the pair arrays
+    int32_t npairs;      // number of queries in the item (<= gmax)
+    int32_t pad;
+};
+
+// Row boxes of the list arena for the scan: four 2-D tensor maps over the
+// arena viewed as [rows, dpad] fp32, box width 32 floats (128 B, SWIZZLE_128B)
+// and heights 64 / 32 / 16 / 8 rows.
+struct RowMaps {
+    CUtensorMap m64, m32, m16, m8;
+};
+
+struct ScanArgs {
+    const float* Q;          // [nq, dpad] queries (rows padded with zeros)
+    int dpad;                // floats per arena / query row (multiple of 4)
+    const int64_t* list_off; // [L] first arena row of each list
+    const int32_t* list_len; // [L] rows in each list
+    const uint8_t* alive;    // [arena rows] tombstones (0 = erased)
+    const float* rnorm2;     // [arena rows] ||x||^2 (non-normalised COSINE only)
+    const float* qnorm2;     // [nq] ||q||^2 (non-normalised COSINE only)
+    const ScanItem* items;
+    const int32_t* n_items;  // device count
+    int32_t* item_counter;   // device, zeroed before launch
+    const int32_t* pair_q;
+    const int32_t* pair_slot;
+    int k, P, metric, normalized;
+    float* part_score;       // [nq, P, k]
+    int64_t* part_row;       // [nq, P, k] arena row, -1 for empty
+    int* err;
+};
+
+int scan_kmax();
+int scan_gmax_for_dim(int dpad);
+cudaError_t launch_list_scan(const RowMaps& maps, const ScanArgs& a, int gmax, int grid,
+                             cudaStream_t st);
+
+// Work list: per-list counts of (query, probe) pairs, items, and the pairs
+// grouped by list.  list_order lists the clusters longest first.
+cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
+                                  const int32_t* list_order, int gmax, int32_t* lcount,
+                                  int32_t* lstart, int32_t* lcursor, ScanItem* items,
+                                  int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
+                                  cudaStream_t st);
+
+// Final merge of the per-(query, probe) partial top-k into the answer.
+cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
+                              const int64_t* row_ids, int nq, int P, int k, int64_t* out_ids,
+                              float* out_scores, int32_t* out_counts, cudaStream_t st);
+
+// Merge of per-shard answers [nshard, nq, k] (scores ascending per row, ids,
+// -1 / +inf padding) into [nq, k]; ties broken by (shard, position).
+cudaError_t launch_merge_shards(const float* scores, const int64_t* ids, int nshard, int nq, int k,
+                                int64_t* out_ids, float* out_scores, int32_t* out_counts,
+                                cudaStream_t st);
+
+}  // namespace m3g

@@ -1,0 +1,43 @@
+// kernels_kmeans.h -- launchers of k_kmeans.cu (internal to libm3gpu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace m3g {
+
+// Rows per chunk of the stable counting sort for n rows and L clusters.
+int64_t sort_chunk_rows(int64_t n, int L);
+// perm[start[l] .. start[l+1]) = rows assigned to l, ascending.  counts holds
+// ceil(n/chunk) * L ints, totals L ints, start L+1 int64s, perm n int64s.
+cudaError_t launch_stable_cluster_sort(const int32_t* assign, int64_t n, int L, int64_t chunk,
+                                       int32_t* counts, int32_t* totals, int64_t* start,
+                                       int64_t* perm, cudaStream_t st);
+cudaError_t launch_centroid_update(const float* X, int64_t ldx, const int64_t* perm,
+                                   const int64_t* start, int L, int d, float* C, int64_t ldc,
+                                   cudaStream_t st);
+
+cudaError_t launch_gather_rows(const float* src, int64_t lds, const int64_t* idx, int64_t n,
+                               int width, float* dst, int64_t ldd, cudaStream_t st);
+cudaError_t launch_scatter_rows(const float* src, int64_t lds, const int64_t* dst_rows, int64_t n,
+                                int width, float* dst, int64_t ldd, cudaStream_t st);
+cudaError_t launch_gather_i64(const int64_t* src, const int64_t* idx, int64_t n, int64_t* dst,
+                              cudaStream_t st);
+cudaError_t launch_gather_f32(const float* src, const int64_t* idx, int64_t n, float* dst,
+                              cudaStream_t st);
+cudaError_t launch_gather_u8(const uint8_t* src, const int64_t* idx, int64_t n, uint8_t* dst,
+                             cudaStream_t st);
+cudaError_t launch_scatter_i64(const int64_t* src, const int64_t* idx, int64_t n, int64_t* dst,
+                               cudaStream_t st);
+cudaError_t launch_set_bytes(uint8_t* dst, const int64_t* idx, int64_t n, uint8_t v,
+                             cudaStream_t st);
+cudaError_t launch_iota_rows(int32_t* out, int64_t nrows, int width, cudaStream_t st);
+cudaError_t launch_broadcast_row(const int32_t* row, int width, int64_t nrows, int32_t* out,
+                                 cudaStream_t st);
+cudaError_t launch_probed_rows(const int32_t* lcount, const int32_t* list_len, int L,
+                               unsigned long long* out_rows, unsigned long long* out_pairs,
+                               cudaStream_t st);
+
+}  // namespace m3g

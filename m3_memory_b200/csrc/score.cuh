@@ -1,0 +1,86 @@
+// score.cuh -- the reference's distance in its exact arithmetic, plus the error
+// bounds that let a faster approximate score stand in for it during selection.
+#pragma once
+
+#include "common.cuh"
+
+namespace m3g {
+
+// unified_score of AgentMemory/M3/include/base.h:22-31 with the kernels of
+// AgentMemory/M3/src/base.cpp:12-41, evaluated with the reference's own
+// rounding: fp32, one rounding per multiply / add / subtract (the reference is
+// built for baseline x86-64, which has no FMA), summed in index order.  The
+// explicit _rn intrinsics keep nvcc from contracting into FMAs.  `a` is read
+// with stride 1 from any memory space; `b` likewise.
+__device__ __forceinline__ float exact_score(const float* __restrict__ a,
+                                             const float* __restrict__ b, int d, int metric,
+                                             bool normalized) {
+    if (metric == kL2) {
+        float s = 0.f;
+        for (int i = 0; i < d; ++i) {
+            float df = __fsub_rn(a[i], b[i]);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+        }
+        return s;
+    }
+    if (metric == kIP || normalized) {
+        float s = 0.f;
+        for (int i = 0; i < d; ++i) s = __fadd_rn(s, __fmul_rn(a[i], b[i]));
+        return metric == kIP ? -s : __fsub_rn(1.f, s);
+    }
+    float dot = 0.f, na = 0.f, nb = 0.f;
+    for (int i = 0; i < d; ++i) {
+        dot = __fadd_rn(dot, __fmul_rn(a[i], b[i]));
+        na = __fadd_rn(na, __fmul_rn(a[i], a[i]));
+        nb = __fadd_rn(nb, __fmul_rn(b[i], b[i]));
+    }
+    if (na == 0.f || nb == 0.f) return 1.f;
+    return __fsub_rn(1.f, __fdiv_rn(dot, __fsqrt_rn(__fmul_rn(na, nb))));
+}
+
+// Bounds for selecting by an approximate inner product.
+//
+// `dot` approximates <q, c> with |dot - <q,c>| <= beta * nq * nc, where nq, nc
+// are upper bounds of the Euclidean norms.  gamma bounds the reference's own
+// sequential-sum error relative to the same norm product (D * 2^-24, with slack).
+// On return [lo, hi] contains both the exact real-valued unified score and the
+// reference's rounded one, for every metric.  qn2 / cn2 are the squared norms in
+// fp32 (used only by L2's approximate value).  Zero-norm vectors under
+// non-normalised COSINE make the interval unbounded: the reference special-cases
+// them (base.cpp:39) and the exact recheck must decide.
+__device__ __forceinline__ void approx_bounds(float dot, float nq, float nc, float qn2, float cn2,
+                                              float beta, float gamma, int metric,
+                                              bool normalized, float* lo, float* hi) {
+    const float INF = __int_as_float(0x7f800000);
+    float a, e;
+    if (metric == kL2) {
+        a = qn2 + cn2 - 2.f * dot;
+        float s = nq + nc;
+        e = (2.f * beta + 2.f * gamma + 1e-6f) * (s * s);
+    } else if (metric == kIP) {
+        a = -dot;
+        e = (beta + gamma) * (nq * nc) * 2.f;
+    } else if (normalized) {
+        a = 1.f - dot;
+        e = (beta + gamma) * (nq * nc) * 2.f + 2.4e-7f * (fabsf(a) + 1.f);
+    } else {
+        float den = nq * nc;
+        if (!(nq > 1e-15f && nc > 1e-15f && nq < 1e15f && nc < 1e15f)) {
+            *lo = -INF;
+            *hi = INF;
+            return;
+        }
+        a = 1.f - dot / den;
+        e = (beta + 2.f * gamma) * 2.f + 4e-6f + 2.4e-7f * (fabsf(a) + 1.f);
+    }
+    e = e + 1e-30f;
+    if (!(fabsf(a) < INF) || !(e < INF)) {
+        *lo = -INF;
+        *hi = INF;
+        return;
+    }
+    *lo = __fsub_rd(a, e);
+    *hi = __fadd_ru(a, e);
+}
+
+}  // namespace m3g
