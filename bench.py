@@ -60,6 +60,8 @@ def make_data():
     from m3_memory_b200 import synthetic as S
 
     rng = np.random.default_rng(SEED)
+    if N_VEC != 1_000_000:
+        log(f"note: reduced profiling case, {N_VEC} vectors / {NLIST} lists (not the headline)")
     means = S.mixture_means(NCOMP, DIM, rng)
     X, _ = S.gaussian_mixture(N_VEC, means, SIGMA, rng)
     Q, _ = S.gaussian_mixture(BATCH * NBATCH, means, SIGMA, rng)
@@ -509,7 +511,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nvec", type=int, default=None,
+                    help="profiling only: fewer vectors (the headline line uses 1M)")
+    ap.add_argument("--nlist", type=int, default=None, help="profiling only: fewer lists")
     args = ap.parse_args()
+    global N_VEC, NLIST, WORKLOAD
+    if args.nvec or args.nlist:
+        N_VEC = args.nvec or N_VEC
+        NLIST = args.nlist or NLIST
+        WORKLOAD = f"PROFILING CASE (not headline): {N_VEC} x {DIM}, nlist {NLIST}"
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

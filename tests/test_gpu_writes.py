@@ -109,8 +109,8 @@ def test_writer_error_surfaces_at_flush(cabi):
     assert e.enqueue_update(0, 1, np.array([7]), v[:1], False)  # absent, no insert
     with pytest.raises(cabi.M3GError, match="id not found"):
         e.flush()
-    assert e.enqueue_insert(0, 9, np.array([8]), v[:1])  # bad cluster
-    with pytest.raises(cabi.M3GError, match="invalid cluster_id"):
+    assert e.enqueue_insert(0, 9, np.array([8]), v[:1])  # bad cluster: std::out_of_range
+    with pytest.raises(IndexError, match="invalid cluster_id"):
         e.flush()
     e.stop()
     assert not e.enqueue_insert(0, 0, np.array([8]), v[:1])  # stopped
