@@ -177,9 +177,17 @@ __device__ uint32_t block_radix_select(KeyOf key_of, int L, unsigned rank, SelSh
         const int shift = 24 - 8 * pass;
         for (int i = threadIdx.x; i < 256; i += SEL_BLOCK) sh.hist[i] = 0;
         __syncthreads();
-        for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
-            const uint32_t k = key_of(c);
-            if ((k & mask) == prefix) atomicAdd(&sh.hist[(k >> shift) & 255u], 1u);
+        for (int c0 = 0; c0 < L; c0 += SEL_BLOCK) {
+            const int c = c0 + threadIdx.x;
+            int bin = -1;
+            if (c < L) {
+                const uint32_t k = key_of(c);
+                if ((k & mask) == prefix) bin = (int)((k >> shift) & 255u);
+            }
+            // near-equal keys share a bin: one atomic per distinct bin per warp
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (bin >= 0 && (threadIdx.x & 31) == __ffs(peers) - 1)
+                atomicAdd(&sh.hist[bin], (unsigned)__popc(peers));
         }
         __syncthreads();
         if (threadIdx.x < 32) {

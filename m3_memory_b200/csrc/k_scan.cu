@@ -12,12 +12,14 @@
 //               item's query rows into a double-buffered query area, and streams
 //               the list's rows through a ring of shared-memory stages with 2-D TMA
 //               (32 dims x up to 64 rows per stage, SWIZZLE_128B, no multicast).
-//   warps 0..7  consumers: split K -- warp w takes chunks w, w+8, ... of each
-//               64-row tile; each lane owns rows lane and lane+32 and keeps one fp32
-//               FMA accumulator per (row, query).  The eight partial sums are
-//               added in a fixed order, turned into the unified score, masked by
-//               tombstones, and each warp w < g folds the tile into the running
-//               top-k of query w.
+//   warps 0..7  consumers: split K inside each stage -- warp w takes 16-byte
+//               column slot w of every 32-dim stage, for rows lane and lane+32,
+//               keeping one fp32 FMA accumulator per (row, query); all eight warps
+//               read each stage, so the whole ring beyond the current stage stays
+//               in flight.  The eight partial sums are added in a fixed order,
+//               turned into the unified score, masked by tombstones, and each warp
+//               w < g folds the tile into the running top-k of query w (a register
+//               bitonic sort + merge for k <= 32, an insertion list for larger k).
 // Ordering: candidates are ranked by (score, probe slot, row in list), which is
 // the reference's visiting order; scores differ from the reference's only by
 // fp32 summation order.
@@ -40,6 +42,7 @@ constexpr int MAX_STAGES = 12;
 constexpr int MIN_STAGES = 4;
 constexpr int PSTRIDE = GMAX + 1;  // partial-sum row stride (bank-conflict padding)
 constexpr int SMEM_LIMIT = 227 * 1024;
+static_assert(NCW == KC / 4, "each consumer warp owns one 16-byte column slot of a stage");
 
 struct ItemInfo {
     int32_t list;      // -1: no more items
@@ -109,6 +112,9 @@ __device__ void drain_stages(uint64_t* full, int nstage, uint32_t seq_end) {
     }
 }
 
+// One 64-row tile: every consumer warp walks all of the tile's stages; warp w
+// takes the 16-byte column slot w of each 32-dim stage for rows lane and
+// lane+32, so the eight warps share each stage and release it together.
 template <int NQ, bool L2>
 __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring,
                                             const float* qbuf, uint64_t* full, uint64_t* empty,
@@ -121,7 +127,10 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
         acc1[i] = 0.f;
     }
     const int r0 = lane, r1 = lane + 32;
-    for (int c = warp; c < nchunks; c += NCW) {
+    const uint32_t off0 = r0 * 128 + ((warp ^ (r0 & 7)) << 4);
+    const uint32_t off1 = r1 * 128 + ((warp ^ (r1 & 7)) << 4);
+    const float* qw = qbuf + warp * 4;
+    for (int c = 0; c < nchunks; ++c) {
         const uint32_t s = seq_tile + (uint32_t)c;
         const int stage = (int)(s % (uint32_t)L.nstage);
         bool got = ok && mbar_wait(&full[stage], (s / (uint32_t)L.nstage) & 1u, err);
@@ -133,34 +142,31 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
             continue;
         }
         const uint32_t base = smem_u32(ring + (size_t)stage * STAGE_BYTES);
-        const float* qc = qbuf + c * KC;
+        const float4 x0 = lds128(base + off0);
+        const float4 x1 = lds128(base + off1);
+        const float* qc = qw + c * KC;
 #pragma unroll
-        for (int j = 0; j < KC / 4; ++j) {
-            const float4 x0 = lds128(base + r0 * 128 + ((j ^ (r0 & 7)) << 4));
-            const float4 x1 = lds128(base + r1 * 128 + ((j ^ (r1 & 7)) << 4));
-#pragma unroll
-            for (int qi = 0; qi < NQ; ++qi) {
-                const float4 qv = *reinterpret_cast<const float4*>(qc + qi * L.qstride + j * 4);
-                if (L2) {
-                    float d;
-                    d = x0.x - qv.x; acc0[qi] = fmaf(d, d, acc0[qi]);
-                    d = x0.y - qv.y; acc0[qi] = fmaf(d, d, acc0[qi]);
-                    d = x0.z - qv.z; acc0[qi] = fmaf(d, d, acc0[qi]);
-                    d = x0.w - qv.w; acc0[qi] = fmaf(d, d, acc0[qi]);
-                    d = x1.x - qv.x; acc1[qi] = fmaf(d, d, acc1[qi]);
-                    d = x1.y - qv.y; acc1[qi] = fmaf(d, d, acc1[qi]);
-                    d = x1.z - qv.z; acc1[qi] = fmaf(d, d, acc1[qi]);
-                    d = x1.w - qv.w; acc1[qi] = fmaf(d, d, acc1[qi]);
-                } else {
-                    acc0[qi] = fmaf(x0.x, qv.x, acc0[qi]);
-                    acc0[qi] = fmaf(x0.y, qv.y, acc0[qi]);
-                    acc0[qi] = fmaf(x0.z, qv.z, acc0[qi]);
-                    acc0[qi] = fmaf(x0.w, qv.w, acc0[qi]);
-                    acc1[qi] = fmaf(x1.x, qv.x, acc1[qi]);
-                    acc1[qi] = fmaf(x1.y, qv.y, acc1[qi]);
-                    acc1[qi] = fmaf(x1.z, qv.z, acc1[qi]);
-                    acc1[qi] = fmaf(x1.w, qv.w, acc1[qi]);
-                }
+        for (int qi = 0; qi < NQ; ++qi) {
+            const float4 qv = *reinterpret_cast<const float4*>(qc + qi * L.qstride);
+            if (L2) {
+                float d;
+                d = x0.x - qv.x; acc0[qi] = fmaf(d, d, acc0[qi]);
+                d = x0.y - qv.y; acc0[qi] = fmaf(d, d, acc0[qi]);
+                d = x0.z - qv.z; acc0[qi] = fmaf(d, d, acc0[qi]);
+                d = x0.w - qv.w; acc0[qi] = fmaf(d, d, acc0[qi]);
+                d = x1.x - qv.x; acc1[qi] = fmaf(d, d, acc1[qi]);
+                d = x1.y - qv.y; acc1[qi] = fmaf(d, d, acc1[qi]);
+                d = x1.z - qv.z; acc1[qi] = fmaf(d, d, acc1[qi]);
+                d = x1.w - qv.w; acc1[qi] = fmaf(d, d, acc1[qi]);
+            } else {
+                acc0[qi] = fmaf(x0.x, qv.x, acc0[qi]);
+                acc0[qi] = fmaf(x0.y, qv.y, acc0[qi]);
+                acc0[qi] = fmaf(x0.z, qv.z, acc0[qi]);
+                acc0[qi] = fmaf(x0.w, qv.w, acc0[qi]);
+                acc1[qi] = fmaf(x1.x, qv.x, acc1[qi]);
+                acc1[qi] = fmaf(x1.y, qv.y, acc1[qi]);
+                acc1[qi] = fmaf(x1.z, qv.z, acc1[qi]);
+                acc1[qi] = fmaf(x1.w, qv.w, acc1[qi]);
             }
         }
         __syncwarp();
@@ -169,16 +175,75 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
 }
 
 template <bool L2>
-__device__ __forceinline__ void tile_dispatch(int nq_rounded, const Layout& L, unsigned char* ring,
+__device__ __forceinline__ void tile_dispatch(int g, const Layout& L, unsigned char* ring,
                                               const float* qbuf, uint64_t* full, uint64_t* empty,
                                               uint32_t seq_tile, int nchunks, int warp, int lane,
                                               float (&acc0)[GMAX], float (&acc1)[GMAX], int* err,
                                               bool& ok) {
-    switch (nq_rounded) {
-        case 1: tile_chunks<1, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
-        case 2: tile_chunks<2, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
-        case 4: tile_chunks<4, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+#define M3G_TILE(n) \
+    case n: tile_chunks<n, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+    switch (g) {
+        M3G_TILE(1) M3G_TILE(2) M3G_TILE(3) M3G_TILE(4) M3G_TILE(5) M3G_TILE(6) M3G_TILE(7)
         default: tile_chunks<8, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+    }
+#undef M3G_TILE
+}
+
+// ---- register top-k for k <= 32: lane i holds the i-th best key of the warp's
+// query, key = (score key << 32) | row, ascending; ~0 marks an empty slot.
+
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+    const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
+    const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
+    return ((unsigned long long)hi << 32) | lo;
+}
+
+__device__ __forceinline__ unsigned long long shfl_u64(unsigned long long v, int src) {
+    const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)v, src);
+    const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(v >> 32), src);
+    return ((unsigned long long)hi << 32) | lo;
+}
+
+// Bitonic sort of one key per lane, ascending across lanes.
+__device__ __forceinline__ unsigned long long warp_sort_asc(unsigned long long v, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const unsigned long long p = shfl_xor_u64(v, j);
+            const bool up = (lane & k) == 0;
+            const bool lower = (lane & j) == 0;
+            v = (lower == up) ? (p < v ? p : v) : (p > v ? p : v);
+        }
+    }
+    return v;
+}
+
+// top (ascending, lane i = entry i) <- the 32 smallest of top and cand (any order).
+__device__ __forceinline__ unsigned long long warp_merge_top(unsigned long long top,
+                                                             unsigned long long cand, int lane) {
+    const unsigned long long b = warp_sort_asc(cand, lane);
+    const unsigned long long rb = shfl_u64(b, 31 - lane);
+    unsigned long long c = top < rb ? top : rb;  // bitonic: the 32 smallest of both
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) {
+        const unsigned long long p = shfl_xor_u64(c, j);
+        const bool lower = (lane & j) == 0;
+        c = lower ? (p < c ? p : c) : (p > c ? p : c);
+    }
+    return c;
+}
+
+// Folds one candidate per lane into the register top-k (k <= 32).
+__device__ __forceinline__ void topk_fold_reg(unsigned long long& top, int k, float s, int32_t row,
+                                              int lane) {
+    const unsigned long long tau = shfl_u64(top, k - 1);
+    const unsigned long long key =
+        score_valid(s) ? (((unsigned long long)float_key(s) << 32) | (uint32_t)row) : ~0ull;
+    const bool cand = key < tau;
+    if (__any_sync(0xffffffffu, cand)) {
+        top = warp_merge_top(top, cand ? key : ~0ull, lane);
+        if (lane >= k) top = ~0ull;
     }
 }
 
@@ -272,7 +337,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < L.nstage; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], NCW);  // every consumer warp reads every stage
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&qfull[b], 1);
@@ -407,21 +472,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (list < 0) return;
         const int g = inf->npairs, nrows = inf->nrows;
         const int64_t off = inf->off;
-        const int nqr = g <= 1 ? 1 : g <= 2 ? 2 : g <= 4 ? 4 : 8;
         const float* qbuf = qbase + qb * qbuf_floats;
-        int cnt = 0;  // this warp's query (warp < g): entries held in tks/tkr
+        int cnt = 0;  // this warp's query (warp < g): entries held in tks/tkr (k > 32)
+        unsigned long long top = ~0ull;  // register top-k (k <= 32)
+        const bool reg_topk = a.k <= 32;
         const int ntiles = (nrows + TR - 1) / TR;
         for (int t = 0; t < ntiles; ++t) {
             float acc0[GMAX], acc1[GMAX];
             const uint32_t seq_tile = seq + (uint32_t)(t * nchunks);
             if (a.metric == kL2)
-                tile_dispatch<true>(nqr, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, a.err, ok);
+                tile_dispatch<true>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, a.err, ok);
             else
-                tile_dispatch<false>(nqr, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, a.err, ok);
+                tile_dispatch<false>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, a.err, ok);
             float* pw = part + warp * TR * PSTRIDE;
 #pragma unroll
             for (int qi = 0; qi < GMAX; ++qi) {
-                if (qi < nqr) {
+                if (qi < g) {
                     pw[lane * PSTRIDE + qi] = acc0[qi];
                     pw[(lane + 32) * PSTRIDE + qi] = acc1[qi];
                 }
@@ -453,16 +519,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (warp < g) {
                 const int rbase = t * TR;
                 const float s0 = sc[warp * TR + lane], s1 = sc[warp * TR + lane + 32];
-                topk_fold(tks, tkr, cnt, a.k, s0, rbase + lane, score_valid(s0), s1,
-                          rbase + lane + 32, score_valid(s1), lane);
+                if (reg_topk) {
+                    topk_fold_reg(top, a.k, s0, rbase + lane, lane);
+                    topk_fold_reg(top, a.k, s1, rbase + lane + 32, lane);
+                } else {
+                    topk_fold(tks, tkr, cnt, a.k, s0, rbase + lane, score_valid(s0), s1,
+                              rbase + lane + 32, score_valid(s1), lane);
+                }
             }
         }
         seq += (uint32_t)(ntiles * nchunks);
         if (warp < g) {
             const int64_t base = ((int64_t)inf->q[warp] * a.P + inf->slot[warp]) * a.k;
-            for (int j = lane; j < a.k; j += 32) {
-                a.part_score[base + j] = j < cnt ? tks[j] : INF;
-                a.part_row[base + j] = j < cnt ? off + tkr[j] : -1;
+            if (reg_topk) {
+                if (lane < a.k) {
+                    const bool v = top != ~0ull;
+                    a.part_score[base + lane] = v ? key_float((uint32_t)(top >> 32)) : INF;
+                    a.part_row[base + lane] = v ? off + (int64_t)(uint32_t)(top & 0xffffffffu) : -1;
+                }
+            } else {
+                for (int j = lane; j < a.k; j += 32) {
+                    a.part_score[base + j] = j < cnt ? tks[j] : INF;
+                    a.part_row[base + j] = j < cnt ? off + tkr[j] : -1;
+                }
             }
         }
         __syncwarp();
