@@ -11,9 +11,9 @@
 //   warp 8      producer: takes items from a global counter, bulk-copies the
 //               item's query rows into a double-buffered query area, and streams
 //               the list's rows through a ring of shared-memory stages with 2-D TMA
-//               (32 dims x up to 64 rows per stage, SWIZZLE_128B, no multicast).
+//               (32 dims x up to 128 rows per stage, SWIZZLE_128B, no multicast).
 //   warps 0..7  consumers: split K inside each stage -- warp w takes 16-byte
-//               column slot w of every 32-dim stage, for rows lane and lane+32,
+//               column slot w of every 32-dim stage, for rows lane + 32 m (m < 4),
 //               keeping one fp32 FMA accumulator per (row, query); all eight warps
 //               read each stage, so the whole ring beyond the current stage stays
 //               in flight.  The eight partial sums are added in a fixed order,
@@ -32,14 +32,15 @@ namespace m3g {
 namespace {
 
 constexpr int KC = 32;          // dims per stage (128 bytes of fp32)
-constexpr int TR = 64;          // rows per tile
+constexpr int RPL = 4;          // rows per lane
+constexpr int TR = 32 * RPL;    // rows per tile
 constexpr int NCW = 8;          // consumer warps
 constexpr int NTHREADS = (NCW + 1) * 32;
 constexpr int GMAX = 8;         // queries per item (upper bound of the runtime gmax)
 constexpr int KMAX = 256;       // largest k the fused top-k keeps
 constexpr int STAGE_BYTES = TR * KC * 4;
 constexpr int MAX_STAGES = 12;
-constexpr int MIN_STAGES = 4;
+constexpr int MIN_STAGES = 3;
 constexpr int PSTRIDE = GMAX + 1;  // partial-sum row stride (bank-conflict padding)
 constexpr int SMEM_LIMIT = 227 * 1024;
 static_assert(NCW == KC / 4, "each consumer warp owns one 16-byte column slot of a stage");
@@ -119,16 +120,13 @@ template <int NQ, bool L2>
 __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring,
                                             const float* qbuf, uint64_t* full, uint64_t* empty,
                                             uint32_t seq_tile, int nchunks, int warp, int lane,
-                                            float (&acc0)[GMAX], float (&acc1)[GMAX], int* err,
-                                            bool& ok) {
+                                            float (&acc)[RPL][GMAX], int* err, bool& ok) {
 #pragma unroll
-    for (int i = 0; i < GMAX; ++i) {
-        acc0[i] = 0.f;
-        acc1[i] = 0.f;
-    }
-    const int r0 = lane, r1 = lane + 32;
-    const uint32_t off0 = r0 * 128 + ((warp ^ (r0 & 7)) << 4);
-    const uint32_t off1 = r1 * 128 + ((warp ^ (r1 & 7)) << 4);
+    for (int r = 0; r < RPL; ++r)
+#pragma unroll
+        for (int i = 0; i < GMAX; ++i) acc[r][i] = 0.f;
+    // rows lane + 32 m share (row & 7) = (lane & 7): the swizzled slot is the same
+    const uint32_t off0 = lane * 128 + ((warp ^ (lane & 7)) << 4);
     const float* qw = qbuf + warp * 4;
     for (int c = 0; c < nchunks; ++c) {
         const uint32_t s = seq_tile + (uint32_t)c;
@@ -141,32 +139,28 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
             ok = false;
             continue;
         }
-        const uint32_t base = smem_u32(ring + (size_t)stage * STAGE_BYTES);
-        const float4 x0 = lds128(base + off0);
-        const float4 x1 = lds128(base + off1);
+        const uint32_t base = smem_u32(ring + (size_t)stage * STAGE_BYTES) + off0;
+        float4 x[RPL];
+#pragma unroll
+        for (int r = 0; r < RPL; ++r) x[r] = lds128(base + r * 32 * 128);
         const float* qc = qw + c * KC;
 #pragma unroll
         for (int qi = 0; qi < NQ; ++qi) {
             const float4 qv = *reinterpret_cast<const float4*>(qc + qi * L.qstride);
-            if (L2) {
-                float d;
-                d = x0.x - qv.x; acc0[qi] = fmaf(d, d, acc0[qi]);
-                d = x0.y - qv.y; acc0[qi] = fmaf(d, d, acc0[qi]);
-                d = x0.z - qv.z; acc0[qi] = fmaf(d, d, acc0[qi]);
-                d = x0.w - qv.w; acc0[qi] = fmaf(d, d, acc0[qi]);
-                d = x1.x - qv.x; acc1[qi] = fmaf(d, d, acc1[qi]);
-                d = x1.y - qv.y; acc1[qi] = fmaf(d, d, acc1[qi]);
-                d = x1.z - qv.z; acc1[qi] = fmaf(d, d, acc1[qi]);
-                d = x1.w - qv.w; acc1[qi] = fmaf(d, d, acc1[qi]);
-            } else {
-                acc0[qi] = fmaf(x0.x, qv.x, acc0[qi]);
-                acc0[qi] = fmaf(x0.y, qv.y, acc0[qi]);
-                acc0[qi] = fmaf(x0.z, qv.z, acc0[qi]);
-                acc0[qi] = fmaf(x0.w, qv.w, acc0[qi]);
-                acc1[qi] = fmaf(x1.x, qv.x, acc1[qi]);
-                acc1[qi] = fmaf(x1.y, qv.y, acc1[qi]);
-                acc1[qi] = fmaf(x1.z, qv.z, acc1[qi]);
-                acc1[qi] = fmaf(x1.w, qv.w, acc1[qi]);
+#pragma unroll
+            for (int r = 0; r < RPL; ++r) {
+                if (L2) {
+                    float d;
+                    d = x[r].x - qv.x; acc[r][qi] = fmaf(d, d, acc[r][qi]);
+                    d = x[r].y - qv.y; acc[r][qi] = fmaf(d, d, acc[r][qi]);
+                    d = x[r].z - qv.z; acc[r][qi] = fmaf(d, d, acc[r][qi]);
+                    d = x[r].w - qv.w; acc[r][qi] = fmaf(d, d, acc[r][qi]);
+                } else {
+                    acc[r][qi] = fmaf(x[r].x, qv.x, acc[r][qi]);
+                    acc[r][qi] = fmaf(x[r].y, qv.y, acc[r][qi]);
+                    acc[r][qi] = fmaf(x[r].z, qv.z, acc[r][qi]);
+                    acc[r][qi] = fmaf(x[r].w, qv.w, acc[r][qi]);
+                }
             }
         }
         __syncwarp();
@@ -178,13 +172,12 @@ template <bool L2>
 __device__ __forceinline__ void tile_dispatch(int g, const Layout& L, unsigned char* ring,
                                               const float* qbuf, uint64_t* full, uint64_t* empty,
                                               uint32_t seq_tile, int nchunks, int warp, int lane,
-                                              float (&acc0)[GMAX], float (&acc1)[GMAX], int* err,
-                                              bool& ok) {
+                                              float (&acc)[RPL][GMAX], int* err, bool& ok) {
 #define M3G_TILE(n) \
-    case n: tile_chunks<n, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+    case n: tile_chunks<n, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
     switch (g) {
         M3G_TILE(1) M3G_TILE(2) M3G_TILE(3) M3G_TILE(4) M3G_TILE(5) M3G_TILE(6) M3G_TILE(7)
-        default: tile_chunks<8, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, err, ok); break;
+        default: tile_chunks<8, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
     }
 #undef M3G_TILE
 }
@@ -346,6 +339,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         fence_mbar_init();
     }
     if (warp == NCW && lane == 0) {
+        prefetch_tensormap(&maps.m128);
         prefetch_tensormap(&maps.m64);
         prefetch_tensormap(&maps.m32);
         prefetch_tensormap(&maps.m16);
@@ -413,12 +407,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 bulk_g2s(qdst + lane * L.qstride, a.Q + (int64_t)myq * a.dpad,
                          (uint32_t)(a.dpad * 4), &qfull[qb]);
             q_issued = it + 1;
-            // stream the list: tiles of 64 rows, each as nchunks stages of 32 dims
+            // stream the list: tiles of 128 rows, each as nchunks stages of 32 dims
             const int ntiles = (nrows + TR - 1) / TR;
             for (int t = 0; t < ntiles && ok; ++t) {
                 const int rows_here = min(TR, nrows - t * TR);
                 const int r8 = (rows_here + 7) & ~7;
                 const int y0 = (int)(off + (int64_t)t * TR);
+                // the tile's rows as boxes of 128 / 64 / 32 / 16 / 8 rows (rows past
+                // the list's end, up to the next multiple of 8, are read and masked)
                 for (int c = 0; c < nchunks; ++c) {
                     const int stage = (int)(seq % (uint32_t)L.nstage);
                     const uint32_t use = seq / (uint32_t)L.nstage;
@@ -431,13 +427,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         mbar_arrive_expect_tx(&full[stage], (uint32_t)(r8 * 128));
                         int r = 0;
                         const int x = c * KC;
-                        if (r8 == 64) {
-                            tma_load_2d(dst, &maps.m64, x, y0, &full[stage]);
-                        } else {
-                            if (r8 - r >= 32) { tma_load_2d(dst + r * 128, &maps.m32, x, y0 + r, &full[stage]); r += 32; }
-                            if (r8 - r >= 16) { tma_load_2d(dst + r * 128, &maps.m16, x, y0 + r, &full[stage]); r += 16; }
-                            if (r8 - r >= 8) { tma_load_2d(dst + r * 128, &maps.m8, x, y0 + r, &full[stage]); r += 8; }
-                        }
+                        if (r8 - r >= 128) { tma_load_2d(dst + r * 128, &maps.m128, x, y0 + r, &full[stage]); r += 128; }
+                        if (r8 - r >= 64) { tma_load_2d(dst + r * 128, &maps.m64, x, y0 + r, &full[stage]); r += 64; }
+                        if (r8 - r >= 32) { tma_load_2d(dst + r * 128, &maps.m32, x, y0 + r, &full[stage]); r += 32; }
+                        if (r8 - r >= 16) { tma_load_2d(dst + r * 128, &maps.m16, x, y0 + r, &full[stage]); r += 16; }
+                        if (r8 - r >= 8) { tma_load_2d(dst + r * 128, &maps.m8, x, y0 + r, &full[stage]); r += 8; }
                     }
                     ++seq;
                 }
@@ -478,20 +472,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const bool reg_topk = a.k <= 32;
         const int ntiles = (nrows + TR - 1) / TR;
         for (int t = 0; t < ntiles; ++t) {
-            float acc0[GMAX], acc1[GMAX];
+            float acc[RPL][GMAX];
             const uint32_t seq_tile = seq + (uint32_t)(t * nchunks);
             if (a.metric == kL2)
-                tile_dispatch<true>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, a.err, ok);
+                tile_dispatch<true>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, a.err, ok);
             else
-                tile_dispatch<false>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc0, acc1, a.err, ok);
+                tile_dispatch<false>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, a.err, ok);
             float* pw = part + warp * TR * PSTRIDE;
 #pragma unroll
-            for (int qi = 0; qi < GMAX; ++qi) {
-                if (qi < g) {
-                    pw[lane * PSTRIDE + qi] = acc0[qi];
-                    pw[(lane + 32) * PSTRIDE + qi] = acc1[qi];
-                }
-            }
+            for (int r = 0; r < RPL; ++r)
+#pragma unroll
+                for (int qi = 0; qi < GMAX; ++qi)
+                    if (qi < g) pw[(lane + 32 * r) * PSTRIDE + qi] = acc[r][qi];
             // uniform stop if any warp's wait gave up during this tile
             if (named_bar_sync_or(1, NCW * 32, !ok)) return;
             const int rows_here = min(TR, nrows - t * TR);
@@ -518,13 +510,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             named_bar_sync(1, NCW * 32);
             if (warp < g) {
                 const int rbase = t * TR;
-                const float s0 = sc[warp * TR + lane], s1 = sc[warp * TR + lane + 32];
-                if (reg_topk) {
-                    topk_fold_reg(top, a.k, s0, rbase + lane, lane);
-                    topk_fold_reg(top, a.k, s1, rbase + lane + 32, lane);
-                } else {
-                    topk_fold(tks, tkr, cnt, a.k, s0, rbase + lane, score_valid(s0), s1,
-                              rbase + lane + 32, score_valid(s1), lane);
+#pragma unroll
+                for (int h = 0; h < RPL; h += 2) {
+                    const int ra = lane + 32 * h, rb = ra + 32;
+                    const float s0 = sc[warp * TR + ra], s1 = sc[warp * TR + rb];
+                    if (reg_topk) {
+                        topk_fold_reg(top, a.k, s0, rbase + ra, lane);
+                        topk_fold_reg(top, a.k, s1, rbase + rb, lane);
+                    } else {
+                        topk_fold(tks, tkr, cnt, a.k, s0, rbase + ra, score_valid(s0), s1,
+                                  rbase + rb, score_valid(s1), lane);
+                    }
                 }
             }
         }
