@@ -23,9 +23,16 @@ enum KernelError : int {
     kErrCapacity = 3,      // a fixed-size buffer would have overflowed
 };
 
-// Spin limit for every mbarrier wait: with the nanosleep back-off below this is
-// on the order of one second before the wait gives up.
+// Every mbarrier wait gives up after kWaitLimitNs of wall time (%globaltimer).
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+// Iteration cap of the waits that must not depend on the timer (drains).
 constexpr uint32_t kWaitSpinLimit = 1u << 22;
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -72,16 +79,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the warp for up to `hint_ns` while
+// the phase is incomplete (no issue slots burnt spinning).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity,
+                                                   uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  Returns false
-// (and records kErrWaitTimeout) when the limit runs out or another thread of the
-// launch has already recorded an error.
+// (and records kErrWaitTimeout) when kWaitLimitNs pass, or as soon as another
+// thread of the launch has recorded an error.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-    for (uint32_t i = 0; i < kWaitSpinLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 1023u) == 1023u) {
-            if (*(volatile int*)err != 0) return false;
-        }
-        if (i > 64) __nanosleep(128);
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+        if (*(volatile int*)err != 0) return false;
+        if (global_ns() - t0 > kWaitLimitNs) break;
     }
     atomicCAS(err, 0, (int)kErrWaitTimeout);
     return false;

@@ -144,25 +144,23 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
 #pragma unroll
         for (int r = 0; r < RPL; ++r) x[r] = lds128(base + r * 32 * 128);
         const float* qc = qw + c * KC;
+        float4 qv[NQ];
 #pragma unroll
-        for (int qi = 0; qi < NQ; ++qi) {
-            const float4 qv = *reinterpret_cast<const float4*>(qc + qi * L.qstride);
-#pragma unroll
-            for (int r = 0; r < RPL; ++r) {
-                if (L2) {
-                    float d;
-                    d = x[r].x - qv.x; acc[r][qi] = fmaf(d, d, acc[r][qi]);
-                    d = x[r].y - qv.y; acc[r][qi] = fmaf(d, d, acc[r][qi]);
-                    d = x[r].z - qv.z; acc[r][qi] = fmaf(d, d, acc[r][qi]);
-                    d = x[r].w - qv.w; acc[r][qi] = fmaf(d, d, acc[r][qi]);
-                } else {
-                    acc[r][qi] = fmaf(x[r].x, qv.x, acc[r][qi]);
-                    acc[r][qi] = fmaf(x[r].y, qv.y, acc[r][qi]);
-                    acc[r][qi] = fmaf(x[r].z, qv.z, acc[r][qi]);
-                    acc[r][qi] = fmaf(x[r].w, qv.w, acc[r][qi]);
-                }
-            }
+        for (int qi = 0; qi < NQ; ++qi)
+            qv[qi] = *reinterpret_cast<const float4*>(qc + qi * L.qstride);
+        // component-major: consecutive FMAs update different accumulators
+#define M3G_COMP(cx)                                                        \
+    _Pragma("unroll") for (int r = 0; r < RPL; ++r)                         \
+        _Pragma("unroll") for (int qi = 0; qi < NQ; ++qi) {                 \
+            if (L2) {                                                       \
+                const float d = x[r].cx - qv[qi].cx;                        \
+                acc[r][qi] = fmaf(d, d, acc[r][qi]);                        \
+            } else {                                                        \
+                acc[r][qi] = fmaf(x[r].cx, qv[qi].cx, acc[r][qi]);          \
+            }                                                               \
         }
+        M3G_COMP(x) M3G_COMP(y) M3G_COMP(z) M3G_COMP(w)
+#undef M3G_COMP
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
     }
