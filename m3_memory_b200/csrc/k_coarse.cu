@@ -162,6 +162,8 @@ constexpr int SEL_BLOCK = 256;
 constexpr int SEL_CAP = 2048;        // candidates rescored and sorted in shared memory
 constexpr int SEL_KEYS_SMEM = 8192;  // upper-bound keys cached in shared memory up to this L
 constexpr int SEL_SORT_MAX = 1024;   // largest P whose selection is returned sorted
+constexpr int SEL_OVERLAP_MAX = 256; // above this many candidates, all are rescored
+constexpr int SEL_EX_CHUNK = 128;    // dims per product chunk of a warp's exact rescoring
 
 struct SelShared {
     unsigned hist[256];
@@ -280,8 +282,12 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     const int q = blockIdx.x;
     float* qs = reinterpret_cast<float*>(sel_smem);                               // D floats
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(qs + ((D + 3) & ~3));  // SEL_CAP
-    uint32_t* hkeys = reinterpret_cast<uint32_t*>(cand + SEL_CAP);               // L (if cached)
+    float2* bnd = reinterpret_cast<float2*>(cand + SEL_CAP);                     // SEL_CAP
+    float* prod = reinterpret_cast<float*>(bnd + SEL_CAP);                       // 8 warps x 3 x chunk
+    unsigned char* needf = reinterpret_cast<unsigned char*>(prod + (SEL_BLOCK / 32) * 3 * SEL_EX_CHUNK);
+    uint32_t* hkeys = reinterpret_cast<uint32_t*>(needf + SEL_CAP);
     const bool cache = L <= SEL_KEYS_SMEM;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const float* qrow = Q + (int64_t)q * ldq;
     for (int i = threadIdx.x; i < D; i += SEL_BLOCK) qs[i] = qrow[i];
@@ -333,18 +339,48 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         if (cnt > (unsigned)SEL_CAP) {
             exact_all = true;
         } else {
-            // --- phase C: rescore candidates exactly, sort by (score, id)
-            int n2 = 1;
-            while (n2 < (int)cnt) n2 <<= 1;
-            for (int i = threadIdx.x; i < n2; i += SEL_BLOCK) {
-                if (i < (int)cnt) {
-                    const int c = (int)cand[i];
-                    const float r = exact_score(qs, C + (int64_t)c * ldc, D, metric, nrm);
-                    cand[i] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
+            // --- phase C: order the candidates by exact score.  A candidate whose
+            // interval overlaps no other candidate's is already ordered by its
+            // approximate value; the rest are rescored in the reference's exact
+            // arithmetic (one warp per candidate).  Keys: (score key, id).
+            for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK) {
+                float lo, hi;
+                bounds((int)cand[i], &lo, &hi);
+                bnd[i] = make_float2(lo, hi);
+            }
+            __syncthreads();
+            const bool all_exact = cnt > (unsigned)SEL_OVERLAP_MAX;
+            if (threadIdx.x == 0) sh.count2 = 0;
+            __syncthreads();
+            for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK) {
+                const float2 bi = bnd[i];
+                bool need = all_exact;
+                for (int j = 0; j < (int)cnt && !need; ++j)
+                    if (j != i && bnd[j].x <= bi.y && bi.x <= bnd[j].y) need = true;
+                const int c = (int)cand[i];
+                needf[i] = need ? 1 : 0;
+                if (need) {
+                    cand[i] = (unsigned)c;  // rescored below
                 } else {
-                    cand[i] = ~0ull;
+                    float lo, hi, a;
+                    approx_bounds(srow[c], nq, cn[c], nq2, cn2[c], beta, gamma, metric, nrm, &lo,
+                                  &hi, &a);
+                    cand[i] = ((unsigned long long)float_key(a) << 32) | (unsigned)c;
                 }
             }
+            __syncthreads();
+            float* wprod = prod + warp * 3 * SEL_EX_CHUNK;
+            for (int i = warp; i < (int)cnt; i += SEL_BLOCK / 32) {
+                if (!needf[i]) continue;
+                const int c = (int)(cand[i] & 0xffffffffu);
+                const float r = warp_exact_score(qs, C + (int64_t)c * ldc, D, metric, nrm, wprod,
+                                                 SEL_EX_CHUNK, lane);
+                if (lane == 0) cand[i] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
+            }
+            __syncthreads();
+            int n2 = 1;
+            while (n2 < (int)cnt) n2 <<= 1;
+            for (int i = (int)cnt + threadIdx.x; i < n2; i += SEL_BLOCK) cand[i] = ~0ull;
             __syncthreads();
             bitonic_sort_u64(cand, n2);
             for (int j = threadIdx.x; j < PP; j += SEL_BLOCK) {
@@ -412,7 +448,9 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
 }
 
 size_t select_smem_bytes(int L, int D) {
-    size_t b = sizeof(float) * (size_t)((D + 3) & ~3) + sizeof(unsigned long long) * SEL_CAP;
+    size_t b = sizeof(float) * (size_t)((D + 3) & ~3) + sizeof(unsigned long long) * SEL_CAP +
+               sizeof(float2) * SEL_CAP + sizeof(float) * (SEL_BLOCK / 32) * 3 * SEL_EX_CHUNK +
+               SEL_CAP;
     if (L <= SEL_KEYS_SMEM) b += sizeof(uint32_t) * (size_t)L;
     return b;
 }

@@ -116,7 +116,7 @@ __device__ void drain_stages(uint64_t* full, int nstage, uint32_t seq_end) {
 // One 64-row tile: every consumer warp walks all of the tile's stages; warp w
 // takes the 16-byte column slot w of each 32-dim stage for rows lane and
 // lane+32, so the eight warps share each stage and release it together.
-template <int NQ, bool L2>
+template <int NQ, int RG, bool L2>
 __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring,
                                             const float* qbuf, uint64_t* full, uint64_t* empty,
                                             uint32_t seq_tile, int nchunks, int warp, int lane,
@@ -140,9 +140,9 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
             continue;
         }
         const uint32_t base = smem_u32(ring + (size_t)stage * STAGE_BYTES) + off0;
-        float4 x[RPL];
+        float4 x[RG];
 #pragma unroll
-        for (int r = 0; r < RPL; ++r) x[r] = lds128(base + r * 32 * 128);
+        for (int r = 0; r < RG; ++r) x[r] = lds128(base + r * 32 * 128);
         const float* qc = qw + c * KC;
         float4 qv[NQ];
 #pragma unroll
@@ -150,7 +150,7 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
             qv[qi] = *reinterpret_cast<const float4*>(qc + qi * L.qstride);
         // component-major: consecutive FMAs update different accumulators
 #define M3G_COMP(cx)                                                        \
-    _Pragma("unroll") for (int r = 0; r < RPL; ++r)                         \
+    _Pragma("unroll") for (int r = 0; r < RG; ++r)                          \
         _Pragma("unroll") for (int qi = 0; qi < NQ; ++qi) {                 \
             if (L2) {                                                       \
                 const float d = x[r].cx - qv[qi].cx;                        \
@@ -166,18 +166,33 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
     }
 }
 
+// g queries, rg active 32-row groups (rows past the tile's end cost nothing).
+template <bool L2, int RG>
+__device__ __forceinline__ void tile_dispatch_g(int g, const Layout& L, unsigned char* ring,
+                                                const float* qbuf, uint64_t* full,
+                                                uint64_t* empty, uint32_t seq_tile, int nchunks,
+                                                int warp, int lane, float (&acc)[RPL][GMAX],
+                                                int* err, bool& ok) {
+#define M3G_TILE(n) \
+    case n: tile_chunks<n, RG, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+    switch (g) {
+        M3G_TILE(1) M3G_TILE(2) M3G_TILE(3) M3G_TILE(4) M3G_TILE(5) M3G_TILE(6) M3G_TILE(7)
+        default: tile_chunks<8, RG, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+    }
+#undef M3G_TILE
+}
+
 template <bool L2>
-__device__ __forceinline__ void tile_dispatch(int g, const Layout& L, unsigned char* ring,
+__device__ __forceinline__ void tile_dispatch(int g, int rg, const Layout& L, unsigned char* ring,
                                               const float* qbuf, uint64_t* full, uint64_t* empty,
                                               uint32_t seq_tile, int nchunks, int warp, int lane,
                                               float (&acc)[RPL][GMAX], int* err, bool& ok) {
-#define M3G_TILE(n) \
-    case n: tile_chunks<n, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
-    switch (g) {
-        M3G_TILE(1) M3G_TILE(2) M3G_TILE(3) M3G_TILE(4) M3G_TILE(5) M3G_TILE(6) M3G_TILE(7)
-        default: tile_chunks<8, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+    switch (rg) {
+        case 1: tile_dispatch_g<L2, 1>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+        case 2: tile_dispatch_g<L2, 2>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+        case 3: tile_dispatch_g<L2, 3>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+        default: tile_dispatch_g<L2, 4>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
     }
-#undef M3G_TILE
 }
 
 // ---- register top-k for k <= 32: lane i holds the i-th best key of the warp's
@@ -225,18 +240,43 @@ __device__ __forceinline__ unsigned long long warp_merge_top(unsigned long long 
     return c;
 }
 
-// Folds one candidate per lane into the register top-k (k <= 32).
-__device__ __forceinline__ void topk_fold_reg(unsigned long long& top, int k, float s, int32_t row,
-                                              int lane) {
-    const unsigned long long tau = shfl_u64(top, k - 1);
-    const unsigned long long key =
-        score_valid(s) ? (((unsigned long long)float_key(s) << 32) | (uint32_t)row) : ~0ull;
-    const bool cand = key < tau;
-    if (__any_sync(0xffffffffu, cand)) {
-        top = warp_merge_top(top, cand ? key : ~0ull, lane);
+// Register top-k (k <= 32) fed through a 32-slot shared-memory buffer: a row
+// that beats the current k-th key is appended; the buffer is merged into the
+// top list (sort + bitonic merge) only when it would overflow, and once more at
+// the end of the item, so merges are rare after the first few rows.
+struct RegTopK {
+    unsigned long long top = ~0ull;  // lane i: i-th best key (ascending)
+    unsigned long long tau = ~0ull;  // current k-th best key (all lanes)
+    int nbuf = 0;                    // keys waiting in the buffer (warp-uniform)
+
+    __device__ __forceinline__ void flush(unsigned long long* buf, int k, int lane) {
+        __syncwarp();
+        const unsigned long long b = lane < nbuf ? buf[lane] : ~0ull;
+        __syncwarp();
+        top = warp_merge_top(top, b, lane);
         if (lane >= k) top = ~0ull;
+        tau = shfl_u64(top, k - 1);
+        nbuf = 0;
     }
-}
+
+    __device__ __forceinline__ void push(unsigned long long* buf, int k, float s, int32_t row,
+                                         int lane) {
+        const unsigned long long key =
+            score_valid(s) ? (((unsigned long long)float_key(s) << 32) | (uint32_t)row) : ~0ull;
+        bool cand = key < tau;
+        unsigned ball = __ballot_sync(0xffffffffu, cand);
+        if (!ball) return;
+        int cnt = __popc(ball);
+        if (nbuf + cnt > 32) {
+            flush(buf, k, lane);
+            cand = key < tau;
+            ball = __ballot_sync(0xffffffffu, cand);
+            cnt = __popc(ball);
+        }
+        if (cand) buf[nbuf + __popc(ball & ((1u << lane) - 1u))] = key;
+        nbuf += cnt;
+    }
+};
 
 // Folds up to 64 new (score, row) candidates (two per lane) into the sorted
 // top-k kept in shared memory (tks ascending by (score, row); rows of this tile
@@ -466,32 +506,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int64_t off = inf->off;
         const float* qbuf = qbase + qb * qbuf_floats;
         int cnt = 0;  // this warp's query (warp < g): entries held in tks/tkr (k > 32)
-        unsigned long long top = ~0ull;  // register top-k (k <= 32)
+        RegTopK rt;   // k <= 32: register top-k with its buffer in the tks area
+        unsigned long long* kbuf = reinterpret_cast<unsigned long long*>(tks_all) + warp * 32;
         const bool reg_topk = a.k <= 32;
         const int ntiles = (nrows + TR - 1) / TR;
         for (int t = 0; t < ntiles; ++t) {
             float acc[RPL][GMAX];
             const uint32_t seq_tile = seq + (uint32_t)(t * nchunks);
+            const int rows_here = min(TR, nrows - t * TR);
+            const int rg = (rows_here + 31) >> 5;  // active 32-row groups
             if (a.metric == kL2)
-                tile_dispatch<true>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, a.err, ok);
+                tile_dispatch<true>(g, rg, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, a.err, ok);
             else
-                tile_dispatch<false>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, a.err, ok);
+                tile_dispatch<false>(g, rg, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, a.err, ok);
             float* pw = part + warp * TR * PSTRIDE;
 #pragma unroll
             for (int r = 0; r < RPL; ++r)
 #pragma unroll
                 for (int qi = 0; qi < GMAX; ++qi)
-                    if (qi < g) pw[(lane + 32 * r) * PSTRIDE + qi] = acc[r][qi];
+                    if (qi < g && r < rg) pw[(lane + 32 * r) * PSTRIDE + qi] = acc[r][qi];
             // uniform stop if any warp's wait gave up during this tile
             if (named_bar_sync_or(1, NCW * 32, !ok)) return;
-            const int rows_here = min(TR, nrows - t * TR);
             for (int e = ctid; e < TR * g; e += NCW * 32) {
                 const int r = e % TR, qi = e / TR;
-                float sum = 0.f;
-#pragma unroll
-                for (int w = 0; w < NCW; ++w) sum += part[(w * TR + r) * PSTRIDE + qi];
                 float s = INF;
                 if (r < rows_here) {
+                    float sum = 0.f;
+#pragma unroll
+                    for (int w = 0; w < NCW; ++w) sum += part[(w * TR + r) * PSTRIDE + qi];
                     const int64_t row = off + (int64_t)t * TR + r;
                     if (a.alive[row]) {
                         if (a.metric == kL2) s = sum;
@@ -513,8 +555,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const int ra = lane + 32 * h, rb = ra + 32;
                     const float s0 = sc[warp * TR + ra], s1 = sc[warp * TR + rb];
                     if (reg_topk) {
-                        topk_fold_reg(top, a.k, s0, rbase + ra, lane);
-                        topk_fold_reg(top, a.k, s1, rbase + rb, lane);
+                        if (32 * h < rows_here) rt.push(kbuf, a.k, s0, rbase + ra, lane);
+                        if (32 * (h + 1) < rows_here) rt.push(kbuf, a.k, s1, rbase + rb, lane);
                     } else {
                         topk_fold(tks, tkr, cnt, a.k, s0, rbase + ra, score_valid(s0), s1,
                                   rbase + rb, score_valid(s1), lane);
@@ -526,10 +568,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (warp < g) {
             const int64_t base = ((int64_t)inf->q[warp] * a.P + inf->slot[warp]) * a.k;
             if (reg_topk) {
+                if (rt.nbuf) rt.flush(kbuf, a.k, lane);
                 if (lane < a.k) {
-                    const bool v = top != ~0ull;
-                    a.part_score[base + lane] = v ? key_float((uint32_t)(top >> 32)) : INF;
-                    a.part_row[base + lane] = v ? off + (int64_t)(uint32_t)(top & 0xffffffffu) : -1;
+                    const bool v = rt.top != ~0ull;
+                    a.part_score[base + lane] = v ? key_float((uint32_t)(rt.top >> 32)) : INF;
+                    a.part_row[base + lane] =
+                        v ? off + (int64_t)(uint32_t)(rt.top & 0xffffffffu) : -1;
                 }
             } else {
                 for (int j = lane; j < a.k; j += 32) {

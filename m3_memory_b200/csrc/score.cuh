@@ -50,7 +50,8 @@ __device__ __forceinline__ float exact_score(const float* __restrict__ a,
 // them (base.cpp:39) and the exact recheck must decide.
 __device__ __forceinline__ void approx_bounds(float dot, float nq, float nc, float qn2, float cn2,
                                               float beta, float gamma, int metric,
-                                              bool normalized, float* lo, float* hi) {
+                                              bool normalized, float* lo, float* hi,
+                                              float* approx = nullptr) {
     const float INF = __int_as_float(0x7f800000);
     float a, e;
     if (metric == kL2) {
@@ -68,12 +69,14 @@ __device__ __forceinline__ void approx_bounds(float dot, float nq, float nc, flo
         if (!(nq > 1e-15f && nc > 1e-15f && nq < 1e15f && nc < 1e15f)) {
             *lo = -INF;
             *hi = INF;
+            if (approx) *approx = 0.f;
             return;
         }
         a = 1.f - dot / den;
         e = (beta + 2.f * gamma) * 2.f + 4e-6f + 2.4e-7f * (fabsf(a) + 1.f);
     }
     e = e + 1e-30f;
+    if (approx) *approx = a;
     if (!(fabsf(a) < INF) || !(e < INF)) {
         *lo = -INF;
         *hi = INF;
@@ -81,6 +84,55 @@ __device__ __forceinline__ void approx_bounds(float dot, float nq, float nc, flo
     }
     *lo = __fsub_rd(a, e);
     *hi = __fadd_ru(a, e);
+}
+
+// The same exact score computed by one warp: the per-element products (each
+// rounded, as the reference's a[i] * b[i]) in parallel, then lane 0 adds them
+// in index order.  `prod` is a per-warp shared buffer of 3 * chunk floats.
+// All lanes return the score.
+__device__ __forceinline__ float warp_exact_score(const float* __restrict__ a,
+                                                  const float* __restrict__ b, int d, int metric,
+                                                  bool normalized, float* prod, int chunk,
+                                                  int lane) {
+    const bool cos_raw = metric == kCosine && !normalized;
+    float s = 0.f, na = 0.f, nb = 0.f;
+    for (int d0 = 0; d0 < d; d0 += chunk) {
+        const int n = min(chunk, d - d0);
+        __syncwarp();
+        for (int i = lane; i < n; i += 32) {
+            const float x = a[d0 + i], y = b[d0 + i];
+            if (metric == kL2) {
+                const float df = __fsub_rn(x, y);
+                prod[i] = __fmul_rn(df, df);
+            } else {
+                prod[i] = __fmul_rn(x, y);
+                if (cos_raw) {
+                    prod[chunk + i] = __fmul_rn(x, x);
+                    prod[2 * chunk + i] = __fmul_rn(y, y);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            if (cos_raw) {
+#pragma unroll 4
+                for (int i = 0; i < n; ++i) {
+                    s = __fadd_rn(s, prod[i]);
+                    na = __fadd_rn(na, prod[chunk + i]);
+                    nb = __fadd_rn(nb, prod[2 * chunk + i]);
+                }
+            } else {
+#pragma unroll 8
+                for (int i = 0; i < n; ++i) s = __fadd_rn(s, prod[i]);
+            }
+        }
+    }
+    float r;
+    if (metric == kL2) r = s;
+    else if (metric == kIP) r = -s;
+    else if (normalized) r = __fsub_rn(1.f, s);
+    else r = (na == 0.f || nb == 0.f) ? 1.f : __fsub_rn(1.f, __fdiv_rn(s, __fsqrt_rn(__fmul_rn(na, nb))));
+    return __shfl_sync(0xffffffffu, r, 0);
 }
 
 }  // namespace m3g
