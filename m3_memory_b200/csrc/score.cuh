@@ -54,16 +54,20 @@ __device__ __forceinline__ void approx_bounds(float dot, float nq, float nc, flo
                                               float* approx = nullptr) {
     const float INF = __int_as_float(0x7f800000);
     float a, e;
+    // beta, gamma already carry 1% slack; the factor 1.01 below covers the fp32
+    // roundings of this bound's own arithmetic (relative 1e-7 each).
     if (metric == kL2) {
         a = qn2 + cn2 - 2.f * dot;
         float s = nq + nc;
-        e = (2.f * beta + 2.f * gamma + 1e-6f) * (s * s);
+        // 2|dot err| <= beta (nq+nc)^2 / 2; reference error <= gamma (nq+nc)^2;
+        // the three-term fp32 sum and the squared norms: <= 8 u (nq+nc)^2
+        e = (beta + gamma + 4.8e-7f) * (s * s) * 1.01f;
     } else if (metric == kIP) {
         a = -dot;
-        e = (beta + gamma) * (nq * nc) * 2.f;
+        e = (beta + gamma) * (nq * nc) * 1.01f;
     } else if (normalized) {
         a = 1.f - dot;
-        e = (beta + gamma) * (nq * nc) * 2.f + 2.4e-7f * (fabsf(a) + 1.f);
+        e = (beta + gamma) * (nq * nc) * 1.01f + 2.4e-7f * (fabsf(a) + 1.f);
     } else {
         float den = nq * nc;
         if (!(nq > 1e-15f && nc > 1e-15f && nq < 1e15f && nc < 1e15f)) {
@@ -73,7 +77,7 @@ __device__ __forceinline__ void approx_bounds(float dot, float nq, float nc, flo
             return;
         }
         a = 1.f - dot / den;
-        e = (beta + 2.f * gamma) * 2.f + 4e-6f + 2.4e-7f * (fabsf(a) + 1.f);
+        e = (beta + 2.f * gamma) * 1.01f + 1e-6f + 2.4e-7f * (fabsf(a) + 1.f);
     }
     e = e + 1e-30f;
     if (approx) *approx = a;
@@ -114,16 +118,28 @@ __device__ __forceinline__ float warp_exact_score(const float* __restrict__ a,
         }
         __syncwarp();
         if (lane == 0) {
+            const int n4 = n & ~3;
             if (cos_raw) {
-#pragma unroll 4
-                for (int i = 0; i < n; ++i) {
+                for (int i = 0; i < n4; i += 4) {
+                    const float4 p = *reinterpret_cast<const float4*>(prod + i);
+                    const float4 pa = *reinterpret_cast<const float4*>(prod + chunk + i);
+                    const float4 pb = *reinterpret_cast<const float4*>(prod + 2 * chunk + i);
+                    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, p.x), p.y), p.z), p.w);
+                    na = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(na, pa.x), pa.y), pa.z), pa.w);
+                    nb = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(nb, pb.x), pb.y), pb.z), pb.w);
+                }
+                for (int i = n4; i < n; ++i) {
                     s = __fadd_rn(s, prod[i]);
                     na = __fadd_rn(na, prod[chunk + i]);
                     nb = __fadd_rn(nb, prod[2 * chunk + i]);
                 }
             } else {
-#pragma unroll 8
-                for (int i = 0; i < n; ++i) s = __fadd_rn(s, prod[i]);
+#pragma unroll 4
+                for (int i = 0; i < n4; i += 4) {
+                    const float4 p = *reinterpret_cast<const float4*>(prod + i);
+                    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, p.x), p.y), p.z), p.w);
+                }
+                for (int i = n4; i < n; ++i) s = __fadd_rn(s, prod[i]);
             }
         }
     }
