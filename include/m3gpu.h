@@ -185,6 +185,24 @@ int m3g_merge_shards_device(m3g_engine* e, const float* d_scores, const int64_t*
                             int nshard, int64_t nq, int k, int64_t* d_out_ids,
                             float* d_out_scores, int32_t* d_out_counts, void* stream);
 
+/* The top-nprobe selection of m3g_select_probes for callers that cannot
+ * allocate GPU memory (a fixed pre-reserved memory pool, a runtime that forbids
+ * allocation after start-up, or code that must not trigger the device
+ * synchronisation cudaMalloc / cudaFree can cause).  No counterpart in the
+ * reference.  Needs no engine: d_queries [nq, dim] and d_centroids [nlist, dim]
+ * are device arrays (dim a multiple of 4, 16-byte aligned), d_out_probes
+ * [nq, min(nprobe, nlist)] int32 is written ascending by exact score, exactly as
+ * m3g_select_probes does.  Its scratch is one fixed 16 MiB device array inside
+ * the library (held by every GPU that loads it until the process exits), so
+ * nq*nlist + 2*nq + 2*nlist must not exceed 4194304; larger requests return
+ * M3G_EUNSUPPORTED.  The first call on a device looks the array up
+ * (cudaGetSymbolAddress); make that call before any stream capture.  All calls
+ * share the array: calls whose work overlaps on the GPU race.  stream NULL:
+ * synchronous; else enqueued on that stream. */
+int m3g_select_probes_noalloc(const float* d_queries, int64_t nq, const float* d_centroids,
+                              int64_t nlist, int dim, int metric, int normalized, int nprobe,
+                              int32_t* d_out_probes, void* stream);
+
 /* Per-stage device time of the most recent search (profiling must be on). */
 typedef struct {
     float ms_prep, ms_coarse_gemm, ms_select, ms_worklist, ms_scan, ms_merge, ms_total;

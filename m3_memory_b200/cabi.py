@@ -70,6 +70,8 @@ SIGNATURES = {
                              _vp]),
     "m3g_split_cluster": (_i32, [_vp, _i32, _i32, _i32, _u64, _pi32]),
     "m3g_merge_shards_device": (_i32, [_vp, _vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp]),
+    "m3g_select_probes_noalloc": (_i32, [_vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp,
+                                         _vp]),
     "m3g_set_profiling": (_i32, [_vp, _i32]),
     "m3g_last_profile": (_i32, [_vp, ct.POINTER(Profile)]),
 }
@@ -119,6 +121,14 @@ def _f32(a):
 
 def _i64a(a):
     return np.ascontiguousarray(a, dtype=np.int64)
+
+
+def select_probes_noalloc(q_ptr, nq, c_ptr, nlist, dim, metric, normalized, nprobe, out_ptr,
+                          stream=None):
+    """m3g_select_probes_noalloc on device pointers (no engine, no allocation)."""
+    check(lib().m3g_select_probes_noalloc(ct.c_void_p(q_ptr), nq, ct.c_void_p(c_ptr), nlist, dim,
+                                          metric, int(normalized), nprobe, ct.c_void_p(out_ptr),
+                                          ct.c_void_p(stream) if stream else None))
 
 
 class Engine:

@@ -316,6 +316,15 @@ int m3g_merge_shards_device(m3g_engine* e, const float* d_scores, const int64_t*
     });
 }
 
+int m3g_select_probes_noalloc(const float* d_queries, int64_t nq, const float* d_centroids,
+                              int64_t nlist, int dim, int metric, int normalized, int nprobe,
+                              int32_t* d_out_probes, void* stream) {
+    return guarded([&] {
+        m3g::select_probes_noalloc(d_queries, nq, d_centroids, nlist, dim, metric, normalized,
+                                   nprobe, d_out_probes, static_cast<cudaStream_t>(stream));
+    });
+}
+
 int m3g_set_profiling(m3g_engine* e, int on) {
     M3G_ENGINE_OR_FAIL(e);
     return guarded([&] { e->eng.set_profiling(on != 0); });

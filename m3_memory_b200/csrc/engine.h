@@ -257,6 +257,13 @@ class Engine {
     cudaStream_t prof_stream_ = nullptr;
 };
 
+// Exact top-nprobe selection with its scratch in a fixed device array
+// (noalloc.cu); allocates nothing.
+void select_probes_noalloc(const float* dQ, int64_t nq, const float* dC, int64_t nlist, int dim,
+                           int metric, int normalized, int nprobe, int32_t* d_out,
+                           cudaStream_t st);
+size_t noalloc_scratch_floats(int64_t nq, int64_t nlist);
+
 // Seeded sampling shared with the oracle: m distinct indices of [0, n) by a
 // partial Fisher-Yates shuffle driven by splitmix64.
 void sample_rows(uint64_t seed, int64_t n, int64_t m, int64_t* out);
