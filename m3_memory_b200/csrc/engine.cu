@@ -11,6 +11,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -89,18 +90,64 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D fp32 tensor map over [rows, dpad], box 32 x h, 128-byte swizzle.
-void make_row_map(CUtensorMap* m, const float* base, int64_t rows, int dpad, int h) {
+}  // namespace
+
+void encode_tma_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                   uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                   CUtensorMapSwizzle swizzle) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) fail(M3G_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
-    cuuint64_t gdim[2] = {(cuuint64_t)dpad, (cuuint64_t)std::max<int64_t>(rows, 1)};
-    cuuint64_t gstride[1] = {(cuuint64_t)dpad * 4};
-    cuuint32_t box[2] = {32, (cuuint32_t)h};
+    cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)std::max<uint64_t>(rows, 1)};
+    cuuint64_t gstride[1] = {(cuuint64_t)row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstride,
-                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) fail(M3G_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    CUresult r = fn(m, dt, 2, const_cast<void*>(base), gdim, gstride, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        fail(M3G_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+}
+
+namespace {
+
+// 2-D fp32 tensor map over [rows, dpad], box 32 x h, 128-byte swizzle.
+void make_row_map(CUtensorMap* m, const float* base, int64_t rows, int dpad, int h) {
+    encode_tma_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, (uint64_t)dpad, (uint64_t)rows,
+                  (uint64_t)dpad * 4, 32, (uint32_t)h, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Which GEMM produces the approximate coarse scores: the tcgen05 bf16x3 kernel
+// (default) or the SIMT fp32 kernel (M3G_COARSE_GEMM=simt).  Either way the
+// selection is exact; only its error bound (and so the candidate count) differs.
+bool use_tc_gemm() {
+    static const bool tc = [] {
+        const char* v = std::getenv("M3G_COARSE_GEMM");
+        return !(v && std::string(v) == "simt");
+    }();
+    return tc;
+}
+
+// S[M, N] ~ A . B^T for fp32 rows A [M, lda], B [N, ldb] (dpad wide).  On the
+// tensor-core path A3 / B3 are the split operands ([M|N, kp] bf16) the caller
+// prepared.  Returns the bound factor beta of the approximation.
+float coarse_gemm(const float* A, int64_t lda, const __nv_bfloat16* A3, const float* B,
+                  int64_t ldb, const __nv_bfloat16* B3, float* S, int64_t lds, int M, int N,
+                  int dpad, int* err, cudaStream_t st) {
+    if (use_tc_gemm()) {
+        const int kp = gemm_tc_kdim(dpad);
+        CUtensorMap ma, mb;
+        encode_tma_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, A3, (uint64_t)kp, (uint64_t)M,
+                      (uint64_t)kp * 2, (uint32_t)gemm_tc_box_k(), (uint32_t)gemm_tc_box_rows_a(),
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+        encode_tma_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, B3, (uint64_t)kp, (uint64_t)N,
+                      (uint64_t)kp * 2, (uint32_t)gemm_tc_box_k(), (uint32_t)gemm_tc_box_rows_b(),
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+        M3G_CK(launch_gemm_tc(ma, mb, S, lds, M, N, kp, err, st));
+        return gemm_tc_error_beta(dpad);
+    }
+    launch_sgemm_nt(A, lda, B, ldb, S, lds, M, N, dpad, st);
+    M3G_CK(cudaGetLastError());
+    return sgemm_error_beta(dpad);
 }
 
 void rebuild_maps(Index& ix) {
@@ -129,9 +176,12 @@ void ensure_centroid_cap(Index& ix, size_t need) {
     if (need <= ix.c_cap && ix.C.p) return;
     size_t cap = std::max<size_t>({need, ix.c_cap * 2, 16});
     DBuf<float> C, cn, cn2;
+    DBuf<__nv_bfloat16> C3;
     DBuf<int64_t> off;
     DBuf<int32_t> len, order;
+    const int kp = gemm_tc_kdim(ix.dpad);
     C.alloc(cap * ix.dpad);
+    C3.alloc(cap * (size_t)kp);
     cn.alloc(cap);
     cn2.alloc(cap);
     off.alloc(cap);
@@ -142,9 +192,12 @@ void ensure_centroid_cap(Index& ix, size_t need) {
         M3G_CK(cudaMemcpyAsync(C.p, ix.C.p, ix.c_cap * ix.dpad * 4, cudaMemcpyDeviceToDevice, ix.wstream));
         M3G_CK(cudaMemcpyAsync(cn.p, ix.cn.p, ix.c_cap * 4, cudaMemcpyDeviceToDevice, ix.wstream));
         M3G_CK(cudaMemcpyAsync(cn2.p, ix.cn2.p, ix.c_cap * 4, cudaMemcpyDeviceToDevice, ix.wstream));
+        M3G_CK(cudaMemcpyAsync(C3.p, ix.C3.p, ix.c_cap * (size_t)kp * 2, cudaMemcpyDeviceToDevice,
+                               ix.wstream));
     }
     M3G_CK(cudaStreamSynchronize(ix.wstream));
     ix.C.swap(C);
+    ix.C3.swap(C3);
     ix.cn.swap(cn);
     ix.cn2.swap(cn2);
     ix.d_list_off.swap(off);
@@ -161,6 +214,9 @@ void upload_centroids(Index& ix, int c0, int n) {
     launch_row_norms(ix.C.p + (size_t)c0 * ix.dpad, ix.dpad, n, ix.dim, ix.cn.p + c0, ix.cn2.p + c0,
                      ix.wstream);
     M3G_CK(cudaGetLastError());
+    const int kp = gemm_tc_kdim(ix.dpad);
+    M3G_CK(launch_split3(ix.C.p + (size_t)c0 * ix.dpad, ix.dpad, n, ix.dpad, kp,
+                         ix.C3.p + (size_t)c0 * kp, true, ix.wstream));
 }
 
 // Uploads per-list offsets / lengths and the longest-first order.
@@ -856,13 +912,14 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
             M3G_CK(launch_iota_rows(w.probes.p, nq, P, st));
             if (profile) M3G_CK(cudaEventRecord(ev[2], st));
         } else {
-            launch_sgemm_nt(dQ, ldq, ix.C.p, ix.dpad, w.S.p, L, (int)nq, L, ix.dpad, st);
-            M3G_CK(cudaGetLastError());
+            if (use_tc_gemm())
+                M3G_CK(launch_split3(dQ, ldq, nq, ix.dpad, gemm_tc_kdim(ix.dpad), w.Q3.p, false, st));
+            const float beta = coarse_gemm(dQ, ldq, w.Q3.p, ix.C.p, ix.dpad, ix.C3.p, w.S.p, L,
+                                           (int)nq, L, ix.dpad, w.err.p, st);
             if (profile) M3G_CK(cudaEventRecord(ev[2], st));
             M3G_CK(launch_select_probes(w.S.p, L, dQ, ldq, ix.C.p, ix.dpad, w.qn.p, w.qn2.p, ix.cn.p,
                                         ix.cn2.p, (int)nq, L, D, ix.metric, ix.normalized ? 1 : 0,
-                                        sgemm_error_beta(ix.dpad), gamma_of(D), P, 0, w.probes.p,
-                                        st));
+                                        beta, gamma_of(D), P, 0, w.probes.p, st));
         }
         probes = w.probes.p;
     } else if (profile) {
@@ -916,7 +973,8 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     if (profile) M3G_CK(cudaEventRecord(ev[6], st));
     // kernels launched: norms, coarse (gemm + select, or iota), 3 work-list
     // kernels, scan, merge (+ the byte counter when profiling)
-    int launches = 1 + (fixed_probes ? 0 : (P >= L ? 1 : 2)) + 3 + (ix.maps_valid ? 1 : 0) + 1;
+    int launches = 1 + (fixed_probes ? 0 : (P >= L ? 1 : (use_tc_gemm() ? 3 : 2))) + 3 +
+                   (ix.maps_valid ? 1 : 0) + 1;
     if (profile) launches += 1;
     last_launches_ += launches;
 }
@@ -936,7 +994,7 @@ bool ws_needs_grow(const Workspace& w, const WsSizes& s) {
            short_of(w.pair_slot, s.nq * s.P) || short_of(w.items, s.nq * s.P) ||
            short_of(w.part_score, s.nq * s.P * s.k) || short_of(w.part_row, s.nq * s.P * s.k) ||
            short_of(w.out_ids, s.nq * s.k) || short_of(w.out_scores, s.nq * s.k) ||
-           short_of(w.out_counts, s.nq);
+           short_of(w.out_counts, s.nq) || short_of(w.Q3, s.nq * gemm_tc_kdim((int)s.dpad));
 }
 void ensure_ws(Workspace& w, const WsSizes& s) {
     if (!w.err.p) {
@@ -962,6 +1020,7 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
     w.out_ids.ensure((size_t)(s.nq * s.k));
     w.out_scores.ensure((size_t)(s.nq * s.k));
     w.out_counts.ensure((size_t)s.nq);
+    w.Q3.ensure((size_t)(s.nq * gemm_tc_kdim((int)s.dpad)));
 }
 
 int64_t chunk_queries(int64_t nq, int L, int P, int k) {
@@ -1205,12 +1264,16 @@ void Engine::select_probes(int index_id, const float* Q, int64_t nq, int nprobe,
         if (P >= L) {
             M3G_CK(launch_iota_rows(ws_.probes.p, m, P, st));
         } else {
-            launch_sgemm_nt(ws_.Q.p, ix->dpad, ix->C.p, ix->dpad, ws_.S.p, L, (int)m, L, ix->dpad, st);
+            if (use_tc_gemm())
+                M3G_CK(launch_split3(ws_.Q.p, ix->dpad, m, ix->dpad, gemm_tc_kdim(ix->dpad),
+                                     ws_.Q3.p, false, st));
+            const float beta = coarse_gemm(ws_.Q.p, ix->dpad, ws_.Q3.p, ix->C.p, ix->dpad,
+                                           ix->C3.p, ws_.S.p, L, (int)m, L, ix->dpad, ws_.err.p,
+                                           st);
             M3G_CK(launch_select_probes(ws_.S.p, L, ws_.Q.p, ix->dpad, ix->C.p, ix->dpad, ws_.qn.p,
                                         ws_.qn2.p, ix->cn.p, ix->cn2.p, (int)m, L, ix->dim,
-                                        ix->metric, ix->normalized ? 1 : 0,
-                                        sgemm_error_beta(ix->dpad), gamma_of(ix->dim), P, 0,
-                                        ws_.probes.p, st));
+                                        ix->metric, ix->normalized ? 1 : 0, beta,
+                                        gamma_of(ix->dim), P, 0, ws_.probes.p, st));
         }
         M3G_CK(cudaMemcpyAsync(out + q0 * P, ws_.probes.p, (size_t)(m * P) * 4, cudaMemcpyDeviceToHost, st));
     }
@@ -1225,17 +1288,28 @@ void Engine::assign_rows(Index& ix, const float* dX, int64_t ld, const float* xn
     const int64_t ch = std::max<int64_t>(
         1, std::min<int64_t>({n, kMaxScoreEntries / std::max(L, 1), kMaxAssignRows}));
     DBuf<float> S;
+    DBuf<__nv_bfloat16> X3;
+    DBuf<int> err;
+    err.alloc(1);
+    M3G_CK(cudaMemsetAsync(err.p, 0, sizeof(int), st));
+    const int kp = gemm_tc_kdim(ix.dpad);
     S.alloc((size_t)(std::min(ch, n) * L));
+    if (use_tc_gemm()) X3.alloc((size_t)(std::min(ch, n) * kp));
     for (int64_t r0 = 0; r0 < n; r0 += ch) {
         const int64_t m = std::min(ch, n - r0);
-        launch_sgemm_nt(dX + r0 * ld, ld, ix.C.p, ix.dpad, S.p, L, (int)m, L, ix.dpad, st);
-        M3G_CK(cudaGetLastError());
+        if (use_tc_gemm())
+            M3G_CK(launch_split3(dX + r0 * ld, ld, m, ix.dpad, kp, X3.p, false, st));
+        const float beta = coarse_gemm(dX + r0 * ld, ld, X3.p, ix.C.p, ix.dpad, ix.C3.p, S.p, L,
+                                       (int)m, L, ix.dpad, err.p, st);
         M3G_CK(launch_select_probes(S.p, L, dX + r0 * ld, ld, ix.C.p, ix.dpad, xn + r0, xn2 + r0,
                                     ix.cn.p, ix.cn2.p, (int)m, L, ix.dim, ix.metric,
-                                    ix.normalized ? 1 : 0, sgemm_error_beta(ix.dpad),
-                                    gamma_of(ix.dim), 1, 1, d_out + r0, st));
+                                    ix.normalized ? 1 : 0, beta, gamma_of(ix.dim), 1, 1,
+                                    d_out + r0, st));
     }
     M3G_CK(cudaStreamSynchronize(st));
+    int herr = 0;
+    M3G_CK(cudaMemcpy(&herr, err.p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) fail(M3G_ETIMEOUT, "assignment: a device-side wait gave up");
 }
 
 void Engine::nearest_clusters(int index_id, const float* vecs, int64_t n, int32_t* out) {
@@ -1321,18 +1395,29 @@ void kmeans_device(const float* X, int64_t ld, int64_t n, int dim, int dpad, int
     const int64_t nchunks = (n + chunk - 1) / chunk;
     DBuf<int32_t> counts, totals;
     DBuf<int64_t> start, perm;
+    DBuf<__nv_bfloat16> X3, C3;
+    DBuf<int> err;
+    err.alloc(1);
+    M3G_CK(cudaMemsetAsync(err.p, 0, sizeof(int), st));
+    const int kp = gemm_tc_kdim(dpad);
+    if (use_tc_gemm()) {
+        X3.alloc((size_t)(ch * kp));
+        C3.alloc((size_t)nlist * kp);
+    }
     counts.alloc((size_t)(nchunks * nlist));
     totals.alloc((size_t)nlist);
     start.alloc((size_t)nlist + 1);
     perm.alloc((size_t)n);
-    const float beta = sgemm_error_beta(dpad);
     const float gam = (float)(dim + 4) * 5.9604645e-8f * 1.01f;
     auto assign_all = [&]() {
         launch_row_norms(C, dpad, nlist, dim, cn.p, cn2.p, st);
+        if (use_tc_gemm()) M3G_CK(launch_split3(C, dpad, nlist, dpad, kp, C3.p, true, st));
         for (int64_t r0 = 0; r0 < n; r0 += ch) {
             const int64_t m = std::min(ch, n - r0);
-            launch_sgemm_nt(X + r0 * ld, ld, C, dpad, S.p, nlist, (int)m, nlist, dpad, st);
-            M3G_CK(cudaGetLastError());
+            if (use_tc_gemm())
+                M3G_CK(launch_split3(X + r0 * ld, ld, m, dpad, kp, X3.p, false, st));
+            const float beta = coarse_gemm(X + r0 * ld, ld, X3.p, C, dpad, C3.p, S.p, nlist,
+                                           (int)m, nlist, dpad, err.p, st);
             M3G_CK(launch_select_probes(S.p, nlist, X + r0 * ld, ld, C, dpad, xn.p + r0, xn2.p + r0,
                                         cn.p, cn2.p, (int)m, nlist, dim, metric, normalized ? 1 : 0,
                                         beta, gam, 1, 1, assign + r0, st));
@@ -1346,6 +1431,9 @@ void kmeans_device(const float* X, int64_t ld, int64_t n, int dim, int dpad, int
     }
     assign_all();
     M3G_CK(cudaStreamSynchronize(st));
+    int herr = 0;
+    M3G_CK(cudaMemcpy(&herr, err.p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) fail(M3G_ETIMEOUT, "k-means: a device-side wait gave up");
 }
 }  // namespace
 

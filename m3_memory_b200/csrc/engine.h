@@ -96,6 +96,7 @@ struct Index {
 
     // device: centroids and their norms
     DBuf<float> C, cn, cn2;  // [cap, dpad], [cap], [cap]
+    DBuf<__nv_bfloat16> C3;  // [cap, kp] split operand [hi | lo | hi] of the tensor-core GEMM
     size_t c_cap = 0;
     // device: the list arena, [arena_cap, dpad] rows + per-row ids / tombstones / norms
     DBuf<float> vecs, rnorm2;
@@ -146,6 +147,7 @@ struct WriteOp {
 // Scratch of the search pipeline, grown on demand and reused across calls.
 struct Workspace {
     DBuf<float> Q, qn, qn2, S;
+    DBuf<__nv_bfloat16> Q3;  // split query operand [hi | hi | lo]
     DBuf<int32_t> probes, lcount, lstart, lcursor, n_items, item_counter, pair_q, pair_slot;
     DBuf<ScanItem> items;
     DBuf<float> part_score;

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -21,6 +22,22 @@ cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t 
                                  const float* cn2, int nq, int L, int D, int metric,
                                  int normalized, float beta, float gamma, int P, int nan_is_none,
                                  int32_t* probes, cudaStream_t st);
+
+// ---- coarse GEMM on the tensor cores (k_gemm_tc.cu) ----
+int gemm_tc_kdim(int dpad);            // K' of the split operands (3 dpad, padded to 64)
+float gemm_tc_error_beta(int dpad);    // |approx dot - exact| <= beta * ||a|| ||b||
+int gemm_tc_box_rows_a();
+int gemm_tc_box_rows_b();
+int gemm_tc_box_k();
+cudaError_t launch_split3(const float* X, int64_t ld, int64_t n, int dpad, int kp,
+                          __nv_bfloat16* out, bool centroid_side, cudaStream_t st);
+cudaError_t launch_gemm_tc(const CUtensorMap& mapA, const CUtensorMap& mapB, float* S, int64_t lds,
+                           int M, int N, int kp, int* err, cudaStream_t st);
+
+// 2-D tiled tensor map (host; driver entry point fetched through the runtime).
+void encode_tma_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                   uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                   CUtensorMapSwizzle swizzle);
 
 // ---- list scan (k_scan.cu) ----
 struct ScanItem {
