@@ -140,10 +140,11 @@ def peaks():
 
 def scan_traffic_per_launch():
     """dram bytes of one scan launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "list_scan_traffic.json"
+    p = ROOT / "profiles" / "list_scan_traffic.txt"
     if p.is_file():
-        d = json.loads(p.read_text())
-        return d.get("dram_bytes_per_launch")
+        for line in p.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(line.split(":")[1])
     return None
 
 
