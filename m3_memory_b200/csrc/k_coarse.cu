@@ -163,7 +163,7 @@ constexpr int SEL_CAP = 2048;        // candidates rescored and sorted in shared
 constexpr int SEL_KEYS_SMEM = 8192;  // upper-bound keys cached in shared memory up to this L
 constexpr int SEL_SORT_MAX = 1024;   // largest P whose selection is returned sorted
 constexpr int SEL_OVERLAP_MAX = 256; // above this many candidates, all are rescored
-constexpr int SEL_EX_CHUNK = 128;    // dims per product chunk of a warp's exact rescoring
+constexpr int SEL_STAGE = 32 * 33;   // per-warp product tile of the exact rescoring
 
 struct SelShared {
     unsigned hist[256];
@@ -283,9 +283,12 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     float* qs = reinterpret_cast<float*>(sel_smem);                               // D floats
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(qs + ((D + 3) & ~3));  // SEL_CAP
     float2* bnd = reinterpret_cast<float2*>(cand + SEL_CAP);                     // SEL_CAP
-    float* prod = reinterpret_cast<float*>(bnd + SEL_CAP);                       // 8 warps x 3 x chunk
-    unsigned char* needf = reinterpret_cast<unsigned char*>(prod + (SEL_BLOCK / 32) * 3 * SEL_EX_CHUNK);
+    int* exl = reinterpret_cast<int*>(bnd);  // reuses bnd once the overlap test is done
+    unsigned char* needf = reinterpret_cast<unsigned char*>(bnd + SEL_CAP);      // SEL_CAP
+    // one area, used first for the cached upper-bound keys, later for the
+    // per-warp product tiles of the exact rescoring
     uint32_t* hkeys = reinterpret_cast<uint32_t*>(needf + SEL_CAP);
+    float* stage_all = reinterpret_cast<float*>(hkeys);
     const bool cache = L <= SEL_KEYS_SMEM;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -369,13 +372,17 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
                 }
             }
             __syncthreads();
-            float* wprod = prod + warp * 3 * SEL_EX_CHUNK;
-            for (int i = warp; i < (int)cnt; i += SEL_BLOCK / 32) {
-                if (!needf[i]) continue;
-                const int c = (int)(cand[i] & 0xffffffffu);
-                const float r = warp_exact_score(qs, C + (int64_t)c * ldc, D, metric, nrm, wprod,
-                                                 SEL_EX_CHUNK, lane);
-                if (lane == 0) cand[i] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
+            // compact the candidates to rescore, then 32 of them per warp
+            for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK)
+                if (needf[i]) exl[atomicAdd(&sh.count2, 1u)] = i;
+            __syncthreads();
+            const int nex = (int)sh.count2;
+            float* stage = stage_all + warp * SEL_STAGE;
+            for (int g = warp * 32; g < nex; g += SEL_BLOCK) {
+                const int idx = g + lane < nex ? exl[g + lane] : -1;
+                const int c = idx >= 0 ? (int)(cand[idx] & 0xffffffffu) : -1;
+                const float r = warp_exact_scores32(qs, C, ldc, D, metric, nrm, c, stage, lane);
+                if (idx >= 0) cand[idx] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
             }
             __syncthreads();
             int n2 = 1;
@@ -449,10 +456,10 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
 
 size_t select_smem_bytes(int L, int D) {
     size_t b = sizeof(float) * (size_t)((D + 3) & ~3) + sizeof(unsigned long long) * SEL_CAP +
-               sizeof(float2) * SEL_CAP + sizeof(float) * (SEL_BLOCK / 32) * 3 * SEL_EX_CHUNK +
-               SEL_CAP;
-    if (L <= SEL_KEYS_SMEM) b += sizeof(uint32_t) * (size_t)L;
-    return b;
+               sizeof(float2) * SEL_CAP + SEL_CAP;
+    const size_t keys = L <= SEL_KEYS_SMEM ? sizeof(uint32_t) * (size_t)L : 0;
+    const size_t tiles = sizeof(float) * (size_t)(SEL_BLOCK / 32) * SEL_STAGE;
+    return b + (keys > tiles ? keys : tiles);
 }
 
 int select_max_dim() { return 8192; }

@@ -151,4 +151,82 @@ __device__ __forceinline__ float warp_exact_score(const float* __restrict__ a,
     return __shfl_sync(0xffffffffu, r, 0);
 }
 
+// The exact score for up to 32 candidates at once, one per lane: the warp
+// computes the per-element products of 32 dims for all 32 candidates (each
+// rounded, as the reference's a[i] * b[i]) into a padded 32 x 33 shared tile,
+// then every lane adds its own candidate's row in index order.  `cid` is the
+// lane's centroid row (-1: none); `stage` is a per-warp buffer of 32 * 33 floats.
+// The next chunk's centroid values are loaded while the current one is summed.
+// Returns the lane's score (undefined for cid < 0).
+__device__ __forceinline__ float warp_exact_scores32(const float* __restrict__ q,
+                                                     const float* __restrict__ C, int64_t ldc,
+                                                     int d, int metric, bool normalized, int cid,
+                                                     float* stage, int lane) {
+    const bool cos_raw = metric == kCosine && !normalized;
+    float s = 0.f, na = 0.f, nb = 0.f;
+    float xs[32];
+    auto load_chunk = [&](int d0, float (&x)[32]) {
+        const int dd = d0 + lane;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+            const int cc = __shfl_sync(0xffffffffu, cid, c);
+            x[c] = (cc >= 0 && dd < d) ? C[(int64_t)cc * ldc + dd] : 0.f;
+        }
+    };
+    load_chunk(0, xs);
+    for (int d0 = 0; d0 < d; d0 += 32) {
+        const int dd = d0 + lane;
+        const float qv = dd < d ? q[dd] : 0.f;
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+            float p;
+            if (metric == kL2) {
+                const float df = __fsub_rn(qv, xs[c]);
+                p = __fmul_rn(df, df);
+            } else {
+                p = __fmul_rn(qv, xs[c]);
+            }
+            stage[c * 33 + lane] = p;
+        }
+        float xn[32];
+        if (cos_raw) {
+            __syncwarp();
+            const int nn = min(32, d - d0);
+            for (int l = 0; l < nn; ++l) s = __fadd_rn(s, stage[lane * 33 + l]);
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) stage[c * 33 + lane] = __fmul_rn(xs[c], xs[c]);
+            __syncwarp();
+            for (int l = 0; l < nn; ++l) {
+                nb = __fadd_rn(nb, stage[lane * 33 + l]);
+                const float a = q[d0 + l];
+                na = __fadd_rn(na, __fmul_rn(a, a));
+            }
+            if (d0 + 32 < d) load_chunk(d0 + 32, xn);
+        } else {
+            if (d0 + 32 < d) load_chunk(d0 + 32, xn);
+            __syncwarp();
+            const int nn = min(32, d - d0);
+            const float* row = stage + lane * 33;
+            if (nn == 32) {
+#pragma unroll
+                for (int l = 0; l < 32; ++l) s = __fadd_rn(s, row[l]);
+            } else {
+                for (int l = 0; l < nn; ++l) s = __fadd_rn(s, row[l]);
+            }
+        }
+        if (d0 + 32 < d) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) xs[c] = xn[c];
+        }
+    }
+    __syncwarp();
+    if (metric == kL2) return s;
+    if (metric == kIP) return -s;
+    if (normalized) return __fsub_rn(1.f, s);
+    return (na == 0.f || nb == 0.f) ? 1.f
+                                    : __fsub_rn(1.f, __fdiv_rn(s, __fsqrt_rn(__fmul_rn(na, nb))));
+}
+
 }  // namespace m3g
