@@ -408,6 +408,7 @@ def run_ours(args, rank, world, local_rank):
     h_sc = torch.empty((BATCH, K), dtype=torch.float32).pin_memory()
     h_cnt = torch.empty((BATCH,), dtype=torch.int32).pin_memory()
     scan_ms, scan_bytes, launches = [], [], 0
+    stage_ms = {}
     if world == 1:
         lib = cabi.lib()
 
@@ -422,6 +423,9 @@ def run_ours(args, rank, world, local_rank):
         for i in range(args.steps):
             e2e_step(i % NBATCH)
             p = eng.last_profile()
+            for key in ("ms_prep", "ms_coarse_gemm", "ms_select", "ms_worklist", "ms_scan",
+                        "ms_merge", "ms_total"):
+                stage_ms.setdefault(key, []).append(p[key])
             scan_ms.append(p["ms_scan"])
             scan_bytes.append(p["scan_bytes"])
             launches += p["kernel_launches"]
@@ -492,6 +496,8 @@ def run_ours(args, rank, world, local_rank):
                    "nprobe": nprobe, "k": K, "batch": BATCH, "recall_at_10": recall,
                    "recall_sweep": {str(k): v for k, v in sweep.items()},
                    "kmeans_iters": KMEANS_ITERS,
+                   "stage_ms_mean": {k[3:]: round(statistics.mean(v), 4)
+                                     for k, v in stage_ms.items()},
                    "l2_flush": "not needed: each step streams ~4 GB of lists (> 126 MB L2)",
                    "parallelism": f"lists sharded over {world} GPU(s)" if world > 1 else "1 GPU"},
         "gpu_launches": int(round(per_step_launches * args.steps)),

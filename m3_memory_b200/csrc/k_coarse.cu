@@ -159,14 +159,18 @@ float sgemm_error_beta(int K) { return (float)(K + 2) * 5.9604645e-8f * 1.01f; }
 // ---------------------------------------------------------------------------
 namespace {
 constexpr int SEL_BLOCK = 256;
-constexpr int SEL_CAP = 2048;        // candidates rescored and sorted in shared memory
+constexpr int SEL_CAP = 1024;        // candidates rescored and sorted in shared memory (>= SEL_SORT_MAX)
 constexpr int SEL_KEYS_SMEM = 8192;  // upper-bound keys cached in shared memory up to this L
 constexpr int SEL_SORT_MAX = 1024;   // largest P whose selection is returned sorted
 constexpr int SEL_OVERLAP_MAX = 256; // above this many candidates, all are rescored
-constexpr int SEL_STAGE = 32 * 33;   // per-warp product tile of the exact rescoring
+constexpr int SEL_STAGE = kExactTileFloats;  // per-warp product tile of the exact rescoring
+constexpr int SEL_FAST_P = 64;       // largest P that takes the pre-filtered threshold path
+static_assert(SEL_CAP >= SEL_SORT_MAX, "the sorted fallback keeps P keys in the candidate array");
+static_assert(3 * SEL_CAP <= (SEL_BLOCK / 32) * SEL_STAGE, "S0 lives in the tile area");
 
 struct SelShared {
     unsigned hist[256];
+    unsigned mins[SEL_BLOCK];
     unsigned prefix, remain, count, count2, m_less, tie_need, wtot[SEL_BLOCK / 32];
 };
 
@@ -301,18 +305,68 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     auto bounds = [&](int c, float* lo, float* hi) {
         approx_bounds(srow[c], nq, cn[c], nq2, cn2[c], beta, gamma, metric, nrm, lo, hi);
     };
-    if (cache) {
+    const int PP = P < L ? P : L;
+    bool exact_all = PP > SEL_SORT_MAX;
+    bool have = false;  // candidates in cand[0, cnt)
+    unsigned cnt = 0;
+    if (!exact_all && PP <= SEL_FAST_P) {
+        // --- pre-filtered threshold.  tau0, the PP-th smallest of the threads'
+        // smallest upper-bound keys, is >= T (the PP-th smallest of all: PP
+        // distinct keys are <= tau0).  Every centroid with hi <= T therefore has
+        // lo <= tau0, so T is the PP-th smallest upper bound within
+        // S0 = {c : lo <= tau0}, and every candidate (lo <= T) is in S0.
+        uint32_t mymin = 0xffffffffu;
         for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
             float lo, hi;
             bounds(c, &lo, &hi);
-            hkeys[c] = float_key(hi);
+            const uint32_t k = float_key(hi);
+            mymin = k < mymin ? k : mymin;
         }
+        sh.mins[threadIdx.x] = mymin;
+        if (threadIdx.x == 0) sh.count = 0;
+        __syncthreads();
+        const uint32_t tau0 =
+            block_radix_select([&](int t) { return sh.mins[t]; }, SEL_BLOCK, (unsigned)PP, sh);
+        uint32_t* f_id = hkeys;  // S0, in the key / tile area (unused until phase C)
+        uint32_t* f_hi = f_id + SEL_CAP;
+        uint32_t* f_lo = f_hi + SEL_CAP;
+        for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
+            float lo, hi;
+            bounds(c, &lo, &hi);
+            const uint32_t lk = lo != lo ? 0u : float_key(lo);
+            if (lk <= tau0) {
+                const unsigned slot = atomicAdd(&sh.count, 1u);
+                if (slot < (unsigned)SEL_CAP) {
+                    f_id[slot] = (uint32_t)c;
+                    f_hi[slot] = float_key(hi);
+                    f_lo[slot] = lk;
+                }
+            }
+        }
+        __syncthreads();
+        const unsigned n0 = sh.count;
+        if (n0 <= (unsigned)SEL_CAP) {
+            const uint32_t tkey =
+                block_radix_select([&](int i) { return f_hi[i]; }, (int)n0, (unsigned)PP, sh);
+            if (threadIdx.x == 0) sh.count2 = 0;
+            __syncthreads();
+            for (int i = threadIdx.x; i < (int)n0; i += SEL_BLOCK)
+                if (f_lo[i] <= tkey) cand[atomicAdd(&sh.count2, 1u)] = f_id[i];
+            __syncthreads();
+            cnt = sh.count2;
+            have = true;
+        }
+        // else S0 overflows: the general path below recomputes every bound
     }
-    __syncthreads();
-
-    const int PP = P < L ? P : L;
-    bool exact_all = PP > SEL_SORT_MAX;
-    if (!exact_all) {
+    if (!exact_all && !have) {
+        if (cache) {
+            for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
+                float lo, hi;
+                bounds(c, &lo, &hi);
+                hkeys[c] = float_key(hi);
+            }
+        }
+        __syncthreads();
         // --- phase A: T = PP-th smallest upper bound
         uint32_t tkey;
         if (cache)
@@ -338,14 +392,16 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
             }
         }
         __syncthreads();
-        const unsigned cnt = sh.count;
-        if (cnt > (unsigned)SEL_CAP) {
-            exact_all = true;
-        } else {
+        cnt = sh.count;
+        if (cnt > (unsigned)SEL_CAP) exact_all = true;
+        else have = true;
+    }
+    if (have) {
+        {
             // --- phase C: order the candidates by exact score.  A candidate whose
             // interval overlaps no other candidate's is already ordered by its
             // approximate value; the rest are rescored in the reference's exact
-            // arithmetic (one warp per candidate).  Keys: (score key, id).
+            // arithmetic, spread evenly over the warps.  Keys: (score key, id).
             for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK) {
                 float lo, hi;
                 bounds((int)cand[i], &lo, &hi);
@@ -378,10 +434,21 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
             __syncthreads();
             const int nex = (int)sh.count2;
             float* stage = stage_all + warp * SEL_STAGE;
-            for (int g = warp * 32; g < nex; g += SEL_BLOCK) {
-                const int idx = g + lane < nex ? exl[g + lane] : -1;
+            for (int r0 = 0; r0 < nex; r0 += SEL_BLOCK) {
+                // up to 256 candidates per round, G = ceil(n / 8) per warp
+                const int n = nex - r0 < SEL_BLOCK ? nex - r0 : SEL_BLOCK;
+                const int G = (n + SEL_BLOCK / 32 - 1) / (SEL_BLOCK / 32);
+                if (warp * G >= n) continue;  // warp-uniform: nothing for this warp
+                const int i = warp * G + lane;
+                const int idx = (lane < G && i < n) ? exl[r0 + i] : -1;
                 const int c = idx >= 0 ? (int)(cand[idx] & 0xffffffffu) : -1;
-                const float r = warp_exact_scores32(qs, C, ldc, D, metric, nrm, c, stage, lane);
+                float r;
+                if (G <= 8)
+                    r = warp_exact_scores<4>(qs, C, ldc, D, metric, nrm, c, stage, lane);
+                else if (G <= 16)
+                    r = warp_exact_scores<2>(qs, C, ldc, D, metric, nrm, c, stage, lane);
+                else
+                    r = warp_exact_scores<1>(qs, C, ldc, D, metric, nrm, c, stage, lane);
                 if (idx >= 0) cand[idx] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
             }
             __syncthreads();

@@ -151,74 +151,127 @@ __device__ __forceinline__ float warp_exact_score(const float* __restrict__ a,
     return __shfl_sync(0xffffffffu, r, 0);
 }
 
-// The exact score for up to 32 candidates at once, one per lane: the warp
-// computes the per-element products of 32 dims for all 32 candidates (each
-// rounded, as the reference's a[i] * b[i]) into a padded 32 x 33 shared tile,
-// then every lane adds its own candidate's row in index order.  `cid` is the
-// lane's centroid row (-1: none); `stage` is a per-warp buffer of 32 * 33 floats.
-// The next chunk's centroid values are loaded while the current one is summed.
-// Returns the lane's score (undefined for cid < 0).
-__device__ __forceinline__ float warp_exact_scores32(const float* __restrict__ q,
-                                                     const float* __restrict__ C, int64_t ldc,
-                                                     int d, int metric, bool normalized, int cid,
-                                                     float* stage, int lane) {
+// VW consecutive floats from p (global memory) into x; p is 4*VW-byte aligned.
+template <int VW>
+__device__ __forceinline__ void load_vec(const float* __restrict__ p, float (&x)[VW]) {
+    if constexpr (VW == 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+    } else if constexpr (VW == 2) {
+        const float2 v = __ldg(reinterpret_cast<const float2*>(p));
+        x[0] = v.x; x[1] = v.y;
+    } else {
+        x[0] = __ldg(p);
+    }
+}
+
+// VW consecutive floats of x to p (shared memory), p 4*VW-byte aligned.
+template <int VW>
+__device__ __forceinline__ void store_vec(float* p, const float (&x)[VW]) {
+    if constexpr (VW == 4) *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+    else if constexpr (VW == 2) *reinterpret_cast<float2*>(p) = make_float2(x[0], x[1]);
+    else p[0] = x[0];
+}
+
+// Row stride (floats) of the product tile of warp_exact_scores<VW>: a chunk of
+// 32*VW products plus 4 floats of padding, so that the 128-bit reads of eight
+// lanes on eight different rows hit disjoint banks.
+template <int VW>
+__host__ __device__ constexpr int exact_tile_stride() { return 32 * VW + 4; }
+// Floats of the per-warp product tile, enough for every VW in {1, 2, 4}.
+constexpr int kExactTileFloats = 32 * (32 + 4);
+
+// The exact score for up to G = 32 / VW candidates at once, one per lane
+// (lanes 0 .. G-1): the warp computes the per-element products of a chunk of
+// 32 * VW dims for every candidate (each rounded, as the reference's
+// a[i] * b[i]) into a shared tile, then each candidate's lane adds its row in
+// index order, which is the reference's summation order.  The next chunk's
+// centroid values are loaded before that serial sum, whose 32 * VW dependent
+// adds hide the load latency; fewer candidates per warp therefore use wider
+// chunks.  `q` is in shared memory, 16-byte aligned, with round_up(d, 4)
+// floats; `cid` is the lane's centroid row (-1: none; every lane >= G passes
+// -1); `stage` holds kExactTileFloats floats, 16-byte aligned.  All 32 lanes
+// call it.  Returns the lane's score (undefined where cid < 0).
+template <int VW>
+__device__ __forceinline__ float warp_exact_scores(const float* __restrict__ q,
+                                                   const float* __restrict__ C, int64_t ldc,
+                                                   int d, int metric, bool normalized, int cid,
+                                                   float* stage, int lane) {
+    constexpr int W = 32 * VW, GM = 32 / VW, RS = exact_tile_stride<VW>();
+    static_assert(GM * RS <= kExactTileFloats, "tile too small");
     const bool cos_raw = metric == kCosine && !normalized;
-    float s = 0.f, na = 0.f, nb = 0.f;
-    float xs[32];
-    auto load_chunk = [&](int d0, float (&x)[32]) {
-        const int dd = d0 + lane;
+    const bool vec = (ldc % VW) == 0 && (reinterpret_cast<uintptr_t>(C) % (4 * VW)) == 0;
+    float x[GM][VW];
+    auto load = [&](int d0) {
+        const int dd = d0 + lane * VW;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-            const int cc = __shfl_sync(0xffffffffu, cid, c);
-            x[c] = (cc >= 0 && dd < d) ? C[(int64_t)cc * ldc + dd] : 0.f;
+        for (int g = 0; g < GM; ++g) {
+            const int cc = __shfl_sync(0xffffffffu, cid, g);
+            if (cc >= 0 && vec && dd + VW <= d) {
+                load_vec<VW>(C + (int64_t)cc * ldc + dd, x[g]);
+            } else {
+#pragma unroll
+                for (int v = 0; v < VW; ++v)
+                    x[g][v] = (cc >= 0 && dd + v < d) ? __ldg(C + (int64_t)cc * ldc + dd + v) : 0.f;
+            }
         }
     };
-    load_chunk(0, xs);
-    for (int d0 = 0; d0 < d; d0 += 32) {
-        const int dd = d0 + lane;
-        const float qv = dd < d ? q[dd] : 0.f;
-        __syncwarp();
+    const bool mine = lane < GM && cid >= 0;
+    const float* row = stage + lane * RS;
+    float s = 0.f, na = 0.f, nb = 0.f;
+    load(0);
+    for (int d0 = 0; d0 < d; d0 += W) {
+        const int dd = d0 + lane * VW;
+        const int nn = min(W, d - d0);
+        float qv[VW];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-            float p;
-            if (metric == kL2) {
-                const float df = __fsub_rn(qv, xs[c]);
-                p = __fmul_rn(df, df);
-            } else {
-                p = __fmul_rn(qv, xs[c]);
+        for (int v = 0; v < VW; ++v) qv[v] = dd + v < d ? q[dd + v] : 0.f;
+        __syncwarp();  // the previous chunk's sums are done with the tile
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            float p[VW];
+#pragma unroll
+            for (int v = 0; v < VW; ++v) {
+                if (metric == kL2) {
+                    const float df = __fsub_rn(qv[v], x[g][v]);
+                    p[v] = __fmul_rn(df, df);
+                } else {
+                    p[v] = __fmul_rn(qv[v], x[g][v]);
+                }
             }
-            stage[c * 33 + lane] = p;
+            store_vec<VW>(stage + g * RS + lane * VW, p);
         }
-        float xn[32];
-        if (cos_raw) {
-            __syncwarp();
-            const int nn = min(32, d - d0);
-            for (int l = 0; l < nn; ++l) s = __fadd_rn(s, stage[lane * 33 + l]);
-            __syncwarp();
+        if (!cos_raw && d0 + W < d) load(d0 + W);  // x is free once the products are stored
+        __syncwarp();
+        if (mine) {
+            if (nn == W) {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) stage[c * 33 + lane] = __fmul_rn(xs[c], xs[c]);
-            __syncwarp();
-            for (int l = 0; l < nn; ++l) {
-                nb = __fadd_rn(nb, stage[lane * 33 + l]);
-                const float a = q[d0 + l];
-                na = __fadd_rn(na, __fmul_rn(a, a));
-            }
-            if (d0 + 32 < d) load_chunk(d0 + 32, xn);
-        } else {
-            if (d0 + 32 < d) load_chunk(d0 + 32, xn);
-            __syncwarp();
-            const int nn = min(32, d - d0);
-            const float* row = stage + lane * 33;
-            if (nn == 32) {
-#pragma unroll
-                for (int l = 0; l < 32; ++l) s = __fadd_rn(s, row[l]);
+                for (int l = 0; l < W; l += 4) {
+                    const float4 r = *reinterpret_cast<const float4*>(row + l);
+                    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, r.x), r.y), r.z), r.w);
+                }
             } else {
                 for (int l = 0; l < nn; ++l) s = __fadd_rn(s, row[l]);
             }
         }
-        if (d0 + 32 < d) {
+        if (cos_raw) {
+            __syncwarp();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) xs[c] = xn[c];
+            for (int g = 0; g < GM; ++g) {
+                float p[VW];
+#pragma unroll
+                for (int v = 0; v < VW; ++v) p[v] = __fmul_rn(x[g][v], x[g][v]);
+                store_vec<VW>(stage + g * RS + lane * VW, p);
+            }
+            if (d0 + W < d) load(d0 + W);
+            __syncwarp();
+            if (mine) {
+                for (int l = 0; l < nn; ++l) {
+                    nb = __fadd_rn(nb, row[l]);
+                    const float a = q[d0 + l];
+                    na = __fadd_rn(na, __fmul_rn(a, a));
+                }
+            }
         }
     }
     __syncwarp();
