@@ -42,6 +42,7 @@ NCOMP = 1000
 SIGMA = 0.3
 NLIST = 4096
 NPROBE = 32
+FIXED_NPROBE = False  # profiling cases: no recall sweep over nprobe
 K = 10
 BATCH = 1024
 NBATCH = 10
@@ -358,7 +359,7 @@ def run_ours(args, rank, world, local_rank):
         del Xd
         torch.cuda.empty_cache()
     sweep = {}
-    for p in (NPROBE, 48, 64, 96, 128, 256):
+    for p in (NPROBE,) if FIXED_NPROBE else (NPROBE, 48, 64, 96, 128, 256):
         found, _ = step(0, p)
         torch.cuda.synchronize()
         eng.sync_errors()
@@ -368,7 +369,7 @@ def run_ours(args, rank, world, local_rank):
             dist.broadcast(t, 0)
             r = float(t.item())
         sweep[p] = r
-        if r >= 0.95:
+        if r >= 0.95 or FIXED_NPROBE:
             nprobe, recall = p, r
             break
     if recall is None:
@@ -523,12 +524,16 @@ def main():
     ap.add_argument("--nvec", type=int, default=None,
                     help="profiling only: fewer vectors (the headline line uses 1M)")
     ap.add_argument("--nlist", type=int, default=None, help="profiling only: fewer lists")
+    ap.add_argument("--nprobe", type=int, default=None, help="profiling only: other nprobe")
     args = ap.parse_args()
-    global N_VEC, NLIST, WORKLOAD
-    if args.nvec or args.nlist:
+    global N_VEC, NLIST, NPROBE, FIXED_NPROBE, WORKLOAD
+    if args.nvec or args.nlist or args.nprobe:
         N_VEC = args.nvec or N_VEC
         NLIST = args.nlist or NLIST
-        WORKLOAD = f"PROFILING CASE (not headline): {N_VEC} x {DIM}, nlist {NLIST}"
+        NPROBE = args.nprobe or NPROBE
+        FIXED_NPROBE = args.nprobe is not None
+        WORKLOAD = (f"PROFILING CASE (not headline): {N_VEC} x {DIM}, nlist {NLIST}, "
+                    f"nprobe {NPROBE}")
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -25,10 +25,11 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               *ARCH, f"-I{INCLUDE}", f"-I{CSRC}"]
 
-CU_SOURCES = ["k_coarse.cu", "k_scan.cu", "k_kmeans.cu", "k_gemm_tc.cu", "engine.cu",
-              "noalloc.cu"]
+CU_SOURCES = ["k_coarse.cu", "k_scan.cu", "k_scan_tc.cu", "k_kmeans.cu", "k_gemm_tc.cu",
+              "engine.cu", "noalloc.cu"]
 CPP_SOURCES = ["api.cpp"]
-HEADERS = ["common.cuh", "score.cuh", "kernels.h", "kernels_kmeans.h", "engine.h"]
+HEADERS = ["common.cuh", "score.cuh", "topk.cuh", "tc.cuh", "kernels.h", "kernels_kmeans.h",
+           "engine.h"]
 
 
 def _newer(target: Path, deps) -> bool:

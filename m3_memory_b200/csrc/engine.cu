@@ -116,6 +116,17 @@ void make_row_map(CUtensorMap* m, const float* base, int64_t rows, int dpad, int
                   (uint64_t)dpad * 4, 32, (uint32_t)h, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Which kernel scans the lists: the tensor-core scan (default, where it
+// applies) or the SIMT scan (M3G_SCAN=simt).  Both rank by (score, probe slot,
+// row); their scores differ only in fp32 rounding.
+bool use_tc_scan() {
+    static const bool tc = [] {
+        const char* v = std::getenv("M3G_SCAN");
+        return !(v && std::string(v) == "simt");
+    }();
+    return tc;
+}
+
 // Which GEMM produces the approximate coarse scores: the tcgen05 bf16x3 kernel
 // (default) or the SIMT fp32 kernel (M3G_COARSE_GEMM=simt).  Either way the
 // selection is exact; only its error bound (and so the candidate count) differs.
@@ -926,7 +937,8 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
         M3G_CK(cudaEventRecord(ev[2], st));
     }
     if (profile) M3G_CK(cudaEventRecord(ev[3], st));
-    const int gmax = scan_gmax_for_dim(ix.dpad);
+    const bool tc_scan = use_tc_scan() && scan_tc_supported(ix.metric, k);
+    const int gmax = tc_scan ? scan_tc_gmax() : scan_gmax_for_dim(ix.dpad);
     if (gmax <= 0) fail(M3G_EUNSUPPORTED, "search: dimension too large for the list scan");
     M3G_CK(launch_build_worklist(probes, (int)nq, P, L, ix.d_list_order.p, gmax, w.lcount.p,
                                  w.lstart.p, w.lcursor.p, w.items.p, w.n_items.p, w.pair_q.p,
@@ -959,7 +971,10 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     a.err = w.err.p;
     const int grid = (int)std::min<int64_t>(num_sms_, std::max<int64_t>(1, nq * P));
     if (ix.maps_valid) {
-        M3G_CK(launch_list_scan(ix.maps, a, gmax, grid, st));
+        if (tc_scan)
+            M3G_CK(launch_list_scan_tc(ix.maps, a, grid, st));
+        else
+            M3G_CK(launch_list_scan(ix.maps, a, gmax, grid, st));
     } else {
         // empty arena: every partial list is empty
         M3G_CK(cudaMemsetAsync(w.part_row.p, 0xff, sizeof(int64_t) * (size_t)(nq * P * k), st));

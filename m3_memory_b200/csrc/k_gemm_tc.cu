@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc.cuh"
 
 namespace m3g {
 namespace {
@@ -39,67 +40,6 @@ constexpr size_t TC_SMEM = (size_t)TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
 // M >> 4 at bits 24-28.
 constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
                               ((uint32_t)(TC_BM >> 4) << 24);
-
-// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle
-// layout TMA writes: start address >> 4, leading byte offset 1 (unused for
-// swizzled K-major), stride byte offset 1024 B (8 rows of 128 B), descriptor
-// version 1, layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1 << 16;
-    d |= (uint64_t)(1024 >> 4) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
-    return d;
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc, bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-            smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-          "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Bounded wait that ignores the launch's error word (used on error paths before
-// leaving, so no copy or MMA is still writing this CTA's memory).
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitSpinLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return;
-        __nanosleep(256);
-    }
-}
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_bf16x3_kernel(const __grid_constant__ CUtensorMap mapA,
@@ -170,7 +110,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t sb = sa + TC_A_BYTES;
 #pragma unroll
             for (int k = 0; k < TC_BK / 16; ++k)
-                tc_mma(tmem, sw128_desc(sa + k * 32), sw128_desc(sb + k * 32), TC_IDESC,
+                tc_mma_f16(tmem, sw128_desc(sa + k * 32), sw128_desc(sb + k * 32), TC_IDESC,
                        (kt | k) != 0);
             tc_commit(&empty[s]);  // frees the stage once these MMAs have read it
         }

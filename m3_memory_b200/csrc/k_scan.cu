@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 namespace m3g {
 namespace {
@@ -57,7 +58,7 @@ struct ItemInfo {
 
 struct Layout {
     int nstage;
-    int qstride;        // floats per query row in shared memory (multiple of 32)
+    int qstride;        // floats per query in shared memory (nchunks * 32, stored chunk-major)
     int gmax;
     uint32_t ring_off, q_off, part_off, sc_off, tks_off, tkr_off, info_off, bar_off, total;
 };
@@ -113,42 +114,37 @@ __device__ void drain_stages(uint64_t* full, int nstage, uint32_t seq_end) {
     }
 }
 
-// One 64-row tile: every consumer warp walks all of the tile's stages; warp w
-// takes the 16-byte column slot w of each 32-dim stage for rows lane and
-// lane+32, so the eight warps share each stage and release it together.
+// One tile of up to 128 rows: every consumer warp walks all of the tile's
+// stages; warp w takes the 16-byte column slot w of each 32-dim stage for rows
+// lane + 32 m, so the eight warps share each stage and release it together.
+// (stage, phase) is the consumer's ring position, advanced once per chunk.
+// The item's queries sit chunk-major in shared memory at qbuf: chunk c of
+// query i at byte (c * gmax + i) * 128.
 template <int NQ, int RG, bool L2>
-__device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring,
-                                            const float* qbuf, uint64_t* full, uint64_t* empty,
-                                            uint32_t seq_tile, int nchunks, int warp, int lane,
+__device__ __forceinline__ void tile_chunks(const Layout& L, uint32_t ring, uint32_t qbuf,
+                                            uint64_t* full, uint64_t* empty, int& stage,
+                                            uint32_t& phase, int nchunks, int warp, int lane,
                                             float (&acc)[RPL][GMAX], int* err, bool& ok) {
 #pragma unroll
     for (int r = 0; r < RPL; ++r)
 #pragma unroll
         for (int i = 0; i < GMAX; ++i) acc[r][i] = 0.f;
     // rows lane + 32 m share (row & 7) = (lane & 7): the swizzled slot is the same
-    const uint32_t off0 = lane * 128 + ((warp ^ (lane & 7)) << 4);
-    const float* qw = qbuf + warp * 4;
-    for (int c = 0; c < nchunks; ++c) {
-        const uint32_t s = seq_tile + (uint32_t)c;
-        const int stage = (int)(s % (uint32_t)L.nstage);
-        bool got = ok && mbar_wait(&full[stage], (s / (uint32_t)L.nstage) & 1u, err);
+    const uint32_t off0 = ring + lane * 128 + ((warp ^ (lane & 7)) << 4);
+    const uint32_t qstep = (uint32_t)L.gmax * KC * 4;
+    uint32_t qa = qbuf + warp * 16;
+    for (int c = 0; c < nchunks; ++c, qa += qstep) {
+        bool got = ok && mbar_wait(&full[stage], phase, err);
         got = __all_sync(0xffffffffu, got);  // one decision per warp
-        if (!got) {
-            // Leave the tile's barrier structure intact; the launch ends at the
-            // next tile boundary with the error already recorded.
-            ok = false;
-            continue;
-        }
-        const uint32_t base = smem_u32(ring + (size_t)stage * STAGE_BYTES) + off0;
-        float4 x[RG];
+        if (got) {
+            const uint32_t base = off0 + (uint32_t)stage * STAGE_BYTES;
+            float4 x[RG];
 #pragma unroll
-        for (int r = 0; r < RG; ++r) x[r] = lds128(base + r * 32 * 128);
-        const float* qc = qw + c * KC;
-        float4 qv[NQ];
+            for (int r = 0; r < RG; ++r) x[r] = lds128(base + r * 32 * 128);
+            float4 qv[NQ];
 #pragma unroll
-        for (int qi = 0; qi < NQ; ++qi)
-            qv[qi] = *reinterpret_cast<const float4*>(qc + qi * L.qstride);
-        // component-major: consecutive FMAs update different accumulators
+            for (int qi = 0; qi < NQ; ++qi) qv[qi] = lds128(qa + qi * KC * 4);
+            // component-major: consecutive FMAs update different accumulators
 #define M3G_COMP(cx)                                                        \
     _Pragma("unroll") for (int r = 0; r < RG; ++r)                          \
         _Pragma("unroll") for (int qi = 0; qi < NQ; ++qi) {                 \
@@ -159,124 +155,53 @@ __device__ __forceinline__ void tile_chunks(const Layout& L, unsigned char* ring
                 acc[r][qi] = fmaf(x[r].cx, qv[qi].cx, acc[r][qi]);          \
             }                                                               \
         }
-        M3G_COMP(x) M3G_COMP(y) M3G_COMP(z) M3G_COMP(w)
+            M3G_COMP(x) M3G_COMP(y) M3G_COMP(z) M3G_COMP(w)
 #undef M3G_COMP
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+        } else {
+            // Leave the tile's barrier structure intact; the launch ends at the
+            // next tile boundary with the error already recorded.
+            ok = false;
+        }
+        if (++stage == L.nstage) {
+            stage = 0;
+            phase ^= 1u;
+        }
     }
 }
 
 // g queries, rg active 32-row groups (rows past the tile's end cost nothing).
+#define M3G_TILE_ARGS L, ring, qbuf, full, empty, stage, phase, nchunks, warp, lane, acc, err, ok
 template <bool L2, int RG>
-__device__ __forceinline__ void tile_dispatch_g(int g, const Layout& L, unsigned char* ring,
-                                                const float* qbuf, uint64_t* full,
-                                                uint64_t* empty, uint32_t seq_tile, int nchunks,
+__device__ __forceinline__ void tile_dispatch_g(int g, const Layout& L, uint32_t ring,
+                                                uint32_t qbuf, uint64_t* full, uint64_t* empty,
+                                                int& stage, uint32_t& phase, int nchunks,
                                                 int warp, int lane, float (&acc)[RPL][GMAX],
                                                 int* err, bool& ok) {
 #define M3G_TILE(n) \
-    case n: tile_chunks<n, RG, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+    case n: tile_chunks<n, RG, L2>(M3G_TILE_ARGS); break;
     switch (g) {
         M3G_TILE(1) M3G_TILE(2) M3G_TILE(3) M3G_TILE(4) M3G_TILE(5) M3G_TILE(6) M3G_TILE(7)
-        default: tile_chunks<8, RG, L2>(L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+        default: tile_chunks<8, RG, L2>(M3G_TILE_ARGS); break;
     }
 #undef M3G_TILE
 }
 
 template <bool L2>
-__device__ __forceinline__ void tile_dispatch(int g, int rg, const Layout& L, unsigned char* ring,
-                                              const float* qbuf, uint64_t* full, uint64_t* empty,
-                                              uint32_t seq_tile, int nchunks, int warp, int lane,
-                                              float (&acc)[RPL][GMAX], int* err, bool& ok) {
+__device__ __forceinline__ void tile_dispatch(int g, int rg, const Layout& L, uint32_t ring,
+                                              uint32_t qbuf, uint64_t* full, uint64_t* empty,
+                                              int& stage, uint32_t& phase, int nchunks, int warp,
+                                              int lane, float (&acc)[RPL][GMAX], int* err,
+                                              bool& ok) {
     switch (rg) {
-        case 1: tile_dispatch_g<L2, 1>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
-        case 2: tile_dispatch_g<L2, 2>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
-        case 3: tile_dispatch_g<L2, 3>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
-        default: tile_dispatch_g<L2, 4>(g, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, err, ok); break;
+        case 1: tile_dispatch_g<L2, 1>(g, M3G_TILE_ARGS); break;
+        case 2: tile_dispatch_g<L2, 2>(g, M3G_TILE_ARGS); break;
+        case 3: tile_dispatch_g<L2, 3>(g, M3G_TILE_ARGS); break;
+        default: tile_dispatch_g<L2, 4>(g, M3G_TILE_ARGS); break;
     }
 }
-
-// ---- register top-k for k <= 32: lane i holds the i-th best key of the warp's
-// query, key = (score key << 32) | row, ascending; ~0 marks an empty slot.
-
-__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
-    const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
-    const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
-    return ((unsigned long long)hi << 32) | lo;
-}
-
-__device__ __forceinline__ unsigned long long shfl_u64(unsigned long long v, int src) {
-    const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)v, src);
-    const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(v >> 32), src);
-    return ((unsigned long long)hi << 32) | lo;
-}
-
-// Bitonic sort of one key per lane, ascending across lanes.
-__device__ __forceinline__ unsigned long long warp_sort_asc(unsigned long long v, int lane) {
-#pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            const unsigned long long p = shfl_xor_u64(v, j);
-            const bool up = (lane & k) == 0;
-            const bool lower = (lane & j) == 0;
-            v = (lower == up) ? (p < v ? p : v) : (p > v ? p : v);
-        }
-    }
-    return v;
-}
-
-// top (ascending, lane i = entry i) <- the 32 smallest of top and cand (any order).
-__device__ __forceinline__ unsigned long long warp_merge_top(unsigned long long top,
-                                                             unsigned long long cand, int lane) {
-    const unsigned long long b = warp_sort_asc(cand, lane);
-    const unsigned long long rb = shfl_u64(b, 31 - lane);
-    unsigned long long c = top < rb ? top : rb;  // bitonic: the 32 smallest of both
-#pragma unroll
-    for (int j = 16; j > 0; j >>= 1) {
-        const unsigned long long p = shfl_xor_u64(c, j);
-        const bool lower = (lane & j) == 0;
-        c = lower ? (p < c ? p : c) : (p > c ? p : c);
-    }
-    return c;
-}
-
-// Register top-k (k <= 32) fed through a 32-slot shared-memory buffer: a row
-// that beats the current k-th key is appended; the buffer is merged into the
-// top list (sort + bitonic merge) only when it would overflow, and once more at
-// the end of the item, so merges are rare after the first few rows.
-struct RegTopK {
-    unsigned long long top = ~0ull;  // lane i: i-th best key (ascending)
-    unsigned long long tau = ~0ull;  // current k-th best key (all lanes)
-    int nbuf = 0;                    // keys waiting in the buffer (warp-uniform)
-
-    __device__ __forceinline__ void flush(unsigned long long* buf, int k, int lane) {
-        __syncwarp();
-        const unsigned long long b = lane < nbuf ? buf[lane] : ~0ull;
-        __syncwarp();
-        top = warp_merge_top(top, b, lane);
-        if (lane >= k) top = ~0ull;
-        tau = shfl_u64(top, k - 1);
-        nbuf = 0;
-    }
-
-    __device__ __forceinline__ void push(unsigned long long* buf, int k, float s, int32_t row,
-                                         int lane) {
-        const unsigned long long key =
-            score_valid(s) ? (((unsigned long long)float_key(s) << 32) | (uint32_t)row) : ~0ull;
-        bool cand = key < tau;
-        unsigned ball = __ballot_sync(0xffffffffu, cand);
-        if (!ball) return;
-        int cnt = __popc(ball);
-        if (nbuf + cnt > 32) {
-            flush(buf, k, lane);
-            cand = key < tau;
-            ball = __ballot_sync(0xffffffffu, cand);
-            cnt = __popc(ball);
-        }
-        if (cand) buf[nbuf + __popc(ball & ((1u << lane) - 1u))] = key;
-        nbuf += cnt;
-    }
-};
+#undef M3G_TILE_ARGS
 
 // Folds up to 64 new (score, row) candidates (two per lane) into the sorted
 // top-k kept in shared memory (tks ascending by (score, row); rows of this tile
@@ -388,7 +313,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (warp == NCW) {
         // ------------------------------ producer ------------------------------
-        uint32_t seq = 0;
+        uint32_t seq = 0;     // stages filled so far
+        int pstage = 0;       // seq % nstage
+        uint32_t pphase = 0;  // (seq / nstage) & 1
         const int nitems = *a.n_items;
         bool ok = true;
         int q_issued = 0;  // items whose query copies were issued
@@ -441,9 +368,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             float* qdst = qbase + qb * qbuf_floats;
             if (lane == 0) mbar_arrive_expect_tx(&qfull[qb], (uint32_t)(np * a.dpad * 4));
             __syncwarp();
-            if (lane < np)
-                bulk_g2s(qdst + lane * L.qstride, a.Q + (int64_t)myq * a.dpad,
-                         (uint32_t)(a.dpad * 4), &qfull[qb]);
+            // chunk-major: chunk c of query i to (c * gmax + i) * 32 floats
+            for (int i = 0; i < np; ++i) {
+                const int qrow = __shfl_sync(0xffffffffu, myq, i);
+                for (int c = lane; c < nchunks; c += 32) {
+                    const int n = min(KC, a.dpad - c * KC);
+                    bulk_g2s(qdst + (c * L.gmax + i) * KC, a.Q + (int64_t)qrow * a.dpad + c * KC,
+                             (uint32_t)(n * 4), &qfull[qb]);
+                }
+            }
             q_issued = it + 1;
             // stream the list: tiles of 128 rows, each as nchunks stages of 32 dims
             const int ntiles = (nrows + TR - 1) / TR;
@@ -454,9 +387,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // the tile's rows as boxes of 128 / 64 / 32 / 16 / 8 rows (rows past
                 // the list's end, up to the next multiple of 8, are read and masked)
                 for (int c = 0; c < nchunks; ++c) {
-                    const int stage = (int)(seq % (uint32_t)L.nstage);
-                    const uint32_t use = seq / (uint32_t)L.nstage;
-                    if (use >= 1 && !mbar_wait(&empty[stage], (use - 1) & 1u, a.err)) {
+                    const int stage = pstage;
+                    if (seq >= (uint32_t)L.nstage && !mbar_wait(&empty[stage], pphase ^ 1u, a.err)) {
                         ok = false;
                         break;
                     }
@@ -472,6 +404,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         if (r8 - r >= 8) { tma_load_2d(dst + r * 128, &maps.m8, x, y0 + r, &full[stage]); r += 8; }
                     }
                     ++seq;
+                    if (++pstage == L.nstage) {
+                        pstage = 0;
+                        pphase ^= 1u;
+                    }
                 }
             }
         }
@@ -490,7 +426,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     // ------------------------------ consumers ------------------------------
     const int ctid = threadIdx.x;  // 0..255
-    uint32_t seq = 0;
+    int stage = 0;        // ring position of the next stage to consume
+    uint32_t phase = 0;
+    const uint32_t ring_u32 = smem_u32(ring);
     float* tks = tks_all + warp * KMAX;
     int32_t* tkr = tkr_all + warp * KMAX;
     const float INF = __int_as_float(0x7f800000);
@@ -504,7 +442,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (list < 0) return;
         const int g = inf->npairs, nrows = inf->nrows;
         const int64_t off = inf->off;
-        const float* qbuf = qbase + qb * qbuf_floats;
+        const uint32_t qbuf = smem_u32(qbase + qb * qbuf_floats);
         int cnt = 0;  // this warp's query (warp < g): entries held in tks/tkr (k > 32)
         RegTopK rt;   // k <= 32: register top-k with its buffer in the tks area
         unsigned long long* kbuf = reinterpret_cast<unsigned long long*>(tks_all) + warp * 32;
@@ -512,13 +450,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int ntiles = (nrows + TR - 1) / TR;
         for (int t = 0; t < ntiles; ++t) {
             float acc[RPL][GMAX];
-            const uint32_t seq_tile = seq + (uint32_t)(t * nchunks);
             const int rows_here = min(TR, nrows - t * TR);
             const int rg = (rows_here + 31) >> 5;  // active 32-row groups
             if (a.metric == kL2)
-                tile_dispatch<true>(g, rg, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, a.err, ok);
+                tile_dispatch<true>(g, rg, L, ring_u32, qbuf, full, empty, stage, phase, nchunks,
+                                    warp, lane, acc, a.err, ok);
             else
-                tile_dispatch<false>(g, rg, L, ring, qbuf, full, empty, seq_tile, nchunks, warp, lane, acc, a.err, ok);
+                tile_dispatch<false>(g, rg, L, ring_u32, qbuf, full, empty, stage, phase, nchunks,
+                                     warp, lane, acc, a.err, ok);
             float* pw = part + warp * TR * PSTRIDE;
 #pragma unroll
             for (int r = 0; r < RPL; ++r)
@@ -564,7 +503,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
         }
-        seq += (uint32_t)(ntiles * nchunks);
         if (warp < g) {
             const int64_t base = ((int64_t)inf->q[warp] * a.P + inf->slot[warp]) * a.k;
             if (reg_topk) {

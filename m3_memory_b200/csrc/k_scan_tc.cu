@@ -1,0 +1,602 @@
+// k_scan_tc.cu -- the inverted-list scan on the tensor cores, for the inner
+// product and cosine metrics (Cluster::search_into, AgentMemory/M3/src/
+// cluster.cpp:229-274, driven by IVFIndex::search_nprobe, AgentMemory/M3/src/
+// m3_index.cpp:368-483), list-centric like the SIMT scan (k_scan.cu): one work
+// item is one list with up to 32 of the queries that probe it, so a list is
+// normally streamed from HBM once per search batch.
+//
+// Arithmetic.  <x, q> in fp32 accuracy from six MMAs per 32-dim chunk:
+//   x_hw . [q_hw | q_lo]   tcgen05.mma kind::tf32 (4 x K=8), N = 2 nq_pad, on the
+//                          raw fp32 stage and the fp32 query tile [q | q - q_hw]
+//                          (the tensor core reads the tf32 part of each fp32:
+//                          the low 13 mantissa bits are dropped, rounding toward
+//                          zero, so raw x and q act as x_hw and q_hw)
+//   bf16(x_lo) . bf16(q)   tcgen05.mma kind::f16 (2 x K=16), N = nq_pad, into the
+//                          q_hw columns
+// with x_lo = x - x_hw and q_lo = q - q_hw exact in fp32.  The two column groups
+// add up to x_hw q_hw + x_hw q_lo + x_lo q = <x, q>.  The terms with a _lo factor
+// are at most 2^-10 of the products, so the tf32 / bf16 rounding of their
+// operands adds ~2^-19 relative error.  Scores differ from the reference's
+// sequential fp32 sum by rounding only, as the SIMT scan's do.
+//
+// CTA (one per SM, 14 warps):
+//   warp 0        producer: takes items from a global counter and streams the
+//                 list's rows by TMA (boxes of 32 dims x 128/64/32/16/8 rows,
+//                 SWIZZLE_128B, no multicast) through a ring of fp32 stages.
+//   warp 1        MMA warp: keeps the loop state warp-uniform, one elected lane
+//                 issues the MMAs and commits; it owns the TMEM allocation.
+//   warps 2..9    split warps: per chunk, the query operand tiles (fp32
+//                 [q | q_lo], bf16 q); per stage, the bf16 x_lo tile.
+//   warps 10..13  epilogue: TMEM -> scores -> a register top-k per query.
+// Work order inside an item: passes of up to 256 / (2 nq_pad) row blocks of 128
+// rows; inside a pass, chunk-outer, block-inner, each block accumulating into
+// its own 2 nq_pad TMEM columns, so the query tiles of a chunk serve every block
+// of the pass.  TMEM is two halves of 256 columns: one pass accumulates while
+// the epilogue drains the previous one.
+// Every wait is bounded (mbar_wait); on an error the roles stop issuing, the
+// issued copies and MMAs are drained, and TMEM is freed before the CTA leaves.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+#include "topk.cuh"
+
+namespace m3g {
+namespace {
+
+constexpr int TK = 32;                        // dims per stage (128 B of fp32)
+constexpr int TROWS = 128;                    // rows per block (MMA M)
+constexpr int X_BYTES = TROWS * TK * 4;       // 16 KB fp32 stage
+constexpr int LO_BYTES = TROWS * 128;         // 16 KB: 128 rows of 128 B (32 bf16 used)
+constexpr int QMAX = 32;                      // queries per item
+constexpr int QB1_BYTES = 2 * QMAX * 128;     // fp32 [q | q_lo] chunk: 64 rows x 128 B
+constexpr int QB2_BYTES = QMAX * 128;         // bf16 q chunk: 32 rows of 128 B (64 B used)
+constexpr int QSLOT_BYTES = QB1_BYTES + QB2_BYTES;
+constexpr int NXS = 7;                        // fp32 stages
+constexpr int NLO = 3;                        // bf16 correction stages
+constexpr int NQS = 2;                        // query chunk slots
+constexpr int NSPLIT = 8;
+constexpr int NEPI = 4;
+constexpr int W_PROD = 0, W_MMA = 1, W_SPLIT0 = 2, W_EPI0 = W_SPLIT0 + NSPLIT;
+constexpr int NWARPS = W_EPI0 + NEPI;
+constexpr int NTHR = NWARPS * 32;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int HALF_COLS = 256;
+constexpr int KMAX_TC = 32;
+constexpr int EPI_BAR = 1;                    // named barrier of the epilogue warps
+static_assert(NSPLIT * 32 == 2 * TROWS, "a split thread owns half a row of a stage");
+static_assert(QSLOT_BYTES % 1024 == 0, "query tiles stay 1024-byte aligned");
+static_assert(NSPLIT * 32 == QMAX * 8, "a split thread owns 16 bytes of a query chunk");
+
+struct ItemTC {
+    int32_t list;  // -1: no more items
+    int32_t np;
+    int32_t nrows;
+    int32_t pad;
+    int64_t off;
+    int32_t q[QMAX];
+    int32_t slot[QMAX];
+};
+
+struct LayoutTC {
+    uint32_t x_off, lo_off, q_off, sc_off, kb_off, info_off, bar_off, total;
+};
+
+__host__ __device__ inline LayoutTC make_layout_tc() {
+    LayoutTC L;
+    uint32_t o = 0;
+    L.x_off = o;
+    o += NXS * X_BYTES;
+    L.lo_off = o;
+    o += NLO * LO_BYTES;
+    L.q_off = o;
+    o += NQS * QSLOT_BYTES;
+    L.sc_off = o;
+    o += QMAX * TROWS * 4;
+    L.kb_off = o;
+    o += QMAX * 32 * 8;
+    L.info_off = o;
+    o += 2 * (uint32_t)sizeof(ItemTC);
+    o = (o + 15u) & ~15u;
+    L.bar_off = o;
+    o += 64 * 8;
+    L.total = o + 1024;  // slack for aligning the base to 1024 bytes
+    return L;
+}
+
+// Ring position: index and phase parity, advanced one use at a time.
+struct Ring {
+    int i = 0;
+    uint32_t ph = 0;
+    uint32_t n = 0;  // uses so far
+    __device__ __forceinline__ void next(int size) {
+        ++n;
+        if (++i == size) {
+            i = 0;
+            ph ^= 1u;
+        }
+    }
+};
+
+__device__ __forceinline__ float tf32_rz(float x) {
+    return __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+}
+
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                       uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ void sts64(uint32_t addr, uint32_t a, uint32_t b) {
+    asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+
+__device__ __forceinline__ float4 lds128f(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
+}
+
+// Item geometry shared by every role.
+struct Geo {
+    int np, nqp, nb, bpp;
+    __device__ __forceinline__ explicit Geo(const ItemTC& inf) {
+        np = inf.np;
+        nqp = np <= 16 ? 16 : 32;
+        nb = (inf.nrows + TROWS - 1) / TROWS;
+        bpp = HALF_COLS / (2 * nqp);
+    }
+};
+
+__global__ void __launch_bounds__(NTHR, 1)
+    list_scan_tc_kernel(const __grid_constant__ RowMaps maps, const ScanArgs a) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const LayoutTC L = make_layout_tc();
+    ItemTC* info = reinterpret_cast<ItemTC*>(smem + L.info_off);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+    uint64_t* xfull = bars;               // NXS
+    uint64_t* xempty = xfull + NXS;       // NXS
+    uint64_t* lofull = xempty + NXS;      // NLO
+    uint64_t* loempty = lofull + NLO;     // NLO
+    uint64_t* qfull = loempty + NLO;      // NQS
+    uint64_t* qempty = qfull + NQS;       // NQS
+    uint64_t* infofull = qempty + NQS;    // 2
+    uint64_t* infoempty = infofull + 2;   // 2
+    uint64_t* accfull = infoempty + 2;    // 2
+    uint64_t* accempty = accfull + 2;     // 2
+    uint64_t* drain = accempty + 2;       // 1
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    float* sc = reinterpret_cast<float*>(smem + L.sc_off);
+    unsigned long long* kbuf = reinterpret_cast<unsigned long long*>(smem + L.kb_off);
+    const uint32_t x_u32 = smem_u32(smem + L.x_off);
+    const uint32_t lo_u32 = smem_u32(smem + L.lo_off);
+    const uint32_t q_u32 = smem_u32(smem + L.q_off);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nchunks = (a.dpad + TK - 1) / TK;
+    int* err = a.err;
+
+    if (warp == W_MMA) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NXS; ++s) {
+            mbar_init(&xfull[s], 1);
+            mbar_init(&xempty[s], 1);
+        }
+        for (int s = 0; s < NLO; ++s) {
+            mbar_init(&lofull[s], NSPLIT);
+            mbar_init(&loempty[s], 1);
+        }
+        for (int s = 0; s < NQS; ++s) {
+            mbar_init(&qfull[s], NSPLIT);
+            mbar_init(&qempty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&infofull[s], 1);
+            mbar_init(&infoempty[s], NSPLIT + 1 + NEPI);
+            mbar_init(&accfull[s], 1);
+            mbar_init(&accempty[s], NEPI);
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == W_PROD && lane == 0) {
+        prefetch_tensormap(&maps.m128);
+        prefetch_tensormap(&maps.m64);
+        prefetch_tensormap(&maps.m32);
+        prefetch_tensormap(&maps.m16);
+        prefetch_tensormap(&maps.m8);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == W_PROD) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            const int nitems = *a.n_items;
+            Ring xr;
+            bool ok = true;
+            for (int it = 0; ok; ++it) {
+                const int slot = it & 1;
+                if (it >= 2 && !mbar_wait(&infoempty[slot], ((it >> 1) - 1) & 1, err)) break;
+                ItemTC* inf = &info[slot];
+                const int item = atomicAdd(a.item_counter, 1);
+                if (item >= nitems) {
+                    inf->list = -1;
+                    mbar_arrive(&infofull[slot]);
+                    break;
+                }
+                const ScanItem wi = a.items[item];
+                const int np = wi.npairs;
+                int nrows = 0;
+                int64_t off = 0;
+                if (wi.list >= 0) {
+                    nrows = a.list_len[wi.list];
+                    off = a.list_off[wi.list];
+                }
+                if (np < 1 || np > QMAX || nrows < 0) {
+                    atomicCAS(err, 0, (int)kErrBadItem);
+                    inf->list = -1;
+                    mbar_arrive(&infofull[slot]);
+                    break;
+                }
+                for (int i = 0; i < np; ++i) {
+                    inf->q[i] = a.pair_q[wi.pair_begin + i];
+                    inf->slot[i] = a.pair_slot[wi.pair_begin + i];
+                }
+                inf->list = wi.list;
+                inf->np = np;
+                inf->nrows = nrows;
+                inf->off = off;
+                mbar_arrive(&infofull[slot]);
+                const Geo g(*inf);
+                for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
+                    const int pb = min(g.bpp, g.nb - p0);
+                    for (int c = 0; c < nchunks && ok; ++c) {
+                        for (int b = 0; b < pb; ++b) {
+                            if (xr.n >= (uint32_t)NXS && !mbar_wait(&xempty[xr.i], xr.ph ^ 1u, err)) {
+                                ok = false;
+                                break;
+                            }
+                            const int row0 = (p0 + b) * TROWS;
+                            const int rows_here = min(TROWS, nrows - row0);
+                            const int r8 = (rows_here + 7) & ~7;
+                            const int y0 = (int)(off + row0);
+                            unsigned char* dst = smem + L.x_off + (size_t)xr.i * X_BYTES;
+                            mbar_arrive_expect_tx(&xfull[xr.i], (uint32_t)(r8 * 128));
+                            int r = 0;
+                            const int x = c * TK;
+                            if (r8 - r >= 128) { tma_load_2d(dst + r * 128, &maps.m128, x, y0 + r, &xfull[xr.i]); r += 128; }
+                            if (r8 - r >= 64) { tma_load_2d(dst + r * 128, &maps.m64, x, y0 + r, &xfull[xr.i]); r += 64; }
+                            if (r8 - r >= 32) { tma_load_2d(dst + r * 128, &maps.m32, x, y0 + r, &xfull[xr.i]); r += 32; }
+                            if (r8 - r >= 16) { tma_load_2d(dst + r * 128, &maps.m16, x, y0 + r, &xfull[xr.i]); r += 16; }
+                            if (r8 - r >= 8) { tma_load_2d(dst + r * 128, &maps.m8, x, y0 + r, &xfull[xr.i]); r += 8; }
+                            xr.next(NXS);
+                        }
+                    }
+                }
+            }
+            // no copy may still be landing when the CTA leaves
+            const uint32_t first = xr.n > (uint32_t)NXS ? xr.n - NXS : 0u;
+            for (uint32_t s = first; s < xr.n; ++s)
+                mbar_drain(&xfull[s % NXS], (s / NXS) & 1u);
+        }
+    } else if (warp == W_MMA) {
+        // ------------------------------ MMA warp ------------------------------
+        // The whole warp walks the schedule (waits, ring positions, descriptors:
+        // all warp-uniform); the elected lane issues the MMAs and the commits.
+        const bool leader = elect_one();
+        // descriptor of slot 0 of each ring; a slot / K-step offset of b bytes
+        // adds b >> 4 to the start-address field (shared addresses < 256 KB)
+        const uint64_t dx0 = sw128_desc(x_u32), dl0 = sw128_desc(lo_u32);
+        const uint64_t dq0 = sw128_desc(q_u32);
+        Ring xr, lr, qr;
+        uint32_t pseq = 0;
+        bool ok = true;
+        for (int it = 0; ok; ++it) {
+            const int slot = it & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it >> 1) & 1, err))) break;
+            const ItemTC* inf = &info[slot];
+            if (inf->list < 0) break;
+            const Geo g(*inf);
+            const uint32_t id_tf32 = tc_idesc_m128(2 * g.nqp, 2u);
+            const uint32_t id_bf16 = tc_idesc_m128(g.nqp, 1u);
+            for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
+                const int pb = min(g.bpp, g.nb - p0);
+                const int h = (int)(pseq & 1u);
+                if (pseq >= 2 &&
+                    !__all_sync(0xffffffffu, mbar_wait(&accempty[h], ((pseq >> 1) - 1) & 1u, err))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int c = 0; c < nchunks && ok; ++c) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&qfull[qr.i], qr.ph, err))) {
+                        ok = false;
+                        break;
+                    }
+                    const uint64_t dq1 = dq0 + (uint64_t)((qr.i * QSLOT_BYTES) >> 4);
+                    const uint64_t dq2 = dq1 + (uint64_t)(QB1_BYTES >> 4);
+                    for (int b = 0; b < pb; ++b) {
+                        bool w = mbar_wait(&xfull[xr.i], xr.ph, err);
+                        if (w) w = mbar_wait(&lofull[lr.i], lr.ph, err);
+                        if (!__all_sync(0xffffffffu, w)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t d = tmem + (uint32_t)(h * HALF_COLS + b * 2 * g.nqp);
+                        const uint64_t dx = dx0 + (uint64_t)((xr.i * X_BYTES) >> 4);
+                        const uint64_t dl = dl0 + (uint64_t)((lr.i * LO_BYTES) >> 4);
+                        if (leader) {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k)  // K = 8 tf32 = 32 B per step
+                                tc_mma_tf32(d, dx + 2 * k, dq1 + 2 * k, id_tf32, (c | k) != 0);
+#pragma unroll
+                            for (int k = 0; k < 2; ++k)  // K = 16 bf16 = 32 B per step
+                                tc_mma_f16(d, dl + 2 * k, dq2 + 2 * k, id_bf16, true);
+                            tc_commit(&xempty[xr.i]);
+                            tc_commit(&loempty[lr.i]);
+                        }
+                        __syncwarp();
+                        xr.next(NXS);
+                        lr.next(NLO);
+                    }
+                    if (!ok) break;
+                    if (leader) tc_commit(&qempty[qr.i]);
+                    __syncwarp();
+                    qr.next(NQS);
+                }
+                if (!ok) break;
+                if (leader) tc_commit(&accfull[h]);
+                __syncwarp();
+                ++pseq;
+            }
+            if (!ok) break;
+            if (leader) mbar_arrive(&infoempty[slot]);
+            __syncwarp();
+        }
+        // fires once every MMA issued above has completed
+        if (leader) {
+            tc_commit(drain);
+            mbar_drain(drain, 0);
+        }
+        __syncwarp();
+    } else if (warp < W_EPI0) {
+        // ------------------------------ split warps ------------------------------
+        const int s = threadIdx.x - W_SPLIT0 * 32;  // 0..255
+        const int r = s & (TROWS - 1), hh = s >> 7;  // stage row, half (16 dims)
+        const int qn = s >> 3, qj = s & 7;           // query row, 16-byte column
+        Ring xr, lr, qr;
+        for (int it = 0;; ++it) {
+            const int slot = it & 1;
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it >> 1) & 1, err));
+            if (!got) break;
+            const ItemTC* inf = &info[slot];
+            if (inf->list < 0) break;
+            const Geo g(*inf);
+            const int myq = qn < g.np ? inf->q[qn] : -1;
+            const float* qrow = myq >= 0 ? a.Q + (int64_t)myq * a.dpad : nullptr;
+            bool ok = true;
+            // this thread's 16 bytes of the query tile of chunk c (global loads one
+            // chunk ahead, so their latency hides behind the chunk's stages)
+            auto qload = [&](int c) {
+                const int d0 = c * TK + qj * 4;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (qrow && d0 < a.dpad) v = __ldg(reinterpret_cast<const float4*>(qrow + d0));
+                return v;
+            };
+            for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
+                const int pb = min(g.bpp, g.nb - p0);
+                float4 qnext = qload(0);
+                for (int c = 0; c < nchunks && ok; ++c) {
+                    // query tiles of chunk c: raw q (tf32 operand) and bf16 [q_lo | q]
+                    const float4 qv = qnext;
+                    if (c + 1 < nchunks) qnext = qload(c + 1);
+                    if (qr.n >= (uint32_t)NQS &&
+                        !__all_sync(0xffffffffu, mbar_wait(&qempty[qr.i], qr.ph ^ 1u, err))) {
+                        ok = false;
+                        break;
+                    }
+                    if (qn < g.nqp) {
+                        // fp32 rows qn (q) and nqp + qn (q_lo); bf16 row qn (q)
+                        const uint32_t sl = q_u32 + (uint32_t)qr.i * QSLOT_BYTES;
+                        const uint32_t sw = (uint32_t)(qn & 7);  // (nqp + qn) & 7 too
+                        const uint32_t col = ((uint32_t)qj ^ sw) << 4;
+                        sts128(sl + qn * 128 + col, __float_as_uint(qv.x), __float_as_uint(qv.y),
+                               __float_as_uint(qv.z), __float_as_uint(qv.w));
+                        const float lx = qv.x - tf32_rz(qv.x), ly = qv.y - tf32_rz(qv.y);
+                        const float lz = qv.z - tf32_rz(qv.z), lw = qv.w - tf32_rz(qv.w);
+                        sts128(sl + (g.nqp + qn) * 128 + col, __float_as_uint(lx),
+                               __float_as_uint(ly), __float_as_uint(lz), __float_as_uint(lw));
+                        const uint32_t cb = ((uint32_t)(qj >> 1) ^ sw) << 4;
+                        sts64(sl + QB1_BYTES + qn * 128 + cb + (uint32_t)(qj & 1) * 8,
+                              bf16x2(qv.x, qv.y), bf16x2(qv.z, qv.w));
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&qfull[qr.i]);
+                    qr.next(NQS);
+                    for (int b = 0; b < pb; ++b) {
+                        bool w = mbar_wait(&xfull[xr.i], xr.ph, err);
+                        if (w && lr.n >= (uint32_t)NLO) w = mbar_wait(&loempty[lr.i], lr.ph ^ 1u, err);
+                        if (!__all_sync(0xffffffffu, w)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t xb = x_u32 + (uint32_t)xr.i * X_BYTES + r * 128;
+                        const uint32_t sw = (uint32_t)(r & 7);
+                        float v[16];
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            const float4 t = lds128f(xb + ((((uint32_t)(hh * 4 + jj)) ^ sw) << 4));
+                            v[4 * jj] = t.x;
+                            v[4 * jj + 1] = t.y;
+                            v[4 * jj + 2] = t.z;
+                            v[4 * jj + 3] = t.w;
+                        }
+                        uint32_t lo[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            lo[e] = bf16x2(v[2 * e] - tf32_rz(v[2 * e]),
+                                           v[2 * e + 1] - tf32_rz(v[2 * e + 1]));
+                        // row r: bf16(x_lo) of dims 16hh.. at 16-byte columns 2hh,
+                        // 2hh+1 (swizzled by r & 7; eight consecutive rows per store
+                        // phase hit distinct bank groups)
+                        const uint32_t lb = lo_u32 + (uint32_t)lr.i * LO_BYTES + r * 128;
+                        sts128(lb + (((uint32_t)(2 * hh) ^ sw) << 4), lo[0], lo[1], lo[2], lo[3]);
+                        sts128(lb + (((uint32_t)(2 * hh + 1) ^ sw) << 4), lo[4], lo[5], lo[6], lo[7]);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&lofull[lr.i]);
+                        xr.next(NXS);
+                        lr.next(NLO);
+                    }
+                }
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&infoempty[slot]);
+        }
+    } else {
+        // ------------------------------ epilogue ------------------------------
+        const int ew = warp - W_EPI0;         // query group: queries ew, ew+4, ...
+        const int quarter = warp & 3;         // TMEM lanes 32*quarter ..
+        const int trow = quarter * 32 + lane; // row of the block this thread drains
+        const float INF = __int_as_float(0x7f800000);
+        uint32_t pseq = 0;
+        for (int it = 0;; ++it) {
+            const int slot = it & 1;
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it >> 1) & 1, err));
+            if (!got) break;
+            const ItemTC* inf = &info[slot];
+            if (inf->list < 0) break;
+            const Geo g(*inf);
+            const int nrows = inf->nrows;
+            const int64_t off = inf->off;
+            RegTopK rt[QMAX / NEPI];
+            bool ok = true;
+            for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
+                const int pb = min(g.bpp, g.nb - p0);
+                const int h = (int)(pseq & 1u);
+                if (!__all_sync(0xffffffffu, mbar_wait(&accfull[h], (pseq >> 1) & 1u, err))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int b = 0; b < pb; ++b) {
+                    const int lrow = (p0 + b) * TROWS + trow;  // row in the list
+                    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) +
+                                           (uint32_t)(h * HALF_COLS + b * 2 * g.nqp);
+                    bool live = lrow < nrows;
+                    float nb2 = 0.f;
+                    if (live) {
+                        live = a.alive[off + lrow] != 0;
+                        if (a.metric == kCosine && !a.normalized) nb2 = a.rnorm2[off + lrow];
+                    }
+                    // columns [0, nqp): x_hw q_hw + x_lo q; [nqp, 2 nqp): x_hw q_lo;
+                    // drained 16 queries at a time
+                    for (int q0 = 0; q0 < g.np; q0 += 16) {
+                        uint32_t c0[16], c1[16];
+                        tmem_ld16(taddr + q0, c0);
+                        tmem_ld16(taddr + g.nqp + q0, c1);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            if (q0 + i < g.np) {
+                                const float dot = __uint_as_float(c0[i]) + __uint_as_float(c1[i]);
+                                float s = INF;
+                                if (live) {
+                                    if (a.metric == kIP) s = -dot;
+                                    else if (a.normalized) s = 1.f - dot;
+                                    else {
+                                        const float na = a.qnorm2[inf->q[q0 + i]];
+                                        s = (na == 0.f || nb2 == 0.f) ? 1.f
+                                                                      : 1.f - dot / sqrtf(na * nb2);
+                                    }
+                                }
+                                sc[(q0 + i) * TROWS + trow] = s;
+                            }
+                        }
+                    }
+                    named_bar_sync(EPI_BAR, NEPI * 32);
+#pragma unroll
+                    for (int j = 0; j < QMAX / NEPI; ++j) {
+                        const int qi = ew + NEPI * j;
+                        if (qi < g.np) {
+                            unsigned long long* kb = kbuf + qi * 32;
+                            const int rbase = (p0 + b) * TROWS;
+#pragma unroll
+                            for (int m = 0; m < TROWS / 32; ++m)
+                                if (rbase + 32 * m < nrows)
+                                    rt[j].push(kb, a.k, sc[qi * TROWS + 32 * m + lane],
+                                               rbase + 32 * m + lane, lane);
+                        }
+                    }
+                    named_bar_sync(EPI_BAR, NEPI * 32);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&accempty[h]);
+                ++pseq;
+            }
+            if (!ok) break;
+            // the item's answers: top-k per (query, probe slot)
+#pragma unroll
+            for (int j = 0; j < QMAX / NEPI; ++j) {
+                const int qi = ew + NEPI * j;
+                if (qi < g.np) {
+                    if (rt[j].nbuf) rt[j].flush(kbuf + qi * 32, a.k, lane);
+                    const int64_t base = ((int64_t)inf->q[qi] * a.P + inf->slot[qi]) * a.k;
+                    if (lane < a.k) {
+                        const unsigned long long t = rt[j].top;
+                        const bool v = t != ~0ull;
+                        a.part_score[base + lane] = v ? key_float((uint32_t)(t >> 32)) : INF;
+                        a.part_row[base + lane] = v ? off + (int64_t)(uint32_t)(t & 0xffffffffu) : -1;
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&infoempty[slot]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == W_MMA) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+}  // namespace
+
+bool scan_tc_supported(int metric, int k) { return metric != kL2 && k >= 1 && k <= KMAX_TC; }
+
+int scan_tc_gmax() { return QMAX; }
+
+cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, int grid, cudaStream_t st) {
+    if (!scan_tc_supported(a.metric, a.k) || (a.dpad & 3)) return cudaErrorInvalidValue;
+    const LayoutTC L = make_layout_tc();
+    cudaError_t e = cudaFuncSetAttribute(list_scan_tc_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    if (e != cudaSuccess) return e;
+    list_scan_tc_kernel<<<grid, NTHR, L.total, st>>>(maps, a);
+    return cudaGetLastError();
+}
+
+}  // namespace m3g

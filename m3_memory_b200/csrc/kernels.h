@@ -78,6 +78,12 @@ int scan_gmax_for_dim(int dpad);
 cudaError_t launch_list_scan(const RowMaps& maps, const ScanArgs& a, int gmax, int grid,
                              cudaStream_t st);
 
+// The tensor-core scan (k_scan_tc.cu): inner product and cosine, k <= 32,
+// items of up to scan_tc_gmax() queries.
+bool scan_tc_supported(int metric, int k);
+int scan_tc_gmax();
+cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, int grid, cudaStream_t st);
+
 // Work list: per-list counts of (query, probe) pairs, items, and the pairs
 // grouped by list.  list_order lists the clusters longest first.
 cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,

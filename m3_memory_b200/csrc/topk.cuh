@@ -1,0 +1,91 @@
+// topk.cuh -- warp-level top-k (k <= 32) of the list scans: lane i of a warp
+// holds the i-th best key of one query, key = (score key << 32) | row,
+// ascending, ~0 marking an empty slot; rows that beat the current k-th key are
+// buffered in shared memory and merged in by a bitonic sort + merge.
+#pragma once
+
+#include "common.cuh"
+
+namespace m3g {
+
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+    const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
+    const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
+    return ((unsigned long long)hi << 32) | lo;
+}
+
+__device__ __forceinline__ unsigned long long shfl_u64(unsigned long long v, int src) {
+    const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)v, src);
+    const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(v >> 32), src);
+    return ((unsigned long long)hi << 32) | lo;
+}
+
+// Bitonic sort of one key per lane, ascending across lanes.
+__device__ __forceinline__ unsigned long long warp_sort_asc(unsigned long long v, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const unsigned long long p = shfl_xor_u64(v, j);
+            const bool up = (lane & k) == 0;
+            const bool lower = (lane & j) == 0;
+            v = (lower == up) ? (p < v ? p : v) : (p > v ? p : v);
+        }
+    }
+    return v;
+}
+
+// top (ascending, lane i = entry i) <- the 32 smallest of top and cand (any order).
+__device__ __forceinline__ unsigned long long warp_merge_top(unsigned long long top,
+                                                             unsigned long long cand, int lane) {
+    const unsigned long long b = warp_sort_asc(cand, lane);
+    const unsigned long long rb = shfl_u64(b, 31 - lane);
+    unsigned long long c = top < rb ? top : rb;  // bitonic: the 32 smallest of both
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) {
+        const unsigned long long p = shfl_xor_u64(c, j);
+        const bool lower = (lane & j) == 0;
+        c = lower ? (p < c ? p : c) : (p > c ? p : c);
+    }
+    return c;
+}
+
+// Register top-k (k <= 32) fed through a 32-slot shared-memory buffer: a row
+// that beats the current k-th key is appended; the buffer is merged into the
+// top list (sort + bitonic merge) only when it would overflow, and once more at
+// the end of the item, so merges are rare after the first few rows.
+struct RegTopK {
+    unsigned long long top = ~0ull;  // lane i: i-th best key (ascending)
+    unsigned long long tau = ~0ull;  // current k-th best key (all lanes)
+    int nbuf = 0;                    // keys waiting in the buffer (warp-uniform)
+
+    __device__ __forceinline__ void flush(unsigned long long* buf, int k, int lane) {
+        __syncwarp();
+        const unsigned long long b = lane < nbuf ? buf[lane] : ~0ull;
+        __syncwarp();
+        top = warp_merge_top(top, b, lane);
+        if (lane >= k) top = ~0ull;
+        tau = shfl_u64(top, k - 1);
+        nbuf = 0;
+    }
+
+    __device__ __forceinline__ void push(unsigned long long* buf, int k, float s, int32_t row,
+                                         int lane) {
+        const unsigned long long key =
+            score_valid(s) ? (((unsigned long long)float_key(s) << 32) | (uint32_t)row) : ~0ull;
+        bool cand = key < tau;
+        unsigned ball = __ballot_sync(0xffffffffu, cand);
+        if (!ball) return;
+        int cnt = __popc(ball);
+        if (nbuf + cnt > 32) {
+            flush(buf, k, lane);
+            cand = key < tau;
+            ball = __ballot_sync(0xffffffffu, cand);
+            cnt = __popc(ball);
+        }
+        if (cand) buf[nbuf + __popc(ball & ((1u << lane) - 1u))] = key;
+        nbuf += cnt;
+    }
+};
+
+}  // namespace m3g
