@@ -227,75 +227,101 @@ __global__ void __launch_bounds__(NTHR, 1)
 
     if (warp == W_PROD) {
         // ------------------------------ producer ------------------------------
-        if (lane == 0) {
-            const int nitems = *a.n_items;
-            Ring xr;
-            bool ok = true;
-            for (int it = 0; ok; ++it) {
-                const int slot = it & 1;
-                if (it >= 2 && !mbar_wait(&infoempty[slot], ((it >> 1) - 1) & 1, err)) break;
-                ItemTC* inf = &info[slot];
-                const int item = atomicAdd(a.item_counter, 1);
-                if (item >= nitems) {
+        // The whole warp walks the schedule with warp-uniform values (so the
+        // copy operands stay in uniform registers); the elected lane issues.
+        const bool leader = elect_one();
+        const int nitems = *a.n_items;
+        const uint32_t xbase = smem_u32(smem + L.x_off);
+        Ring xr;
+        bool ok = true;
+        for (int it = 0; ok; ++it) {
+            const int slot = it & 1;
+            if (it >= 2 &&
+                !__all_sync(0xffffffffu, mbar_wait(&infoempty[slot], ((it >> 1) - 1) & 1, err)))
+                break;
+            ItemTC* inf = &info[slot];
+            int item = 0;
+            if (leader) item = atomicAdd(a.item_counter, 1);
+            item = __shfl_sync(0xffffffffu, item, __ffs(__ballot_sync(0xffffffffu, leader)) - 1);
+            if (item >= nitems) {
+                if (leader) {
                     inf->list = -1;
                     mbar_arrive(&infofull[slot]);
-                    break;
                 }
-                const ScanItem wi = a.items[item];
-                const int np = wi.npairs;
-                int nrows = 0;
-                int64_t off = 0;
-                if (wi.list >= 0) {
-                    nrows = a.list_len[wi.list];
-                    off = a.list_off[wi.list];
-                }
-                if (np < 1 || np > QMAX || nrows < 0) {
+                break;
+            }
+            const ScanItem wi = a.items[item];
+            const int np = wi.npairs;
+            int nrows = 0;
+            int64_t off = 0;
+            if (wi.list >= 0) {
+                nrows = a.list_len[wi.list];
+                off = a.list_off[wi.list];
+            }
+            if (np < 1 || np > QMAX || nrows < 0) {
+                if (leader) {
                     atomicCAS(err, 0, (int)kErrBadItem);
                     inf->list = -1;
                     mbar_arrive(&infofull[slot]);
-                    break;
                 }
-                for (int i = 0; i < np; ++i) {
-                    inf->q[i] = a.pair_q[wi.pair_begin + i];
-                    inf->slot[i] = a.pair_slot[wi.pair_begin + i];
-                }
+                break;
+            }
+            if (lane < np) {
+                inf->q[lane] = a.pair_q[wi.pair_begin + lane];
+                inf->slot[lane] = a.pair_slot[wi.pair_begin + lane];
+            }
+            if (leader) {
                 inf->list = wi.list;
                 inf->np = np;
                 inf->nrows = nrows;
                 inf->off = off;
-                mbar_arrive(&infofull[slot]);
-                const Geo g(*inf);
-                for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
-                    const int pb = min(g.bpp, g.nb - p0);
-                    for (int c = 0; c < nchunks && ok; ++c) {
-                        for (int b = 0; b < pb; ++b) {
-                            if (xr.n >= (uint32_t)NXS && !mbar_wait(&xempty[xr.i], xr.ph ^ 1u, err)) {
-                                ok = false;
-                                break;
-                            }
-                            const int row0 = (p0 + b) * TROWS;
-                            const int rows_here = min(TROWS, nrows - row0);
-                            const int r8 = (rows_here + 7) & ~7;
-                            const int y0 = (int)(off + row0);
-                            unsigned char* dst = smem + L.x_off + (size_t)xr.i * X_BYTES;
-                            mbar_arrive_expect_tx(&xfull[xr.i], (uint32_t)(r8 * 128));
-                            int r = 0;
-                            const int x = c * TK;
-                            if (r8 - r >= 128) { tma_load_2d(dst + r * 128, &maps.m128, x, y0 + r, &xfull[xr.i]); r += 128; }
-                            if (r8 - r >= 64) { tma_load_2d(dst + r * 128, &maps.m64, x, y0 + r, &xfull[xr.i]); r += 64; }
-                            if (r8 - r >= 32) { tma_load_2d(dst + r * 128, &maps.m32, x, y0 + r, &xfull[xr.i]); r += 32; }
-                            if (r8 - r >= 16) { tma_load_2d(dst + r * 128, &maps.m16, x, y0 + r, &xfull[xr.i]); r += 16; }
-                            if (r8 - r >= 8) { tma_load_2d(dst + r * 128, &maps.m8, x, y0 + r, &xfull[xr.i]); r += 8; }
-                            xr.next(NXS);
+            }
+            __syncwarp();
+            if (leader) mbar_arrive(&infofull[slot]);
+            const int nb = (nrows + TROWS - 1) / TROWS;
+            const int bpp = HALF_COLS / (2 * (np <= 16 ? 16 : 32));
+            for (int p0 = 0; p0 < nb && ok; p0 += bpp) {
+                const int pb = min(bpp, nb - p0);
+                for (int c = 0; c < nchunks && ok; ++c) {
+                    const int x = c * TK;
+                    for (int b = 0; b < pb; ++b) {
+                        if (xr.n >= (uint32_t)NXS &&
+                            !__all_sync(0xffffffffu, mbar_wait(&xempty[xr.i], xr.ph ^ 1u, err))) {
+                            ok = false;
+                            break;
                         }
+                        // the block's rows as boxes of 128 / 64 / 32 / 16 / 8 rows (rows
+                        // past the list's end, up to the next multiple of 8, are read and
+                        // masked later)
+                        const int row0 = (p0 + b) * TROWS;
+                        const int r8 = (min(TROWS, nrows - row0) + 7) & ~7;
+                        const int y0 = (int)(off + row0);
+                        const uint32_t dst = xbase + (uint32_t)xr.i * X_BYTES;
+                        uint64_t* bar = &xfull[xr.i];
+                        if (leader) {
+                            mbar_arrive_expect_tx(bar, (uint32_t)(r8 * 128));
+                            if (r8 == 128) {
+                                tma_load_2d_u32(dst, &maps.m128, x, y0, bar);
+                            } else {
+                                int r = 0;
+                                if (r8 - r >= 64) { tma_load_2d_u32(dst + r * 128, &maps.m64, x, y0 + r, bar); r += 64; }
+                                if (r8 - r >= 32) { tma_load_2d_u32(dst + r * 128, &maps.m32, x, y0 + r, bar); r += 32; }
+                                if (r8 - r >= 16) { tma_load_2d_u32(dst + r * 128, &maps.m16, x, y0 + r, bar); r += 16; }
+                                if (r8 - r >= 8) { tma_load_2d_u32(dst + r * 128, &maps.m8, x, y0 + r, bar); r += 8; }
+                            }
+                        }
+                        __syncwarp();
+                        xr.next(NXS);
                     }
                 }
             }
-            // no copy may still be landing when the CTA leaves
-            const uint32_t first = xr.n > (uint32_t)NXS ? xr.n - NXS : 0u;
-            for (uint32_t s = first; s < xr.n; ++s)
+        }
+        // no copy may still be landing when the CTA leaves
+        if (leader) {
+            for (uint32_t s = xr.n > (uint32_t)NXS ? xr.n - NXS : 0u; s < xr.n; ++s)
                 mbar_drain(&xfull[s % NXS], (s / NXS) & 1u);
         }
+        __syncwarp();
     } else if (warp == W_MMA) {
         // ------------------------------ MMA warp ------------------------------
         // The whole warp walks the schedule (waits, ring positions, descriptors:
