@@ -139,9 +139,16 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def scan_kernel_name():
+    """The list-scan kernel the engine runs for this workload (inner product, k <= 32)."""
+    return "list_scan_kernel" if os.environ.get("M3G_SCAN") == "simt" else "list_scan_tc_kernel"
+
+
 def scan_traffic_per_launch():
     """dram bytes of one scan launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "list_scan_traffic.txt"
+    name = "list_scan_traffic.txt" if scan_kernel_name() == "list_scan_kernel" \
+        else "list_scan_tc_traffic.txt"
+    p = ROOT / "profiles" / name
     if p.is_file():
         for line in p.read_text().splitlines():
             if line.startswith("dram_bytes_per_launch:"):
@@ -474,7 +481,7 @@ def run_ours(args, rank, world, local_rank):
         achieved = avg_bytes / (avg_ms / 1e3) / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": achieved / peak, "traffic": scan_traffic_per_launch(),
-                    "kernel": "list_scan_kernel",
+                    "kernel": scan_kernel_name(),
                     "bytes_per_launch": avg_bytes, "ms_per_launch": avg_ms,
                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                     if peak_kind == "measured" else "fallback 6650 GB/s"}
