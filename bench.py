@@ -57,6 +57,26 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+_RESULT_OUT = None
+
+
+def emit(obj):
+    """The one JSON line on stdout (the result); everything else goes to stderr."""
+    out = _RESULT_OUT or sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
+
+
+def keep_stdout_for_result():
+    """Point file descriptor 1 at stderr for the rest of the process (libraries such as
+    NCCL print banners there) and keep a private copy of the original stdout for the
+    result line."""
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
 def make_data():
     from m3_memory_b200 import synthetic as S
 
@@ -183,17 +203,6 @@ def recall_at_k(found_ids, exact_ids, k):
     return hit / (len(found_ids) * k)
 
 
-def shard_lists(sizes, world):
-    """Greedy balancing: largest list first onto the least-loaded rank."""
-    load = [0] * world
-    owner = np.empty(len(sizes), np.int32)
-    for l in np.argsort(-np.asarray(sizes), kind="stable"):
-        r = int(np.argmin(load))
-        owner[l] = r
-        load[r] += int(sizes[l])
-    return owner
-
-
 def cpu_reference_qps(C, X, assign, Q_all, threads, target_s=12.0, warm_q=None):
     """The reference core's IVFIndex::search_nprobe on the host: returns
     (qps, sample description)."""
@@ -233,9 +242,9 @@ def run_reference(args, rank, world):
         except Exception:
             pass
     if not O.have_ref():
-        print(json.dumps({"impl": "reference",
-                          "unavailable": "oracle/_ref/liboracle_ref.so (the reference core) "
-                                         "was not built on this box"}))
+        emit({"impl": "reference",
+              "unavailable": "oracle/_ref/liboracle_ref.so (the reference core) "
+                             "was not built on this box"})
         return
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     X, Qb = make_data()
@@ -289,7 +298,7 @@ def run_reference(args, rank, world):
     dt = time.perf_counter() - t0
     qps = per_step * args.steps / dt
     sample = f"{per_step} queries per step over {threads} host threads"
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": "search QPS at recall@10>=0.95 (IVF, dim 1024)",
         "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
@@ -300,7 +309,7 @@ def run_reference(args, rank, world):
                          "kind": "reference", "sample": sample},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }))
+    })
 
 
 # ---------------------------------------------------------------- our arm
@@ -309,6 +318,7 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from m3_memory_b200 import cabi
+    from m3_memory_b200.sharding import ShardedSearch, shard_lists
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -321,7 +331,7 @@ def run_ours(args, rank, world, local_rank):
     C, assign = eng.kmeans(X, NLIST, KMEANS_ITERS, SEED, METRIC_IP, False)
     log(f"[rank {rank}] k-means {KMEANS_ITERS} it on the GPU: {time.perf_counter() - t0:.1f}s")
     sizes = np.bincount(assign, minlength=NLIST)
-    owner = shard_lists(sizes, world) if world > 1 else np.zeros(NLIST, np.int32)
+    owner = shard_lists(sizes, world)
     eng.create_ivf(1, DIM, METRIC_IP, False, C)
     order = np.argsort(assign, kind="stable")
     bounds = np.searchsorted(assign[order], np.arange(NLIST + 1))
@@ -336,26 +346,11 @@ def run_ours(args, rank, world, local_rank):
         f"after {time.perf_counter() - t_setup:.1f}s")
 
     Qd = torch.from_numpy(Qb).to(dev)  # [NBATCH, BATCH, DIM]
-    out_ids = torch.empty((BATCH, K), dtype=torch.int64, device=dev)
-    out_sc = torch.empty((BATCH, K), dtype=torch.float32, device=dev)
-    out_cnt = torch.empty((BATCH,), dtype=torch.int32, device=dev)
-    g_ids = torch.empty((world, BATCH, K), dtype=torch.int64, device=dev)
-    g_sc = torch.empty((world, BATCH, K), dtype=torch.float32, device=dev)
-    m_ids = torch.empty((BATCH, K), dtype=torch.int64, device=dev)
-    m_sc = torch.empty((BATCH, K), dtype=torch.float32, device=dev)
-    m_cnt = torch.empty((BATCH,), dtype=torch.int32, device=dev)
+    sharded = ShardedSearch(eng, 1, K, BATCH, world, dev)
 
     def step(b, nprobe):
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        eng.search_device(1, Qd[b].data_ptr(), BATCH, K, nprobe, out_ids.data_ptr(),
-                          out_sc.data_ptr(), out_cnt.data_ptr(), stream)
-        if world == 1:
-            return out_ids, out_sc
-        dist.all_gather_into_tensor(g_sc, out_sc)
-        dist.all_gather_into_tensor(g_ids, out_ids)
-        eng.merge_shards_device(g_sc.data_ptr(), g_ids.data_ptr(), world, BATCH, K,
-                                m_ids.data_ptr(), m_sc.data_ptr(), m_cnt.data_ptr(), stream)
-        return m_ids, m_sc
+        ids, sc, _ = sharded.search(Qd[b], nprobe)
+        return ids, sc
 
     # ---- recall@10 against exact search (untimed); pick nprobe
     nprobe = NPROBE
@@ -440,18 +435,11 @@ def run_ours(args, rank, world, local_rank):
         e2e_s = time.perf_counter() - t0
         eng.set_profiling(False)
     else:
-        stream = torch.cuda.current_stream(dev)
         qdev = torch.empty((BATCH, DIM), dtype=torch.float32, device=dev)
 
         def e2e_step(b):
             qdev.copy_(pinned[b], non_blocking=True)
-            s = stream.cuda_stream
-            eng.search_device(1, qdev.data_ptr(), BATCH, K, nprobe, out_ids.data_ptr(),
-                              out_sc.data_ptr(), out_cnt.data_ptr(), s)
-            dist.all_gather_into_tensor(g_sc, out_sc)
-            dist.all_gather_into_tensor(g_ids, out_ids)
-            eng.merge_shards_device(g_sc.data_ptr(), g_ids.data_ptr(), world, BATCH, K,
-                                    m_ids.data_ptr(), m_sc.data_ptr(), m_cnt.data_ptr(), s)
+            m_ids, m_sc, m_cnt = sharded.search(qdev, nprobe)
             h_ids.copy_(m_ids, non_blocking=True)
             h_sc.copy_(m_sc, non_blocking=True)
             h_cnt.copy_(m_cnt, non_blocking=True)
@@ -472,7 +460,7 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return
     per_step_launches = (launches / args.steps) if launches else (
-        8 if world == 1 else 9)
+        9 if world == 1 else 10)
     peak, peak_kind = peaks()
     roofline = None
     if scan_ms:
@@ -518,7 +506,7 @@ def run_ours(args, rank, world, local_rank):
         "roofline": roofline,
         "cpu_baseline": cpu,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
@@ -533,6 +521,7 @@ def main():
     ap.add_argument("--nlist", type=int, default=None, help="profiling only: fewer lists")
     ap.add_argument("--nprobe", type=int, default=None, help="profiling only: other nprobe")
     args = ap.parse_args()
+    keep_stdout_for_result()
     global N_VEC, NLIST, NPROBE, FIXED_NPROBE, WORKLOAD
     if args.nvec or args.nlist or args.nprobe:
         N_VEC = args.nvec or N_VEC

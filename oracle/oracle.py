@@ -398,6 +398,29 @@ def search_nprobe(Q, C, lists: CsrLists, metric, normalized, k, nprobe, want_pro
     return ids, sc, cnt
 
 
+def merge_shards(scores, ids):
+    """Per-shard answers [nshard, nq, k] (ascending scores, -1 / +inf padding) merged
+    into [nq, k]: the k smallest valid (finite, non-NaN) scores by (score, shard,
+    position) -- the final ascending sort of IVFIndex::search_nprobe
+    (AgentMemory/M3/src/m3_index.cpp:444-475) applied across shards.  Returns
+    (ids, scores, counts) padded with -1 / +inf."""
+    scores = np.asarray(scores, np.float32)
+    ids = np.asarray(ids, np.int64)
+    ns, nq, k = scores.shape
+    out_ids = np.full((nq, k), -1, np.int64)
+    out_sc = np.full((nq, k), np.inf, np.float32)
+    cnt = np.zeros(nq, np.int32)
+    for q in range(nq):
+        s = scores[:, q, :].reshape(-1)  # flat index = shard * k + position
+        valid = np.flatnonzero(s < np.inf)  # NaN and +inf compare false
+        order = valid[np.lexsort((valid, s[valid]))][:k]
+        c = len(order)
+        out_sc[q, :c] = s[order]
+        out_ids[q, :c] = ids[:, q, :].reshape(-1)[order]
+        cnt[q] = c
+    return out_ids, out_sc, cnt
+
+
 def search_on(Q, lists: CsrLists, cids, metric, normalized, k):
     """IVFIndex::search_on restated (explicit cluster list, no coarse step)."""
     Q = _f32(Q)

@@ -1,0 +1,143 @@
+"""List sharding on CPU with world size 2 over gloo (no GPU).
+
+Each rank owns the lists m3_memory_b200.sharding.shard_lists gives it, searches
+only those lists with the oracle (the reference's algorithm, replicated coarse
+selection), the per-rank answers are all-gathered and merged by the shard-merge
+rule; the merged answer must equal the unsharded search.  This is the
+decomposition the GPU path uses (search per rank, all-gather, merge kernel)."""
+import datetime
+import multiprocessing as mp
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from helpers import compare_search
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(seed=3):
+    rng = np.random.default_rng(seed)
+    L, d, nq, k, nprobe = 24, 40, 30, 7, 6
+    sizes = np.minimum((60 * rng.zipf(1.6, L)) % 400, 400)
+    sizes[[3, 11]] = 0  # empty lists
+    C = rng.standard_normal((L, d)).astype(np.float32)
+    owner_of_row = np.repeat(np.arange(L), sizes)
+    X = (C[owner_of_row] + 0.8 * rng.standard_normal((len(owner_of_row), d))).astype(np.float32)
+    Q = (C[rng.integers(0, L, nq)] + 0.8 * rng.standard_normal((nq, d))).astype(np.float32)
+    ids = np.arange(len(X), dtype=np.int64) * 3 + 1
+    alive = (rng.random(len(X)) > 0.05).astype(np.uint8)
+    off = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    return dict(C=C, X=X, Q=Q, ids=ids, alive=alive, off=off, sizes=sizes, k=k, nprobe=nprobe)
+
+
+def _local_lists(O, c, owner, rank):
+    """CSR lists of this rank: its own lists' rows, the others empty."""
+    off, X, ids, alive = c["off"], c["X"], c["ids"], c["alive"]
+    keep = np.concatenate([np.arange(off[l], off[l + 1]) for l in range(len(off) - 1)
+                           if owner[l] == rank] + [np.zeros(0, np.int64)]).astype(np.int64)
+    lens = np.array([off[l + 1] - off[l] if owner[l] == rank else 0
+                     for l in range(len(off) - 1)], np.int64)
+    loff = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    return O.CsrLists(loff, X[keep], ids[keep], alive[keep])
+
+
+def _rank_main(rank, world, port, metric, normalized, out):
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+
+    from m3_memory_b200.sharding import shard_lists
+    from oracle import oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        c = _case()
+        owner = shard_lists(c["sizes"], world)
+        lists = _local_lists(O, c, owner, rank)
+        ids, sc, cnt = O.search_nprobe(c["Q"], c["C"], lists, metric, normalized, c["k"],
+                                       c["nprobe"])
+        g_sc = [torch.empty_like(torch.from_numpy(sc)) for _ in range(world)]
+        g_ids = [torch.empty_like(torch.from_numpy(ids)) for _ in range(world)]
+        dist.all_gather(g_sc, torch.from_numpy(sc))
+        dist.all_gather(g_ids, torch.from_numpy(ids))
+        if rank == 0:
+            merged = O.merge_shards(np.stack([t.numpy() for t in g_sc]),
+                                    np.stack([t.numpy() for t in g_ids]))
+            out.put(("ok", merged, owner))
+    except Exception as ex:  # reported to the parent, which fails the test
+        out.put(("error", repr(ex), None))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("metric,normalized", [(1, False), (0, False), (2, False)])
+def test_sharded_search_equals_unsharded(oracle_mod, metric, normalized):
+    from m3_memory_b200.sharding import shard_load, shard_lists
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, metric, normalized, out))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        status, merged, owner = out.get(timeout=120)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert status == "ok", merged
+    c = _case()
+    np.testing.assert_array_equal(owner, shard_lists(c["sizes"], world))
+    lists = oracle_mod.CsrLists(c["off"], c["X"], c["ids"], c["alive"])
+    ref = oracle_mod.search_nprobe(c["Q"], c["C"], lists, metric, normalized, c["k"],
+                                   c["nprobe"])
+    compare_search(merged, ref, exact=True)
+    assert all(p.exitcode == 0 for p in procs)
+    # every list has one owner; the two ranks' rows differ by less than the largest list
+    load = shard_load(c["sizes"], owner, world)
+    assert load.sum() == c["sizes"].sum()
+    assert abs(int(load[0]) - int(load[1])) <= int(c["sizes"].max())
+
+
+def test_shard_lists_balance_and_determinism():
+    from m3_memory_b200.sharding import shard_load, shard_lists
+
+    rng = np.random.default_rng(0)
+    sizes = rng.zipf(1.3, 4096) % 5000
+    for world in (1, 2, 4, 8):
+        owner = shard_lists(sizes, world)
+        assert owner.min() >= 0 and owner.max() < world
+        np.testing.assert_array_equal(owner, shard_lists(sizes.copy(), world))
+        load = shard_load(sizes, owner, world)
+        assert load.sum() == sizes.sum()
+        assert load.max() - load.min() <= sizes.max()
+    with pytest.raises(ValueError):
+        shard_lists(sizes, 0)
+
+
+def test_merge_shards_rule(oracle_mod):
+    inf, nan = np.inf, np.nan
+    sc = np.array([[[0.1, 0.3, inf]], [[0.1, 0.2, nan]]], np.float32)
+    ids = np.array([[[5, 6, -1]], [[7, 8, -1]]], np.int64)
+    got_ids, got_sc, cnt = oracle_mod.merge_shards(sc, ids)
+    np.testing.assert_array_equal(got_ids, [[5, 7, 8]])  # tie 0.1: shard 0 first
+    np.testing.assert_array_equal(got_sc, np.array([[0.1, 0.1, 0.2]], np.float32))
+    np.testing.assert_array_equal(cnt, [3])
