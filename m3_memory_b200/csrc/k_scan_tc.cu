@@ -29,8 +29,9 @@
 //                 [q | q_lo], bf16 q); per stage, the bf16 x_lo tile.
 //   warps 10..13  epilogue: TMEM -> scores -> a register top-k per query.
 // Work order inside an item: passes of up to 256 / (2 nq_pad) row blocks of 128
-// rows; inside a pass, chunk-outer, block-inner, each block accumulating into
-// its own 2 nq_pad TMEM columns, so the query tiles of a chunk serve every block
+// rows; inside a pass, chunk-outer, block-inner (a 32 KB stage carries the
+// chunk of two consecutive blocks, which halves the per-stage handshakes), each
+// block accumulating into its own 2 nq_pad TMEM columns, so the query tiles of a chunk serve every block
 // of the pass.  TMEM is two halves of 256 columns: one pass accumulates while
 // the epilogue drains the previous one.
 // Every wait is bounded (mbar_wait); on an error the roles stop issuing, the
@@ -48,13 +49,15 @@ namespace {
 
 constexpr int TK = 32;                        // dims per stage (128 B of fp32)
 constexpr int TROWS = 128;                    // rows per block (MMA M)
-constexpr int X_BYTES = TROWS * TK * 4;       // 16 KB fp32 stage
-constexpr int LO_BYTES = TROWS * 128;         // 16 KB: 128 rows of 128 B (32 bf16 used)
+constexpr int SBLK = 2;                       // row blocks per stage
+constexpr int BLK_BYTES = TROWS * TK * 4;     // 16 KB: one block's 32-dim chunk, fp32
+constexpr int X_BYTES = SBLK * BLK_BYTES;     // 32 KB fp32 stage (256 rows x 32 dims)
+constexpr int LO_BYTES = TROWS * 128;         // 16 KB: block j's x_lo in bytes 64 j .. of each row
 constexpr int QMAX = 32;                      // queries per item
 constexpr int QB1_BYTES = 2 * QMAX * 128;     // fp32 [q | q_lo] chunk: 64 rows x 128 B
 constexpr int QB2_BYTES = QMAX * 128;         // bf16 q chunk: 32 rows of 128 B (64 B used)
 constexpr int QSLOT_BYTES = QB1_BYTES + QB2_BYTES;
-constexpr int NXS = 7;                        // fp32 stages
+constexpr int NXS = 4;                        // fp32 stages
 constexpr int NLO = 3;                        // bf16 correction stages
 constexpr int NQS = 2;                        // query chunk slots
 constexpr int NSPLIT = 8;
@@ -66,7 +69,7 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int HALF_COLS = 256;
 constexpr int KMAX_TC = 32;
 constexpr int EPI_BAR = 1;                    // named barrier of the epilogue warps
-static_assert(NSPLIT * 32 == 2 * TROWS, "a split thread owns half a row of a stage");
+static_assert(NSPLIT * 32 == SBLK * TROWS, "a split thread owns one row of a stage");
 static_assert(QSLOT_BYTES % 1024 == 0, "query tiles stay 1024-byte aligned");
 static_assert(NSPLIT * 32 == QMAX * 8, "a split thread owns 16 bytes of a query chunk");
 
@@ -284,30 +287,36 @@ __global__ void __launch_bounds__(NTHR, 1)
                 const int pb = min(bpp, nb - p0);
                 for (int c = 0; c < nchunks && ok; ++c) {
                     const int x = c * TK;
-                    for (int b = 0; b < pb; ++b) {
+                    for (int b = 0; b < pb; b += SBLK) {
                         if (xr.n >= (uint32_t)NXS &&
                             !__all_sync(0xffffffffu, mbar_wait(&xempty[xr.i], xr.ph ^ 1u, err))) {
                             ok = false;
                             break;
                         }
-                        // the block's rows as boxes of 128 / 64 / 32 / 16 / 8 rows (rows
+                        const int nblk = min(SBLK, pb - b);
+                        // each block's rows as boxes of 128 / 64 / 32 / 16 / 8 rows (rows
                         // past the list's end, up to the next multiple of 8, are read and
-                        // masked later)
-                        const int row0 = (p0 + b) * TROWS;
-                        const int r8 = (min(TROWS, nrows - row0) + 7) & ~7;
-                        const int y0 = (int)(off + row0);
-                        const uint32_t dst = xbase + (uint32_t)xr.i * X_BYTES;
+                        // masked later); block j of the stage at byte 16 KB * j
+                        int bytes = 0;
+                        for (int j = 0; j < nblk; ++j)
+                            bytes += ((min(TROWS, nrows - (p0 + b + j) * TROWS) + 7) & ~7) * 128;
                         uint64_t* bar = &xfull[xr.i];
                         if (leader) {
-                            mbar_arrive_expect_tx(bar, (uint32_t)(r8 * 128));
-                            if (r8 == 128) {
-                                tma_load_2d_u32(dst, &maps.m128, x, y0, bar);
-                            } else {
-                                int r = 0;
-                                if (r8 - r >= 64) { tma_load_2d_u32(dst + r * 128, &maps.m64, x, y0 + r, bar); r += 64; }
-                                if (r8 - r >= 32) { tma_load_2d_u32(dst + r * 128, &maps.m32, x, y0 + r, bar); r += 32; }
-                                if (r8 - r >= 16) { tma_load_2d_u32(dst + r * 128, &maps.m16, x, y0 + r, bar); r += 16; }
-                                if (r8 - r >= 8) { tma_load_2d_u32(dst + r * 128, &maps.m8, x, y0 + r, bar); r += 8; }
+                            mbar_arrive_expect_tx(bar, (uint32_t)bytes);
+                            for (int j = 0; j < nblk; ++j) {
+                                const int row0 = (p0 + b + j) * TROWS;
+                                const int r8 = (min(TROWS, nrows - row0) + 7) & ~7;
+                                const int y0 = (int)(off + row0);
+                                const uint32_t dst = xbase + (uint32_t)xr.i * X_BYTES + j * BLK_BYTES;
+                                if (r8 == 128) {
+                                    tma_load_2d_u32(dst, &maps.m128, x, y0, bar);
+                                } else {
+                                    int r = 0;
+                                    if (r8 - r >= 64) { tma_load_2d_u32(dst + r * 128, &maps.m64, x, y0 + r, bar); r += 64; }
+                                    if (r8 - r >= 32) { tma_load_2d_u32(dst + r * 128, &maps.m32, x, y0 + r, bar); r += 32; }
+                                    if (r8 - r >= 16) { tma_load_2d_u32(dst + r * 128, &maps.m16, x, y0 + r, bar); r += 16; }
+                                    if (r8 - r >= 8) { tma_load_2d_u32(dst + r * 128, &maps.m8, x, y0 + r, bar); r += 8; }
+                                }
                             }
                         }
                         __syncwarp();
@@ -358,7 +367,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
                     const uint64_t dq1 = dq0 + (uint64_t)((qr.i * QSLOT_BYTES) >> 4);
                     const uint64_t dq2 = dq1 + (uint64_t)(QB1_BYTES >> 4);
-                    for (int b = 0; b < pb; ++b) {
+                    for (int b = 0; b < pb; b += SBLK) {
                         bool w = mbar_wait(&xfull[xr.i], xr.ph, err);
                         if (w) w = mbar_wait(&lofull[lr.i], lr.ph, err);
                         if (!__all_sync(0xffffffffu, w)) {
@@ -366,16 +375,21 @@ __global__ void __launch_bounds__(NTHR, 1)
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t d = tmem + (uint32_t)(h * HALF_COLS + b * 2 * g.nqp);
-                        const uint64_t dx = dx0 + (uint64_t)((xr.i * X_BYTES) >> 4);
-                        const uint64_t dl = dl0 + (uint64_t)((lr.i * LO_BYTES) >> 4);
+                        const int nblk = min(SBLK, pb - b);
                         if (leader) {
+                            for (int j = 0; j < nblk; ++j) {
+                                const uint32_t d =
+                                    tmem + (uint32_t)(h * HALF_COLS + (b + j) * 2 * g.nqp);
+                                const uint64_t dx =
+                                    dx0 + (uint64_t)((xr.i * X_BYTES + j * BLK_BYTES) >> 4);
+                                const uint64_t dl = dl0 + (uint64_t)((lr.i * LO_BYTES + j * 64) >> 4);
 #pragma unroll
-                            for (int k = 0; k < 4; ++k)  // K = 8 tf32 = 32 B per step
-                                tc_mma_tf32(d, dx + 2 * k, dq1 + 2 * k, id_tf32, (c | k) != 0);
+                                for (int k = 0; k < 4; ++k)  // K = 8 tf32 = 32 B per step
+                                    tc_mma_tf32(d, dx + 2 * k, dq1 + 2 * k, id_tf32, (c | k) != 0);
 #pragma unroll
-                            for (int k = 0; k < 2; ++k)  // K = 16 bf16 = 32 B per step
-                                tc_mma_f16(d, dl + 2 * k, dq2 + 2 * k, id_bf16, true);
+                                for (int k = 0; k < 2; ++k)  // K = 16 bf16 = 32 B per step
+                                    tc_mma_f16(d, dl + 2 * k, dq2 + 2 * k, id_bf16, true);
+                            }
                             tc_commit(&xempty[xr.i]);
                             tc_commit(&loempty[lr.i]);
                         }
@@ -406,7 +420,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     } else if (warp < W_EPI0) {
         // ------------------------------ split warps ------------------------------
         const int s = threadIdx.x - W_SPLIT0 * 32;  // 0..255
-        const int r = s & (TROWS - 1), hh = s >> 7;  // stage row, half (16 dims)
+        const int blk = s >> 7, r = s & (TROWS - 1);  // block of the stage, row in the block
         const int qn = s >> 3, qj = s & 7;           // query row, 16-byte column
         Ring xr, lr, qr;
         for (int it = 0;; ++it) {
@@ -458,35 +472,36 @@ __global__ void __launch_bounds__(NTHR, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&qfull[qr.i]);
                     qr.next(NQS);
-                    for (int b = 0; b < pb; ++b) {
+                    for (int b = 0; b < pb; b += SBLK) {
                         bool w = mbar_wait(&xfull[xr.i], xr.ph, err);
                         if (w && lr.n >= (uint32_t)NLO) w = mbar_wait(&loempty[lr.i], lr.ph ^ 1u, err);
                         if (!__all_sync(0xffffffffu, w)) {
                             ok = false;
                             break;
                         }
-                        const uint32_t xb = x_u32 + (uint32_t)xr.i * X_BYTES + r * 128;
-                        const uint32_t sw = (uint32_t)(r & 7);
-                        float v[16];
+                        if (b + blk < pb) {  // warp-uniform: a warp's rows share a block
+                            // row s of the stage (row r of block blk): 32 dims in two halves;
+                            // x_lo of dims 8jj.. to 16-byte column 4 blk + jj of row r of the
+                            // correction tile (swizzled by r & 7; eight consecutive rows per
+                            // load / store phase hit distinct bank groups)
+                            const uint32_t xb = x_u32 + (uint32_t)xr.i * X_BYTES + s * 128;
+                            const uint32_t lb = lo_u32 + (uint32_t)lr.i * LO_BYTES + r * 128;
+                            const uint32_t sw = (uint32_t)(r & 7);
 #pragma unroll
-                        for (int jj = 0; jj < 4; ++jj) {
-                            const float4 t = lds128f(xb + ((((uint32_t)(hh * 4 + jj)) ^ sw) << 4));
-                            v[4 * jj] = t.x;
-                            v[4 * jj + 1] = t.y;
-                            v[4 * jj + 2] = t.z;
-                            v[4 * jj + 3] = t.w;
+                            for (int hf = 0; hf < 2; ++hf) {
+                                uint32_t lo[8];
+#pragma unroll
+                                for (int q4 = 0; q4 < 4; ++q4) {
+                                    const float4 t =
+                                        lds128f(xb + ((((uint32_t)(hf * 4 + q4)) ^ sw) << 4));
+                                    lo[2 * q4] = bf16x2(t.x - tf32_rz(t.x), t.y - tf32_rz(t.y));
+                                    lo[2 * q4 + 1] = bf16x2(t.z - tf32_rz(t.z), t.w - tf32_rz(t.w));
+                                }
+                                const uint32_t c0 = (uint32_t)(blk * 4 + hf * 2);
+                                sts128(lb + ((c0 ^ sw) << 4), lo[0], lo[1], lo[2], lo[3]);
+                                sts128(lb + (((c0 + 1) ^ sw) << 4), lo[4], lo[5], lo[6], lo[7]);
+                            }
                         }
-                        uint32_t lo[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            lo[e] = bf16x2(v[2 * e] - tf32_rz(v[2 * e]),
-                                           v[2 * e + 1] - tf32_rz(v[2 * e + 1]));
-                        // row r: bf16(x_lo) of dims 16hh.. at 16-byte columns 2hh,
-                        // 2hh+1 (swizzled by r & 7; eight consecutive rows per store
-                        // phase hit distinct bank groups)
-                        const uint32_t lb = lo_u32 + (uint32_t)lr.i * LO_BYTES + r * 128;
-                        sts128(lb + (((uint32_t)(2 * hh) ^ sw) << 4), lo[0], lo[1], lo[2], lo[3]);
-                        sts128(lb + (((uint32_t)(2 * hh + 1) ^ sw) << 4), lo[4], lo[5], lo[6], lo[7]);
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&lofull[lr.i]);
