@@ -20,14 +20,16 @@
 // sequential fp32 sum by rounding only, as the SIMT scan's do.
 //
 // CTA (one per SM, 14 warps):
-//   warp 0        producer: takes items from a global counter and streams the
-//                 list's rows by TMA (boxes of 32 dims x 128/64/32/16/8 rows,
+//   warp 0        producer: streams each queued item's rows by TMA (boxes of 32 dims x 128/64/32/16/8 rows,
 //                 SWIZZLE_128B, no multicast) through a ring of fp32 stages.
 //   warp 1        MMA warp: keeps the loop state warp-uniform, one elected lane
 //                 issues the MMAs and commits; it owns the TMEM allocation.
 //   warps 2..9    split warps: per chunk, the query operand tiles (fp32
 //                 [q | q_lo], bf16 q); per stage, the bf16 x_lo tile.
 //   warps 10..13  epilogue: TMEM -> scores -> a register top-k per query.
+//   warp 14       scheduler: takes items from the global counter and queues
+//                 their descriptors (list, rows, queries) up to NINFO ahead, so
+//                 no role waits on that chain of global loads between items.
 // Work order inside an item: passes of up to 256 / (2 nq_pad) row blocks of 128
 // rows; inside a pass, chunk-outer, block-inner (a 32 KB stage carries the
 // chunk of two consecutive blocks, which halves the per-stage handshakes), each
@@ -63,7 +65,9 @@ constexpr int NQS = 2;                        // query chunk slots
 constexpr int NSPLIT = 8;
 constexpr int NEPI = 4;
 constexpr int W_PROD = 0, W_MMA = 1, W_SPLIT0 = 2, W_EPI0 = W_SPLIT0 + NSPLIT;
-constexpr int NWARPS = W_EPI0 + NEPI;
+constexpr int W_SCHED = W_EPI0 + NEPI;        // item scheduler warp
+constexpr int NWARPS = W_SCHED + 1;
+constexpr int NINFO = 4;                      // work items queued ahead of the roles
 constexpr int NTHR = NWARPS * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int HALF_COLS = 256;
@@ -87,8 +91,8 @@ struct LayoutTC {
     uint32_t x_off, lo_off, q_off, sc_off, kb_off, info_off, bar_off, total;
 };
 
-__host__ __device__ inline LayoutTC make_layout_tc() {
-    LayoutTC L;
+__host__ __device__ constexpr LayoutTC make_layout_tc() {
+    LayoutTC L{};
     uint32_t o = 0;
     L.x_off = o;
     o += NXS * X_BYTES;
@@ -101,13 +105,15 @@ __host__ __device__ inline LayoutTC make_layout_tc() {
     L.kb_off = o;
     o += QMAX * 32 * 8;
     L.info_off = o;
-    o += 2 * (uint32_t)sizeof(ItemTC);
+    o += NINFO * (uint32_t)sizeof(ItemTC);
     o = (o + 15u) & ~15u;
     L.bar_off = o;
     o += 64 * 8;
     L.total = o + 1024;  // slack for aligning the base to 1024 bytes
     return L;
 }
+
+static_assert(make_layout_tc().total <= 227u * 1024u, "shared memory layout too large");
 
 // Ring position: index and phase parity, advanced one use at a time.
 struct Ring {
@@ -176,9 +182,9 @@ __global__ void __launch_bounds__(NTHR, 1)
     uint64_t* loempty = lofull + NLO;     // NLO
     uint64_t* qfull = loempty + NLO;      // NQS
     uint64_t* qempty = qfull + NQS;       // NQS
-    uint64_t* infofull = qempty + NQS;    // 2
-    uint64_t* infoempty = infofull + 2;   // 2
-    uint64_t* accfull = infoempty + 2;    // 2
+    uint64_t* infofull = qempty + NQS;    // NINFO
+    uint64_t* infoempty = infofull + NINFO;  // NINFO
+    uint64_t* accfull = infoempty + NINFO;   // 2
     uint64_t* accempty = accfull + 2;     // 2
     uint64_t* drain = accempty + 2;       // 1
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -206,9 +212,11 @@ __global__ void __launch_bounds__(NTHR, 1)
             mbar_init(&qfull[s], NSPLIT);
             mbar_init(&qempty[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < NINFO; ++s) {
             mbar_init(&infofull[s], 1);
-            mbar_init(&infoempty[s], NSPLIT + 1 + NEPI);
+            mbar_init(&infoempty[s], 1 + NSPLIT + 1 + NEPI);  // producer, split, MMA, epilogue
+        }
+        for (int s = 0; s < 2; ++s) {
             mbar_init(&accfull[s], 1);
             mbar_init(&accempty[s], NEPI);
         }
@@ -233,54 +241,16 @@ __global__ void __launch_bounds__(NTHR, 1)
         // The whole warp walks the schedule with warp-uniform values (so the
         // copy operands stay in uniform registers); the elected lane issues.
         const bool leader = elect_one();
-        const int nitems = *a.n_items;
         const uint32_t xbase = smem_u32(smem + L.x_off);
         Ring xr;
         bool ok = true;
         for (int it = 0; ok; ++it) {
-            const int slot = it & 1;
-            if (it >= 2 &&
-                !__all_sync(0xffffffffu, mbar_wait(&infoempty[slot], ((it >> 1) - 1) & 1, err)))
-                break;
-            ItemTC* inf = &info[slot];
-            int item = 0;
-            if (leader) item = atomicAdd(a.item_counter, 1);
-            item = __shfl_sync(0xffffffffu, item, __ffs(__ballot_sync(0xffffffffu, leader)) - 1);
-            if (item >= nitems) {
-                if (leader) {
-                    inf->list = -1;
-                    mbar_arrive(&infofull[slot]);
-                }
-                break;
-            }
-            const ScanItem wi = a.items[item];
-            const int np = wi.npairs;
-            int nrows = 0;
-            int64_t off = 0;
-            if (wi.list >= 0) {
-                nrows = a.list_len[wi.list];
-                off = a.list_off[wi.list];
-            }
-            if (np < 1 || np > QMAX || nrows < 0) {
-                if (leader) {
-                    atomicCAS(err, 0, (int)kErrBadItem);
-                    inf->list = -1;
-                    mbar_arrive(&infofull[slot]);
-                }
-                break;
-            }
-            if (lane < np) {
-                inf->q[lane] = a.pair_q[wi.pair_begin + lane];
-                inf->slot[lane] = a.pair_slot[wi.pair_begin + lane];
-            }
-            if (leader) {
-                inf->list = wi.list;
-                inf->np = np;
-                inf->nrows = nrows;
-                inf->off = off;
-            }
-            __syncwarp();
-            if (leader) mbar_arrive(&infofull[slot]);
+            const int slot = it % NINFO;
+            if (!__all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it / NINFO) & 1, err))) break;
+            const ItemTC* inf = &info[slot];
+            if (inf->list < 0) break;
+            const int np = inf->np, nrows = inf->nrows;
+            const int64_t off = inf->off;
             const int nb = (nrows + TROWS - 1) / TROWS;
             const int bpp = HALF_COLS / (2 * (np <= 16 ? 16 : 32));
             for (int p0 = 0; p0 < nb && ok; p0 += bpp) {
@@ -324,6 +294,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
                 }
             }
+            if (ok && leader) mbar_arrive(&infoempty[slot]);
+            __syncwarp();
         }
         // no copy may still be landing when the CTA leaves
         if (leader) {
@@ -344,8 +316,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         uint32_t pseq = 0;
         bool ok = true;
         for (int it = 0; ok; ++it) {
-            const int slot = it & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it >> 1) & 1, err))) break;
+            const int slot = it % NINFO;
+            if (!__all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it / NINFO) & 1, err))) break;
             const ItemTC* inf = &info[slot];
             if (inf->list < 0) break;
             const Geo g(*inf);
@@ -424,8 +396,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         const int qn = s >> 3, qj = s & 7;           // query row, 16-byte column
         Ring xr, lr, qr;
         for (int it = 0;; ++it) {
-            const int slot = it & 1;
-            const bool got = __all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it >> 1) & 1, err));
+            const int slot = it % NINFO;
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it / NINFO) & 1, err));
             if (!got) break;
             const ItemTC* inf = &info[slot];
             if (inf->list < 0) break;
@@ -514,6 +486,56 @@ __global__ void __launch_bounds__(NTHR, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&infoempty[slot]);
         }
+    } else if (warp == W_SCHED) {
+        // ------------------------------ scheduler ------------------------------
+        const bool leader = elect_one();
+        const int nitems = *a.n_items;
+        for (int it = 0;; ++it) {
+            const int slot = it % NINFO;
+            if (it >= NINFO &&
+                !__all_sync(0xffffffffu,
+                            mbar_wait(&infoempty[slot], ((it / NINFO) - 1) & 1, err)))
+                break;
+            ItemTC* inf = &info[slot];
+            int item = 0;
+            if (leader) item = atomicAdd(a.item_counter, 1);
+            item = __shfl_sync(0xffffffffu, item, __ffs(__ballot_sync(0xffffffffu, leader)) - 1);
+            if (item >= nitems) {
+                if (leader) {
+                    inf->list = -1;
+                    mbar_arrive(&infofull[slot]);
+                }
+                break;
+            }
+            const ScanItem wi = a.items[item];
+            const int np = wi.npairs;
+            int nrows = 0;
+            int64_t off = 0;
+            if (wi.list >= 0) {
+                nrows = a.list_len[wi.list];
+                off = a.list_off[wi.list];
+            }
+            if (np < 1 || np > QMAX || nrows < 0) {
+                if (leader) {
+                    atomicCAS(err, 0, (int)kErrBadItem);
+                    inf->list = -1;
+                    mbar_arrive(&infofull[slot]);
+                }
+                break;
+            }
+            if (lane < np) {
+                inf->q[lane] = a.pair_q[wi.pair_begin + lane];
+                inf->slot[lane] = a.pair_slot[wi.pair_begin + lane];
+            }
+            if (leader) {
+                inf->list = wi.list;
+                inf->np = np;
+                inf->nrows = nrows;
+                inf->off = off;
+            }
+            __syncwarp();
+            if (leader) mbar_arrive(&infofull[slot]);
+        }
     } else {
         // ------------------------------ epilogue ------------------------------
         const int ew = warp - W_EPI0;         // query group: queries ew, ew+4, ...
@@ -522,8 +544,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         const float INF = __int_as_float(0x7f800000);
         uint32_t pseq = 0;
         for (int it = 0;; ++it) {
-            const int slot = it & 1;
-            const bool got = __all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it >> 1) & 1, err));
+            const int slot = it % NINFO;
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it / NINFO) & 1, err));
             if (!got) break;
             const ItemTC* inf = &info[slot];
             if (inf->list < 0) break;
