@@ -224,6 +224,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         fence_mbar_init();
     }
     if (warp == W_PROD && lane == 0) {
+        prefetch_tensormap(&maps.m256);
         prefetch_tensormap(&maps.m128);
         prefetch_tensormap(&maps.m64);
         prefetch_tensormap(&maps.m32);
@@ -264,14 +265,22 @@ __global__ void __launch_bounds__(NTHR, 1)
                             break;
                         }
                         const int nblk = min(SBLK, pb - b);
-                        // each block's rows as boxes of 128 / 64 / 32 / 16 / 8 rows (rows
-                        // past the list's end, up to the next multiple of 8, are read and
-                        // masked later); block j of the stage at byte 16 KB * j
+                        // two full blocks as one 256-row box; otherwise each block's rows as
+                        // boxes of 128 / 64 / 32 / 16 / 8 rows (rows past the list's end, up
+                        // to the next multiple of 8, are read and masked later); block j of
+                        // the stage at byte 16 KB * j
                         int bytes = 0;
                         for (int j = 0; j < nblk; ++j)
                             bytes += ((min(TROWS, nrows - (p0 + b + j) * TROWS) + 7) & ~7) * 128;
                         uint64_t* bar = &xfull[xr.i];
-                        if (leader) {
+                        const uint32_t dst0 = xbase + (uint32_t)xr.i * X_BYTES;
+                        if (bytes == X_BYTES) {  // two full blocks: one 256-row box
+                            if (leader) {
+                                mbar_arrive_expect_tx(bar, (uint32_t)bytes);
+                                tma_load_2d_u32(dst0, &maps.m256, x, (int)(off + (p0 + b) * TROWS),
+                                                bar);
+                            }
+                        } else if (leader) {
                             mbar_arrive_expect_tx(bar, (uint32_t)bytes);
                             for (int j = 0; j < nblk; ++j) {
                                 const int row0 = (p0 + b + j) * TROWS;

@@ -47,11 +47,11 @@ struct ScanItem {
     int32_t pad;
 };
 
-// Row boxes of the list arena for the scan: four 2-D tensor maps over the
-// arena viewed as [rows, dpad] fp32, box width 32 floats (128 B, SWIZZLE_128B)
-// and heights 128 / 64 / 32 / 16 / 8 rows.
+// Row boxes of the list arena for the scans: 2-D tensor maps over the arena
+// viewed as [rows, dpad] fp32, box width 32 floats (128 B, SWIZZLE_128B) and
+// heights 256 / 128 / 64 / 32 / 16 / 8 rows.
 struct RowMaps {
-    CUtensorMap m128, m64, m32, m16, m8;
+    CUtensorMap m256, m128, m64, m32, m16, m8;
 };
 
 struct ScanArgs {
