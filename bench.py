@@ -346,7 +346,12 @@ def run_ours(args, rank, world, local_rank):
         f"after {time.perf_counter() - t_setup:.1f}s")
 
     Qd = torch.from_numpy(Qb).to(dev)  # [NBATCH, BATCH, DIM]
-    sharded = ShardedSearch(eng, 1, K, BATCH, world, dev)
+    coarse = {}
+    if world > 1 and args.coarse == "sharded":
+        # each rank scores only the centroids of the lists it owns
+        eng.create_ivf(2, DIM, METRIC_IP, False, C[np.flatnonzero(owner == rank)])
+        coarse = dict(coarse_index_id=2, owner=owner, rank=rank)
+    sharded = ShardedSearch(eng, 1, K, BATCH, world, dev, **coarse)
 
     def step(b, nprobe):
         ids, sc, _ = sharded.search(Qd[b], nprobe)
@@ -459,8 +464,11 @@ def run_ours(args, rank, world, local_rank):
 
     if rank != 0:
         return
+    # our kernels per step: norms, split, coarse GEMM, select, 3 work-list, scan, merge;
+    # N > 1 adds the shard merge, and with the sharded coarse step the pair scores,
+    # the top-P merge, the second row-norm pass and the partial-list clear
     per_step_launches = (launches / args.steps) if launches else (
-        9 if world == 1 else 10)
+        9 if world == 1 else (10 if args.coarse == "replicated" else 14))
     peak, peak_kind = peaks()
     roofline = None
     if scan_ms:
@@ -495,14 +503,19 @@ def run_ours(args, rank, world, local_rank):
                    "stage_ms_mean": {k[3:]: round(statistics.mean(v), 4)
                                      for k, v in stage_ms.items()},
                    "l2_flush": "not needed: each step streams ~4 GB of lists (> 126 MB L2)",
-                   "parallelism": f"lists sharded over {world} GPU(s)" if world > 1 else "1 GPU"},
+                   "parallelism": (f"lists sharded over {world} GPU(s), {args.coarse} coarse "
+                                   "selection") if world > 1 else "1 GPU"},
         "gpu_launches": int(round(per_step_launches * args.steps)),
         "clocks": clocks,
         "e2e": {"value": e2e_qps, "unit": "queries/s",
                 "h2d_bytes_per_step": BATCH * DIM * 4,
                 "d2h_bytes_per_step": BATCH * K * 12 + BATCH * 4,
                 "path": "m3g_search (C ABI, pinned host buffers)" if world == 1
-                else "H2D + m3g_search_device + NCCL all-gather + m3g_merge_shards_device + D2H"},
+                else ("H2D + m3g_search_device + NCCL all-gather + m3g_merge_shards_device + D2H"
+                      if args.coarse == "replicated" else
+                      "H2D + m3g_select_probes_device + m3g_probe_scores_device (own centroids) + "
+                      "NCCL all-gather + m3g_merge_shards_device (top-P) + "
+                      "m3g_search_probes_device + NCCL all-gather + m3g_merge_shards_device + D2H")},
         "roofline": roofline,
         "cpu_baseline": cpu,
     }
@@ -516,6 +529,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--coarse", choices=["sharded", "replicated"], default="replicated",
+                    help="N > 1: coarse selection per rank over its own centroids (sharded) or "
+                         "over all centroids on every rank (replicated)")
     ap.add_argument("--nvec", type=int, default=None,
                     help="profiling only: fewer vectors (the headline line uses 1M)")
     ap.add_argument("--nlist", type=int, default=None, help="profiling only: fewer lists")

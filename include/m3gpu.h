@@ -185,6 +185,30 @@ int m3g_merge_shards_device(m3g_engine* e, const float* d_scores, const int64_t*
                             int nshard, int64_t nq, int k, int64_t* d_out_ids,
                             float* d_out_scores, int32_t* d_out_counts, void* stream);
 
+/* The pieces of a list-sharded search whose coarse step is sharded as well
+ * (each GPU scores only the centroids of the lists it owns).  No single
+ * counterpart in the reference: together they restate the coarse selection of
+ * IVFIndex::search_nprobe (select_nprobe_for_query, m3_index.cpp:492-523) and
+ * its list scan (:390-441) across GPUs.  Device pointers; enqueued on `stream`
+ * (NULL: the engine's own stream, waited for).
+ *
+ * m3g_select_probes_device: m3g_select_probes on device queries [nq, dim],
+ * writing [nq, min(nprobe, nlist)] cluster ids ascending by exact score.
+ * m3g_probe_scores_device: the exact unified score (unified_score,
+ * base.h:22-31, in the reference's fp32 arithmetic) of each pair
+ * (query q, centroid d_probes[q, j]), [nq, nprobe]; +inf for ids out of range.
+ * m3g_search_probes_device: search_nprobe's scan and merge over the given
+ * probes [nq, nprobe] (slot j of query q scans list d_probes[q, j]; -1 skips
+ * the slot); outputs as m3g_search_device. */
+int m3g_select_probes_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
+                             int nprobe, int32_t* d_out_probes, void* stream);
+int m3g_probe_scores_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
+                            const int32_t* d_probes, int nprobe, float* d_out_scores,
+                            void* stream);
+int m3g_search_probes_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
+                             int k, const int32_t* d_probes, int nprobe, int64_t* d_out_ids,
+                             float* d_out_scores, int32_t* d_out_counts, void* stream);
+
 /* The top-nprobe selection of m3g_select_probes for callers that cannot
  * allocate GPU memory (a fixed pre-reserved memory pool, a runtime that forbids
  * allocation after start-up, or code that must not trigger the device

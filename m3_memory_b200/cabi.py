@@ -70,6 +70,10 @@ SIGNATURES = {
                              _vp]),
     "m3g_split_cluster": (_i32, [_vp, _i32, _i32, _i32, _u64, _pi32]),
     "m3g_merge_shards_device": (_i32, [_vp, _vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp]),
+    "m3g_select_probes_device": (_i32, [_vp, _i32, _vp, _i64, _i32, _vp, _vp]),
+    "m3g_probe_scores_device": (_i32, [_vp, _i32, _vp, _i64, _vp, _i32, _vp, _vp]),
+    "m3g_search_probes_device": (_i32, [_vp, _i32, _vp, _i64, _i32, _vp, _i32, _vp, _vp, _vp,
+                                        _vp]),
     "m3g_select_probes_noalloc": (_i32, [_vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp,
                                          _vp]),
     "m3g_set_profiling": (_i32, [_vp, _i32]),
@@ -319,6 +323,24 @@ class Engine:
                                             ct.c_void_p(out_scores_ptr),
                                             ct.c_void_p(out_counts_ptr),
                                             ct.c_void_p(stream) if stream else None))
+
+    def select_probes_device(self, index_id, q_ptr, nq, nprobe, out_ptr, stream=None):
+        check(lib().m3g_select_probes_device(self.h, index_id, ct.c_void_p(q_ptr), nq, nprobe,
+                                             ct.c_void_p(out_ptr),
+                                             ct.c_void_p(stream) if stream else None))
+
+    def probe_scores_device(self, index_id, q_ptr, nq, probes_ptr, nprobe, out_ptr,
+                            stream=None):
+        check(lib().m3g_probe_scores_device(self.h, index_id, ct.c_void_p(q_ptr), nq,
+                                            ct.c_void_p(probes_ptr), nprobe, ct.c_void_p(out_ptr),
+                                            ct.c_void_p(stream) if stream else None))
+
+    def search_probes_device(self, index_id, q_ptr, nq, k, probes_ptr, nprobe, ids_ptr,
+                             scores_ptr, counts_ptr, stream=None):
+        check(lib().m3g_search_probes_device(self.h, index_id, ct.c_void_p(q_ptr), nq, k,
+                                             ct.c_void_p(probes_ptr), nprobe, ct.c_void_p(ids_ptr),
+                                             ct.c_void_p(scores_ptr), ct.c_void_p(counts_ptr),
+                                             ct.c_void_p(stream) if stream else None))
 
     def sync_errors(self):
         check(lib().m3g_sync_errors(self.h))

@@ -316,6 +316,38 @@ int m3g_merge_shards_device(m3g_engine* e, const float* d_scores, const int64_t*
     });
 }
 
+int m3g_select_probes_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
+                             int nprobe, int32_t* d_out_probes, void* stream) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (nq < 0) m3g::fail(M3G_EINVAL, "select_probes_device: nq < 0");
+        e->eng.select_probes_device(index_id, d_queries, nq, nprobe, d_out_probes,
+                                    static_cast<cudaStream_t>(stream));
+    });
+}
+
+int m3g_probe_scores_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
+                            const int32_t* d_probes, int nprobe, float* d_out_scores,
+                            void* stream) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (nq < 0 || nprobe < 0) m3g::fail(M3G_EINVAL, "probe_scores_device: bad sizes");
+        e->eng.probe_scores_device(index_id, d_queries, nq, d_probes, nprobe, d_out_scores,
+                                   static_cast<cudaStream_t>(stream));
+    });
+}
+
+int m3g_search_probes_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
+                             int k, const int32_t* d_probes, int nprobe, int64_t* d_out_ids,
+                             float* d_out_scores, int32_t* d_out_counts, void* stream) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (nq < 0) m3g::fail(M3G_EINVAL, "search_probes_device: nq < 0");
+        e->eng.search_probes_device(index_id, d_queries, nq, k, d_probes, nprobe, d_out_ids,
+                                    d_out_scores, d_out_counts, static_cast<cudaStream_t>(stream));
+    });
+}
+
 int m3g_select_probes_noalloc(const float* d_queries, int64_t nq, const float* d_centroids,
                               int64_t nlist, int dim, int metric, int normalized, int nprobe,
                               int32_t* d_out_probes, void* stream) {

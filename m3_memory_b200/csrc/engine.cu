@@ -909,7 +909,7 @@ float gamma_of(int D) { return (float)(D + 4) * 5.9604645e-8f * 1.01f; }
 // the device (skips the coarse step).  Outputs [nq, k] / [nq] on the device.
 void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int k, int P,
                         const int32_t* fixed_probes, int64_t* d_ids, float* d_scores,
-                        int32_t* d_counts, cudaStream_t st, bool profile) {
+                        int32_t* d_counts, cudaStream_t st, bool profile, bool clear_partials) {
     Workspace& w = ws_;
     const int L = ix.nlist();
     const int D = ix.dim;
@@ -950,6 +950,9 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
         M3G_CK(cudaEventRecord(ev[4], st));
     }
     M3G_CK(cudaMemsetAsync(w.item_counter.p, 0, sizeof(int32_t), st));
+    // probe slots the work list skips (probe -1) keep empty partial lists
+    if (clear_partials)
+        M3G_CK(launch_clear_partials(w.part_score.p, w.part_row.p, nq * P * k, st));
     ScanArgs a{};
     a.Q = dQ;
     a.dpad = (int)ldq;
@@ -1295,6 +1298,103 @@ void Engine::select_probes(int index_id, const float* Q, int64_t nq, int nprobe,
     }
     M3G_CK(cudaEventRecord(ws_.done, st));
     M3G_CK(cudaStreamSynchronize(st));
+}
+
+const float* Engine::stage_queries(const Index& ix, const float* dQ, int64_t m, cudaStream_t st) {
+    if (ix.dpad == ix.dim && (reinterpret_cast<uintptr_t>(dQ) & 15u) == 0) return dQ;
+    if (ix.dpad != ix.dim) M3G_CK(cudaMemsetAsync(ws_.Q.p, 0, (size_t)(m * ix.dpad) * 4, st));
+    M3G_CK(cudaMemcpy2DAsync(ws_.Q.p, (size_t)ix.dpad * 4, dQ, (size_t)ix.dim * 4,
+                             (size_t)ix.dim * 4, (size_t)m, cudaMemcpyDeviceToDevice, st));
+    return ws_.Q.p;
+}
+
+void Engine::select_probes_device(int index_id, const float* dQ, int64_t nq, int nprobe,
+                                  int32_t* d_out, cudaStream_t ext) {
+    auto ix = get(index_id, "select_probes_device");
+    DeviceGuard g(device_);
+    std::shared_lock lk(ix->mu);
+    const int L = ix->nlist();
+    if (nq <= 0 || L == 0 || nprobe == 0) return;
+    if (!dQ || !d_out) fail(M3G_EINVAL, "select_probes_device: buffers missing");
+    const int P = nprobe < 0 ? L : std::min(nprobe, L);
+    const int64_t ch = chunk_queries(nq, L, P, 1);
+    std::lock_guard wl(ws_.mu);
+    acquire_ws(ext, ch, L, P, 1, ix->dpad);
+    cudaStream_t st = ext ? ext : ws_.stream;
+    for (int64_t q0 = 0; q0 < nq; q0 += ch) {
+        const int64_t m = std::min(ch, nq - q0);
+        const float* q = stage_queries(*ix, dQ + q0 * ix->dim, m, st);
+        int32_t* out = d_out + q0 * P;
+        launch_row_norms(q, ix->dpad, m, ix->dim, ws_.qn.p, ws_.qn2.p, st);
+        if (P >= L) {
+            M3G_CK(launch_iota_rows(out, m, P, st));
+        } else {
+            if (use_tc_gemm())
+                M3G_CK(launch_split3(q, ix->dpad, m, ix->dpad, gemm_tc_kdim(ix->dpad), ws_.Q3.p,
+                                     false, st));
+            const float beta = coarse_gemm(q, ix->dpad, ws_.Q3.p, ix->C.p, ix->dpad, ix->C3.p,
+                                           ws_.S.p, L, (int)m, L, ix->dpad, ws_.err.p, st);
+            M3G_CK(launch_select_probes(ws_.S.p, L, q, ix->dpad, ix->C.p, ix->dpad, ws_.qn.p,
+                                        ws_.qn2.p, ix->cn.p, ix->cn2.p, (int)m, L, ix->dim,
+                                        ix->metric, ix->normalized ? 1 : 0, beta,
+                                        gamma_of(ix->dim), P, 0, out, st));
+        }
+    }
+    M3G_CK(cudaEventRecord(ws_.done, st));
+    if (!ext) M3G_CK(cudaStreamSynchronize(st));
+}
+
+void Engine::probe_scores_device(int index_id, const float* dQ, int64_t nq,
+                                 const int32_t* d_probes, int P, float* d_scores,
+                                 cudaStream_t ext) {
+    auto ix = get(index_id, "probe_scores_device");
+    DeviceGuard g(device_);
+    std::shared_lock lk(ix->mu);
+    if (nq <= 0 || P <= 0) return;
+    if (!dQ || !d_probes || !d_scores) fail(M3G_EINVAL, "probe_scores_device: buffers missing");
+    if (ix->dim > select_max_dim()) fail(M3G_EUNSUPPORTED, "probe_scores_device: dim too large");
+    const int L = ix->nlist();
+    const int64_t ch = chunk_queries(nq, std::max(L, 1), P, 1);
+    std::lock_guard wl(ws_.mu);
+    acquire_ws(ext, ch, std::max(L, 1), P, 1, ix->dpad);
+    cudaStream_t st = ext ? ext : ws_.stream;
+    for (int64_t q0 = 0; q0 < nq; q0 += ch) {
+        const int64_t m = std::min(ch, nq - q0);
+        const float* q = stage_queries(*ix, dQ + q0 * ix->dim, m, st);
+        M3G_CK(launch_probe_scores(q, ix->dpad, ix->C.p, ix->dpad, L, d_probes + q0 * P, m, P,
+                                   ix->dim, ix->metric, ix->normalized ? 1 : 0, d_scores + q0 * P,
+                                   st));
+    }
+    M3G_CK(cudaEventRecord(ws_.done, st));
+    if (!ext) M3G_CK(cudaStreamSynchronize(st));
+}
+
+void Engine::search_probes_device(int index_id, const float* dQ, int64_t nq, int k,
+                                  const int32_t* d_probes, int P, int64_t* d_ids, float* d_scores,
+                                  int32_t* d_counts, cudaStream_t ext) {
+    auto ix = get(index_id, "search_probes_device");
+    DeviceGuard g(device_);
+    if (nq <= 0) return;
+    if (k <= 0 || P <= 0) fail(M3G_EINVAL, "search_probes_device: k and P must be positive");
+    if (k > scan_kmax())
+        fail(M3G_EUNSUPPORTED,
+             "search_probes_device: k > " + std::to_string(scan_kmax()) + " is not supported");
+    if (!dQ || !d_probes || !d_ids || !d_scores || !d_counts)
+        fail(M3G_EINVAL, "search_probes_device: buffers missing");
+    std::shared_lock lk(ix->mu);
+    const int L = std::max(ix->nlist(), 1);
+    const int64_t ch = chunk_queries(nq, L, P, k);
+    std::lock_guard wl(ws_.mu);
+    acquire_ws(ext, ch, L, P, k, ix->dpad);
+    cudaStream_t st = ext ? ext : ws_.stream;
+    for (int64_t q0 = 0; q0 < nq; q0 += ch) {
+        const int64_t m = std::min(ch, nq - q0);
+        const float* q = stage_queries(*ix, dQ + q0 * ix->dim, m, st);
+        run_search(*ix, q, ix->dpad, m, k, P, d_probes + q0 * P, d_ids + q0 * k,
+                   d_scores + q0 * k, d_counts + q0, st, false, true);
+    }
+    M3G_CK(cudaEventRecord(ws_.done, st));
+    if (!ext) M3G_CK(cudaStreamSynchronize(st));
 }
 
 // Exact nearest-centroid assignment of n device rows (P = 1 selection).

@@ -191,6 +191,17 @@ class Engine {
     void search_on(int index_id, const int32_t* cids, int ncids, const float* Q, int64_t nq, int k,
                    int64_t* out_ids, float* out_scores, int32_t* out_counts);
     void select_probes(int index_id, const float* Q, int64_t nq, int nprobe, int32_t* out);
+    // Device-pointer pieces of a list-sharded search whose coarse step is sharded
+    // too: the selection over this index's centroids, the exact scores of given
+    // (query, centroid) pairs, and a search over caller-given probes (-1: none).
+    // Enqueued on ext_stream (null: the engine's stream, waited for).
+    void select_probes_device(int index_id, const float* dQ, int64_t nq, int nprobe,
+                              int32_t* d_out, cudaStream_t ext_stream);
+    void probe_scores_device(int index_id, const float* dQ, int64_t nq, const int32_t* d_probes,
+                             int P, float* d_scores, cudaStream_t ext_stream);
+    void search_probes_device(int index_id, const float* dQ, int64_t nq, int k,
+                              const int32_t* d_probes, int P, int64_t* d_ids, float* d_scores,
+                              int32_t* d_counts, cudaStream_t ext_stream);
     void nearest_clusters(int index_id, const float* vecs, int64_t n, int32_t* out);
     void sync_errors();
 
@@ -222,7 +233,11 @@ class Engine {
     // device helpers (callers hold the right index lock)
     void run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int k, int P,
                     const int32_t* fixed_probes, int64_t* d_ids, float* d_scores,
-                    int32_t* d_counts, cudaStream_t st, bool profile);
+                    int32_t* d_counts, cudaStream_t st, bool profile,
+                    bool clear_partials = false);
+    // Queries [m, dim] on the device as the index's padded rows: the pointer itself
+    // when it already is, else a copy into the workspace.
+    const float* stage_queries(const Index& ix, const float* dQ, int64_t m, cudaStream_t st);
     void assign_rows(Index& ix, const float* dX, int64_t ld, const float* xn, const float* xn2,
                      int64_t n, int32_t* d_out, cudaStream_t st);
     // Creates the workspace stream / events on first use; then orders `st` after

@@ -531,6 +531,59 @@ size_t select_smem_bytes(int L, int D) {
 
 int select_max_dim() { return 8192; }
 
+namespace {
+constexpr int PS_BLOCK = 256;
+
+// Exact unified scores of given (query, centroid) pairs, one block per query:
+// the pairs of a query are spread over the warps, ceil(n / 8) per warp, each
+// scored by warp_exact_scores (the reference's arithmetic and summation order).
+// probes[q * P + j] < 0 or >= L scores +inf.
+__global__ void __launch_bounds__(PS_BLOCK) probe_scores_kernel(
+    const float* __restrict__ Q, int64_t ldq, const float* __restrict__ C, int64_t ldc, int L,
+    const int32_t* __restrict__ probes, int P, int D, int metric, int normalized,
+    float* __restrict__ out) {
+    extern __shared__ __align__(16) unsigned char ps_smem[];
+    float* qs = reinterpret_cast<float*>(ps_smem);                       // round_up(D, 4) floats
+    float* stage_all = qs + ((D + 3) & ~3);                               // 8 tiles
+    const int q = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* qrow = Q + (int64_t)q * ldq;
+    for (int i = threadIdx.x; i < D; i += PS_BLOCK) qs[i] = qrow[i];
+    __syncthreads();
+    const bool nrm = normalized != 0;
+    float* stage = stage_all + warp * kExactTileFloats;
+    const int32_t* pr = probes + (int64_t)q * P;
+    float* o = out + (int64_t)q * P;
+    for (int r0 = 0; r0 < P; r0 += PS_BLOCK) {
+        const int n = P - r0 < PS_BLOCK ? P - r0 : PS_BLOCK;
+        const int G = (n + PS_BLOCK / 32 - 1) / (PS_BLOCK / 32);
+        if (warp * G >= n) continue;  // warp-uniform
+        const int i = warp * G + lane;
+        const bool mine = lane < G && i < n;
+        int c = mine ? pr[r0 + i] : -1;
+        if (c >= L) c = -1;
+        float r;
+        if (G <= 8) r = warp_exact_scores<4>(qs, C, ldc, D, metric, nrm, c, stage, lane);
+        else if (G <= 16) r = warp_exact_scores<2>(qs, C, ldc, D, metric, nrm, c, stage, lane);
+        else r = warp_exact_scores<1>(qs, C, ldc, D, metric, nrm, c, stage, lane);
+        if (mine) o[r0 + i] = c >= 0 ? r : __int_as_float(0x7f800000);
+    }
+}
+}  // namespace
+
+cudaError_t launch_probe_scores(const float* Q, int64_t ldq, const float* C, int64_t ldc, int L,
+                                const int32_t* probes, int64_t nq, int P, int D, int metric,
+                                int normalized, float* out, cudaStream_t st) {
+    if (nq <= 0 || P <= 0) return cudaSuccess;
+    const size_t smem = sizeof(float) * ((size_t)((D + 3) & ~3) +
+                                         (size_t)(PS_BLOCK / 32) * kExactTileFloats);
+    cudaError_t e = cudaFuncSetAttribute(probe_scores_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    probe_scores_kernel<<<(unsigned)nq, PS_BLOCK, smem, st>>>(Q, ldq, C, ldc, L, probes, P, D,
+                                                              metric, normalized, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t ldq, const float* C,
                                  int64_t ldc, const float* qn, const float* qn2, const float* cn,
                                  const float* cn2, int nq, int L, int D, int metric,

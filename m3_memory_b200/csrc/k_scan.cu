@@ -25,6 +25,8 @@
 // fp32 summation order.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "topk.cuh"
@@ -841,6 +843,23 @@ cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(part_score, part_row, row_ids, P, k,
                                                 (int64_t)P * k, k, out_ids, out_scores,
                                                 out_counts);
+    return cudaGetLastError();
+}
+
+namespace {
+__global__ void clear_partials_kernel(float* __restrict__ s, int64_t* __restrict__ r, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        s[i] = __int_as_float(0x7f800000);
+        r[i] = -1;
+    }
+}
+}  // namespace
+
+cudaError_t launch_clear_partials(float* part_score, int64_t* part_row, int64_t n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, 4096);
+    clear_partials_kernel<<<(unsigned)blocks, 256, 0, st>>>(part_score, part_row, n);
     return cudaGetLastError();
 }
 

@@ -99,6 +99,15 @@ cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
 
 // Merge of per-shard answers [nshard, nq, k] (scores ascending per row, ids,
 // -1 / +inf padding) into [nq, k]; ties broken by (shard, position).
+// Empty partial top-k lists (+inf, -1): for probe slots a search skips.
+cudaError_t launch_clear_partials(float* part_score, int64_t* part_row, int64_t n, cudaStream_t st);
+
+// Exact unified scores (the reference's arithmetic) of the pairs (q, probes[q, j]),
+// +inf where the probe is out of [0, L).
+cudaError_t launch_probe_scores(const float* Q, int64_t ldq, const float* C, int64_t ldc, int L,
+                                const int32_t* probes, int64_t nq, int P, int D, int metric,
+                                int normalized, float* out, cudaStream_t st);
+
 cudaError_t launch_merge_shards(const float* scores, const int64_t* ids, int nshard, int nq, int k,
                                 int64_t* out_ids, float* out_scores, int32_t* out_counts,
                                 cudaStream_t st);

@@ -11,6 +11,17 @@ is the final ascending sort of ``IVFIndex::search_nprobe``
 
 The exchange is the only collective on the path; its size is
 ``world * Q * k * 12`` bytes per batch.
+
+With ``coarse_index_id`` the coarse step is sharded too, so it shrinks with the
+number of GPUs instead of being repeated on each: every rank keeps a second
+index holding only the centroids of its own lists (ascending cluster id), takes
+their exact top-P (``m3g_select_probes_device``) with exact scores
+(``m3g_probe_scores_device``, the reference's arithmetic), the ``[Q, P]``
+candidates of all ranks are all-gathered and merged into the global top-P by
+(score, rank, position) -- the same P lists, in the same order, as the
+single-GPU selection except between centroids whose exact scores tie -- and each
+rank scans the winners it owns (``m3g_search_probes_device``, -1 for the
+others) before the top-k exchange above.
 """
 from __future__ import annotations
 
@@ -48,11 +59,34 @@ class ShardedSearch:
     """
 
     def __init__(self, engine, index_id: int, k: int, max_q: int, world: int, device,
-                 group=None):
+                 group=None, coarse_index_id=None, owner=None, rank: int = 0,
+                 max_nprobe: int = 256):
         import torch
 
         self.engine, self.index_id, self.k, self.world = engine, index_id, k, world
         self.group = group
+        self.coarse_index_id = coarse_index_id
+        if coarse_index_id is not None:
+            if owner is None:
+                raise ValueError("a sharded coarse step needs the list owners")
+            owner = np.asarray(owner, dtype=np.int32)
+            own = np.flatnonzero(owner == rank).astype(np.int64)
+            self.nlist = len(owner)
+            self.n_own = len(own)
+            self.own_ids = torch.from_numpy(own).to(device)          # local -> global id
+            self.owner = torch.from_numpy(owner).to(device)
+            self.rank = rank
+            p = min(max_nprobe, self.nlist)
+            self.loc = torch.empty((max_q, p), dtype=torch.int32, device=device)
+            self.loc_sc = torch.empty((max_q, p), dtype=torch.float32, device=device)
+            self.cand_sc = torch.empty((max_q, p), dtype=torch.float32, device=device)
+            self.cand_id = torch.empty((max_q, p), dtype=torch.int64, device=device)
+            self.gc_sc = torch.empty((world, max_q, p), dtype=torch.float32, device=device)
+            self.gc_id = torch.empty((world, max_q, p), dtype=torch.int64, device=device)
+            self.top_id = torch.empty((max_q, p), dtype=torch.int64, device=device)
+            self.top_sc = torch.empty((max_q, p), dtype=torch.float32, device=device)
+            self.top_cnt = torch.empty((max_q,), dtype=torch.int32, device=device)
+            self.max_nprobe = p
         self.ids = torch.empty((max_q, k), dtype=torch.int64, device=device)
         self.sc = torch.empty((max_q, k), dtype=torch.float32, device=device)
         self.cnt = torch.empty((max_q,), dtype=torch.int32, device=device)
@@ -76,8 +110,12 @@ class ShardedSearch:
             raise ValueError(f"batch of {nq} queries exceeds max_q={self.max_q}")
         k = self.k
         s = torch.cuda.current_stream(q.device).cuda_stream
-        self.engine.search_device(self.index_id, q.data_ptr(), nq, k, nprobe,
-                                  self.ids.data_ptr(), self.sc.data_ptr(), self.cnt.data_ptr(), s)
+        if self.coarse_index_id is not None:
+            self._search_sharded_coarse(q, nq, nprobe, s)
+        else:
+            self.engine.search_device(self.index_id, q.data_ptr(), nq, k, nprobe,
+                                      self.ids.data_ptr(), self.sc.data_ptr(),
+                                      self.cnt.data_ptr(), s)
         if self.world == 1:
             return self.ids[:nq], self.sc[:nq], self.cnt[:nq]
         # [world, nq, k] views over the start of the gather buffers (contiguous)
@@ -89,3 +127,44 @@ class ShardedSearch:
                                         self.out_ids.data_ptr(), self.out_sc.data_ptr(),
                                         self.out_cnt.data_ptr(), s)
         return self.out_ids[:nq], self.out_sc[:nq], self.out_cnt[:nq]
+
+    def _search_sharded_coarse(self, q, nq, nprobe, s):
+        """Global top-P from the ranks' exact local top-P, then the scan of the
+        winners this rank owns; leaves the rank's top-k in self.ids / sc / cnt."""
+        import torch
+        import torch.distributed as dist
+
+        P = min(nprobe if nprobe > 0 else self.nlist, self.nlist)
+        if P > self.max_nprobe:
+            raise ValueError(f"nprobe {P} exceeds max_nprobe={self.max_nprobe}")
+        pl = min(P, self.n_own)
+        cand_sc = self.cand_sc.view(-1)[:nq * P].view(nq, P)
+        cand_id = self.cand_id.view(-1)[:nq * P].view(nq, P)
+        cand_sc.fill_(float("inf"))
+        cand_id.fill_(-1)
+        if pl > 0:
+            loc = self.loc.view(-1)[:nq * pl].view(nq, pl)
+            loc_sc = self.loc_sc.view(-1)[:nq * pl].view(nq, pl)
+            self.engine.select_probes_device(self.coarse_index_id, q.data_ptr(), nq, pl,
+                                             loc.data_ptr(), s)
+            self.engine.probe_scores_device(self.coarse_index_id, q.data_ptr(), nq,
+                                            loc.data_ptr(), pl, loc_sc.data_ptr(), s)
+            cand_sc[:, :pl] = loc_sc
+            cand_id[:, :pl] = self.own_ids[loc.long()]
+        if self.world > 1:
+            g_sc = self.gc_sc.view(-1)[:self.world * nq * P].view(self.world, nq, P)
+            g_id = self.gc_id.view(-1)[:self.world * nq * P].view(self.world, nq, P)
+            dist.all_gather_into_tensor(g_sc, cand_sc, group=self.group)
+            dist.all_gather_into_tensor(g_id, cand_id, group=self.group)
+        else:
+            g_sc, g_id = cand_sc.unsqueeze(0), cand_id.unsqueeze(0)
+        top_id = self.top_id.view(-1)[:nq * P].view(nq, P)
+        top_sc = self.top_sc.view(-1)[:nq * P].view(nq, P)
+        self.engine.merge_shards_device(g_sc.data_ptr(), g_id.data_ptr(), self.world, nq, P,
+                                        top_id.data_ptr(), top_sc.data_ptr(),
+                                        self.top_cnt.data_ptr(), s)
+        mine = (top_id >= 0) & (self.owner[top_id.clamp(min=0)] == self.rank)
+        probes = torch.where(mine, top_id, torch.full_like(top_id, -1)).to(torch.int32)
+        self.engine.search_probes_device(self.index_id, q.data_ptr(), nq, self.k,
+                                         probes.data_ptr(), P, self.ids.data_ptr(),
+                                         self.sc.data_ptr(), self.cnt.data_ptr(), s)

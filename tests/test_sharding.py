@@ -141,3 +141,33 @@ def test_merge_shards_rule(oracle_mod):
     np.testing.assert_array_equal(got_ids, [[5, 7, 8]])  # tie 0.1: shard 0 first
     np.testing.assert_array_equal(got_sc, np.array([[0.1, 0.1, 0.2]], np.float32))
     np.testing.assert_array_equal(cnt, [3])
+
+
+def test_global_top_p_from_ranks_exact_local_top_p(oracle_mod):
+    """The sharded coarse step: every rank's exact top-P over its own centroids,
+    merged by (exact score, rank, position), gives the single-index selection
+    (all three metrics; the case has no exact score ties)."""
+    from m3_memory_b200.sharding import shard_lists
+
+    c = _case()
+    L = len(c["C"])
+    for world in (2, 3, 4):
+        owner = shard_lists(c["sizes"], world)
+        for metric, norm, P in ((1, False, 6), (0, False, 9), (2, False, 4)):
+            sc = np.full((world, len(c["Q"]), P), np.inf, np.float32)
+            ids = np.full((world, len(c["Q"]), P), -1, np.int64)
+            for r in range(world):
+                own = np.flatnonzero(owner == r)
+                if len(own) == 0:
+                    continue
+                pl = min(P, len(own))
+                for i, q in enumerate(c["Q"]):
+                    loc = oracle_mod.select_nprobe(q, c["C"][own], metric, norm, pl)
+                    sc[r, i, :pl] = [oracle_mod.score(q, c["C"][own[j]], metric, norm)
+                                     for j in loc]
+                    ids[r, i, :pl] = own[loc]
+            top, _, cnt = oracle_mod.merge_shards(sc, ids)
+            assert (cnt == min(P, L)).all()
+            for i, q in enumerate(c["Q"]):
+                want = oracle_mod.select_nprobe(q, c["C"], metric, norm, P)
+                np.testing.assert_array_equal(top[i], want)
