@@ -250,6 +250,21 @@ __device__ unsigned block_flag_scan(bool flag, unsigned* total, SelShared& sh) {
     return base + below;
 }
 
+// Bitonic sort of one key per lane, ascending across lanes.
+__device__ __forceinline__ uint32_t warp_sort_asc_u32(uint32_t v, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const uint32_t p = __shfl_xor_sync(0xffffffffu, v, j);
+            const bool up = (lane & k) == 0;
+            const bool lower = (lane & j) == 0;
+            v = (lower == up) ? (p < v ? p : v) : (p > v ? p : v);
+        }
+    }
+    return v;
+}
+
 __device__ void bitonic_sort_u64(unsigned long long* a, int n) {
     // n is a power of two
     for (int k = 2; k <= n; k <<= 1) {
@@ -310,33 +325,48 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     bool have = false;  // candidates in cand[0, cnt)
     unsigned cnt = 0;
     if (!exact_all && PP <= SEL_FAST_P) {
-        // --- pre-filtered threshold.  tau0, the PP-th smallest of the threads'
-        // smallest upper-bound keys, is >= T (the PP-th smallest of all: PP
-        // distinct keys are <= tau0).  Every centroid with hi <= T therefore has
-        // lo <= tau0, so T is the PP-th smallest upper bound within
-        // S0 = {c : lo <= tau0}, and every candidate (lo <= T) is in S0.
+        // --- pre-filtered threshold.  Each warp sorts its threads' smallest
+        // upper-bound keys and offers its ceil(PP/8)-th smallest; tau0, the largest
+        // offer, has at least 8 * ceil(PP/8) >= PP distinct keys <= it, so
+        // tau0 >= T (the PP-th smallest upper bound of all).  Every centroid with
+        // hi <= T therefore has lo <= tau0, so T is the PP-th smallest upper bound
+        // within S0 = {c : lo <= tau0}, and every candidate (lo <= T) is in S0.
+        // The lower-bound keys of the first pass are kept when they fit beside S0.
+        uint32_t* lkeys = hkeys;
+        const bool keep_lo = (size_t)L + 3 * SEL_CAP <= (size_t)(SEL_BLOCK / 32) * SEL_STAGE;
         uint32_t mymin = 0xffffffffu;
         for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
             float lo, hi;
             bounds(c, &lo, &hi);
             const uint32_t k = float_key(hi);
             mymin = k < mymin ? k : mymin;
+            if (keep_lo) lkeys[c] = lo != lo ? 0u : float_key(lo);
         }
-        sh.mins[threadIdx.x] = mymin;
+        {
+            const uint32_t sorted = warp_sort_asc_u32(mymin, lane);
+            const uint32_t offer = __shfl_sync(0xffffffffu, sorted, (PP + 7) / 8 - 1);
+            if (lane == 0) sh.mins[warp] = offer;
+        }
         if (threadIdx.x == 0) sh.count = 0;
         __syncthreads();
-        const uint32_t tau0 =
-            block_radix_select([&](int t) { return sh.mins[t]; }, SEL_BLOCK, (unsigned)PP, sh);
-        uint32_t* f_id = hkeys;  // S0, in the key / tile area (unused until phase C)
+        uint32_t tau0 = 0;
+        for (int w = 0; w < SEL_BLOCK / 32; ++w) tau0 = sh.mins[w] > tau0 ? sh.mins[w] : tau0;
+        uint32_t* f_id = hkeys + (keep_lo ? L : 0);  // S0, in the key / tile area
         uint32_t* f_hi = f_id + SEL_CAP;
         uint32_t* f_lo = f_hi + SEL_CAP;
         for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
+            uint32_t lk;
             float lo, hi;
-            bounds(c, &lo, &hi);
-            const uint32_t lk = lo != lo ? 0u : float_key(lo);
+            if (keep_lo) {
+                lk = lkeys[c];
+            } else {
+                bounds(c, &lo, &hi);
+                lk = lo != lo ? 0u : float_key(lo);
+            }
             if (lk <= tau0) {
                 const unsigned slot = atomicAdd(&sh.count, 1u);
                 if (slot < (unsigned)SEL_CAP) {
+                    if (keep_lo) bounds(c, &lo, &hi);
                     f_id[slot] = (uint32_t)c;
                     f_hi[slot] = float_key(hi);
                     f_lo[slot] = lk;
