@@ -165,13 +165,18 @@ constexpr int SEL_SORT_MAX = 1024;   // largest P whose selection is returned so
 constexpr int SEL_OVERLAP_MAX = 256; // above this many candidates, all are rescored
 constexpr int SEL_STAGE = kExactTileFloats;  // per-warp product tile of the exact rescoring
 constexpr int SEL_FAST_P = 64;       // largest P that takes the pre-filtered threshold path
+constexpr int SEL_UNROLL = 8;        // centroids per thread whose bounds load together
+// largest L whose lower-bound keys stay in shared memory beside S0 (3 arrays of SEL_CAP)
+constexpr int SEL_KEEP_LO_MAX = (SEL_BLOCK / 32) * SEL_STAGE - 3 * SEL_CAP;
+constexpr uint32_t kKeyNegInf = 0x007fffffu;  // float_key(-inf)
+constexpr uint32_t kKeyPosInf = 0xff800000u;  // float_key(+inf)
 static_assert(SEL_CAP >= SEL_SORT_MAX, "the sorted fallback keeps P keys in the candidate array");
 static_assert(3 * SEL_CAP <= (SEL_BLOCK / 32) * SEL_STAGE, "S0 lives in the tile area");
 
 struct SelShared {
     unsigned hist[256];
     unsigned mins[SEL_BLOCK];
-    unsigned prefix, remain, count, count2, m_less, tie_need, wtot[SEL_BLOCK / 32];
+    unsigned prefix, remain, count, count2, m_less, tie_need, tkey, nex, wtot[SEL_BLOCK / 32];
 };
 
 // Finds the rank-th smallest (1-based) of the keys produced by key_of(c),
@@ -316,6 +321,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     float* srow = S + (int64_t)q * lds;
     const float nq = qn[q], nq2 = qn2[q];
     const bool nrm = normalized != 0;
+    if (threadIdx.x == 0) sh.nex = 0;  // read after later barriers on every path
 
     auto bounds = [&](int c, float* lo, float* hi) {
         approx_bounds(srow[c], nq, cn[c], nq2, cn2[c], beta, gamma, metric, nrm, lo, hi);
@@ -324,6 +330,8 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     bool exact_all = PP > SEL_SORT_MAX;
     bool have = false;  // candidates in cand[0, cnt)
     unsigned cnt = 0;
+    // interval of candidate i as keys (lower, upper), beside cand[i]
+    uint2* ik = reinterpret_cast<uint2*>(bnd);
     if (!exact_all && PP <= SEL_FAST_P) {
         // --- pre-filtered threshold.  Each warp sorts its threads' smallest
         // upper-bound keys and offers its ceil(PP/8)-th smallest; tau0, the largest
@@ -332,56 +340,119 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         // hi <= T therefore has lo <= tau0, so T is the PP-th smallest upper bound
         // within S0 = {c : lo <= tau0}, and every candidate (lo <= T) is in S0.
         // The lower-bound keys of the first pass are kept when they fit beside S0.
+        // Loops over centroids take SEL_UNROLL of them per thread at a time with
+        // their loads issued together.
         uint32_t* lkeys = hkeys;
-        const bool keep_lo = (size_t)L + 3 * SEL_CAP <= (size_t)(SEL_BLOCK / 32) * SEL_STAGE;
+        const bool keep_lo = L <= SEL_KEEP_LO_MAX;
         uint32_t mymin = 0xffffffffu;
-        for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
-            float lo, hi;
-            bounds(c, &lo, &hi);
-            const uint32_t k = float_key(hi);
-            mymin = k < mymin ? k : mymin;
-            if (keep_lo) lkeys[c] = lo != lo ? 0u : float_key(lo);
+        for (int c0 = threadIdx.x; c0 < L; c0 += SEL_UNROLL * SEL_BLOCK) {
+            float sv[SEL_UNROLL], av[SEL_UNROLL], bv[SEL_UNROLL];
+#pragma unroll
+            for (int u = 0; u < SEL_UNROLL; ++u) {
+                const int c = c0 + u * SEL_BLOCK;
+                sv[u] = c < L ? srow[c] : 0.f;
+                av[u] = c < L ? cn[c] : 0.f;
+                bv[u] = c < L ? cn2[c] : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < SEL_UNROLL; ++u) {
+                const int c = c0 + u * SEL_BLOCK;
+                if (c < L) {
+                    float lo, hi;
+                    approx_bounds(sv[u], nq, av[u], nq2, bv[u], beta, gamma, metric, nrm, &lo, &hi);
+                    const uint32_t k = float_key(hi);
+                    mymin = k < mymin ? k : mymin;
+                    if (keep_lo) lkeys[c] = lo != lo ? 0u : float_key(lo);
+                }
+            }
         }
         {
             const uint32_t sorted = warp_sort_asc_u32(mymin, lane);
             const uint32_t offer = __shfl_sync(0xffffffffu, sorted, (PP + 7) / 8 - 1);
             if (lane == 0) sh.mins[warp] = offer;
         }
-        if (threadIdx.x == 0) sh.count = 0;
+        if (threadIdx.x == 0) {
+            sh.count = 0;
+            sh.count2 = 0;
+            sh.tkey = 0xffffffffu;
+        }
         __syncthreads();
         uint32_t tau0 = 0;
         for (int w = 0; w < SEL_BLOCK / 32; ++w) tau0 = sh.mins[w] > tau0 ? sh.mins[w] : tau0;
         uint32_t* f_id = hkeys + (keep_lo ? L : 0);  // S0, in the key / tile area
-        uint32_t* f_hi = f_id + SEL_CAP;
-        uint32_t* f_lo = f_hi + SEL_CAP;
-        for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
-            uint32_t lk;
-            float lo, hi;
-            if (keep_lo) {
-                lk = lkeys[c];
-            } else {
-                bounds(c, &lo, &hi);
-                lk = lo != lo ? 0u : float_key(lo);
-            }
+        uint32_t* f_lo = f_id + SEL_CAP;
+        uint32_t* f_hi = f_lo + SEL_CAP;
+        auto s0_add = [&](int c, uint32_t lk) {
             if (lk <= tau0) {
                 const unsigned slot = atomicAdd(&sh.count, 1u);
                 if (slot < (unsigned)SEL_CAP) {
-                    if (keep_lo) bounds(c, &lo, &hi);
                     f_id[slot] = (uint32_t)c;
-                    f_hi[slot] = float_key(hi);
                     f_lo[slot] = lk;
+                }
+            }
+        };
+        if (keep_lo) {
+            for (int c = threadIdx.x; c < L; c += SEL_BLOCK) s0_add(c, lkeys[c]);
+        } else {
+            for (int c0 = threadIdx.x; c0 < L; c0 += SEL_UNROLL * SEL_BLOCK) {
+                float sv[SEL_UNROLL], av[SEL_UNROLL], bv[SEL_UNROLL];
+#pragma unroll
+                for (int u = 0; u < SEL_UNROLL; ++u) {
+                    const int c = c0 + u * SEL_BLOCK;
+                    sv[u] = c < L ? srow[c] : 0.f;
+                    av[u] = c < L ? cn[c] : 0.f;
+                    bv[u] = c < L ? cn2[c] : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < SEL_UNROLL; ++u) {
+                    const int c = c0 + u * SEL_BLOCK;
+                    if (c < L) {
+                        float lo, hi;
+                        approx_bounds(sv[u], nq, av[u], nq2, bv[u], beta, gamma, metric, nrm, &lo,
+                                      &hi);
+                        s0_add(c, lo != lo ? 0u : float_key(lo));
+                    }
                 }
             }
         }
         __syncthreads();
         const unsigned n0 = sh.count;
         if (n0 <= (unsigned)SEL_CAP) {
-            const uint32_t tkey =
-                block_radix_select([&](int i) { return f_hi[i]; }, (int)n0, (unsigned)PP, sh);
-            if (threadIdx.x == 0) sh.count2 = 0;
+            // upper bounds of S0: few centroids, their loads in parallel
+            for (int i = threadIdx.x; i < (int)n0; i += SEL_BLOCK) {
+                float lo, hi;
+                bounds((int)f_id[i], &lo, &hi);
+                f_hi[i] = float_key(hi);
+            }
             __syncthreads();
-            for (int i = threadIdx.x; i < (int)n0; i += SEL_BLOCK)
-                if (f_lo[i] <= tkey) cand[atomicAdd(&sh.count2, 1u)] = f_id[i];
+            // T = the PP-th smallest upper bound in S0 (n0 >= PP, see above)
+            uint32_t tkey;
+            if (n0 <= (unsigned)SEL_BLOCK) {
+                // by counting: the one key value with fewer than PP keys below it
+                // and at least PP at or below it
+                if (threadIdx.x < n0) {
+                    const uint32_t k = f_hi[threadIdx.x];
+                    unsigned less = 0, le = 0;
+                    for (int j = 0; j < (int)n0; ++j) {
+                        const uint32_t kj = f_hi[j];
+                        less += kj < k ? 1u : 0u;
+                        le += kj <= k ? 1u : 0u;
+                    }
+                    if (less < (unsigned)PP && le >= (unsigned)PP) sh.tkey = k;
+                }
+                __syncthreads();
+                tkey = sh.tkey;
+            } else {
+                tkey = block_radix_select([&](int i) { return f_hi[i]; }, (int)n0, (unsigned)PP, sh);
+            }
+            // candidates: lo <= T, with their intervals
+            for (int i = threadIdx.x; i < (int)n0; i += SEL_BLOCK) {
+                if (f_lo[i] <= tkey) {
+                    const unsigned slot = atomicAdd(&sh.count2, 1u);
+                    cand[slot] = f_id[i];
+                    ik[slot] = make_uint2(f_lo[i], f_hi[i]);
+                }
+            }
             __syncthreads();
             cnt = sh.count2;
             have = true;
@@ -416,9 +487,13 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
             float lo, hi;
             bounds(c, &lo, &hi);
-            if (float_key(lo) <= tkey || lo != lo) {
+            const uint32_t lk = lo != lo ? 0u : float_key(lo);
+            if (lk <= tkey) {
                 const unsigned slot = atomicAdd(&sh.count, 1u);
-                if (slot < (unsigned)SEL_CAP) cand[slot] = (unsigned long long)c;
+                if (slot < (unsigned)SEL_CAP) {
+                    cand[slot] = (unsigned long long)c;
+                    ik[slot] = make_uint2(lk, float_key(hi));
+                }
             }
         }
         __syncthreads();
@@ -427,74 +502,74 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         else have = true;
     }
     if (have) {
-        {
-            // --- phase C: order the candidates by exact score.  A candidate whose
-            // interval overlaps no other candidate's is already ordered by its
-            // approximate value; the rest are rescored in the reference's exact
-            // arithmetic, spread evenly over the warps.  Keys: (score key, id).
-            for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK) {
-                float lo, hi;
-                bounds((int)cand[i], &lo, &hi);
-                bnd[i] = make_float2(lo, hi);
+        // --- phase C: order the candidates by exact score.  The intervals hold
+        // the reference's scores, so a candidate whose finite interval overlaps no
+        // other candidate's is ordered, against all others (their exact scores
+        // included), by its lower bound; the rest are rescored in the reference's
+        // exact arithmetic.  Keys: (score key, id), all distinct.
+        const bool all_exact = cnt > (unsigned)SEL_OVERLAP_MAX;
+        for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK) {
+            const uint2 bi = ik[i];
+            bool need = all_exact || bi.x <= kKeyNegInf || bi.y >= kKeyPosInf;
+            for (int j = 0; j < (int)cnt && !need; ++j) {
+                const uint2 bj = ik[j];
+                if (j != i && bj.x <= bi.y && bi.x <= bj.y) need = true;
             }
-            __syncthreads();
-            const bool all_exact = cnt > (unsigned)SEL_OVERLAP_MAX;
-            if (threadIdx.x == 0) sh.count2 = 0;
-            __syncthreads();
-            for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK) {
-                const float2 bi = bnd[i];
-                bool need = all_exact;
-                for (int j = 0; j < (int)cnt && !need; ++j)
-                    if (j != i && bnd[j].x <= bi.y && bi.x <= bnd[j].y) need = true;
-                const int c = (int)cand[i];
-                needf[i] = need ? 1 : 0;
-                if (need) {
-                    cand[i] = (unsigned)c;  // rescored below
-                } else {
-                    float lo, hi, a;
-                    approx_bounds(srow[c], nq, cn[c], nq2, cn2[c], beta, gamma, metric, nrm, &lo,
-                                  &hi, &a);
-                    cand[i] = ((unsigned long long)float_key(a) << 32) | (unsigned)c;
+            const unsigned c = (unsigned)cand[i];
+            needf[i] = need ? 1 : 0;
+            cand[i] = need ? (unsigned long long)c : ((unsigned long long)bi.x << 32) | c;
+        }
+        __syncthreads();
+        // compact the candidates to rescore (exl reuses the interval array)
+        for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK)
+            if (needf[i]) exl[atomicAdd(&sh.nex, 1u)] = i;
+        __syncthreads();
+        const int nex = (int)sh.nex;
+        float* stage = stage_all + warp * SEL_STAGE;
+        for (int r0 = 0; r0 < nex; r0 += SEL_BLOCK) {
+            // up to 256 candidates per round, G = ceil(n / 8) per warp
+            const int n = nex - r0 < SEL_BLOCK ? nex - r0 : SEL_BLOCK;
+            const int G = (n + SEL_BLOCK / 32 - 1) / (SEL_BLOCK / 32);
+            if (warp * G >= n) continue;  // warp-uniform: nothing for this warp
+            const int i = warp * G + lane;
+            const int idx = (lane < G && i < n) ? exl[r0 + i] : -1;
+            const int c = idx >= 0 ? (int)(cand[idx] & 0xffffffffu) : -1;
+            float r;
+            if (G <= 8)
+                r = warp_exact_scores<4>(qs, C, ldc, D, metric, nrm, c, stage, lane);
+            else if (G <= 16)
+                r = warp_exact_scores<2>(qs, C, ldc, D, metric, nrm, c, stage, lane);
+            else
+                r = warp_exact_scores<1>(qs, C, ldc, D, metric, nrm, c, stage, lane);
+            if (idx >= 0) cand[idx] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
+        }
+        __syncthreads();
+        if (cnt <= (unsigned)SEL_BLOCK) {
+            // output position = rank among the candidates (cnt >= PP)
+            if (threadIdx.x < cnt) {
+                const unsigned long long kk = cand[threadIdx.x];
+                unsigned r = 0;
+                for (int j = 0; j < (int)cnt; ++j) r += cand[j] < kk ? 1u : 0u;
+                if (r < (unsigned)PP) {
+                    int32_t id = (int32_t)(kk & 0xffffffffu);
+                    if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
+                    probes[(int64_t)q * P + r] = id;
                 }
-            }
-            __syncthreads();
-            // compact the candidates to rescore, then 32 of them per warp
-            for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK)
-                if (needf[i]) exl[atomicAdd(&sh.count2, 1u)] = i;
-            __syncthreads();
-            const int nex = (int)sh.count2;
-            float* stage = stage_all + warp * SEL_STAGE;
-            for (int r0 = 0; r0 < nex; r0 += SEL_BLOCK) {
-                // up to 256 candidates per round, G = ceil(n / 8) per warp
-                const int n = nex - r0 < SEL_BLOCK ? nex - r0 : SEL_BLOCK;
-                const int G = (n + SEL_BLOCK / 32 - 1) / (SEL_BLOCK / 32);
-                if (warp * G >= n) continue;  // warp-uniform: nothing for this warp
-                const int i = warp * G + lane;
-                const int idx = (lane < G && i < n) ? exl[r0 + i] : -1;
-                const int c = idx >= 0 ? (int)(cand[idx] & 0xffffffffu) : -1;
-                float r;
-                if (G <= 8)
-                    r = warp_exact_scores<4>(qs, C, ldc, D, metric, nrm, c, stage, lane);
-                else if (G <= 16)
-                    r = warp_exact_scores<2>(qs, C, ldc, D, metric, nrm, c, stage, lane);
-                else
-                    r = warp_exact_scores<1>(qs, C, ldc, D, metric, nrm, c, stage, lane);
-                if (idx >= 0) cand[idx] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
-            }
-            __syncthreads();
-            int n2 = 1;
-            while (n2 < (int)cnt) n2 <<= 1;
-            for (int i = (int)cnt + threadIdx.x; i < n2; i += SEL_BLOCK) cand[i] = ~0ull;
-            __syncthreads();
-            bitonic_sort_u64(cand, n2);
-            for (int j = threadIdx.x; j < PP; j += SEL_BLOCK) {
-                const unsigned long long kk = cand[j];
-                int32_t id = (int32_t)(kk & 0xffffffffu);
-                if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
-                probes[(int64_t)q * P + j] = id;
             }
             return;
         }
+        int n2 = 1;
+        while (n2 < (int)cnt) n2 <<= 1;
+        for (int i = (int)cnt + threadIdx.x; i < n2; i += SEL_BLOCK) cand[i] = ~0ull;
+        __syncthreads();
+        bitonic_sort_u64(cand, n2);
+        for (int j = threadIdx.x; j < PP; j += SEL_BLOCK) {
+            const unsigned long long kk = cand[j];
+            int32_t id = (int32_t)(kk & 0xffffffffu);
+            if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
+            probes[(int64_t)q * P + j] = id;
+        }
+        return;
     }
 
     // --- fallback: exact scores for every centroid, selection by (score, id)
