@@ -17,6 +17,8 @@
 // in the reference's exact arithmetic and sorted by (score, id).
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "score.cuh"
@@ -158,37 +160,57 @@ float sgemm_error_beta(int K) { return (float)(K + 2) * 5.9604645e-8f * 1.01f; }
 // Exact selection.
 // ---------------------------------------------------------------------------
 namespace {
-constexpr int SEL_BLOCK = 256;
-constexpr int SEL_CAP = 1024;        // candidates rescored and sorted in shared memory (>= SEL_SORT_MAX)
+// Two shapes of the selection block: a small one (128 threads, 256 candidates,
+// about 28 KB of shared memory for 4096 centroids of dim 1024, so that seven
+// blocks share an SM and a batch of 1024 queries runs in one wave: every phase
+// waits on memory, and more resident queries hide more of it) for P <= 128, and
+// a large one (256 threads, 1024 candidates) for larger P.
+constexpr int SEL_SMALL_NT = 128, SEL_SMALL_CAP = 256, SEL_SMALL_MINB = 7;
+constexpr int SEL_LARGE_NT = 256, SEL_LARGE_CAP = 1024;
+constexpr int SEL_SMALL_P = 128;     // largest P for the small block
 constexpr int SEL_KEYS_SMEM = 8192;  // upper-bound keys cached in shared memory up to this L
 constexpr int SEL_SORT_MAX = 1024;   // largest P whose selection is returned sorted
 constexpr int SEL_OVERLAP_MAX = 256; // above this many candidates, all are rescored
 constexpr int SEL_STAGE = kExactTileFloats;  // per-warp product tile of the exact rescoring
-constexpr int SEL_FAST_P = 64;       // largest P that takes the pre-filtered threshold path
+constexpr int SEL_FAST_P = 128;      // largest P that takes the pre-filtered threshold path
+constexpr int SEL_KEEP_LO_L = 8192;  // largest L whose lower-bound keys stay beside S0
 constexpr int SEL_UNROLL = 8;        // centroids per thread whose bounds load together
-// largest L whose lower-bound keys stay in shared memory beside S0 (3 arrays of SEL_CAP)
-constexpr int SEL_KEEP_LO_MAX = (SEL_BLOCK / 32) * SEL_STAGE - 3 * SEL_CAP;
 constexpr uint32_t kKeyNegInf = 0x007fffffu;  // float_key(-inf)
 constexpr uint32_t kKeyPosInf = 0xff800000u;  // float_key(+inf)
-static_assert(SEL_CAP >= SEL_SORT_MAX, "the sorted fallback keeps P keys in the candidate array");
-static_assert(3 * SEL_CAP <= (SEL_BLOCK / 32) * SEL_STAGE, "S0 lives in the tile area");
+static_assert(SEL_LARGE_CAP >= SEL_SORT_MAX && SEL_SMALL_CAP >= SEL_SMALL_P,
+              "the sorted fallback keeps P keys in the candidate array");
+static_assert(3 * SEL_SMALL_CAP <= (SEL_SMALL_NT / 32) * SEL_STAGE &&
+                  3 * SEL_LARGE_CAP <= (SEL_LARGE_NT / 32) * SEL_STAGE,
+              "S0 lives in the tile area");
+static_assert(SEL_FAST_P <= 32 * (SEL_SMALL_NT / 32), "each warp offers its ceil(P / warps)-th key");
 
+// 32-bit words of the shared area that holds, in turn, the cached upper-bound
+// keys or the lower-bound keys beside S0, and the per-warp product tiles.
+template <int NT, int CAP>
+__host__ __device__ constexpr size_t sel_area_words(int L) {
+    size_t a = (size_t)(NT / 32) * SEL_STAGE;
+    if (L <= SEL_KEYS_SMEM && (size_t)L > a) a = (size_t)L;
+    if (L <= SEL_KEEP_LO_L && (size_t)L + 3 * CAP > a) a = (size_t)L + 3 * CAP;
+    return a;
+}
+
+template <int NT>
 struct SelShared {
     unsigned hist[256];
-    unsigned mins[SEL_BLOCK];
-    unsigned prefix, remain, count, count2, m_less, tie_need, tkey, nex, wtot[SEL_BLOCK / 32];
+    unsigned mins[NT / 32];
+    unsigned prefix, remain, count, count2, m_less, tie_need, tkey, nex, wtot[NT / 32];
 };
 
 // Finds the rank-th smallest (1-based) of the keys produced by key_of(c),
 // c in [0, L), by 4 passes of an 8-bit radix select.  All threads return it.
-template <class KeyOf>
-__device__ uint32_t block_radix_select(KeyOf key_of, int L, unsigned rank, SelShared& sh) {
+template <int NT, class KeyOf>
+__device__ uint32_t block_radix_select(KeyOf key_of, int L, unsigned rank, SelShared<NT>& sh) {
     uint32_t prefix = 0, mask = 0;
     for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
-        for (int i = threadIdx.x; i < 256; i += SEL_BLOCK) sh.hist[i] = 0;
+        for (int i = threadIdx.x; i < 256; i += NT) sh.hist[i] = 0;
         __syncthreads();
-        for (int c0 = 0; c0 < L; c0 += SEL_BLOCK) {
+        for (int c0 = 0; c0 < L; c0 += NT) {
             const int c = c0 + threadIdx.x;
             int bin = -1;
             if (c < L) {
@@ -239,14 +261,15 @@ __device__ uint32_t block_radix_select(KeyOf key_of, int L, unsigned rank, SelSh
 
 // Block-wide exclusive scan of one flag per thread; returns the thread's offset
 // and writes the block total to *total.
-__device__ unsigned block_flag_scan(bool flag, unsigned* total, SelShared& sh) {
+template <int NT>
+__device__ unsigned block_flag_scan(bool flag, unsigned* total, SelShared<NT>& sh) {
     const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const unsigned ball = __ballot_sync(0xffffffffu, flag);
     const unsigned below = __popc(ball & ((1u << lane) - 1u));
     if (lane == 0) sh.wtot[w] = __popc(ball);
     __syncthreads();
     unsigned base = 0, tot = 0;
-    for (unsigned i = 0; i < SEL_BLOCK / 32; ++i) {
+    for (unsigned i = 0; i < NT / 32; ++i) {
         if (i < w) base += sh.wtot[i];
         tot += sh.wtot[i];
     }
@@ -270,11 +293,12 @@ __device__ __forceinline__ uint32_t warp_sort_asc_u32(uint32_t v, int lane) {
     return v;
 }
 
+template <int NT>
 __device__ void bitonic_sort_u64(unsigned long long* a, int n) {
     // n is a power of two
     for (int k = 2; k <= n; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < n; i += SEL_BLOCK) {
+            for (int i = threadIdx.x; i < n; i += NT) {
                 const int p = i ^ j;
                 if (p > i) {
                     const unsigned long long x = a[i], y = a[p];
@@ -295,29 +319,31 @@ __device__ void bitonic_sort_u64(unsigned long long* a, int n) {
 // with exact scores on the fallback path).  Writes P cluster ids per query into
 // probes (ascending by exact score when P <= 1024, else in ascending id order),
 // or -1 for the nearest-cluster form (P == 1, nan_is_none) when every score is NaN.
-__global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
+template <int NT, int CAP, int MINB>
+__global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
     float* __restrict__ S, int64_t lds, const float* __restrict__ Q, int64_t ldq,
     const float* __restrict__ C, int64_t ldc, const float* __restrict__ qn,
     const float* __restrict__ qn2, const float* __restrict__ cn, const float* __restrict__ cn2,
     int L, int D, int metric, int normalized, float beta, float gamma, int P, int nan_is_none,
     int32_t* __restrict__ probes) {
     extern __shared__ __align__(16) unsigned char sel_smem[];
-    __shared__ SelShared sh;
+    __shared__ SelShared<NT> sh;
+    constexpr int NW = NT / 32;
     const int q = blockIdx.x;
     float* qs = reinterpret_cast<float*>(sel_smem);                               // D floats
-    unsigned long long* cand = reinterpret_cast<unsigned long long*>(qs + ((D + 3) & ~3));  // SEL_CAP
-    float2* bnd = reinterpret_cast<float2*>(cand + SEL_CAP);                     // SEL_CAP
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(qs + ((D + 3) & ~3));  // CAP
+    float2* bnd = reinterpret_cast<float2*>(cand + CAP);                     // CAP
     int* exl = reinterpret_cast<int*>(bnd);  // reuses bnd once the overlap test is done
-    unsigned char* needf = reinterpret_cast<unsigned char*>(bnd + SEL_CAP);      // SEL_CAP
+    unsigned char* needf = reinterpret_cast<unsigned char*>(bnd + CAP);      // CAP
     // one area, used first for the cached upper-bound keys, later for the
     // per-warp product tiles of the exact rescoring
-    uint32_t* hkeys = reinterpret_cast<uint32_t*>(needf + SEL_CAP);
+    uint32_t* hkeys = reinterpret_cast<uint32_t*>(needf + CAP);
     float* stage_all = reinterpret_cast<float*>(hkeys);
     const bool cache = L <= SEL_KEYS_SMEM;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const float* qrow = Q + (int64_t)q * ldq;
-    for (int i = threadIdx.x; i < D; i += SEL_BLOCK) qs[i] = qrow[i];
+    for (int i = threadIdx.x; i < D; i += NT) qs[i] = qrow[i];
     float* srow = S + (int64_t)q * lds;
     const float nq = qn[q], nq2 = qn2[q];
     const bool nrm = normalized != 0;
@@ -333,9 +359,9 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     // interval of candidate i as keys (lower, upper), beside cand[i]
     uint2* ik = reinterpret_cast<uint2*>(bnd);
     if (!exact_all && PP <= SEL_FAST_P) {
-        // --- pre-filtered threshold.  Each warp sorts its threads' smallest
-        // upper-bound keys and offers its ceil(PP/8)-th smallest; tau0, the largest
-        // offer, has at least 8 * ceil(PP/8) >= PP distinct keys <= it, so
+        // --- pre-filtered threshold.  Each of the NW warps sorts its threads'
+        // smallest upper-bound keys and offers its ceil(PP/NW)-th smallest; tau0,
+        // the largest offer, has at least NW * ceil(PP/NW) >= PP distinct keys <= it, so
         // tau0 >= T (the PP-th smallest upper bound of all).  Every centroid with
         // hi <= T therefore has lo <= tau0, so T is the PP-th smallest upper bound
         // within S0 = {c : lo <= tau0}, and every candidate (lo <= T) is in S0.
@@ -343,20 +369,20 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         // Loops over centroids take SEL_UNROLL of them per thread at a time with
         // their loads issued together.
         uint32_t* lkeys = hkeys;
-        const bool keep_lo = L <= SEL_KEEP_LO_MAX;
+        const bool keep_lo = L <= SEL_KEEP_LO_L;  // the area then holds L + 3 CAP words
         uint32_t mymin = 0xffffffffu;
-        for (int c0 = threadIdx.x; c0 < L; c0 += SEL_UNROLL * SEL_BLOCK) {
+        for (int c0 = threadIdx.x; c0 < L; c0 += SEL_UNROLL * NT) {
             float sv[SEL_UNROLL], av[SEL_UNROLL], bv[SEL_UNROLL];
 #pragma unroll
             for (int u = 0; u < SEL_UNROLL; ++u) {
-                const int c = c0 + u * SEL_BLOCK;
+                const int c = c0 + u * NT;
                 sv[u] = c < L ? srow[c] : 0.f;
                 av[u] = c < L ? cn[c] : 0.f;
                 bv[u] = c < L ? cn2[c] : 0.f;
             }
 #pragma unroll
             for (int u = 0; u < SEL_UNROLL; ++u) {
-                const int c = c0 + u * SEL_BLOCK;
+                const int c = c0 + u * NT;
                 if (c < L) {
                     float lo, hi;
                     approx_bounds(sv[u], nq, av[u], nq2, bv[u], beta, gamma, metric, nrm, &lo, &hi);
@@ -368,7 +394,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         }
         {
             const uint32_t sorted = warp_sort_asc_u32(mymin, lane);
-            const uint32_t offer = __shfl_sync(0xffffffffu, sorted, (PP + 7) / 8 - 1);
+            const uint32_t offer = __shfl_sync(0xffffffffu, sorted, (PP + NW - 1) / NW - 1);
             if (lane == 0) sh.mins[warp] = offer;
         }
         if (threadIdx.x == 0) {
@@ -378,34 +404,34 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         }
         __syncthreads();
         uint32_t tau0 = 0;
-        for (int w = 0; w < SEL_BLOCK / 32; ++w) tau0 = sh.mins[w] > tau0 ? sh.mins[w] : tau0;
+        for (int w = 0; w < NW; ++w) tau0 = sh.mins[w] > tau0 ? sh.mins[w] : tau0;
         uint32_t* f_id = hkeys + (keep_lo ? L : 0);  // S0, in the key / tile area
-        uint32_t* f_lo = f_id + SEL_CAP;
-        uint32_t* f_hi = f_lo + SEL_CAP;
+        uint32_t* f_lo = f_id + CAP;
+        uint32_t* f_hi = f_lo + CAP;
         auto s0_add = [&](int c, uint32_t lk) {
             if (lk <= tau0) {
                 const unsigned slot = atomicAdd(&sh.count, 1u);
-                if (slot < (unsigned)SEL_CAP) {
+                if (slot < (unsigned)CAP) {
                     f_id[slot] = (uint32_t)c;
                     f_lo[slot] = lk;
                 }
             }
         };
         if (keep_lo) {
-            for (int c = threadIdx.x; c < L; c += SEL_BLOCK) s0_add(c, lkeys[c]);
+            for (int c = threadIdx.x; c < L; c += NT) s0_add(c, lkeys[c]);
         } else {
-            for (int c0 = threadIdx.x; c0 < L; c0 += SEL_UNROLL * SEL_BLOCK) {
+            for (int c0 = threadIdx.x; c0 < L; c0 += SEL_UNROLL * NT) {
                 float sv[SEL_UNROLL], av[SEL_UNROLL], bv[SEL_UNROLL];
 #pragma unroll
                 for (int u = 0; u < SEL_UNROLL; ++u) {
-                    const int c = c0 + u * SEL_BLOCK;
+                    const int c = c0 + u * NT;
                     sv[u] = c < L ? srow[c] : 0.f;
                     av[u] = c < L ? cn[c] : 0.f;
                     bv[u] = c < L ? cn2[c] : 0.f;
                 }
 #pragma unroll
                 for (int u = 0; u < SEL_UNROLL; ++u) {
-                    const int c = c0 + u * SEL_BLOCK;
+                    const int c = c0 + u * NT;
                     if (c < L) {
                         float lo, hi;
                         approx_bounds(sv[u], nq, av[u], nq2, bv[u], beta, gamma, metric, nrm, &lo,
@@ -417,9 +443,9 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         }
         __syncthreads();
         const unsigned n0 = sh.count;
-        if (n0 <= (unsigned)SEL_CAP) {
+        if (n0 <= (unsigned)CAP) {
             // upper bounds of S0: few centroids, their loads in parallel
-            for (int i = threadIdx.x; i < (int)n0; i += SEL_BLOCK) {
+            for (int i = threadIdx.x; i < (int)n0; i += NT) {
                 float lo, hi;
                 bounds((int)f_id[i], &lo, &hi);
                 f_hi[i] = float_key(hi);
@@ -427,7 +453,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
             __syncthreads();
             // T = the PP-th smallest upper bound in S0 (n0 >= PP, see above)
             uint32_t tkey;
-            if (n0 <= (unsigned)SEL_BLOCK) {
+            if (n0 <= (unsigned)NT) {
                 // by counting: the one key value with fewer than PP keys below it
                 // and at least PP at or below it
                 if (threadIdx.x < n0) {
@@ -446,7 +472,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
                 tkey = block_radix_select([&](int i) { return f_hi[i]; }, (int)n0, (unsigned)PP, sh);
             }
             // candidates: lo <= T, with their intervals
-            for (int i = threadIdx.x; i < (int)n0; i += SEL_BLOCK) {
+            for (int i = threadIdx.x; i < (int)n0; i += NT) {
                 if (f_lo[i] <= tkey) {
                     const unsigned slot = atomicAdd(&sh.count2, 1u);
                     cand[slot] = f_id[i];
@@ -461,7 +487,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     }
     if (!exact_all && !have) {
         if (cache) {
-            for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
+            for (int c = threadIdx.x; c < L; c += NT) {
                 float lo, hi;
                 bounds(c, &lo, &hi);
                 hkeys[c] = float_key(hi);
@@ -484,13 +510,13 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         // so a NaN bound, key 0xffffffff for hi / mapped low for lo, is kept)
         if (threadIdx.x == 0) sh.count = 0;
         __syncthreads();
-        for (int c = threadIdx.x; c < L; c += SEL_BLOCK) {
+        for (int c = threadIdx.x; c < L; c += NT) {
             float lo, hi;
             bounds(c, &lo, &hi);
             const uint32_t lk = lo != lo ? 0u : float_key(lo);
             if (lk <= tkey) {
                 const unsigned slot = atomicAdd(&sh.count, 1u);
-                if (slot < (unsigned)SEL_CAP) {
+                if (slot < (unsigned)CAP) {
                     cand[slot] = (unsigned long long)c;
                     ik[slot] = make_uint2(lk, float_key(hi));
                 }
@@ -498,7 +524,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         }
         __syncthreads();
         cnt = sh.count;
-        if (cnt > (unsigned)SEL_CAP) exact_all = true;
+        if (cnt > (unsigned)CAP) exact_all = true;
         else have = true;
     }
     if (have) {
@@ -508,7 +534,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         // included), by its lower bound; the rest are rescored in the reference's
         // exact arithmetic.  Keys: (score key, id), all distinct.
         const bool all_exact = cnt > (unsigned)SEL_OVERLAP_MAX;
-        for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK) {
+        for (int i = threadIdx.x; i < (int)cnt; i += NT) {
             const uint2 bi = ik[i];
             bool need = all_exact || bi.x <= kKeyNegInf || bi.y >= kKeyPosInf;
             for (int j = 0; j < (int)cnt && !need; ++j) {
@@ -521,15 +547,15 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         }
         __syncthreads();
         // compact the candidates to rescore (exl reuses the interval array)
-        for (int i = threadIdx.x; i < (int)cnt; i += SEL_BLOCK)
+        for (int i = threadIdx.x; i < (int)cnt; i += NT)
             if (needf[i]) exl[atomicAdd(&sh.nex, 1u)] = i;
         __syncthreads();
         const int nex = (int)sh.nex;
         float* stage = stage_all + warp * SEL_STAGE;
-        for (int r0 = 0; r0 < nex; r0 += SEL_BLOCK) {
-            // up to 256 candidates per round, G = ceil(n / 8) per warp
-            const int n = nex - r0 < SEL_BLOCK ? nex - r0 : SEL_BLOCK;
-            const int G = (n + SEL_BLOCK / 32 - 1) / (SEL_BLOCK / 32);
+        for (int r0 = 0; r0 < nex; r0 += NT) {
+            // up to NT candidates per round, G = ceil(n / NW) per warp
+            const int n = nex - r0 < NT ? nex - r0 : NT;
+            const int G = (n + NW - 1) / NW;
             if (warp * G >= n) continue;  // warp-uniform: nothing for this warp
             const int i = warp * G + lane;
             const int idx = (lane < G && i < n) ? exl[r0 + i] : -1;
@@ -544,7 +570,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
             if (idx >= 0) cand[idx] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
         }
         __syncthreads();
-        if (cnt <= (unsigned)SEL_BLOCK) {
+        if (cnt <= (unsigned)NT) {
             // output position = rank among the candidates (cnt >= PP)
             if (threadIdx.x < cnt) {
                 const unsigned long long kk = cand[threadIdx.x];
@@ -560,10 +586,10 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         }
         int n2 = 1;
         while (n2 < (int)cnt) n2 <<= 1;
-        for (int i = (int)cnt + threadIdx.x; i < n2; i += SEL_BLOCK) cand[i] = ~0ull;
+        for (int i = (int)cnt + threadIdx.x; i < n2; i += NT) cand[i] = ~0ull;
         __syncthreads();
-        bitonic_sort_u64(cand, n2);
-        for (int j = threadIdx.x; j < PP; j += SEL_BLOCK) {
+        bitonic_sort_u64<NT>(cand, n2);
+        for (int j = threadIdx.x; j < PP; j += NT) {
             const unsigned long long kk = cand[j];
             int32_t id = (int32_t)(kk & 0xffffffffu);
             if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
@@ -574,7 +600,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
 
     // --- fallback: exact scores for every centroid, selection by (score, id)
     __syncthreads();
-    for (int c = threadIdx.x; c < L; c += SEL_BLOCK)
+    for (int c = threadIdx.x; c < L; c += NT)
         srow[c] = exact_score(qs, C + (int64_t)c * ldc, D, metric, nrm);
     __syncthreads();
     const uint32_t kth =
@@ -584,7 +610,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
         sh.count2 = 0;
     }
     __syncthreads();
-    for (int c = threadIdx.x; c < L; c += SEL_BLOCK)
+    for (int c = threadIdx.x; c < L; c += NT)
         if (float_key(srow[c]) < kth) atomicAdd(&sh.count, 1u);
     __syncthreads();
     const unsigned m_less = sh.count;
@@ -592,7 +618,7 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     // ordered compaction: keys < kth, then the first tie_need ids with key == kth
     const bool sorted = PP <= SEL_SORT_MAX;
     unsigned out_pos = 0, ties_taken = 0;
-    for (int c0 = 0; c0 < L; c0 += SEL_BLOCK) {
+    for (int c0 = 0; c0 < L; c0 += NT) {
         const int c = c0 + threadIdx.x;
         const uint32_t k = c < L ? float_key(srow[c]) : 0xffffffffu;
         const bool tie = c < L && k == kth;
@@ -614,10 +640,10 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     if (sorted) {
         int n2 = 1;
         while (n2 < PP) n2 <<= 1;
-        for (int i = PP + threadIdx.x; i < n2; i += SEL_BLOCK) cand[i] = ~0ull;
+        for (int i = PP + threadIdx.x; i < n2; i += NT) cand[i] = ~0ull;
         __syncthreads();
-        bitonic_sort_u64(cand, n2);
-        for (int j = threadIdx.x; j < PP; j += SEL_BLOCK) {
+        bitonic_sort_u64<NT>(cand, n2);
+        for (int j = threadIdx.x; j < PP; j += NT) {
             const unsigned long long kk = cand[j];
             int32_t id = (int32_t)(kk & 0xffffffffu);
             if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
@@ -626,12 +652,17 @@ __global__ void __launch_bounds__(SEL_BLOCK) select_probes_kernel(
     }
 }
 
+namespace {
+template <int NT, int CAP>
+size_t select_smem_bytes_t(int L, int D) {
+    return sizeof(float) * (size_t)((D + 3) & ~3) + sizeof(unsigned long long) * CAP +
+           sizeof(float2) * CAP + CAP + sizeof(uint32_t) * sel_area_words<NT, CAP>(L);
+}
+}  // namespace
+
 size_t select_smem_bytes(int L, int D) {
-    size_t b = sizeof(float) * (size_t)((D + 3) & ~3) + sizeof(unsigned long long) * SEL_CAP +
-               sizeof(float2) * SEL_CAP + SEL_CAP;
-    const size_t keys = L <= SEL_KEYS_SMEM ? sizeof(uint32_t) * (size_t)L : 0;
-    const size_t tiles = sizeof(float) * (size_t)(SEL_BLOCK / 32) * SEL_STAGE;
-    return b + (keys > tiles ? keys : tiles);
+    return std::max(select_smem_bytes_t<SEL_SMALL_NT, SEL_SMALL_CAP>(L, D),
+                    select_smem_bytes_t<SEL_LARGE_NT, SEL_LARGE_CAP>(L, D));
 }
 
 int select_max_dim() { return 8192; }
@@ -695,14 +726,19 @@ cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t 
                                  int normalized, float beta, float gamma, int P, int nan_is_none,
                                  int32_t* probes, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
-    const size_t smem = select_smem_bytes(L, D);
-    cudaError_t e = cudaFuncSetAttribute(select_probes_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    select_probes_kernel<<<nq, SEL_BLOCK, smem, st>>>(S, lds, Q, ldq, C, ldc, qn, qn2, cn, cn2, L,
-                                                      D, metric, normalized, beta, gamma, P,
-                                                      nan_is_none, probes);
-    return cudaGetLastError();
+    auto run = [&](auto kernel, int nt, size_t smem) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        kernel<<<nq, nt, smem, st>>>(S, lds, Q, ldq, C, ldc, qn, qn2, cn, cn2, L, D, metric,
+                                     normalized, beta, gamma, P, nan_is_none, probes);
+        return cudaGetLastError();
+    };
+    if ((P < L ? P : L) <= SEL_SMALL_P)
+        return run(select_probes_kernel<SEL_SMALL_NT, SEL_SMALL_CAP, SEL_SMALL_MINB>, SEL_SMALL_NT,
+                   select_smem_bytes_t<SEL_SMALL_NT, SEL_SMALL_CAP>(L, D));
+    return run(select_probes_kernel<SEL_LARGE_NT, SEL_LARGE_CAP, 3>, SEL_LARGE_NT,
+               select_smem_bytes_t<SEL_LARGE_NT, SEL_LARGE_CAP>(L, D));
 }
 
 }  // namespace m3g

@@ -1,0 +1,64 @@
+"""The exact top-P selection across its block shapes and paths, against the
+oracle's select_nprobe (the reference's SelectNprobe order: ascending exact
+score, ties by lower id).
+
+P runs over both block shapes (the small one takes P <= 128, the large one
+the rest), over the pre-filtered threshold (P <= 128) and the general path,
+and past 1024 (ids returned unsorted).  The centroid sets cover a clustered
+mixture (close scores: most candidates are rescored), more centroids than the
+shared-memory key caches hold (L = 9000), and near-duplicate centroids whose
+intervals all overlap (S0 and the candidate list overflow into the exact
+fallback)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+# name: metric (0 L2, 1 IP, 2 COSINE), normalized, L, dim, nq, P values
+CASES = {
+    "ip_mixture": (1, False, 2048, 256, 48, (1, 8, 32, 64, 100, 128, 129, 256, 1024, 1500)),
+    "l2_mixture": (0, False, 2048, 96, 32, (1, 32, 128, 200)),
+    "cos_raw": (2, False, 1500, 130, 32, (1, 32, 127, 300)),
+    "cos_norm_wide": (2, True, 9000, 64, 24, (1, 16, 64, 128, 500)),
+    "ip_near_duplicates": (1, False, 600, 128, 16, (1, 8, 64, 128, 400)),
+}
+
+
+def make_case(name):
+    metric, normalized, L, d, nq, _ = CASES[name]
+    rng = np.random.default_rng(sum(map(ord, name)))
+    if name == "ip_near_duplicates":
+        base = rng.standard_normal(d).astype(np.float32)
+        C = (base + 1e-6 * rng.standard_normal((L, d))).astype(np.float32)
+        C[::7] = base  # exact duplicates: exact ties, broken by id
+        Q = (base + 0.5 * rng.standard_normal((nq, d))).astype(np.float32)
+    else:
+        means = rng.standard_normal((16, d)).astype(np.float32)
+        C = (means[rng.integers(0, 16, L)] + 0.3 * rng.standard_normal((L, d))).astype(np.float32)
+        Q = (means[rng.integers(0, 16, nq)] + 0.3 * rng.standard_normal((nq, d))).astype(np.float32)
+    if normalized:
+        C /= np.linalg.norm(C, axis=1, keepdims=True)
+        Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    return metric, normalized, C, Q
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_select_matches_oracle(cuda_ok, oracle_mod, name):
+    from m3_memory_b200 import cabi
+
+    O = oracle_mod
+    metric, normalized, C, Q = make_case(name)
+    e = cabi.Engine()
+    e.create_ivf(1, C.shape[1], metric, normalized, C)
+    for p in CASES[name][5]:
+        got = e.select_probes(1, Q, p)
+        pp = min(p, len(C))
+        assert got.shape == (len(Q), pp), (name, p, got.shape)
+        for q in range(len(Q)):
+            want = O.select_nprobe(Q[q], C, metric, normalized, p)
+            if pp > 1024:
+                # above 1024 the set is returned in ascending id order
+                np.testing.assert_array_equal(np.sort(got[q]), np.sort(want), err_msg=f"{name} P={p} q={q}")
+                np.testing.assert_array_equal(got[q], np.sort(got[q]))
+            else:
+                np.testing.assert_array_equal(got[q], want, err_msg=f"{name} P={p} q={q}")
