@@ -282,84 +282,4 @@ __device__ __forceinline__ float warp_exact_scores(const float* __restrict__ q,
                                     : __fsub_rn(1.f, __fdiv_rn(s, __fsqrt_rn(__fmul_rn(na, nb))));
 }
 
-// warp_exact_scores for up to GM <= 4 candidates (lanes 0 .. GM-1) and every
-// metric but non-normalised COSINE, with two register buffers of centroid
-// values: the loads of chunk i+1 are issued before the products of chunk i, so
-// they overlap that chunk's products and serial sums (a single buffer can only
-// be refilled after its products are stored, and measured no overlap).  Same
-// products, order and result as warp_exact_scores; the centroid rows must allow
-// 16-byte loads (ldc % 4 == 0, C 16-byte aligned).
-template <int GM>
-__device__ __forceinline__ float warp_exact_scores_db(const float* __restrict__ q,
-                                                      const float* __restrict__ C, int64_t ldc,
-                                                      int d, int metric, int cid, float* stage,
-                                                      int lane) {
-    constexpr int W = 128, RS = exact_tile_stride<4>();
-    static_assert(GM >= 1 && GM <= 4, "two buffers of GM x 4 floats per lane");
-    const bool mine = lane < GM && cid >= 0;
-    const float* row = stage + lane * RS;
-    auto load = [&](float (&x)[GM][4], int d0) {
-        const int dd = d0 + lane * 4;
-#pragma unroll
-        for (int g = 0; g < GM; ++g) {
-            const int cc = __shfl_sync(0xffffffffu, cid, g);
-            if (cc >= 0 && dd + 4 <= d) {
-                load_vec<4>(C + (int64_t)cc * ldc + dd, x[g]);
-            } else {
-#pragma unroll
-                for (int v = 0; v < 4; ++v)
-                    x[g][v] = (cc >= 0 && dd + v < d) ? __ldg(C + (int64_t)cc * ldc + dd + v) : 0.f;
-            }
-        }
-    };
-    float s = 0.f;
-    auto chunk = [&](const float (&x)[GM][4], int d0) {
-        const int dd = d0 + lane * 4;
-        const int nn = min(W, d - d0);
-        float qv[4];
-#pragma unroll
-        for (int v = 0; v < 4; ++v) qv[v] = dd + v < d ? q[dd + v] : 0.f;
-        __syncwarp();  // the previous chunk's sums are done with the tile
-#pragma unroll
-        for (int g = 0; g < GM; ++g) {
-            float p[4];
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-                if (metric == kL2) {
-                    const float df = __fsub_rn(qv[v], x[g][v]);
-                    p[v] = __fmul_rn(df, df);
-                } else {
-                    p[v] = __fmul_rn(qv[v], x[g][v]);
-                }
-            }
-            store_vec<4>(stage + g * RS + lane * 4, p);
-        }
-        __syncwarp();
-        if (mine) {
-            if (nn == W) {
-#pragma unroll
-                for (int l = 0; l < W; l += 4) {
-                    const float4 r = *reinterpret_cast<const float4*>(row + l);
-                    s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, r.x), r.y), r.z), r.w);
-                }
-            } else {
-                for (int l = 0; l < nn; ++l) s = __fadd_rn(s, row[l]);
-            }
-        }
-    };
-    float xa[GM][4], xb[GM][4];
-    load(xa, 0);
-    for (int d0 = 0; d0 < d; d0 += 2 * W) {
-        if (d0 + W < d) load(xb, d0 + W);
-        chunk(xa, d0);
-        if (d0 + W >= d) break;
-        if (d0 + 2 * W < d) load(xa, d0 + 2 * W);
-        chunk(xb, d0 + W);
-    }
-    __syncwarp();
-    if (metric == kL2) return s;
-    if (metric == kIP) return -s;
-    return __fsub_rn(1.f, s);  // normalised COSINE
-}
-
 }  // namespace m3g
