@@ -5,27 +5,26 @@
 // item is one list with up to 32 of the queries that probe it, so a list is
 // normally streamed from HBM once per search batch.
 //
-// Arithmetic.  <x, q> in fp32 accuracy from six MMAs per 32-dim chunk:
-//   x_hw . [q_hw | q_lo]   tcgen05.mma kind::tf32 (4 x K=8), N = 2 nq_pad, on the
-//                          raw fp32 stage and the fp32 query tile [q | q - q_hw]
-//                          (the tensor core reads the tf32 part of each fp32:
-//                          the low 13 mantissa bits are dropped, rounding toward
-//                          zero, so raw x and q act as x_hw and q_hw)
-//   bf16(x_lo) . bf16(q)   tcgen05.mma kind::f16 (2 x K=16), N = nq_pad, into the
-//                          q_hw columns
-// with x_lo = x - x_hw and q_lo = q - q_hw exact in fp32.  The two column groups
-// add up to x_hw q_hw + x_hw q_lo + x_lo q = <x, q>.  The terms with a _lo factor
-// are at most 2^-10 of the products, so the tf32 / bf16 rounding of their
-// operands adds ~2^-19 relative error.  Scores differ from the reference's
-// sequential fp32 sum by rounding only, as the SIMT scan's do.
+// Arithmetic.  <x, q> in fp32 accuracy from four bf16 MMAs per 32-dim chunk
+// (tcgen05.mma kind::f16, K = 16, fp32 accumulation in TMEM): each fp32 value
+// is split into two bf16 halves, x = x_hi + x_lo + e with x_hi = bf16(x),
+// x_lo = bf16(x - x_hi) (round to nearest), |e| <= 2^-18 |x|, and likewise q.
+//   x_hi . [q_hi | q_lo]   N = 2 nq_pad
+//   x_lo . [q_hi | q_lo]   N = 2 nq_pad, into the same columns
+// Every bf16 x bf16 product is exact in fp32; the column groups add up to
+// (x_hi + x_lo)(q_hi + q_lo), within ~2^-17 of each product x_i q_i.  The
+// split warps convert each landed fp32 stage in place: a row's 128 bytes (32
+// fp32 dims) become 64 bytes of x_hi and 64 bytes of x_lo, so the tensor core
+// reads 16 KB per 128-row block and chunk (the fp32 data itself is never an
+// MMA operand), and no second ring of correction tiles is needed.
 //
-// CTA (one per SM, 14 warps):
-//   warp 0        producer: streams each queued item's rows by TMA (boxes of 32 dims x 128/64/32/16/8 rows,
-//                 SWIZZLE_128B, no multicast) through a ring of fp32 stages.
+// CTA (one per SM, 15 warps):
+//   warp 0        producer: streams each queued item's rows by TMA (boxes of 32 dims x 256/128/64/32/16/8
+//                 rows, SWIZZLE_128B, no multicast) through a ring of fp32 stages.
 //   warp 1        MMA warp: keeps the loop state warp-uniform, one elected lane
 //                 issues the MMAs and commits; it owns the TMEM allocation.
-//   warps 2..9    split warps: per chunk, the query operand tiles (fp32
-//                 [q | q_lo], bf16 q); per stage, the bf16 x_lo tile.
+//   warps 2..9    split warps: per chunk, the bf16 query tile [q_hi | q_lo]; per
+//                 stage, the in-place conversion of each row to [x_hi | x_lo].
 //   warps 10..13  epilogue: TMEM -> scores -> a register top-k per query.
 //   warp 14       scheduler: takes items from the global counter and queues
 //                 their descriptors (list, rows, queries) up to NINFO ahead, so
@@ -54,13 +53,9 @@ constexpr int TROWS = 128;                    // rows per block (MMA M)
 constexpr int SBLK = 2;                       // row blocks per stage
 constexpr int BLK_BYTES = TROWS * TK * 4;     // 16 KB: one block's 32-dim chunk, fp32
 constexpr int X_BYTES = SBLK * BLK_BYTES;     // 32 KB fp32 stage (256 rows x 32 dims)
-constexpr int LO_BYTES = TROWS * 128;         // 16 KB: block j's x_lo in bytes 64 j .. of each row
 constexpr int QMAX = 32;                      // queries per item
-constexpr int QB1_BYTES = 2 * QMAX * 128;     // fp32 [q | q_lo] chunk: 64 rows x 128 B
-constexpr int QB2_BYTES = QMAX * 128;         // bf16 q chunk: 32 rows of 128 B (64 B used)
-constexpr int QSLOT_BYTES = QB1_BYTES + QB2_BYTES;
-constexpr int NXS = 4;                        // fp32 stages
-constexpr int NLO = 3;                        // bf16 correction stages
+constexpr int QSLOT_BYTES = 2 * QMAX * 128;   // bf16 [q_hi | q_lo] chunk: 64 rows of 128 B (64 B used)
+constexpr int NXS = 5;                        // stages (fp32 as loaded, bf16 hi / lo once converted)
 constexpr int NQS = 2;                        // query chunk slots
 constexpr int NSPLIT = 8;
 constexpr int NEPI = 4;
@@ -88,7 +83,7 @@ struct ItemTC {
 };
 
 struct LayoutTC {
-    uint32_t x_off, lo_off, q_off, sc_off, kb_off, info_off, bar_off, total;
+    uint32_t x_off, q_off, sc_off, kb_off, info_off, bar_off, total;
 };
 
 __host__ __device__ constexpr LayoutTC make_layout_tc() {
@@ -96,8 +91,6 @@ __host__ __device__ constexpr LayoutTC make_layout_tc() {
     uint32_t o = 0;
     L.x_off = o;
     o += NXS * X_BYTES;
-    L.lo_off = o;
-    o += NLO * LO_BYTES;
     L.q_off = o;
     o += NQS * QSLOT_BYTES;
     L.sc_off = o;
@@ -129,13 +122,14 @@ struct Ring {
     }
 };
 
-__device__ __forceinline__ float tf32_rz(float x) {
-    return __uint_as_float(__float_as_uint(x) & 0xffffe000u);
-}
-
-__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t*>(&v);
+// bf16 pairs (round to nearest) of (a, b) in *hi and of the remainders
+// (a - hi_a, b - hi_b) in *lo; element a in the low half.
+__device__ __forceinline__ void bf16x2_split(float a, float b, uint32_t* hi, uint32_t* lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    *hi = *reinterpret_cast<const uint32_t*>(&h);
+    *lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
@@ -178,9 +172,8 @@ __global__ void __launch_bounds__(NTHR, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* xfull = bars;               // NXS
     uint64_t* xempty = xfull + NXS;       // NXS
-    uint64_t* lofull = xempty + NXS;      // NLO
-    uint64_t* loempty = lofull + NLO;     // NLO
-    uint64_t* qfull = loempty + NLO;      // NQS
+    uint64_t* xready = xempty + NXS;      // NXS: converted to bf16 by the split warps
+    uint64_t* qfull = xready + NXS;       // NQS
     uint64_t* qempty = qfull + NQS;       // NQS
     uint64_t* infofull = qempty + NQS;    // NINFO
     uint64_t* infoempty = infofull + NINFO;  // NINFO
@@ -191,7 +184,6 @@ __global__ void __launch_bounds__(NTHR, 1)
     float* sc = reinterpret_cast<float*>(smem + L.sc_off);
     unsigned long long* kbuf = reinterpret_cast<unsigned long long*>(smem + L.kb_off);
     const uint32_t x_u32 = smem_u32(smem + L.x_off);
-    const uint32_t lo_u32 = smem_u32(smem + L.lo_off);
     const uint32_t q_u32 = smem_u32(smem + L.q_off);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -203,10 +195,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         for (int s = 0; s < NXS; ++s) {
             mbar_init(&xfull[s], 1);
             mbar_init(&xempty[s], 1);
-        }
-        for (int s = 0; s < NLO; ++s) {
-            mbar_init(&lofull[s], NSPLIT);
-            mbar_init(&loempty[s], 1);
+            mbar_init(&xready[s], NSPLIT);
         }
         for (int s = 0; s < NQS; ++s) {
             mbar_init(&qfull[s], NSPLIT);
@@ -319,9 +308,9 @@ __global__ void __launch_bounds__(NTHR, 1)
         const bool leader = elect_one();
         // descriptor of slot 0 of each ring; a slot / K-step offset of b bytes
         // adds b >> 4 to the start-address field (shared addresses < 256 KB)
-        const uint64_t dx0 = sw128_desc(x_u32), dl0 = sw128_desc(lo_u32);
+        const uint64_t dx0 = sw128_desc(x_u32);
         const uint64_t dq0 = sw128_desc(q_u32);
-        Ring xr, lr, qr;
+        Ring xr, qr;
         uint32_t pseq = 0;
         bool ok = true;
         for (int it = 0; ok; ++it) {
@@ -330,8 +319,7 @@ __global__ void __launch_bounds__(NTHR, 1)
             const ItemTC* inf = &info[slot];
             if (inf->list < 0) break;
             const Geo g(*inf);
-            const uint32_t id_tf32 = tc_idesc_m128(2 * g.nqp, 2u);
-            const uint32_t id_bf16 = tc_idesc_m128(g.nqp, 1u);
+            const uint32_t id_bf16 = tc_idesc_m128(2 * g.nqp, 1u);
             for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
                 const int pb = min(g.bpp, g.nb - p0);
                 const int h = (int)(pseq & 1u);
@@ -346,12 +334,9 @@ __global__ void __launch_bounds__(NTHR, 1)
                         ok = false;
                         break;
                     }
-                    const uint64_t dq1 = dq0 + (uint64_t)((qr.i * QSLOT_BYTES) >> 4);
-                    const uint64_t dq2 = dq1 + (uint64_t)(QB1_BYTES >> 4);
+                    const uint64_t dq = dq0 + (uint64_t)((qr.i * QSLOT_BYTES) >> 4);
                     for (int b = 0; b < pb; b += SBLK) {
-                        bool w = mbar_wait(&xfull[xr.i], xr.ph, err);
-                        if (w) w = mbar_wait(&lofull[lr.i], lr.ph, err);
-                        if (!__all_sync(0xffffffffu, w)) {
+                        if (!__all_sync(0xffffffffu, mbar_wait(&xready[xr.i], xr.ph, err))) {
                             ok = false;
                             break;
                         }
@@ -361,22 +346,20 @@ __global__ void __launch_bounds__(NTHR, 1)
                             for (int j = 0; j < nblk; ++j) {
                                 const uint32_t d =
                                     tmem + (uint32_t)(h * HALF_COLS + (b + j) * 2 * g.nqp);
+                                // block j's rows: x_hi in bytes 0..63, x_lo in 64..127
                                 const uint64_t dx =
                                     dx0 + (uint64_t)((xr.i * X_BYTES + j * BLK_BYTES) >> 4);
-                                const uint64_t dl = dl0 + (uint64_t)((lr.i * LO_BYTES + j * 64) >> 4);
-#pragma unroll
-                                for (int k = 0; k < 4; ++k)  // K = 8 tf32 = 32 B per step
-                                    tc_mma_tf32(d, dx + 2 * k, dq1 + 2 * k, id_tf32, (c | k) != 0);
 #pragma unroll
                                 for (int k = 0; k < 2; ++k)  // K = 16 bf16 = 32 B per step
-                                    tc_mma_f16(d, dl + 2 * k, dq2 + 2 * k, id_bf16, true);
+                                    tc_mma_f16(d, dx + 2 * k, dq + 2 * k, id_bf16, (c | k) != 0);
+#pragma unroll
+                                for (int k = 0; k < 2; ++k)
+                                    tc_mma_f16(d, dx + 4 + 2 * k, dq + 2 * k, id_bf16, true);
                             }
                             tc_commit(&xempty[xr.i]);
-                            tc_commit(&loempty[lr.i]);
                         }
                         __syncwarp();
                         xr.next(NXS);
-                        lr.next(NLO);
                     }
                     if (!ok) break;
                     if (leader) tc_commit(&qempty[qr.i]);
@@ -403,7 +386,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         const int s = threadIdx.x - W_SPLIT0 * 32;  // 0..255
         const int blk = s >> 7, r = s & (TROWS - 1);  // block of the stage, row in the block
         const int qn = s >> 3, qj = s & 7;           // query row, 16-byte column
-        Ring xr, lr, qr;
+        Ring xr, qr;
         for (int it = 0;; ++it) {
             const int slot = it % NINFO;
             const bool got = __all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it / NINFO) & 1, err));
@@ -426,7 +409,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                 const int pb = min(g.bpp, g.nb - p0);
                 float4 qnext = qload(0);
                 for (int c = 0; c < nchunks && ok; ++c) {
-                    // query tiles of chunk c: raw q (tf32 operand) and bf16 [q_lo | q]
+                    // query tile of chunk c: bf16 rows q_hi (qn) and q_lo (nqp + qn)
                     const float4 qv = qnext;
                     if (c + 1 < nchunks) qnext = qload(c + 1);
                     if (qr.n >= (uint32_t)NQS &&
@@ -435,59 +418,52 @@ __global__ void __launch_bounds__(NTHR, 1)
                         break;
                     }
                     if (qn < g.nqp) {
-                        // fp32 rows qn (q) and nqp + qn (q_lo); bf16 row qn (q)
+                        // dims 4 qj .. 4 qj + 3 of the chunk: 8 bytes in 16-byte column
+                        // qj / 2 of rows qn and nqp + qn (swizzled by row & 7, the same
+                        // for both rows as nqp is a multiple of 8)
                         const uint32_t sl = q_u32 + (uint32_t)qr.i * QSLOT_BYTES;
-                        const uint32_t sw = (uint32_t)(qn & 7);  // (nqp + qn) & 7 too
-                        const uint32_t col = ((uint32_t)qj ^ sw) << 4;
-                        sts128(sl + qn * 128 + col, __float_as_uint(qv.x), __float_as_uint(qv.y),
-                               __float_as_uint(qv.z), __float_as_uint(qv.w));
-                        const float lx = qv.x - tf32_rz(qv.x), ly = qv.y - tf32_rz(qv.y);
-                        const float lz = qv.z - tf32_rz(qv.z), lw = qv.w - tf32_rz(qv.w);
-                        sts128(sl + (g.nqp + qn) * 128 + col, __float_as_uint(lx),
-                               __float_as_uint(ly), __float_as_uint(lz), __float_as_uint(lw));
-                        const uint32_t cb = ((uint32_t)(qj >> 1) ^ sw) << 4;
-                        sts64(sl + QB1_BYTES + qn * 128 + cb + (uint32_t)(qj & 1) * 8,
-                              bf16x2(qv.x, qv.y), bf16x2(qv.z, qv.w));
+                        const uint32_t sw = (uint32_t)(qn & 7);
+                        const uint32_t cb = (((uint32_t)(qj >> 1) ^ sw) << 4) + (uint32_t)(qj & 1) * 8;
+                        uint32_t h0, h1, l0, l1;
+                        bf16x2_split(qv.x, qv.y, &h0, &l0);
+                        bf16x2_split(qv.z, qv.w, &h1, &l1);
+                        sts64(sl + qn * 128 + cb, h0, h1);
+                        sts64(sl + (g.nqp + qn) * 128 + cb, l0, l1);
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&qfull[qr.i]);
                     qr.next(NQS);
                     for (int b = 0; b < pb; b += SBLK) {
-                        bool w = mbar_wait(&xfull[xr.i], xr.ph, err);
-                        if (w && lr.n >= (uint32_t)NLO) w = mbar_wait(&loempty[lr.i], lr.ph ^ 1u, err);
-                        if (!__all_sync(0xffffffffu, w)) {
+                        if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xr.i], xr.ph, err))) {
                             ok = false;
                             break;
                         }
                         if (b + blk < pb) {  // warp-uniform: a warp's rows share a block
-                            // row s of the stage (row r of block blk): 32 dims in two halves;
-                            // x_lo of dims 8jj.. to 16-byte column 4 blk + jj of row r of the
-                            // correction tile (swizzled by r & 7; eight consecutive rows per
-                            // load / store phase hit distinct bank groups)
+                            // row s of the stage (row r of block blk), in place: the 32 fp32
+                            // dims (16-byte columns 0..7) become x_hi in columns 0..3 and
+                            // x_lo in columns 4..7, all swizzled by s & 7 (= r & 7), the
+                            // layout the MMA descriptors read.  The thread owns the row.
                             const uint32_t xb = x_u32 + (uint32_t)xr.i * X_BYTES + s * 128;
-                            const uint32_t lb = lo_u32 + (uint32_t)lr.i * LO_BYTES + r * 128;
                             const uint32_t sw = (uint32_t)(r & 7);
+                            float4 t[8];
 #pragma unroll
-                            for (int hf = 0; hf < 2; ++hf) {
-                                uint32_t lo[8];
+                            for (int c8 = 0; c8 < 8; ++c8) t[c8] = lds128f(xb + (((uint32_t)c8 ^ sw) << 4));
 #pragma unroll
-                                for (int q4 = 0; q4 < 4; ++q4) {
-                                    const float4 t =
-                                        lds128f(xb + ((((uint32_t)(hf * 4 + q4)) ^ sw) << 4));
-                                    lo[2 * q4] = bf16x2(t.x - tf32_rz(t.x), t.y - tf32_rz(t.y));
-                                    lo[2 * q4 + 1] = bf16x2(t.z - tf32_rz(t.z), t.w - tf32_rz(t.w));
-                                }
-                                const uint32_t c0 = (uint32_t)(blk * 4 + hf * 2);
-                                sts128(lb + ((c0 ^ sw) << 4), lo[0], lo[1], lo[2], lo[3]);
-                                sts128(lb + (((c0 + 1) ^ sw) << 4), lo[4], lo[5], lo[6], lo[7]);
+                            for (int c4 = 0; c4 < 4; ++c4) {
+                                uint32_t h[4], l[4];
+                                bf16x2_split(t[2 * c4].x, t[2 * c4].y, &h[0], &l[0]);
+                                bf16x2_split(t[2 * c4].z, t[2 * c4].w, &h[1], &l[1]);
+                                bf16x2_split(t[2 * c4 + 1].x, t[2 * c4 + 1].y, &h[2], &l[2]);
+                                bf16x2_split(t[2 * c4 + 1].z, t[2 * c4 + 1].w, &h[3], &l[3]);
+                                sts128(xb + (((uint32_t)c4 ^ sw) << 4), h[0], h[1], h[2], h[3]);
+                                sts128(xb + (((uint32_t)(4 + c4) ^ sw) << 4), l[0], l[1], l[2], l[3]);
                             }
                         }
                         fence_proxy_async_smem();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&lofull[lr.i]);
+                        if (lane == 0) mbar_arrive(&xready[xr.i]);
                         xr.next(NXS);
-                        lr.next(NLO);
                     }
                 }
             }
