@@ -166,7 +166,6 @@ void rebuild_maps(Index& ix) {
         ix.maps_valid = false;
         return;
     }
-    make_row_map(&ix.maps.m256, ix.vecs.p, ix.arena_cap, ix.dpad, 256);
     make_row_map(&ix.maps.m128, ix.vecs.p, ix.arena_cap, ix.dpad, 128);
     make_row_map(&ix.maps.m64, ix.vecs.p, ix.arena_cap, ix.dpad, 64);
     make_row_map(&ix.maps.m32, ix.vecs.p, ix.arena_cap, ix.dpad, 32);

@@ -19,7 +19,7 @@
 // MMA operand), and no second ring of correction tiles is needed.
 //
 // CTA (one per SM, 15 warps):
-//   warp 0        producer: streams each queued item's rows by TMA (boxes of 32 dims x 256/128/64/32/16/8
+//   warp 0        producer: streams each queued item's rows by TMA (boxes of 32 dims x 128/64/32/16/8
 //                 rows, SWIZZLE_128B, no multicast) through a ring of fp32 stages.
 //   warp 1        MMA warp: keeps the loop state warp-uniform, one elected lane
 //                 issues the MMAs and commits; it owns the TMEM allocation.
@@ -30,10 +30,10 @@
 //                 their descriptors (list, rows, queries) up to NINFO ahead, so
 //                 no role waits on that chain of global loads between items.
 // Work order inside an item: passes of up to 256 / (2 nq_pad) row blocks of 128
-// rows; inside a pass, chunk-outer, block-inner (a 32 KB stage carries the
-// chunk of two consecutive blocks, which halves the per-stage handshakes), each
-// block accumulating into its own 2 nq_pad TMEM columns, so the query tiles of a chunk serve every block
-// of the pass.  TMEM is two halves of 256 columns: one pass accumulates while
+// rows; inside a pass, chunk-pair-outer, block-inner: a 32 KB stage carries two
+// consecutive 32-dim chunks of one block (so every stage is full but for a
+// list's last, partial block), each block accumulating into its own 2 nq_pad
+// TMEM columns, so the query tiles of a chunk pair serve every block of the pass.  TMEM is two halves of 256 columns: one pass accumulates while
 // the epilogue drains the previous one.
 // Every wait is bounded (mbar_wait); on an error the roles stop issuing, the
 // issued copies and MMAs are drained, and TMEM is freed before the CTA leaves.
@@ -50,11 +50,12 @@ namespace {
 
 constexpr int TK = 32;                        // dims per stage (128 B of fp32)
 constexpr int TROWS = 128;                    // rows per block (MMA M)
-constexpr int SBLK = 2;                       // row blocks per stage
-constexpr int BLK_BYTES = TROWS * TK * 4;     // 16 KB: one block's 32-dim chunk, fp32
-constexpr int X_BYTES = SBLK * BLK_BYTES;     // 32 KB fp32 stage (256 rows x 32 dims)
+constexpr int SCHK = 2;                       // chunks per stage
+constexpr int CHK_BYTES = TROWS * TK * 4;     // 16 KB: one block's 32-dim chunk, fp32
+constexpr int X_BYTES = SCHK * CHK_BYTES;     // 32 KB stage: one block (128 rows) x 64 dims
 constexpr int QMAX = 32;                      // queries per item
-constexpr int QSLOT_BYTES = 2 * QMAX * 128;   // bf16 [q_hi | q_lo] chunk: 64 rows of 128 B (64 B used)
+constexpr int QCHK_BYTES = 2 * QMAX * 128;    // bf16 [q_hi | q_lo] chunk: 64 rows of 128 B (64 B used)
+constexpr int QSLOT_BYTES = SCHK * QCHK_BYTES;  // the query tiles of a stage's chunks
 constexpr int NXS = 5;                        // stages (fp32 as loaded, bf16 hi / lo once converted)
 constexpr int NQS = 2;                        // query chunk slots
 constexpr int NSPLIT = 8;
@@ -68,7 +69,7 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int HALF_COLS = 256;
 constexpr int KMAX_TC = 32;
 constexpr int EPI_BAR = 1;                    // named barrier of the epilogue warps
-static_assert(NSPLIT * 32 == SBLK * TROWS, "a split thread owns one row of a stage");
+static_assert(NSPLIT * 32 == SCHK * TROWS, "a split thread owns one row of one chunk of a stage");
 static_assert(QSLOT_BYTES % 1024 == 0, "query tiles stay 1024-byte aligned");
 static_assert(NSPLIT * 32 == QMAX * 8, "a split thread owns 16 bytes of a query chunk");
 
@@ -213,7 +214,6 @@ __global__ void __launch_bounds__(NTHR, 1)
         fence_mbar_init();
     }
     if (warp == W_PROD && lane == 0) {
-        prefetch_tensormap(&maps.m256);
         prefetch_tensormap(&maps.m128);
         prefetch_tensormap(&maps.m64);
         prefetch_tensormap(&maps.m32);
@@ -245,37 +245,26 @@ __global__ void __launch_bounds__(NTHR, 1)
             const int bpp = HALF_COLS / (2 * (np <= 16 ? 16 : 32));
             for (int p0 = 0; p0 < nb && ok; p0 += bpp) {
                 const int pb = min(bpp, nb - p0);
-                for (int c = 0; c < nchunks && ok; ++c) {
-                    const int x = c * TK;
-                    for (int b = 0; b < pb; b += SBLK) {
+                for (int c = 0; c < nchunks && ok; c += SCHK) {
+                    const int nch = min(SCHK, nchunks - c);
+                    for (int b = 0; b < pb; ++b) {
                         if (xr.n >= (uint32_t)NXS &&
                             !__all_sync(0xffffffffu, mbar_wait(&xempty[xr.i], xr.ph ^ 1u, err))) {
                             ok = false;
                             break;
                         }
-                        const int nblk = min(SBLK, pb - b);
-                        // two full blocks as one 256-row box; otherwise each block's rows as
-                        // boxes of 128 / 64 / 32 / 16 / 8 rows (rows past the list's end, up
-                        // to the next multiple of 8, are read and masked later); block j of
-                        // the stage at byte 16 KB * j
-                        int bytes = 0;
-                        for (int j = 0; j < nblk; ++j)
-                            bytes += ((min(TROWS, nrows - (p0 + b + j) * TROWS) + 7) & ~7) * 128;
+                        // the block's rows of each chunk as boxes of 128 / 64 / 32 / 16 / 8
+                        // rows (rows past the list's end, up to the next multiple of 8, are
+                        // read and masked later); chunk j of the stage at byte 16 KB * j
+                        const int row0 = (p0 + b) * TROWS;
+                        const int r8 = (min(TROWS, nrows - row0) + 7) & ~7;
+                        const int y0 = (int)(off + row0);
                         uint64_t* bar = &xfull[xr.i];
-                        const uint32_t dst0 = xbase + (uint32_t)xr.i * X_BYTES;
-                        if (bytes == X_BYTES) {  // two full blocks: one 256-row box
-                            if (leader) {
-                                mbar_arrive_expect_tx(bar, (uint32_t)bytes);
-                                tma_load_2d_u32(dst0, &maps.m256, x, (int)(off + (p0 + b) * TROWS),
-                                                bar);
-                            }
-                        } else if (leader) {
-                            mbar_arrive_expect_tx(bar, (uint32_t)bytes);
-                            for (int j = 0; j < nblk; ++j) {
-                                const int row0 = (p0 + b + j) * TROWS;
-                                const int r8 = (min(TROWS, nrows - row0) + 7) & ~7;
-                                const int y0 = (int)(off + row0);
-                                const uint32_t dst = xbase + (uint32_t)xr.i * X_BYTES + j * BLK_BYTES;
+                        if (leader) {
+                            mbar_arrive_expect_tx(bar, (uint32_t)(nch * r8 * 128));
+                            for (int j = 0; j < nch; ++j) {
+                                const int x = (c + j) * TK;
+                                const uint32_t dst = xbase + (uint32_t)xr.i * X_BYTES + j * CHK_BYTES;
                                 if (r8 == 128) {
                                     tma_load_2d_u32(dst, &maps.m128, x, y0, bar);
                                 } else {
@@ -329,32 +318,33 @@ __global__ void __launch_bounds__(NTHR, 1)
                     break;
                 }
                 tc_fence_after();
-                for (int c = 0; c < nchunks && ok; ++c) {
+                for (int c = 0; c < nchunks && ok; c += SCHK) {
+                    const int nch = min(SCHK, nchunks - c);
                     if (!__all_sync(0xffffffffu, mbar_wait(&qfull[qr.i], qr.ph, err))) {
                         ok = false;
                         break;
                     }
                     const uint64_t dq = dq0 + (uint64_t)((qr.i * QSLOT_BYTES) >> 4);
-                    for (int b = 0; b < pb; b += SBLK) {
+                    for (int b = 0; b < pb; ++b) {
                         if (!__all_sync(0xffffffffu, mbar_wait(&xready[xr.i], xr.ph, err))) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const int nblk = min(SBLK, pb - b);
                         if (leader) {
-                            for (int j = 0; j < nblk; ++j) {
-                                const uint32_t d =
-                                    tmem + (uint32_t)(h * HALF_COLS + (b + j) * 2 * g.nqp);
-                                // block j's rows: x_hi in bytes 0..63, x_lo in 64..127
+                            const uint32_t d = tmem + (uint32_t)(h * HALF_COLS + b * 2 * g.nqp);
+                            for (int j = 0; j < nch; ++j) {
+                                // chunk j's rows: x_hi in bytes 0..63, x_lo in 64..127
                                 const uint64_t dx =
-                                    dx0 + (uint64_t)((xr.i * X_BYTES + j * BLK_BYTES) >> 4);
+                                    dx0 + (uint64_t)((xr.i * X_BYTES + j * CHK_BYTES) >> 4);
+                                const uint64_t dqj = dq + (uint64_t)((j * QCHK_BYTES) >> 4);
 #pragma unroll
                                 for (int k = 0; k < 2; ++k)  // K = 16 bf16 = 32 B per step
-                                    tc_mma_f16(d, dx + 2 * k, dq + 2 * k, id_bf16, (c | k) != 0);
+                                    tc_mma_f16(d, dx + 2 * k, dqj + 2 * k, id_bf16,
+                                               ((c + j) | k) != 0);
 #pragma unroll
                                 for (int k = 0; k < 2; ++k)
-                                    tc_mma_f16(d, dx + 4 + 2 * k, dq + 2 * k, id_bf16, true);
+                                    tc_mma_f16(d, dx + 4 + 2 * k, dqj + 2 * k, id_bf16, true);
                             }
                             tc_commit(&xempty[xr.i]);
                         }
@@ -384,7 +374,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     } else if (warp < W_EPI0) {
         // ------------------------------ split warps ------------------------------
         const int s = threadIdx.x - W_SPLIT0 * 32;  // 0..255
-        const int blk = s >> 7, r = s & (TROWS - 1);  // block of the stage, row in the block
+        const int jh = s >> 7, r = s & (TROWS - 1);   // chunk of the stage, row of the block
         const int qn = s >> 3, qj = s & 7;           // query row, 16-byte column
         Ring xr, qr;
         for (int it = 0;; ++it) {
@@ -407,44 +397,58 @@ __global__ void __launch_bounds__(NTHR, 1)
             };
             for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
                 const int pb = min(g.bpp, g.nb - p0);
-                float4 qnext = qload(0);
-                for (int c = 0; c < nchunks && ok; ++c) {
-                    // query tile of chunk c: bf16 rows q_hi (qn) and q_lo (nqp + qn)
-                    const float4 qv = qnext;
-                    if (c + 1 < nchunks) qnext = qload(c + 1);
+                float4 qnext[SCHK];
+#pragma unroll
+                for (int j = 0; j < SCHK; ++j) qnext[j] = qload(j);
+                for (int c = 0; c < nchunks && ok; c += SCHK) {
+                    const int nch = min(SCHK, nchunks - c);
+                    // query tiles of chunks c, c + 1: bf16 rows q_hi (qn) and q_lo (nqp + qn)
+                    float4 qv[SCHK];
+#pragma unroll
+                    for (int j = 0; j < SCHK; ++j) {
+                        qv[j] = qnext[j];
+                        if (c + SCHK + j < nchunks) qnext[j] = qload(c + SCHK + j);
+                    }
                     if (qr.n >= (uint32_t)NQS &&
                         !__all_sync(0xffffffffu, mbar_wait(&qempty[qr.i], qr.ph ^ 1u, err))) {
                         ok = false;
                         break;
                     }
                     if (qn < g.nqp) {
-                        // dims 4 qj .. 4 qj + 3 of the chunk: 8 bytes in 16-byte column
+                        // dims 4 qj .. 4 qj + 3 of each chunk: 8 bytes in 16-byte column
                         // qj / 2 of rows qn and nqp + qn (swizzled by row & 7, the same
                         // for both rows as nqp is a multiple of 8)
-                        const uint32_t sl = q_u32 + (uint32_t)qr.i * QSLOT_BYTES;
                         const uint32_t sw = (uint32_t)(qn & 7);
                         const uint32_t cb = (((uint32_t)(qj >> 1) ^ sw) << 4) + (uint32_t)(qj & 1) * 8;
-                        uint32_t h0, h1, l0, l1;
-                        bf16x2_split(qv.x, qv.y, &h0, &l0);
-                        bf16x2_split(qv.z, qv.w, &h1, &l1);
-                        sts64(sl + qn * 128 + cb, h0, h1);
-                        sts64(sl + (g.nqp + qn) * 128 + cb, l0, l1);
+#pragma unroll
+                        for (int j = 0; j < SCHK; ++j) {
+                            if (j < nch) {
+                                const uint32_t sl =
+                                    q_u32 + (uint32_t)qr.i * QSLOT_BYTES + (uint32_t)j * QCHK_BYTES;
+                                uint32_t h0, h1, l0, l1;
+                                bf16x2_split(qv[j].x, qv[j].y, &h0, &l0);
+                                bf16x2_split(qv[j].z, qv[j].w, &h1, &l1);
+                                sts64(sl + qn * 128 + cb, h0, h1);
+                                sts64(sl + (g.nqp + qn) * 128 + cb, l0, l1);
+                            }
+                        }
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&qfull[qr.i]);
                     qr.next(NQS);
-                    for (int b = 0; b < pb; b += SBLK) {
+                    for (int b = 0; b < pb; ++b) {
                         if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xr.i], xr.ph, err))) {
                             ok = false;
                             break;
                         }
-                        if (b + blk < pb) {  // warp-uniform: a warp's rows share a block
-                            // row s of the stage (row r of block blk), in place: the 32 fp32
-                            // dims (16-byte columns 0..7) become x_hi in columns 0..3 and
-                            // x_lo in columns 4..7, all swizzled by s & 7 (= r & 7), the
-                            // layout the MMA descriptors read.  The thread owns the row.
-                            const uint32_t xb = x_u32 + (uint32_t)xr.i * X_BYTES + s * 128;
+                        if (jh < nch) {  // warp-uniform: a warp's rows share a chunk
+                            // row r of chunk jh of the stage, in place: the 32 fp32 dims
+                            // (16-byte columns 0..7) become x_hi in columns 0..3 and x_lo in
+                            // columns 4..7, all swizzled by r & 7, the layout the MMA
+                            // descriptors read.  The thread owns the row.
+                            const uint32_t xb =
+                                x_u32 + (uint32_t)xr.i * X_BYTES + (uint32_t)jh * CHK_BYTES + r * 128;
                             const uint32_t sw = (uint32_t)(r & 7);
                             float4 t[8];
 #pragma unroll

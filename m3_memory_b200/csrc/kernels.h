@@ -49,9 +49,9 @@ struct ScanItem {
 
 // Row boxes of the list arena for the scans: 2-D tensor maps over the arena
 // viewed as [rows, dpad] fp32, box width 32 floats (128 B, SWIZZLE_128B) and
-// heights 256 / 128 / 64 / 32 / 16 / 8 rows.
+// heights 128 / 64 / 32 / 16 / 8 rows.
 struct RowMaps {
-    CUtensorMap m256, m128, m64, m32, m16, m8;
+    CUtensorMap m128, m64, m32, m16, m8;
 };
 
 struct ScanArgs {
