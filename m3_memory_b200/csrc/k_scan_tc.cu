@@ -54,12 +54,14 @@ constexpr int SCHK = 2;                       // chunks per stage
 constexpr int CHK_BYTES = TROWS * TK * 4;     // 16 KB: one block's 32-dim chunk, fp32
 constexpr int X_BYTES = SCHK * CHK_BYTES;     // 32 KB stage: one block (128 rows) x 64 dims
 constexpr int QMAX = 32;                      // queries per item
-constexpr int QCHK_BYTES = 2 * QMAX * 128;    // bf16 [q_hi | q_lo] chunk: 64 rows of 128 B (64 B used)
-constexpr int QSLOT_BYTES = SCHK * QCHK_BYTES;  // the query tiles of a stage's chunks
-constexpr int NXS = 5;                        // stages (fp32 as loaded, bf16 hi / lo once converted)
+// the query tiles of a stage's two chunks: 64 rows [q_hi | q_lo] of 128 B, chunk j's
+// 32 bf16 dims in bytes 64 j .. 64 j + 63 of each row
+constexpr int QSLOT_BYTES = 2 * QMAX * 128;
+constexpr int NXS = 6;                        // stages (fp32 as loaded, bf16 hi / lo once converted)
 constexpr int NQS = 2;                        // query chunk slots
 constexpr int NSPLIT = 8;
 constexpr int NEPI = 4;
+constexpr int QHALF = 16;                     // queries per epilogue round through the score tile
 constexpr int W_PROD = 0, W_MMA = 1, W_SPLIT0 = 2, W_EPI0 = W_SPLIT0 + NSPLIT;
 constexpr int W_SCHED = W_EPI0 + NEPI;        // item scheduler warp
 constexpr int NWARPS = W_SCHED + 1;
@@ -95,7 +97,7 @@ __host__ __device__ constexpr LayoutTC make_layout_tc() {
     L.q_off = o;
     o += NQS * QSLOT_BYTES;
     L.sc_off = o;
-    o += QMAX * TROWS * 4;
+    o += QHALF * TROWS * 4;
     L.kb_off = o;
     o += QMAX * 32 * 8;
     L.info_off = o;
@@ -337,7 +339,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                                 // chunk j's rows: x_hi in bytes 0..63, x_lo in 64..127
                                 const uint64_t dx =
                                     dx0 + (uint64_t)((xr.i * X_BYTES + j * CHK_BYTES) >> 4);
-                                const uint64_t dqj = dq + (uint64_t)((j * QCHK_BYTES) >> 4);
+                                const uint64_t dqj = dq + (uint64_t)(4 * j);  // 64 B per chunk
 #pragma unroll
                                 for (int k = 0; k < 2; ++k)  // K = 16 bf16 = 32 B per step
                                     tc_mma_f16(d, dx + 2 * k, dqj + 2 * k, id_bf16,
@@ -415,16 +417,16 @@ __global__ void __launch_bounds__(NTHR, 1)
                         break;
                     }
                     if (qn < g.nqp) {
-                        // dims 4 qj .. 4 qj + 3 of each chunk: 8 bytes in 16-byte column
-                        // qj / 2 of rows qn and nqp + qn (swizzled by row & 7, the same
-                        // for both rows as nqp is a multiple of 8)
+                        // dims 4 qj .. 4 qj + 3 of chunk j: 8 bytes in 16-byte column
+                        // 4 j + qj / 2 of rows qn and nqp + qn (swizzled by row & 7, the
+                        // same for both rows as nqp is a multiple of 8)
                         const uint32_t sw = (uint32_t)(qn & 7);
-                        const uint32_t cb = (((uint32_t)(qj >> 1) ^ sw) << 4) + (uint32_t)(qj & 1) * 8;
+                        const uint32_t sl = q_u32 + (uint32_t)qr.i * QSLOT_BYTES;
 #pragma unroll
                         for (int j = 0; j < SCHK; ++j) {
                             if (j < nch) {
-                                const uint32_t sl =
-                                    q_u32 + (uint32_t)qr.i * QSLOT_BYTES + (uint32_t)j * QCHK_BYTES;
+                                const uint32_t cb = ((((uint32_t)(4 * j + (qj >> 1))) ^ sw) << 4) +
+                                                    (uint32_t)(qj & 1) * 8;
                                 uint32_t h0, h1, l0, l1;
                                 bf16x2_split(qv[j].x, qv[j].y, &h0, &l0);
                                 bf16x2_split(qv[j].z, qv[j].w, &h1, &l1);
@@ -561,14 +563,17 @@ __global__ void __launch_bounds__(NTHR, 1)
                         live = a.alive[off + lrow] != 0;
                         if (a.metric == kCosine && !a.normalized) nb2 = a.rnorm2[off + lrow];
                     }
-                    // columns [0, nqp): x_hw q_hw + x_lo q; [nqp, 2 nqp): x_hw q_lo;
-                    // drained 16 queries at a time
-                    for (int q0 = 0; q0 < g.np; q0 += 16) {
-                        uint32_t c0[16], c1[16];
+                    // columns [0, nqp): x q_hi; [nqp, 2 nqp): x q_lo; 16 queries per
+                    // round: drained to the score tile, then pushed into the top-k
+#pragma unroll
+                    for (int hq = 0; hq < QMAX / QHALF; ++hq) {
+                        const int q0 = hq * QHALF;
+                        if (q0 >= g.np) break;  // the same for every epilogue warp
+                        uint32_t c0[QHALF], c1[QHALF];
                         tmem_ld16(taddr + q0, c0);
                         tmem_ld16(taddr + g.nqp + q0, c1);
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
+                        for (int i = 0; i < QHALF; ++i) {
                             if (q0 + i < g.np) {
                                 const float dot = __uint_as_float(c0[i]) + __uint_as_float(c1[i]);
                                 float s = INF;
@@ -581,25 +586,26 @@ __global__ void __launch_bounds__(NTHR, 1)
                                                                       : 1.f - dot / sqrtf(na * nb2);
                                     }
                                 }
-                                sc[(q0 + i) * TROWS + trow] = s;
+                                sc[i * TROWS + trow] = s;
                             }
                         }
-                    }
-                    named_bar_sync(EPI_BAR, NEPI * 32);
+                        named_bar_sync(EPI_BAR, NEPI * 32);
 #pragma unroll
-                    for (int j = 0; j < QMAX / NEPI; ++j) {
-                        const int qi = ew + NEPI * j;
-                        if (qi < g.np) {
-                            unsigned long long* kb = kbuf + qi * 32;
-                            const int rbase = (p0 + b) * TROWS;
+                        for (int jj = 0; jj < QHALF / NEPI; ++jj) {
+                            const int j = hq * (QHALF / NEPI) + jj;  // query ew + NEPI j
+                            const int qi = ew + NEPI * j;
+                            if (qi < g.np) {
+                                unsigned long long* kb = kbuf + qi * 32;
+                                const int rbase = (p0 + b) * TROWS;
 #pragma unroll
-                            for (int m = 0; m < TROWS / 32; ++m)
-                                if (rbase + 32 * m < nrows)
-                                    rt[j].push(kb, a.k, sc[qi * TROWS + 32 * m + lane],
-                                               rbase + 32 * m + lane, lane);
+                                for (int m = 0; m < TROWS / 32; ++m)
+                                    if (rbase + 32 * m < nrows)
+                                        rt[j].push(kb, a.k, sc[(qi - q0) * TROWS + 32 * m + lane],
+                                                   rbase + 32 * m + lane, lane);
+                            }
                         }
+                        named_bar_sync(EPI_BAR, NEPI * 32);
                     }
-                    named_bar_sync(EPI_BAR, NEPI * 32);
                 }
                 tc_fence_before();
                 __syncwarp();
