@@ -948,7 +948,8 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
         M3G_CK(launch_probed_rows(w.lcount.p, ix.d_list_len.p, L, w.stats.p, w.stats.p + 1, st));
         M3G_CK(cudaEventRecord(ev[4], st));
     }
-    M3G_CK(cudaMemsetAsync(w.item_counter.p, 0, sizeof(int32_t), st));
+    // the item counter and the per-query score bounds of the tensor-core scan
+    M3G_CK(cudaMemsetAsync(w.item_counter.p, 0, sizeof(int32_t) * (size_t)(1 + nq), st));
     // probe slots the work list skips (probe -1) keep empty partial lists
     if (clear_partials)
         M3G_CK(launch_clear_partials(w.part_score.p, w.part_row.p, nq * P * k, st));
@@ -963,6 +964,7 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     a.items = w.items.p;
     a.n_items = w.n_items.p;
     a.item_counter = w.item_counter.p;
+    a.qbound = reinterpret_cast<uint32_t*>(w.item_counter.p + 1);
     a.pair_q = w.pair_q.p;
     a.pair_slot = w.pair_slot.p;
     a.k = k;
@@ -1012,7 +1014,8 @@ bool ws_needs_grow(const Workspace& w, const WsSizes& s) {
            short_of(w.pair_slot, s.nq * s.P) || short_of(w.items, s.nq * s.P) ||
            short_of(w.part_score, s.nq * s.P * s.k) || short_of(w.part_row, s.nq * s.P * s.k) ||
            short_of(w.out_ids, s.nq * s.k) || short_of(w.out_scores, s.nq * s.k) ||
-           short_of(w.out_counts, s.nq) || short_of(w.Q3, s.nq * gemm_tc_kdim((int)s.dpad));
+           short_of(w.out_counts, s.nq) || short_of(w.Q3, s.nq * gemm_tc_kdim((int)s.dpad)) ||
+           short_of(w.item_counter, 1 + s.nq);
 }
 void ensure_ws(Workspace& w, const WsSizes& s) {
     if (!w.err.p) {
@@ -1020,8 +1023,8 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
         M3G_CK(cudaMemset(w.err.p, 0, sizeof(int)));
         w.stats.alloc(2);
         w.n_items.alloc(1);
-        w.item_counter.alloc(1);
     }
+    w.item_counter.ensure((size_t)(1 + s.nq));
     w.Q.ensure((size_t)(s.nq * s.dpad));
     w.qn.ensure((size_t)s.nq);
     w.qn2.ensure((size_t)s.nq);

@@ -543,7 +543,17 @@ __global__ void __launch_bounds__(NTHR, 1)
             const Geo g(*inf);
             const int nrows = inf->nrows;
             const int64_t off = inf->off;
+            // rows scoring above a query's bound cannot reach its answer: the bound
+            // is the k-th best score of one of its lists already scanned
             RegTopK rt[QMAX / NEPI];
+#pragma unroll
+            for (int j = 0; j < QMAX / NEPI; ++j) {
+                const int qi = ew + NEPI * j;
+                if (qi < g.np && a.qbound) {
+                    const uint32_t bk = ~a.qbound[inf->q[qi]];  // score key (0xffffffff: none)
+                    if (bk != 0xffffffffu) rt[j].set_cap(((unsigned long long)bk << 32) | 0xffffffffull);
+                }
+            }
             bool ok = true;
             for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
                 const int pb = min(g.bpp, g.nb - p0);
@@ -619,6 +629,10 @@ __global__ void __launch_bounds__(NTHR, 1)
                 const int qi = ew + NEPI * j;
                 if (qi < g.np) {
                     if (rt[j].nbuf) rt[j].flush(kbuf + qi * 32, a.k, lane);
+                    // a full top-k bounds the query's final k-th score
+                    const unsigned long long kth = shfl_u64(rt[j].top, a.k - 1);
+                    if (a.qbound && lane == 0 && kth != ~0ull)
+                        atomicMax(&a.qbound[inf->q[qi]], ~(uint32_t)(kth >> 32));
                     const int64_t base = ((int64_t)inf->q[qi] * a.P + inf->slot[qi]) * a.k;
                     if (lane < a.k) {
                         const unsigned long long t = rt[j].top;

@@ -65,6 +65,8 @@ struct ScanArgs {
     const ScanItem* items;
     const int32_t* n_items;  // device count
     int32_t* item_counter;   // device, zeroed before launch
+    uint32_t* qbound;        // [nq] ~(score key) bounding each query's k-th best score, zeroed
+                             // (no bound) before launch; null: not used
     const int32_t* pair_q;
     const int32_t* pair_slot;
     int k, P, metric, normalized;

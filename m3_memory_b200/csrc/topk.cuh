@@ -54,10 +54,19 @@ __device__ __forceinline__ unsigned long long warp_merge_top(unsigned long long 
 // that beats the current k-th key is appended; the buffer is merged into the
 // top list (sort + bitonic merge) only when it would overflow, and once more at
 // the end of the item, so merges are rare after the first few rows.
+//
+// `cap` bounds tau from above: keys at or above it can be left out (a bound
+// known from outside this list, see the tensor-core scan's per-query bound).
 struct RegTopK {
     unsigned long long top = ~0ull;  // lane i: i-th best key (ascending)
-    unsigned long long tau = ~0ull;  // current k-th best key (all lanes)
+    unsigned long long tau = ~0ull;  // keys below it enter the buffer (all lanes)
+    unsigned long long cap = ~0ull;  // upper bound of tau
     int nbuf = 0;                    // keys waiting in the buffer (warp-uniform)
+
+    __device__ __forceinline__ void set_cap(unsigned long long c) {
+        cap = c;
+        tau = tau < c ? tau : c;
+    }
 
     __device__ __forceinline__ void flush(unsigned long long* buf, int k, int lane) {
         __syncwarp();
@@ -66,6 +75,7 @@ struct RegTopK {
         top = warp_merge_top(top, b, lane);
         if (lane >= k) top = ~0ull;
         tau = shfl_u64(top, k - 1);
+        tau = tau < cap ? tau : cap;
         nbuf = 0;
     }
 
