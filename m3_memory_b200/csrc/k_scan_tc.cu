@@ -156,9 +156,10 @@ __device__ __forceinline__ float4 lds128f(uint32_t addr) {
 
 // Item geometry shared by every role.
 struct Geo {
-    int np, nqp, nb, bpp;
+    int np, nqp, nb, bpp, nrows;
     __device__ __forceinline__ explicit Geo(const ItemTC& inf) {
         np = inf.np;
+        nrows = inf.nrows;
         nqp = np <= 16 ? 16 : 32;
         nb = (inf.nrows + TROWS - 1) / TROWS;
         bpp = HALF_COLS / (2 * nqp);
@@ -444,7 +445,10 @@ __global__ void __launch_bounds__(NTHR, 1)
                             ok = false;
                             break;
                         }
-                        if (jh < nch) {  // warp-uniform: a warp's rows share a chunk
+                        // warp-uniform: a warp's 32 rows share a chunk; rows past the
+                        // block's last loaded one (a list's last block) hold stale bytes
+                        // whose results the epilogue masks, so they are not converted
+                        if (jh < nch && (p0 + b) * TROWS + (r & ~31) < g.nrows) {
                             // row r of chunk jh of the stage, in place: the 32 fp32 dims
                             // (16-byte columns 0..7) become x_hi in columns 0..3 and x_lo in
                             // columns 4..7, all swizzled by r & 7, the layout the MMA
