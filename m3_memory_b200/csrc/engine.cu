@@ -568,6 +568,8 @@ Engine::~Engine() {
     ws_.out_scores.release();
     ws_.out_counts.release();
     ws_.err.release();
+    if (ws_.err_host) cudaFreeHost(ws_.err_host);
+    ws_.err_host = nullptr;
     ws_.stats.release();
 }
 
@@ -1021,6 +1023,7 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
     if (!w.err.p) {
         w.err.alloc(1);
         M3G_CK(cudaMemset(w.err.p, 0, sizeof(int)));
+        if (!w.err_host) M3G_CK(cudaMallocHost(&w.err_host, sizeof(int)));
         w.stats.alloc(2);
         w.n_items.alloc(1);
     }
@@ -1129,11 +1132,16 @@ void Engine::search(int index_id, const float* Q, int64_t nq, int k, int nprobe,
         if (direct_q) {
             dQ = Q + q0 * ix->dim;
         } else {
-            if (ix->dpad != ix->dim)
+            const cudaMemcpyKind kind = q_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+            if (ix->dpad != ix->dim) {
                 M3G_CK(cudaMemsetAsync(ws_.Q.p, 0, (size_t)(m * ix->dpad) * 4, st));
-            M3G_CK(cudaMemcpy2DAsync(ws_.Q.p, (size_t)ix->dpad * 4, Q + q0 * ix->dim,
-                                     (size_t)ix->dim * 4, (size_t)ix->dim * 4, (size_t)m,
-                                     q_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+                M3G_CK(cudaMemcpy2DAsync(ws_.Q.p, (size_t)ix->dpad * 4, Q + q0 * ix->dim,
+                                         (size_t)ix->dim * 4, (size_t)ix->dim * 4, (size_t)m, kind,
+                                         st));
+            } else {
+                M3G_CK(cudaMemcpyAsync(ws_.Q.p, Q + q0 * ix->dim, (size_t)(m * ix->dim) * 4, kind,
+                                       st));
+            }
             dQ = ws_.Q.p;
         }
         int64_t* oi = out_dev ? out_ids + q0 * k : ws_.out_ids.p;
@@ -1157,9 +1165,10 @@ void Engine::search(int index_id, const float* Q, int64_t nq, int k, int nprobe,
         prof_.k = k;
     }
     if (!ext_stream) {
+        // the error flag comes back with the results: one round trip per call
+        M3G_CK(cudaMemcpyAsync(ws_.err_host, ws_.err.p, sizeof(int), cudaMemcpyDeviceToHost, st));
         M3G_CK(cudaStreamSynchronize(st));
-        int err = 0;
-        M3G_CK(cudaMemcpy(&err, ws_.err.p, sizeof(int), cudaMemcpyDeviceToHost));
+        const int err = *ws_.err_host;
         if (err) {
             M3G_CK(cudaMemset(ws_.err.p, 0, sizeof(int)));
             fail(M3G_ETIMEOUT, "search: a device-side wait gave up (kernel error " + std::to_string(err) + ")");

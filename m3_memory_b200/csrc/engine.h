@@ -156,6 +156,7 @@ struct Workspace {
     DBuf<float> out_scores;
     DBuf<int32_t> out_counts;
     DBuf<int> err;
+    int* err_host = nullptr;  // pinned copy of err, read after the stream's last sync
     DBuf<unsigned long long> stats;
     cudaStream_t stream = nullptr;
     cudaStream_t last_stream = nullptr;  // stream of the last user (ordered by `done`)

@@ -12,6 +12,15 @@ is the final ascending sort of ``IVFIndex::search_nprobe``
 The exchange is the only collective on the path; its size is
 ``world * Q * k * 12`` bytes per batch.
 
+With ``split_coarse=True`` the coarse step is split by query instead of being
+repeated: rank r selects the probes of its slice of the batch (queries
+r * ceil(Q / world) ..) over all centroids (``m3g_select_probes_device``, the
+same exact selection), the ``[Q, P]`` probe lists are all-gathered (Q * P * 4
+bytes), and every rank scans its own lists for the whole batch
+(``m3g_search_probes_device``; lists it does not own hold no rows here) before
+the top-k exchange above.  The coarse work per rank then shrinks with the
+number of GPUs.
+
 With ``coarse_index_id`` the coarse step is sharded too, so it shrinks with the
 number of GPUs instead of being repeated on each: every rank keeps a second
 index holding only the centroids of its own lists (ascending cluster id), takes
@@ -60,12 +69,21 @@ class ShardedSearch:
 
     def __init__(self, engine, index_id: int, k: int, max_q: int, world: int, device,
                  group=None, coarse_index_id=None, owner=None, rank: int = 0,
-                 max_nprobe: int = 256):
+                 max_nprobe: int = 256, split_coarse: bool = False):
         import torch
 
         self.engine, self.index_id, self.k, self.world = engine, index_id, k, world
         self.group = group
         self.coarse_index_id = coarse_index_id
+        self.split_coarse = split_coarse and coarse_index_id is None
+        self.rank = rank
+        if self.split_coarse:
+            self.nlist = int(engine.info(index_id)[3])
+            p = min(max_nprobe, self.nlist)
+            chunk = -(-max_q // world)
+            self.sp_loc = torch.empty((chunk, p), dtype=torch.int32, device=device)
+            self.sp_all = torch.empty((world * chunk, p), dtype=torch.int32, device=device)
+            self.max_nprobe = p
         if coarse_index_id is not None:
             if owner is None:
                 raise ValueError("a sharded coarse step needs the list owners")
@@ -112,6 +130,8 @@ class ShardedSearch:
         s = torch.cuda.current_stream(q.device).cuda_stream
         if self.coarse_index_id is not None:
             self._search_sharded_coarse(q, nq, nprobe, s)
+        elif self.split_coarse:
+            self._search_split_coarse(q, nq, nprobe, s)
         else:
             self.engine.search_device(self.index_id, q.data_ptr(), nq, k, nprobe,
                                       self.ids.data_ptr(), self.sc.data_ptr(),
@@ -127,6 +147,34 @@ class ShardedSearch:
                                         self.out_ids.data_ptr(), self.out_sc.data_ptr(),
                                         self.out_cnt.data_ptr(), s)
         return self.out_ids[:nq], self.out_sc[:nq], self.out_cnt[:nq]
+
+    def _search_split_coarse(self, q, nq, nprobe, s):
+        """Probes of this rank's query slice, all-gathered, then the scan of the
+        rank's lists for the whole batch; leaves the rank's top-k in self.ids /
+        sc / cnt."""
+        import torch.distributed as dist
+
+        P = min(nprobe if nprobe > 0 else self.nlist, self.nlist)
+        if P > self.max_nprobe:
+            raise ValueError(f"nprobe {P} exceeds max_nprobe={self.max_nprobe}")
+        chunk = -(-nq // self.world)
+        q0 = min(nq, self.rank * chunk)
+        nloc = min(nq, q0 + chunk) - q0
+        loc = self.sp_loc.view(-1)[:chunk * P].view(chunk, P)
+        if nloc > 0:
+            row = q.stride(0) * q.element_size()
+            self.engine.select_probes_device(self.index_id, q.data_ptr() + q0 * row, nloc, P,
+                                             loc.data_ptr(), s)
+        if nloc < chunk:
+            loc[nloc:].fill_(-1)
+        probes = self.sp_all.view(-1)[:self.world * chunk * P].view(self.world * chunk, P)
+        if self.world > 1:
+            dist.all_gather_into_tensor(probes, loc, group=self.group)
+        else:
+            probes.copy_(loc)
+        self.engine.search_probes_device(self.index_id, q.data_ptr(), nq, self.k,
+                                         probes.data_ptr(), P, self.ids.data_ptr(),
+                                         self.sc.data_ptr(), self.cnt.data_ptr(), s)
 
     def _search_sharded_coarse(self, q, nq, nprobe, s):
         """Global top-P from the ranks' exact local top-P, then the scan of the

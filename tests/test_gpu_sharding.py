@@ -212,6 +212,52 @@ def test_sharded_coarse_two_engines_equal_one(cuda_ok):
     compare_search(merged, full.search(1, c["Q"], k, P), exact=True)
 
 
+def test_split_coarse_two_engines_equal_one(cuda_ok):
+    """The query-split coarse steps for a world of 3 (odd split of 64 queries), each
+    rank an engine on this GPU: every rank selects the probes of its query slice over
+    all centroids, the slices are concatenated (the all-gather), every rank scans its
+    own lists for all queries, and the shard merge gives the one-engine answer; a
+    one-rank ShardedSearch in this mode equals the plain search."""
+    import torch
+
+    from m3_memory_b200 import cabi
+    from m3_memory_b200.sharding import ShardedSearch, shard_lists
+
+    c = _index_case(zlib.crc32(b"split"))
+    nq, k, P, world = len(c["Q"]), 10, 9, 3
+    owner = shard_lists(c["sizes"], world)
+    q = torch.from_numpy(c["Q"]).cuda()
+    engines = [_engine(cabi, c, lambda l, r=r: owner[l] == r) for r in range(world)]
+    chunk = -(-nq // world)
+    slices = []
+    for r, e in enumerate(engines):
+        q0, q1 = min(nq, r * chunk), min(nq, (r + 1) * chunk)
+        loc = torch.full((chunk, P), -1, dtype=torch.int32, device="cuda")
+        if q1 > q0:
+            e.select_probes_device(1, q.data_ptr() + q0 * q.stride(0) * 4, q1 - q0, P,
+                                   loc.data_ptr())
+        slices.append(loc)
+    probes = torch.cat(slices)[:nq].contiguous()
+    full = _engine(cabi, c, lambda l: True)
+    np.testing.assert_array_equal(probes.cpu().numpy(), full.select_probes(1, c["Q"], P))
+    parts = []
+    for e in engines:
+        ids = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+        sc = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+        cnt = torch.empty((nq,), dtype=torch.int32, device="cuda")
+        e.search_probes_device(1, q.data_ptr(), nq, k, probes.data_ptr(), P, ids.data_ptr(),
+                               sc.data_ptr(), cnt.data_ptr())
+        parts.append((ids.cpu().numpy(), sc.cpu().numpy()))
+    merged = _merge_device(cabi, torch, np.stack([p[1] for p in parts]),
+                           np.stack([p[0] for p in parts]))
+    want = full.search(1, c["Q"], k, P)
+    compare_search(merged, want, exact=True)
+    ss = ShardedSearch(full, 1, k, nq, 1, "cuda", split_coarse=True)
+    ids, sc, cnt = ss.search(q, P)
+    torch.cuda.synchronize()
+    compare_search((ids.cpu().numpy(), sc.cpu().numpy(), cnt.cpu().numpy()), want, exact=True)
+
+
 _NCCL_CHILD = r"""
 import os, sys, numpy as np, torch, torch.distributed as dist, datetime
 sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/tests")
@@ -228,7 +274,8 @@ own = np.flatnonzero(owner == rank)
 e = T._engine(cabi, c, lambda l: owner[l] == rank, own)
 q = torch.from_numpy(c["Q"]).cuda()
 out = {}
-for name, kw in (("replicated", {}), ("sharded", dict(coarse_index_id=2, owner=owner, rank=rank))):
+for name, kw in (("replicated", {}), ("sharded", dict(coarse_index_id=2, owner=owner, rank=rank)),
+                 ("split", dict(split_coarse=True, rank=rank))):
     ss = ShardedSearch(e, 1, 10, len(c["Q"]), world, "cuda", **kw)
     ids, sc, cnt = ss.search(q, 12)
     torch.cuda.synchronize()
@@ -271,6 +318,6 @@ def test_sharded_search_over_nccl_two_gpus(cuda_ok, tmp_path):
     got = np.load(f)
     c = _index_case(5)
     full = _engine(cabi, c, lambda l: True).search(1, c["Q"], 10, 12)
-    for name in ("replicated", "sharded"):
+    for name in ("replicated", "sharded", "split"):
         compare_search((got[name + "_ids"], got[name + "_sc"], got[name + "_cnt"]), full,
                        exact=True)
