@@ -583,35 +583,66 @@ constexpr int PLAN_THREADS = 1024;
 
 __device__ __forceinline__ int items_of(int c, int gmax) { return (c + gmax - 1) / gmax; }
 
+constexpr int PLAN_CACHE = 8;  // lists per thread kept in registers (L <= 8192)
+
+// Inclusive block-wide sum of one value per thread (PLAN_THREADS threads).
+__device__ __forceinline__ int32_t plan_block_scan(int32_t v, int32_t* wsum) {
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int32_t u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    if (lane == 31) wsum[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        int32_t s = lane < PLAN_THREADS / 32 ? wsum[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int32_t u = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += u;
+        }
+        if (lane < PLAN_THREADS / 32) wsum[lane] = s;
+    }
+    __syncthreads();
+    return v + (w > 0 ? wsum[w - 1] : 0);
+}
+
 // One block: walks the clusters in list_order, assigns each its pair range and
-// its items (the pairs split into ceil(c / gmax) near-equal groups).
+// its items (the pairs split into ceil(c / gmax) near-equal groups).  Each
+// thread takes a run of consecutive positions of list_order; up to PLAN_CACHE
+// per thread their loads are issued together and kept in registers.
 __global__ void __launch_bounds__(PLAN_THREADS) plan_items_kernel(
     const int32_t* __restrict__ lcount, const int32_t* __restrict__ order, int L, int gmax,
     int32_t* __restrict__ lstart, ScanItem* __restrict__ items, int32_t* __restrict__ n_items) {
-    __shared__ int32_t sp[PLAN_THREADS], si[PLAN_THREADS];
+    __shared__ int32_t wp[PLAN_THREADS / 32], wi[PLAN_THREADS / 32];
     const int t = threadIdx.x;
     const int per = (L + PLAN_THREADS - 1) / PLAN_THREADS;
     const int b = t * per, e = min(L, b + per);
+    const bool cached = per <= PLAN_CACHE;
+    int32_t lo[PLAN_CACHE], lc[PLAN_CACHE];
     int32_t np = 0, ni = 0;
-    for (int i = b; i < e; ++i) {
-        const int c = lcount[order[i]];
-        np += c;
-        ni += items_of(c, gmax);
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < PLAN_CACHE; ++j) lo[j] = b + j < e ? order[b + j] : 0;
+#pragma unroll
+        for (int j = 0; j < PLAN_CACHE; ++j) lc[j] = b + j < e ? lcount[lo[j]] : 0;
+#pragma unroll
+        for (int j = 0; j < PLAN_CACHE; ++j) {
+            np += lc[j];
+            ni += items_of(lc[j], gmax);  // 0 for c = 0
+        }
+    } else {
+        for (int i = b; i < e; ++i) {
+            const int c = lcount[order[i]];
+            np += c;
+            ni += items_of(c, gmax);
+        }
     }
-    sp[t] = np;
-    si[t] = ni;
-    __syncthreads();
-    for (int o = 1; o < PLAN_THREADS; o <<= 1) {
-        int32_t vp = t >= o ? sp[t - o] : 0, vi = t >= o ? si[t - o] : 0;
-        __syncthreads();
-        sp[t] += vp;
-        si[t] += vi;
-        __syncthreads();
-    }
-    int32_t pbase = sp[t] - np, ibase = si[t] - ni;
-    for (int i = b; i < e; ++i) {
-        const int l = order[i];
-        const int c = lcount[l];
+    const int32_t pinc = plan_block_scan(np, wp);
+    const int32_t iinc = plan_block_scan(ni, wi);
+    int32_t pbase = pinc - np, ibase = iinc - ni;
+    auto place = [&](int l, int c) {
         lstart[l] = pbase;
         const int n = items_of(c, gmax);
         int pb = pbase;
@@ -622,8 +653,18 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_items_kernel(
         }
         pbase += c;
         ibase += n;
+    };
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < PLAN_CACHE; ++j)
+            if (b + j < e) place(lo[j], lc[j]);
+    } else {
+        for (int i = b; i < e; ++i) {
+            const int l = order[i];
+            place(l, lcount[l]);
+        }
     }
-    if (t == PLAN_THREADS - 1) *n_items = si[t];
+    if (t == PLAN_THREADS - 1) *n_items = iinc;
 }
 
 __global__ void pair_scatter_kernel(const int32_t* __restrict__ probes, int nq, int P, int L,
