@@ -144,3 +144,34 @@ def test_config1_shape_subset(cabi, oracle_mod):
     sub = np.arange(0, 1000, 7)[:150]
     compare_search((got[0][sub], got[1][sub], got[2][sub]),
                    O.search_nprobe(Q[sub], C, lists, O.COSINE, True, 10, 16))
+
+
+def test_host_query_batches_match_device_queries(cabi, oracle_mod):
+    """The host-buffer search (queries copied into the engine's workspace, results
+    copied back) gives the device-query path's answers bit for bit, on
+    consecutive calls and batch sizes that are not multiples of the tile sizes."""
+    import torch
+
+    rng = np.random.default_rng(11)
+    L, d = 300, 128
+    C = rng.standard_normal((L, d)).astype(np.float32)
+    assign = rng.integers(0, L, 20000)
+    X = (C[assign] + 0.5 * rng.standard_normal((20000, d))).astype(np.float32)
+    e = cabi.Engine()
+    e.create_ivf(1, d, oracle_mod.IP, False, C)
+    for c in range(L):
+        rows = np.flatnonzero(assign == c)
+        if len(rows):
+            e.load_cluster(1, c, rows.astype(np.int64), X[rows])
+    for nq in (700, 512, 1031):
+        Q = (C[rng.integers(0, L, nq)] + 0.5 * rng.standard_normal((nq, d))).astype(np.float32)
+        got = e.search(1, Q, 10, 17)
+        qd = torch.from_numpy(Q).cuda()
+        ids = torch.empty((nq, 10), dtype=torch.int64, device="cuda")
+        sc = torch.empty((nq, 10), dtype=torch.float32, device="cuda")
+        cnt = torch.empty((nq,), dtype=torch.int32, device="cuda")
+        e.search_device(1, qd.data_ptr(), nq, 10, 17, ids.data_ptr(), sc.data_ptr(), cnt.data_ptr())
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(got[2], cnt.cpu().numpy())
+        np.testing.assert_array_equal(got[0], ids.cpu().numpy())
+        np.testing.assert_array_equal(got[1], sc.cpu().numpy())
