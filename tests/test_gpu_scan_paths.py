@@ -111,3 +111,40 @@ def test_tensor_core_and_simt_scans_agree(cuda_ok, tmp_path):
         ref = (simt[name + "_ids"], simt[name + "_sc"], simt[name + "_cnt"])
         # both are fp32-accurate restatements: same counts, near-identical scores
         compare_search(got, ref, rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("metric", [1, 2])
+def test_exact_duplicates_across_lists_keep_the_reference_order(cuda_ok, oracle_mod, metric):
+    """The same 24 vectors stored in each of 6 lists (plus distinct rows): the
+    top-k is made of exact score ties across lists.  Rows tying the per-query
+    bound of the tensor-core scan (a finished list's k-th score) must stay in:
+    the exact scores of the rows returned must be the oracle's, position by
+    position (which copies fill a tie group at the k-th place is left open, as
+    the reference's final sort leaves it)."""
+    from m3_memory_b200 import cabi
+
+    rng = np.random.default_rng(77 + metric)
+    d, L, nq = 64, 6, 16
+    C = rng.standard_normal((L, d)).astype(np.float32)
+    base = rng.standard_normal((24, d)).astype(np.float32)
+    rows, lid = [], []
+    for c in range(L):
+        rows += [base, (C[c] + 0.3 * rng.standard_normal((40 + 7 * c, d))).astype(np.float32)]
+        lid += [c] * (24 + 40 + 7 * c)
+    X = np.concatenate(rows)
+    sizes = np.bincount(lid, minlength=L)
+    off = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    ids = np.arange(len(X), dtype=np.int64) * 5 + 2
+    Q = (base[rng.integers(0, 24, nq)] + 0.05 * rng.standard_normal((nq, d))).astype(np.float32)
+    case = dict(metric=metric, normalized=False, C=C, X=X, Q=Q, ids=ids,
+                alive=np.ones(len(X), np.uint8), off=off, nprobe=5, k=10)
+    got = engine_search(cabi, case)
+    lists = oracle_mod.CsrLists(off, X, ids, case["alive"])
+    ref = oracle_mod.search_nprobe(Q, C, lists, metric, False, 10, 5)
+    np.testing.assert_array_equal(got[2], ref[2])
+    row_of = {int(i): r for r, i in enumerate(ids)}
+    for q in range(nq):
+        c = int(ref[2][q])
+        exact = [oracle_mod.score(Q[q], X[row_of[int(i)]], metric, False) for i in got[0][q, :c]]
+        np.testing.assert_array_equal(np.array(exact, np.float32), ref[1][q, :c], err_msg=str(q))
+    compare_search(got, ref)
