@@ -942,9 +942,11 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     const bool tc_scan = use_tc_scan() && scan_tc_supported(ix.metric, k);
     const int gmax = tc_scan ? scan_tc_gmax() : scan_gmax_for_dim(ix.dpad);
     if (gmax <= 0) fail(M3G_EUNSUPPORTED, "search: dimension too large for the list scan");
+    // with cleared partial lists, pairs probing empty lists (on a shard: the lists
+    // other ranks own) are not queued
     M3G_CK(launch_build_worklist(probes, (int)nq, P, L, ix.d_list_order.p, gmax, w.lcount.p,
                                  w.lstart.p, w.lcursor.p, w.items.p, w.n_items.p, w.pair_q.p,
-                                 w.pair_slot.p, st));
+                                 w.pair_slot.p, st, clear_partials ? ix.d_list_len.p : nullptr));
     if (profile) {
         M3G_CK(cudaMemsetAsync(w.stats.p, 0, 2 * sizeof(unsigned long long), st));
         M3G_CK(launch_probed_rows(w.lcount.p, ix.d_list_len.p, L, w.stats.p, w.stats.p + 1, st));

@@ -570,12 +570,19 @@ cudaError_t launch_list_scan(const RowMaps& maps, const ScanArgs& a, int gmax, i
 // ---------------------------------------------------------------------------
 namespace {
 
+// A pair enters the work list when its probe is a list id and, with skip_len,
+// the list holds rows.
+__device__ __forceinline__ bool pair_wanted(int l, int L, const int32_t* skip_len) {
+    return l >= 0 && l < L && (!skip_len || skip_len[l] > 0);
+}
+
 __global__ void probe_hist_kernel(const int32_t* __restrict__ probes, int64_t n, int L,
+                                  const int32_t* __restrict__ skip_len,
                                   int32_t* __restrict__ lcount) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int l = probes[i];
-        if (l >= 0 && l < L) atomicAdd(&lcount[l], 1);
+        if (pair_wanted(l, L, skip_len)) atomicAdd(&lcount[l], 1);
     }
 }
 
@@ -668,6 +675,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_items_kernel(
 }
 
 __global__ void pair_scatter_kernel(const int32_t* __restrict__ probes, int nq, int P, int L,
+                                    const int32_t* __restrict__ skip_len,
                                     const int32_t* __restrict__ lstart,
                                     int32_t* __restrict__ lcursor, int32_t* __restrict__ pair_q,
                                     int32_t* __restrict__ pair_slot) {
@@ -675,7 +683,7 @@ __global__ void pair_scatter_kernel(const int32_t* __restrict__ probes, int nq, 
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int l = probes[i];
-        if (l < 0 || l >= L) continue;
+        if (!pair_wanted(l, L, skip_len)) continue;
         const int pos = lstart[l] + atomicAdd(&lcursor[l], 1);
         pair_q[pos] = (int32_t)(i / P);
         pair_slot[pos] = (int32_t)(i % P);
@@ -688,18 +696,18 @@ cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
                                   const int32_t* list_order, int gmax, int32_t* lcount,
                                   int32_t* lstart, int32_t* lcursor, ScanItem* items,
                                   int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, const int32_t* skip_len) {
     cudaError_t e;
     if ((e = cudaMemsetAsync(lcount, 0, sizeof(int32_t) * (size_t)L, st)) != cudaSuccess) return e;
     if ((e = cudaMemsetAsync(lcursor, 0, sizeof(int32_t) * (size_t)L, st)) != cudaSuccess) return e;
     const int64_t n = (int64_t)nq * P;
     const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
-    if (n > 0) probe_hist_kernel<<<blocks, 256, 0, st>>>(probes, n, L, lcount);
+    if (n > 0) probe_hist_kernel<<<blocks, 256, 0, st>>>(probes, n, L, skip_len, lcount);
     plan_items_kernel<<<1, PLAN_THREADS, 0, st>>>(lcount, list_order, L, gmax, lstart, items,
                                                   n_items);
     if (n > 0)
-        pair_scatter_kernel<<<blocks, 256, 0, st>>>(probes, nq, P, L, lstart, lcursor, pair_q,
-                                                    pair_slot);
+        pair_scatter_kernel<<<blocks, 256, 0, st>>>(probes, nq, P, L, skip_len, lstart, lcursor,
+                                                    pair_q, pair_slot);
     return cudaGetLastError();
 }
 

@@ -87,12 +87,14 @@ int scan_tc_gmax();
 cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, int grid, cudaStream_t st);
 
 // Work list: per-list counts of (query, probe) pairs, items, and the pairs
-// grouped by list.  list_order lists the clusters longest first.
+// grouped by list.  list_order lists the clusters longest first.  With
+// skip_len ([L] rows per list), pairs probing an empty list are left out (their
+// partial lists must then be cleared beforehand).
 cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
                                   const int32_t* list_order, int gmax, int32_t* lcount,
                                   int32_t* lstart, int32_t* lcursor, ScanItem* items,
                                   int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
-                                  cudaStream_t st);
+                                  cudaStream_t st, const int32_t* skip_len = nullptr);
 
 // Final merge of the per-(query, probe) partial top-k into the answer.
 cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
