@@ -1,5 +1,5 @@
 // tc.cuh -- tcgen05 building blocks shared by the tensor-core kernels: shared
-// memory matrix descriptors, MMA issue (kind::f16 and kind::tf32), commit to an
+// memory matrix descriptors, MMA issue (kind::f16), commit to an
 // mbarrier, TMEM loads, allocation.  Plain PTX for sm_100a.
 #pragma once
 
@@ -68,22 +68,8 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     }
 }
 
-
-// kind::tf32: A and B are fp32 in shared memory, of which the tensor core uses
-// the tf32 part: the low 13 mantissa bits are ignored (round toward zero).
-__device__ __forceinline__ void tc_mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                            uint32_t idesc, bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
-        : "memory");
-}
-
 // Instruction descriptor of a 128 x n (n % 16 == 0, 16..256) MMA with fp32
-// accumulation and K-major operands: a_fmt = b_fmt = 1 for bf16 (kind::f16),
-// 2 for tf32 (kind::tf32).
+// accumulation and K-major operands: a_fmt = b_fmt = 1 for bf16 (kind::f16).
 __host__ __device__ constexpr uint32_t tc_idesc_m128(int n, uint32_t fmt) {
     return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) |
            ((uint32_t)(128 >> 4) << 24);
