@@ -466,6 +466,19 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
+        # per-phase device times of the device-resident step on this rank (every rank
+        # runs the same calls; outside the timed loops)
+        marks_per_step = []
+        for i in range(min(args.steps, 50)):
+            sharded.marks = []
+            step(i % NBATCH, nprobe)
+            marks_per_step.append(sharded.marks)
+        sharded.marks = None
+        torch.cuda.synchronize()
+        for m in marks_per_step:
+            for (_, ea), (name, eb) in zip(m, m[1:]):
+                stage_ms.setdefault("ms_" + name, []).append(ea.elapsed_time(eb))
+            stage_ms.setdefault("ms_total", []).append(m[0][1].elapsed_time(m[-1][1]))
     e2e_qps = BATCH * args.steps / e2e_s
 
     if rank != 0:

@@ -114,6 +114,17 @@ class ShardedSearch:
         self.out_sc = torch.empty((max_q, k), dtype=torch.float32, device=device)
         self.out_cnt = torch.empty((max_q,), dtype=torch.int32, device=device)
         self.max_q = max_q
+        # set to a list to have search() append (phase, CUDA event) pairs, recorded on
+        # the current stream at the end of each phase ("start" first)
+        self.marks = None
+
+    def _mark(self, name):
+        if self.marks is not None:
+            import torch
+
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.marks.append((name, e))
 
     def search(self, q, nprobe: int):
         """Top-k over all shards for the device query batch ``q`` ([nq, dim]
@@ -128,6 +139,7 @@ class ShardedSearch:
             raise ValueError(f"batch of {nq} queries exceeds max_q={self.max_q}")
         k = self.k
         s = torch.cuda.current_stream(q.device).cuda_stream
+        self._mark("start")
         if self.coarse_index_id is not None:
             self._search_sharded_coarse(q, nq, nprobe, s)
         elif self.split_coarse:
@@ -136,6 +148,7 @@ class ShardedSearch:
             self.engine.search_device(self.index_id, q.data_ptr(), nq, k, nprobe,
                                       self.ids.data_ptr(), self.sc.data_ptr(),
                                       self.cnt.data_ptr(), s)
+            self._mark("search")
         if self.world == 1:
             return self.ids[:nq], self.sc[:nq], self.cnt[:nq]
         # [world, nq, k] views over the start of the gather buffers (contiguous)
@@ -146,6 +159,7 @@ class ShardedSearch:
         self.engine.merge_shards_device(g_sc.data_ptr(), g_ids.data_ptr(), self.world, nq, k,
                                         self.out_ids.data_ptr(), self.out_sc.data_ptr(),
                                         self.out_cnt.data_ptr(), s)
+        self._mark("topk_exchange")
         return self.out_ids[:nq], self.out_sc[:nq], self.out_cnt[:nq]
 
     def _search_split_coarse(self, q, nq, nprobe, s):
@@ -167,14 +181,17 @@ class ShardedSearch:
                                              loc.data_ptr(), s)
         if nloc < chunk:
             loc[nloc:].fill_(-1)
+        self._mark("coarse")
         probes = self.sp_all.view(-1)[:self.world * chunk * P].view(self.world * chunk, P)
         if self.world > 1:
             dist.all_gather_into_tensor(probes, loc, group=self.group)
         else:
             probes.copy_(loc)
+        self._mark("probe_exchange")
         self.engine.search_probes_device(self.index_id, q.data_ptr(), nq, self.k,
                                          probes.data_ptr(), P, self.ids.data_ptr(),
                                          self.sc.data_ptr(), self.cnt.data_ptr(), s)
+        self._mark("search")
 
     def _search_sharded_coarse(self, q, nq, nprobe, s):
         """Global top-P from the ranks' exact local top-P, then the scan of the

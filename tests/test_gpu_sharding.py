@@ -253,9 +253,12 @@ def test_split_coarse_two_engines_equal_one(cuda_ok):
     want = full.search(1, c["Q"], k, P)
     compare_search(merged, want, exact=True)
     ss = ShardedSearch(full, 1, k, nq, 1, "cuda", split_coarse=True)
+    ss.marks = []  # per-phase events, as bench.py records them for N > 1
     ids, sc, cnt = ss.search(q, P)
     torch.cuda.synchronize()
     compare_search((ids.cpu().numpy(), sc.cpu().numpy(), cnt.cpu().numpy()), want, exact=True)
+    assert [n for n, _ in ss.marks] == ["start", "coarse", "probe_exchange", "search"]
+    assert all(a.elapsed_time(b) >= 0 for (_, a), (_, b) in zip(ss.marks, ss.marks[1:]))
 
 
 _NCCL_CHILD = r"""
