@@ -151,6 +151,22 @@ int m3g_info(m3g_engine* e, int index_id, int* dim, int* metric, int* normalized
 int m3g_cluster_size(m3g_engine* e, int index_id, int cluster_id, int64_t* size, int64_t* live);
 /* The routing centroids [nlist, dim] (IVFIndex::centroid_ptr, m3_index.cpp:170-175). */
 int m3g_get_centroids(m3g_engine* e, int index_id, float* out);
+/* The live rows of one list, in row order: their ids [n] and vectors [n, dim]
+ * (the data Cluster keeps in ids_ / mat_ with alive_ set, cluster.h:73-86).
+ * *out_n is always set to n; with out_ids / out_vecs null only the count is
+ * returned, otherwise capacity must be at least n (M3G_EINVAL if not). */
+int m3g_get_cluster(m3g_engine* e, int index_id, int cluster_id, int64_t* out_ids,
+                    float* out_vecs, int64_t capacity, int64_t* out_n);
+/* Native save / load of a whole index: centroids and every list's live rows
+ * (writes applied so far; call m3g_flush first for queued ones).  No
+ * counterpart in the reference, whose only persistence is the Faiss import
+ * (faiss_loader.py).  m3g_load_index replaces index_id (as m3g_create_ivf
+ * does) only after the whole file has been read; a missing, truncated or
+ * foreign file returns M3G_ERUNTIME / M3G_EINVAL and changes nothing.
+ * The file holds an 8-byte magic, int32 dim, metric, normalized, nlist, the
+ * centroids, then per list int64 n, int64 ids[n], float vectors[n * dim]. */
+int m3g_save_index(m3g_engine* e, int index_id, const char* path);
+int m3g_load_index(m3g_engine* e, int index_id, const char* path);
 /* IVFIndex::add_cluster / set_centroid (m3_index.cpp:133-163). */
 int m3g_add_cluster(m3g_engine* e, int index_id, const float* centroid, int32_t* out_cluster_id);
 int m3g_set_centroid(m3g_engine* e, int index_id, int cluster_id, const float* centroid);

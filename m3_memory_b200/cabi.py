@@ -74,6 +74,9 @@ SIGNATURES = {
     "m3g_probe_scores_device": (_i32, [_vp, _i32, _vp, _i64, _vp, _i32, _vp, _vp]),
     "m3g_search_probes_device": (_i32, [_vp, _i32, _vp, _i64, _i32, _vp, _i32, _vp, _vp, _vp,
                                         _vp]),
+    "m3g_get_cluster": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _vp]),
+    "m3g_save_index": (_i32, [_vp, _i32, ct.c_char_p]),
+    "m3g_load_index": (_i32, [_vp, _i32, ct.c_char_p]),
     "m3g_select_probes_noalloc": (_i32, [_vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp,
                                          _vp]),
     "m3g_set_profiling": (_i32, [_vp, _i32]),
@@ -251,6 +254,23 @@ class Engine:
         check(lib().m3g_info(self.h, index_id, ct.byref(d), ct.byref(m), ct.byref(n),
                              ct.byref(L)))
         return d.value, m.value, bool(n.value), L.value
+
+    def get_cluster(self, index_id, cid):
+        """(ids [n], vectors [n, dim]) of a list's live rows, in row order."""
+        n = ct.c_int64()
+        check(lib().m3g_get_cluster(self.h, index_id, cid, None, None, 0, ct.byref(n)))
+        d = self.info(index_id)[0]
+        ids = np.empty(n.value, np.int64)
+        vecs = np.empty((n.value, d), np.float32)
+        check(lib().m3g_get_cluster(self.h, index_id, cid, _p(ids), _p(vecs), n.value,
+                                    ct.byref(n)))
+        return ids, vecs
+
+    def save_index(self, index_id, path):
+        check(lib().m3g_save_index(self.h, index_id, str(path).encode()))
+
+    def load_index(self, index_id, path):
+        check(lib().m3g_load_index(self.h, index_id, str(path).encode()))
 
     def cluster_size(self, index_id, cid):
         s, l_ = ct.c_int64(), ct.c_int64()

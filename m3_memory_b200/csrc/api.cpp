@@ -248,6 +248,23 @@ int m3g_get_centroids(m3g_engine* e, int index_id, float* out) {
     return guarded([&] { e->eng.get_centroids(index_id, out); });
 }
 
+int m3g_get_cluster(m3g_engine* e, int index_id, int cluster_id, int64_t* out_ids,
+                    float* out_vecs, int64_t capacity, int64_t* out_n) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded(
+        [&] { e->eng.get_cluster(index_id, cluster_id, out_ids, out_vecs, capacity, out_n); });
+}
+
+int m3g_save_index(m3g_engine* e, int index_id, const char* path) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.save_index(index_id, path); });
+}
+
+int m3g_load_index(m3g_engine* e, int index_id, const char* path) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.load_index(index_id, path); });
+}
+
 int m3g_add_cluster(m3g_engine* e, int index_id, const float* centroid, int32_t* out_cluster_id) {
     M3G_ENGINE_OR_FAIL(e);
     return guarded([&] {

@@ -12,7 +12,7 @@
 // Additions beyond the reference surface (all new, none shadows a reference
 // method): search_into_device (tensor fast path by raw device pointers),
 // nearest_clusters, select_probes, search_on, kmeans, train_ivf, split_cluster,
-// cluster_size, centroids, add_cluster, set_centroid, compact_cluster,
+// cluster_size, centroids, save_index, load_index, add_cluster, set_centroid, compact_cluster,
 // maintenance_pass, set_device, set_profiling, last_profile.
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
@@ -481,6 +481,28 @@ PYBIND11_MODULE(_m3_async, m) {
                 return py::make_tuple(sz, live);
             },
             py::arg("index_id"), py::arg("cluster_id"))
+        .def(
+            "save_index",
+            [](AsyncEngine& e, int index_id, const std::string& path) {
+                int rc;
+                {
+                    py::gil_scoped_release g;
+                    rc = m3g_save_index(e.h(), index_id, path.c_str());
+                }
+                raise_status(rc);
+            },
+            py::arg("index_id"), py::arg("path"))
+        .def(
+            "load_index",
+            [](AsyncEngine& e, int index_id, const std::string& path) {
+                int rc;
+                {
+                    py::gil_scoped_release g;
+                    rc = m3g_load_index(e.h(), index_id, path.c_str());
+                }
+                raise_status(rc);
+            },
+            py::arg("index_id"), py::arg("path"))
         .def(
             "centroids",
             [](AsyncEngine& e, int index_id) {

@@ -11,6 +11,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <chrono>
 #include <cmath>
@@ -865,6 +866,119 @@ void Engine::get_centroids(int index_id, float* out) {
     auto ix = get(index_id, "get_centroids");
     std::shared_lock lk(ix->mu);
     std::copy(ix->centroids.begin(), ix->centroids.end(), out);
+}
+
+namespace {
+// Live rows of list `cid` of an index held under its lock: ids and vectors
+// (dim floats per row) in row order.
+void live_rows(Index& ix, int cid, std::vector<int64_t>* ids, std::vector<float>* vecs) {
+    const ListMeta& L = ix.lists[(size_t)cid];
+    ids->clear();
+    vecs->clear();
+    if (L.len == 0 || L.live == 0) return;
+    std::vector<float> all((size_t)(L.len * ix.dim));
+    M3G_CK(cudaStreamSynchronize(ix.wstream));
+    M3G_CK(cudaMemcpy2D(all.data(), (size_t)ix.dim * 4, ix.vecs.p + L.off * ix.dpad,
+                        (size_t)ix.dpad * 4, (size_t)ix.dim * 4, (size_t)L.len,
+                        cudaMemcpyDeviceToHost));
+    ids->reserve((size_t)L.live);
+    vecs->reserve((size_t)(L.live * ix.dim));
+    for (int64_t r = 0; r < L.len; ++r) {
+        if (!L.alive[(size_t)r]) continue;
+        ids->push_back(L.ids[(size_t)r]);
+        vecs->insert(vecs->end(), all.begin() + r * ix.dim, all.begin() + (r + 1) * ix.dim);
+    }
+}
+
+constexpr char kIndexMagic[8] = {'M', '3', 'G', 'I', 'V', 'F', '0', '1'};
+}  // namespace
+
+void Engine::get_cluster(int index_id, int cid, int64_t* ids, float* vecs, int64_t cap,
+                         int64_t* n_live) {
+    auto ix = get(index_id, "get_cluster");
+    DeviceGuard g(device_);
+    std::shared_lock lk(ix->mu);
+    if (cid < 0 || cid >= ix->nlist()) fail(M3G_ERANGE, "get_cluster: invalid cluster_id");
+    const int64_t live = ix->lists[(size_t)cid].live;
+    if (n_live) *n_live = live;
+    if (!ids && !vecs) return;
+    if (cap < live) fail(M3G_EINVAL, "get_cluster: output capacity below the list's live rows");
+    std::vector<int64_t> i;
+    std::vector<float> v;
+    live_rows(*ix, cid, &i, &v);
+    if (ids) std::copy(i.begin(), i.end(), ids);
+    if (vecs) std::copy(v.begin(), v.end(), vecs);
+}
+
+// File layout (little-endian): 8-byte magic "M3GIVF01"; int32 dim, metric,
+// normalized, nlist; float centroids[nlist * dim]; then per list int64 n,
+// int64 ids[n], float vectors[n * dim] (the live rows, in row order).
+void Engine::save_index(int index_id, const char* path) {
+    auto ix = get(index_id, "save_index");
+    if (!path) fail(M3G_EINVAL, "save_index: path missing");
+    DeviceGuard g(device_);
+    std::shared_lock lk(ix->mu);
+    FILE* f = std::fopen(path, "wb");
+    if (!f) fail(M3G_ERUNTIME, std::string("save_index: cannot open ") + path);
+    bool ok = true;
+    auto put = [&](const void* p, size_t bytes) {
+        if (ok && bytes && std::fwrite(p, 1, bytes, f) != bytes) ok = false;
+    };
+    const int32_t hdr[4] = {ix->dim, ix->metric, ix->normalized ? 1 : 0, ix->nlist()};
+    put(kIndexMagic, sizeof(kIndexMagic));
+    put(hdr, sizeof(hdr));
+    put(ix->centroids.data(), ix->centroids.size() * 4);
+    std::vector<int64_t> ids;
+    std::vector<float> vecs;
+    for (int c = 0; c < ix->nlist() && ok; ++c) {
+        live_rows(*ix, c, &ids, &vecs);
+        const int64_t n = (int64_t)ids.size();
+        put(&n, sizeof(n));
+        put(ids.data(), ids.size() * 8);
+        put(vecs.data(), vecs.size() * 4);
+    }
+    if (std::fclose(f) != 0) ok = false;
+    if (!ok) fail(M3G_ERUNTIME, std::string("save_index: write failed: ") + path);
+}
+
+void Engine::load_index(int index_id, const char* path) {
+    if (!path) fail(M3G_EINVAL, "load_index: path missing");
+    FILE* f = std::fopen(path, "rb");
+    if (!f) fail(M3G_ERUNTIME, std::string("load_index: cannot open ") + path);
+    std::unique_ptr<FILE, int (*)(FILE*)> guard(f, std::fclose);
+    auto get_bytes = [&](void* p, size_t bytes) {
+        if (bytes && std::fread(p, 1, bytes, f) != bytes)
+            fail(M3G_ERUNTIME, std::string("load_index: truncated file: ") + path);
+    };
+    char magic[8];
+    get_bytes(magic, sizeof(magic));
+    if (std::memcmp(magic, kIndexMagic, sizeof(magic)) != 0)
+        fail(M3G_EINVAL, std::string("load_index: not an index file: ") + path);
+    int32_t hdr[4];
+    get_bytes(hdr, sizeof(hdr));
+    const int dim = hdr[0], metric = hdr[1], nlist = hdr[3];
+    if (dim <= 0 || metric < 0 || metric > 2 || nlist < 0)
+        fail(M3G_EINVAL, std::string("load_index: bad header: ") + path);
+    std::vector<float> C((size_t)nlist * dim);
+    get_bytes(C.data(), C.size() * 4);
+    // every list is read before the index is replaced, so a bad file changes nothing
+    std::vector<std::vector<int64_t>> ids((size_t)nlist);
+    std::vector<std::vector<float>> vecs((size_t)nlist);
+    for (int c = 0; c < nlist; ++c) {
+        int64_t n = 0;
+        get_bytes(&n, sizeof(n));
+        if (n < 0 || n > (int64_t(1) << 40))
+            fail(M3G_EINVAL, std::string("load_index: bad list size: ") + path);
+        ids[(size_t)c].resize((size_t)n);
+        vecs[(size_t)c].resize((size_t)n * dim);
+        get_bytes(ids[(size_t)c].data(), (size_t)n * 8);
+        get_bytes(vecs[(size_t)c].data(), (size_t)n * dim * 4);
+    }
+    create_ivf(index_id, dim, metric, hdr[2] != 0, C.data(), nlist);
+    for (int c = 0; c < nlist; ++c)
+        if (!ids[(size_t)c].empty())
+            load_cluster(index_id, c, ids[(size_t)c].data(), vecs[(size_t)c].data(),
+                         (int64_t)ids[(size_t)c].size());
 }
 
 int Engine::add_cluster(int index_id, const float* c) {

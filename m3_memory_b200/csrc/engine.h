@@ -209,6 +209,11 @@ class Engine {
     void info(int index_id, int* dim, int* metric, int* normalized, int* nlist);
     void cluster_size(int index_id, int cid, int64_t* size, int64_t* live);
     void get_centroids(int index_id, float* out);
+    // the live rows of a list, in row order; *n_live always, ids / vecs when given
+    void get_cluster(int index_id, int cid, int64_t* ids, float* vecs, int64_t cap,
+                     int64_t* n_live);
+    void save_index(int index_id, const char* path);
+    void load_index(int index_id, const char* path);
     int add_cluster(int index_id, const float* c);
     void set_centroid(int index_id, int cid, const float* c);
     void compact_cluster(int index_id, int cid);
