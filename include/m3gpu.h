@@ -90,7 +90,13 @@ int m3g_load_cluster(m3g_engine* e, int index_id, int cluster_id, const int64_t*
 /* AsyncEngine::enqueue_insert / enqueue_update / enqueue_delete
  * (m3_async.cpp:123-187; applied by writer threads as Cluster::add_batch /
  * update_batch / erase_batch, cluster.cpp:55-150).  *accepted = 0 when the
- * engine is stopped or the queue is full with block_on_full = 0. */
+ * engine is stopped or the queue is full with block_on_full = 0.
+ * Addition without a reference counterpart: an update or delete with
+ * cluster_id -1 applies to every list holding the id when the writer reaches it
+ * (so callers need not know where an id lives; the reference's backend sends
+ * every update and delete to cluster 0); ids held nowhere are ignored, and an
+ * update with cluster_id -1 cannot insert (insert_if_absent gives
+ * M3G_EINVAL; new ids go through m3g_enqueue_insert_auto). */
 int m3g_enqueue_insert(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
                        const float* vecs, int64_t n, int* accepted);
 int m3g_enqueue_update(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,

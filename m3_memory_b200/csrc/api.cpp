@@ -132,6 +132,10 @@ int enqueue_op(m3g_engine* e, m3g::WriteOp::Kind kind, int index_id, int cluster
         e->eng.info(index_id, &dim, nullptr, nullptr, nullptr);
         if (kind != m3g::WriteOp::kDelete && dim <= 0)
             m3g::fail(M3G_ERUNTIME, "enqueue: unknown index_id (call create_ivf first)");
+        if (cluster_id == m3g::kAnyList && insert_if_absent)
+            m3g::fail(M3G_EINVAL,
+                      "enqueue_update: insert_if_absent needs a cluster_id (new ids: "
+                      "enqueue_insert_auto)");
         m3g::WriteOp op;
         op.kind = kind;
         op.index_id = index_id;

@@ -710,12 +710,44 @@ void Engine::record_error(const std::string& msg, int code) {
     }
 }
 
+namespace {
+// Positions in `ids` of the ids each list holds (a live row), in op order, for
+// updates and deletes addressed to every list (cluster_id kAnyList).  Probes
+// every list's id map per id, or walks every list's map once when that is less
+// work.
+std::vector<std::vector<int64_t>> positions_by_list(const Index& ix, const std::vector<int64_t>& ids) {
+    const int L = ix.nlist();
+    std::vector<std::vector<int64_t>> pos((size_t)L);
+    const int64_t n = (int64_t)ids.size();
+    int64_t rows = 0;
+    for (const auto& m : ix.lists) rows += (int64_t)m.id2row.size();
+    if ((double)n * L <= (double)rows) {
+        for (int l = 0; l < L; ++l)
+            for (int64_t i = 0; i < n; ++i)
+                if (ix.lists[(size_t)l].id2row.count(ids[(size_t)i])) pos[(size_t)l].push_back(i);
+        return pos;
+    }
+    std::unordered_map<int64_t, std::vector<int64_t>> at;
+    for (int64_t i = 0; i < n; ++i) at[ids[(size_t)i]].push_back(i);
+    for (int l = 0; l < L; ++l) {
+        auto& p = pos[(size_t)l];
+        for (const auto& kv : ix.lists[(size_t)l].id2row) {
+            auto it = at.find(kv.first);
+            if (it != at.end()) p.insert(p.end(), it->second.begin(), it->second.end());
+        }
+        std::sort(p.begin(), p.end());
+    }
+    return pos;
+}
+}  // namespace
+
 void Engine::apply(const WriteOp& op) {
     auto ix = find(op.index_id);
     if (!ix) fail(M3G_ERANGE, "writer: index " + std::to_string(op.index_id) + " not found");
     DeviceGuard g(device_);
     std::unique_lock lk(ix->mu);
-    if (op.cluster_id < 0 || op.cluster_id >= ix->nlist()) {
+    const bool any_list = op.cluster_id == kAnyList && op.kind != WriteOp::kInsert;
+    if (!any_list && (op.cluster_id < 0 || op.cluster_id >= ix->nlist())) {
         const char* w = op.kind == WriteOp::kInsert   ? "IVFIndex::add_batch: invalid cluster_id"
                         : op.kind == WriteOp::kUpdate ? "IVFIndex::update_batch: invalid cluster_id"
                                                       : "IVFIndex::erase_batch: invalid cluster_id";
@@ -732,6 +764,28 @@ void Engine::apply(const WriteOp& op) {
             }
         }
     } refresh{*ix};
+    if (any_list) {
+        const auto pos = positions_by_list(*ix, op.ids);
+        std::vector<int64_t> sub_ids;
+        std::vector<float> sub_vecs;
+        for (int l = 0; l < ix->nlist(); ++l) {
+            const auto& p = pos[(size_t)l];
+            if (p.empty()) continue;
+            sub_ids.clear();
+            sub_vecs.clear();
+            for (int64_t i : p) {
+                sub_ids.push_back(op.ids[(size_t)i]);
+                if (op.kind == WriteOp::kUpdate)
+                    sub_vecs.insert(sub_vecs.end(), op.vecs.begin() + i * ix->dim,
+                                    op.vecs.begin() + (i + 1) * ix->dim);
+            }
+            if (op.kind == WriteOp::kUpdate)
+                list_update(*ix, l, sub_ids.data(), sub_vecs.data(), (int64_t)sub_ids.size(), false);
+            else
+                list_erase(*ix, l, sub_ids.data(), (int64_t)sub_ids.size());
+        }
+        return;
+    }
     switch (op.kind) {
         case WriteOp::kInsert:
             list_add(*ix, op.cluster_id, op.ids.data(), op.vecs.data(), n);

@@ -136,6 +136,9 @@ struct MaintenancePolicy {
     bool auto_split = false;
 };
 
+// cluster_id of an update or delete addressed to every list holding the id
+constexpr int kAnyList = -1;
+
 struct WriteOp {
     enum Kind { kInsert, kUpdate, kDelete } kind = kInsert;
     int index_id = 0, cluster_id = 0;

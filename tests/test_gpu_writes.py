@@ -141,3 +141,43 @@ def test_maintenance_compacts(cabi):
     ids, sc, cnt = e.search(0, np.zeros((1, 4), np.float32), 10, 1)
     assert sorted(ids[0, :cnt[0]].tolist()) == [5, 6, 7, 8, 9]
     e.stop()
+
+
+def test_updates_and_deletes_addressed_to_every_list(cuda_ok, oracle_mod):
+    """cluster_id -1: an update or delete applies to every list holding the id
+    (an id stored in two lists is changed in both), ids held nowhere are ignored,
+    and such an update cannot insert."""
+    from m3_memory_b200 import cabi
+
+    rng = np.random.default_rng(21)
+    L, d, per = 5, 16, 40
+    C = rng.standard_normal((L, d)).astype(np.float32)
+    e = cabi.Engine()
+    e.create_ivf(1, d, oracle_mod.IP, False, C)
+    rows = {}
+    for c in range(L):
+        ids = np.arange(c * 1000, c * 1000 + per, dtype=np.int64)
+        if c in (1, 3):
+            ids[-1] = 999  # the same id in lists 1 and 3
+        X = (C[c] + 0.3 * rng.standard_normal((per, d))).astype(np.float32)
+        e.load_cluster(1, c, ids, X)
+        rows[c] = (ids, X)
+    e.start(1, 0)
+    gone = np.array([5, 1007, 999, 4031, 123456], np.int64)  # 123456 is held nowhere
+    assert e.enqueue_delete(1, -1, gone)
+    new = np.array([2003, 3004], np.int64)
+    nv = rng.standard_normal((2, d)).astype(np.float32)
+    assert e.enqueue_update(1, -1, new, nv)
+    e.flush()
+    with pytest.raises(ValueError):
+        e.enqueue_update(1, -1, new, nv, insert_if_absent=True)
+    for c in range(L):
+        ids, X = rows[c]
+        keep = ~np.isin(ids, gone)
+        want_ids, want_X = ids[keep], X[keep].copy()
+        for i, v in zip(new, nv):
+            want_X[want_ids == i] = v
+        got_ids, got_X = e.get_cluster(1, c)
+        np.testing.assert_array_equal(got_ids, want_ids)
+        np.testing.assert_array_equal(got_X, want_X)
+    e.stop()
