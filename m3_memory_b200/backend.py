@@ -197,6 +197,9 @@ class M3Backend:
                 ids = self._ids(op.ext_ids, "DELETE_IDS requires 'ext_ids'")
                 self._eng.enqueue_delete(idx, -1, ids)
                 stored.difference_update(ids.tolist())
+                if not any(i in st for st in self._stored.values() for i in ids.tolist()):
+                    for i in ids.tolist():
+                        self._key_of.pop(i, None)
                 deleted += len(ids)
             elif kind == "FLUSH":
                 self._eng.flush()
