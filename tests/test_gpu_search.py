@@ -175,3 +175,27 @@ def test_host_query_batches_match_device_queries(cabi, oracle_mod):
         np.testing.assert_array_equal(got[2], cnt.cpu().numpy())
         np.testing.assert_array_equal(got[0], ids.cpu().numpy())
         np.testing.assert_array_equal(got[1], sc.cpu().numpy())
+
+
+@pytest.mark.parametrize("L", [5000, 9000])
+def test_many_lists_match_oracle(cabi, oracle_mod, L):
+    """Thousands of small lists (the work list's planner then takes several lists
+    per thread, within and beyond the count it keeps in registers)."""
+    rng = np.random.default_rng(L)
+    d, n, nq = 32, 30000, 64
+    C = rng.standard_normal((L, d)).astype(np.float32)
+    assign = rng.integers(0, L, n)
+    X = (C[assign] + 0.3 * rng.standard_normal((n, d))).astype(np.float32)
+    Q = (C[rng.integers(0, L, nq)] + 0.3 * rng.standard_normal((nq, d))).astype(np.float32)
+    ids = np.arange(n, dtype=np.int64) * 3
+    e = cabi.Engine()
+    e.create_ivf(1, d, oracle_mod.IP, False, C)
+    order = np.argsort(assign, kind="stable")
+    bounds = np.searchsorted(assign[order], np.arange(L + 1))
+    for c in range(L):
+        rows = order[bounds[c]:bounds[c + 1]]
+        if len(rows):
+            e.load_cluster(1, c, ids[rows], X[rows])
+    lists = oracle_mod.CsrLists.from_assign(X, ids, assign, L)
+    compare_search(e.search(1, Q, 5, 16), oracle_mod.search_nprobe(Q, C, lists, oracle_mod.IP,
+                                                                  False, 5, 16))
