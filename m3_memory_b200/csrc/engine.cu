@@ -531,6 +531,7 @@ Engine::Engine() {
     else
         num_sms_ = kDefaultNsm;
     cudaGetLastError();
+    if (const char* v = std::getenv("M3G_SEARCH_GRAPH")) graphs_off_ = std::string(v) == "0";
 }
 
 Engine::~Engine() {
@@ -543,6 +544,8 @@ Engine::~Engine() {
         std::unique_lock lk(imu_);
         indices_.clear();
     }
+    if (graph_.exec) cudaGraphExecDestroy(graph_.exec);
+    graph_.exec = nullptr;
     if (ws_.stream) {
         cudaStreamSynchronize(ws_.stream);
         cudaStreamDestroy(ws_.stream);
@@ -1171,6 +1174,64 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     last_launches_ += launches;
 }
 
+std::vector<uintptr_t> Engine::graph_key(const Index& ix, int64_t nq, int k, int P) const {
+    const Workspace& w = ws_;
+    auto u = [](const void* p) { return reinterpret_cast<uintptr_t>(p); };
+    return {u(&ix), u(ix.vecs.p), u(ix.ids.p), u(ix.alive.p), u(ix.rnorm2.p), u(ix.C.p),
+            u(ix.C3.p), u(ix.cn.p), u(ix.cn2.p), u(ix.d_list_off.p), u(ix.d_list_len.p),
+            u(ix.d_list_order.p), (uintptr_t)ix.arena_cap, (uintptr_t)ix.nlist(),
+            (uintptr_t)ix.dim, (uintptr_t)ix.dpad, (uintptr_t)ix.metric,
+            (uintptr_t)ix.normalized, (uintptr_t)ix.maps_valid, (uintptr_t)nq, (uintptr_t)k,
+            (uintptr_t)P, u(w.Q.p), u(w.Q3.p), u(w.S.p), u(w.qn.p), u(w.qn2.p), u(w.probes.p),
+            u(w.lcount.p), u(w.lstart.p), u(w.lcursor.p), u(w.items.p), u(w.n_items.p),
+            u(w.item_counter.p), u(w.pair_q.p), u(w.pair_slot.p), u(w.part_score.p),
+            u(w.part_row.p), u(w.out_ids.p), u(w.out_scores.p), u(w.out_counts.p), u(w.err.p),
+            (uintptr_t)use_tc_scan(), (uintptr_t)use_tc_gemm()};
+}
+
+// Replays (capturing first when the key changed) run_search on ws_.Q into
+// ws_.out_* on stream st.  False when graphs are off or a capture failed (the
+// caller then runs the kernels directly).
+bool Engine::run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t st) {
+    if (graphs_off_) return false;
+    auto key = graph_key(ix, nq, k, P);
+    if (!graph_.exec || graph_.key != key) {
+        if (graph_.exec) cudaGraphExecDestroy(graph_.exec);
+        graph_.exec = nullptr;
+        graph_.key.clear();
+        // captured on the engine's own stream (a caller's stream may be the legacy
+        // default stream, which cannot be captured); launched on the caller's
+        const int32_t launches = last_launches_;
+        cudaGraph_t g = nullptr;
+        bool ok = cudaStreamBeginCapture(ws_.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+        if (ok) {
+            try {
+                run_search(ix, ws_.Q.p, ix.dpad, nq, k, P, nullptr, ws_.out_ids.p,
+                           ws_.out_scores.p, ws_.out_counts.p, ws_.stream, false);
+            } catch (...) {
+                ok = false;
+            }
+            if (cudaStreamEndCapture(ws_.stream, &g) != cudaSuccess) ok = false;
+        }
+        if (ok && g) ok = cudaGraphInstantiate(&graph_.exec, g, 0) == cudaSuccess;
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();  // a failed capture leaves no error behind
+        if (!ok || !graph_.exec) {
+            graph_.exec = nullptr;
+            graphs_off_ = true;
+            last_launches_ = launches;
+            return false;
+        }
+        graph_.key = std::move(key);
+    } else {
+        // the kernels a replay runs, for the caller's accounting
+        last_launches_ += 1 + (P >= ix.nlist() ? 1 : (use_tc_gemm() ? 3 : 2)) + 3 +
+                          (ix.maps_valid ? 1 : 0) + 1;
+    }
+    M3G_CK(cudaGraphLaunch(graph_.exec, st));
+    return true;
+}
+
 namespace {
 struct WsSizes {
     int64_t nq, L, P, k, dpad;
@@ -1298,9 +1359,16 @@ void Engine::search(int index_id, const float* Q, int64_t nq, int k, int nprobe,
     const bool direct_q = q_dev && ix->dpad == ix->dim && (reinterpret_cast<uintptr_t>(Q) & 15u) == 0;
     for (int64_t q0 = 0; q0 < nq; q0 += ch) {
         const int64_t m = std::min(ch, nq - q0);
+        // one chunk without stage events: replayed as a CUDA graph (queries staged
+        // in ws_.Q, answers copied out of ws_.out_*)
+        const bool graph = m == nq && !profile && ix->maps_valid && !graphs_off_;
         const float* dQ;
-        if (direct_q) {
+        if (direct_q && !graph) {
             dQ = Q + q0 * ix->dim;
+        } else if (direct_q) {
+            M3G_CK(cudaMemcpyAsync(ws_.Q.p, Q + q0 * ix->dim, (size_t)(m * ix->dim) * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+            dQ = ws_.Q.p;
         } else {
             const cudaMemcpyKind kind = q_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
             if (ix->dpad != ix->dim) {
@@ -1313,6 +1381,13 @@ void Engine::search(int index_id, const float* Q, int64_t nq, int k, int nprobe,
                                        st));
             }
             dQ = ws_.Q.p;
+        }
+        if (graph && run_search_graph(*ix, m, k, P, st)) {
+            const cudaMemcpyKind kind = out_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+            M3G_CK(cudaMemcpyAsync(out_ids + q0 * k, ws_.out_ids.p, (size_t)(m * k) * 8, kind, st));
+            M3G_CK(cudaMemcpyAsync(out_scores + q0 * k, ws_.out_scores.p, (size_t)(m * k) * 4, kind, st));
+            M3G_CK(cudaMemcpyAsync(out_counts + q0, ws_.out_counts.p, (size_t)m * 4, kind, st));
+            continue;
         }
         int64_t* oi = out_dev ? out_ids + q0 * k : ws_.out_ids.p;
         float* os = out_dev ? out_scores + q0 * k : ws_.out_scores.p;

@@ -281,6 +281,17 @@ class Engine {
     int64_t prof_row_bytes_ = 0, prof_dim_ = 0;
     int32_t last_launches_ = 0;  // kernels the last search call launched
     cudaStream_t prof_stream_ = nullptr;
+
+    // The search pipeline of one batch shape captured as a CUDA graph (queries in
+    // ws_.Q, answers in ws_.out_*), replayed while nothing it baked in changes:
+    // every pointer and size its kernels were given is part of the key.
+    struct SearchGraph {
+        std::vector<uintptr_t> key;
+        cudaGraphExec_t exec = nullptr;
+    } graph_;
+    bool graphs_off_ = false;  // set when a capture failed, or by M3G_SEARCH_GRAPH=0
+    std::vector<uintptr_t> graph_key(const Index& ix, int64_t nq, int k, int P) const;
+    bool run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t st);
 };
 
 // Exact top-nprobe selection with its scratch in a fixed device array

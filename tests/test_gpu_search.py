@@ -199,3 +199,38 @@ def test_many_lists_match_oracle(cabi, oracle_mod, L):
     lists = oracle_mod.CsrLists.from_assign(X, ids, assign, L)
     compare_search(e.search(1, Q, 5, 16), oracle_mod.search_nprobe(Q, C, lists, oracle_mod.IP,
                                                                   False, 5, 16))
+
+
+def test_graph_replay_matches_direct_launches(cabi, oracle_mod):
+    """A search batch shape is captured once as a CUDA graph and replayed; the
+    answers equal those of the directly launched kernels (the stage-timed path),
+    also after the index's lists change between replays."""
+    rng = np.random.default_rng(8)
+    L, d = 64, 96
+    C = rng.standard_normal((L, d)).astype(np.float32)
+    assign = rng.integers(0, L, 6000)
+    X = (C[assign] + 0.4 * rng.standard_normal((6000, d))).astype(np.float32)
+    e = cabi.Engine()
+    e.create_ivf(1, d, oracle_mod.IP, False, C)
+    for c in range(L):
+        rows = np.flatnonzero(assign == c)
+        e.load_cluster(1, c, rows.astype(np.int64), X[rows])
+    Q = (C[rng.integers(0, L, 300)] + 0.4 * rng.standard_normal((300, d))).astype(np.float32)
+
+    def direct():
+        e.set_profiling(True)
+        try:
+            return e.search(1, Q, 10, 8)
+        finally:
+            e.set_profiling(False)
+
+    for step in range(2):
+        want = direct()
+        for _ in range(3):  # capture, then replays
+            got = e.search(1, Q, 10, 8)
+            for w, x in zip(want, got):
+                np.testing.assert_array_equal(x, w)
+        # change two lists' contents between replays
+        for c in (3, 5):
+            rows = np.flatnonzero(assign == c)[: 10 + step]
+            e.load_cluster(1, c, rows.astype(np.int64) + 100000, X[rows] * 1.5)
