@@ -8,11 +8,11 @@
 // Arithmetic.  <x, q> in fp32 accuracy from four bf16 MMAs per 32-dim chunk
 // (tcgen05.mma kind::f16, K = 16, fp32 accumulation in TMEM): each fp32 value
 // is split into two bf16 halves, x = x_hi + x_lo + e with x_hi = bf16(x),
-// x_lo = bf16(x - x_hi) (round to nearest), |e| <= 2^-18 |x|, and likewise q.
+// x_lo = bf16(x - x_hi) (round to nearest), |e| <= 2^-17 |x|, and likewise q.
 //   x_hi . [q_hi | q_lo]   N = 2 nq_pad
 //   x_lo . [q_hi | q_lo]   N = 2 nq_pad, into the same columns
 // Every bf16 x bf16 product is exact in fp32; the column groups add up to
-// (x_hi + x_lo)(q_hi + q_lo), within ~2^-17 of each product x_i q_i.  The
+// (x_hi + x_lo)(q_hi + q_lo), within 2^-16 of each product x_i q_i.  The
 // split warps convert each landed fp32 stage in place: a row's 128 bytes (32
 // fp32 dims) become 64 bytes of x_hi and 64 bytes of x_lo, so the tensor core
 // reads 16 KB per 128-row block and chunk (the fp32 data itself is never an
