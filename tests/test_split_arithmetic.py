@@ -56,3 +56,19 @@ def test_products_of_split_operands():
         for b in (qh, ql):
             p64 = a.astype(np.float64) * b.astype(np.float64)
             assert np.all(p64.astype(np.float32).astype(np.float64) == p64)
+
+
+def test_coarse_gemm_three_products():
+    """The coarse GEMM's operands [hi | hi | lo] . [hi | lo | hi] leave out lo lo
+    (|lo| <= 2^-8 |x|): hi hi + hi lo + lo hi is within 2^-16 + 2 * 2^-17 (+2^-34)
+    of x q, inside the 3.02 * 2^-16 its error bound allows for representation."""
+    rng = np.random.default_rng(2)
+    x, q = sample(rng, 1 << 20), sample(rng, 1 << 20)
+    xh, xl = split(x)
+    qh, ql = split(q)
+    f = lambda a: a.astype(np.float64)  # noqa: E731
+    exact = f(x) * f(q)
+    three = f(xh) * f(qh) + f(xh) * f(ql) + f(xl) * f(qh)
+    bound = (2.0 ** -16 + 2 * 2.0 ** -17 + 2.0 ** -34) * np.abs(exact)
+    assert np.all(np.abs(three - exact) <= bound)
+    assert 2.0 ** -16 + 2 * 2.0 ** -17 + 2.0 ** -34 <= 3.02 * 2.0 ** -16
