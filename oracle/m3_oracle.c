@@ -286,6 +286,105 @@ int orc_kmeans_train(const float* X, int64_t n, int d, int metric, int normalize
     return 0;
 }
 
+/* The GEMM estimate of one unified score and its error bound (see below). */
+static inline void orc_interval(int metric, float s, double xi, double ci, double g, double g3,
+                                double* est, double* e) {
+    const double u = 1.0 / 16777216.0;
+    const double e0 = 2.0 * g * xi * ci;
+    if (metric == ORC_IP) {
+        *est = -(double)s;
+        *e = e0;
+    } else if (metric == ORC_COSINE) {
+        *est = 1.0 - (double)s;
+        *e = e0 + 1.01 * u * (fabs(*est) + e0);
+    } else {
+        *est = xi * xi + ci * ci - 2.0 * (double)s;
+        *e = 2.0 * e0 + g3 * (fabs(*est) + 2.0 * e0) + 4.0 * u * u * (xi * xi + ci * ci);
+    }
+}
+
+/* The nearest_clusters rule above (strict '<', lowest id on exact ties) for large
+ * inputs, given S[n, nlist] = X C^T from any fp32 GEMM (BLAS: any summation order,
+ * FMA or not).  For every row the GEMM's estimate of each unified score is within
+ * a rigorous bound e_c of the exact score; only the centroids whose interval
+ * [est_c - e_c, est_c + e_c] reaches below the smallest upper bound can be the
+ * argmin, and when there is more than one they are rescored exactly with
+ * orc_score (the reference's own arithmetic) and compared as nearest_clusters
+ * does.  The result therefore equals orc_nearest_clusters bit for bit.
+ *
+ * Bound (u = 2^-24, D = d): any fp32 sum of D rounded products is within
+ * gamma_D sum|x_i c_i| <= gamma_D |x| |c| of the exact dot product, for the
+ * reference's sequential order and for the GEMM's alike, so the two differ by
+ * at most 2 gamma_D |x| |c| (gamma_D = D u / (1 - D u)).  COSINE (normalized):
+ * fl(1 - s) adds u |1 - s|.  L2: |x|^2 + |c|^2 - 2 s differs from the exact sum
+ * of squares by 2 gamma_D |x||c| (plus the fp64 terms), and the reference's own
+ * sum of rounded squared differences is within gamma_{D+3} of it.
+ * xn / cn are the fp64 norms |x|, |c|.  Metric COSINE without normalisation is
+ * not covered (returns -1); call orc_nearest_clusters for it. */
+int orc_assign_prefiltered(const float* S, const float* X, int64_t n, const float* C, int nlist,
+                           int d, int metric, int normalized, const double* xn, const double* cn,
+                           int32_t* out, int64_t* n_rescored) {
+    if (metric == ORC_COSINE && !normalized) return -1;
+    const double u = 1.0 / 16777216.0;
+    const double g = 1.01 * (double)d * u / (1.0 - (double)d * u);
+    const double g3 = 1.01 * (double)(d + 3) * u / (1.0 - (double)(d + 3) * u);
+    int64_t rescored = 0;
+#pragma omp parallel for schedule(dynamic, 64) reduction(+ : rescored)
+    for (int64_t i = 0; i < n; ++i) {
+        const float* s = S + (size_t)i * nlist;
+        const double xi = xn[i];
+        /* pass 1: the smallest upper bound */
+        double ub = INFINITY;
+        for (int c = 0; c < nlist; ++c) {
+            double est, e;
+            orc_interval(metric, s[c], xi, cn[c], g, g3, &est, &e);
+            if (est + e < ub) ub = est + e;
+        }
+        /* pass 2: candidates in ascending id order; the first one found is kept
+         * unless an exact rescoring is needed */
+        int32_t first = -1;
+        int many = 0;
+        for (int c = 0; c < nlist && !many; ++c) {
+            double est, e;
+            orc_interval(metric, s[c], xi, cn[c], g, g3, &est, &e);
+            if (est - e <= ub) {
+                if (first < 0) first = c;
+                else many = 1;
+            }
+        }
+        if (!many) {
+            out[i] = first;
+            continue;
+        }
+        /* exact rescoring of every candidate, nearest_clusters' strict '<' */
+        ++rescored;
+        float best = INFINITY;
+        int32_t bid = -1;
+        for (int c = 0; c < nlist; ++c) {
+            double est, e;
+            orc_interval(metric, s[c], xi, cn[c], g, g3, &est, &e);
+            if (est - e > ub) continue;
+            const float sc = orc_score(X + (size_t)i * d, C + (size_t)c * d, d, metric, normalized);
+            if (sc < best) {
+                best = sc;
+                bid = c;
+            }
+        }
+        out[i] = bid;
+    }
+    if (n_rescored) *n_rescored = rescored;
+    return 0;
+}
+
+/* Exact unified scores of n (row, centroid) pairs: out[j] = orc_score(X[rows[j]],
+ * C[cols[j]]).  Threaded over the pairs. */
+void orc_score_pairs(const float* X, const int64_t* rows, const float* C, const int32_t* cols,
+                     int64_t n, int d, int metric, int normalized, float* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t j = 0; j < n; ++j)
+        out[j] = orc_score(X + (size_t)rows[j] * d, C + (size_t)cols[j] * d, d, metric, normalized);
+}
+
 /* Two-means split of one list's live rows (rows in list order): the init rows are
  * orc_sample_rows(seed, n, 2); then niter E/M steps as above; out_assign gets the
  * final side (0 or 1) of each row.  Returns -1 when n < 2. */

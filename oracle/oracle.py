@@ -26,7 +26,9 @@ HERE = Path(__file__).resolve().parent
 REF_DIR = HERE / "_ref"
 C_LIB = REF_DIR / "liboracle_c.so"
 REF_LIB = REF_DIR / "liboracle_ref.so"
-REFERENCE_ROOT = Path(os.environ.get("M3_REFERENCE_ROOT", "/root/reference"))
+# The reference checkout: $M3_REFERENCE_ROOT, else a `reference` directory beside
+# this repository's checkout.
+REFERENCE_ROOT = Path(os.environ.get("M3_REFERENCE_ROOT", str(HERE.parent.parent / "reference")))
 
 L2, IP, COSINE = 0, 1, 2
 
@@ -34,6 +36,7 @@ _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
 
 
 def build(ref: bool | None = None) -> None:
@@ -83,6 +86,13 @@ def clib():
         lib.orc_kmeans_train.restype = ct.c_int
         lib.orc_kmeans_train.argtypes = [_f32p, ct.c_int64, ct.c_int, ct.c_int, ct.c_int,
                                          ct.c_int, ct.c_int, ct.c_uint64, _f32p, _i32p]
+        lib.orc_assign_prefiltered.restype = ct.c_int
+        lib.orc_assign_prefiltered.argtypes = [_f32p, _f32p, ct.c_int64, _f32p, ct.c_int,
+                                               ct.c_int, ct.c_int, ct.c_int, _f64p, _f64p, _i32p,
+                                               ct.POINTER(ct.c_int64)]
+        lib.orc_score_pairs.restype = None
+        lib.orc_score_pairs.argtypes = [_f32p, _i64p, _f32p, _i32p, ct.c_int64, ct.c_int,
+                                        ct.c_int, ct.c_int, _f32p]
         lib.orc_split_2means.restype = ct.c_int
         lib.orc_split_2means.argtypes = [_f32p, ct.c_int64, ct.c_int, ct.c_int, ct.c_int,
                                          ct.c_int, ct.c_uint64, _f32p, _i32p]
@@ -462,6 +472,73 @@ def kmeans_train(X, nlist, niter, seed, metric, normalized):
     if rc:
         raise ValueError("kmeans_train: nlist must be in [1, n]")
     return C, a
+
+
+def _norms64(A, block=1 << 16):
+    out = np.empty(A.shape[0], np.float64)
+    for b in range(0, A.shape[0], block):
+        a = A[b:b + block].astype(np.float64)
+        out[b:b + block] = np.sqrt(np.einsum("ij,ij->i", a, a))
+    return out
+
+
+def nearest_clusters_fast(X, C, metric, normalized, block=8192, stats=None):
+    """``nearest_clusters`` (strict '<', lowest id on exact ties) for large inputs:
+    an fp32 BLAS product X C^T proposes, a rigorous error bound keeps every
+    centroid that could be the argmin, and those are rescored in the reference's
+    own arithmetic (``orc_assign_prefiltered``).  Equal to ``nearest_clusters``
+    bit for bit; COSINE without normalisation falls back to it."""
+    X, C = _f32(X), _f32(C)
+    if metric == COSINE and not normalized:
+        return nearest_clusters(X, C, metric, normalized)
+    n, d = X.shape
+    out = np.empty(n, np.int32)
+    if C.shape[0] == 0:
+        out[:] = -1
+        return out
+    cn = _norms64(C)
+    Ct = np.ascontiguousarray(C.T)
+    resc = ct.c_int64()
+    total = 0
+    for b in range(0, n, block):
+        Xb = X[b:b + block]
+        S = np.ascontiguousarray(Xb @ Ct, dtype=np.float32)
+        rc = clib().orc_assign_prefiltered(S.reshape(-1), Xb.reshape(-1), Xb.shape[0],
+                                           C.reshape(-1), C.shape[0], d, metric,
+                                           int(normalized), _norms64(Xb), cn, out[b:b + block],
+                                           ct.byref(resc))
+        if rc:
+            raise ValueError("orc_assign_prefiltered: unsupported metric")
+        total += resc.value
+    if stats is not None:
+        stats["rescored_rows"] = total
+    return out
+
+
+def score_pairs(X, rows, C, cols, metric, normalized):
+    """Exact unified scores of the pairs (X[rows[j]], C[cols[j]])."""
+    X, C = _f32(X), _f32(C)
+    rows = _i64(rows)
+    cols = np.ascontiguousarray(cols, np.int32)
+    out = np.empty(rows.shape[0], np.float32)
+    clib().orc_score_pairs(X.reshape(-1), rows, C.reshape(-1), cols, rows.shape[0], X.shape[1],
+                           metric, int(normalized), out)
+    return out
+
+
+def kmeans_train_fast(X, nlist, niter, seed, metric, normalized):
+    """``kmeans_train`` with the E-steps done by ``nearest_clusters_fast``: the same
+    procedure (seeded init rows, exact assignment, fp64 row-order means, final
+    assignment), so the same centroids and assignment bit for bit, at BLAS speed."""
+    X = _f32(X)
+    n, d = X.shape
+    if nlist <= 0 or nlist > n:
+        raise ValueError("kmeans_train: nlist must be in [1, n]")
+    C = np.ascontiguousarray(X[sample_rows(seed, n, nlist)])
+    for _ in range(niter):
+        a = nearest_clusters_fast(X, C, metric, normalized)
+        C = kmeans_update(X, a, C)
+    return C, nearest_clusters_fast(X, C, metric, normalized)
 
 
 def split_2means(X, niter, seed, metric, normalized):

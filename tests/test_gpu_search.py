@@ -121,31 +121,6 @@ def test_odd_dimension_and_small_k(cabi, oracle_mod):
         compare_search(e.search(0, Q, k, p), O.search_nprobe(Q, C, lists, O.L2, False, k, p))
 
 
-def test_config1_shape_subset(cabi, oracle_mod):
-    """100k x 1024 unit-norm COSINE, nlist 256, nprobe 16, k 10 (the CPU-runnable
-    configuration): full batch on the GPU; 150 queries checked against the oracle,
-    all 1000 for size-independent properties."""
-    O = oracle_mod
-    from m3_memory_b200 import synthetic as S
-
-    rng = np.random.default_rng(0)
-    X = S.unit_gaussian(100_000, 1024, rng)
-    Q = S.unit_gaussian(1000, 1024, rng)
-    e = cabi.Engine()
-    ids = np.arange(100_000, dtype=np.int64)
-    C = e.train_ivf(1, 1024, O.COSINE, True, ids, X, 256, 2, 0)
-    got = e.search(1, Q, 10, 16)
-    assert (got[2] == 10).all()
-    assert (np.diff(got[1], axis=1) >= 0).all()
-    assert ((got[0] >= 0) & (got[0] < 100_000)).all()
-    # reference side: lists from the GPU's own assignment (bit-exact with the oracle's)
-    a = e.nearest_clusters(1, X)
-    lists = O.CsrLists.from_assign(X, ids, a, 256)
-    sub = np.arange(0, 1000, 7)[:150]
-    compare_search((got[0][sub], got[1][sub], got[2][sub]),
-                   O.search_nprobe(Q[sub], C, lists, O.COSINE, True, 10, 16))
-
-
 def test_host_query_batches_match_device_queries(cabi, oracle_mod):
     """The host-buffer search (queries copied into the engine's workspace, results
     copied back) gives the device-query path's answers bit for bit, on

@@ -124,3 +124,36 @@ def test_engine_default_nprobe(oracle_mod, have_ref):
         eng.set_search_policy(dn)
         compare_search(eng.search(1, Q, 10, 0),
                        O.search_nprobe(Q, C, lists, O.L2, False, 10, dn), exact=True)
+
+
+@pytest.mark.parametrize("metric,normalized", [(1, False), (2, True), (0, False)])
+def test_fast_assignment_equals_exact(oracle_mod, metric, normalized):
+    """The BLAS-proposed, bound-filtered, exactly rescored assignment equals the
+    plain nearest_clusters rule bit for bit, also with exact duplicate centroids
+    (ties to the lower id) and near-duplicates inside the error bound."""
+    O = oracle_mod
+    rng = np.random.default_rng(40 + metric)
+    d = 200
+    means = rng.standard_normal((6, d)).astype(np.float32)
+    X = (means[rng.integers(0, 6, 4000)] + 0.3 * rng.standard_normal((4000, d))).astype(np.float32)
+    C = X[rng.choice(4000, 150, replace=False)].copy()
+    C[60] = C[7]
+    C[61] = np.nextafter(C[7], np.float32(np.inf))
+    X[:20] = C[7]
+    if normalized:
+        X /= np.linalg.norm(X, axis=1, keepdims=True)
+        C /= np.linalg.norm(C, axis=1, keepdims=True)
+    stats = {}
+    got = O.nearest_clusters_fast(X, C, metric, normalized, block=1024, stats=stats)
+    np.testing.assert_array_equal(got, O.nearest_clusters(X, C, metric, normalized))
+    assert stats["rescored_rows"] >= 20  # the rows sitting on the duplicated centroid
+
+
+@pytest.mark.parametrize("case", KMEANS_CASES)
+def test_fast_kmeans_equals_restatement(oracle_mod, case):
+    O = oracle_mod
+    g = load_golden(case)
+    C, a = O.kmeans_train_fast(g["X"], int(g["nlist"]), int(g["niter"]), int(g["seed"]),
+                               int(g["metric"]), bool(g["normalized"]))
+    np.testing.assert_array_equal(C, g["C"])
+    np.testing.assert_array_equal(a, g["assign"])
