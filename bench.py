@@ -5,9 +5,13 @@ list scan's HBM bandwidth.
 Workload (one step = one search batch): 1M fp32 unit-norm vectors, dim 1024,
 from a 1,000-component Gaussian mixture (component means N(0, I) normalised,
 per-point noise sigma = 0.3 in norm, renormalised; seeded synthetic data, no
-dataset), inner-product metric, nlist = 4096 lists trained by k-means on the
-GPU (10 iterations, seeded random init), nprobe = 32, k = 10, 10 batches of
-1,024 queries from the same mixture, one batch per step.
+dataset), inner-product metric, nlist = 4096 lists by k-means (10 iterations,
+seeded random init, exact assignment) on a seeded 262,144-row sample (64 rows
+per list), then every row assigned to its nearest centroid; nprobe = 32,
+k = 10, 10 batches of 1,024 queries from the same mixture, one batch per step.
+Both arms build this same index (bit for bit: the k-means and the assignment
+follow the reference's nearest_clusters rule exactly) and print its
+fingerprint.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -47,6 +51,7 @@ K = 10
 BATCH = 1024
 NBATCH = 10
 KMEANS_ITERS = 10
+KMEANS_SAMPLE = 262_144  # k-means training rows (64 per list), a seeded sample
 SEED = 0
 METRIC_IP = 1
 WORKLOAD = (f"ivf-search: {N_VEC // 1_000_000}M x {DIM} fp32 unit-norm mixture({NCOMP}), "
@@ -75,6 +80,30 @@ def keep_stdout_for_result():
     sys.stdout.flush()
     _RESULT_OUT = os.fdopen(os.dup(1), "w")
     os.dup2(2, 1)
+
+
+def kmeans_sample():
+    """The seeded k-means training rows (ascending row order), the same in both arms."""
+    m = min(N_VEC, KMEANS_SAMPLE)
+    return np.sort(np.random.default_rng(SEED + 1).choice(N_VEC, m, replace=False))
+
+
+def bench_config(nprobe):
+    """The workload as both arms name it (identical by construction)."""
+    return {"workload": WORKLOAD, "n_vectors": N_VEC, "dim": DIM, "nlist": NLIST,
+            "nprobe": nprobe, "k": K, "batch": BATCH, "metric": "inner product",
+            "kmeans": (f"{KMEANS_ITERS} iterations, seeded random init, exact assignment, on a "
+                       f"seeded {min(N_VEC, KMEANS_SAMPLE)}-row sample; every row then assigned "
+                       "to its nearest centroid"),
+            "l2_flush": "not needed: each step streams ~4 GB of lists (> 126 MB L2)"}
+
+
+def index_fingerprint(C, assign):
+    import hashlib
+
+    h = hashlib.sha256(np.ascontiguousarray(C, np.float32).tobytes())
+    h.update(np.ascontiguousarray(assign, np.int32).tobytes())
+    return h.hexdigest()[:16]
 
 
 def make_data():
@@ -203,31 +232,77 @@ def recall_at_k(found_ids, exact_ids, k):
     return hit / (len(found_ids) * k)
 
 
-def cpu_reference_qps(C, X, assign, Q_all, threads, target_s=12.0, warm_q=None):
-    """The reference core's IVFIndex::search_nprobe on the host: returns
-    (qps, sample description)."""
+def ref_index_of(C, X, assign):
+    """The reference core's IVFIndex holding the given centroids and lists (rows of a
+    list in ascending row order, ids = row numbers)."""
     from oracle import oracle as O
 
     ref = O.RefIndex(DIM, METRIC_IP, False)
     ref.set_centroids(C)
     order = np.argsort(assign, kind="stable")
     bounds = np.searchsorted(assign[order], np.arange(NLIST + 1))
-    ids = np.arange(len(X), dtype=np.int64)
     for c in range(NLIST):
         b, e = bounds[c], bounds[c + 1]
         if e > b:
             rows = order[b:e]
-            ref.rebuild_cluster(c, ids[rows], X[rows])
+            ref.rebuild_cluster(c, rows.astype(np.int64), X[rows])
+    return ref
+
+
+def cpu_reference_qps(ref, Q_all, nprobe, threads, target_s=12.0):
+    """The reference core's IVFIndex::search_nprobe on the host over a bounded sample
+    of the queries: returns (qps, sample description, the queries' row numbers, the
+    reference's answers (ids, scores, counts))."""
     Qf = Q_all.reshape(-1, DIM)
     probe = Qf[: max(threads, 1) * 2]
     t0 = time.perf_counter()
-    ref.search_nprobe(probe, K, NPROBE, threads=threads)
+    ref.search_nprobe(probe, K, nprobe, threads=threads)
     rate = len(probe) / max(time.perf_counter() - t0, 1e-6)
     n = int(min(len(Qf), max(threads, rate * target_s)))
     t0 = time.perf_counter()
-    ref.search_nprobe(Qf[:n], K, NPROBE, threads=threads)
+    ans = ref.search_nprobe(Qf[:n], K, nprobe, threads=threads)
     dt = time.perf_counter() - t0
-    return n / dt, f"{n} of the {len(Qf)} queries, search_nprobe split over {threads} threads"
+    return (n / dt, f"{n} of the {len(Qf)} queries, search_nprobe split over {threads} threads",
+            np.arange(n), ans)
+
+
+def parity_vs_reference(got, want):
+    """Our answers against the reference core's for the same queries on the same
+    index: recall of its ids, the largest relative score difference over the ids
+    both return, and how many queries' id lists are identical."""
+    g_ids, g_sc, g_cnt = got
+    r_ids, r_sc, r_cnt = want
+    hit = tot = same = 0
+    err = 0.0
+    for q in range(len(r_cnt)):
+        c = int(r_cnt[q])
+        rmap = dict(zip(r_ids[q, :c].tolist(), r_sc[q, :c].tolist()))
+        gi = g_ids[q, :int(g_cnt[q])].tolist()
+        same += int(gi == r_ids[q, :c].tolist())
+        for i, sc in zip(gi, g_sc[q, :len(gi)].tolist()):
+            if i in rmap:
+                hit += 1
+                err = max(err, abs(sc - rmap[i]) / max(abs(rmap[i]), 1e-6))
+        tot += c
+    return {"recall_vs_reference": hit / max(tot, 1), "max_rel_score_err": err,
+            "n_queries": int(len(r_cnt)), "identical_id_lists": same,
+            "counts_equal": bool(np.array_equal(g_cnt, r_cnt)),
+            "bar": "recall >= 0.999, relative score error <= 1e-3"}
+
+
+def exact_topk_ip_host(X, Q, k, block=1 << 17):
+    """Exact top-k ids by inner product on the host (fp32 BLAS), for the recall of
+    the reference arm."""
+    best_s = np.full((len(Q), k), -np.inf, np.float32)
+    best_i = np.zeros((len(Q), k), np.int64)
+    for b in range(0, len(X), block):
+        s = Q @ X[b:b + block].T
+        i = np.argpartition(-s, k - 1, axis=1)[:, :k]
+        v = np.take_along_axis(s, i, 1)
+        cs, ci = np.concatenate([best_s, v], 1), np.concatenate([best_i, i + b], 1)
+        o = np.argpartition(-cs, k - 1, axis=1)[:, :k]
+        best_s, best_i = np.take_along_axis(cs, o, 1), np.take_along_axis(ci, o, 1)
+    return best_i
 
 
 # ---------------------------------------------------------------- reference arm
@@ -247,64 +322,44 @@ def run_reference(args, rank, world):
                              "was not built on this box"})
         return
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    t_setup = time.perf_counter()
     X, Qb = make_data()
-    # Index for the reference arm, built on the host without the GPU engine:
-    # k-means init rows (the same seeded sampler), 2 Lloyd rounds with BLAS.
-    C = X[O.sample_rows(SEED, N_VEC, NLIST)].copy()
-    step = 1 << 16
+    # The same index as the GPU arm, built on the host without the GPU engine: the
+    # same k-means (seeded init rows, exact nearest_clusters assignment, fp64
+    # row-order means) with its E-steps proposed by host BLAS and settled in the
+    # reference's own arithmetic wherever the BLAS bound leaves two candidates.
+    C, _ = O.kmeans_train_fast(X[kmeans_sample()], NLIST, KMEANS_ITERS, SEED, METRIC_IP, False)
+    assign = O.nearest_clusters_fast(X, C, METRIC_IP, False)
+    ref = ref_index_of(C, X, assign)
+    log(f"[reference] index built on the host in {time.perf_counter() - t_setup:.1f}s")
+    nprobe = NPROBE
+    found = []
 
-    def assign_of(C):
-        a = np.empty(N_VEC, np.int32)
-        for b in range(0, N_VEC, step):
-            a[b:b + step] = np.argmax(X[b:b + step] @ C.T, axis=1)
-        return a
+    def one_step(i):
+        ids, _, _ = ref.search_nprobe(Qb[i % NBATCH], K, nprobe, threads=threads)
+        found.append((i % NBATCH, ids))
 
-    from scipy import sparse
-
-    for _ in range(2):
-        a = assign_of(C)
-        onehot = sparse.csr_matrix((np.ones(N_VEC, np.float32), (a, np.arange(N_VEC))),
-                                   shape=(NLIST, N_VEC))
-        sums = np.asarray(onehot @ X)
-        cnt = np.bincount(a, minlength=NLIST)
-        nz = cnt > 0
-        C[nz] = (sums[nz] / cnt[nz, None]).astype(np.float32)
-    a = assign_of(C)
-    ref = O.RefIndex(DIM, METRIC_IP, False)
-    ref.set_centroids(C)
-    order = np.argsort(a, kind="stable")
-    bounds = np.searchsorted(a[order], np.arange(NLIST + 1))
-    ids = np.arange(N_VEC, dtype=np.int64)
-    for c in range(NLIST):
-        b, e = bounds[c], bounds[c + 1]
-        if e > b:
-            rows = order[b:e]
-            ref.rebuild_cluster(c, ids[rows], X[rows])
-    Qf = Qb.reshape(-1, DIM)
-    per_step = max(threads * 4, 16)
-    pos = 0
-
-    def one_step():
-        nonlocal pos
-        q = np.take(Qf, np.arange(pos, pos + per_step) % len(Qf), axis=0)
-        pos += per_step
-        ref.search_nprobe(q, K, NPROBE, threads=threads)
-
-    for _ in range(args.warmup):
-        one_step()
+    for w in range(args.warmup):
+        one_step(w)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        one_step()
+    for i in range(args.steps):
+        one_step(i)
     dt = time.perf_counter() - t0
-    qps = per_step * args.steps / dt
-    sample = f"{per_step} queries per step over {threads} host threads"
+    qps = BATCH * args.steps / dt
+    exact = exact_topk_ip_host(X, Qb[0], K)
+    b0 = [ids for b, ids in found if b == 0][0]
+    recall = recall_at_k(b0, exact, K)
+    sample = f"{BATCH} queries (one full batch) per step over {threads} host threads"
     emit({
         "impl": "reference", "metric": "search QPS at recall@10>=0.95 (IVF, dim 1024)",
         "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "nq_per_step": per_step,
-                   "index": "host k-means (2 Lloyd rounds, BLAS) -- setup only"},
+        "config": bench_config(nprobe),
+        "recall_at_10": recall,
+        "index": {"fingerprint": index_fingerprint(C, assign),
+                  "built": "host: BLAS-proposed exact k-means + assignment (setup, untimed)"},
+        "parallelism": f"IVFIndex::search_nprobe, queries split over {threads} host threads",
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads,
                          "kind": "reference", "sample": sample},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0,
@@ -328,11 +383,13 @@ def run_ours(args, rank, world, local_rank):
     eng = cabi.Engine()
     ids = np.arange(N_VEC, dtype=np.int64)
     t0 = time.perf_counter()
-    C, assign = eng.kmeans(X, NLIST, KMEANS_ITERS, SEED, METRIC_IP, False)
-    log(f"[rank {rank}] k-means {KMEANS_ITERS} it on the GPU: {time.perf_counter() - t0:.1f}s")
+    C, _ = eng.kmeans(X[kmeans_sample()], NLIST, KMEANS_ITERS, SEED, METRIC_IP, False)
+    eng.create_ivf(1, DIM, METRIC_IP, False, C)
+    assign = eng.nearest_clusters(1, X)
+    log(f"[rank {rank}] k-means {KMEANS_ITERS} it + assignment on the GPU: "
+        f"{time.perf_counter() - t0:.1f}s")
     sizes = np.bincount(assign, minlength=NLIST)
     owner = shard_lists(sizes, world)
-    eng.create_ivf(1, DIM, METRIC_IP, False, C)
     order = np.argsort(assign, kind="stable")
     bounds = np.searchsorted(assign[order], np.arange(NLIST + 1))
     local_rows = 0
@@ -384,6 +441,12 @@ def run_ours(args, rank, world, local_rank):
     if recall is None:
         nprobe, recall = max(sweep, key=sweep.get), max(sweep.values())
     log(f"[rank {rank}] recall@10 sweep {sweep} -> nprobe {nprobe}")
+    # every batch's answer at the chosen nprobe (untimed), for the parity check
+    # against the reference core on the same index
+    all_answers = [[], [], []]
+    for b in range(NBATCH):
+        for lst, t in zip(all_answers, sharded.search(Qd[b], nprobe)):
+            lst.append(t.cpu().numpy())
 
     # ---- device-resident timing
     for w in range(args.warmup):
@@ -503,30 +566,35 @@ def run_ours(args, rank, world, local_rank):
                     "bytes_per_launch": avg_bytes, "ms_per_launch": avg_ms,
                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                     if peak_kind == "measured" else "fallback 6650 GB/s"}
-    cpu = None
+    cpu = parity = None
     if world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as O
 
         if O.have_ref():
             threads = len(os.sched_getaffinity(0))
-            v, sample = cpu_reference_qps(C, X, assign, Qb, threads)
+            ref = ref_index_of(C, X, assign)
+            v, sample, qrows, want = cpu_reference_qps(ref, Qb, nprobe, threads)
+            del ref
             cpu = {"value": v, "unit": "queries/s", "cores": threads, "kind": "reference",
                    "sample": sample}
+            got = tuple(np.concatenate([a[i] for i in range(NBATCH)])[qrows]
+                        for a in all_answers)
+            parity = parity_vs_reference(got, want)
     line = {
         "metric": "search QPS at recall@10>=0.95 (IVF, dim 1024)",
         "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Gaussian mixture; no dataset)",
-        "config": {"workload": WORKLOAD, "n_vectors": N_VEC, "dim": DIM, "nlist": NLIST,
-                   "nprobe": nprobe, "k": K, "batch": BATCH, "recall_at_10": recall,
-                   "recall_sweep": {str(k): v for k, v in sweep.items()},
-                   "kmeans_iters": KMEANS_ITERS,
-                   "stage_ms_mean": {k[3:]: round(statistics.mean(v), 4)
-                                     for k, v in stage_ms.items()},
-                   "l2_flush": "not needed: each step streams ~4 GB of lists (> 126 MB L2)",
-                   "parallelism": (f"lists sharded over {world} GPU(s), {args.coarse} coarse "
-                                   "selection") if world > 1 else "1 GPU"},
+        "config": bench_config(nprobe),
+        "recall_at_10": recall,
+        "recall_sweep": {str(k): v for k, v in sweep.items()},
+        "stage_ms_mean": {k[3:]: round(statistics.mean(v), 4) for k, v in stage_ms.items()},
+        "parallelism": (f"lists sharded over {world} GPU(s), {args.coarse} coarse "
+                        "selection") if world > 1 else "1 GPU",
+        "index": {"fingerprint": index_fingerprint(C, assign),
+                  "built": "GPU: m3g_kmeans on the sample + m3g_nearest_clusters (setup, untimed)"},
+        "parity": parity,
         "gpu_launches": int(round(per_step_launches * args.steps)),
         "clocks": clocks,
         "e2e": {"value": e2e_qps, "unit": "queries/s",
@@ -547,6 +615,258 @@ def run_ours(args, rank, world, local_rank):
     emit(line)
 
 
+# ---------------------------------------------------------------- bf16-stored lists
+# 10M x 768 vectors stored as bf16, 10k-component mixture, squared L2, nlist
+# 16384, k 100, nprobe 8 / 32 / 128 and batches of 1 / 64 / 4096 queries.
+C3_N = 10_000_000
+C3_DIM = 768
+C3_NCOMP = 10_000
+C3_NLIST = 16384
+C3_K = 100
+C3_NPROBES = (8, 32, 128)
+C3_BATCHES = (1, 64, 4096)
+C3_NQ = 10_240
+C3_SAMPLE_PER_LIST = 64
+
+
+def device_mixture(n, nq, d, ncomp, sigma, seed, dev, chunk=1 << 20):
+    """Seeded mixture data generated on the GPU (torch's CUDA generator), the
+    same on every rank: unit-norm component means, points = mean + sigma / sqrt(d)
+    noise, renormalised.  Returns (X [n, d] fp32, Q [nq, d] fp32) on dev."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    means = torch.randn(ncomp, d, generator=g, device=dev)
+    means /= means.norm(dim=1, keepdim=True)
+
+    def draw(m):
+        out = torch.empty(m, d, device=dev)
+        comp = torch.randint(0, ncomp, (m,), generator=g, device=dev)
+        for b in range(0, m, chunk):
+            e = min(m, b + chunk)
+            x = means[comp[b:e]] + (sigma / d ** 0.5) * torch.randn(e - b, d, generator=g,
+                                                                   device=dev)
+            out[b:e] = x / x.norm(dim=1, keepdim=True)
+        return out
+
+    X = draw(n)
+    Q = draw(nq)
+    return X, Q
+
+
+def exact_topk_l2_device(X, Q, k, step=1 << 20):
+    """Exact top-k ids by squared L2 (fp32, TF32 off), chunked over X."""
+    import torch
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    best_s = best_i = None
+    for b in range(0, X.shape[0], step):
+        xb = X[b:b + step]
+        s = 2.0 * (Q @ xb.T) - (xb * xb).sum(1)[None, :]  # larger is nearer
+        v, i = torch.topk(s, k, dim=1)
+        i = i + b
+        if best_s is None:
+            best_s, best_i = v, i
+        else:
+            cs, ci = torch.cat([best_s, v], 1), torch.cat([best_i, i], 1)
+            best_s, o = torch.topk(cs, k, dim=1)
+            best_i = torch.gather(ci, 1, o)
+    return best_i
+
+
+def run_config3(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from m3_memory_b200 import cabi
+    from m3_memory_b200.sharding import ShardedSearch, shard_lists
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    n, d, nlist, K3 = args.c3_n or C3_N, C3_DIM, C3_NLIST, C3_K
+    storage = cabi.BF16 if args.storage == "bf16" else cabi.F32
+    t0 = time.perf_counter()
+    X, Qd = device_mixture(n, C3_NQ, d, C3_NCOMP, SIGMA, SEED + 3, dev)
+    log(f"[rank {rank}] {n} x {d} generated on the GPU in {time.perf_counter() - t0:.1f}s")
+    eng = cabi.Engine()
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 4)
+    m = min(n, nlist * C3_SAMPLE_PER_LIST)
+    sample = torch.randperm(n, generator=g, device=dev)[:m].sort().values
+    t0 = time.perf_counter()
+    C, _ = eng.kmeans(X[sample].cpu().numpy(), nlist, KMEANS_ITERS, SEED, 0, False)
+    eng.create_ivf(1, d, 0, False, C, storage=storage)
+    assign = torch.empty(n, dtype=torch.int32, device=dev)
+    step = 1 << 21
+    for b in range(0, n, step):
+        e = min(n, b + step)
+        eng.nearest_clusters_device(1, X[b:e].data_ptr(), e - b, assign[b:e].data_ptr())
+    log(f"[rank {rank}] k-means ({KMEANS_ITERS} it on {m} rows) + assignment: "
+        f"{time.perf_counter() - t0:.1f}s")
+    sizes = torch.bincount(assign.long(), minlength=nlist).cpu().numpy()
+    owner = shard_lists(sizes, world)
+    order = torch.argsort(assign, stable=True)
+    bounds = np.concatenate([[0], np.cumsum(sizes)])
+    t0 = time.perf_counter()
+    local_rows = 0
+    for c in range(nlist):
+        b, e = int(bounds[c]), int(bounds[c + 1])
+        if e > b and owner[c] == rank:
+            rows = order[b:e]
+            xs = X[rows].contiguous()
+            eng.load_cluster_device(1, c, rows.data_ptr(), xs.data_ptr(), e - b, cabi.F32)
+            local_rows += e - b
+    torch.cuda.synchronize()
+    log(f"[rank {rank}] {local_rows} rows loaded ({args.storage} lists) in "
+        f"{time.perf_counter() - t0:.1f}s")
+    exact = exact_topk_l2_device(X, Qd[:1024], 10).cpu().numpy() if rank == 0 else None
+    del X, order, assign
+    torch.cuda.empty_cache()
+
+    sharded = ShardedSearch(eng, 1, K3, max(C3_BATCHES), world, dev, rank=rank,
+                            max_nprobe=max(C3_NPROBES), split_coarse=world > 1)
+    recall = {}
+    for P in C3_NPROBES:
+        ids, _, _ = sharded.search(Qd[:1024], P)
+        torch.cuda.synchronize()
+        r = recall_at_k(ids.cpu().numpy(), exact, 10) if rank == 0 else 0.0
+        if world > 1:
+            t = torch.tensor([r], device=dev)
+            dist.broadcast(t, 0)
+            r = float(t.item())
+        recall[P] = r
+    eng.sync_errors()
+    ok = [P for P in C3_NPROBES if recall[P] >= 0.95]
+    head_p = min(ok) if ok else max(recall, key=recall.get)
+    log(f"[rank {rank}] recall@10 by nprobe {recall} -> headline nprobe {head_p}")
+
+    def timed(P, B, steps):
+        span = C3_NQ - B + 1
+        for w in range(args.warmup):
+            sharded.search(Qd[(w * B) % span:(w * B) % span + B], P)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for i in range(steps):
+            o = (i * B) % span
+            sharded.search(Qd[o:o + B], P)
+        ev1.record()
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return B * steps / (ms / 1e3), ms / steps
+
+    sweep = {}
+    for P in C3_NPROBES:
+        for B in C3_BATCHES:
+            if (P, B) == (head_p, 4096):
+                continue
+            qps, ms = timed(P, B, min(args.steps, 50))
+            sweep[f"nprobe{P}_batch{B}"] = {"qps": qps, "ms_per_step": ms, "recall_at_10": recall[P]}
+    eng.sync_errors()
+    with ClockSampler(gpu_selector(local_rank)) as clk:
+        qps, ms = timed(head_p, 4096, args.steps)
+    clocks = clk.summary()
+    eng.sync_errors()
+    sweep[f"nprobe{head_p}_batch4096"] = {"qps": qps, "ms_per_step": ms,
+                                          "recall_at_10": recall[head_p]}
+    if rank != 0:
+        return
+    # end to end, roofline, reference sample (one GPU only)
+    e2e = roofline = cpu = parity = None
+    B = 4096
+    if world == 1:
+        lib = cabi.lib()
+        Qh = Qd.cpu().numpy()
+        pinned = torch.from_numpy(Qh).pin_memory()
+        h_ids = torch.empty((B, K3), dtype=torch.int64).pin_memory()
+        h_sc = torch.empty((B, K3), dtype=torch.float32).pin_memory()
+        h_cnt = torch.empty((B,), dtype=torch.int32).pin_memory()
+        span = C3_NQ - B + 1
+
+        def e2e_step(i):
+            o = (i * B) % span
+            cabi.check(lib.m3g_search(eng.h, 1, pinned[o].data_ptr(), B, K3, head_p,
+                                      h_ids.data_ptr(), h_sc.data_ptr(), h_cnt.data_ptr()))
+
+        for w in range(args.warmup):
+            e2e_step(w)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            e2e_step(i)
+        e2e = {"value": B * args.steps / (time.perf_counter() - t0), "unit": "queries/s",
+               "h2d_bytes_per_step": B * d * 4, "d2h_bytes_per_step": B * K3 * 12 + B * 4,
+               "path": "m3g_search (C ABI, pinned host buffers)"}
+        eng.set_profiling(True)
+        sm, sb, stages = [], [], {}
+        for i in range(min(args.steps, 20)):
+            e2e_step(i)
+            p = eng.last_profile()
+            sm.append(p["ms_scan"])
+            sb.append(p["scan_bytes"])
+            for key in ("ms_prep", "ms_coarse_gemm", "ms_select", "ms_worklist", "ms_scan",
+                        "ms_merge", "ms_total"):
+                stages.setdefault(key[3:], []).append(p[key])
+        eng.set_profiling(False)
+        peak, peak_kind = peaks()
+        ach = statistics.mean(sb) / (statistics.mean(sm) / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                    "frac": ach / peak, "traffic": None, "kernel": "list_scan_tc_kernel<bf16 rows>",
+                    "bytes_per_launch": statistics.mean(sb),
+                    "ms_per_launch": statistics.mean(sm),
+                    "stage_ms_mean": {k: round(statistics.mean(v), 4) for k, v in stages.items()},
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+        if not args.no_cpu_baseline:
+            from oracle import oracle as O
+
+            if O.have_ref():
+                nq_ref = 64
+                Qs = Qh[:nq_ref]
+                probes = eng.select_probes(1, Qs, head_p)
+                need = np.unique(probes)
+                ref = O.RefIndex(d, 0, False)
+                ref.set_centroids(C)
+                for c in need.tolist():
+                    ci, cv = eng.get_cluster(1, c)  # the stored (bf16) values as fp32
+                    if len(ci):
+                        ref.rebuild_cluster(c, ci, cv)
+                threads = len(os.sched_getaffinity(0))
+                t0 = time.perf_counter()
+                want = ref.search_nprobe(Qs, K3, head_p, threads=threads)
+                v = nq_ref / (time.perf_counter() - t0)
+                cpu = {"value": v, "unit": "queries/s", "cores": threads, "kind": "reference",
+                       "sample": f"{nq_ref} queries, IVFIndex::search_nprobe over the lists "
+                                 f"they probe ({len(need)} lists, stored values as fp32), "
+                                 f"{threads} threads"}
+                parity = parity_vs_reference(eng.search(1, Qs, K3, head_p), want)
+    emit({
+        "metric": "search QPS at recall@10>=0.95 (IVF, dim 768, bf16-stored lists)",
+        "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "bf16 rows, fp32 queries and accumulation",
+        "data": "synthetic (seeded 10k-component Gaussian mixture generated on the GPU)",
+        "config": {"workload": f"ivf-search: {n // 1_000_000}M x {d} {args.storage}-stored "
+                               f"mixture({C3_NCOMP}), L2, nlist {nlist}, nprobe {head_p}, "
+                               f"k {K3}, batch {B}",
+                   "n_vectors": n, "dim": d, "nlist": nlist, "nprobe": head_p, "k": K3,
+                   "batch": B, "storage": args.storage, "metric": "squared L2",
+                   "l2_flush": "not needed: each batch streams GBs of lists (> 126 MB L2)"},
+        "recall_at_10": recall[head_p], "recall_by_nprobe": {str(k): v for k, v in recall.items()},
+        "sweep": sweep,
+        "parallelism": f"lists sharded over {world} GPU(s), split coarse selection"
+        if world > 1 else "1 GPU",
+        "gpu_launches": None, "clocks": clocks, "e2e": e2e, "roofline": roofline,
+        "cpu_baseline": cpu, "parity": parity,
+    })
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -562,6 +882,12 @@ def main():
                     help="profiling only: fewer vectors (the headline line uses 1M)")
     ap.add_argument("--nlist", type=int, default=None, help="profiling only: fewer lists")
     ap.add_argument("--nprobe", type=int, default=None, help="profiling only: other nprobe")
+    ap.add_argument("--config", type=int, choices=[2, 3], default=2,
+                    help="2: the headline (1M x 1024 fp32, IP); 3: 10M x 768 bf16-stored lists, "
+                         "L2, nlist 16384, k 100, nprobe x batch sweep")
+    ap.add_argument("--storage", choices=["bf16", "fp32"], default="bf16",
+                    help="config 3: list storage")
+    ap.add_argument("--c3-n", type=int, default=None, help="config 3, profiling only: rows")
     args = ap.parse_args()
     keep_stdout_for_result()
     global N_VEC, NLIST, NPROBE, FIXED_NPROBE, WORKLOAD
@@ -590,7 +916,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.config == 3:
+            run_config3(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

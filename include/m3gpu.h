@@ -49,6 +49,13 @@ typedef enum {
 /* m3::Metric, AgentMemory/M3/include/base.h:10 */
 typedef enum { M3G_L2 = 0, M3G_IP = 1, M3G_COSINE = 2 } m3g_metric;
 
+/* Element types of vectors crossing the ABI (m3g_load_cluster) and of an
+ * index's list storage (m3g_create_ivf_ex).  The reference stores fp32 only
+ * (Cluster::mat_, AgentMemory/M3/include/cluster.h:83). */
+typedef enum { M3G_F32 = 0, M3G_BF16 = 1 } m3g_dtype;
+#define M3G_STORE_FP32 M3G_F32
+#define M3G_STORE_BF16 M3G_BF16
+
 /* Message of the last failing call on this thread ("" if none). */
 const char* m3g_last_error(void);
 /* ABI version (major * 10000 + minor * 100 + patch). */
@@ -82,10 +89,30 @@ int m3g_set_maintenance_policy(m3g_engine* e, double period_sec, size_t split_th
 int m3g_create_ivf(m3g_engine* e, int index_id, int dim, int metric, int normalized,
                    const float* centroids, int64_t nlist);
 
+/* AsyncEngine::create_ivf with the list storage chosen: M3G_F32 (as
+ * m3g_create_ivf) or M3G_BF16, rows kept as bf16 (round to nearest) in HBM --
+ * half the bytes every search streams.  A bf16 index scores its rows as the
+ * bf16 values widened to fp32 (the reference's arithmetic on those values) and
+ * serves k <= 128 (M3G_EUNSUPPORTED above).  No counterpart in the reference,
+ * which stores fp32 only (cluster.h:83). */
+int m3g_create_ivf_ex(m3g_engine* e, int index_id, int dim, int metric, int normalized,
+                      const float* centroids, int64_t nlist, int storage);
+/* The list storage of an index (M3G_F32 / M3G_BF16); M3G_ERANGE if unknown. */
+int m3g_storage_of(m3g_engine* e, int index_id, int* storage);
+
 /* AsyncEngine::load_cluster (m3_async.cpp:237-260 -> Cluster::rebuild_from,
- * cluster.cpp:152-178): synchronous full replace of one list. */
+ * cluster.cpp:152-178): synchronous full replace of one list.  vecs: [n, dim]
+ * of dtype M3G_F32 (float) or M3G_BF16 (uint16 bf16 bit patterns); the rows
+ * are stored in the index's own storage type. */
 int m3g_load_cluster(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
-                     const float* vecs, int64_t n);
+                     const void* vecs, int64_t n, int dtype);
+
+/* m3g_load_cluster with the rows already on the engine's device: d_ids [n]
+ * int64 and d_vecs [n, dim] of dtype M3G_F32 / M3G_BF16 are device pointers
+ * (the zero-host-copy path for data that lives in GPU memory, e.g. a CUDA
+ * tensor).  Synchronous. */
+int m3g_load_cluster_device(m3g_engine* e, int index_id, int cluster_id, const int64_t* d_ids,
+                            const void* d_vecs, int64_t n, int dtype);
 
 /* AsyncEngine::enqueue_insert / enqueue_update / enqueue_delete
  * (m3_async.cpp:123-187; applied by writer threads as Cluster::add_batch /
@@ -142,6 +169,11 @@ int m3g_search_on(m3g_engine* e, int index_id, const int32_t* cluster_ids, int n
  * score, lowest id on ties, -1 if the index has no lists.  Bit-exact. */
 int m3g_nearest_clusters(m3g_engine* e, int index_id, const float* vecs, int64_t n,
                          int32_t* out_cluster);
+
+/* m3g_nearest_clusters on device rows d_vecs [n, dim] fp32, writing
+ * d_out_cluster [n] int32 on the device.  Synchronous. */
+int m3g_nearest_clusters_device(m3g_engine* e, int index_id, const float* d_vecs, int64_t n,
+                                int32_t* d_out_cluster);
 
 /* The top-nprobe centroid selection (IVFIndex::select_nprobe_for_query,
  * m3_index.cpp:492-523) on its own: out_probes[nq, min(nprobe, nlist)]

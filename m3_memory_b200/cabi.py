@@ -16,6 +16,21 @@ LIB_PATH = Path(__file__).resolve().parent / "libm3gpu.so"
 M3G_OK, M3G_EINVAL, M3G_ERANGE, M3G_ERUNTIME, M3G_ECUDA, M3G_ENCCL, M3G_ETIMEOUT, \
     M3G_EUNSUPPORTED = range(8)
 L2, IP, COSINE = 0, 1, 2
+F32, BF16 = 0, 1  # m3g_dtype: vector element types and list storage
+
+
+def bf16_bits(x):
+    """fp32 values -> their bf16 bit patterns (uint16, round to nearest even)."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(np.asarray(x, np.float32))
+    r[nan] = 0x7FC0
+    return r
+
+
+def bf16_round(x):
+    """fp32 values rounded to bf16 precision (kept as fp32)."""
+    return (bf16_bits(x).astype(np.uint32) << 16).view(np.float32)
 
 # Every symbol include/m3gpu.h declares, with (restype, argtypes).
 _vp = ct.c_void_p
@@ -46,7 +61,11 @@ SIGNATURES = {
     "m3g_set_search_policy": (_i32, [_vp, _i32, _i32]),
     "m3g_set_maintenance_policy": (_i32, [_vp, _f64, _sz, _f64, _i32]),
     "m3g_create_ivf": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _i64]),
-    "m3g_load_cluster": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64]),
+    "m3g_create_ivf_ex": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _i64, _i32]),
+    "m3g_storage_of": (_i32, [_vp, _i32, _pi]),
+    "m3g_load_cluster": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
+    "m3g_load_cluster_device": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
+    "m3g_nearest_clusters_device": (_i32, [_vp, _i32, _vp, _i64, _vp]),
     "m3g_enqueue_insert": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _pi]),
     "m3g_enqueue_update": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32, _pi]),
     "m3g_enqueue_delete": (_i32, [_vp, _i32, _i32, _vp, _i64, _pi]),
@@ -173,14 +192,40 @@ class Engine:
                                                compact_ratio, int(auto_split)))
 
     # index
-    def create_ivf(self, index_id, dim, metric, normalized, C):
+    def create_ivf(self, index_id, dim, metric, normalized, C, storage=F32):
         C = _f32(C).reshape(-1, dim) if np.size(C) else np.zeros((0, dim), np.float32)
-        check(lib().m3g_create_ivf(self.h, index_id, dim, metric, int(normalized), _p(C),
-                                   C.shape[0]))
+        if storage == F32:
+            check(lib().m3g_create_ivf(self.h, index_id, dim, metric, int(normalized), _p(C),
+                                       C.shape[0]))
+        else:
+            check(lib().m3g_create_ivf_ex(self.h, index_id, dim, metric, int(normalized), _p(C),
+                                          C.shape[0], storage))
+
+    def storage_of(self, index_id):
+        s = ct.c_int()
+        check(lib().m3g_storage_of(self.h, index_id, ct.byref(s)))
+        return s.value
 
     def load_cluster(self, index_id, cid, ids, vecs):
-        ids, vecs = _i64a(ids), _f32(vecs)
-        check(lib().m3g_load_cluster(self.h, index_id, cid, _p(ids), _p(vecs), ids.shape[0]))
+        """vecs: float32 rows, or uint16 rows of bf16 bit patterns."""
+        ids = _i64a(ids)
+        if np.asarray(vecs).dtype == np.uint16:
+            v = np.ascontiguousarray(vecs, np.uint16)
+            check(lib().m3g_load_cluster(self.h, index_id, cid, _p(ids), _p(v), ids.shape[0],
+                                         BF16))
+        else:
+            v = _f32(vecs)
+            check(lib().m3g_load_cluster(self.h, index_id, cid, _p(ids), _p(v), ids.shape[0],
+                                         F32))
+
+    def load_cluster_device(self, index_id, cid, ids_ptr, vecs_ptr, n, dtype=F32):
+        """Device pointers: ids int64 [n], vectors [n, dim] fp32 or bf16 bits."""
+        check(lib().m3g_load_cluster_device(self.h, index_id, cid, ct.c_void_p(ids_ptr),
+                                            ct.c_void_p(vecs_ptr), n, dtype))
+
+    def nearest_clusters_device(self, index_id, vecs_ptr, n, out_ptr):
+        check(lib().m3g_nearest_clusters_device(self.h, index_id, ct.c_void_p(vecs_ptr), n,
+                                                ct.c_void_p(out_ptr)))
 
     def enqueue_insert(self, index_id, cid, ids, vecs):
         ids, vecs = _i64a(ids), _f32(vecs)

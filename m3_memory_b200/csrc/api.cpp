@@ -48,7 +48,7 @@ extern "C" {
 
 const char* m3g_last_error(void) { return g_last_error.c_str(); }
 
-int m3g_version(void) { return 100; }
+int m3g_version(void) { return 20000; }
 
 int m3g_engine_create(m3g_engine** out) {
     if (!out) return bad_handle();
@@ -115,10 +115,45 @@ int m3g_create_ivf(m3g_engine* e, int index_id, int dim, int metric, int normali
         [&] { e->eng.create_ivf(index_id, dim, metric, normalized != 0, centroids, nlist); });
 }
 
-int m3g_load_cluster(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
-                     const float* vecs, int64_t n) {
+int m3g_create_ivf_ex(m3g_engine* e, int index_id, int dim, int metric, int normalized,
+                      const float* centroids, int64_t nlist, int storage) {
     M3G_ENGINE_OR_FAIL(e);
-    return guarded([&] { e->eng.load_cluster(index_id, cluster_id, ids, vecs, n); });
+    return guarded([&] {
+        e->eng.create_ivf(index_id, dim, metric, normalized != 0, centroids, nlist, storage);
+    });
+}
+
+int m3g_storage_of(m3g_engine* e, int index_id, int* storage) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        const int s = e->eng.storage_of(index_id);
+        if (storage) *storage = s;
+    });
+}
+
+int m3g_load_cluster(m3g_engine* e, int index_id, int cluster_id, const int64_t* ids,
+                     const void* vecs, int64_t n, int dtype) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (dtype == M3G_F32) {
+            e->eng.load_cluster(index_id, cluster_id, ids, static_cast<const float*>(vecs), n);
+            return;
+        }
+        if (dtype != M3G_BF16) m3g::fail(M3G_EINVAL, "load_cluster: unknown dtype");
+        int dim = 0;
+        e->eng.info(index_id, &dim, nullptr, nullptr, nullptr);
+        if (dim <= 0) m3g::fail(M3G_ERANGE, "AsyncEngine::load_cluster: index not found");
+        if (n < 0 || (n > 0 && !vecs))
+            m3g::fail(M3G_EINVAL, "AsyncEngine::load_cluster: vecs.size mismatch");
+        // bf16 bit patterns widened to fp32 (exact); a bf16 index stores them unchanged
+        const uint16_t* b = static_cast<const uint16_t*>(vecs);
+        std::vector<float> wide((size_t)(n * dim));
+        for (size_t i = 0; i < wide.size(); ++i) {
+            const uint32_t u = (uint32_t)b[i] << 16;
+            std::memcpy(&wide[i], &u, 4);
+        }
+        e->eng.load_cluster(index_id, cluster_id, ids, wide.data(), n);
+    });
 }
 
 namespace {
@@ -229,6 +264,22 @@ int m3g_nearest_clusters(m3g_engine* e, int index_id, const float* vecs, int64_t
                          int32_t* out_cluster) {
     M3G_ENGINE_OR_FAIL(e);
     return guarded([&] { e->eng.nearest_clusters(index_id, vecs, n, out_cluster); });
+}
+
+int m3g_nearest_clusters_device(m3g_engine* e, int index_id, const float* d_vecs, int64_t n,
+                                int32_t* d_out_cluster) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (n > 0 && (!d_vecs || !d_out_cluster))
+            m3g::fail(M3G_EINVAL, "nearest_clusters_device: buffers missing");
+        e->eng.nearest_clusters(index_id, d_vecs, n, d_out_cluster, true);
+    });
+}
+
+int m3g_load_cluster_device(m3g_engine* e, int index_id, int cluster_id, const int64_t* d_ids,
+                            const void* d_vecs, int64_t n, int dtype) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.load_cluster_device(index_id, cluster_id, d_ids, d_vecs, n, dtype); });
 }
 
 int m3g_select_probes(m3g_engine* e, int index_id, const float* queries, int64_t nq, int nprobe,

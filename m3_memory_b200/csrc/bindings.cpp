@@ -169,23 +169,28 @@ PYBIND11_MODULE(_m3_async, m) {
         .def(
             "create_ivf",
             [](AsyncEngine& e, int index_id, int dim, Metric metric, bool normalized,
-               f32arr centroids) {
+               f32arr centroids, const std::string& storage) {
                 auto b = centroids.request();
                 if (b.ndim != 2) throw std::runtime_error("centroids must be 2D [nlist, dim]");
                 if (b.shape[1] != dim)
                     throw std::runtime_error("centroids dim mismatch: expected " +
                                              std::to_string(dim) + ", got " +
                                              std::to_string(b.shape[1]));
+                // storage: "fp32" (the reference's) or "bf16" (rows rounded to bf16 in HBM)
+                int st = M3G_STORE_FP32;
+                if (storage == "bf16") st = M3G_STORE_BF16;
+                else if (storage != "fp32")
+                    throw py::value_error("create_ivf: storage must be 'fp32' or 'bf16'");
                 int rc;
                 {
                     py::gil_scoped_release g;
-                    rc = m3g_create_ivf(e.h(), index_id, dim, (int)metric, normalized ? 1 : 0,
-                                        static_cast<const float*>(b.ptr), b.shape[0]);
+                    rc = m3g_create_ivf_ex(e.h(), index_id, dim, (int)metric, normalized ? 1 : 0,
+                                           static_cast<const float*>(b.ptr), b.shape[0], st);
                 }
                 raise_status(rc);
             },
             py::arg("index_id"), py::arg("dim"), py::arg("metric"), py::arg("normalized"),
-            py::arg("centroids"))
+            py::arg("centroids"), py::arg("storage") = "fp32")
         .def(
             "set_queue_policy",
             [](AsyncEngine& e, size_t capacity, size_t pop_batch_max, bool block_on_full) {
@@ -287,8 +292,8 @@ PYBIND11_MODULE(_m3_async, m) {
                 {
                     py::gil_scoped_release g;
                     rc = m3g_load_cluster(e.h(), index_id, cluster_id,
-                                          static_cast<const int64_t*>(ib.ptr),
-                                          static_cast<const float*>(vb.ptr), ib.shape[0]);
+                                          static_cast<const int64_t*>(ib.ptr), vb.ptr,
+                                          ib.shape[0], M3G_F32);
                 }
                 raise_status(rc);
             },

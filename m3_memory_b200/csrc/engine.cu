@@ -111,10 +111,17 @@ void encode_tma_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uin
 
 namespace {
 
-// 2-D fp32 tensor map over [rows, dpad], box 32 x h, 128-byte swizzle.
-void make_row_map(CUtensorMap* m, const float* base, int64_t rows, int dpad, int h) {
-    encode_tma_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, (uint64_t)dpad, (uint64_t)rows,
-                  (uint64_t)dpad * 4, 32, (uint32_t)h, CU_TENSOR_MAP_SWIZZLE_128B);
+// 2-D tensor map over the arena's [rows, ldr] elements, boxes of 128 bytes
+// (32 fp32 or 64 bf16) x h rows, 128-byte swizzle.
+void make_row_map(CUtensorMap* m, const Index& ix, int h) {
+    if (ix.bf16_rows())
+        encode_tma_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, ix.vecs.p, (uint64_t)ix.ldr,
+                      (uint64_t)ix.arena_cap, (uint64_t)ix.ldr * 2, 64, (uint32_t)h,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    else
+        encode_tma_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, ix.vecs.p, (uint64_t)ix.ldr,
+                      (uint64_t)ix.arena_cap, (uint64_t)ix.ldr * 4, 32, (uint32_t)h,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // Which kernel scans the lists: the tensor-core scan (default, where it
@@ -167,11 +174,11 @@ void rebuild_maps(Index& ix) {
         ix.maps_valid = false;
         return;
     }
-    make_row_map(&ix.maps.m128, ix.vecs.p, ix.arena_cap, ix.dpad, 128);
-    make_row_map(&ix.maps.m64, ix.vecs.p, ix.arena_cap, ix.dpad, 64);
-    make_row_map(&ix.maps.m32, ix.vecs.p, ix.arena_cap, ix.dpad, 32);
-    make_row_map(&ix.maps.m16, ix.vecs.p, ix.arena_cap, ix.dpad, 16);
-    make_row_map(&ix.maps.m8, ix.vecs.p, ix.arena_cap, ix.dpad, 8);
+    make_row_map(&ix.maps.m128, ix, 128);
+    make_row_map(&ix.maps.m64, ix, 64);
+    make_row_map(&ix.maps.m32, ix, 32);
+    make_row_map(&ix.maps.m16, ix, 16);
+    make_row_map(&ix.maps.m8, ix, 8);
     ix.maps_valid = true;
 }
 
@@ -258,17 +265,19 @@ void grow_arena(Index& ix, int64_t extra) {
     DBuf<float> vecs, rn;
     DBuf<int64_t> ids;
     DBuf<uint8_t> alive;
-    vecs.alloc((size_t)cap * ix.dpad);
+    const int64_t rb = ix.row_bytes();
+    vecs.alloc((size_t)(cap * rb / 4));
     rn.alloc((size_t)cap);
     ids.alloc((size_t)cap);
     alive.alloc((size_t)cap);
-    M3G_CK(cudaMemsetAsync(vecs.p, 0, (size_t)cap * ix.dpad * 4, ix.wstream));
+    M3G_CK(cudaMemsetAsync(vecs.p, 0, (size_t)(cap * rb), ix.wstream));
     M3G_CK(cudaMemsetAsync(alive.p, 0, (size_t)cap, ix.wstream));
     int64_t pos = 0;
     for (auto& l : ix.lists) {
         if (l.len > 0) {
-            M3G_CK(cudaMemcpyAsync(vecs.p + pos * ix.dpad, ix.vecs.p + l.off * ix.dpad,
-                                   (size_t)l.len * ix.dpad * 4, cudaMemcpyDeviceToDevice, ix.wstream));
+            M3G_CK(cudaMemcpyAsync(reinterpret_cast<unsigned char*>(vecs.p) + pos * rb,
+                                   ix.row_ptr(l.off), (size_t)(l.len * rb),
+                                   cudaMemcpyDeviceToDevice, ix.wstream));
             M3G_CK(cudaMemcpyAsync(rn.p + pos, ix.rnorm2.p + l.off, (size_t)l.len * 4,
                                    cudaMemcpyDeviceToDevice, ix.wstream));
             M3G_CK(cudaMemcpyAsync(ids.p + pos, ix.ids.p + l.off, (size_t)l.len * 8,
@@ -301,8 +310,8 @@ void relocate(Index& ix, int l, int64_t cap, int64_t keep) {
     }
     const int64_t dst = ix.arena_used;
     if (keep > 0) {
-        M3G_CK(cudaMemcpyAsync(ix.vecs.p + dst * ix.dpad, ix.vecs.p + L.off * ix.dpad,
-                               (size_t)keep * ix.dpad * 4, cudaMemcpyDeviceToDevice, ix.wstream));
+        M3G_CK(cudaMemcpyAsync(ix.row_ptr(dst), ix.row_ptr(L.off), (size_t)(keep * ix.row_bytes()),
+                               cudaMemcpyDeviceToDevice, ix.wstream));
         M3G_CK(cudaMemcpyAsync(ix.rnorm2.p + dst, ix.rnorm2.p + L.off, (size_t)keep * 4,
                                cudaMemcpyDeviceToDevice, ix.wstream));
         M3G_CK(cudaMemcpyAsync(ix.ids.p + dst, ix.ids.p + L.off, (size_t)keep * 8,
@@ -322,15 +331,48 @@ void ensure_list_room(Index& ix, int l, int64_t need_len) {
     relocate(ix, l, cap, L.len);
 }
 
+// Device rows stage [n, dpad] fp32 (zero padded; a bf16 index rounds them in
+// place) into the arena format at device rows dst, with their squared norms (of
+// the stored values) into nrm2[n].
+void store_staged_rows(Index& ix, unsigned char* dst, float* stage, int64_t n, float* nrm2) {
+    if (n <= 0) return;
+    if (ix.bf16_rows()) M3G_CK(launch_round_bf16_rows(stage, ix.dpad, n, ix.dim, ix.wstream));
+    launch_row_norms(stage, ix.dpad, n, ix.dim, nullptr, nrm2, ix.wstream);
+    M3G_CK(cudaGetLastError());
+    if (ix.bf16_rows())
+        M3G_CK(launch_pack_bf16_rows(stage, ix.dpad, n, ix.dim,
+                                     reinterpret_cast<__nv_bfloat16*>(dst), ix.ldr, ix.wstream));
+    else
+        M3G_CK(cudaMemcpyAsync(dst, stage, (size_t)(n * ix.dpad) * 4, cudaMemcpyDeviceToDevice,
+                               ix.wstream));
+}
+
+// Host rows [n, dim] fp32 into the arena format at device rows dst (fp32 rows
+// copied straight in; bf16 rows staged as fp32, rounded, packed), with their
+// squared norms into nrm2[n].
+void store_rows(Index& ix, unsigned char* dst, const float* vecs, int64_t n, float* nrm2) {
+    if (n <= 0) return;
+    if (!ix.bf16_rows()) {
+        float* d = reinterpret_cast<float*>(dst);
+        h2d_rows(d, ix.ldr, vecs, ix.dim, n, ix.wstream);
+        launch_row_norms(d, ix.ldr, n, ix.dim, nullptr, nrm2, ix.wstream);
+        M3G_CK(cudaGetLastError());
+        return;
+    }
+    DBuf<float> stage;
+    stage.alloc((size_t)(n * ix.dpad));
+    if (ix.dpad != ix.dim) M3G_CK(cudaMemsetAsync(stage.p, 0, (size_t)(n * ix.dpad) * 4, ix.wstream));
+    h2d_rows(stage.p, ix.dpad, vecs, ix.dim, n, ix.wstream);
+    store_staged_rows(ix, dst, stage.p, n, nrm2);
+    M3G_CK(cudaStreamSynchronize(ix.wstream));  // the staging buffer is freed on return
+}
+
 // Writes rows (ids, host vectors) at arena rows [row0, row0 + n) of list l.
 void write_rows(Index& ix, int64_t row0, const int64_t* ids, const float* vecs, int64_t n) {
     if (n <= 0) return;
-    h2d_rows(ix.vecs.p + row0 * ix.dpad, ix.dpad, vecs, ix.dim, n, ix.wstream);
     M3G_CK(cudaMemcpyAsync(ix.ids.p + row0, ids, (size_t)n * 8, cudaMemcpyHostToDevice, ix.wstream));
     M3G_CK(cudaMemsetAsync(ix.alive.p + row0, 1, (size_t)n, ix.wstream));
-    launch_row_norms(ix.vecs.p + row0 * ix.dpad, ix.dpad, n, ix.dim, nullptr, ix.rnorm2.p + row0,
-                     ix.wstream);
-    M3G_CK(cudaGetLastError());
+    store_rows(ix, ix.row_ptr(row0), vecs, n, ix.rnorm2.p + row0);
 }
 
 // Host-side staging of int64 index arrays for the scatter / gather kernels.
@@ -356,6 +398,43 @@ void list_rebuild(Index& ix, int l, const int64_t* ids, const float* vecs, int64
     L.id2row.clear();
     L.id2row.reserve((size_t)n);
     for (int64_t r = 0; r < n; ++r) L.id2row.emplace(ids[r], r);
+}
+
+// Cluster::rebuild_from with the rows on the device: d_vecs [n, dim] fp32 or
+// bf16 bits (dtype), d_ids [n].  The ids come to the host for the id map.
+void list_rebuild_device(Index& ix, int l, const int64_t* d_ids, const void* d_vecs, int dtype,
+                         int64_t n) {
+    std::vector<int64_t> ids((size_t)n);
+    if (n > 0)
+        M3G_CK(cudaMemcpyAsync(ids.data(), d_ids, (size_t)n * 8, cudaMemcpyDeviceToHost, ix.wstream));
+    ListMeta& L = ix.lists[l];
+    if (n > L.cap) relocate(ix, l, std::max<int64_t>(n, 16), 0);
+    if (n > 0) {
+        DBuf<float> stage;
+        stage.alloc((size_t)(n * ix.dpad));
+        if (dtype == M3G_BF16) {
+            M3G_CK(launch_unpack_bf16_rows(static_cast<const __nv_bfloat16*>(d_vecs), ix.dim, n,
+                                           ix.dim, stage.p, ix.dpad, ix.wstream));
+        } else {
+            if (ix.dpad != ix.dim)
+                M3G_CK(cudaMemsetAsync(stage.p, 0, (size_t)(n * ix.dpad) * 4, ix.wstream));
+            M3G_CK(cudaMemcpy2DAsync(stage.p, (size_t)ix.dpad * 4, d_vecs, (size_t)ix.dim * 4,
+                                     (size_t)ix.dim * 4, (size_t)n, cudaMemcpyDeviceToDevice,
+                                     ix.wstream));
+        }
+        store_staged_rows(ix, ix.row_ptr(L.off), stage.p, n, ix.rnorm2.p + L.off);
+        M3G_CK(cudaMemcpyAsync(ix.ids.p + L.off, d_ids, (size_t)n * 8, cudaMemcpyDeviceToDevice,
+                               ix.wstream));
+        M3G_CK(cudaMemsetAsync(ix.alive.p + L.off, 1, (size_t)n, ix.wstream));
+        M3G_CK(cudaStreamSynchronize(ix.wstream));
+    }
+    L.len = n;
+    L.live = n;
+    L.ids = std::move(ids);
+    L.alive.assign((size_t)n, 1);
+    L.id2row.clear();
+    L.id2row.reserve((size_t)n);
+    for (int64_t r = 0; r < n; ++r) L.id2row.emplace(L.ids[(size_t)r], r);
 }
 
 // Cluster::add_batch (cluster.cpp:55-101).
@@ -421,20 +500,20 @@ void list_update(Index& ix, int l, const int64_t* ids, const float* vecs, int64_
             row_ids.push_back(ids[kv.second]);
         }
         const int64_t m = (int64_t)dst_rows.size();
-        DBuf<float> d_src;
-        d_src.alloc((size_t)m * ix.dpad);
-        M3G_CK(cudaMemsetAsync(d_src.p, 0, (size_t)m * ix.dpad * 4, ix.wstream));
-        h2d_rows(d_src.p, ix.dpad, staging.data(), ix.dim, m, ix.wstream);
+        // the rows in the arena's format (and their norms), then scattered into place
+        DBuf<float> d_src, nrm;
+        d_src.alloc((size_t)(m * ix.row_bytes() / 4));
+        nrm.alloc((size_t)m);
+        if (ix.ldr != ix.dim || ix.bf16_rows())
+            M3G_CK(cudaMemsetAsync(d_src.p, 0, (size_t)(m * ix.row_bytes()), ix.wstream));
+        store_rows(ix, reinterpret_cast<unsigned char*>(d_src.p), staging.data(), m, nrm.p);
         DevIdx di, dids;
         di.upload(dst_rows, ix.wstream);
         dids.upload(row_ids, ix.wstream);
-        M3G_CK(launch_scatter_rows(d_src.p, ix.dpad, di.d.p, m, ix.dpad, ix.vecs.p, ix.dpad, ix.wstream));
+        const int w = ix.row_words();
+        M3G_CK(launch_scatter_rows(d_src.p, w, di.d.p, m, w, ix.vecs.p, w, ix.wstream));
         M3G_CK(launch_scatter_i64(dids.d.p, di.d.p, m, ix.ids.p, ix.wstream));
         M3G_CK(launch_set_bytes(ix.alive.p, di.d.p, m, 1, ix.wstream));
-        // refresh the norms of the written rows
-        DBuf<float> nrm;
-        nrm.alloc((size_t)m);
-        launch_row_norms(d_src.p, ix.dpad, m, ix.dim, nullptr, nrm.p, ix.wstream);
         M3G_CK(launch_scatter_rows(nrm.p, 1, di.d.p, m, 1, ix.rnorm2.p, 1, ix.wstream));
         M3G_CK(cudaStreamSynchronize(ix.wstream));
     }
@@ -490,8 +569,9 @@ void regroup_rows(Index& ix, int l, const std::vector<int64_t>& rows, int dst_li
     if (n > 0) {
         DevIdx di;
         di.upload(src_abs, ix.wstream);
-        M3G_CK(launch_gather_rows(ix.vecs.p, ix.dpad, di.d.p, n, ix.dpad, ix.vecs.p + dst * ix.dpad,
-                                  ix.dpad, ix.wstream));
+        const int w = ix.row_words();
+        M3G_CK(launch_gather_rows(ix.vecs.p, w, di.d.p, n, w, reinterpret_cast<float*>(ix.row_ptr(dst)),
+                                  w, ix.wstream));
         M3G_CK(launch_gather_f32(ix.rnorm2.p, di.d.p, n, ix.rnorm2.p + dst, ix.wstream));
         M3G_CK(launch_gather_i64(ix.ids.p, di.d.p, n, ix.ids.p + dst, ix.wstream));
         M3G_CK(cudaMemsetAsync(ix.alive.p + dst, 1, (size_t)n, ix.wstream));
@@ -629,8 +709,10 @@ void Engine::stop() {
 // ---------------- index lifecycle ----------------
 
 void Engine::create_ivf(int index_id, int dim, int metric, bool normalized, const float* C,
-                        int64_t nlist) {
+                        int64_t nlist, int storage) {
     if (dim <= 0) fail(M3G_EINVAL, "IVFIndex: dim must be > 0");
+    if (storage != M3G_STORE_FP32 && storage != M3G_STORE_BF16)
+        fail(M3G_EINVAL, "create_ivf: unknown storage type");
     if (metric < 0 || metric > 2) fail(M3G_EINVAL, "create_ivf: unknown metric");
     if (nlist < 0 || (nlist > 0 && !C)) fail(M3G_EINVAL, "create_ivf: centroids missing");
     if (nlist > (int64_t)INT32_MAX / 2) fail(M3G_EUNSUPPORTED, "create_ivf: too many lists");
@@ -639,6 +721,9 @@ void Engine::create_ivf(int index_id, int dim, int metric, bool normalized, cons
     ix->device = device_;
     ix->dim = dim;
     ix->dpad = round_up4(dim);
+    ix->storage = storage;
+    ix->esize = storage == M3G_STORE_BF16 ? 2 : 4;
+    ix->ldr = storage == M3G_STORE_BF16 ? std::max(64, (dim + 7) & ~7) : ix->dpad;
     ix->metric = metric;
     ix->normalized = normalized;
     M3G_CK(cudaStreamCreateWithFlags(&ix->wstream, cudaStreamNonBlocking));
@@ -659,6 +744,26 @@ void Engine::create_ivf(int index_id, int dim, int metric, bool normalized, cons
         std::unique_lock lk(old->mu);
         if (ws_.done) cudaEventSynchronize(ws_.done);
     }
+}
+
+void Engine::load_cluster_device(int index_id, int cid, const int64_t* d_ids, const void* d_vecs,
+                                 int64_t n, int dtype) {
+    auto ix = get(index_id, "AsyncEngine::load_cluster");
+    if (n < 0 || (n > 0 && (!d_ids || !d_vecs)))
+        fail(M3G_EINVAL, "AsyncEngine::load_cluster: vecs.size mismatch");
+    if (dtype != M3G_F32 && dtype != M3G_BF16) fail(M3G_EINVAL, "load_cluster: unknown dtype");
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (cid < 0 || cid >= ix->nlist())
+        fail(M3G_ERANGE, "IVFIndex::rebuild_cluster: invalid cluster_id");
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    list_rebuild_device(*ix, cid, d_ids, d_vecs, dtype, n);
+    refresh_list_meta(*ix);
+}
+
+int Engine::storage_of(int index_id) {
+    auto ix = get(index_id, "storage_of");
+    return ix->storage;
 }
 
 void Engine::load_cluster(int index_id, int cid, const int64_t* ids, const float* vecs, int64_t n) {
@@ -935,9 +1040,19 @@ void live_rows(Index& ix, int cid, std::vector<int64_t>* ids, std::vector<float>
     if (L.len == 0 || L.live == 0) return;
     std::vector<float> all((size_t)(L.len * ix.dim));
     M3G_CK(cudaStreamSynchronize(ix.wstream));
-    M3G_CK(cudaMemcpy2D(all.data(), (size_t)ix.dim * 4, ix.vecs.p + L.off * ix.dpad,
-                        (size_t)ix.dpad * 4, (size_t)ix.dim * 4, (size_t)L.len,
-                        cudaMemcpyDeviceToHost));
+    if (ix.bf16_rows()) {
+        // widened on the device (the bf16 values exactly), then copied out
+        DBuf<float> wide;
+        wide.alloc((size_t)(L.len * ix.dim));
+        M3G_CK(launch_unpack_bf16_rows(reinterpret_cast<const __nv_bfloat16*>(ix.row_ptr(L.off)),
+                                       ix.ldr, L.len, ix.dim, wide.p, ix.dim, ix.wstream));
+        M3G_CK(cudaMemcpyAsync(all.data(), wide.p, all.size() * 4, cudaMemcpyDeviceToHost,
+                               ix.wstream));
+        M3G_CK(cudaStreamSynchronize(ix.wstream));
+    } else {
+        M3G_CK(cudaMemcpy2D(all.data(), (size_t)ix.dim * 4, ix.row_ptr(L.off), (size_t)ix.ldr * 4,
+                            (size_t)ix.dim * 4, (size_t)L.len, cudaMemcpyDeviceToHost));
+    }
     ids->reserve((size_t)L.live);
     vecs->reserve((size_t)(L.live * ix.dim));
     for (int64_t r = 0; r < L.len; ++r) {
@@ -948,6 +1063,8 @@ void live_rows(Index& ix, int cid, std::vector<int64_t>* ids, std::vector<float>
 }
 
 constexpr char kIndexMagic[8] = {'M', '3', 'G', 'I', 'V', 'F', '0', '1'};
+// version 2 adds the list storage type (int32) after the four header fields
+constexpr char kIndexMagic2[8] = {'M', '3', 'G', 'I', 'V', 'F', '0', '2'};
 }  // namespace
 
 void Engine::get_cluster(int index_id, int cid, int64_t* ids, float* vecs, int64_t cap,
@@ -967,9 +1084,11 @@ void Engine::get_cluster(int index_id, int cid, int64_t* ids, float* vecs, int64
     if (vecs) std::copy(v.begin(), v.end(), vecs);
 }
 
-// File layout (little-endian): 8-byte magic "M3GIVF01"; int32 dim, metric,
-// normalized, nlist; float centroids[nlist * dim]; then per list int64 n,
-// int64 ids[n], float vectors[n * dim] (the live rows, in row order).
+// File layout (little-endian): 8-byte magic "M3GIVF02"; int32 dim, metric,
+// normalized, nlist, storage; float centroids[nlist * dim]; then per list int64
+// n, int64 ids[n], float vectors[n * dim] (the live rows, in row order; a bf16
+// index's rows as their exact fp32 values).  "M3GIVF01" files (no storage
+// field, fp32) still load.
 void Engine::save_index(int index_id, const char* path) {
     auto ix = get(index_id, "save_index");
     if (!path) fail(M3G_EINVAL, "save_index: path missing");
@@ -981,8 +1100,8 @@ void Engine::save_index(int index_id, const char* path) {
     auto put = [&](const void* p, size_t bytes) {
         if (ok && bytes && std::fwrite(p, 1, bytes, f) != bytes) ok = false;
     };
-    const int32_t hdr[4] = {ix->dim, ix->metric, ix->normalized ? 1 : 0, ix->nlist()};
-    put(kIndexMagic, sizeof(kIndexMagic));
+    const int32_t hdr[5] = {ix->dim, ix->metric, ix->normalized ? 1 : 0, ix->nlist(), ix->storage};
+    put(kIndexMagic2, sizeof(kIndexMagic2));
     put(hdr, sizeof(hdr));
     put(ix->centroids.data(), ix->centroids.size() * 4);
     std::vector<int64_t> ids;
@@ -1009,12 +1128,14 @@ void Engine::load_index(int index_id, const char* path) {
     };
     char magic[8];
     get_bytes(magic, sizeof(magic));
-    if (std::memcmp(magic, kIndexMagic, sizeof(magic)) != 0)
+    const bool v2 = std::memcmp(magic, kIndexMagic2, sizeof(magic)) == 0;
+    if (!v2 && std::memcmp(magic, kIndexMagic, sizeof(magic)) != 0)
         fail(M3G_EINVAL, std::string("load_index: not an index file: ") + path);
-    int32_t hdr[4];
-    get_bytes(hdr, sizeof(hdr));
-    const int dim = hdr[0], metric = hdr[1], nlist = hdr[3];
-    if (dim <= 0 || metric < 0 || metric > 2 || nlist < 0)
+    int32_t hdr[5] = {0, 0, 0, 0, M3G_STORE_FP32};
+    get_bytes(hdr, (v2 ? 5 : 4) * sizeof(int32_t));
+    const int dim = hdr[0], metric = hdr[1], nlist = hdr[3], storage = hdr[4];
+    if (dim <= 0 || metric < 0 || metric > 2 || nlist < 0 ||
+        (storage != M3G_STORE_FP32 && storage != M3G_STORE_BF16))
         fail(M3G_EINVAL, std::string("load_index: bad header: ") + path);
     std::vector<float> C((size_t)nlist * dim);
     get_bytes(C.data(), C.size() * 4);
@@ -1031,7 +1152,7 @@ void Engine::load_index(int index_id, const char* path) {
         get_bytes(ids[(size_t)c].data(), (size_t)n * 8);
         get_bytes(vecs[(size_t)c].data(), (size_t)n * dim * 4);
     }
-    create_ivf(index_id, dim, metric, hdr[2] != 0, C.data(), nlist);
+    create_ivf(index_id, dim, metric, hdr[2] != 0, C.data(), nlist, storage);
     for (int c = 0; c < nlist; ++c)
         if (!ids[(size_t)c].empty())
             load_cluster(index_id, c, ids[(size_t)c].data(), vecs[(size_t)c].data(),
@@ -1110,8 +1231,11 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
         M3G_CK(cudaEventRecord(ev[2], st));
     }
     if (profile) M3G_CK(cudaEventRecord(ev[3], st));
-    const bool tc_scan = use_tc_scan() && scan_tc_supported(ix.metric, k);
-    const int gmax = tc_scan ? scan_tc_gmax() : scan_gmax_for_dim(ix.dpad);
+    // bf16 rows are scanned by the tensor-core kernel only
+    const bool tc_scan = (use_tc_scan() || ix.bf16_rows()) && scan_tc_supported(ix.metric, k);
+    if (!tc_scan && ix.bf16_rows())
+        fail(M3G_EUNSUPPORTED, "search: an index with bf16 storage serves k <= 128");
+    const int gmax = tc_scan ? scan_tc_gmax(k) : scan_gmax_for_dim(ix.dpad);
     if (gmax <= 0) fail(M3G_EUNSUPPORTED, "search: dimension too large for the list scan");
     // with cleared partial lists, pairs probing empty lists (on a shard: the lists
     // other ranks own) are not queued
@@ -1152,7 +1276,7 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     const int grid = (int)std::min<int64_t>(num_sms_, std::max<int64_t>(1, nq * P));
     if (ix.maps_valid) {
         if (tc_scan)
-            M3G_CK(launch_list_scan_tc(ix.maps, a, grid, st));
+            M3G_CK(launch_list_scan_tc(ix.maps, a, ix.bf16_rows(), grid, st));
         else
             M3G_CK(launch_list_scan(ix.maps, a, gmax, grid, st));
     } else {
@@ -1163,8 +1287,12 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
         M3G_CK(cudaStreamSynchronize(st));
     }
     if (profile) M3G_CK(cudaEventRecord(ev[5], st));
+    // the tensor-core scan ranks squared L2 by its expansion; the answer's rows are
+    // rescored in the reference's arithmetic
+    MergeRescore rs{dQ, ldq, ix.vecs.p, ix.ldr, D, ix.bf16_rows() ? 1 : 0};
+    const bool rescore = tc_scan && ix.metric == M3G_L2 && ix.maps_valid;
     M3G_CK(launch_merge_topk(w.part_score.p, w.part_row.p, ix.ids.p, (int)nq, P, k, d_ids, d_scores,
-                             d_counts, st));
+                             d_counts, st, rescore ? &rs : nullptr));
     if (profile) M3G_CK(cudaEventRecord(ev[6], st));
     // kernels launched: norms, coarse (gemm + select, or iota), 3 work-list
     // kernels, scan, merge (+ the byte counter when profiling)
@@ -1180,7 +1308,8 @@ std::vector<uintptr_t> Engine::graph_key(const Index& ix, int64_t nq, int k, int
     return {u(&ix), u(ix.vecs.p), u(ix.ids.p), u(ix.alive.p), u(ix.rnorm2.p), u(ix.C.p),
             u(ix.C3.p), u(ix.cn.p), u(ix.cn2.p), u(ix.d_list_off.p), u(ix.d_list_len.p),
             u(ix.d_list_order.p), (uintptr_t)ix.arena_cap, (uintptr_t)ix.nlist(),
-            (uintptr_t)ix.dim, (uintptr_t)ix.dpad, (uintptr_t)ix.metric,
+            (uintptr_t)ix.dim, (uintptr_t)ix.dpad, (uintptr_t)ix.ldr, (uintptr_t)ix.esize,
+            (uintptr_t)ix.metric,
             (uintptr_t)ix.normalized, (uintptr_t)ix.maps_valid, (uintptr_t)nq, (uintptr_t)k,
             (uintptr_t)P, u(w.Q.p), u(w.Q3.p), u(w.S.p), u(w.qn.p), u(w.qn2.p), u(w.probes.p),
             u(w.lcount.p), u(w.lstart.p), u(w.lcursor.p), u(w.items.p), u(w.n_items.p),
@@ -1684,14 +1813,16 @@ void Engine::assign_rows(Index& ix, const float* dX, int64_t ld, const float* xn
     if (herr) fail(M3G_ETIMEOUT, "assignment: a device-side wait gave up");
 }
 
-void Engine::nearest_clusters(int index_id, const float* vecs, int64_t n, int32_t* out) {
+void Engine::nearest_clusters(int index_id, const float* vecs, int64_t n, int32_t* out,
+                              bool on_device) {
     auto ix = get(index_id, "nearest_clusters");
     DeviceGuard g(device_);
     if (n <= 0) return;
     std::shared_lock lk(ix->mu);
     const int L = ix->nlist();
     if (L == 0) {
-        std::fill(out, out + n, -1);
+        if (on_device) M3G_CK(cudaMemset(out, 0xff, (size_t)n * 4));
+        else std::fill(out, out + n, -1);
         return;
     }
     cudaStream_t st;
@@ -1707,10 +1838,13 @@ void Engine::nearest_clusters(int index_id, const float* vecs, int64_t n, int32_
     xn2.alloc((size_t)n);
     a.alloc((size_t)n);
     if (ix->dpad != ix->dim) M3G_CK(cudaMemsetAsync(X.p, 0, (size_t)(n * ix->dpad) * 4, st));
-    h2d_rows(X.p, ix->dpad, vecs, ix->dim, n, st);
+    M3G_CK(cudaMemcpy2DAsync(X.p, (size_t)ix->dpad * 4, vecs, (size_t)ix->dim * 4,
+                             (size_t)ix->dim * 4, (size_t)n,
+                             on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
     launch_row_norms(X.p, ix->dpad, n, ix->dim, xn.p, xn2.p, st);
     assign_rows(*ix, X.p, ix->dpad, xn.p, xn2.p, n, a.p, st);
-    M3G_CK(cudaMemcpyAsync(out, a.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    M3G_CK(cudaMemcpyAsync(out, a.p, (size_t)n * 4,
+                           on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
     M3G_CK(cudaStreamSynchronize(st));
 }
 
@@ -1892,18 +2026,26 @@ int Engine::split_cluster(int index_id, int cid, int niter, uint64_t seed) {
     }
     cudaStream_t st = ix->wstream;
     const int dpad = ix->dpad;
-    DBuf<float> dC;
+    DBuf<float> dC, wide;
     DBuf<int32_t> da;
     dC.alloc((size_t)2 * dpad);
     da.alloc((size_t)n);
+    // the list's rows as fp32 [n, dpad]: the arena itself, or bf16 rows widened
+    const float* X = reinterpret_cast<const float*>(ix->row_ptr(L.off));
+    if (ix->bf16_rows()) {
+        wide.alloc((size_t)(n * dpad));
+        M3G_CK(launch_unpack_bf16_rows(reinterpret_cast<const __nv_bfloat16*>(ix->row_ptr(L.off)),
+                                       ix->ldr, n, ix->dim, wide.p, dpad, st));
+        X = wide.p;
+    }
     int64_t init[2];
     sample_rows(seed, n, 2, init);
-    std::vector<int64_t> init_abs = {L.off + init[0], L.off + init[1]};
+    std::vector<int64_t> init_abs = {init[0], init[1]};
     DevIdx di;
     di.upload(init_abs, st);
-    M3G_CK(launch_gather_rows(ix->vecs.p, dpad, di.d.p, 2, dpad, dC.p, dpad, st));
-    kmeans_device(ix->vecs.p + L.off * dpad, dpad, n, ix->dim, dpad, ix->metric, ix->normalized, 2,
-                  niter, dC.p, da.p, st, num_sms_);
+    M3G_CK(launch_gather_rows(X, dpad, di.d.p, 2, dpad, dC.p, dpad, st));
+    kmeans_device(X, dpad, n, ix->dim, dpad, ix->metric, ix->normalized, 2, niter, dC.p, da.p, st,
+                  num_sms_);
     std::vector<float> c2((size_t)2 * ix->dim);
     M3G_CK(cudaMemcpy2DAsync(c2.data(), (size_t)ix->dim * 4, dC.p, (size_t)dpad * 4,
                              (size_t)ix->dim * 4, 2, cudaMemcpyDeviceToHost, st));

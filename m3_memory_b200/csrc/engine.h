@@ -91,6 +91,18 @@ struct Index {
     int device = 0;
     int dim = 0, dpad = 0, metric = 0;
     bool normalized = false;
+    // list arena row format: fp32 rows of ldr = dpad floats, or (storage bf16)
+    // bf16 rows of ldr = max(dim rounded up to 8, 64) elements (16-byte rows, at
+    // least one 64-wide TMA box)
+    int storage = 0;  // M3G_STORE_FP32 / M3G_STORE_BF16
+    int esize = 4, ldr = 0;
+    int64_t row_bytes() const { return (int64_t)ldr * esize; }
+    // arena row r (as bytes) and its width in fp32 words (for the row copy kernels)
+    unsigned char* row_ptr(int64_t r) const {
+        return reinterpret_cast<unsigned char*>(vecs.p) + r * row_bytes();
+    }
+    int row_words() const { return (int)(row_bytes() / 4); }
+    bool bf16_rows() const { return esize == 2; }
     std::vector<float> centroids;  // [nlist, dim] host copy (routing centroids)
     std::vector<ListMeta> lists;
 
@@ -98,7 +110,8 @@ struct Index {
     DBuf<float> C, cn, cn2;  // [cap, dpad], [cap], [cap]
     DBuf<__nv_bfloat16> C3;  // [cap, kp] split operand [hi | lo | hi] of the tensor-core GEMM
     size_t c_cap = 0;
-    // device: the list arena, [arena_cap, dpad] rows + per-row ids / tombstones / norms
+    // device: the list arena, [arena_cap] rows of row_bytes() (fp32 or bf16) + per-row
+    // ids / tombstones / norms (vecs is sized in fp32 words)
     DBuf<float> vecs, rnorm2;
     DBuf<int64_t> ids;
     DBuf<uint8_t> alive;
@@ -181,8 +194,13 @@ class Engine {
     void set_search_policy(const SearchPolicy& p) { spol_ = p; }
     void set_maintenance_policy(const MaintenancePolicy& p) { mpol_ = p; }
 
-    void create_ivf(int index_id, int dim, int metric, bool normalized, const float* C, int64_t nlist);
+    void create_ivf(int index_id, int dim, int metric, bool normalized, const float* C, int64_t nlist,
+                    int storage = M3G_STORE_FP32);
     void load_cluster(int index_id, int cid, const int64_t* ids, const float* vecs, int64_t n);
+    // the same with device rows: d_vecs [n, dim] fp32 or bf16 bits (dtype), d_ids [n]
+    void load_cluster_device(int index_id, int cid, const int64_t* d_ids, const void* d_vecs,
+                             int64_t n, int dtype);
+    int storage_of(int index_id);
     bool enqueue(WriteOp&& op);
     bool enqueue_insert_auto(int index_id, const int64_t* ids, const float* vecs, int64_t n);
     void flush();
@@ -206,7 +224,8 @@ class Engine {
     void search_probes_device(int index_id, const float* dQ, int64_t nq, int k,
                               const int32_t* d_probes, int P, int64_t* d_ids, float* d_scores,
                               int32_t* d_counts, cudaStream_t ext_stream);
-    void nearest_clusters(int index_id, const float* vecs, int64_t n, int32_t* out);
+    void nearest_clusters(int index_id, const float* vecs, int64_t n, int32_t* out,
+                          bool on_device = false);
     void sync_errors();
 
     void info(int index_id, int* dim, int* metric, int* normalized, int* nlist);

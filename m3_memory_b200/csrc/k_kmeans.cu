@@ -11,6 +11,7 @@
 // put in (cluster, row) order by a stable counting sort, then one thread per
 // (cluster, dim) sums its cluster's rows sequentially -- a segmented reduction
 // with no atomics on the data path.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -231,6 +232,61 @@ cudaError_t launch_centroid_update(const float* X, int64_t ldx, const int64_t* p
     if (L <= 0) return cudaSuccess;
     dim3 grid((d + 127) / 128, L);
     centroid_update_kernel<<<grid, 128, 0, st>>>(X, ldx, perm, start, d, C, ldc);
+    return cudaGetLastError();
+}
+
+namespace {
+__global__ void round_bf16_rows_kernel(float* __restrict__ X, int64_t ld, int64_t n, int dim) {
+    const int64_t total = n * dim;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        float* p = X + (t / dim) * ld + t % dim;
+        *p = __bfloat162float(__float2bfloat16_rn(*p));
+    }
+}
+
+__global__ void pack_bf16_rows_kernel(const float* __restrict__ src, int64_t lds, int64_t n, int dim,
+                                      __nv_bfloat16* __restrict__ dst, int64_t ldd) {
+    const int64_t total = n * ldd;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = t / ldd, i = t % ldd;
+        dst[r * ldd + i] = i < dim ? __float2bfloat16_rn(src[r * lds + i]) : __float2bfloat16_rn(0.f);
+    }
+}
+
+__global__ void unpack_bf16_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_t lds,
+                                        int64_t n, int dim, float* __restrict__ dst, int64_t ldd) {
+    const int64_t total = n * ldd;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = t / ldd, i = t % ldd;
+        dst[r * ldd + i] = i < dim ? __bfloat162float(src[r * lds + i]) : 0.f;
+    }
+}
+
+unsigned grid_for(int64_t total) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 8192));
+}
+}  // namespace
+
+cudaError_t launch_round_bf16_rows(float* X, int64_t ld, int64_t n, int dim, cudaStream_t st) {
+    if (n <= 0 || dim <= 0) return cudaSuccess;
+    round_bf16_rows_kernel<<<grid_for(n * dim), 256, 0, st>>>(X, ld, n, dim);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack_bf16_rows(const float* src, int64_t lds, int64_t n, int dim,
+                                  __nv_bfloat16* dst, int64_t ldd, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    pack_bf16_rows_kernel<<<grid_for(n * ldd), 256, 0, st>>>(src, lds, n, dim, dst, ldd);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_unpack_bf16_rows(const __nv_bfloat16* src, int64_t lds, int64_t n, int dim,
+                                    float* dst, int64_t ldd, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    unpack_bf16_rows_kernel<<<grid_for(n * ldd), 256, 0, st>>>(src, lds, n, dim, dst, ldd);
     return cudaGetLastError();
 }
 

@@ -776,12 +776,49 @@ __device__ uint32_t radix_select32(F key_of, int64_t n, unsigned rank, unsigned*
 // Candidate i = slot * k + j of query q lives at q * stride_q + slot * stride_slot
 // + j.  part_row holds arena rows mapped through row_ids, or, when row_ids is
 // null, the ids themselves.
+// The reference's squared L2 (base.cpp:12-20): one rounding per subtract,
+// multiply and add, summed in index order.  Padding dims are zero in both rows.
+template <bool XB>
+__device__ float exact_l2_row(const float* __restrict__ q, const void* __restrict__ rows,
+                              int64_t row, int64_t ld, int dim) {
+    float s = 0.f;
+    if (XB) {
+        const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(rows) + row * ld;
+        for (int i = 0; i < dim; ++i) {
+            const float df = __fsub_rn(q[i], __bfloat162float(x[i]));
+            s = __fadd_rn(s, __fmul_rn(df, df));
+        }
+    } else {
+        const float* x = reinterpret_cast<const float*>(rows) + row * ld;
+        int i = 0;
+        for (; i + 4 <= dim; i += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(q + i);
+            const float4 b = __ldg(reinterpret_cast<const float4*>(x + i));
+            float df = __fsub_rn(a.x, b.x);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+            df = __fsub_rn(a.y, b.y);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+            df = __fsub_rn(a.z, b.z);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+            df = __fsub_rn(a.w, b.w);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+        }
+        for (; i < dim; ++i) {
+            const float df = __fsub_rn(q[i], x[i]);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+        }
+    }
+    return s;
+}
+
 __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
     const float* __restrict__ part_score, const int64_t* __restrict__ part_row,
     const int64_t* __restrict__ row_ids, int P, int k, int64_t stride_q, int64_t stride_slot,
     int64_t* __restrict__ out_ids, float* __restrict__ out_scores,
-    int32_t* __restrict__ out_counts) {
+    int32_t* __restrict__ out_counts, MergeRescore rs, int rescore) {
     __shared__ unsigned long long cand[MCAP];
+    __shared__ unsigned long long won[MRG_BLOCK];
+    __shared__ float exact[MRG_BLOCK];
     __shared__ unsigned hist[256];
     __shared__ unsigned shv[4];
     __shared__ unsigned s_tau, s_cnt, s_valid;
@@ -869,14 +906,40 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
         __syncthreads();
         bitonic_u64(cand, n2);
     }
+    if (rescore) {
+        // the winners' exact scores (k <= MRG_BLOCK: one per thread), then a sort by
+        // (exact score, rank by the estimate)
+        const int j = threadIdx.x;
+        float e = INF;
+        if (j < kk) {
+            won[j] = cand[j];
+            const int64_t row = pr[at((int64_t)(cand[j] & 0xffffffffu))];
+            const float* qr = rs.Q + (int64_t)q * rs.ldq;
+            e = rs.bf16_rows ? exact_l2_row<true>(qr, rs.rows, row, rs.row_ld, rs.dim)
+                             : exact_l2_row<false>(qr, rs.rows, row, rs.row_ld, rs.dim);
+            exact[j] = e;
+        }
+        __syncthreads();
+        int n2 = 1;
+        while (n2 < kk) n2 <<= 1;
+        if (j < n2) cand[j] = j < kk ? (((unsigned long long)float_key(e) << 32) | (uint32_t)j) : ~0ull;
+        __syncthreads();
+        bitonic_u64(cand, n2);
+    }
     for (int j = threadIdx.x; j < k; j += MRG_BLOCK) {
         int64_t id = -1;
         float s = INF;
         if (j < kk) {
             const unsigned long long c = cand[j];
-            const int64_t off = at((int64_t)(c & 0xffffffffu));
-            s = ps[off];
-            id = row_ids ? row_ids[pr[off]] : pr[off];
+            if (rescore) {
+                const uint32_t w = (uint32_t)(c & 0xffffffffu);
+                s = exact[w];
+                id = row_ids[pr[at((int64_t)(won[w] & 0xffffffffu))]];
+            } else {
+                const int64_t off = at((int64_t)(c & 0xffffffffu));
+                s = ps[off];
+                id = row_ids ? row_ids[pr[off]] : pr[off];
+            }
         }
         out_ids[(int64_t)q * k + j] = id;
         out_scores[(int64_t)q * k + j] = s;
@@ -887,11 +950,14 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
 
 cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
                               const int64_t* row_ids, int nq, int P, int k, int64_t* out_ids,
-                              float* out_scores, int32_t* out_counts, cudaStream_t st) {
+                              float* out_scores, int32_t* out_counts, cudaStream_t st,
+                              const MergeRescore* rs) {
     if (nq <= 0) return cudaSuccess;
+    if (rs && (k > MRG_BLOCK || !row_ids)) return cudaErrorInvalidValue;
+    const MergeRescore none{};
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(part_score, part_row, row_ids, P, k,
                                                 (int64_t)P * k, k, out_ids, out_scores,
-                                                out_counts);
+                                                out_counts, rs ? *rs : none, rs ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -917,7 +983,8 @@ cudaError_t launch_merge_shards(const float* scores, const int64_t* ids, int nsh
                                 cudaStream_t st) {
     if (nq <= 0 || k <= 0) return cudaSuccess;
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(scores, ids, nullptr, nshard, k, k,
-                                                (int64_t)nq * k, out_ids, out_scores, out_counts);
+                                                (int64_t)nq * k, out_ids, out_scores, out_counts,
+                                                MergeRescore{}, 0);
     return cudaGetLastError();
 }
 

@@ -1,9 +1,17 @@
-// k_scan_tc.cu -- the inverted-list scan on the tensor cores, for the inner
-// product and cosine metrics (Cluster::search_into, AgentMemory/M3/src/
-// cluster.cpp:229-274, driven by IVFIndex::search_nprobe, AgentMemory/M3/src/
-// m3_index.cpp:368-483), list-centric like the SIMT scan (k_scan.cu): one work
-// item is one list with up to 32 of the queries that probe it, so a list is
+// k_scan_tc.cu -- the inverted-list scan on the tensor cores, for every metric
+// (Cluster::search_into, AgentMemory/M3/src/cluster.cpp:229-274, driven by
+// IVFIndex::search_nprobe, AgentMemory/M3/src/m3_index.cpp:368-483),
+// list-centric like the SIMT scan (k_scan.cu): one work item is one list with
+// up to 32 (k <= 32) or 16 (k <= 128) of the queries that probe it, so a list is
 // normally streamed from HBM once per search batch.
+//
+// Two row formats: fp32 rows (the reference's storage, split into bf16 hi / lo
+// on chip as below) and bf16 rows (half the bytes; the row is its own bf16 hi
+// part, so only q is split: x . [q_hi | q_lo], two MMAs per 32 dims).
+// Squared L2 is ranked by ||x||^2 - 2 <x, q> + ||q||^2 from the same dot
+// product; the merge then rescores the answer's rows in the reference's own
+// arithmetic (sum of (q_i - x_i)^2 in index order), since the expansion loses
+// relative accuracy for rows very close to the query.
 //
 // Arithmetic.  <x, q> in fp32 accuracy from four bf16 MMAs per 32-dim chunk
 // (tcgen05.mma kind::f16, K = 16, fp32 accumulation in TMEM): each fp32 value
@@ -48,16 +56,16 @@
 namespace m3g {
 namespace {
 
-constexpr int TK = 32;                        // dims per stage (128 B of fp32)
+constexpr int TK = 32;                        // dims per chunk (128 B of fp32)
 constexpr int TROWS = 128;                    // rows per block (MMA M)
-constexpr int SCHK = 2;                       // chunks per stage
+constexpr int SCHK = 2;                       // chunks per stage (64 dims)
 constexpr int CHK_BYTES = TROWS * TK * 4;     // 16 KB: one block's 32-dim chunk, fp32
-constexpr int X_BYTES = SCHK * CHK_BYTES;     // 32 KB stage: one block (128 rows) x 64 dims
-constexpr int QMAX = 32;                      // queries per item
+constexpr int QMAX = 32;                      // queries per item (at most)
 // the query tiles of a stage's two chunks: 64 rows [q_hi | q_lo] of 128 B, chunk j's
 // 32 bf16 dims in bytes 64 j .. 64 j + 63 of each row
 constexpr int QSLOT_BYTES = 2 * QMAX * 128;
-constexpr int NXS = 6;                        // stages (fp32 as loaded, bf16 hi / lo once converted)
+constexpr int RING_BYTES = 192 * 1024;        // the stage ring: 6 x 32 KB fp32, 12 x 16 KB bf16
+constexpr int NXS_MAX = 12;
 constexpr int NQS = 2;                        // query chunk slots
 constexpr int NSPLIT = 8;
 constexpr int NEPI = 4;
@@ -69,8 +77,21 @@ constexpr int NINFO = 4;                      // work items queued ahead of the 
 constexpr int NTHR = NWARPS * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int HALF_COLS = 256;
-constexpr int KMAX_TC = 32;
+constexpr int KMAX_TC = 128;
 constexpr int EPI_BAR = 1;                    // named barrier of the epilogue warps
+
+// Stage geometry of one row format: a stage is one 128-row block x 64 dims.
+template <bool XB>
+struct StageFmt {
+    static constexpr int X_BYTES = XB ? TROWS * 128 : 2 * CHK_BYTES;  // 16 KB bf16, 32 KB fp32
+    static constexpr int NXS = RING_BYTES / X_BYTES;                  // 12 / 6 stages
+};
+// Queries per item and register top-k width for a k limit.
+template <int KW>
+struct ItemFmt {
+    static constexpr int QM = KW == 1 ? 32 : 16;  // queries per item
+    static constexpr int QPW = QM / 4;            // queries per epilogue warp
+};
 static_assert(NSPLIT * 32 == SCHK * TROWS, "a split thread owns one row of one chunk of a stage");
 static_assert(QSLOT_BYTES % 1024 == 0, "query tiles stay 1024-byte aligned");
 static_assert(NSPLIT * 32 == QMAX * 8, "a split thread owns 16 bytes of a query chunk");
@@ -93,7 +114,7 @@ __host__ __device__ constexpr LayoutTC make_layout_tc() {
     LayoutTC L{};
     uint32_t o = 0;
     L.x_off = o;
-    o += NXS * X_BYTES;
+    o += RING_BYTES;
     L.q_off = o;
     o += NQS * QSLOT_BYTES;
     L.sc_off = o;
@@ -104,7 +125,7 @@ __host__ __device__ constexpr LayoutTC make_layout_tc() {
     o += NINFO * (uint32_t)sizeof(ItemTC);
     o = (o + 15u) & ~15u;
     L.bar_off = o;
-    o += 64 * 8;
+    o += 3 * NXS_MAX * 8 + 64 * 8;
     L.total = o + 1024;  // slack for aligning the base to 1024 bytes
     return L;
 }
@@ -166,8 +187,14 @@ struct Geo {
     }
 };
 
+// XB: bf16 rows (else fp32); KW: register top-k width (k <= 32 KW).
+template <bool XB, int KW>
 __global__ void __launch_bounds__(NTHR, 1)
     list_scan_tc_kernel(const __grid_constant__ RowMaps maps, const ScanArgs a) {
+    constexpr int X_BYTES = StageFmt<XB>::X_BYTES;
+    constexpr int NXS = StageFmt<XB>::NXS;
+    constexpr int QM = ItemFmt<KW>::QM;
+    constexpr int QPW = ItemFmt<KW>::QPW;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -263,9 +290,11 @@ __global__ void __launch_bounds__(NTHR, 1)
                         const int r8 = (min(TROWS, nrows - row0) + 7) & ~7;
                         const int y0 = (int)(off + row0);
                         uint64_t* bar = &xfull[xr.i];
+                        // bf16 rows: one 64-dim box (128 B per row) covers the stage
+                        const int nbox = XB ? 1 : nch;
                         if (leader) {
-                            mbar_arrive_expect_tx(bar, (uint32_t)(nch * r8 * 128));
-                            for (int j = 0; j < nch; ++j) {
+                            mbar_arrive_expect_tx(bar, (uint32_t)(nbox * r8 * 128));
+                            for (int j = 0; j < nbox; ++j) {
                                 const int x = (c + j) * TK;
                                 const uint32_t dst = xbase + (uint32_t)xr.i * X_BYTES + j * CHK_BYTES;
                                 if (r8 == 128) {
@@ -329,12 +358,23 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
                     const uint64_t dq = dq0 + (uint64_t)((qr.i * QSLOT_BYTES) >> 4);
                     for (int b = 0; b < pb; ++b) {
-                        if (!__all_sync(0xffffffffu, mbar_wait(&xready[xr.i], xr.ph, err))) {
+                        // fp32 rows wait for the split warps' conversion; bf16 rows are
+                        // MMA operands as they land
+                        uint64_t* ready = XB ? &xfull[xr.i] : &xready[xr.i];
+                        if (!__all_sync(0xffffffffu, mbar_wait(ready, xr.ph, err))) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        if (leader) {
+                        if (leader && XB) {
+                            // row r of the stage: dims 0..63 as bf16 in its 128 B; K step
+                            // k (16 dims, 32 B) meets the query tile's bytes 32 k .. 32 k + 31
+                            const uint32_t d = tmem + (uint32_t)(h * HALF_COLS + b * 2 * g.nqp);
+                            const uint64_t dx = dx0 + (uint64_t)((xr.i * X_BYTES) >> 4);
+                            for (int k = 0; k < 2 * nch; ++k)
+                                tc_mma_f16(d, dx + 2 * k, dq + 2 * k, id_bf16, (c | k) != 0);
+                            tc_commit(&xempty[xr.i]);
+                        } else if (leader) {
                             const uint32_t d = tmem + (uint32_t)(h * HALF_COLS + b * 2 * g.nqp);
                             for (int j = 0; j < nch; ++j) {
                                 // chunk j's rows: x_hi in bytes 0..63, x_lo in 64..127
@@ -425,22 +465,21 @@ __global__ void __launch_bounds__(NTHR, 1)
                         const uint32_t sl = q_u32 + (uint32_t)qr.i * QSLOT_BYTES;
 #pragma unroll
                         for (int j = 0; j < SCHK; ++j) {
-                            if (j < nch) {
-                                const uint32_t cb = ((((uint32_t)(4 * j + (qj >> 1))) ^ sw) << 4) +
-                                                    (uint32_t)(qj & 1) * 8;
-                                uint32_t h0, h1, l0, l1;
-                                bf16x2_split(qv[j].x, qv[j].y, &h0, &l0);
-                                bf16x2_split(qv[j].z, qv[j].w, &h1, &l1);
-                                sts64(sl + qn * 128 + cb, h0, h1);
-                                sts64(sl + (g.nqp + qn) * 128 + cb, l0, l1);
-                            }
+                            // (a chunk past the last holds zeros: qload gives them)
+                            const uint32_t cb = ((((uint32_t)(4 * j + (qj >> 1))) ^ sw) << 4) +
+                                                (uint32_t)(qj & 1) * 8;
+                            uint32_t h0, h1, l0, l1;
+                            bf16x2_split(qv[j].x, qv[j].y, &h0, &l0);
+                            bf16x2_split(qv[j].z, qv[j].w, &h1, &l1);
+                            sts64(sl + qn * 128 + cb, h0, h1);
+                            sts64(sl + (g.nqp + qn) * 128 + cb, l0, l1);
                         }
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&qfull[qr.i]);
                     qr.next(NQS);
-                    for (int b = 0; b < pb; ++b) {
+                    for (int b = 0; b < (XB ? 0 : pb); ++b) {
                         if (!__all_sync(0xffffffffu, mbar_wait(&xfull[xr.i], xr.ph, err))) {
                             ok = false;
                             break;
@@ -510,7 +549,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                 nrows = a.list_len[wi.list];
                 off = a.list_off[wi.list];
             }
-            if (np < 1 || np > QMAX || nrows < 0) {
+            if (np < 1 || np > QM || nrows < 0) {
                 if (leader) {
                     atomicCAS(err, 0, (int)kErrBadItem);
                     inf->list = -1;
@@ -549,9 +588,9 @@ __global__ void __launch_bounds__(NTHR, 1)
             const int64_t off = inf->off;
             // rows scoring above a query's bound cannot reach its answer: the bound
             // is the k-th best score of one of its lists already scanned
-            RegTopK rt[QMAX / NEPI];
+            RegTopKW<KW> rt[QPW];
 #pragma unroll
-            for (int j = 0; j < QMAX / NEPI; ++j) {
+            for (int j = 0; j < QPW; ++j) {
                 const int qi = ew + NEPI * j;
                 if (qi < g.np && a.qbound) {
                     const uint32_t bk = ~a.qbound[inf->q[qi]];  // score key (0xffffffff: none)
@@ -575,12 +614,13 @@ __global__ void __launch_bounds__(NTHR, 1)
                     float nb2 = 0.f;
                     if (live) {
                         live = a.alive[off + lrow] != 0;
-                        if (a.metric == kCosine && !a.normalized) nb2 = a.rnorm2[off + lrow];
+                        if (a.metric == kL2 || (a.metric == kCosine && !a.normalized))
+                            nb2 = a.rnorm2[off + lrow];
                     }
                     // columns [0, nqp): x q_hi; [nqp, 2 nqp): x q_lo; 16 queries per
                     // round: drained to the score tile, then pushed into the top-k
 #pragma unroll
-                    for (int hq = 0; hq < QMAX / QHALF; ++hq) {
+                    for (int hq = 0; hq < QM / QHALF; ++hq) {
                         const int q0 = hq * QHALF;
                         if (q0 >= g.np) break;  // the same for every epilogue warp
                         uint32_t c0[QHALF], c1[QHALF];
@@ -593,6 +633,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                                 float s = INF;
                                 if (live) {
                                     if (a.metric == kIP) s = -dot;
+                                    else if (a.metric == kL2)  // ranking only; rescored at the merge
+                                        s = (nb2 + a.qnorm2[inf->q[q0 + i]]) - 2.f * dot;
                                     else if (a.normalized) s = 1.f - dot;
                                     else {
                                         const float na = a.qnorm2[inf->q[q0 + i]];
@@ -629,20 +671,25 @@ __global__ void __launch_bounds__(NTHR, 1)
             if (!ok) break;
             // the item's answers: top-k per (query, probe slot)
 #pragma unroll
-            for (int j = 0; j < QMAX / NEPI; ++j) {
+            for (int j = 0; j < QPW; ++j) {
                 const int qi = ew + NEPI * j;
                 if (qi < g.np) {
                     if (rt[j].nbuf) rt[j].flush(kbuf + qi * 32, a.k, lane);
                     // a full top-k bounds the query's final k-th score
-                    const unsigned long long kth = shfl_u64(rt[j].top, a.k - 1);
+                    const unsigned long long kth = rt[j].entry(a.k - 1);
                     if (a.qbound && lane == 0 && kth != ~0ull)
                         atomicMax(&a.qbound[inf->q[qi]], ~(uint32_t)(kth >> 32));
                     const int64_t base = ((int64_t)inf->q[qi] * a.P + inf->slot[qi]) * a.k;
-                    if (lane < a.k) {
-                        const unsigned long long t = rt[j].top;
-                        const bool v = t != ~0ull;
-                        a.part_score[base + lane] = v ? key_float((uint32_t)(t >> 32)) : INF;
-                        a.part_row[base + lane] = v ? off + (int64_t)(uint32_t)(t & 0xffffffffu) : -1;
+#pragma unroll
+                    for (int w = 0; w < KW; ++w) {
+                        const int e = 32 * w + lane;
+                        if (e < a.k) {
+                            const unsigned long long t = rt[j].top[w];
+                            const bool v = t != ~0ull;
+                            a.part_score[base + e] = v ? key_float((uint32_t)(t >> 32)) : INF;
+                            a.part_row[base + e] =
+                                v ? off + (int64_t)(uint32_t)(t & 0xffffffffu) : -1;
+                        }
                     }
                 }
             }
@@ -661,18 +708,25 @@ __global__ void __launch_bounds__(NTHR, 1)
 
 }  // namespace
 
-bool scan_tc_supported(int metric, int k) { return metric != kL2 && k >= 1 && k <= KMAX_TC; }
+bool scan_tc_supported(int metric, int k) {
+    return metric >= kL2 && metric <= kCosine && k >= 1 && k <= KMAX_TC;
+}
 
-int scan_tc_gmax() { return QMAX; }
+int scan_tc_gmax(int k) { return k <= 32 ? ItemFmt<1>::QM : ItemFmt<4>::QM; }
 
-cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, int grid, cudaStream_t st) {
+cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, bool bf16_rows, int grid,
+                                cudaStream_t st) {
     if (!scan_tc_supported(a.metric, a.k) || (a.dpad & 3)) return cudaErrorInvalidValue;
     const LayoutTC L = make_layout_tc();
-    cudaError_t e = cudaFuncSetAttribute(list_scan_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
-    if (e != cudaSuccess) return e;
-    list_scan_tc_kernel<<<grid, NTHR, L.total, st>>>(maps, a);
-    return cudaGetLastError();
+    auto go = [&](auto kern) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)L.total);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, NTHR, L.total, st>>>(maps, a);
+        return cudaGetLastError();
+    };
+    if (bf16_rows) return a.k <= 32 ? go(list_scan_tc_kernel<true, 1>) : go(list_scan_tc_kernel<true, 4>);
+    return a.k <= 32 ? go(list_scan_tc_kernel<false, 1>) : go(list_scan_tc_kernel<false, 4>);
 }
 
 }  // namespace m3g

@@ -80,11 +80,13 @@ int scan_gmax_for_dim(int dpad);
 cudaError_t launch_list_scan(const RowMaps& maps, const ScanArgs& a, int gmax, int grid,
                              cudaStream_t st);
 
-// The tensor-core scan (k_scan_tc.cu): inner product and cosine, k <= 32,
-// items of up to scan_tc_gmax() queries.
+// The tensor-core scan (k_scan_tc.cu): every metric, k <= 128, items of up to
+// scan_tc_gmax(k) queries; rows fp32 or (bf16_rows) bf16.  Squared L2 comes out
+// as a ranking estimate that the merge must rescore (MergeRescore).
 bool scan_tc_supported(int metric, int k);
-int scan_tc_gmax();
-cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, int grid, cudaStream_t st);
+int scan_tc_gmax(int k);
+cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, bool bf16_rows, int grid,
+                                cudaStream_t st);
 
 // Work list: per-list counts of (query, probe) pairs, items, and the pairs
 // grouped by list.  list_order lists the clusters longest first.  With
@@ -96,10 +98,24 @@ cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
                                   int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
                                   cudaStream_t st, const int32_t* skip_len = nullptr);
 
-// Final merge of the per-(query, probe) partial top-k into the answer.
+// Exact squared-L2 rescoring of a merge's winners: the reference's sum of
+// (q_i - x_i)^2 in index order (AgentMemory/M3/src/base.cpp:12-20) over the
+// arena rows (fp32, or bf16 widened to fp32) and the queries.
+struct MergeRescore {
+    const float* Q;        // [nq, ldq] queries
+    int64_t ldq;
+    const void* rows;      // arena rows, row_ld elements apart
+    int64_t row_ld;
+    int dim;
+    int bf16_rows;
+};
+
+// Final merge of the per-(query, probe) partial top-k into the answer; with rs,
+// the winners' scores are replaced by exact squared-L2 scores and re-sorted.
 cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
                               const int64_t* row_ids, int nq, int P, int k, int64_t* out_ids,
-                              float* out_scores, int32_t* out_counts, cudaStream_t st);
+                              float* out_scores, int32_t* out_counts, cudaStream_t st,
+                              const MergeRescore* rs = nullptr);
 
 // Merge of per-shard answers [nshard, nq, k] (scores ascending per row, ids,
 // -1 / +inf padding) into [nq, k]; ties broken by (shard, position).

@@ -1,6 +1,7 @@
 // kernels_kmeans.h -- launchers of k_kmeans.cu (internal to libm3gpu).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -23,6 +24,13 @@ cudaError_t launch_gather_rows(const float* src, int64_t lds, const int64_t* idx
                                int width, float* dst, int64_t ldd, cudaStream_t st);
 cudaError_t launch_scatter_rows(const float* src, int64_t lds, const int64_t* dst_rows, int64_t n,
                                 int width, float* dst, int64_t ldd, cudaStream_t st);
+// bf16 rows of the list arena: values rounded to bf16 in place (kept as fp32),
+// packed fp32 -> bf16 rows (columns dim .. ldd zero), and widened back.
+cudaError_t launch_round_bf16_rows(float* X, int64_t ld, int64_t n, int dim, cudaStream_t st);
+cudaError_t launch_pack_bf16_rows(const float* src, int64_t lds, int64_t n, int dim,
+                                  __nv_bfloat16* dst, int64_t ldd, cudaStream_t st);
+cudaError_t launch_unpack_bf16_rows(const __nv_bfloat16* src, int64_t lds, int64_t n, int dim,
+                                    float* dst, int64_t ldd, cudaStream_t st);
 cudaError_t launch_gather_i64(const int64_t* src, const int64_t* idx, int64_t n, int64_t* dst,
                               cudaStream_t st);
 cudaError_t launch_gather_f32(const float* src, const int64_t* idx, int64_t n, float* dst,

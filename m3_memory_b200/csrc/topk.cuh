@@ -1,7 +1,8 @@
-// topk.cuh -- warp-level top-k (k <= 32) of the list scans: lane i of a warp
-// holds the i-th best key of one query, key = (score key << 32) | row,
-// ascending, ~0 marking an empty slot; rows that beat the current k-th key are
-// buffered in shared memory and merged in by a bitonic sort + merge.
+// topk.cuh -- warp-level top-k of the list scans: a warp holds one query's best
+// keys, key = (score key << 32) | row, ascending, ~0 marking an empty slot;
+// rows that beat the current k-th key are buffered in shared memory and merged
+// in by a bitonic sort + merge.  RegTopK: k <= 32, lane i holds entry i.
+// RegTopKW<KW>: k <= 32 KW, lane i holds entries i, 32 + i, ..., 32 (KW-1) + i.
 #pragma once
 
 #include "common.cuh"
@@ -75,6 +76,90 @@ struct RegTopK {
         top = warp_merge_top(top, b, lane);
         if (lane >= k) top = ~0ull;
         tau = shfl_u64(top, k - 1);
+        tau = tau < cap ? tau : cap;
+        nbuf = 0;
+    }
+
+    __device__ __forceinline__ void push(unsigned long long* buf, int k, float s, int32_t row,
+                                         int lane) {
+        const unsigned long long key =
+            score_valid(s) ? (((unsigned long long)float_key(s) << 32) | (uint32_t)row) : ~0ull;
+        bool cand = key < tau;
+        unsigned ball = __ballot_sync(0xffffffffu, cand);
+        if (!ball) return;
+        int cnt = __popc(ball);
+        if (nbuf + cnt > 32) {
+            flush(buf, k, lane);
+            cand = key < tau;
+            ball = __ballot_sync(0xffffffffu, cand);
+            cnt = __popc(ball);
+        }
+        if (cand) buf[nbuf + __popc(ball & ((1u << lane) - 1u))] = key;
+        nbuf += cnt;
+    }
+};
+
+// Second half of a bitonic merge: v is bitonic across the warp; afterwards it
+// is ascending.
+__device__ __forceinline__ unsigned long long warp_bitonic_clean(unsigned long long v, int lane) {
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) {
+        const unsigned long long p = shfl_xor_u64(v, j);
+        const bool lower = (lane & j) == 0;
+        v = lower ? (p < v ? p : v) : (p > v ? p : v);
+    }
+    return v;
+}
+
+// Register top-k of up to 32 KW entries, fed like RegTopK.  A flush sorts the
+// buffer and merges it level by level: level w keeps the 32 smallest of its
+// entries and the carried keys, and carries the 32 largest on (the smallest 32
+// of the union of an ascending list and anything can only come from the
+// list's first 32 entries and that thing, so the cascade keeps the whole list
+// sorted).  KW = 1 is RegTopK exactly.
+template <int KW>
+struct RegTopKW {
+    unsigned long long top[KW];      // lane i: entries i + 32 w (ascending)
+    unsigned long long tau = ~0ull;  // keys below it enter the buffer (all lanes)
+    unsigned long long cap = ~0ull;  // upper bound of tau
+    int nbuf = 0;                    // keys waiting in the buffer (warp-uniform)
+
+    __device__ __forceinline__ RegTopKW() {
+#pragma unroll
+        for (int w = 0; w < KW; ++w) top[w] = ~0ull;
+    }
+
+    __device__ __forceinline__ void set_cap(unsigned long long c) {
+        cap = c;
+        tau = tau < c ? tau : c;
+    }
+
+    // key of entry e (warp-uniform e < 32 KW), in every lane
+    __device__ __forceinline__ unsigned long long entry(int e) const {
+        unsigned long long v = ~0ull;
+#pragma unroll
+        for (int w = 0; w < KW; ++w)
+            if ((e >> 5) == w) v = top[w];
+        return shfl_u64(v, e & 31);
+    }
+
+    __device__ __forceinline__ void flush(unsigned long long* buf, int k, int lane) {
+        __syncwarp();
+        const unsigned long long b = lane < nbuf ? buf[lane] : ~0ull;
+        __syncwarp();
+        unsigned long long c = warp_sort_asc(b, lane);
+#pragma unroll
+        for (int w = 0; w < KW; ++w) {
+            const unsigned long long rc = shfl_u64(c, 31 - lane);
+            const unsigned long long lo = top[w] < rc ? top[w] : rc;
+            const unsigned long long hi = top[w] < rc ? rc : top[w];
+            top[w] = warp_bitonic_clean(lo, lane);
+            if (w + 1 < KW) c = warp_bitonic_clean(hi, lane);
+        }
+#pragma unroll
+        for (int w = 0; w < KW; ++w)
+            if (32 * w + lane >= k) top[w] = ~0ull;
+        tau = entry(k - 1);
         tau = tau < cap ? tau : cap;
         nbuf = 0;
     }

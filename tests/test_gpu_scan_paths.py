@@ -1,11 +1,13 @@
-"""The tensor-core list scan (the default for inner product and cosine with
-k <= 32) against the oracle, and against the SIMT scan (M3G_SCAN=simt, run in a
-child process because the choice is read once per process).
+"""The tensor-core list scan (the default for every metric with k <= 128)
+against the oracle, and against the SIMT scan (M3G_SCAN=simt, run in a child
+process because the choice is read once per process).
 
 The cases exercise the scan's structure: a list longer than one pass of row
-blocks (2100 rows), ragged last blocks, a dimension that is not a multiple of
-32, empty and tiny lists, erased rows, items of up to 32 queries, k up to
-32, and both cosine forms."""
+blocks (2100 rows), ragged last blocks, dimensions that are not a multiple of
+32 or 64, empty and tiny lists, erased rows, items of up to 32 queries (k <= 32)
+or 16 queries (k <= 128, four register entries per lane), k up to 128, squared
+L2 (ranked by its expansion, rescored exactly at the merge) and both cosine
+forms."""
 import os
 import subprocess
 import sys
@@ -27,6 +29,11 @@ CASES = {
     "ip_narrow_items": (1, False, 96, 40, 1, 10),   # one probe: tiny lists alone
     "cos_raw_k32": (2, False, 64, 48, 3, 32),
     "cos_norm_all": (2, True, 128, 30, -1, 7),
+    "l2_k10": (0, False, 96, 40, 2, 10),
+    "l2_k100_dim100": (0, False, 100, 40, 3, 100),
+    "ip_k64": (1, False, 96, 40, 3, 64),
+    "cos_raw_k128": (2, False, 64, 24, 4, 128),
+    "l2_k33_all": (0, False, 36, 20, -1, 33),
 }
 
 
@@ -113,7 +120,7 @@ def test_tensor_core_and_simt_scans_agree(cuda_ok, tmp_path):
         compare_search(got, ref, rtol=1e-4, atol=1e-6)
 
 
-@pytest.mark.parametrize("metric", [1, 2])
+@pytest.mark.parametrize("metric", [0, 1, 2])
 def test_exact_duplicates_across_lists_keep_the_reference_order(cuda_ok, oracle_mod, metric):
     """The same 24 vectors stored in each of 6 lists (plus distinct rows): the
     top-k is made of exact score ties across lists.  Rows tying the per-query
@@ -147,4 +154,38 @@ def test_exact_duplicates_across_lists_keep_the_reference_order(cuda_ok, oracle_
         c = int(ref[2][q])
         exact = [oracle_mod.score(Q[q], X[row_of[int(i)]], metric, False) for i in got[0][q, :c]]
         np.testing.assert_array_equal(np.array(exact, np.float32), ref[1][q, :c], err_msg=str(q))
+    compare_search(got, ref)
+
+
+@pytest.mark.parametrize("k", [10, 100])
+def test_l2_queries_on_stored_rows_get_exact_scores(cuda_ok, oracle_mod, k):
+    """Queries equal to stored rows (distance 0) and a hair away from them: the
+    expansion ||x||^2 - 2<x,q> + ||q||^2 cannot resolve these, the merge's exact
+    rescoring must -- every returned score is the reference's own sum of
+    squared differences, and the stored row itself comes first."""
+    from m3_memory_b200 import cabi
+
+    rng = np.random.default_rng(5 + k)
+    d, L = 192, 8
+    C = (3.0 * rng.standard_normal((L, d))).astype(np.float32)
+    sizes = [300, 520, 10, 0, 410, 130, 999, 64]
+    owner = np.repeat(np.arange(L), sizes)
+    X = (C[owner] + rng.standard_normal((len(owner), d))).astype(np.float32)
+    off = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    pick = rng.choice(len(X), 24, replace=False)
+    Q = X[pick].copy()
+    Q[12:] += np.float32(1e-3) * rng.standard_normal((12, d)).astype(np.float32)
+    ids = np.arange(len(X), dtype=np.int64) + 1000
+    case = dict(metric=0, normalized=False, C=C, X=X, Q=Q, ids=ids,
+                alive=np.ones(len(X), np.uint8), off=off, nprobe=3, k=k)
+    got = engine_search(cabi, case)
+    lists = oracle_mod.CsrLists(off, X, ids, case["alive"])
+    ref = oracle_mod.search_nprobe(Q, C, lists, 0, False, k, 3)
+    np.testing.assert_array_equal(got[2], ref[2])
+    for q in range(len(Q)):
+        c = int(ref[2][q])
+        exact = [oracle_mod.score(Q[q], X[int(i) - 1000], 0, False) for i in got[0][q, :c]]
+        np.testing.assert_array_equal(np.array(exact, np.float32), got[1][q, :c], err_msg=str(q))
+        if q < 12:
+            assert got[0][q, 0] == ids[pick[q]] and got[1][q, 0] == 0.0
     compare_search(got, ref)
