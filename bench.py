@@ -368,6 +368,30 @@ def run_reference(args, rank, world):
 
 
 # ---------------------------------------------------------------- our arm
+def build_headline_index(eng, X, rank=0, world=1):
+    """The headline index on the engine (index id 1): k-means on the seeded sample,
+    every row assigned to its nearest centroid, this rank's lists loaded (ids = row
+    numbers).  Returns (centroids, assignment, list owners)."""
+    from m3_memory_b200.sharding import shard_lists
+
+    t0 = time.perf_counter()
+    C, _ = eng.kmeans(X[kmeans_sample()], NLIST, KMEANS_ITERS, SEED, METRIC_IP, False)
+    eng.create_ivf(1, DIM, METRIC_IP, False, C)
+    assign = eng.nearest_clusters(1, X)
+    log(f"[rank {rank}] k-means {KMEANS_ITERS} it + assignment on the GPU: "
+        f"{time.perf_counter() - t0:.1f}s")
+    sizes = np.bincount(assign, minlength=NLIST)
+    owner = shard_lists(sizes, world)
+    order = np.argsort(assign, kind="stable")
+    bounds = np.searchsorted(assign[order], np.arange(NLIST + 1))
+    for c in range(NLIST):
+        b, e = bounds[c], bounds[c + 1]
+        if e > b and owner[c] == rank:
+            rows = order[b:e]
+            eng.load_cluster(1, c, rows.astype(np.int64), X[rows])
+    return C, assign, owner
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -381,26 +405,8 @@ def run_ours(args, rank, world, local_rank):
     X, Qb = make_data()
     log(f"[rank {rank}] data ready in {time.perf_counter() - t_setup:.1f}s")
     eng = cabi.Engine()
-    ids = np.arange(N_VEC, dtype=np.int64)
-    t0 = time.perf_counter()
-    C, _ = eng.kmeans(X[kmeans_sample()], NLIST, KMEANS_ITERS, SEED, METRIC_IP, False)
-    eng.create_ivf(1, DIM, METRIC_IP, False, C)
-    assign = eng.nearest_clusters(1, X)
-    log(f"[rank {rank}] k-means {KMEANS_ITERS} it + assignment on the GPU: "
-        f"{time.perf_counter() - t0:.1f}s")
-    sizes = np.bincount(assign, minlength=NLIST)
-    owner = shard_lists(sizes, world)
-    order = np.argsort(assign, kind="stable")
-    bounds = np.searchsorted(assign[order], np.arange(NLIST + 1))
-    local_rows = 0
-    for c in range(NLIST):
-        b, e = bounds[c], bounds[c + 1]
-        if e > b and owner[c] == rank:
-            rows = order[b:e]
-            eng.load_cluster(1, c, ids[rows], X[rows])
-            local_rows += e - b
-    log(f"[rank {rank}] index loaded ({local_rows} rows local) "
-        f"after {time.perf_counter() - t_setup:.1f}s")
+    C, assign, owner = build_headline_index(eng, X, rank, world)
+    log(f"[rank {rank}] index ready after {time.perf_counter() - t_setup:.1f}s")
 
     Qd = torch.from_numpy(Qb).to(dev)  # [NBATCH, BATCH, DIM]
     coarse = {}
@@ -684,7 +690,7 @@ def run_config3(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    n, d, nlist, K3 = args.c3_n or C3_N, C3_DIM, C3_NLIST, C3_K
+    n, d, nlist, K3 = args.c3_n or C3_N, C3_DIM, C3_NLIST, args.c3_k or C3_K
     storage = cabi.BF16 if args.storage == "bf16" else cabi.F32
     t0 = time.perf_counter()
     X, Qd = device_mixture(n, C3_NQ, d, C3_NCOMP, SIGMA, SEED + 3, dev)
@@ -852,7 +858,9 @@ def run_config3(args, rank, world, local_rank):
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "bf16 rows, fp32 queries and accumulation",
         "data": "synthetic (seeded 10k-component Gaussian mixture generated on the GPU)",
-        "config": {"workload": f"ivf-search: {n // 1_000_000}M x {d} {args.storage}-stored "
+        "config": {"workload": ("PROFILING CASE (not the bf16 configuration): "
+                                if (args.c3_n or args.c3_k) else "") +
+                               f"ivf-search: {n // 1_000_000}M x {d} {args.storage}-stored "
                                f"mixture({C3_NCOMP}), L2, nlist {nlist}, nprobe {head_p}, "
                                f"k {K3}, batch {B}",
                    "n_vectors": n, "dim": d, "nlist": nlist, "nprobe": head_p, "k": K3,
@@ -864,6 +872,133 @@ def run_config3(args, rank, world, local_rank):
         if world > 1 else "1 GPU",
         "gpu_launches": None, "clocks": clocks, "e2e": e2e, "roofline": roofline,
         "cpu_baseline": cpu, "parity": parity,
+    })
+
+
+# ---------------------------------------------------------------- insert + split stream
+# From the headline index: 1M new rows from shifted mixture means (offset
+# N(0, 0.5^2) in norm), in batches of 8,192 routed by enqueue_insert_auto; after
+# every batch one split pass (lists over 2x the mean size, 2-means, 5 rounds)
+# and a 1,024-query search (k 10, nprobe 32).
+C5_INSERT = 1_000_000
+C5_BATCH = 8192
+C5_SPLIT_FACTOR = 2.0
+C5_SPLIT_ITERS = 5
+
+
+def run_config5(args, rank, world, local_rank):
+    import torch
+
+    from m3_memory_b200 import cabi
+    from m3_memory_b200 import synthetic as S
+
+    if world > 1:
+        raise SystemExit("the insert + split stream runs on one GPU (one engine)")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    n_ins = args.c5_n or C5_INSERT
+    rng = np.random.default_rng(SEED)
+    means = S.mixture_means(NCOMP, DIM, rng)
+    X, _ = S.gaussian_mixture(N_VEC, means, SIGMA, rng)
+    Q, _ = S.gaussian_mixture(BATCH * NBATCH, means, SIGMA, rng)
+    shifted = S.shifted_means(means, 0.5, np.random.default_rng(SEED + 5))
+    Xi, _ = S.gaussian_mixture(n_ins, shifted, SIGMA, np.random.default_rng(SEED + 6))
+    Qs, _ = S.gaussian_mixture(BATCH * NBATCH, shifted, SIGMA, np.random.default_rng(SEED + 7))
+    eng = cabi.Engine()
+    build_headline_index(eng, X)
+    eng.start(2, 0)
+    # searches alternate between the original and the shifted distribution
+    Qd = torch.from_numpy(np.concatenate([Q, Qs]).reshape(-1, BATCH, DIM)).to(dev)
+    ids_d = torch.empty((BATCH, K), dtype=torch.int64, device=dev)
+    sc_d = torch.empty((BATCH, K), dtype=torch.float32, device=dev)
+    cnt_d = torch.empty((BATCH,), dtype=torch.int32, device=dev)
+
+    def search(i):
+        eng.search_device(1, Qd[i % Qd.shape[0]].data_ptr(), BATCH, K, NPROBE, ids_d.data_ptr(),
+                          sc_d.data_ptr(), cnt_d.data_ptr(),
+                          torch.cuda.current_stream(dev).cuda_stream)
+
+    nb = -(-n_ins // C5_BATCH)
+    warm = min(args.warmup, nb)
+    t_ins = t_split = 0.0
+    s_ms = []
+    splits = 0
+    t_all = None
+    for b in range(nb):
+        if b == warm:
+            torch.cuda.synchronize()
+            t_all = time.perf_counter()
+            t_ins = t_split = 0.0
+            s_ms = []
+        lo, hi = b * C5_BATCH, min(n_ins, (b + 1) * C5_BATCH)
+        t0 = time.perf_counter()
+        assert eng.enqueue_insert_auto(1, np.arange(N_VEC + lo, N_VEC + hi, dtype=np.int64), Xi[lo:hi])
+        eng.flush()
+        t1 = time.perf_counter()
+        splits += eng.split_oversized(1, C5_SPLIT_FACTOR, C5_SPLIT_ITERS, 1000 + b)
+        t2 = time.perf_counter()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        search(b)
+        ev1.record()
+        torch.cuda.synchronize()
+        t_ins += t1 - t0
+        t_split += t2 - t1
+        s_ms.append(ev0.elapsed_time(ev1))
+    wall = time.perf_counter() - t_all
+    eng.sync_errors()
+    timed_rows = n_ins - warm * C5_BATCH
+    nlist = eng.info(1)[3]
+    # recall of the final index against exact search over every row
+    Xall = torch.from_numpy(np.concatenate([X, Xi])).to(dev)
+    qe = Qd[1]
+    exact = exact_topk_ip(Xall, qe, K).cpu().numpy()
+    del Xall
+    got, _, _ = eng.search(1, qe.cpu().numpy(), K, NPROBE)
+    recall = recall_at_k(got, exact, K)
+    eng.stop()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+
+        if O.have_ref():
+            # the reference's own insert path (enqueue_insert_auto + flush) on the same
+            # centroids, a bounded batch
+            eng_centroids = eng.centroids(1)
+            re = O.RefEngine()
+            re.start(2, 0)
+            re.create_ivf(1, DIM, METRIC_IP, False, eng_centroids)
+            m = 1024
+            t0 = time.perf_counter()
+            re.enqueue_insert_auto(1, np.arange(m, dtype=np.int64), Xi[:m])
+            re.flush()
+            v = m / (time.perf_counter() - t0)
+            re.stop()
+            cpu = {"value": v, "unit": "rows/s", "cores": 1, "kind": "reference",
+                   "sample": f"one {m}-row enqueue_insert_auto + flush into the reference "
+                             f"AsyncEngine over the final {len(eng_centroids)} centroids "
+                             "(its routing is one thread)"}
+    emit({
+        "metric": "online insert+split stream: inserted rows/s with a 1,024-query search "
+                  "after every 8,192-row batch",
+        "value": timed_rows / wall, "unit": "rows/s", "n_gpus": 1, "steps": nb - warm,
+        "warmup": warm, "ms_per_step": 1e3 * wall / max(nb - warm, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded mixture; inserts from means shifted by N(0, 0.5^2) in norm)",
+        "config": {"workload": f"insert+split stream: {N_VEC // 1_000_000}M x {DIM} IP index, "
+                               f"nlist {NLIST} at start, {n_ins} inserts in batches of "
+                               f"{C5_BATCH}, split lists over {C5_SPLIT_FACTOR}x the mean "
+                               f"(2-means, {C5_SPLIT_ITERS} rounds), search k {K} nprobe "
+                               f"{NPROBE} batch {BATCH} after each batch",
+                   "parallelism": "1 GPU"},
+        "stream": {"insert_s": t_ins, "split_s": t_split, "search_ms_mean": statistics.mean(s_ms),
+                   "search_qps_mean": BATCH / (statistics.mean(s_ms) / 1e3),
+                   "splits": splits, "nlist_final": nlist, "recall_at_10_final": recall},
+        "cpu_baseline": cpu,
+        "e2e": {"value": timed_rows / wall, "unit": "rows/s",
+                "h2d_bytes_per_step": C5_BATCH * DIM * 4, "d2h_bytes_per_step": 0,
+                "path": "host rows through m3g_enqueue_insert_auto + m3g_flush + "
+                        "m3g_split_oversized; searches on device queries"},
     })
 
 
@@ -882,12 +1017,15 @@ def main():
                     help="profiling only: fewer vectors (the headline line uses 1M)")
     ap.add_argument("--nlist", type=int, default=None, help="profiling only: fewer lists")
     ap.add_argument("--nprobe", type=int, default=None, help="profiling only: other nprobe")
-    ap.add_argument("--config", type=int, choices=[2, 3], default=2,
+    ap.add_argument("--config", type=int, choices=[2, 3, 5], default=2,
                     help="2: the headline (1M x 1024 fp32, IP); 3: 10M x 768 bf16-stored lists, "
-                         "L2, nlist 16384, k 100, nprobe x batch sweep")
+                         "L2, nlist 16384, k 100, nprobe x batch sweep; 5: online insert + split "
+                         "stream from the headline index")
+    ap.add_argument("--c5-n", type=int, default=None, help="config 5, profiling only: inserts")
     ap.add_argument("--storage", choices=["bf16", "fp32"], default="bf16",
                     help="config 3: list storage")
     ap.add_argument("--c3-n", type=int, default=None, help="config 3, profiling only: rows")
+    ap.add_argument("--c3-k", type=int, default=None, help="config 3, profiling only: k")
     args = ap.parse_args()
     keep_stdout_for_result()
     global N_VEC, NLIST, NPROBE, FIXED_NPROBE, WORKLOAD
@@ -918,6 +1056,8 @@ def main():
     try:
         if args.config == 3:
             run_config3(args, rank, world, local_rank)
+        elif args.config == 5:
+            run_config5(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

@@ -83,6 +83,14 @@ int m3g_set_search_policy(m3g_engine* e, int default_nprobe, int parallel_querie
 int m3g_set_maintenance_policy(m3g_engine* e, double period_sec, size_t split_threshold,
                                double compact_ratio, int auto_split);
 
+/* The split rule of the maintenance pass (no reference counterpart: its
+ * split is a TODO, m3_index.cpp:304-311).  mean_factor > 0: with auto_split on,
+ * every pass splits the lists holding more than mean_factor x the mean live
+ * rows over all lists (m3g_split_oversized) instead of using split_threshold;
+ * niter: 2-means rounds per split (default 5).  m3g_set_maintenance_policy
+ * leaves this rule as it is. */
+int m3g_set_split_policy(m3g_engine* e, double mean_factor, int niter);
+
 /* AsyncEngine::create_ivf (m3_async.cpp:36-49 -> IVFIndex::set_centroids,
  * m3_index.cpp:98-131).  centroids: [nlist, dim]; nlist may be 0.  Replaces
  * an existing index of the same id. */
@@ -205,6 +213,16 @@ int m3g_get_cluster(m3g_engine* e, int index_id, int cluster_id, int64_t* out_id
  * centroids, then per list int64 n, int64 ids[n], float vectors[n * dim]. */
 int m3g_save_index(m3g_engine* e, int index_id, const char* path);
 int m3g_load_index(m3g_engine* e, int index_id, const char* path);
+/* rebuild_from_faiss (AgentMemory/M3/faiss_loader.py:24-79): replaces index_id
+ * with the contents of a Faiss IndexIVFFlat file (its flat quantizer's
+ * centroids, every inverted list's ids and fp32 vectors), read from Faiss's
+ * published serialization layout without the faiss package; metric L2 -> L2,
+ * inner product -> IP; normalized as given; storage M3G_F32 / M3G_BF16.  Only
+ * a plain IndexIVFFlat ("IwFl") with array inverted lists is read
+ * (M3G_EUNSUPPORTED otherwise); a missing file is M3G_ERUNTIME, a damaged one
+ * M3G_EINVAL / M3G_ERUNTIME, and neither changes the index. */
+int m3g_rebuild_from_faiss(m3g_engine* e, int index_id, const char* path, int normalized,
+                           int storage);
 /* IVFIndex::add_cluster / set_centroid (m3_index.cpp:133-163). */
 int m3g_add_cluster(m3g_engine* e, int index_id, const float* centroid, int32_t* out_cluster_id);
 int m3g_set_centroid(m3g_engine* e, int index_id, int cluster_id, const float* centroid);
@@ -228,6 +246,15 @@ int m3g_train_ivf(m3g_engine* e, int index_id, int dim, int metric, int normaliz
  * list order.  *out_new_cluster = -1 when the list has fewer than 2 live rows. */
 int m3g_split_cluster(m3g_engine* e, int index_id, int cluster_id, int niter, uint64_t seed,
                       int32_t* out_new_cluster);
+
+/* One split pass now: every list whose live rows exceed mean_factor times the
+ * mean live rows over all lists (taken once, before the first split) is split
+ * by m3g_split_cluster in ascending id order, list l with seed + l; new lists
+ * take the next ids.  *out_nsplit = lists split.  Built from the primitives
+ * the reference's TODO names (set_centroid, add_cluster, rebuild_cluster,
+ * m3_index.cpp:133-163, 304-311). */
+int m3g_split_oversized(m3g_engine* e, int index_id, double mean_factor, int niter, uint64_t seed,
+                        int* out_nsplit);
 
 /* Final merge of a list-sharded search (one shard of the lists per GPU): each
  * shard's answer [nq, k] (as m3g_search_device writes it) gathered into

@@ -27,7 +27,7 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-r
 
 CU_SOURCES = ["k_coarse.cu", "k_scan.cu", "k_scan_tc.cu", "k_kmeans.cu", "k_gemm_tc.cu",
               "engine.cu", "noalloc.cu"]
-CPP_SOURCES = ["api.cpp"]
+CPP_SOURCES = ["api.cpp", "faiss_io.cpp"]
 HEADERS = ["common.cuh", "score.cuh", "topk.cuh", "tc.cuh", "kernels.h", "kernels_kmeans.h",
            "engine.h"]
 

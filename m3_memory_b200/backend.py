@@ -153,6 +153,26 @@ class M3Backend:
         self._indices.add(index_id)
         self._stored[index_id] = set()
 
+    # ---------- rebuild from faiss (m3.py:186-198) ----------
+
+    def rebuild_index_from_faiss(self, index_id: int, *, path: str,
+                                 normalized: Optional[bool] = None) -> None:
+        """The index replaced by a Faiss IndexIVFFlat dump (read by the engine,
+        ``m3_memory_b200.faiss_loader.rebuild_from_faiss``); its ids become this
+        backend's stored ids, so later UPDATE / DELETE_IDS requests reach them."""
+        from m3_memory_b200.faiss_loader import rebuild_from_faiss
+
+        if self._autostart:
+            self._ensure_started()
+        rebuild_from_faiss(self._eng, index_id=index_id, path=path,
+                           normalized=bool(normalized) if normalized is not None else True)
+        self._indices.add(index_id)
+        stored = self._stored.setdefault(index_id, set())
+        stored.clear()
+        for c in range(int(self._eng.nlist_of(index_id))):
+            ids, _ = self._eng.get_cluster(index_id, c, False)
+            stored.update(np.asarray(ids).tolist())
+
     # ---------- requests (m3.py:120-180) ----------
 
     def _ids(self, keys, err) -> np.ndarray:

@@ -65,6 +65,9 @@ SIGNATURES = {
     "m3g_storage_of": (_i32, [_vp, _i32, _pi]),
     "m3g_load_cluster": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
     "m3g_load_cluster_device": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
+    "m3g_set_split_policy": (_i32, [_vp, _f64, _i32]),
+    "m3g_rebuild_from_faiss": (_i32, [_vp, _i32, ct.c_char_p, _i32, _i32]),
+    "m3g_split_oversized": (_i32, [_vp, _i32, _f64, _i32, _u64, _pi]),
     "m3g_nearest_clusters_device": (_i32, [_vp, _i32, _vp, _i64, _vp]),
     "m3g_enqueue_insert": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _pi]),
     "m3g_enqueue_update": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32, _pi]),
@@ -311,6 +314,10 @@ class Engine:
                                     ct.byref(n)))
         return ids, vecs
 
+    def rebuild_from_faiss(self, index_id, path, normalized=True, storage=F32):
+        check(lib().m3g_rebuild_from_faiss(self.h, index_id, str(path).encode(), int(normalized),
+                                           storage))
+
     def save_index(self, index_id, path):
         check(lib().m3g_save_index(self.h, index_id, str(path).encode()))
 
@@ -359,6 +366,15 @@ class Engine:
         check(lib().m3g_train_ivf(self.h, index_id, dim, metric, int(normalized), _p(ids), _p(X),
                                   X.shape[0], nlist, niter, seed, _p(C)))
         return C
+
+    def set_split_policy(self, mean_factor=0.0, niter=5):
+        check(lib().m3g_set_split_policy(self.h, mean_factor, niter))
+
+    def split_oversized(self, index_id, mean_factor=2.0, niter=5, seed=0):
+        out = ct.c_int()
+        check(lib().m3g_split_oversized(self.h, index_id, mean_factor, niter, seed,
+                                        ct.byref(out)))
+        return out.value
 
     def split_cluster(self, index_id, cid, niter=5, seed=0):
         out = ct.c_int32()

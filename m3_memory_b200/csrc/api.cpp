@@ -108,11 +108,35 @@ int m3g_set_maintenance_policy(m3g_engine* e, double period_sec, size_t split_th
     });
 }
 
+int m3g_set_split_policy(m3g_engine* e, double mean_factor, int niter) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (mean_factor < 0 || niter < 0) m3g::fail(M3G_EINVAL, "set_split_policy: negative value");
+        e->eng.set_split_policy(mean_factor, niter);
+    });
+}
+
+int m3g_split_oversized(m3g_engine* e, int index_id, double mean_factor, int niter, uint64_t seed,
+                        int* out_nsplit) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (niter < 0) m3g::fail(M3G_EINVAL, "split_oversized: niter < 0");
+        const int n = e->eng.split_oversized(index_id, mean_factor, niter, seed);
+        if (out_nsplit) *out_nsplit = n;
+    });
+}
+
 int m3g_create_ivf(m3g_engine* e, int index_id, int dim, int metric, int normalized,
                    const float* centroids, int64_t nlist) {
     M3G_ENGINE_OR_FAIL(e);
     return guarded(
         [&] { e->eng.create_ivf(index_id, dim, metric, normalized != 0, centroids, nlist); });
+}
+
+int m3g_rebuild_from_faiss(m3g_engine* e, int index_id, const char* path, int normalized,
+                           int storage) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.rebuild_from_faiss(index_id, path, normalized != 0, storage); });
 }
 
 int m3g_create_ivf_ex(m3g_engine* e, int index_id, int dim, int metric, int normalized,

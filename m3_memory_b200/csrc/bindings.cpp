@@ -12,8 +12,9 @@
 // Additions beyond the reference surface (all new, none shadows a reference
 // method): search_into_device (tensor fast path by raw device pointers),
 // nearest_clusters, select_probes, search_on, kmeans, train_ivf, split_cluster,
-// cluster_size, centroids, save_index, load_index, add_cluster, set_centroid, compact_cluster,
-// maintenance_pass, set_device, set_profiling, last_profile.
+// split_oversized, set_split_policy, rebuild_from_faiss, get_cluster, cluster_size, centroids, save_index, load_index,
+// add_cluster, set_centroid, compact_cluster, maintenance_pass, set_device, set_profiling,
+// last_profile; and create_ivf's optional `storage` ("fp32" default, or "bf16").
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
@@ -479,6 +480,26 @@ PYBIND11_MODULE(_m3_async, m) {
             },
             py::arg("index_id"), py::arg("cluster_id"), py::arg("niter") = 5, py::arg("seed") = 0)
         .def(
+            "split_oversized",
+            [](AsyncEngine& e, int index_id, double mean_factor, int niter, uint64_t seed) {
+                int n = 0;
+                int rc;
+                {
+                    py::gil_scoped_release g;
+                    rc = m3g_split_oversized(e.h(), index_id, mean_factor, niter, seed, &n);
+                }
+                raise_status(rc);
+                return n;
+            },
+            py::arg("index_id"), py::arg("mean_factor") = 2.0, py::arg("niter") = 5,
+            py::arg("seed") = 0)
+        .def(
+            "set_split_policy",
+            [](AsyncEngine& e, double mean_factor, int niter) {
+                raise_status(m3g_set_split_policy(e.h(), mean_factor, niter));
+            },
+            py::arg("mean_factor") = 0.0, py::arg("niter") = 5)
+        .def(
             "cluster_size",
             [](AsyncEngine& e, int index_id, int cluster_id) {
                 int64_t sz = 0, live = 0;
@@ -486,6 +507,42 @@ PYBIND11_MODULE(_m3_async, m) {
                 return py::make_tuple(sz, live);
             },
             py::arg("index_id"), py::arg("cluster_id"))
+        .def(
+            "rebuild_from_faiss",
+            [](AsyncEngine& e, int index_id, const std::string& path, bool normalized,
+               const std::string& storage) {
+                int st = M3G_STORE_FP32;
+                if (storage == "bf16") st = M3G_STORE_BF16;
+                else if (storage != "fp32")
+                    throw py::value_error("rebuild_from_faiss: storage must be 'fp32' or 'bf16'");
+                int rc;
+                {
+                    py::gil_scoped_release g;
+                    rc = m3g_rebuild_from_faiss(e.h(), index_id, path.c_str(), normalized ? 1 : 0,
+                                                st);
+                }
+                raise_status(rc);
+            },
+            py::arg("index_id"), py::arg("path"), py::arg("normalized") = true,
+            py::arg("storage") = "fp32")
+        .def(
+            "get_cluster",
+            [](AsyncEngine& e, int index_id, int cluster_id, bool with_vectors) {
+                int64_t n = 0;
+                raise_status(m3g_get_cluster(e.h(), index_id, cluster_id, nullptr, nullptr, 0, &n));
+                const int d = e.dim_of(index_id);
+                py::array_t<int64_t> ids(n);
+                py::array_t<float> vecs(std::vector<py::ssize_t>{with_vectors ? n : 0, d});
+                int rc;
+                {
+                    py::gil_scoped_release g;
+                    rc = m3g_get_cluster(e.h(), index_id, cluster_id, ids.mutable_data(),
+                                         with_vectors ? vecs.mutable_data() : nullptr, n, &n);
+                }
+                raise_status(rc);
+                return py::make_tuple(ids, vecs);
+            },
+            py::arg("index_id"), py::arg("cluster_id"), py::arg("with_vectors") = true)
         .def(
             "save_index",
             [](AsyncEngine& e, int index_id, const std::string& path) {

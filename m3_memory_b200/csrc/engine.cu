@@ -980,11 +980,42 @@ void Engine::maintenance_pass(int index_id) {
                 list_compact(*ix, l);
                 changed = true;
             }
-            if (mpol_.auto_split && (size_t)L.live > mpol_.split_threshold) to_split.push_back(l);
+            if (mpol_.auto_split && mpol_.split_mean_factor <= 0 &&
+                (size_t)L.live > mpol_.split_threshold)
+                to_split.push_back(l);
         }
         if (changed) refresh_list_meta(*ix);
     }
-    for (int l : to_split) split_cluster(index_id, l, 5, 0x5eed0000ull + (uint64_t)l);
+    if (mpol_.auto_split && mpol_.split_mean_factor > 0) {
+        split_oversized(index_id, mpol_.split_mean_factor, mpol_.split_niter, 0x5eed0000ull);
+        return;
+    }
+    for (int l : to_split) split_cluster(index_id, l, mpol_.split_niter, 0x5eed0000ull + (uint64_t)l);
+}
+
+std::vector<int> Engine::oversized_lists(int index_id, double mean_factor) {
+    auto ix = get(index_id, "split_oversized");
+    std::shared_lock lk(ix->mu);
+    std::vector<int> out;
+    const int L = ix->nlist();
+    if (L == 0) return out;
+    int64_t total = 0;
+    for (const auto& l : ix->lists) total += l.live;
+    const double limit = mean_factor * ((double)total / (double)L);
+    for (int l = 0; l < L; ++l)
+        if ((double)ix->lists[(size_t)l].live > limit) out.push_back(l);
+    return out;
+}
+
+int Engine::split_oversized(int index_id, double mean_factor, int niter, uint64_t seed) {
+    if (!(mean_factor > 0)) fail(M3G_EINVAL, "split_oversized: mean_factor must be > 0");
+    // the lists over the limit when the pass starts (live rows > factor x the mean
+    // over all lists), split in ascending id order; new lists join at the end
+    const std::vector<int> todo = oversized_lists(index_id, mean_factor);
+    int n = 0;
+    for (int l : todo)
+        if (split_cluster(index_id, l, niter, seed + (uint64_t)l) >= 0) ++n;
+    return n;
 }
 
 void Engine::compact_cluster(int index_id, int cid) {
@@ -1532,7 +1563,7 @@ void Engine::search(int index_id, const float* Q, int64_t nq, int k, int nprobe,
     if (profile) {
         prof_pending_ = true;
         prof_.kernel_launches = last_launches_;
-        prof_row_bytes_ = (int64_t)ix->dim * 4;
+        prof_row_bytes_ = (int64_t)ix->dim * ix->esize;  // algorithmic bytes of a stored row
         prof_dim_ = ix->dim;
         prof_.nq = (int32_t)nq;
         prof_.nprobe = P;

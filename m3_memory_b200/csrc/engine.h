@@ -147,6 +147,10 @@ struct MaintenancePolicy {
     size_t split_threshold = 200000;
     double compact_ratio = 0.7;
     bool auto_split = false;
+    // > 0: auto_split splits lists with more live rows than this factor times the
+    // mean over all lists (split_oversized) instead of the absolute split_threshold
+    double split_mean_factor = 0.0;
+    int split_niter = 5;  // 2-means rounds per split
 };
 
 // cluster_id of an update or delete addressed to every list holding the id
@@ -192,7 +196,14 @@ class Engine {
     void stop();
     void set_queue_policy(const QueuePolicy& p) { qpol_ = p; }
     void set_search_policy(const SearchPolicy& p) { spol_ = p; }
-    void set_maintenance_policy(const MaintenancePolicy& p) { mpol_ = p; }
+    // (keeps the split rule of set_split_policy)
+    void set_maintenance_policy(const MaintenancePolicy& p) {
+        const double f = mpol_.split_mean_factor;
+        const int ni = mpol_.split_niter;
+        mpol_ = p;
+        mpol_.split_mean_factor = f;
+        mpol_.split_niter = ni;
+    }
 
     void create_ivf(int index_id, int dim, int metric, bool normalized, const float* C, int64_t nlist,
                     int storage = M3G_STORE_FP32);
@@ -235,6 +246,8 @@ class Engine {
     void get_cluster(int index_id, int cid, int64_t* ids, float* vecs, int64_t cap,
                      int64_t* n_live);
     void save_index(int index_id, const char* path);
+    // Faiss IndexIVFFlat file -> index_id (faiss_io.cpp)
+    void rebuild_from_faiss(int index_id, const char* path, bool normalized, int storage);
     void load_index(int index_id, const char* path);
     int add_cluster(int index_id, const float* c);
     void set_centroid(int index_id, int cid, const float* c);
@@ -246,6 +259,15 @@ class Engine {
     void train_ivf(int index_id, int dim, int metric, bool normalized, const int64_t* ids,
                    const float* X, int64_t n, int nlist, int niter, uint64_t seed, float* C_out);
     int split_cluster(int index_id, int cid, int niter, uint64_t seed);
+    // Splits every list whose live rows exceed mean_factor x the mean live rows over
+    // all lists (evaluated once, before the first split), in ascending id order,
+    // list l with seed + l.  Returns the number of lists split.
+    int split_oversized(int index_id, double mean_factor, int niter, uint64_t seed);
+    std::vector<int> oversized_lists(int index_id, double mean_factor);
+    void set_split_policy(double mean_factor, int niter) {
+        mpol_.split_mean_factor = mean_factor;
+        mpol_.split_niter = niter;
+    }
 
     void set_profiling(bool on) { profiling_ = on; }
     m3g_profile last_profile();

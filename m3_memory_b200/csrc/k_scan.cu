@@ -776,40 +776,9 @@ __device__ uint32_t radix_select32(F key_of, int64_t n, unsigned rank, unsigned*
 // Candidate i = slot * k + j of query q lives at q * stride_q + slot * stride_slot
 // + j.  part_row holds arena rows mapped through row_ids, or, when row_ids is
 // null, the ids themselves.
-// The reference's squared L2 (base.cpp:12-20): one rounding per subtract,
-// multiply and add, summed in index order.  Padding dims are zero in both rows.
-template <bool XB>
-__device__ float exact_l2_row(const float* __restrict__ q, const void* __restrict__ rows,
-                              int64_t row, int64_t ld, int dim) {
-    float s = 0.f;
-    if (XB) {
-        const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(rows) + row * ld;
-        for (int i = 0; i < dim; ++i) {
-            const float df = __fsub_rn(q[i], __bfloat162float(x[i]));
-            s = __fadd_rn(s, __fmul_rn(df, df));
-        }
-    } else {
-        const float* x = reinterpret_cast<const float*>(rows) + row * ld;
-        int i = 0;
-        for (; i + 4 <= dim; i += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(q + i);
-            const float4 b = __ldg(reinterpret_cast<const float4*>(x + i));
-            float df = __fsub_rn(a.x, b.x);
-            s = __fadd_rn(s, __fmul_rn(df, df));
-            df = __fsub_rn(a.y, b.y);
-            s = __fadd_rn(s, __fmul_rn(df, df));
-            df = __fsub_rn(a.z, b.z);
-            s = __fadd_rn(s, __fmul_rn(df, df));
-            df = __fsub_rn(a.w, b.w);
-            s = __fadd_rn(s, __fmul_rn(df, df));
-        }
-        for (; i < dim; ++i) {
-            const float df = __fsub_rn(q[i], x[i]);
-            s = __fadd_rn(s, __fmul_rn(df, df));
-        }
-    }
-    return s;
-}
+// Exact rescoring (MergeRescore) takes at most this many winners per query.
+constexpr int RS_MAX = 128;
+static_assert(RS_MAX * 33 * 4 <= MCAP * 8, "the staging tile fits in the candidate array");
 
 __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
     const float* __restrict__ part_score, const int64_t* __restrict__ part_row,
@@ -817,8 +786,8 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
     int64_t* __restrict__ out_ids, float* __restrict__ out_scores,
     int32_t* __restrict__ out_counts, MergeRescore rs, int rescore) {
     __shared__ unsigned long long cand[MCAP];
-    __shared__ unsigned long long won[MRG_BLOCK];
-    __shared__ float exact[MRG_BLOCK];
+    __shared__ unsigned long long won[RS_MAX];
+    __shared__ float exact[RS_MAX];
     __shared__ unsigned hist[256];
     __shared__ unsigned shv[4];
     __shared__ unsigned s_tau, s_cnt, s_valid;
@@ -907,18 +876,65 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
         bitonic_u64(cand, n2);
     }
     if (rescore) {
-        // the winners' exact scores (k <= MRG_BLOCK: one per thread), then a sort by
-        // (exact score, rank by the estimate)
+        // The winners' exact scores (kk <= RS_MAX; thread j sums winner j's row in
+        // index order), then a sort by (exact score, rank by the estimate).  Rows
+        // are staged 32 dims at a time through shared memory (the candidate array,
+        // free once the winners are copied): coalesced 16-byte loads, rows padded
+        // to 33 words so the per-thread reads hit distinct banks.
         const int j = threadIdx.x;
-        float e = INF;
-        if (j < kk) {
-            won[j] = cand[j];
-            const int64_t row = pr[at((int64_t)(cand[j] & 0xffffffffu))];
-            const float* qr = rs.Q + (int64_t)q * rs.ldq;
-            e = rs.bf16_rows ? exact_l2_row<true>(qr, rs.rows, row, rs.row_ld, rs.dim)
-                             : exact_l2_row<false>(qr, rs.rows, row, rs.row_ld, rs.dim);
-            exact[j] = e;
+        if (j < kk) won[j] = cand[j];
+        __syncthreads();
+        float* tile = reinterpret_cast<float*>(cand);  // [RS_MAX][33]
+        __shared__ float qt[32];
+        __shared__ int64_t wrow[RS_MAX];
+        if (j < kk) wrow[j] = pr[at((int64_t)(won[j] & 0xffffffffu))];
+        const float* qr = rs.Q + (int64_t)q * rs.ldq;
+        float e = 0.f;
+        for (int d0 = 0; d0 < rs.dim; d0 += 32) {
+            __syncthreads();
+            if (j < 32) qt[j] = d0 + j < rs.dim ? qr[d0 + j] : 0.f;
+            if (rs.bf16_rows) {
+                // 4 x 16 B (8 bf16) per row and chunk
+                for (int t = j; t < kk * 4; t += MRG_BLOCK) {
+                    const int r = t >> 2, c = t & 3;
+                    const __nv_bfloat16* src =
+                        reinterpret_cast<const __nv_bfloat16*>(rs.rows) + wrow[r] * rs.row_ld + d0 + 8 * c;
+                    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                    if (d0 + 8 * c + 8 <= rs.row_ld) {
+                        const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+                        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            v[2 * h] = __uint_as_float(w[h] << 16);
+                            v[2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+                        }
+                    }
+#pragma unroll
+                    for (int h = 0; h < 8; ++h) tile[r * 33 + 8 * c + h] = v[h];
+                }
+            } else {
+                // 8 x 16 B (4 fp32) per row and chunk
+                for (int t = j; t < kk * 8; t += MRG_BLOCK) {
+                    const int r = t >> 3, c = t & 7;
+                    const float* src = reinterpret_cast<const float*>(rs.rows) + wrow[r] * rs.row_ld + d0 + 4 * c;
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (d0 + 4 * c + 4 <= rs.row_ld) v = __ldg(reinterpret_cast<const float4*>(src));
+                    tile[r * 33 + 4 * c] = v.x;
+                    tile[r * 33 + 4 * c + 1] = v.y;
+                    tile[r * 33 + 4 * c + 2] = v.z;
+                    tile[r * 33 + 4 * c + 3] = v.w;
+                }
+            }
+            __syncthreads();
+            if (j < kk) {
+                const int n = min(32, rs.dim - d0);  // padding dims are never summed
+                for (int i = 0; i < n; ++i) {
+                    const float df = __fsub_rn(qt[i], tile[j * 33 + i]);
+                    e = __fadd_rn(e, __fmul_rn(df, df));
+                }
+            }
         }
+        if (j < kk) exact[j] = e;
         __syncthreads();
         int n2 = 1;
         while (n2 < kk) n2 <<= 1;
@@ -953,7 +969,7 @@ cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
                               float* out_scores, int32_t* out_counts, cudaStream_t st,
                               const MergeRescore* rs) {
     if (nq <= 0) return cudaSuccess;
-    if (rs && (k > MRG_BLOCK || !row_ids)) return cudaErrorInvalidValue;
+    if (rs && (k > RS_MAX || !row_ids)) return cudaErrorInvalidValue;
     const MergeRescore none{};
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(part_score, part_row, row_ids, P, k,
                                                 (int64_t)P * k, k, out_ids, out_scores,

@@ -551,3 +551,35 @@ def split_2means(X, niter, seed, metric, normalized):
     if rc:
         raise ValueError("split_2means: needs at least 2 rows")
     return C, a
+
+
+def split_oversized(ref: "RefIndex", lists_rows, mean_factor, niter, seed, metric, normalized):
+    """The split pass restated on the reference core: every list with more live rows
+    than mean_factor x the mean over all lists (taken before the first split) is
+    split, in ascending id order, by the oracle's 2-means (list l seeded seed + l)
+    and applied through the reference's own primitives -- set_centroid(l, c0),
+    add_cluster(c1), rebuild_cluster of both lists (AgentMemory/M3/src/
+    m3_index.cpp:133-163, the steps its TODO at :304-311 names).
+
+    lists_rows: per list a pair (ids int64 [n], vecs float32 [n, d]) of its live
+    rows in list order, updated in place (new lists appended).  Returns the new
+    lists' ids."""
+    L = len(lists_rows)
+    total = sum(len(i) for i, _ in lists_rows)
+    limit = mean_factor * (total / L) if L else 0.0
+    todo = [l for l in range(L) if len(lists_rows[l][0]) > limit]
+    new = []
+    for l in todo:
+        ids, vecs = lists_rows[l]
+        if len(ids) < 2:
+            continue
+        C2, side = split_2means(vecs, niter, seed + l, metric, normalized)
+        ref.set_centroid(l, C2[0])
+        nid = ref.add_cluster(C2[1])
+        a, b = side == 0, side == 1
+        lists_rows[l] = (ids[a], vecs[a])
+        lists_rows.append((ids[b], vecs[b]))
+        ref.rebuild_cluster(l, ids[a], vecs[a])
+        ref.rebuild_cluster(nid, ids[b], vecs[b])
+        new.append(nid)
+    return new
