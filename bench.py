@@ -712,22 +712,19 @@ def run_config3(args, rank, world, local_rank):
         f"{time.perf_counter() - t0:.1f}s")
     sizes = torch.bincount(assign.long(), minlength=nlist).cpu().numpy()
     owner = shard_lists(sizes, world)
-    order = torch.argsort(assign, stable=True)
-    bounds = np.concatenate([[0], np.cumsum(sizes)])
     t0 = time.perf_counter()
-    local_rows = 0
-    for c in range(nlist):
-        b, e = int(bounds[c]), int(bounds[c + 1])
-        if e > b and owner[c] == rank:
-            rows = order[b:e]
-            xs = X[rows].contiguous()
-            eng.load_cluster_device(1, c, rows.data_ptr(), xs.data_ptr(), e - b, cabi.F32)
-            local_rows += e - b
+    # this rank's lists, loaded in one pass (rows of other ranks' lists: -1)
+    own = torch.from_numpy(owner == rank).to(dev)
+    mine = torch.where(own[assign.long()], assign, torch.full_like(assign, -1))
+    row_ids = torch.arange(n, dtype=torch.int64, device=dev)
+    eng.load_lists_device(1, mine.data_ptr(), row_ids.data_ptr(), X.data_ptr(), n)
+    local_rows = int((mine >= 0).sum().item())
+    del mine, row_ids
     torch.cuda.synchronize()
     log(f"[rank {rank}] {local_rows} rows loaded ({args.storage} lists) in "
         f"{time.perf_counter() - t0:.1f}s")
     exact = exact_topk_l2_device(X, Qd[:1024], 10).cpu().numpy() if rank == 0 else None
-    del X, order, assign
+    del X, assign
     torch.cuda.empty_cache()
 
     sharded = ShardedSearch(eng, 1, K3, max(C3_BATCHES), world, dev, rank=rank,
@@ -875,6 +872,183 @@ def run_config3(args, rank, world, local_rank):
     })
 
 
+# ---------------------------------------------------------------- Zipf-skewed shards
+# Weak scaling by shard: every GPU holds one shard of 12.5M unit-norm rows x 1024
+# (its own Zipf(1.1)-skewed mixture of 8192 components, k-means lists trained on
+# the shard), the index is the union of the N shards (N x 8192 lists, every
+# rank holding all centroids), cosine, nprobe 64, k 10, batches of 4096 x N
+# queries drawn from the union.  At N = 8 this is the 100M x 1024, 65,536-list
+# configuration.
+C4_N = 12_500_000
+C4_NLIST = 8192
+C4_ZIPF = 1.1
+C4_NPROBE = 64
+C4_BATCH_PER_GPU = 4096
+
+
+def device_zipf_means(ncomp, d, seed, dev):
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    means = torch.randn(ncomp, d, generator=g, device=dev)
+    return means / means.norm(dim=1, keepdim=True)
+
+
+def device_zipf_rows(means, n, zipf, sigma, seed, dev, chunk=1 << 20):
+    """n unit-norm rows of a mixture whose component c has weight ~ (c + 1)^-zipf."""
+    import torch
+
+    ncomp, d = means.shape
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    w = torch.arange(1, ncomp + 1, device=dev, dtype=torch.float64) ** (-zipf)
+    comp = torch.multinomial(w, n, replacement=True, generator=g)
+    out = torch.empty(n, d, device=dev)
+    for b in range(0, n, chunk):
+        e = min(n, b + chunk)
+        x = means[comp[b:e]] + (sigma / d ** 0.5) * torch.randn(e - b, d, generator=g, device=dev)
+        out[b:e] = x / x.norm(dim=1, keepdim=True)
+    return out
+
+
+def run_config4(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from m3_memory_b200 import cabi
+    from m3_memory_b200.sharding import ShardedSearch
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    n, d, nl = args.c4_n or C4_N, DIM, C4_NLIST
+    B = C4_BATCH_PER_GPU * world
+    t0 = time.perf_counter()
+    means = [device_zipf_means(nl, d, SEED + 200 + r, dev) for r in range(world)]
+    X = device_zipf_rows(means[rank], n, C4_ZIPF, SIGMA, SEED + 300 + rank, dev)
+    eng = cabi.Engine()
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 400 + rank)
+    sample = torch.randperm(n, generator=g, device=dev)[:min(n, nl * 64)].sort().values
+    C, _ = eng.kmeans(X[sample].cpu().numpy(), nl, KMEANS_ITERS, SEED + rank, 2, True)
+    # the shard's own lists: every row to its nearest centroid of this shard
+    eng.create_ivf(2, d, 2, True, C)
+    assign = torch.empty(n, dtype=torch.int32, device=dev)
+    for b in range(0, n, 1 << 21):
+        e = min(n, b + (1 << 21))
+        eng.nearest_clusters_device(2, X[b:e].data_ptr(), e - b, assign[b:e].data_ptr())
+    # the union index: every shard's centroids (rank-major), this rank's lists
+    Cd = torch.from_numpy(C).to(dev)
+    if world > 1:
+        Call = torch.empty((world * nl, d), device=dev)
+        dist.all_gather_into_tensor(Call, Cd)
+    else:
+        Call = Cd
+    eng.create_ivf(1, d, 2, True, Call.cpu().numpy())
+    glob = assign + rank * nl
+    row_ids = torch.arange(n, dtype=torch.int64, device=dev) + rank * n
+    eng.load_lists_device(1, glob.data_ptr(), row_ids.data_ptr(), X.data_ptr(), n)
+    sizes = torch.bincount(assign.long(), minlength=nl).cpu().numpy()
+    log(f"[rank {rank}] shard of {n} rows in {nl} lists (largest {sizes.max()}, median "
+        f"{int(np.median(sizes))}) ready in {time.perf_counter() - t0:.1f}s")
+    # queries from the union (the same on every rank): shard, then its mixture
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(SEED + 500)
+    nq_pool = 2 * B
+    qshard = torch.randint(0, world, (nq_pool,), generator=gq, device=dev)
+    Q = torch.empty((nq_pool, d), device=dev)
+    for r in range(world):
+        sel = torch.nonzero(qshard == r).flatten()
+        if len(sel):
+            Q[sel] = device_zipf_rows(means[r], len(sel), C4_ZIPF, SIGMA, SEED + 600 + r, dev)
+    # exact global top-10 of 1024 queries: each rank's shard, merged over ranks
+    qe = Q[:1024]
+    best_s = best_i = None
+    for b in range(0, n, 1 << 20):
+        v, i = torch.topk(qe @ X[b:b + (1 << 20)].T, 10, dim=1)
+        i = i + b
+        if best_s is None:
+            best_s, best_i = v, i
+        else:
+            cs, ci = torch.cat([best_s, v], 1), torch.cat([best_i, i], 1)
+            best_s, o = torch.topk(cs, 10, dim=1)
+            best_i = torch.gather(ci, 1, o)
+    best_i = best_i + rank * n
+    if world > 1:
+        gs = torch.empty((world, 1024, 10), device=dev)
+        gi = torch.empty((world, 1024, 10), dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(gs, best_s.contiguous())
+        dist.all_gather_into_tensor(gi, best_i.contiguous())
+        cs, ci = gs.permute(1, 0, 2).reshape(1024, -1), gi.permute(1, 0, 2).reshape(1024, -1)
+        _, o = torch.topk(cs, 10, dim=1)
+        exact = torch.gather(ci, 1, o).cpu().numpy()
+    else:
+        exact = best_i.cpu().numpy()
+    del X, glob, row_ids, assign
+    torch.cuda.empty_cache()
+    sharded = ShardedSearch(eng, 1, K, B, world, dev, rank=rank, max_nprobe=C4_NPROBE,
+                            split_coarse=world > 1)
+    ids, _, _ = sharded.search(Q[:B], C4_NPROBE)
+    torch.cuda.synchronize()
+    recall = recall_at_k(ids[:1024].cpu().numpy(), exact, K)
+    eng.sync_errors()
+
+    def step(i):
+        o = (i % 2) * B
+        sharded.search(Q[o:o + B], C4_NPROBE)
+
+    for w in range(args.warmup):
+        step(w)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_selector(local_rank)) as clk:
+        ev0.record()
+        for i in range(args.steps):
+            step(i)
+        ev1.record()
+        torch.cuda.synchronize()
+    eng.sync_errors()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    sharded.marks = []
+    step(0)
+    torch.cuda.synchronize()
+    m = sharded.marks
+    stage = {name: ea_eb for name, ea_eb in
+             ((nm, ea.elapsed_time(eb)) for (_, ea), (nm, eb) in zip(m, m[1:]))}
+    sharded.marks = None
+    if rank != 0:
+        return
+    qps = B * args.steps / (ms / 1e3)
+    emit({
+        "metric": "search QPS at recall@10>=0.95 (IVF, dim 1024, Zipf-skewed lists, "
+                  "one 12.5M-row shard per GPU)",
+        "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (per shard a seeded Zipf(1.1) mixture of 8192 components, on the GPU)",
+        "config": {"workload": ("PROFILING CASE (not the 12.5M-row shard): " if args.c4_n else "")
+                               + f"ivf-search: {world} x {n} x {d} fp32 unit-norm, cosine, "
+                               f"nlist {world * nl}, nprobe {C4_NPROBE}, k {K}, batch {B}",
+                   "rows_per_gpu": n, "nlist": world * nl, "nprobe": C4_NPROBE, "k": K,
+                   "batch": B, "metric": "cosine (normalized)",
+                   "scaling_protocol": "weak: one shard (rows, lists, 4096 queries) per GPU; "
+                                       "N = 8 is the 100M-row, 65,536-list index",
+                   "l2_flush": "not needed: each batch streams the shards (> 126 MB L2)"},
+        "recall_at_10": recall,
+        "stage_ms_rank0": {k: round(v, 4) for k, v in stage.items()},
+        "parallelism": f"{world} shard(s), split coarse selection, one all-gather of probes "
+                       "and one of top-k records per batch" if world > 1 else "1 GPU",
+        "clocks": clk.summary(), "gpu_launches": None,
+        "e2e": None, "roofline": None, "cpu_baseline": None,
+    })
+
+
 # ---------------------------------------------------------------- insert + split stream
 # From the headline index: 1M new rows from shifted mixture means (offset
 # N(0, 0.5^2) in norm), in batches of 8,192 routed by enqueue_insert_auto; after
@@ -1017,11 +1191,13 @@ def main():
                     help="profiling only: fewer vectors (the headline line uses 1M)")
     ap.add_argument("--nlist", type=int, default=None, help="profiling only: fewer lists")
     ap.add_argument("--nprobe", type=int, default=None, help="profiling only: other nprobe")
-    ap.add_argument("--config", type=int, choices=[2, 3, 5], default=2,
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
                     help="2: the headline (1M x 1024 fp32, IP); 3: 10M x 768 bf16-stored lists, "
                          "L2, nlist 16384, k 100, nprobe x batch sweep; 5: online insert + split "
-                         "stream from the headline index")
+                         "stream from the headline index; 4: Zipf-skewed 12.5M-row shard per GPU, "
+                         "cosine, nlist 8192 per shard, nprobe 64 (weak scaling)")
     ap.add_argument("--c5-n", type=int, default=None, help="config 5, profiling only: inserts")
+    ap.add_argument("--c4-n", type=int, default=None, help="config 4, profiling only: rows per GPU")
     ap.add_argument("--storage", choices=["bf16", "fp32"], default="bf16",
                     help="config 3: list storage")
     ap.add_argument("--c3-n", type=int, default=None, help="config 3, profiling only: rows")
@@ -1056,6 +1232,8 @@ def main():
     try:
         if args.config == 3:
             run_config3(args, rank, world, local_rank)
+        elif args.config == 4:
+            run_config4(args, rank, world, local_rank)
         elif args.config == 5:
             run_config5(args, rank, world, local_rank)
         else:

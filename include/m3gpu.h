@@ -122,6 +122,14 @@ int m3g_load_cluster(m3g_engine* e, int index_id, int cluster_id, const int64_t*
 int m3g_load_cluster_device(m3g_engine* e, int index_id, int cluster_id, const int64_t* d_ids,
                             const void* d_vecs, int64_t n, int dtype);
 
+/* Every list of index_id replaced at once (Cluster::rebuild_from per list,
+ * cluster.cpp:152-178) by the device rows assigned to it: d_assign [n] int32
+ * (the list of each row, -1 for none), d_ids [n] int64, d_vecs [n, dim] fp32,
+ * all device pointers; a list's rows keep their order.  The same index as
+ * m3g_load_cluster list by list, built in one pass over the rows.  Synchronous. */
+int m3g_load_lists_device(m3g_engine* e, int index_id, const int32_t* d_assign,
+                          const int64_t* d_ids, const float* d_vecs, int64_t n);
+
 /* AsyncEngine::enqueue_insert / enqueue_update / enqueue_delete
  * (m3_async.cpp:123-187; applied by writer threads as Cluster::add_batch /
  * update_batch / erase_batch, cluster.cpp:55-150).  *accepted = 0 when the
@@ -265,6 +273,15 @@ int m3g_split_oversized(m3g_engine* e, int index_id, double mean_factor, int nit
 int m3g_merge_shards_device(m3g_engine* e, const float* d_scores, const int64_t* d_ids,
                             int nshard, int64_t nq, int k, int64_t* d_out_ids,
                             float* d_out_scores, int32_t* d_out_counts, void* stream);
+
+/* m3g_merge_shards_device over one gathered buffer, so a single all-gather
+ * moves scores and ids: shard s's record starts at d_packed + s * shard_bytes
+ * and holds its [nq, k] fp32 scores, then at byte ids_offset its [nq, k] int64
+ * ids (shard_bytes, ids_offset and d_packed multiples of 8 bytes). */
+int m3g_merge_shards_packed_device(m3g_engine* e, const void* d_packed, int nshard, int64_t nq,
+                                   int k, int64_t shard_bytes, int64_t ids_offset,
+                                   int64_t* d_out_ids, float* d_out_scores, int32_t* d_out_counts,
+                                   void* stream);
 
 /* The pieces of a list-sharded search whose coarse step is sharded as well
  * (each GPU scores only the centroids of the lists it owns).  No single

@@ -66,6 +66,9 @@ SIGNATURES = {
     "m3g_load_cluster": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
     "m3g_load_cluster_device": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
     "m3g_set_split_policy": (_i32, [_vp, _f64, _i32]),
+    "m3g_load_lists_device": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64]),
+    "m3g_merge_shards_packed_device": (_i32, [_vp, _vp, _i32, _i64, _i32, _i64, _i64, _vp, _vp,
+                                              _vp, _vp]),
     "m3g_rebuild_from_faiss": (_i32, [_vp, _i32, ct.c_char_p, _i32, _i32]),
     "m3g_split_oversized": (_i32, [_vp, _i32, _f64, _i32, _u64, _pi]),
     "m3g_nearest_clusters_device": (_i32, [_vp, _i32, _vp, _i64, _vp]),
@@ -225,6 +228,11 @@ class Engine:
         """Device pointers: ids int64 [n], vectors [n, dim] fp32 or bf16 bits."""
         check(lib().m3g_load_cluster_device(self.h, index_id, cid, ct.c_void_p(ids_ptr),
                                             ct.c_void_p(vecs_ptr), n, dtype))
+
+    def load_lists_device(self, index_id, assign_ptr, ids_ptr, vecs_ptr, n):
+        """Device pointers: assign int32 [n] (-1: none), ids int64 [n], vectors fp32 [n, dim]."""
+        check(lib().m3g_load_lists_device(self.h, index_id, ct.c_void_p(assign_ptr),
+                                          ct.c_void_p(ids_ptr), ct.c_void_p(vecs_ptr), n))
 
     def nearest_clusters_device(self, index_id, vecs_ptr, n, out_ptr):
         check(lib().m3g_nearest_clusters_device(self.h, index_id, ct.c_void_p(vecs_ptr), n,
@@ -396,6 +404,13 @@ class Engine:
                                       ct.c_void_p(ids_ptr), ct.c_void_p(scores_ptr),
                                       ct.c_void_p(counts_ptr),
                                       ct.c_void_p(stream) if stream else None))
+
+    def merge_shards_packed_device(self, packed_ptr, nshard, nq, k, shard_bytes, ids_offset,
+                                   out_ids_ptr, out_scores_ptr, out_counts_ptr, stream=None):
+        check(lib().m3g_merge_shards_packed_device(
+            self.h, ct.c_void_p(packed_ptr), nshard, nq, k, shard_bytes, ids_offset,
+            ct.c_void_p(out_ids_ptr), ct.c_void_p(out_scores_ptr), ct.c_void_p(out_counts_ptr),
+            ct.c_void_p(stream) if stream else None))
 
     def merge_shards_device(self, scores_ptr, ids_ptr, nshard, nq, k, out_ids_ptr,
                             out_scores_ptr, out_counts_ptr, stream=None):

@@ -290,6 +290,12 @@ int m3g_nearest_clusters(m3g_engine* e, int index_id, const float* vecs, int64_t
     return guarded([&] { e->eng.nearest_clusters(index_id, vecs, n, out_cluster); });
 }
 
+int m3g_load_lists_device(m3g_engine* e, int index_id, const int32_t* d_assign,
+                          const int64_t* d_ids, const float* d_vecs, int64_t n) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.load_lists_device(index_id, d_assign, d_ids, d_vecs, n); });
+}
+
 int m3g_nearest_clusters_device(m3g_engine* e, int index_id, const float* d_vecs, int64_t n,
                                 int32_t* d_out_cluster) {
     M3G_ENGINE_OR_FAIL(e);
@@ -408,6 +414,28 @@ int m3g_merge_shards_device(m3g_engine* e, const float* d_scores, const int64_t*
         auto st = static_cast<cudaStream_t>(stream);
         M3G_CK(m3g::launch_merge_shards(d_scores, d_ids, nshard, (int)nq, k, d_out_ids,
                                         d_out_scores, d_out_counts, st));
+        if (!st) M3G_CK(cudaStreamSynchronize(st));
+    });
+}
+
+int m3g_merge_shards_packed_device(m3g_engine* e, const void* d_packed, int nshard, int64_t nq,
+                                   int k, int64_t shard_bytes, int64_t ids_offset,
+                                   int64_t* d_out_ids, float* d_out_scores, int32_t* d_out_counts,
+                                   void* stream) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (nshard <= 0 || nq < 0 || k < 0 || nq > INT32_MAX)
+            m3g::fail(M3G_EINVAL, "merge_shards_packed: bad sizes");
+        if (nq > 0 && k > 0 && (!d_packed || !d_out_ids || !d_out_scores || !d_out_counts))
+            m3g::fail(M3G_EINVAL, "merge_shards_packed: buffers missing");
+        if (shard_bytes % 8 || ids_offset % 8 || ids_offset < nq * k * 4 ||
+            shard_bytes < ids_offset + nq * k * 8)
+            m3g::fail(M3G_EINVAL, "merge_shards_packed: bad record layout");
+        m3g::DeviceGuard g(e->eng.device());
+        auto st = static_cast<cudaStream_t>(stream);
+        M3G_CK(m3g::launch_merge_shards_packed(static_cast<const unsigned char*>(d_packed), nshard,
+                                               (int)nq, k, shard_bytes, ids_offset, d_out_ids,
+                                               d_out_scores, d_out_counts, st));
         if (!st) M3G_CK(cudaStreamSynchronize(st));
     });
 }

@@ -461,6 +461,142 @@ void list_add(Index& ix, int l, const int64_t* ids, const float* vecs, int64_t n
     L.live += n;
 }
 
+// Cluster::add_batch for many lists at once (the per-cluster ops of
+// enqueue_insert_auto, m3_async.cpp:262-313): rows grouped by list (ascending
+// list id, call order within a list); a list whose rows repeat an id, in the
+// batch or in the list, is skipped and reported through on_error, as its own
+// add_batch would have thrown.  Lists that outgrow their segment move first (at
+// most one arena rebuild), then every row is staged once and scattered to its
+// arena row with its id, tombstone and norm.
+template <class OnError>
+void list_add_routed(Index& ix, const std::vector<int64_t>& ids, const std::vector<float>& vecs,
+                     const std::vector<int32_t>& clusters, OnError on_error) {
+    const int64_t n = (int64_t)ids.size();
+    if (n == 0) return;
+    const int L = ix.nlist();
+    std::vector<int64_t> cnt((size_t)L + 1, 0);
+    for (int64_t i = 0; i < n; ++i) {
+        const int c = clusters[(size_t)i];
+        if (c < 0 || c >= L) {
+            on_error("IVFIndex::add_batch: invalid cluster_id");
+            return;
+        }
+        cnt[(size_t)c + 1]++;
+    }
+    for (int l = 0; l < L; ++l) cnt[(size_t)l + 1] += cnt[(size_t)l];
+    std::vector<int64_t> order((size_t)n);
+    {
+        std::vector<int64_t> cur(cnt.begin(), cnt.end() - 1);
+        for (int64_t i = 0; i < n; ++i) order[(size_t)cur[(size_t)clusters[(size_t)i]]++] = i;
+    }
+    // duplicate checks per list (Cluster::add_batch, cluster.cpp:55-101)
+    std::vector<char> ok((size_t)L, 1);
+    std::vector<int> touched;
+    for (int l = 0; l < L; ++l) {
+        const int64_t b = cnt[(size_t)l], e = cnt[(size_t)l + 1];
+        if (b == e) continue;
+        ListMeta& M = ix.lists[(size_t)l];
+        std::unordered_set<int64_t> seen;
+        seen.reserve((size_t)(e - b) * 2);
+        for (int64_t j = b; j < e && ok[(size_t)l]; ++j) {
+            const int64_t id = ids[(size_t)order[(size_t)j]];
+            if (!seen.insert(id).second) {
+                on_error("Cluster::add_batch: duplicate id in batch");
+                ok[(size_t)l] = 0;
+            } else if (M.id2row.count(id)) {
+                on_error("Cluster::add_batch: duplicate id exists");
+                ok[(size_t)l] = 0;
+            }
+        }
+        if (ok[(size_t)l]) touched.push_back(l);
+    }
+    // room: lists that outgrow their segment get max(need, 2 cap, 16) rows
+    int64_t extra = 0;
+    std::vector<std::pair<int, int64_t>> moves;
+    for (int l : touched) {
+        ListMeta& M = ix.lists[(size_t)l];
+        const int64_t need = M.len + cnt[(size_t)l + 1] - cnt[(size_t)l];
+        if (need > M.cap) {
+            const int64_t cap = std::max<int64_t>({need, M.cap * 2, 16});
+            moves.emplace_back(l, cap);
+            extra += cap;
+        }
+    }
+    if (!moves.empty()) {
+        if (ix.arena_used + extra > ix.arena_cap) {
+            // one rebuild lays every list out again, these at their new capacity
+            for (auto& mv : moves) ix.lists[(size_t)mv.first].cap = mv.second;
+            grow_arena(ix, 0);
+        } else {
+            // every moved list to a fresh segment at the arena's end, in one kernel
+            std::vector<int64_t> src, dstr;
+            for (auto& mv : moves) {
+                ListMeta& M = ix.lists[(size_t)mv.first];
+                const int64_t to = ix.arena_used;
+                for (int64_t r = 0; r < M.len; ++r) {
+                    src.push_back(M.off + r);
+                    dstr.push_back(to + r);
+                }
+                M.off = to;
+                M.cap = mv.second;
+                ix.arena_used += mv.second;
+            }
+            if (!src.empty()) {
+                DevIdx ds, dd;
+                ds.upload(src, ix.wstream);
+                dd.upload(dstr, ix.wstream);
+                M3G_CK(launch_move_rows(ix.vecs.p, ix.row_words(), ix.rnorm2.p, ix.ids.p,
+                                        ix.alive.p, ds.d.p, dd.d.p, (int64_t)src.size(),
+                                        ix.wstream));
+                M3G_CK(cudaStreamSynchronize(ix.wstream));
+            }
+        }
+    }
+    // destination arena rows of the kept rows, in staging order
+    std::vector<int64_t> dst, src_rows;
+    dst.reserve((size_t)n);
+    src_rows.reserve((size_t)n);
+    for (int l : touched) {
+        ListMeta& M = ix.lists[(size_t)l];
+        const int64_t b = cnt[(size_t)l], e = cnt[(size_t)l + 1];
+        for (int64_t j = b; j < e; ++j) {
+            const int64_t i = order[(size_t)j];
+            const int64_t row = M.len + (j - b);
+            dst.push_back(M.off + row);
+            src_rows.push_back(i);
+            M.id2row.emplace(ids[(size_t)i], row);
+            M.ids.push_back(ids[(size_t)i]);
+            M.alive.push_back(1);
+        }
+        M.len += e - b;
+        M.live += e - b;
+    }
+    const int64_t m = (int64_t)dst.size();
+    if (m == 0) return;
+    std::vector<float> staging((size_t)(m * ix.dim));
+    std::vector<int64_t> row_ids((size_t)m);
+    for (int64_t j = 0; j < m; ++j) {
+        std::memcpy(&staging[(size_t)(j * ix.dim)], &vecs[(size_t)(src_rows[(size_t)j] * ix.dim)],
+                    sizeof(float) * ix.dim);
+        row_ids[(size_t)j] = ids[(size_t)src_rows[(size_t)j]];
+    }
+    DBuf<float> d_src, nrm;
+    d_src.alloc((size_t)(m * ix.row_bytes() / 4));
+    nrm.alloc((size_t)m);
+    if (ix.ldr != ix.dim || ix.bf16_rows())
+        M3G_CK(cudaMemsetAsync(d_src.p, 0, (size_t)(m * ix.row_bytes()), ix.wstream));
+    store_rows(ix, reinterpret_cast<unsigned char*>(d_src.p), staging.data(), m, nrm.p);
+    DevIdx di, dids;
+    di.upload(dst, ix.wstream);
+    dids.upload(row_ids, ix.wstream);
+    const int w = ix.row_words();
+    M3G_CK(launch_scatter_rows(d_src.p, w, di.d.p, m, w, ix.vecs.p, w, ix.wstream));
+    M3G_CK(launch_scatter_i64(dids.d.p, di.d.p, m, ix.ids.p, ix.wstream));
+    M3G_CK(launch_set_bytes(ix.alive.p, di.d.p, m, 1, ix.wstream));
+    M3G_CK(launch_scatter_rows(nrm.p, 1, di.d.p, m, 1, ix.rnorm2.p, 1, ix.wstream));
+    M3G_CK(cudaStreamSynchronize(ix.wstream));
+}
+
 // Cluster::update_batch (cluster.cpp:103-133): rows apply in order; a missing
 // id without insert_if_absent raises after the earlier rows were applied.
 void list_update(Index& ix, int l, const int64_t* ids, const float* vecs, int64_t n,
@@ -761,6 +897,83 @@ void Engine::load_cluster_device(int index_id, int cid, const int64_t* d_ids, co
     refresh_list_meta(*ix);
 }
 
+void Engine::load_lists_device(int index_id, const int32_t* d_assign, const int64_t* d_ids,
+                               const float* d_vecs, int64_t n) {
+    auto ix = get(index_id, "load_lists_device");
+    if (n < 0 || (n > 0 && (!d_assign || !d_ids || !d_vecs)))
+        fail(M3G_EINVAL, "load_lists_device: buffers missing");
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    const int L = ix->nlist();
+    cudaStream_t st = ix->wstream;
+    std::vector<int32_t> a((size_t)n);
+    std::vector<int64_t> ids((size_t)n);
+    if (n > 0) {
+        M3G_CK(cudaMemcpyAsync(a.data(), d_assign, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+        M3G_CK(cudaMemcpyAsync(ids.data(), d_ids, (size_t)n * 8, cudaMemcpyDeviceToHost, st));
+        M3G_CK(cudaStreamSynchronize(st));
+    }
+    // stable grouping by list: the arena is laid out list after list in ascending
+    // id order, each list exactly its rows long, so sorted position j is arena row j
+    std::vector<int64_t> cnt((size_t)L + 1, 0);
+    for (int64_t i = 0; i < n; ++i) {
+        const int c = a[(size_t)i];
+        if (c >= L) fail(M3G_ERANGE, "load_lists_device: cluster id out of range");
+        if (c >= 0) cnt[(size_t)c + 1]++;
+    }
+    for (int l = 0; l < L; ++l) cnt[(size_t)l + 1] += cnt[(size_t)l];
+    const int64_t m = cnt[(size_t)L];
+    std::vector<int64_t> order((size_t)m);
+    {
+        std::vector<int64_t> cur(cnt.begin(), cnt.end() - 1);
+        for (int64_t i = 0; i < n; ++i)
+            if (a[(size_t)i] >= 0) order[(size_t)cur[(size_t)a[(size_t)i]]++] = i;
+    }
+    for (int l = 0; l < L; ++l) {
+        ListMeta& M = ix->lists[(size_t)l];
+        M.off = cnt[(size_t)l];
+        M.len = M.cap = M.live = cnt[(size_t)l + 1] - cnt[(size_t)l];
+        M.ids.resize((size_t)M.len);
+        M.alive.assign((size_t)M.len, 1);
+        M.id2row.clear();
+        M.id2row.reserve((size_t)M.len);
+        for (int64_t r = 0; r < M.len; ++r) {
+            M.ids[(size_t)r] = ids[(size_t)order[(size_t)(M.off + r)]];
+            M.id2row.emplace(M.ids[(size_t)r], r);
+        }
+    }
+    // a fresh arena of exactly m rows (it grows as inserts need)
+    const int64_t cap = std::max<int64_t>(m, 1024);
+    ix->vecs.alloc((size_t)(cap * ix->row_bytes() / 4));
+    ix->rnorm2.alloc((size_t)cap);
+    ix->ids.alloc((size_t)cap);
+    ix->alive.alloc((size_t)cap);
+    M3G_CK(cudaMemsetAsync(ix->vecs.p, 0, (size_t)(cap * ix->row_bytes()), st));
+    M3G_CK(cudaMemsetAsync(ix->alive.p, 0, (size_t)cap, st));
+    ix->arena_cap = cap;
+    ix->arena_used = m;
+    const int64_t chunk = std::max<int64_t>(1, (int64_t(1) << 28) / ((int64_t)ix->dpad * 4));
+    DBuf<float> stage;
+    DBuf<int64_t> d_order;
+    stage.alloc((size_t)(std::min(chunk, std::max<int64_t>(m, 1)) * ix->dpad));
+    d_order.alloc((size_t)std::max<int64_t>(m, 1));
+    if (m > 0)
+        M3G_CK(cudaMemcpyAsync(d_order.p, order.data(), (size_t)m * 8, cudaMemcpyHostToDevice, st));
+    for (int64_t j0 = 0; j0 < m; j0 += chunk) {
+        const int64_t k = std::min(chunk, m - j0);
+        if (ix->dpad != ix->dim)
+            M3G_CK(cudaMemsetAsync(stage.p, 0, (size_t)(k * ix->dpad) * 4, st));
+        M3G_CK(launch_gather_rows(d_vecs, ix->dim, d_order.p + j0, k, ix->dim, stage.p, ix->dpad, st));
+        store_staged_rows(*ix, ix->row_ptr(j0), stage.p, k, ix->rnorm2.p + j0);
+        M3G_CK(launch_gather_i64(d_ids, d_order.p + j0, k, ix->ids.p + j0, st));
+    }
+    if (m > 0) M3G_CK(cudaMemsetAsync(ix->alive.p, 1, (size_t)m, st));
+    M3G_CK(cudaStreamSynchronize(st));
+    rebuild_maps(*ix);
+    refresh_list_meta(*ix);
+}
+
 int Engine::storage_of(int index_id) {
     auto ix = get(index_id, "storage_of");
     return ix->storage;
@@ -849,29 +1062,53 @@ std::vector<std::vector<int64_t>> positions_by_list(const Index& ix, const std::
 }
 }  // namespace
 
-void Engine::apply(const WriteOp& op) {
-    auto ix = find(op.index_id);
-    if (!ix) fail(M3G_ERANGE, "writer: index " + std::to_string(op.index_id) + " not found");
+void Engine::apply_run(std::vector<WriteOp>& ops, size_t b, size_t e) {
+    auto ix = find(ops[b].index_id);
+    if (!ix) {
+        for (size_t i = b; i < e; ++i) {
+            record_error("writer: index " + std::to_string(ops[i].index_id) + " not found",
+                         M3G_ERANGE);
+            ++applied_;
+        }
+        return;
+    }
     DeviceGuard g(device_);
     std::unique_lock lk(ix->mu);
-    const bool any_list = op.cluster_id == kAnyList && op.kind != WriteOp::kInsert;
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
+    for (size_t i = b; i < e; ++i) {
+        try {
+            apply_locked(*ix, ops[i]);
+        } catch (const Error& err) {
+            record_error(err.what(), err.code);
+        } catch (const std::exception& err) {
+            record_error(err.what(), M3G_ERUNTIME);
+        }
+    }
+    try {
+        refresh_list_meta(*ix);
+    } catch (const Error& err) {
+        record_error(err.what(), err.code);
+    }
+    applied_ += (uint64_t)(e - b);
+}
+
+void Engine::apply_locked(Index& ixr, const WriteOp& op) {
+    Index* ix = &ixr;
+    const bool any_list = op.cluster_id == kAnyList && op.kind != WriteOp::kInsert &&
+                          op.kind != WriteOp::kInsertRouted;
+    if (op.kind == WriteOp::kInsertRouted) {
+        list_add_routed(*ix, op.ids, op.vecs, op.clusters, [this](const std::string& m) {
+            record_error(m, M3G_ERUNTIME);
+        });
+        return;
+    }
     if (!any_list && (op.cluster_id < 0 || op.cluster_id >= ix->nlist())) {
         const char* w = op.kind == WriteOp::kInsert   ? "IVFIndex::add_batch: invalid cluster_id"
                         : op.kind == WriteOp::kUpdate ? "IVFIndex::update_batch: invalid cluster_id"
                                                       : "IVFIndex::erase_batch: invalid cluster_id";
         fail(M3G_ERANGE, w);
     }
-    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
     const int64_t n = (int64_t)op.ids.size();
-    struct MetaRefresh {
-        Index& ix;
-        ~MetaRefresh() {
-            try {
-                refresh_list_meta(ix);
-            } catch (...) {
-            }
-        }
-    } refresh{*ix};
     if (any_list) {
         const auto pos = positions_by_list(*ix, op.ids);
         std::vector<int64_t> sub_ids;
@@ -904,6 +1141,8 @@ void Engine::apply(const WriteOp& op) {
         case WriteOp::kDelete:
             list_erase(*ix, op.cluster_id, op.ids.data(), n);
             break;
+        default:
+            break;
     }
 }
 
@@ -922,15 +1161,12 @@ void Engine::writer_loop() {
             }
             q_not_full_.notify_all();
         }
-        for (auto& op : batch) {
-            try {
-                apply(op);
-            } catch (const Error& e) {
-                record_error(e.what(), e.code);
-            } catch (const std::exception& e) {
-                record_error(e.what(), M3G_ERUNTIME);
-            }
-            ++applied_;
+        // runs of consecutive ops on one index share the lock and the metadata refresh
+        for (size_t b = 0; b < batch.size();) {
+            size_t e = b + 1;
+            while (e < batch.size() && batch[e].index_id == batch[b].index_id) ++e;
+            apply_run(batch, b, e);
+            b = e;
         }
         std::lock_guard lk(qmu_);
         q_not_full_.notify_all();
@@ -1009,13 +1245,102 @@ std::vector<int> Engine::oversized_lists(int index_id, double mean_factor) {
 
 int Engine::split_oversized(int index_id, double mean_factor, int niter, uint64_t seed) {
     if (!(mean_factor > 0)) fail(M3G_EINVAL, "split_oversized: mean_factor must be > 0");
+    if (niter < 0) fail(M3G_EINVAL, "split_oversized: niter < 0");
+    auto ix = get(index_id, "split_oversized");
+    DeviceGuard g(device_);
+    std::unique_lock lk(ix->mu);
+    if (ws_.done) M3G_CK(cudaEventSynchronize(ws_.done));
     // the lists over the limit when the pass starts (live rows > factor x the mean
-    // over all lists), split in ascending id order; new lists join at the end
-    const std::vector<int> todo = oversized_lists(index_id, mean_factor);
-    int n = 0;
-    for (int l : todo)
-        if (split_cluster(index_id, l, niter, seed + (uint64_t)l) >= 0) ++n;
-    return n;
+    // over all lists); every one is split as split_cluster would split it, all at
+    // once: one segmented 2-means over their rows, then the regrouping in
+    // ascending list order, so new lists get the next ids in that order
+    const int L0 = ix->nlist();
+    if (L0 == 0) return 0;
+    int64_t total = 0;
+    for (const auto& l : ix->lists) total += l.live;
+    const double limit = mean_factor * ((double)total / (double)L0);
+    std::vector<int> todo;
+    for (int l = 0; l < L0; ++l)
+        if ((double)ix->lists[(size_t)l].live > limit) {
+            list_compact(*ix, l);
+            if (ix->lists[(size_t)l].len >= 2) todo.push_back(l);
+        }
+    if (todo.empty()) {
+        refresh_list_meta(*ix);
+        return 0;
+    }
+    const int nseg = (int)todo.size();
+    const int dpad = ix->dpad;
+    cudaStream_t st = ix->wstream;
+    std::vector<int64_t> seg_off((size_t)nseg + 1, 0);
+    for (int s = 0; s < nseg; ++s) seg_off[(size_t)s + 1] = seg_off[(size_t)s] + ix->lists[(size_t)todo[(size_t)s]].len;
+    const int64_t n = seg_off[(size_t)nseg];
+    // the rows as fp32 [n, dpad], segment by segment
+    DBuf<float> X, C2;
+    DBuf<int32_t> side, row_seg;
+    DBuf<int64_t> d_off;
+    X.alloc((size_t)(n * dpad));
+    C2.alloc((size_t)(2 * nseg) * dpad);
+    side.alloc((size_t)n);
+    row_seg.alloc((size_t)n);
+    for (int s = 0; s < nseg; ++s) {
+        const ListMeta& M = ix->lists[(size_t)todo[(size_t)s]];
+        float* dst = X.p + seg_off[(size_t)s] * dpad;
+        if (ix->bf16_rows())
+            M3G_CK(launch_unpack_bf16_rows(reinterpret_cast<const __nv_bfloat16*>(ix->row_ptr(M.off)),
+                                           ix->ldr, M.len, ix->dim, dst, dpad, st));
+        else
+            M3G_CK(cudaMemcpyAsync(dst, ix->row_ptr(M.off), (size_t)(M.len * dpad) * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+    }
+    std::vector<int32_t> rs((size_t)n);
+    std::vector<int64_t> init((size_t)2 * nseg);
+    for (int s = 0; s < nseg; ++s) {
+        const int64_t b = seg_off[(size_t)s], e = seg_off[(size_t)s + 1];
+        std::fill(rs.begin() + b, rs.begin() + e, s);
+        int64_t pick[2];
+        sample_rows(seed + (uint64_t)todo[(size_t)s], e - b, 2, pick);
+        init[(size_t)2 * s] = b + pick[0];
+        init[(size_t)2 * s + 1] = b + pick[1];
+    }
+    M3G_CK(cudaMemcpyAsync(row_seg.p, rs.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st));
+    d_off.alloc((size_t)nseg + 1);
+    M3G_CK(cudaMemcpyAsync(d_off.p, seg_off.data(), seg_off.size() * 8, cudaMemcpyHostToDevice, st));
+    DevIdx di;
+    di.upload(init, st);
+    M3G_CK(launch_gather_rows(X.p, dpad, di.d.p, 2 * nseg, dpad, C2.p, dpad, st));
+    const int nz = ix->normalized ? 1 : 0;
+    for (int it = 0; it < niter; ++it) {
+        M3G_CK(launch_seg2_assign(X.p, dpad, row_seg.p, n, C2.p, ix->dim, ix->metric, nz, side.p, st));
+        M3G_CK(launch_seg2_update(X.p, dpad, d_off.p, nseg, side.p, ix->dim, C2.p, st));
+    }
+    M3G_CK(launch_seg2_assign(X.p, dpad, row_seg.p, n, C2.p, ix->dim, ix->metric, nz, side.p, st));
+    std::vector<float> c2((size_t)(2 * nseg) * ix->dim);
+    M3G_CK(cudaMemcpy2DAsync(c2.data(), (size_t)ix->dim * 4, C2.p, (size_t)dpad * 4,
+                             (size_t)ix->dim * 4, (size_t)(2 * nseg), cudaMemcpyDeviceToHost, st));
+    std::vector<int32_t> sd((size_t)n);
+    M3G_CK(cudaMemcpyAsync(sd.data(), side.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    M3G_CK(cudaStreamSynchronize(st));
+    // set_centroid(l, c0); add_cluster(c1); rows regrouped in list order
+    // (m3_index.cpp:133-163), list by list in ascending id order
+    ensure_centroid_cap(*ix, (size_t)(L0 + nseg));
+    for (int s = 0; s < nseg; ++s) {
+        const int l = todo[(size_t)s];
+        const float* c0 = &c2[(size_t)(2 * s) * ix->dim];
+        std::copy(c0, c0 + ix->dim, ix->centroids.begin() + (size_t)l * ix->dim);
+        upload_centroids(*ix, l, 1);
+        const int nid = ix->nlist();
+        ix->centroids.insert(ix->centroids.end(), c0 + ix->dim, c0 + 2 * ix->dim);
+        ix->lists.emplace_back();
+        upload_centroids(*ix, nid, 1);
+        std::vector<int64_t> side0, side1;
+        for (int64_t r = seg_off[(size_t)s]; r < seg_off[(size_t)s + 1]; ++r)
+            (sd[(size_t)r] == 1 ? side1 : side0).push_back(r - seg_off[(size_t)s]);
+        regroup_rows(*ix, l, side1, nid);
+        regroup_rows(*ix, l, side0, l);
+    }
+    refresh_list_meta(*ix);
+    return nseg;
 }
 
 void Engine::compact_cluster(int index_id, int cid) {
@@ -1887,27 +2212,20 @@ bool Engine::enqueue_insert_auto(int index_id, const int64_t* ids, const float* 
         fail(M3G_EINVAL, "AsyncEngine::enqueue_insert_auto: vecs size mismatch");
     std::vector<int32_t> assign((size_t)n);
     nearest_clusters(index_id, vecs, n, assign.data());
-    const int dim = ix->dim;
-    std::vector<int> order;
-    std::unordered_map<int, WriteOp> per;
-    for (int64_t i = 0; i < n; ++i) {
-        const int c = assign[(size_t)i];
-        if (c < 0) fail(M3G_ERUNTIME, "AsyncEngine::enqueue_insert_auto: unable to assign cluster");
-        auto [it, ins] = per.emplace(c, WriteOp{});
-        if (ins) {
-            it->second.kind = WriteOp::kInsert;
-            it->second.index_id = index_id;
-            it->second.cluster_id = c;
-            order.push_back(c);
-        }
-        it->second.ids.push_back(ids[i]);
-        it->second.vecs.insert(it->second.vecs.end(), vecs + i * dim, vecs + (i + 1) * dim);
-    }
-    std::sort(order.begin(), order.end());
-    bool ok = true;
-    for (int c : order)
-        if (!enqueue(std::move(per[c]))) ok = false;
-    return ok;
+    for (int64_t i = 0; i < n; ++i)
+        if (assign[(size_t)i] < 0)
+            fail(M3G_ERUNTIME, "AsyncEngine::enqueue_insert_auto: unable to assign cluster");
+    // one op carrying every row and its list: the writer applies it as one
+    // add_batch per list (ascending list id, rows in call order), under one lock
+    // with one staging copy and one scatter, instead of one queued op per list
+    WriteOp op;
+    op.kind = WriteOp::kInsertRouted;
+    op.index_id = index_id;
+    op.cluster_id = -1;
+    op.ids.assign(ids, ids + n);
+    op.vecs.assign(vecs, vecs + n * (int64_t)ix->dim);
+    op.clusters = std::move(assign);
+    return enqueue(std::move(op));
 }
 
 // ---------------- k-means / split ----------------

@@ -157,11 +157,14 @@ struct MaintenancePolicy {
 constexpr int kAnyList = -1;
 
 struct WriteOp {
-    enum Kind { kInsert, kUpdate, kDelete } kind = kInsert;
+    // kInsertRouted: the rows of one enqueue_insert_auto call with their lists
+    // (clusters[i] for row i), applied as one Cluster::add_batch per list
+    enum Kind { kInsert, kUpdate, kDelete, kInsertRouted } kind = kInsert;
     int index_id = 0, cluster_id = 0;
     bool insert_if_absent = false;
     std::vector<int64_t> ids;
     std::vector<float> vecs;
+    std::vector<int32_t> clusters;
 };
 
 // Scratch of the search pipeline, grown on demand and reused across calls.
@@ -211,6 +214,10 @@ class Engine {
     // the same with device rows: d_vecs [n, dim] fp32 or bf16 bits (dtype), d_ids [n]
     void load_cluster_device(int index_id, int cid, const int64_t* d_ids, const void* d_vecs,
                              int64_t n, int dtype);
+    // every list replaced at once by the rows assigned to it (d_assign[i], -1:
+    // none), rows of a list in ascending row order; device rows fp32 [n, dim]
+    void load_lists_device(int index_id, const int32_t* d_assign, const int64_t* d_ids,
+                           const float* d_vecs, int64_t n);
     int storage_of(int index_id);
     bool enqueue(WriteOp&& op);
     bool enqueue_insert_auto(int index_id, const int64_t* ids, const float* vecs, int64_t n);
@@ -277,7 +284,10 @@ class Engine {
     std::shared_ptr<Index> get(int index_id, const char* who) const;
     void writer_loop();
     void maintenance_loop();
-    void apply(const WriteOp& op);
+    // applies a run of ops of one index under one exclusive lock, one list
+    // metadata refresh at the end; per-op errors are recorded
+    void apply_run(std::vector<WriteOp>& ops, size_t b, size_t e);
+    void apply_locked(Index& ix, const WriteOp& op);
     void record_error(const std::string& msg, int code);
 
     // device helpers (callers hold the right index lock)

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "score.cuh"
 #include "kernels_kmeans.h"
 
 namespace m3g {
@@ -269,6 +270,104 @@ unsigned grid_for(int64_t total) {
     return (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 8192));
 }
 }  // namespace
+
+// ---------------------------------------------------------------------------
+// Segmented 2-means (the split pass): segment s = rows [seg_off[s],
+// seg_off[s+1]) of X, two centroids per segment in C2 [2 nseg, ld].  The same
+// rules as the k-means above, per segment: exact nearest_clusters assignment
+// (strict '<', centroid 0 wins ties, -1 if both scores are NaN) and fp64 means
+// in ascending row order, an empty side keeping its centroid.
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void seg2_assign_kernel(const float* __restrict__ X, int64_t ld,
+                                   const int32_t* __restrict__ row_seg, int64_t n,
+                                   const float* __restrict__ C2, int dim, int metric,
+                                   int normalized, int32_t* __restrict__ side) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n) return;
+    const int s = row_seg[r];
+    const float* x = X + r * ld;
+    const float s0 = exact_score(x, C2 + (int64_t)(2 * s) * ld, dim, metric, normalized != 0);
+    const float s1 = exact_score(x, C2 + (int64_t)(2 * s + 1) * ld, dim, metric, normalized != 0);
+    float best = __int_as_float(0x7f800000);
+    int bid = -1;
+    if (s0 < best) {
+        best = s0;
+        bid = 0;
+    }
+    if (s1 < best) bid = 1;
+    side[r] = bid;
+}
+
+__global__ void seg2_update_kernel(const float* __restrict__ X, int64_t ld,
+                                   const int64_t* __restrict__ seg_off, int nseg,
+                                   const int32_t* __restrict__ side, int dim,
+                                   float* __restrict__ C2) {
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    const int s = blockIdx.y >> 1, which = blockIdx.y & 1;
+    if (d >= dim || s >= nseg) return;
+    double acc = 0.0;
+    int64_t cnt = 0;
+    for (int64_t r = seg_off[s]; r < seg_off[s + 1]; ++r)
+        if (side[r] == which) {
+            acc += (double)X[r * ld + d];
+            ++cnt;
+        }
+    if (cnt > 0) C2[(int64_t)(2 * s + which) * ld + d] = (float)(acc / (double)cnt);
+}
+}  // namespace
+
+cudaError_t launch_seg2_assign(const float* X, int64_t ld, const int32_t* row_seg, int64_t n,
+                               const float* C2, int dim, int metric, int normalized,
+                               int32_t* side, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    seg2_assign_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(X, ld, row_seg, n, C2, dim,
+                                                                    metric, normalized, side);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_seg2_update(const float* X, int64_t ld, const int64_t* seg_off, int nseg,
+                               const int32_t* side, int dim, float* C2, cudaStream_t st) {
+    if (nseg <= 0) return cudaSuccess;
+    for (int s0 = 0; s0 < nseg; s0 += 32768) {
+        const int m = std::min(32768, nseg - s0);
+        dim3 grid((unsigned)((dim + 127) / 128), (unsigned)(2 * m));
+        seg2_update_kernel<<<grid, 128, 0, st>>>(X, ld, seg_off + s0, m, side, dim,
+                                                 C2 + (int64_t)(2 * s0) * ld);
+    }
+    return cudaGetLastError();
+}
+
+namespace {
+// Row moves inside one arena (disjoint source and destination rows): the row
+// words, the norm, the id and the tombstone of row src[i] go to row dst[i].
+__global__ void move_rows_kernel(float* __restrict__ vecs, int64_t words, float* __restrict__ nrm,
+                                 int64_t* __restrict__ ids, uint8_t* __restrict__ alive,
+                                 const int64_t* __restrict__ src, const int64_t* __restrict__ dst,
+                                 int64_t n) {
+    const int64_t r = blockIdx.y + (int64_t)blockIdx.z * 65535;
+    if (r >= n) return;
+    const int64_t s = src[r], t = dst[r];
+    for (int64_t j = blockIdx.x * blockDim.x + threadIdx.x; j < words; j += gridDim.x * blockDim.x)
+        vecs[t * words + j] = vecs[s * words + j];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        nrm[t] = nrm[s];
+        ids[t] = ids[s];
+        alive[t] = alive[s];
+    }
+}
+}  // namespace
+
+cudaError_t launch_move_rows(float* vecs, int64_t words, float* nrm, int64_t* ids, uint8_t* alive,
+                             const int64_t* src, const int64_t* dst, int64_t n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int64_t z = (n + 65534) / 65535;
+    if (z > 65535) return cudaErrorInvalidValue;
+    dim3 grid((unsigned)std::min<int64_t>((words + 255) / 256, 8), (unsigned)std::min<int64_t>(n, 65535),
+              (unsigned)z);
+    move_rows_kernel<<<grid, 256, 0, st>>>(vecs, words, nrm, ids, alive, src, dst, n);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_round_bf16_rows(float* X, int64_t ld, int64_t n, int dim, cudaStream_t st) {
     if (n <= 0 || dim <= 0) return cudaSuccess;

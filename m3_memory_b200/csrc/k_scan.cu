@@ -783,8 +783,9 @@ static_assert(RS_MAX * 33 * 4 <= MCAP * 8, "the staging tile fits in the candida
 __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
     const float* __restrict__ part_score, const int64_t* __restrict__ part_row,
     const int64_t* __restrict__ row_ids, int P, int k, int64_t stride_q, int64_t stride_slot,
-    int64_t* __restrict__ out_ids, float* __restrict__ out_scores,
-    int32_t* __restrict__ out_counts, MergeRescore rs, int rescore) {
+    int64_t rstride_q, int64_t rstride_slot, int64_t* __restrict__ out_ids,
+    float* __restrict__ out_scores, int32_t* __restrict__ out_counts, MergeRescore rs,
+    int rescore) {
     __shared__ unsigned long long cand[MCAP];
     __shared__ unsigned long long won[RS_MAX];
     __shared__ float exact[RS_MAX];
@@ -794,9 +795,11 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
     const int q = blockIdx.x;
     const int64_t n = (int64_t)P * k;
     const float* ps = part_score + (int64_t)q * stride_q;
-    const int64_t* pr = part_row + (int64_t)q * stride_q;
+    const int64_t* pr = part_row + (int64_t)q * rstride_q;
     const float INF = __int_as_float(0x7f800000);
+    // candidate i = slot * k + j: its score at ps[at(i)], its row / id at pr[rat(i)]
     auto at = [&](int64_t i) -> int64_t { return (i / k) * stride_slot + (i % k); };
+    auto rat = [&](int64_t i) -> int64_t { return (i / k) * rstride_slot + (i % k); };
 
     // tau: smallest k-th score among full partial lists; count valid candidates
     float tau = INF;
@@ -887,7 +890,7 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
         float* tile = reinterpret_cast<float*>(cand);  // [RS_MAX][33]
         __shared__ float qt[32];
         __shared__ int64_t wrow[RS_MAX];
-        if (j < kk) wrow[j] = pr[at((int64_t)(won[j] & 0xffffffffu))];
+        if (j < kk) wrow[j] = pr[rat((int64_t)(won[j] & 0xffffffffu))];
         const float* qr = rs.Q + (int64_t)q * rs.ldq;
         float e = 0.f;
         for (int d0 = 0; d0 < rs.dim; d0 += 32) {
@@ -950,11 +953,12 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
             if (rescore) {
                 const uint32_t w = (uint32_t)(c & 0xffffffffu);
                 s = exact[w];
-                id = row_ids[pr[at((int64_t)(won[w] & 0xffffffffu))]];
+                id = row_ids[pr[rat((int64_t)(won[w] & 0xffffffffu))]];
             } else {
-                const int64_t off = at((int64_t)(c & 0xffffffffu));
-                s = ps[off];
-                id = row_ids ? row_ids[pr[off]] : pr[off];
+                const int64_t i = (int64_t)(c & 0xffffffffu);
+                s = ps[at(i)];
+                const int64_t r = pr[rat(i)];
+                id = row_ids ? row_ids[r] : r;
             }
         }
         out_ids[(int64_t)q * k + j] = id;
@@ -972,8 +976,9 @@ cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
     if (rs && (k > RS_MAX || !row_ids)) return cudaErrorInvalidValue;
     const MergeRescore none{};
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(part_score, part_row, row_ids, P, k,
-                                                (int64_t)P * k, k, out_ids, out_scores,
-                                                out_counts, rs ? *rs : none, rs ? 1 : 0);
+                                                (int64_t)P * k, k, (int64_t)P * k, k, out_ids,
+                                                out_scores, out_counts, rs ? *rs : none,
+                                                rs ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -999,8 +1004,22 @@ cudaError_t launch_merge_shards(const float* scores, const int64_t* ids, int nsh
                                 cudaStream_t st) {
     if (nq <= 0 || k <= 0) return cudaSuccess;
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(scores, ids, nullptr, nshard, k, k,
-                                                (int64_t)nq * k, out_ids, out_scores, out_counts,
-                                                MergeRescore{}, 0);
+                                                (int64_t)nq * k, k, (int64_t)nq * k, out_ids,
+                                                out_scores, out_counts, MergeRescore{}, 0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_shards_packed(const unsigned char* packed, int nshard, int nq, int k,
+                                       int64_t shard_bytes, int64_t ids_offset, int64_t* out_ids,
+                                       float* out_scores, int32_t* out_counts, cudaStream_t st) {
+    if (nq <= 0 || k <= 0) return cudaSuccess;
+    if (shard_bytes % 8 || ids_offset % 8 || (reinterpret_cast<uintptr_t>(packed) & 7) ||
+        ids_offset < (int64_t)nq * k * 4 || shard_bytes < ids_offset + (int64_t)nq * k * 8)
+        return cudaErrorInvalidValue;
+    merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(
+        reinterpret_cast<const float*>(packed), reinterpret_cast<const int64_t*>(packed + ids_offset),
+        nullptr, nshard, k, k, shard_bytes / 4, k, shard_bytes / 8, out_ids, out_scores, out_counts,
+        MergeRescore{}, 0);
     return cudaGetLastError();
 }
 

@@ -128,6 +128,12 @@ cudaError_t launch_probe_scores(const float* Q, int64_t ldq, const float* C, int
                                 const int32_t* probes, int64_t nq, int P, int D, int metric,
                                 int normalized, float* out, cudaStream_t st);
 
+// The same over one gathered buffer: shard s's record starts at packed + s *
+// shard_bytes and holds its [nq, k] fp32 scores, then at ids_offset its [nq, k]
+// int64 ids (both multiples of 8 bytes).
+cudaError_t launch_merge_shards_packed(const unsigned char* packed, int nshard, int nq, int k,
+                                       int64_t shard_bytes, int64_t ids_offset, int64_t* out_ids,
+                                       float* out_scores, int32_t* out_counts, cudaStream_t st);
 cudaError_t launch_merge_shards(const float* scores, const int64_t* ids, int nshard, int nq, int k,
                                 int64_t* out_ids, float* out_scores, int32_t* out_counts,
                                 cudaStream_t st);

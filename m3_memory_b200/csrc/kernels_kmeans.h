@@ -24,6 +24,18 @@ cudaError_t launch_gather_rows(const float* src, int64_t lds, const int64_t* idx
                                int width, float* dst, int64_t ldd, cudaStream_t st);
 cudaError_t launch_scatter_rows(const float* src, int64_t lds, const int64_t* dst_rows, int64_t n,
                                 int width, float* dst, int64_t ldd, cudaStream_t st);
+// Segmented 2-means of the split pass: per row its segment's exact nearest of
+// two centroids (side 0 / 1, -1 if both scores are NaN); per (segment, side,
+// dim) the fp64 mean over the segment's rows on that side, in row order.
+cudaError_t launch_seg2_assign(const float* X, int64_t ld, const int32_t* row_seg, int64_t n,
+                               const float* C2, int dim, int metric, int normalized,
+                               int32_t* side, cudaStream_t st);
+cudaError_t launch_seg2_update(const float* X, int64_t ld, const int64_t* seg_off, int nseg,
+                               const int32_t* side, int dim, float* C2, cudaStream_t st);
+// Moves arena rows src[i] -> dst[i] (disjoint sets): row words, norm, id and
+// tombstone.
+cudaError_t launch_move_rows(float* vecs, int64_t words, float* nrm, int64_t* ids, uint8_t* alive,
+                             const int64_t* src, const int64_t* dst, int64_t n, cudaStream_t st);
 // bf16 rows of the list arena: values rounded to bf16 in place (kept as fp32),
 // packed fp32 -> bf16 rows (columns dim .. ldd zero), and widened back.
 cudaError_t launch_round_bf16_rows(float* X, int64_t ld, int64_t n, int dim, cudaStream_t st);

@@ -134,13 +134,17 @@ struct RegTopKW {
         tau = tau < c ? tau : c;
     }
 
-    // key of entry e (warp-uniform e < 32 KW), in every lane
+    // key of entry e (warp-uniform e < 32 KW), in every lane.  Every level is
+    // shuffled and the right one selected, so top[] is never indexed by a runtime
+    // value (which would move it to local memory).
     __device__ __forceinline__ unsigned long long entry(int e) const {
         unsigned long long v = ~0ull;
 #pragma unroll
-        for (int w = 0; w < KW; ++w)
-            if ((e >> 5) == w) v = top[w];
-        return shfl_u64(v, e & 31);
+        for (int w = 0; w < KW; ++w) {
+            const unsigned long long t = shfl_u64(top[w], e & 31);
+            v = (e >> 5) == w ? t : v;
+        }
+        return v;
     }
 
     __device__ __forceinline__ void flush(unsigned long long* buf, int k, int lane) {
@@ -154,7 +158,11 @@ struct RegTopKW {
             const unsigned long long lo = top[w] < rc ? top[w] : rc;
             const unsigned long long hi = top[w] < rc ? rc : top[w];
             top[w] = warp_bitonic_clean(lo, lane);
-            if (w + 1 < KW) c = warp_bitonic_clean(hi, lane);
+            if (w + 1 < KW) {
+                // nothing carried on: the lower levels are unchanged
+                if (__all_sync(0xffffffffu, hi == ~0ull)) break;
+                c = warp_bitonic_clean(hi, lane);
+            }
         }
 #pragma unroll
         for (int w = 0; w < KW; ++w)

@@ -9,8 +9,10 @@ go through one all-gather (NCCL over NVLink) and are merged on the GPU by
 is the final ascending sort of ``IVFIndex::search_nprobe``
 (AgentMemory/M3/src/m3_index.cpp:444-475) applied across shards.
 
-The exchange is the only collective on the path; its size is
-``world * Q * k * 12`` bytes per batch.
+The exchange is the only collective on the path: each rank's answer is one
+record (its ``[Q, k]`` fp32 scores, then its ``[Q, k]`` int64 ids), so a single
+all-gather of ``world * Q * k * 12`` bytes per batch moves both, and the merge
+reads the gathered records in place (``m3g_merge_shards_packed_device``).
 
 With ``split_coarse=True`` the coarse step is split by query instead of being
 repeated: rank r selects the probes of its slice of the batch (queries
@@ -35,6 +37,12 @@ others) before the top-k exchange above.
 from __future__ import annotations
 
 import numpy as np
+
+
+def torch_dtype(name):
+    import torch
+
+    return getattr(torch, name)
 
 
 def shard_lists(sizes, world: int) -> np.ndarray:
@@ -108,8 +116,10 @@ class ShardedSearch:
         self.ids = torch.empty((max_q, k), dtype=torch.int64, device=device)
         self.sc = torch.empty((max_q, k), dtype=torch.float32, device=device)
         self.cnt = torch.empty((max_q,), dtype=torch.int32, device=device)
-        self.g_ids = torch.empty((world, max_q, k), dtype=torch.int64, device=device)
-        self.g_sc = torch.empty((world, max_q, k), dtype=torch.float32, device=device)
+        # this rank's answer as one record (scores, then ids), and the gathered records
+        self.rec = torch.empty(self.record_bytes(max_q), dtype=torch.uint8, device=device)
+        self.g_rec = torch.empty(world * self.record_bytes(max_q), dtype=torch.uint8,
+                                 device=device)
         self.out_ids = torch.empty((max_q, k), dtype=torch.int64, device=device)
         self.out_sc = torch.empty((max_q, k), dtype=torch.float32, device=device)
         self.out_cnt = torch.empty((max_q,), dtype=torch.int32, device=device)
@@ -117,6 +127,24 @@ class ShardedSearch:
         # set to a list to have search() append (phase, CUDA event) pairs, recorded on
         # the current stream at the end of each phase ("start" first)
         self.marks = None
+
+    def record_bytes(self, nq: int) -> int:
+        """Bytes of one rank's answer record for nq queries: [nq, k] fp32 scores,
+        padded to 8 bytes, then [nq, k] int64 ids."""
+        return self.ids_offset(nq) + nq * self.k * 8
+
+    def ids_offset(self, nq: int) -> int:
+        return (nq * self.k * 4 + 7) // 8 * 8
+
+    def _answer_views(self, nq):
+        """Where this rank's search writes its answer: for world > 1 straight into
+        its record (scores, ids), else the plain buffers."""
+        if self.world == 1:
+            return self.ids[:nq], self.sc[:nq]
+        k, off = self.k, self.ids_offset(nq)
+        sc = self.rec[:nq * k * 4].view(torch_dtype("float32")).view(nq, k)
+        ids = self.rec[off:off + nq * k * 8].view(torch_dtype("int64")).view(nq, k)
+        return ids, sc
 
     def _mark(self, name):
         if self.marks is not None:
@@ -140,32 +168,31 @@ class ShardedSearch:
         k = self.k
         s = torch.cuda.current_stream(q.device).cuda_stream
         self._mark("start")
+        a_ids, a_sc = self._answer_views(nq)
         if self.coarse_index_id is not None:
-            self._search_sharded_coarse(q, nq, nprobe, s)
+            self._search_sharded_coarse(q, nq, nprobe, s, a_ids, a_sc)
         elif self.split_coarse:
-            self._search_split_coarse(q, nq, nprobe, s)
+            self._search_split_coarse(q, nq, nprobe, s, a_ids, a_sc)
         else:
             self.engine.search_device(self.index_id, q.data_ptr(), nq, k, nprobe,
-                                      self.ids.data_ptr(), self.sc.data_ptr(),
-                                      self.cnt.data_ptr(), s)
+                                      a_ids.data_ptr(), a_sc.data_ptr(), self.cnt.data_ptr(), s)
             self._mark("search")
         if self.world == 1:
             return self.ids[:nq], self.sc[:nq], self.cnt[:nq]
-        # [world, nq, k] views over the start of the gather buffers (contiguous)
-        g_sc = self.g_sc.view(-1)[:self.world * nq * k].view(self.world, nq, k)
-        g_ids = self.g_ids.view(-1)[:self.world * nq * k].view(self.world, nq, k)
-        dist.all_gather_into_tensor(g_sc, self.sc[:nq], group=self.group)
-        dist.all_gather_into_tensor(g_ids, self.ids[:nq], group=self.group)
-        self.engine.merge_shards_device(g_sc.data_ptr(), g_ids.data_ptr(), self.world, nq, k,
-                                        self.out_ids.data_ptr(), self.out_sc.data_ptr(),
-                                        self.out_cnt.data_ptr(), s)
+        # one all-gather of the answer records, merged where they land
+        R = self.record_bytes(nq)
+        g = self.g_rec[:self.world * R]
+        dist.all_gather_into_tensor(g, self.rec[:R], group=self.group)
+        self.engine.merge_shards_packed_device(g.data_ptr(), self.world, nq, k, R,
+                                               self.ids_offset(nq), self.out_ids.data_ptr(),
+                                               self.out_sc.data_ptr(), self.out_cnt.data_ptr(), s)
         self._mark("topk_exchange")
         return self.out_ids[:nq], self.out_sc[:nq], self.out_cnt[:nq]
 
-    def _search_split_coarse(self, q, nq, nprobe, s):
+    def _search_split_coarse(self, q, nq, nprobe, s, a_ids, a_sc):
         """Probes of this rank's query slice, all-gathered, then the scan of the
-        rank's lists for the whole batch; leaves the rank's top-k in self.ids /
-        sc / cnt."""
+        rank's lists for the whole batch; writes the rank's top-k to a_ids / a_sc
+        (counts to self.cnt)."""
         import torch.distributed as dist
 
         P = min(nprobe if nprobe > 0 else self.nlist, self.nlist)
@@ -189,13 +216,14 @@ class ShardedSearch:
             probes.copy_(loc)
         self._mark("probe_exchange")
         self.engine.search_probes_device(self.index_id, q.data_ptr(), nq, self.k,
-                                         probes.data_ptr(), P, self.ids.data_ptr(),
-                                         self.sc.data_ptr(), self.cnt.data_ptr(), s)
+                                         probes.data_ptr(), P, a_ids.data_ptr(),
+                                         a_sc.data_ptr(), self.cnt.data_ptr(), s)
         self._mark("search")
 
-    def _search_sharded_coarse(self, q, nq, nprobe, s):
+    def _search_sharded_coarse(self, q, nq, nprobe, s, a_ids, a_sc):
         """Global top-P from the ranks' exact local top-P, then the scan of the
-        winners this rank owns; leaves the rank's top-k in self.ids / sc / cnt."""
+        winners this rank owns; writes the rank's top-k to a_ids / a_sc (counts to
+        self.cnt)."""
         import torch
         import torch.distributed as dist
 
@@ -231,5 +259,5 @@ class ShardedSearch:
         mine = (top_id >= 0) & (self.owner[top_id.clamp(min=0)] == self.rank)
         probes = torch.where(mine, top_id, torch.full_like(top_id, -1)).to(torch.int32)
         self.engine.search_probes_device(self.index_id, q.data_ptr(), nq, self.k,
-                                         probes.data_ptr(), P, self.ids.data_ptr(),
-                                         self.sc.data_ptr(), self.cnt.data_ptr(), s)
+                                         probes.data_ptr(), P, a_ids.data_ptr(),
+                                         a_sc.data_ptr(), self.cnt.data_ptr(), s)

@@ -190,3 +190,42 @@ def test_device_loading_equals_host_loading(cabi, storage):
     dev.nearest_clusters_device(1, xd.data_ptr(), len(X), out.data_ptr())
     torch.cuda.synchronize()
     np.testing.assert_array_equal(out.cpu().numpy(), host.nearest_clusters(1, X))
+
+
+@pytest.mark.parametrize("storage", [0, 1])
+def test_one_pass_device_load_equals_list_by_list(cabi, storage):
+    """m3g_load_lists_device (every list at once from device rows and their
+    assignment, -1 skipping a row) builds the same lists as m3g_load_cluster
+    called per list with each list's rows in order, and later inserts grow it."""
+    import torch
+
+    rng = np.random.default_rng(31 + storage)
+    d, L, n = 72, 9, 3000
+    C = rng.standard_normal((L, d)).astype(np.float32)
+    a = rng.integers(-1, L, n).astype(np.int32)
+    a[a == 4] = 5  # an empty list
+    X = (C[np.maximum(a, 0)] + 0.5 * rng.standard_normal((n, d))).astype(np.float32)
+    ids = rng.permutation(10 * n)[:n].astype(np.int64)
+    one, per = cabi.Engine(), cabi.Engine()
+    for e in (one, per):
+        e.create_ivf(1, d, 0, False, C, storage=storage)
+    for c in range(L):
+        rows = np.flatnonzero(a == c)
+        per.load_cluster(1, c, ids[rows], X[rows])
+    ta, ti, tx = (torch.from_numpy(v).cuda() for v in (a, ids, X))
+    one.load_lists_device(1, ta.data_ptr(), ti.data_ptr(), tx.data_ptr(), n)
+    torch.cuda.synchronize()
+    for c in range(L):
+        for u, v in zip(one.get_cluster(1, c), per.get_cluster(1, c)):
+            np.testing.assert_array_equal(u, v)
+    Q = (C[rng.integers(0, L, 25)] + 0.5 * rng.standard_normal((25, d))).astype(np.float32)
+    for u, v in zip(one.search(1, Q, 10, 4), per.search(1, Q, 10, 4)):
+        np.testing.assert_array_equal(u, v)
+    for e in (one, per):
+        e.start(1, 0)
+        assert e.enqueue_insert_auto(1, np.arange(10 * n, 10 * n + 500, dtype=np.int64),
+                                     (C[rng.integers(0, L, 500) * 0 + 2] + 0.5).astype(np.float32))
+        e.flush()
+        e.stop()
+    for u, v in zip(one.search(1, Q, 10, 4), per.search(1, Q, 10, 4)):
+        np.testing.assert_array_equal(u, v)

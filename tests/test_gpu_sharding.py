@@ -50,6 +50,42 @@ def test_merge_kernel_matches_rule(cuda_ok, oracle_mod, ns, nq, k):
         np.testing.assert_array_equal(a, b)
 
 
+@pytest.mark.parametrize("ns,nq,k", [(2, 50, 10), (3, 7, 3), (4, 9, 64)])
+def test_packed_records_merge_as_separate_arrays(cuda_ok, oracle_mod, ns, nq, k):
+    """One gathered buffer of answer records ([nq, k] scores, padded to 8 bytes,
+    then [nq, k] ids per shard, the layout ShardedSearch all-gathers) merges
+    exactly as the separate arrays do."""
+    import torch
+
+    from m3_memory_b200 import cabi
+
+    rng = np.random.default_rng(ns * 77 + k)
+    sc = np.sort(rng.integers(0, 30, (ns, nq, k)).astype(np.float32) / 4, axis=2)
+    ids = rng.integers(0, 10**12, (ns, nq, k)).astype(np.int64)
+    sc[:, 1, k // 2:] = np.inf
+    ids[:, 1, k // 2:] = -1
+    off = (nq * k * 4 + 7) // 8 * 8
+    R = off + nq * k * 8
+    buf = np.zeros(ns * R, np.uint8)
+    for r in range(ns):
+        buf[r * R:r * R + nq * k * 4] = sc[r].reshape(-1).view(np.uint8)
+        buf[r * R + off:r * R + off + nq * k * 8] = ids[r].reshape(-1).view(np.uint8)
+    e = cabi.Engine()
+    d = torch.from_numpy(buf).cuda()
+    o_ids = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    o_sc = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+    o_cnt = torch.empty((nq,), dtype=torch.int32, device="cuda")
+    e.merge_shards_packed_device(d.data_ptr(), ns, nq, k, R, off, o_ids.data_ptr(),
+                                 o_sc.data_ptr(), o_cnt.data_ptr())
+    torch.cuda.synchronize()
+    want = oracle_mod.merge_shards(sc, ids)
+    for a, b in zip((o_ids.cpu().numpy(), o_sc.cpu().numpy(), o_cnt.cpu().numpy()), want):
+        np.testing.assert_array_equal(a, b)
+    with pytest.raises(ValueError):  # a record too short for its ids
+        e.merge_shards_packed_device(d.data_ptr(), ns, nq, k, off, off, o_ids.data_ptr(),
+                                     o_sc.data_ptr(), o_cnt.data_ptr())
+
+
 def test_two_shards_on_one_gpu_equal_one_engine(cuda_ok):
     import torch
 
