@@ -986,16 +986,26 @@ def run_config4(args, rank, world, local_rank):
         exact = best_i.cpu().numpy()
     del X, glob, row_ids, assign
     torch.cuda.empty_cache()
-    sharded = ShardedSearch(eng, 1, K, B, world, dev, rank=rank, max_nprobe=C4_NPROBE,
+    sweep_p = (C4_NPROBE, 128, 256, 512)
+    sharded = ShardedSearch(eng, 1, K, B, world, dev, rank=rank, max_nprobe=max(sweep_p),
                             split_coarse=world > 1)
-    ids, _, _ = sharded.search(Q[:B], C4_NPROBE)
-    torch.cuda.synchronize()
-    recall = recall_at_k(ids[:1024].cpu().numpy(), exact, K)
+    # recall@10 from nprobe 64 upward until it reaches 0.95 (skewed lists spread a
+    # dense component's neighbours over many lists)
+    sweep = {}
+    for p in sweep_p:
+        ids, _, _ = sharded.search(Q[:B], p)
+        torch.cuda.synchronize()
+        sweep[p] = recall_at_k(ids[:1024].cpu().numpy(), exact, K)
+        if sweep[p] >= 0.95:
+            break
+    nprobe = next((p for p in sweep if sweep[p] >= 0.95), max(sweep, key=sweep.get))
+    recall = sweep[nprobe]
     eng.sync_errors()
+    log(f"[rank {rank}] recall@10 by nprobe {sweep} -> nprobe {nprobe}")
 
     def step(i):
         o = (i % 2) * B
-        sharded.search(Q[o:o + B], C4_NPROBE)
+        sharded.search(Q[o:o + B], nprobe)
 
     for w in range(args.warmup):
         step(w)
@@ -1034,13 +1044,13 @@ def run_config4(args, rank, world, local_rank):
         "data": "synthetic (per shard a seeded Zipf(1.1) mixture of 8192 components, on the GPU)",
         "config": {"workload": ("PROFILING CASE (not the 12.5M-row shard): " if args.c4_n else "")
                                + f"ivf-search: {world} x {n} x {d} fp32 unit-norm, cosine, "
-                               f"nlist {world * nl}, nprobe {C4_NPROBE}, k {K}, batch {B}",
-                   "rows_per_gpu": n, "nlist": world * nl, "nprobe": C4_NPROBE, "k": K,
+                               f"nlist {world * nl}, nprobe {nprobe}, k {K}, batch {B}",
+                   "rows_per_gpu": n, "nlist": world * nl, "nprobe": nprobe, "k": K,
                    "batch": B, "metric": "cosine (normalized)",
                    "scaling_protocol": "weak: one shard (rows, lists, 4096 queries) per GPU; "
                                        "N = 8 is the 100M-row, 65,536-list index",
                    "l2_flush": "not needed: each batch streams the shards (> 126 MB L2)"},
-        "recall_at_10": recall,
+        "recall_at_10": recall, "recall_sweep": {str(p): r for p, r in sweep.items()},
         "stage_ms_rank0": {k: round(v, 4) for k, v in stage.items()},
         "parallelism": f"{world} shard(s), split coarse selection, one all-gather of probes "
                        "and one of top-k records per batch" if world > 1 else "1 GPU",

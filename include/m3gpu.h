@@ -318,12 +318,24 @@ int m3g_search_probes_device(m3g_engine* e, int index_id, const float* d_queries
  * the library (held by every GPU that loads it until the process exits), so
  * nq*nlist + 2*nq + 2*nlist must not exceed 4194304; larger requests return
  * M3G_EUNSUPPORTED.  The first call on a device looks the array up
- * (cudaGetSymbolAddress); make that call before any stream capture.  All calls
- * share the array: calls whose work overlaps on the GPU race.  stream NULL:
- * synchronous; else enqueued on that stream. */
+ * (cudaGetSymbolAddress) and keeps its address for the life of the process;
+ * make that call before any stream capture, and do not reset the device
+ * (cudaDeviceReset) while the library is loaded.  All calls share the array:
+ * calls whose work overlaps on the GPU race.  stream NULL: the work goes to the
+ * legacy default stream and the call waits for it (which also waits for other
+ * blocking streams); callers that must not synchronise pass a non-blocking
+ * stream of their own, on which the call only enqueues. */
 int m3g_select_probes_noalloc(const float* d_queries, int64_t nq, const float* d_centroids,
                               int64_t nlist, int dim, int metric, int normalized, int nprobe,
                               int32_t* d_out_probes, void* stream);
+
+/* Test hook for the device-side failure path: with ns > 0, every tensor-core
+ * list scan first waits up to ns nanoseconds on a barrier that nothing
+ * completes, records the timeout and ends without scanning, so the search
+ * returns M3G_ETIMEOUT (the path a real stalled wait takes: every role leaves,
+ * copies and MMAs in flight are drained, TMEM is freed, the context stays
+ * usable).  0 (the default) turns it off.  No counterpart in the reference. */
+int m3g_set_test_wait_limit(m3g_engine* e, uint64_t ns);
 
 /* Per-stage device time of the most recent search (profiling must be on). */
 typedef struct {
@@ -332,6 +344,8 @@ typedef struct {
     int64_t probed_pairs;   /* (query, list) pairs scanned */
     int32_t kernel_launches;
     int32_t nq, nprobe, k;
+    int64_t graph_launches;          /* searches replayed as a CUDA graph so far */
+    int64_t graph_capture_failures;  /* batch shapes whose capture failed (run directly) */
 } m3g_profile;
 int m3g_set_profiling(m3g_engine* e, int on);
 int m3g_last_profile(m3g_engine* e, m3g_profile* out);

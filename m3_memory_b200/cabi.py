@@ -46,7 +46,8 @@ class Profile(ct.Structure):
                 ("ms_scan", ct.c_float), ("ms_merge", ct.c_float), ("ms_total", ct.c_float),
                 ("scan_bytes", ct.c_int64), ("probed_pairs", ct.c_int64),
                 ("kernel_launches", ct.c_int32), ("nq", ct.c_int32), ("nprobe", ct.c_int32),
-                ("k", ct.c_int32)]
+                ("k", ct.c_int32), ("graph_launches", ct.c_int64),
+                ("graph_capture_failures", ct.c_int64)]
 
 
 SIGNATURES = {
@@ -66,6 +67,7 @@ SIGNATURES = {
     "m3g_load_cluster": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
     "m3g_load_cluster_device": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
     "m3g_set_split_policy": (_i32, [_vp, _f64, _i32]),
+    "m3g_set_test_wait_limit": (_i32, [_vp, _u64]),
     "m3g_load_lists_device": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64]),
     "m3g_merge_shards_packed_device": (_i32, [_vp, _vp, _i32, _i64, _i32, _i64, _i64, _vp, _vp,
                                               _vp, _vp]),
@@ -374,6 +376,9 @@ class Engine:
         check(lib().m3g_train_ivf(self.h, index_id, dim, metric, int(normalized), _p(ids), _p(X),
                                   X.shape[0], nlist, niter, seed, _p(C)))
         return C
+
+    def set_test_wait_limit(self, ns):
+        check(lib().m3g_set_test_wait_limit(self.h, ns))
 
     def set_split_policy(self, mean_factor=0.0, niter=5):
         check(lib().m3g_set_split_policy(self.h, mean_factor, niter))

@@ -139,6 +139,11 @@ int m3g_rebuild_from_faiss(m3g_engine* e, int index_id, const char* path, int no
     return guarded([&] { e->eng.rebuild_from_faiss(index_id, path, normalized != 0, storage); });
 }
 
+int m3g_set_test_wait_limit(m3g_engine* e, uint64_t ns) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] { e->eng.set_test_wait_ns(ns); });
+}
+
 int m3g_create_ivf_ex(m3g_engine* e, int index_id, int dim, int metric, int normalized,
                       const float* centroids, int64_t nlist, int storage) {
     M3G_ENGINE_OR_FAIL(e);

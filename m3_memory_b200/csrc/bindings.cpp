@@ -634,6 +634,8 @@ PYBIND11_MODULE(_m3_async, m) {
             d["nq"] = p.nq;
             d["nprobe"] = p.nprobe;
             d["k"] = p.k;
+            d["graph_launches"] = p.graph_launches;
+            d["graph_capture_failures"] = p.graph_capture_failures;
             return d;
         });
 }

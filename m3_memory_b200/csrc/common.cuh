@@ -97,16 +97,21 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
 // Bounded wait for the phase with the given parity to complete.  Returns false
 // (and records kErrWaitTimeout) when kWaitLimitNs pass, or as soon as another
 // thread of the launch has recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err,
+                                              uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
         if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
         if (*(volatile int*)err != 0) return false;
-        if (global_ns() - t0 > kWaitLimitNs) break;
+        if (global_ns() - t0 > limit_ns) break;
     }
     atomicCAS(err, 0, (int)kErrWaitTimeout);
     return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    return mbar_wait_for(bar, parity, err, kWaitLimitNs);
 }
 
 // ---------------- bulk / tensor copies (TMA), no multicast ----------------

@@ -1629,6 +1629,7 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     a.part_score = w.part_score.p;
     a.part_row = w.part_row.p;
     a.err = w.err.p;
+    a.test_wait_ns = test_wait_ns_;
     const int grid = (int)std::min<int64_t>(num_sms_, std::max<int64_t>(1, nq * P));
     if (ix.maps_valid) {
         if (tc_scan)
@@ -1671,7 +1672,7 @@ std::vector<uintptr_t> Engine::graph_key(const Index& ix, int64_t nq, int k, int
             u(w.lcount.p), u(w.lstart.p), u(w.lcursor.p), u(w.items.p), u(w.n_items.p),
             u(w.item_counter.p), u(w.pair_q.p), u(w.pair_slot.p), u(w.part_score.p),
             u(w.part_row.p), u(w.out_ids.p), u(w.out_scores.p), u(w.out_counts.p), u(w.err.p),
-            (uintptr_t)use_tc_scan(), (uintptr_t)use_tc_gemm()};
+            (uintptr_t)use_tc_scan(), (uintptr_t)use_tc_gemm(), (uintptr_t)test_wait_ns_};
 }
 
 // Replays (capturing first when the key changed) run_search on ws_.Q into
@@ -1680,6 +1681,8 @@ std::vector<uintptr_t> Engine::graph_key(const Index& ix, int64_t nq, int k, int
 bool Engine::run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t st) {
     if (graphs_off_) return false;
     auto key = graph_key(ix, nq, k, P);
+    for (const auto& f : graph_failed_)
+        if (f == key) return false;
     if (!graph_.exec || graph_.key != key) {
         if (graph_.exec) cudaGraphExecDestroy(graph_.exec);
         graph_.exec = nullptr;
@@ -1702,8 +1705,12 @@ bool Engine::run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t 
         if (g) cudaGraphDestroy(g);
         cudaGetLastError();  // a failed capture leaves no error behind
         if (!ok || !graph_.exec) {
+            // this shape runs its kernels directly from now on; other shapes keep
+            // their graphs (the failure is counted in m3g_last_profile)
             graph_.exec = nullptr;
-            graphs_off_ = true;
+            if (graph_failed_.size() >= 64) graph_failed_.erase(graph_failed_.begin());
+            graph_failed_.push_back(std::move(key));
+            ++graph_failures_;
             last_launches_ = launches;
             return false;
         }
@@ -1714,6 +1721,7 @@ bool Engine::run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t 
                           (ix.maps_valid ? 1 : 0) + 1;
     }
     M3G_CK(cudaGraphLaunch(graph_.exec, st));
+    ++graph_launches_;
     return true;
 }
 
@@ -1922,6 +1930,8 @@ void Engine::sync_errors() {
 m3g_profile Engine::last_profile() {
     DeviceGuard g(device_);
     std::lock_guard wl(ws_.mu);
+    prof_.graph_launches = graph_launches_;
+    prof_.graph_capture_failures = graph_failures_;
     if (!prof_pending_) return prof_;
     M3G_CK(cudaEventSynchronize(ws_.done));
     float t[6];

@@ -277,6 +277,7 @@ class Engine {
     }
 
     void set_profiling(bool on) { profiling_ = on; }
+    void set_test_wait_ns(uint64_t ns) { test_wait_ns_ = ns; }
     m3g_profile last_profile();
 
    private:
@@ -327,6 +328,7 @@ class Engine {
 
     Workspace ws_;
     std::atomic<bool> profiling_{false};
+    uint64_t test_wait_ns_ = 0;  // test hook of the tensor-core scan (0: off)
     m3g_profile prof_{};
     bool prof_pending_ = false;
     int64_t prof_row_bytes_ = 0, prof_dim_ = 0;
@@ -340,7 +342,11 @@ class Engine {
         std::vector<uintptr_t> key;
         cudaGraphExec_t exec = nullptr;
     } graph_;
-    bool graphs_off_ = false;  // set when a capture failed, or by M3G_SEARCH_GRAPH=0
+    bool graphs_off_ = false;  // set by M3G_SEARCH_GRAPH=0
+    // keys whose capture failed (those shapes run their kernels directly; others
+    // keep their graphs), and how graphs were used, for m3g_last_profile
+    std::vector<std::vector<uintptr_t>> graph_failed_;
+    int64_t graph_launches_ = 0, graph_failures_ = 0;
     std::vector<uintptr_t> graph_key(const Index& ix, int64_t nq, int k, int P) const;
     bool run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t st);
 };

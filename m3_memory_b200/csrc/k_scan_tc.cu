@@ -211,7 +211,8 @@ __global__ void __launch_bounds__(NTHR, 1)
     uint64_t* accfull = infoempty + NINFO;   // 2
     uint64_t* accempty = accfull + 2;     // 2
     uint64_t* drain = accempty + 2;       // 1
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* never = drain + 1;          // 1: the test hook's barrier, never arrived at
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(never + 1);
     float* sc = reinterpret_cast<float*>(smem + L.sc_off);
     unsigned long long* kbuf = reinterpret_cast<unsigned long long*>(smem + L.kb_off);
     const uint32_t x_u32 = smem_u32(smem + L.x_off);
@@ -241,6 +242,7 @@ __global__ void __launch_bounds__(NTHR, 1)
             mbar_init(&accempty[s], NEPI);
         }
         mbar_init(drain, 1);
+        mbar_init(never, 1);
         fence_mbar_init();
     }
     if (warp == W_PROD && lane == 0) {
@@ -524,7 +526,17 @@ __global__ void __launch_bounds__(NTHR, 1)
         // ------------------------------ scheduler ------------------------------
         const bool leader = elect_one();
         const int nitems = *a.n_items;
-        for (int it = 0;; ++it) {
+        if (a.test_wait_ns) {
+            // a bounded wait that runs out (its barrier never completes): the
+            // timeout is recorded and the scan ends as if it had no items
+            __all_sync(0xffffffffu, mbar_wait_for(never, 0, err, a.test_wait_ns));
+            if (leader) {
+                info[0].list = -1;
+                mbar_arrive(&infofull[0]);
+            }
+            __syncwarp();
+        }
+        for (int it = 0; !a.test_wait_ns; ++it) {
             const int slot = it % NINFO;
             if (it >= NINFO &&
                 !__all_sync(0xffffffffu,

@@ -73,6 +73,9 @@ struct ScanArgs {
     float* part_score;       // [nq, P, k]
     int64_t* part_row;       // [nq, P, k] arena row, -1 for empty
     int* err;
+    // test hook (tensor-core scan): when nonzero, the scheduler first waits this
+    // long on a barrier nothing arrives at, records the timeout and ends the scan
+    uint64_t test_wait_ns;
 };
 
 int scan_kmax();

@@ -60,6 +60,51 @@ def test_noalloc_matches_engine_on_consecutive_calls(cuda_ok, oracle_mod):
         _same_selection(oracle_mod, g, got, want)
 
 
+def _synthetic(nq, L, d, metric, normalized, seed):
+    rng = np.random.default_rng(seed)
+    means = rng.standard_normal((12, d)).astype(np.float32)
+    C = (means[rng.integers(0, 12, L)] + 0.3 * rng.standard_normal((L, d))).astype(np.float32)
+    Q = (means[rng.integers(0, 12, nq)] + 0.3 * rng.standard_normal((nq, d))).astype(np.float32)
+    if normalized:
+        C /= np.linalg.norm(C, axis=1, keepdims=True)
+        Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    return {"Q": Q, "C": C, "metric": metric, "normalized": normalized}
+
+
+def test_noalloc_more_shapes(cuda_ok, oracle_mod):
+    """The large-P selection kernel (P = 200 and P = 1500 > 1024, returned in id
+    order), a call within 1 KB of the fixed scratch's end, a call enqueued on a
+    caller's stream, and the normalised-cosine golden case."""
+    import torch
+
+    from m3_memory_b200 import cabi
+
+    cases = [(_synthetic(24, 2048, 64, 1, False, 1), 200),
+             (_synthetic(12, 2048, 32, 0, False, 2), 1500),
+             (_synthetic(1024, 4085, 16, 1, False, 3), 8),  # needs 4193280 of 4194304 floats
+             (load_golden("cosine_norm"), 6)]
+    for g, nprobe in cases:
+        got = _noalloc_probes(cabi, torch, g, nprobe)
+        want = _engine_probes(cabi, g, nprobe)
+        assert got.shape == want.shape
+        if nprobe > 1024:  # above 1024 the set comes back in id order
+            for q in range(len(got)):
+                np.testing.assert_array_equal(np.sort(got[q]), np.sort(want[q]))
+        else:
+            _same_selection(oracle_mod, g, got, want)
+    # enqueued on a caller's non-blocking stream
+    g = cases[0][0]
+    Q = torch.from_numpy(g["Q"]).cuda()
+    C = torch.from_numpy(g["C"]).cuda()
+    out = torch.full((len(g["Q"]), 32), -7, dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    cabi.select_probes_noalloc(Q.data_ptr(), Q.shape[0], C.data_ptr(), C.shape[0], C.shape[1],
+                               1, False, 32, out.data_ptr(), s.cuda_stream)
+    s.synchronize()
+    _same_selection(oracle_mod, g, out.cpu().numpy(), _engine_probes(cabi, g, 32))
+
+
 def test_noalloc_limits(cuda_ok):
     import torch
 
