@@ -690,7 +690,7 @@ def run_config3(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    n, d, nlist, K3 = args.c3_n or C3_N, C3_DIM, C3_NLIST, args.c3_k or C3_K
+    n, d, nlist, K3 = args.c3_n or C3_N, C3_DIM, args.c3_nlist or C3_NLIST, args.c3_k or C3_K
     storage = cabi.BF16 if args.storage == "bf16" else cabi.F32
     t0 = time.perf_counter()
     X, Qd = device_mixture(n, C3_NQ, d, C3_NCOMP, SIGMA, SEED + 3, dev)
@@ -858,7 +858,7 @@ def run_config3(args, rank, world, local_rank):
         "dtype": "bf16 rows, fp32 queries and accumulation",
         "data": "synthetic (seeded 10k-component Gaussian mixture generated on the GPU)",
         "config": {"workload": ("PROFILING CASE (not the bf16 configuration): "
-                                if (args.c3_n or args.c3_k) else "") +
+                                if (args.c3_n or args.c3_k or args.c3_nlist) else "") +
                                f"ivf-search: {n // 1_000_000}M x {d} {args.storage}-stored "
                                f"mixture({C3_NCOMP}), L2, nlist {nlist}, nprobe {head_p}, "
                                f"k {K3}, batch {B}",
@@ -1216,6 +1216,7 @@ def main():
                     help="config 3: list storage")
     ap.add_argument("--c3-n", type=int, default=None, help="config 3, profiling only: rows")
     ap.add_argument("--c3-k", type=int, default=None, help="config 3, profiling only: k")
+    ap.add_argument("--c3-nlist", type=int, default=None, help="config 3, profiling only: nlist")
     args = ap.parse_args()
     keep_stdout_for_result()
     global N_VEC, NLIST, NPROBE, FIXED_NPROBE, WORKLOAD

@@ -584,36 +584,71 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
     } else {
         // ------------------------------ epilogue ------------------------------
-        const int ew = warp - W_EPI0;         // query group: queries ew, ew+4, ...
+        // Two ways to spread an item over the four epilogue warps:
+        //  * k > 32 and few queries (np <= QPW, "row split"): every warp takes the rows of its own
+        //    TMEM lanes for every query, straight from its tcgen05.ld, and keeps a
+        //    top-k per query over those rows; at the item's end the four lists of a
+        //    query are merged by the warp that owns it (query j: warp j % 4);
+        //  * more queries: warp ew keeps queries ew, ew + 4, ...; each block's scores
+        //    pass through the score tile so that each warp reads all 128 rows.
+        // Every decision that leads to a named barrier is taken by all four warps
+        // together (named_bar_sync_or), so no barrier is ever left half-joined.
+        const int ew = warp - W_EPI0;
         const int quarter = warp & 3;         // TMEM lanes 32*quarter ..
         const int trow = quarter * 32 + lane; // row of the block this thread drains
         const float INF = __int_as_float(0x7f800000);
+        // the row split's list exchange: [warp][query][32 KW] keys over the score tile
+        // and the key buffers (both idle by then), 16 KB
+        unsigned long long* pub = reinterpret_cast<unsigned long long*>(smem + L.sc_off);
+        static_assert(NEPI * QPW * 32 * KW * 8 <= QHALF * TROWS * 4 + QMAX * 32 * 8,
+                      "the row split's list exchange fits the score tile and key buffers");
+        static_assert(NEPI * QPW * 32 <= QMAX * 32, "the row split's key buffers fit");
         uint32_t pseq = 0;
         for (int it = 0;; ++it) {
             const int slot = it % NINFO;
             const bool got = __all_sync(0xffffffffu, mbar_wait(&infofull[slot], (it / NINFO) & 1, err));
-            if (!got) break;
+            if (named_bar_sync_or(EPI_BAR, NEPI * 32, !got)) break;
             const ItemTC* inf = &info[slot];
             if (inf->list < 0) break;
             const Geo g(*inf);
             const int nrows = inf->nrows;
             const int64_t off = inf->off;
-            // rows scoring above a query's bound cannot reach its answer: the bound
-            // is the k-th best score of one of its lists already scanned
+            // (measured: a gain for the 4-level top-k of k > 32, a loss for k <= 32,
+            // whose 32-entry lists are cheap and whose tau tightens faster over all rows)
+            const bool rsplit = KW > 1 && g.np <= QPW;
+            // state j holds query (rsplit ? j : ew + NEPI j); rows scoring above a
+            // query's bound cannot reach its answer (the bound is the k-th best score
+            // of one of its lists already scanned)
             RegTopKW<KW> rt[QPW];
 #pragma unroll
             for (int j = 0; j < QPW; ++j) {
-                const int qi = ew + NEPI * j;
+                const int qi = rsplit ? j : ew + NEPI * j;
                 if (qi < g.np && a.qbound) {
                     const uint32_t bk = ~a.qbound[inf->q[qi]];  // score key (0xffffffff: none)
                     if (bk != 0xffffffffu) rt[j].set_cap(((unsigned long long)bk << 32) | 0xffffffffull);
                 }
             }
             bool ok = true;
-            for (int p0 = 0; p0 < g.nb && ok; p0 += g.bpp) {
+            for (int p0 = 0; p0 < g.nb; p0 += g.bpp) {
                 const int pb = min(g.bpp, g.nb - p0);
                 const int h = (int)(pseq & 1u);
-                if (!__all_sync(0xffffffffu, mbar_wait(&accfull[h], (pseq >> 1) & 1u, err))) {
+                // this thread's rows of the pass: tombstones and norms are loaded before
+                // the accumulators are waited for, so their latency overlaps the MMAs
+                constexpr int MAXB = HALF_COLS / 32;
+                uint32_t livem = 0;
+                float nb2v[MAXB];
+                const bool need_n2 = a.metric == kL2 || (a.metric == kCosine && !a.normalized);
+#pragma unroll
+                for (int b = 0; b < MAXB; ++b) {
+                    nb2v[b] = 0.f;
+                    const int lrow = (p0 + b) * TROWS + trow;
+                    if (b < pb && lrow < nrows) {
+                        if (a.alive[off + lrow] != 0) livem |= 1u << b;
+                        if (need_n2) nb2v[b] = a.rnorm2[off + lrow];
+                    }
+                }
+                const bool acc = __all_sync(0xffffffffu, mbar_wait(&accfull[h], (pseq >> 1) & 1u, err));
+                if (named_bar_sync_or(EPI_BAR, NEPI * 32, !acc)) {
                     ok = false;
                     break;
                 }
@@ -622,15 +657,42 @@ __global__ void __launch_bounds__(NTHR, 1)
                     const int lrow = (p0 + b) * TROWS + trow;  // row in the list
                     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) +
                                            (uint32_t)(h * HALF_COLS + b * 2 * g.nqp);
-                    bool live = lrow < nrows;
+                    const bool live = (livem >> b) & 1u;
                     float nb2 = 0.f;
-                    if (live) {
-                        live = a.alive[off + lrow] != 0;
-                        if (a.metric == kL2 || (a.metric == kCosine && !a.normalized))
-                            nb2 = a.rnorm2[off + lrow];
+#pragma unroll
+                    for (int bb = 0; bb < MAXB; ++bb)
+                        if (bb == b) nb2 = nb2v[bb];
+                    // columns [0, nqp): x q_hi; [nqp, 2 nqp): x q_lo
+                    auto score_of = [&](uint32_t c0, uint32_t c1, int qi) {
+                        const float dot = __uint_as_float(c0) + __uint_as_float(c1);
+                        float s = INF;
+                        if (live) {
+                            if (a.metric == kIP) s = -dot;
+                            else if (a.metric == kL2)  // ranking only; rescored at the merge
+                                s = (nb2 + a.qnorm2[inf->q[qi]]) - 2.f * dot;
+                            else if (a.normalized) s = 1.f - dot;
+                            else {
+                                const float na = a.qnorm2[inf->q[qi]];
+                                s = (na == 0.f || nb2 == 0.f) ? 1.f : 1.f - dot / sqrtf(na * nb2);
+                            }
+                        }
+                        return s;
+                    };
+                    if (rsplit) {
+                        // this warp's 32 rows for every query, no score tile
+                        uint32_t c0[QHALF], c1[QHALF];
+                        tmem_ld16(taddr, c0);
+                        tmem_ld16(taddr + g.nqp, c1);
+                        if ((p0 + b) * TROWS + quarter * 32 < nrows) {  // warp-uniform
+#pragma unroll
+                            for (int j = 0; j < QPW; ++j)
+                                if (j < g.np)
+                                    rt[j].push(kbuf + (ew * QPW + j) * 32, a.k,
+                                               score_of(c0[j], c1[j], j), lrow, lane);
+                        }
+                        continue;
                     }
-                    // columns [0, nqp): x q_hi; [nqp, 2 nqp): x q_lo; 16 queries per
-                    // round: drained to the score tile, then pushed into the top-k
+                    // 16 queries per round: drained to the score tile, then pushed
 #pragma unroll
                     for (int hq = 0; hq < QM / QHALF; ++hq) {
                         const int q0 = hq * QHALF;
@@ -639,24 +701,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                         tmem_ld16(taddr + q0, c0);
                         tmem_ld16(taddr + g.nqp + q0, c1);
 #pragma unroll
-                        for (int i = 0; i < QHALF; ++i) {
-                            if (q0 + i < g.np) {
-                                const float dot = __uint_as_float(c0[i]) + __uint_as_float(c1[i]);
-                                float s = INF;
-                                if (live) {
-                                    if (a.metric == kIP) s = -dot;
-                                    else if (a.metric == kL2)  // ranking only; rescored at the merge
-                                        s = (nb2 + a.qnorm2[inf->q[q0 + i]]) - 2.f * dot;
-                                    else if (a.normalized) s = 1.f - dot;
-                                    else {
-                                        const float na = a.qnorm2[inf->q[q0 + i]];
-                                        s = (na == 0.f || nb2 == 0.f) ? 1.f
-                                                                      : 1.f - dot / sqrtf(na * nb2);
-                                    }
-                                }
-                                sc[i * TROWS + trow] = s;
-                            }
-                        }
+                        for (int i = 0; i < QHALF; ++i)
+                            if (q0 + i < g.np) sc[i * TROWS + trow] = score_of(c0[i], c1[i], q0 + i);
                         named_bar_sync(EPI_BAR, NEPI * 32);
 #pragma unroll
                         for (int jj = 0; jj < QHALF / NEPI; ++jj) {
@@ -680,12 +726,36 @@ __global__ void __launch_bounds__(NTHR, 1)
                 if (lane == 0) mbar_arrive(&accempty[h]);
                 ++pseq;
             }
-            if (!ok) break;
+            if (!ok) break;  // the same in every epilogue warp
+            if (rsplit) {
+                // drain the buffers, publish the lists of the queries other warps
+                // own, and merge the three other lists of each owned query
+#pragma unroll
+                for (int j = 0; j < QPW; ++j)
+                    if (j < g.np && rt[j].nbuf) rt[j].flush(kbuf + (ew * QPW + j) * 32, a.k, lane);
+                named_bar_sync(EPI_BAR, NEPI * 32);
+#pragma unroll
+                for (int j = 0; j < QPW; ++j)
+                    if (j < g.np && (j & (NEPI - 1)) != ew) {
+#pragma unroll
+                        for (int w = 0; w < KW; ++w)
+                            pub[(ew * QPW + j) * 32 * KW + 32 * w + lane] = rt[j].top[w];
+                    }
+                named_bar_sync(EPI_BAR, NEPI * 32);
+#pragma unroll
+                for (int j = 0; j < QPW; ++j)
+                    if (j < g.np && (j & (NEPI - 1)) == ew) {
+#pragma unroll
+                        for (int v = 0; v < NEPI; ++v)
+                            if (v != ew) rt[j].merge_sorted(pub + (v * QPW + j) * 32 * KW, a.k, lane);
+                    }
+            }
             // the item's answers: top-k per (query, probe slot)
 #pragma unroll
             for (int j = 0; j < QPW; ++j) {
-                const int qi = ew + NEPI * j;
-                if (qi < g.np) {
+                const int qi = rsplit ? j : ew + NEPI * j;
+                const bool mine = rsplit ? (j < g.np && (j & (NEPI - 1)) == ew) : qi < g.np;
+                if (mine) {
                     if (rt[j].nbuf) rt[j].flush(kbuf + qi * 32, a.k, lane);
                     // a full top-k bounds the query's final k-th score
                     const unsigned long long kth = rt[j].entry(a.k - 1);
@@ -705,6 +775,8 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
                 }
             }
+            // the exchange area and key buffers are reused by the next item
+            if (rsplit) named_bar_sync(EPI_BAR, NEPI * 32);
             __syncwarp();
             if (lane == 0) mbar_arrive(&infoempty[slot]);
         }

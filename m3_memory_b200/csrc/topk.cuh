@@ -189,6 +189,35 @@ struct RegTopKW {
         if (cand) buf[nbuf + __popc(ball & ((1u << lane) - 1u))] = key;
         nbuf += cnt;
     }
+
+    // Merges another top-k list, given as its ascending 32-key chunks (entry
+    // 32 c + lane of the list at other[32 c + lane]), into this one (its buffer
+    // empty).  Keys are unique, so the result does not depend on which list is
+    // merged into which.
+    __device__ __forceinline__ void merge_sorted(const unsigned long long* other, int k, int lane) {
+#pragma unroll
+        for (int c = 0; c < KW; ++c) {
+            unsigned long long v = other[32 * c + lane];
+            if (__all_sync(0xffffffffu, !(v < tau))) break;  // the rest of that list is worse
+            v = v < tau ? v : ~0ull;
+#pragma unroll
+            for (int w = 0; w < KW; ++w) {
+                const unsigned long long rc = shfl_u64(v, 31 - lane);
+                const unsigned long long lo = top[w] < rc ? top[w] : rc;
+                const unsigned long long hi = top[w] < rc ? rc : top[w];
+                top[w] = warp_bitonic_clean(lo, lane);
+                if (w + 1 < KW) {
+                    if (__all_sync(0xffffffffu, hi == ~0ull)) break;
+                    v = warp_bitonic_clean(hi, lane);
+                }
+            }
+#pragma unroll
+            for (int w = 0; w < KW; ++w)
+                if (32 * w + lane >= k) top[w] = ~0ull;
+            tau = entry(k - 1);
+            tau = tau < cap ? tau : cap;
+        }
+    }
 };
 
 }  // namespace m3g
