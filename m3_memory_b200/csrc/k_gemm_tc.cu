@@ -10,10 +10,12 @@
 // order (3D * 2^-23 of the sum of |terms|).  gemm_tc_error_beta() returns the
 // resulting bound factor, which the exact selection (k_coarse.cu) relies on.
 //
-// Kernel: one CTA per 128 x 256 output tile; warp 0 lane 0 drives TMA (no
-// multicast) through a 4-stage ring of 48 KB stages, warp 1 lane 0 issues
-// tcgen05.mma (M=128, N=256, K=16, bf16 -> fp32 in TMEM, 256 columns), and all
-// four warps drain TMEM with tcgen05.ld in the epilogue.  Every wait is bounded.
+// Kernel: persistent, one CTA per SM walking 128 x 256 output tiles; warp 0
+// lane 0 drives TMA (no multicast) through a 4-stage ring of 48 KB stages
+// across tiles, warp 1 lane 0 issues tcgen05.mma (M=128, N=256, K=16, bf16 ->
+// fp32 in TMEM) into one of two 256-column accumulators, and warps 2-5 drain the
+// other with tcgen05.ld and store it, so a tile's epilogue overlaps the next
+// tile's MMAs.  Every wait is bounded.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -31,8 +33,9 @@ constexpr int TC_STAGES = 4;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;  // 32 KB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
-constexpr int TC_THREADS = 128;
-constexpr uint32_t TC_TMEM_COLS = 256;
+constexpr int TC_EPI0 = 2, TC_EPI_WARPS = 4;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int TC_THREADS = (TC_EPI0 + TC_EPI_WARPS) * 32;
+constexpr uint32_t TC_TMEM_COLS = 2 * TC_BN;  // two accumulators: one fills while one drains
 constexpr size_t TC_SMEM = (size_t)TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
 
 // kind::f16 instruction descriptor: D fp32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1),
@@ -44,17 +47,28 @@ constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(T
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_bf16x3_kernel(const __grid_constant__ CUtensorMap mapA,
                        const __grid_constant__ CUtensorMap mapB, float* __restrict__ S,
-                       int64_t lds, int M, int N, int nk, int* err) {
+                       int64_t lds, int M, int N, int nk, int m_fast, int* err) {
     extern __shared__ unsigned char tc_smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
     uint64_t* empty = full + TC_STAGES;
-    uint64_t* done = empty + TC_STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* accfull = empty + TC_STAGES;  // 2: a tile's accumulator is complete
+    uint64_t* accempty = accfull + 2;       // 2: the epilogue has drained it
+    uint64_t* drain = accempty + 2;         // 1: every MMA issued has completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * TC_BN;
+    const int64_t mt = (M + TC_BM - 1) / TC_BM, nt = (N + TC_BN - 1) / TC_BN;
+    const int64_t ntiles = mt * nt;
+    // tile t -> (row tile, column tile); consecutive tiles share the larger
+    // operand's tile while they walk the smaller operand, which stays in L2
+    auto tile_of = [&](int64_t t, int* m0, int* n0) {
+        const int64_t mi = m_fast ? t % mt : t / nt;
+        const int64_t ni = m_fast ? t / mt : t % nt;
+        *m0 = (int)(mi * TC_BM);
+        *n0 = (int)(ni * TC_BN);
+    };
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -68,7 +82,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(done, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&accfull[s], 1);
+            mbar_init(&accempty[s], TC_EPI_WARPS);
+        }
+        mbar_init(drain, 1);
         fence_mbar_init();
     }
     if (threadIdx.x == 0) {
@@ -80,83 +98,99 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    int issued = 0;  // TMA stages issued (producer lane)
     if (warp == 0 && lane == 0) {
-        // ---- TMA producer
-        bool pok = true;
-        for (int kt = 0; kt < nk; ++kt) {
-            const int s = kt % TC_STAGES;
-            if (kt >= TC_STAGES && !mbar_wait(&empty[s], ((kt / TC_STAGES) - 1) & 1, err)) {
-                pok = false;
-                break;
+        // ---- TMA producer: every k-step of every tile of this CTA through the ring
+        int64_t it = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            int m0, n0;
+            tile_of(t, &m0, &n0);
+            for (int kt = 0; kt < nk; ++kt, ++it) {
+                const int s = (int)(it % TC_STAGES);
+                if (it >= TC_STAGES &&
+                    !mbar_wait(&empty[s], (uint32_t)((it / TC_STAGES) - 1) & 1u, err)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* sa = smem + s * TC_STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[s], TC_STAGE_BYTES);
+                tma_load_2d(sa, &mapA, kt * TC_BK, m0, &full[s]);
+                tma_load_2d(sa + TC_A_BYTES, &mapB, kt * TC_BK, n0, &full[s]);
             }
-            unsigned char* sa = smem + s * TC_STAGE_BYTES;
-            mbar_arrive_expect_tx(&full[s], TC_STAGE_BYTES);
-            tma_load_2d(sa, &mapA, kt * TC_BK, m0, &full[s]);
-            tma_load_2d(sa + TC_A_BYTES, &mapB, kt * TC_BK, n0, &full[s]);
-            issued = kt + 1;
         }
-        if (!pok) {  // error path: let the copies in flight land before leaving
-            for (int kt = issued > TC_STAGES ? issued - TC_STAGES : 0; kt < issued; ++kt)
-                mbar_drain(&full[kt % TC_STAGES], (kt / TC_STAGES) & 1);
-        }
+        // no copy may still be landing when the CTA leaves
+        for (int64_t k = it > TC_STAGES ? it - TC_STAGES : 0; k < it; ++k)
+            mbar_drain(&full[k % TC_STAGES], (uint32_t)(k / TC_STAGES) & 1u);
     } else if (warp == 1 && lane == 0) {
-        // ---- MMA issuer (one thread)
-        for (int kt = 0; kt < nk; ++kt) {
-            const int s = kt % TC_STAGES;
-            if (!mbar_wait(&full[s], (kt / TC_STAGES) & 1, err)) break;
+        // ---- MMA issuer: tile i accumulates in TMEM half i & 1 while the
+        // epilogue drains the other half
+        int64_t it = 0, lt = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++lt) {
+            const int h = (int)(lt & 1);
+            if (lt >= 2 && !mbar_wait(&accempty[h], (uint32_t)((lt >> 1) - 1) & 1u, err)) break;
             tc_fence_after();
-            const uint32_t sa = smem_u32(smem + s * TC_STAGE_BYTES);
-            const uint32_t sb = sa + TC_A_BYTES;
+            const uint32_t d = tmem + (uint32_t)(h * TC_BN);
+            for (int kt = 0; kt < nk; ++kt, ++it) {
+                const int s = (int)(it % TC_STAGES);
+                if (!mbar_wait(&full[s], (uint32_t)(it / TC_STAGES) & 1u, err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * TC_STAGE_BYTES);
+                const uint32_t sb = sa + TC_A_BYTES;
 #pragma unroll
-            for (int k = 0; k < TC_BK / 16; ++k)
-                tc_mma_f16(tmem, sw128_desc(sa + k * 32), sw128_desc(sb + k * 32), TC_IDESC,
-                       (kt | k) != 0);
-            tc_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                for (int k = 0; k < TC_BK / 16; ++k)
+                    tc_mma_f16(d, sw128_desc(sa + k * 32), sw128_desc(sb + k * 32), TC_IDESC,
+                               (kt | k) != 0);
+                tc_commit(&empty[s]);  // frees the stage once these MMAs have read it
+            }
+            if (ok) tc_commit(&accfull[h]);
         }
         // fires once every MMA issued above has completed (also on an error path)
-        tc_commit(done);
-    }
-
-    // ---- epilogue: warp w owns TMEM lanes 32w .. 32w+31 (= output rows)
-    __syncwarp();
-    bool ok = mbar_wait(done, 0, err);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-        tc_fence_after();
-        const int row = m0 + warp * 32 + lane;
-        float* srow = S + (int64_t)row * lds;
+        tc_commit(drain);
+        mbar_drain(drain, 0);
+    } else if (warp >= TC_EPI0) {
+        // ---- epilogue: warp w drains TMEM lanes 32 (w % 4) .. (= the tile's rows)
+        const int quarter = warp & 3;
+        int64_t lt = 0;
+        for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
+            const int h = (int)(lt & 1);
+            if (!__all_sync(0xffffffffu, mbar_wait(&accfull[h], (uint32_t)(lt >> 1) & 1u, err))) break;
+            tc_fence_after();
+            int m0, n0;
+            tile_of(t, &m0, &n0);
+            const int row = m0 + quarter * 32 + lane;
+            float* srow = S + (int64_t)row * lds;
 #pragma unroll 1
-        for (int c0 = 0; c0 < TC_BN; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
-            if (row < M) {
-                const int col = n0 + c0;
-                if (col + 32 <= N && (lds & 3) == 0) {
+            for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * TC_BN + c0), r);
+                if (row < M) {
+                    const int col = n0 + c0;
+                    if (col + 32 <= N && (lds & 3) == 0) {
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4*>(srow + col + j) =
-                            make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                        __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-                } else {
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(srow + col + j) =
+                                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (col + j < N) srow[col + j] = __uint_as_float(r[j]);
+                        for (int j = 0; j < 32; ++j)
+                            if (col + j < N) srow[col + j] = __uint_as_float(r[j]);
+                    }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accempty[h]);
         }
-    } else if (warp == 1 && lane == 0) {
-        // error path: the MMAs that were issued still complete into TMEM; wait
-        // for them (bounded) before TMEM is released below
-        mbar_drain(done, 0);
-    } else if (warp == 0 && lane == 0) {
-        // error path: no TMA copy may still be landing when the CTA leaves
-        for (int kt = issued > TC_STAGES ? issued - TC_STAGES : 0; kt < issued; ++kt)
-            mbar_drain(&full[kt % TC_STAGES], (kt / TC_STAGES) & 1);
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
+        __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(TC_TMEM_COLS)
@@ -214,13 +248,23 @@ cudaError_t launch_split3(const float* X, int64_t ld, int64_t n, int dpad, int k
 cudaError_t launch_gemm_tc(const CUtensorMap& mapA, const CUtensorMap& mapB, float* S, int64_t lds,
                            int M, int N, int kp, int* err, cudaStream_t st) {
     if (M <= 0 || N <= 0) return cudaSuccess;
-    if (kp % TC_BK != 0 || M > 65535 * TC_BM) return cudaErrorInvalidValue;
+    if (kp % TC_BK != 0) return cudaErrorInvalidValue;
+    const int64_t mt = (M + TC_BM - 1) / TC_BM, nt = (N + TC_BN - 1) / TC_BN;
+    // walk the smaller operand fastest: the A rows (M) when the B side is larger
+    const int m_fast = N > M ? 1 : 0;
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess || sms <= 0) sms = 148;
+    }
     cudaError_t e = cudaFuncSetAttribute(gemm_bf16x3_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
     if (e != cudaSuccess) return e;
-    dim3 grid((N + TC_BN - 1) / TC_BN, (M + TC_BM - 1) / TC_BM);
+    const unsigned grid = (unsigned)std::min<int64_t>(mt * nt, sms);
     gemm_bf16x3_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(mapA, mapB, S, lds, M, N, kp / TC_BK,
-                                                          err);
+                                                          m_fast, err);
     return cudaGetLastError();
 }
 
