@@ -767,6 +767,7 @@ Engine::~Engine() {
         cudaStreamDestroy(ws_.stream);
     }
     if (ws_.done) cudaEventDestroy(ws_.done);
+    if (ws_.legacy) cudaEventDestroy(ws_.legacy);
     for (auto& e : ws_.ev)
         if (e) cudaEventDestroy(e);
     ws_.Q.release();
@@ -1787,7 +1788,15 @@ void Engine::acquire_ws(cudaStream_t st, int64_t nq, int64_t L, int64_t P, int64
         for (auto& e : ws_.ev) M3G_CK(cudaEventCreate(&e));
         M3G_CK(cudaEventRecord(ws_.done, ws_.stream));
     }
-    if (!st) st = ws_.stream;
+    if (!st) {
+        // a call without a stream may read device data the caller produced on the
+        // legacy default stream (torch's default stream, for one): the engine's own
+        // stream starts after that work
+        if (!ws_.legacy) M3G_CK(cudaEventCreateWithFlags(&ws_.legacy, cudaEventDisableTiming));
+        M3G_CK(cudaEventRecord(ws_.legacy, cudaStreamLegacy));
+        M3G_CK(cudaStreamWaitEvent(ws_.stream, ws_.legacy, 0));
+        st = ws_.stream;
+    }
     const WsSizes sz{nq, L, P, k, dpad};
     if (ws_needs_grow(ws_, sz)) {
         M3G_CK(cudaEventSynchronize(ws_.done));

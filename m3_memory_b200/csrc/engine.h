@@ -185,6 +185,7 @@ struct Workspace {
     cudaStream_t last_stream = nullptr;  // stream of the last user (ordered by `done`)
     cudaEvent_t done = nullptr;
     cudaEvent_t ev[8] = {};
+    cudaEvent_t legacy = nullptr;  // orders a NULL-stream call after the legacy default stream
     std::mutex mu;
 };
 

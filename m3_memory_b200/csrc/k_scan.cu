@@ -677,6 +677,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_items_kernel(
 __global__ void pair_scatter_kernel(const int32_t* __restrict__ probes, int nq, int P, int L,
                                     const int32_t* __restrict__ skip_len,
                                     const int32_t* __restrict__ lstart,
+                                    const int32_t* __restrict__ lcount,
                                     int32_t* __restrict__ lcursor, int32_t* __restrict__ pair_q,
                                     int32_t* __restrict__ pair_slot) {
     const int64_t n = (int64_t)nq * P;
@@ -684,9 +685,10 @@ __global__ void pair_scatter_kernel(const int32_t* __restrict__ probes, int nq, 
          i += (int64_t)gridDim.x * blockDim.x) {
         const int l = probes[i];
         if (!pair_wanted(l, L, skip_len)) continue;
-        const int pos = lstart[l] + atomicAdd(&lcursor[l], 1);
-        pair_q[pos] = (int32_t)(i / P);
-        pair_slot[pos] = (int32_t)(i % P);
+        const int c = atomicAdd(&lcursor[l], 1);
+        if (c >= lcount[l]) continue;  // never past the list's counted range
+        pair_q[lstart[l] + c] = (int32_t)(i / P);
+        pair_slot[lstart[l] + c] = (int32_t)(i % P);
     }
 }
 
@@ -706,8 +708,8 @@ cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
     plan_items_kernel<<<1, PLAN_THREADS, 0, st>>>(lcount, list_order, L, gmax, lstart, items,
                                                   n_items);
     if (n > 0)
-        pair_scatter_kernel<<<blocks, 256, 0, st>>>(probes, nq, P, L, skip_len, lstart, lcursor,
-                                                    pair_q, pair_slot);
+        pair_scatter_kernel<<<blocks, 256, 0, st>>>(probes, nq, P, L, skip_len, lstart, lcount,
+                                                    lcursor, pair_q, pair_slot);
     return cudaGetLastError();
 }
 

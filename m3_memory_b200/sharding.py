@@ -124,8 +124,12 @@ class ShardedSearch:
         self.out_sc = torch.empty((max_q, k), dtype=torch.float32, device=device)
         self.out_cnt = torch.empty((max_q,), dtype=torch.int32, device=device)
         self.max_q = max_q
+        # every engine call and collective of a search runs on this one stream, so the
+        # engine's kernels and NCCL's writes are ordered with each other; it waits for
+        # the caller's stream on entry and the caller's stream waits for it on exit
+        self.stream = torch.cuda.Stream(device)
         # set to a list to have search() append (phase, CUDA event) pairs, recorded on
-        # the current stream at the end of each phase ("start" first)
+        # the search's stream at the end of each phase ("start" first)
         self.marks = None
 
     def record_bytes(self, nq: int) -> int:
@@ -156,9 +160,19 @@ class ShardedSearch:
 
     def search(self, q, nprobe: int):
         """Top-k over all shards for the device query batch ``q`` ([nq, dim]
-        fp32, nq <= max_q), enqueued on torch's current stream (the collectives
-        are ordered after it).  Returns (ids, scores, counts) views of device
-        buffers that the next call overwrites."""
+        fp32, nq <= max_q), ordered after torch's current stream, which waits for
+        the answer.  Returns (ids, scores, counts) views of device buffers that the
+        next call overwrites."""
+        import torch
+
+        caller = torch.cuda.current_stream(q.device)
+        self.stream.wait_stream(caller)
+        with torch.cuda.stream(self.stream):
+            out = self._search(q, nprobe)
+        caller.wait_stream(self.stream)
+        return out
+
+    def _search(self, q, nprobe: int):
         import torch
         import torch.distributed as dist
 
@@ -166,7 +180,7 @@ class ShardedSearch:
         if nq > self.max_q:
             raise ValueError(f"batch of {nq} queries exceeds max_q={self.max_q}")
         k = self.k
-        s = torch.cuda.current_stream(q.device).cuda_stream
+        s = self.stream.cuda_stream
         self._mark("start")
         a_ids, a_sc = self._answer_views(nq)
         if self.coarse_index_id is not None:
