@@ -88,10 +88,18 @@ def kmeans_sample():
     return np.sort(np.random.default_rng(SEED + 1).choice(N_VEC, m, replace=False))
 
 
-def bench_config(nprobe):
+def weak_mode(args, world):
+    """N > 1 with every GPU bringing its own batch of queries per step (the
+    default), as opposed to one batch split over the GPUs."""
+    return world > 1 and args.scaling == "weak"
+
+
+def bench_config(nprobe, world=1, weak=True):
     """The workload as both arms name it (identical by construction)."""
     return {"workload": WORKLOAD, "n_vectors": N_VEC, "dim": DIM, "nlist": NLIST,
-            "nprobe": nprobe, "k": K, "batch": BATCH, "metric": "inner product",
+            "nprobe": nprobe, "k": K, "batch": BATCH,
+            "global_batch": BATCH * world if weak else BATCH,
+            "metric": "inner product",
             "kmeans": (f"{KMEANS_ITERS} iterations, seeded random init, exact assignment, on a "
                        f"seeded {min(N_VEC, KMEANS_SAMPLE)}-row sample; every row then assigned "
                        "to its nearest centroid"),
@@ -354,8 +362,9 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": "search QPS at recall@10>=0.95 (IVF, dim 1024)",
         "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": bench_config(nprobe),
+        "scaling": "weak" if world == 1 or weak_mode(args, world) else "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": bench_config(nprobe, world, world == 1 or weak_mode(args, world)),
         "recall_at_10": recall,
         "index": {"fingerprint": index_fingerprint(C, assign),
                   "built": "host: BLAS-proposed exact k-means + assignment (setup, untimed)"},
@@ -405,21 +414,35 @@ def run_ours(args, rank, world, local_rank):
     X, Qb = make_data()
     log(f"[rank {rank}] data ready in {time.perf_counter() - t_setup:.1f}s")
     eng = cabi.Engine()
+    if args.tile_rows is not None:
+        eng.set_scan_tile_rows(args.tile_rows)
     C, assign, owner = build_headline_index(eng, X, rank, world)
     log(f"[rank {rank}] index ready after {time.perf_counter() - t_setup:.1f}s")
 
     Qd = torch.from_numpy(Qb).to(dev)  # [NBATCH, BATCH, DIM]
+    weak = weak_mode(args, world)
     coarse = {}
-    if world > 1 and args.coarse == "split":
+    if weak:
+        coarse = dict(rank=rank)
+    elif world > 1 and args.coarse == "split":
         coarse = dict(split_coarse=True, rank=rank)
-    if world > 1 and args.coarse == "sharded":
+    elif world > 1 and args.coarse == "sharded":
         # each rank scores only the centroids of the lists it owns
         eng.create_ivf(2, DIM, METRIC_IP, False, C[np.flatnonzero(owner == rank)])
         coarse = dict(coarse_index_id=2, owner=owner, rank=rank)
     sharded = ShardedSearch(eng, 1, K, BATCH, world, dev, **coarse)
+    # queries answered per step by the whole job
+    per_step = BATCH * world if weak else BATCH
 
-    def step(b, nprobe):
-        ids, sc, _ = sharded.search(Qd[b], nprobe)
+    def own_batch(i):
+        """The batch rank brings at step i (weak scaling: a different one per rank)."""
+        return (i * world + rank) % NBATCH if weak else i % NBATCH
+
+    def step(i, nprobe):
+        if weak:
+            ids, sc, _ = sharded.search_own_batch(Qd[own_batch(i)], nprobe)
+        else:
+            ids, sc, _ = sharded.search(Qd[i % NBATCH], nprobe)
         return ids, sc
 
     # ---- recall@10 against exact search (untimed); pick nprobe
@@ -450,13 +473,13 @@ def run_ours(args, rank, world, local_rank):
     # every batch's answer at the chosen nprobe (untimed), for the parity check
     # against the reference core on the same index
     all_answers = [[], [], []]
-    for b in range(NBATCH):
+    for b in range(NBATCH if world == 1 else 0):
         for lst, t in zip(all_answers, sharded.search(Qd[b], nprobe)):
             lst.append(t.cpu().numpy())
 
     # ---- device-resident timing
     for w in range(args.warmup):
-        step(w % NBATCH, nprobe)
+        step(w, nprobe)
     torch.cuda.synchronize()
     eng.sync_errors()
     if world > 1:
@@ -467,7 +490,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.nvtx.range_push("timed")  # lets ncu --nvtx-include "timed/" select this loop
         ev0.record()
         for i in range(args.steps):
-            step(i % NBATCH, nprobe)
+            step(i, nprobe)
         ev1.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
@@ -478,7 +501,7 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    qps = BATCH * args.steps / (ms / 1e3)
+    qps = per_step * args.steps / (ms / 1e3)
     clocks = clk.summary()
 
     # ---- end to end through the C ABI with host buffers (H2D + D2H inside)
@@ -554,20 +577,23 @@ def run_ours(args, rank, world, local_rank):
     else:
         qdev = torch.empty((BATCH, DIM), dtype=torch.float32, device=dev)
 
-        def e2e_step(b):
-            qdev.copy_(pinned[b], non_blocking=True)
-            m_ids, m_sc, m_cnt = sharded.search(qdev, nprobe)
+        def e2e_step(i):
+            qdev.copy_(pinned[own_batch(i)], non_blocking=True)
+            if weak:
+                m_ids, m_sc, m_cnt = sharded.search_own_batch(qdev, nprobe)
+            else:
+                m_ids, m_sc, m_cnt = sharded.search(qdev, nprobe)
             h_ids.copy_(m_ids, non_blocking=True)
             h_sc.copy_(m_sc, non_blocking=True)
             h_cnt.copy_(m_cnt, non_blocking=True)
             torch.cuda.synchronize()
 
         for w in range(args.warmup):
-            e2e_step(w % NBATCH)
+            e2e_step(w)
         dist.barrier()
         t0 = time.perf_counter()
         for i in range(args.steps):
-            e2e_step(i % NBATCH)
+            e2e_step(i)
         e2e_s = time.perf_counter() - t0
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -577,7 +603,7 @@ def run_ours(args, rank, world, local_rank):
         marks_per_step = []
         for i in range(min(args.steps, 50)):
             sharded.marks = []
-            step(i % NBATCH, nprobe)
+            step(i, nprobe)
             marks_per_step.append(sharded.marks)
         sharded.marks = None
         torch.cuda.synchronize()
@@ -585,7 +611,7 @@ def run_ours(args, rank, world, local_rank):
             for (_, ea), (name, eb) in zip(m, m[1:]):
                 stage_ms.setdefault("ms_" + name, []).append(ea.elapsed_time(eb))
             stage_ms.setdefault("ms_total", []).append(m[0][1].elapsed_time(m[-1][1]))
-    e2e_qps = BATCH * args.steps / e2e_s
+    e2e_qps = per_step * args.steps / e2e_s
     e2e_sync_qps = BATCH * args.steps / e2e_sync_s if world == 1 else None
 
     if rank != 0:
@@ -593,11 +619,14 @@ def run_ours(args, rank, world, local_rank):
     # our kernels per step: norms, split, coarse GEMM, select, 3 work-list, scan, merge;
     # N > 1 adds the shard merge; the query-split coarse step a second row-norm pass and
     # the partial-list clear; the sharded coarse step also the pair scores and the
-    # top-P merge
+    # top-P merge; the own-batch (weak) step: norms, split, coarse GEMM, select for the
+    # rank's batch, then norms, 3 work-list, partial clear, scan, merge for all batches,
+    # and the shard merge
     # (the profiled calls add the engine's probed-byte counter, one launch per step, which
     # the timed loop does not run)
     per_step_launches = (launches / args.steps - 1) if launches else (
-        9 if world == 1 else {"replicated": 10, "split": 12, "sharded": 14}[args.coarse])
+        9 if world == 1 else 12 if weak else
+        {"replicated": 10, "split": 12, "sharded": 14}[args.coarse])
     peak, peak_kind = peaks()
     roofline = None
     if scan_ms:
@@ -628,14 +657,20 @@ def run_ours(args, rank, world, local_rank):
         "metric": "search QPS at recall@10>=0.95 (IVF, dim 1024)",
         "value": qps, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong" if world > 1 and not weak else "weak", "vs_baseline": None,
+        "dtype": "f32",
         "data": "synthetic (seeded Gaussian mixture; no dataset)",
-        "config": bench_config(nprobe),
+        "config": bench_config(nprobe, world, world == 1 or weak),
         "recall_at_10": recall,
         "recall_sweep": {str(k): v for k, v in sweep.items()},
         "stage_ms_mean": {k[3:]: round(statistics.mean(v), 4) for k, v in stage_ms.items()},
-        "parallelism": (f"lists sharded over {world} GPU(s), {args.coarse} coarse "
-                        "selection") if world > 1 else "1 GPU",
+        "parallelism": ("1 GPU" if world == 1 else
+                        f"lists sharded over {world} GPUs; every GPU brings its own batch of "
+                        f"{BATCH} queries per step (batches all-gathered, probes of each batch "
+                        "selected on its GPU and all-gathered, per-shard top-k returned to the "
+                        "batch's GPU by one all-to-all)" if weak else
+                        f"lists sharded over {world} GPUs, one batch per step, {args.coarse} "
+                        "coarse selection"),
         "index": {"fingerprint": index_fingerprint(C, assign),
                   "built": "GPU: m3g_kmeans on the sample + m3g_nearest_clusters (setup, untimed)"},
         "parity": parity,
@@ -648,6 +683,11 @@ def run_ours(args, rank, world, local_rank):
                 "path": "pinned host queries -> H2D + m3g_search_device + D2H of the answer, two "
                         "steps in flight on alternating streams (sync_call_value: one blocking "
                         "m3g_search per step)" if world == 1
+                else "per GPU: H2D of its own batch + NCCL all-gather of the batches + "
+                     "m3g_select_probes_device (own batch) + NCCL all-gather of the probes + "
+                     "m3g_search_probes_device (all batches, own lists) + NCCL all-to-all of "
+                     "the packed top-k records + m3g_merge_shards_packed_device + D2H of its "
+                     "batch's answer; bytes per GPU" if weak
                 else ("H2D + m3g_search_device + NCCL all-gather + m3g_merge_shards_device + D2H"
                       if args.coarse == "replicated" else
                       "H2D + m3g_select_probes_device (this rank's query slice) + NCCL all-gather "
@@ -737,6 +777,8 @@ def run_config3(args, rank, world, local_rank):
     X, Qd = device_mixture(n, C3_NQ, d, C3_NCOMP, SIGMA, SEED + 3, dev)
     log(f"[rank {rank}] {n} x {d} generated on the GPU in {time.perf_counter() - t0:.1f}s")
     eng = cabi.Engine()
+    if args.tile_rows is not None:
+        eng.set_scan_tile_rows(args.tile_rows)
     g = torch.Generator(device=dev)
     g.manual_seed(SEED + 4)
     m = min(n, nlist * C3_SAMPLE_PER_LIST)
@@ -970,6 +1012,8 @@ def run_config4(args, rank, world, local_rank):
     means = [device_zipf_means(nl, d, SEED + 200 + r, dev) for r in range(world)]
     X = device_zipf_rows(means[rank], n, C4_ZIPF, SIGMA, SEED + 300 + rank, dev)
     eng = cabi.Engine()
+    if args.tile_rows is not None:
+        eng.set_scan_tile_rows(args.tile_rows)
     g = torch.Generator(device=dev)
     g.manual_seed(SEED + 400 + rank)
     sample = torch.randperm(n, generator=g, device=dev)[:min(n, nl * 64)].sort().values
@@ -1030,15 +1074,26 @@ def run_config4(args, rank, world, local_rank):
     del X, glob, row_ids, assign
     torch.cuda.empty_cache()
     sweep_p = (C4_NPROBE, 128, 256, 512)
-    sharded = ShardedSearch(eng, 1, K, B, world, dev, rank=rank, max_nprobe=max(sweep_p),
-                            split_coarse=world > 1)
+    own = C4_BATCH_PER_GPU  # every rank brings its own batch per step
+    sharded = ShardedSearch(eng, 1, K, own, world, dev, rank=rank, max_nprobe=max(sweep_p))
+
+    def own_search(i, p):
+        o = (i % 2) * B + rank * own
+        return sharded.search_own_batch(Q[o:o + own], p)
+
     # recall@10 from nprobe 64 upward until it reaches 0.95 (skewed lists spread a
-    # dense component's neighbours over many lists)
+    # dense component's neighbours over many lists); rank 0's first batch holds the
+    # queries with exact answers
     sweep = {}
     for p in sweep_p:
-        ids, _, _ = sharded.search(Q[:B], p)
+        ids, _, _ = own_search(0, p)
         torch.cuda.synchronize()
-        sweep[p] = recall_at_k(ids[:1024].cpu().numpy(), exact, K)
+        r = recall_at_k(ids[:1024].cpu().numpy(), exact, K) if rank == 0 else 0.0
+        if world > 1:
+            t = torch.tensor([r], device=dev)
+            dist.broadcast(t, 0)
+            r = float(t.item())
+        sweep[p] = r
         if sweep[p] >= 0.95:
             break
     nprobe = next((p for p in sweep if sweep[p] >= 0.95), max(sweep, key=sweep.get))
@@ -1047,8 +1102,7 @@ def run_config4(args, rank, world, local_rank):
     log(f"[rank {rank}] recall@10 by nprobe {sweep} -> nprobe {nprobe}")
 
     def step(i):
-        o = (i % 2) * B
-        sharded.search(Q[o:o + B], nprobe)
+        own_search(i, nprobe)
 
     for w in range(args.warmup):
         step(w)
@@ -1077,6 +1131,37 @@ def run_config4(args, rank, world, local_rank):
     stage = {name: ea_eb for name, ea_eb in
              ((nm, ea.elapsed_time(eb)) for (_, ea), (nm, eb) in zip(m, m[1:]))}
     sharded.marks = None
+    # one GPU: the engine's stage events and probed bytes over the same batches (the
+    # blocking device call, outside the timed loop)
+    eng_stage, roofline = {}, None
+    if world == 1:
+        ids_d = torch.empty((own, K), dtype=torch.int64, device=dev)
+        sc_d = torch.empty((own, K), dtype=torch.float32, device=dev)
+        cnt_d = torch.empty((own,), dtype=torch.int32, device=dev)
+        eng.set_profiling(True)
+        scan_ms, scan_bytes, streamed = [], [], []
+        for i in range(4):
+            o = (i % 2) * B
+            eng.search_device(1, Q[o:o + own].data_ptr(), own, K, nprobe, ids_d.data_ptr(),
+                              sc_d.data_ptr(), cnt_d.data_ptr())
+            p = eng.last_profile()
+            for key in ("ms_prep", "ms_coarse_gemm", "ms_select", "ms_worklist", "ms_scan",
+                        "ms_merge", "ms_total"):
+                eng_stage.setdefault(key[3:], []).append(p[key])
+            scan_ms.append(p["ms_scan"])
+            scan_bytes.append(p["scan_bytes"])
+            streamed.append(p["streamed_bytes"])
+        eng.set_profiling(False)
+        eng_stage = {k: round(statistics.mean(v), 4) for k, v in eng_stage.items()}
+        peak, peak_kind = peaks()
+        achieved = statistics.mean(scan_bytes) / (statistics.mean(scan_ms) / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "traffic": None, "kernel": scan_kernel_name(),
+                    "bytes_per_launch": statistics.mean(scan_bytes),
+                    "streamed_bytes_per_launch": statistics.mean(streamed),
+                    "streamed_gbs": statistics.mean(streamed) / (statistics.mean(scan_ms) / 1e3) / 1e9,
+                    "ms_per_launch": statistics.mean(scan_ms),
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
     if rank != 0:
         return
     qps = B * args.steps / (ms / 1e3)
@@ -1097,10 +1182,13 @@ def run_config4(args, rank, world, local_rank):
                    "l2_flush": "not needed: each batch streams the shards (> 126 MB L2)"},
         "recall_at_10": recall, "recall_sweep": {str(p): r for p, r in sweep.items()},
         "stage_ms_rank0": {k: round(v, 4) for k, v in stage.items()},
-        "parallelism": f"{world} shard(s), split coarse selection, one all-gather of probes "
-                       "and one of top-k records per batch" if world > 1 else "1 GPU",
+        "stage_ms_engine": eng_stage or None,
+        "parallelism": f"{world} shards; every GPU brings its own {own} queries per step: "
+                       "batches all-gathered, probes selected per batch on its GPU and "
+                       "all-gathered, per-shard top-k returned by one all-to-all"
+                       if world > 1 else "1 GPU",
         "clocks": clk.summary(), "gpu_launches": None,
-        "e2e": None, "roofline": None, "cpu_baseline": None,
+        "e2e": None, "roofline": roofline, "cpu_baseline": None,
     })
 
 
@@ -1134,6 +1222,8 @@ def run_config5(args, rank, world, local_rank):
     Xi, _ = S.gaussian_mixture(n_ins, shifted, SIGMA, np.random.default_rng(SEED + 6))
     Qs, _ = S.gaussian_mixture(BATCH * NBATCH, shifted, SIGMA, np.random.default_rng(SEED + 7))
     eng = cabi.Engine()
+    if args.tile_rows is not None:
+        eng.set_scan_tile_rows(args.tile_rows)
     build_headline_index(eng, X)
     eng.start(2, 0)
     # searches alternate between the original and the shifted distribution
@@ -1242,6 +1332,10 @@ def main():
                     help="N > 1: coarse selection of each rank's slice of the queries over all "
                          "centroids, probes all-gathered (split); per rank over its own "
                          "centroids (sharded); or of every query on every rank (replicated)")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="N > 1: every GPU brings its own batch of queries per step, the lists "
+                         "sharded over the GPUs (weak); or one batch per step split over the "
+                         "GPUs (strong)")
     ap.add_argument("--nvec", type=int, default=None,
                     help="profiling only: fewer vectors (the headline line uses 1M)")
     ap.add_argument("--nlist", type=int, default=None, help="profiling only: fewer lists")
@@ -1258,6 +1352,9 @@ def main():
     ap.add_argument("--c3-n", type=int, default=None, help="config 3, profiling only: rows")
     ap.add_argument("--c3-k", type=int, default=None, help="config 3, profiling only: k")
     ap.add_argument("--c3-nlist", type=int, default=None, help="config 3, profiling only: nlist")
+    ap.add_argument("--tile-rows", type=int, default=None,
+                    help="row tiles of long lists in the scan: rows per tile (multiple of 128), "
+                         "0 automatic (the default), -1 none")
     args = ap.parse_args()
     keep_stdout_for_result()
     global N_VEC, NLIST, NPROBE, FIXED_NPROBE, WORKLOAD

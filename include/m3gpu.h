@@ -337,6 +337,14 @@ int m3g_select_probes_noalloc(const float* d_queries, int64_t nq, const float* d
  * usable).  0 (the default) turns it off.  No counterpart in the reference. */
 int m3g_set_test_wait_limit(m3g_engine* e, uint64_t ns);
 
+/* Row tiles of the list scan (tensor-core path): a list longer than `rows` rows
+ * is scanned as tiles of `rows` rows, spread over the SMs, each with its own
+ * partial top-k, merged per (query, probe) by the last tile to finish.  rows: a
+ * positive multiple of 128; 0 (the default) sizes tiles to about 4 MB of rows;
+ * -1 scans every list whole.  Answers do not depend on it.  No counterpart in
+ * the reference (its list loop is serial, m3_index.cpp:426-442). */
+int m3g_set_scan_tile_rows(m3g_engine* e, int rows);
+
 /* Per-stage device time of the most recent search (profiling must be on). */
 typedef struct {
     float ms_prep, ms_coarse_gemm, ms_select, ms_worklist, ms_scan, ms_merge, ms_total;
@@ -346,6 +354,9 @@ typedef struct {
     int32_t nq, nprobe, k;
     int64_t graph_launches;          /* searches replayed as a CUDA graph so far */
     int64_t graph_capture_failures;  /* batch shapes whose capture failed (run directly) */
+    int64_t streamed_bytes;  /* rows * row bytes the scan's items stream: a list probed by more
+                                queries than one item takes is streamed once per item (the
+                                repeats are often served by L2) */
 } m3g_profile;
 int m3g_set_profiling(m3g_engine* e, int on);
 int m3g_last_profile(m3g_engine* e, m3g_profile* out);

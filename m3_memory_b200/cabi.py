@@ -47,7 +47,7 @@ class Profile(ct.Structure):
                 ("scan_bytes", ct.c_int64), ("probed_pairs", ct.c_int64),
                 ("kernel_launches", ct.c_int32), ("nq", ct.c_int32), ("nprobe", ct.c_int32),
                 ("k", ct.c_int32), ("graph_launches", ct.c_int64),
-                ("graph_capture_failures", ct.c_int64)]
+                ("graph_capture_failures", ct.c_int64), ("streamed_bytes", ct.c_int64)]
 
 
 SIGNATURES = {
@@ -68,6 +68,7 @@ SIGNATURES = {
     "m3g_load_cluster_device": (_i32, [_vp, _i32, _i32, _vp, _vp, _i64, _i32]),
     "m3g_set_split_policy": (_i32, [_vp, _f64, _i32]),
     "m3g_set_test_wait_limit": (_i32, [_vp, _u64]),
+    "m3g_set_scan_tile_rows": (_i32, [_vp, _i32]),
     "m3g_load_lists_device": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64]),
     "m3g_merge_shards_packed_device": (_i32, [_vp, _vp, _i32, _i64, _i32, _i64, _i64, _vp, _vp,
                                               _vp, _vp]),
@@ -379,6 +380,9 @@ class Engine:
 
     def set_test_wait_limit(self, ns):
         check(lib().m3g_set_test_wait_limit(self.h, ns))
+
+    def set_scan_tile_rows(self, rows):
+        check(lib().m3g_set_scan_tile_rows(self.h, rows))
 
     def set_split_policy(self, mean_factor=0.0, niter=5):
         check(lib().m3g_set_split_policy(self.h, mean_factor, niter))

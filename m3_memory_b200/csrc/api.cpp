@@ -144,6 +144,15 @@ int m3g_set_test_wait_limit(m3g_engine* e, uint64_t ns) {
     return guarded([&] { e->eng.set_test_wait_ns(ns); });
 }
 
+int m3g_set_scan_tile_rows(m3g_engine* e, int rows) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (rows < -1 || (rows > 0 && rows % 128))
+            m3g::fail(M3G_EINVAL, "set_scan_tile_rows: rows must be -1, 0 or a positive multiple of 128");
+        e->eng.set_scan_tile_rows(rows);
+    });
+}
+
 int m3g_create_ivf_ex(m3g_engine* e, int index_id, int dim, int metric, int normalized,
                       const float* centroids, int64_t nlist, int storage) {
     M3G_ENGINE_OR_FAIL(e);

@@ -636,6 +636,7 @@ PYBIND11_MODULE(_m3_async, m) {
             d["k"] = p.k;
             d["graph_launches"] = p.graph_launches;
             d["graph_capture_failures"] = p.graph_capture_failures;
+            d["streamed_bytes"] = p.streamed_bytes;
             return d;
         });
 }

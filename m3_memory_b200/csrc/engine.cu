@@ -1550,6 +1550,12 @@ constexpr int64_t kMaxChunkQueries = 8192;
 constexpr int64_t kMaxScoreEntries = int64_t(1) << 26;  // nq * L per chunk
 constexpr int64_t kMaxPartEntries = int64_t(1) << 25;   // nq * P * k per chunk
 constexpr int64_t kMaxAssignRows = int64_t(1) << 22;    // GEMM grid.y stays < 65536
+// Partial lists of the row-tile region (tensor-core scan): as many as the
+// (query, probe) pairs of a chunk, and at least kMinTilePartials.
+constexpr int64_t kMinTilePartials = 16384;
+int64_t tile_partials(int64_t nq, int64_t P) { return std::max(nq * P, kMinTilePartials); }
+// Row tile of a long list when none is set: about this many bytes of rows.
+constexpr int64_t kAutoTileBytes = int64_t(4) << 20;
 
 float gamma_of(int D) { return (float)(D + 4) * 5.9604645e-8f * 1.01f; }
 }  // namespace
@@ -1557,6 +1563,13 @@ float gamma_of(int D) { return (float)(D + 4) * 5.9604645e-8f * 1.01f; }
 // Runs one query chunk whose queries (rows of dQ, stride ldq >= dpad, zero padded)
 // are on the device.  fixed_probes: if non-null, [nq, P] probe lists already on
 // the device (skips the coarse step).  Outputs [nq, k] / [nq] on the device.
+int Engine::scan_tile_rows(const Index& ix) const {
+    if (scan_tile_rows_ < 0) return 0;
+    if (scan_tile_rows_ > 0) return scan_tile_rows_;
+    const int64_t rows = kAutoTileBytes / std::max<int64_t>(1, ix.row_bytes());
+    return (int)std::min<int64_t>(std::max<int64_t>(128, rows & ~int64_t(127)), int64_t(1) << 20);
+}
+
 void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int k, int P,
                         const int32_t* fixed_probes, int64_t* d_ids, float* d_scores,
                         int32_t* d_counts, cudaStream_t st, bool profile, bool clear_partials) {
@@ -1596,12 +1609,19 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     if (gmax <= 0) fail(M3G_EUNSUPPORTED, "search: dimension too large for the list scan");
     // with cleared partial lists, pairs probing empty lists (on a shard: the lists
     // other ranks own) are not queued
+    // long lists are scanned in row tiles (tensor-core scan), so that their rows
+    // spread over the SMs
+    const int tile_rows = tc_scan ? scan_tile_rows(ix) : 0;
+    const int64_t tcap = tile_partials(nq, P);
     M3G_CK(launch_build_worklist(probes, (int)nq, P, L, ix.d_list_order.p, gmax, w.lcount.p,
                                  w.lstart.p, w.lcursor.p, w.items.p, w.n_items.p, w.pair_q.p,
-                                 w.pair_slot.p, st, clear_partials ? ix.d_list_len.p : nullptr));
+                                 w.pair_slot.p, st, clear_partials ? ix.d_list_len.p : nullptr,
+                                 ix.d_list_len.p, tile_rows, (int)std::min<int64_t>(tcap, INT32_MAX)));
+    if (tile_rows > 0) M3G_CK(cudaMemsetAsync(w.tile_cnt.p, 0, sizeof(int32_t) * (size_t)tcap, st));
     if (profile) {
-        M3G_CK(cudaMemsetAsync(w.stats.p, 0, 2 * sizeof(unsigned long long), st));
-        M3G_CK(launch_probed_rows(w.lcount.p, ix.d_list_len.p, L, w.stats.p, w.stats.p + 1, st));
+        M3G_CK(cudaMemsetAsync(w.stats.p, 0, 3 * sizeof(unsigned long long), st));
+        M3G_CK(launch_probed_rows(w.lcount.p, ix.d_list_len.p, L, gmax, w.stats.p, w.stats.p + 1,
+                                  w.stats.p + 2, st));
         M3G_CK(cudaEventRecord(ev[4], st));
     }
     // the item counter and the per-query score bounds of the tensor-core scan
@@ -1631,6 +1651,8 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     a.part_row = w.part_row.p;
     a.err = w.err.p;
     a.test_wait_ns = test_wait_ns_;
+    a.tile_base = nq * P;
+    a.tile_cnt = w.tile_cnt.p;
     const int grid = (int)std::min<int64_t>(num_sms_, std::max<int64_t>(1, nq * P));
     if (ix.maps_valid) {
         if (tc_scan)
@@ -1653,9 +1675,10 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
                              d_counts, st, rescore ? &rs : nullptr));
     if (profile) M3G_CK(cudaEventRecord(ev[6], st));
     // kernels launched: norms, coarse (gemm + select, or iota), 3 work-list
-    // kernels, scan, merge (+ the byte counter when profiling)
+    // kernels, scan, merge (+ the exact rescoring for L2, + the byte counter when
+    // profiling)
     int launches = 1 + (fixed_probes ? 0 : (P >= L ? 1 : (use_tc_gemm() ? 3 : 2))) + 3 +
-                   (ix.maps_valid ? 1 : 0) + 1;
+                   (ix.maps_valid ? 1 : 0) + 1 + (rescore ? 1 : 0);
     if (profile) launches += 1;
     last_launches_ += launches;
 }
@@ -1673,7 +1696,8 @@ std::vector<uintptr_t> Engine::graph_key(const Index& ix, int64_t nq, int k, int
             u(w.lcount.p), u(w.lstart.p), u(w.lcursor.p), u(w.items.p), u(w.n_items.p),
             u(w.item_counter.p), u(w.pair_q.p), u(w.pair_slot.p), u(w.part_score.p),
             u(w.part_row.p), u(w.out_ids.p), u(w.out_scores.p), u(w.out_counts.p), u(w.err.p),
-            (uintptr_t)use_tc_scan(), (uintptr_t)use_tc_gemm(), (uintptr_t)test_wait_ns_};
+            (uintptr_t)use_tc_scan(), (uintptr_t)use_tc_gemm(), (uintptr_t)test_wait_ns_,
+            (uintptr_t)(intptr_t)scan_tile_rows(ix), u(w.tile_cnt.p)};
 }
 
 // Replays (capturing first when the key changed) run_search on ws_.Q into
@@ -1735,11 +1759,12 @@ bool short_of(const DBuf<T>& b, int64_t n) {
     return (size_t)n > b.n;
 }
 bool ws_needs_grow(const Workspace& w, const WsSizes& s) {
+    const int64_t np = s.nq * s.P, nt = tile_partials(s.nq, s.P);
     return !w.err.p || short_of(w.Q, s.nq * s.dpad) || short_of(w.qn, s.nq) ||
-           short_of(w.S, s.nq * s.L) || short_of(w.probes, s.nq * s.P) || short_of(w.lcount, s.L) ||
-           short_of(w.lstart, s.L) || short_of(w.lcursor, s.L) || short_of(w.pair_q, s.nq * s.P) ||
-           short_of(w.pair_slot, s.nq * s.P) || short_of(w.items, s.nq * s.P) ||
-           short_of(w.part_score, s.nq * s.P * s.k) || short_of(w.part_row, s.nq * s.P * s.k) ||
+           short_of(w.S, s.nq * s.L) || short_of(w.probes, np) || short_of(w.lcount, s.L) ||
+           short_of(w.lstart, s.L) || short_of(w.lcursor, s.L) || short_of(w.pair_q, np) ||
+           short_of(w.pair_slot, np) || short_of(w.items, np + nt) || short_of(w.tile_cnt, nt) ||
+           short_of(w.part_score, (np + nt) * s.k) || short_of(w.part_row, (np + nt) * s.k) ||
            short_of(w.out_ids, s.nq * s.k) || short_of(w.out_scores, s.nq * s.k) ||
            short_of(w.out_counts, s.nq) || short_of(w.Q3, s.nq * gemm_tc_kdim((int)s.dpad)) ||
            short_of(w.item_counter, 1 + s.nq);
@@ -1749,7 +1774,7 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
         w.err.alloc(1);
         M3G_CK(cudaMemset(w.err.p, 0, sizeof(int)));
         if (!w.err_host) M3G_CK(cudaMallocHost(&w.err_host, sizeof(int)));
-        w.stats.alloc(2);
+        w.stats.alloc(3);
         w.n_items.alloc(1);
     }
     w.item_counter.ensure((size_t)(1 + s.nq));
@@ -1763,9 +1788,11 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
     w.lcursor.ensure((size_t)s.L);
     w.pair_q.ensure((size_t)(s.nq * s.P));
     w.pair_slot.ensure((size_t)(s.nq * s.P));
-    w.items.ensure((size_t)(s.nq * s.P));
-    w.part_score.ensure((size_t)(s.nq * s.P * s.k));
-    w.part_row.ensure((size_t)(s.nq * s.P * s.k));
+    const int64_t nt = tile_partials(s.nq, s.P);
+    w.items.ensure((size_t)(s.nq * s.P + nt));
+    w.tile_cnt.ensure((size_t)nt);
+    w.part_score.ensure((size_t)((s.nq * s.P + nt) * s.k));
+    w.part_row.ensure((size_t)((s.nq * s.P + nt) * s.k));
     w.out_ids.ensure((size_t)(s.nq * s.k));
     w.out_scores.ensure((size_t)(s.nq * s.k));
     w.out_counts.ensure((size_t)s.nq);
@@ -1952,12 +1979,13 @@ m3g_profile Engine::last_profile() {
     prof_.ms_scan = t[4];
     prof_.ms_merge = t[5];
     M3G_CK(cudaEventElapsedTime(&prof_.ms_total, ws_.ev[0], ws_.ev[6]));
-    unsigned long long st[2];
+    unsigned long long st[3];
     M3G_CK(cudaMemcpy(st, ws_.stats.p, sizeof(st), cudaMemcpyDeviceToHost));
     // algorithmic bytes: every probed list read once, the queries, the results
     prof_.scan_bytes = (int64_t)st[0] * prof_row_bytes_ + (int64_t)prof_.nq * prof_dim_ * 4 +
                        (int64_t)prof_.nq * prof_.k * 12;
     prof_.probed_pairs = (int64_t)st[1];
+    prof_.streamed_bytes = (int64_t)st[2] * prof_row_bytes_;
     prof_pending_ = false;
     return prof_;
 }

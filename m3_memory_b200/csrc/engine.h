@@ -172,6 +172,7 @@ struct Workspace {
     DBuf<float> Q, qn, qn2, S;
     DBuf<__nv_bfloat16> Q3;  // split query operand [hi | hi | lo]
     DBuf<int32_t> probes, lcount, lstart, lcursor, n_items, item_counter, pair_q, pair_slot;
+    DBuf<int32_t> tile_cnt;  // finished row tiles per tiled pair (tensor-core scan)
     DBuf<ScanItem> items;
     DBuf<float> part_score;
     DBuf<int64_t> part_row;
@@ -279,6 +280,10 @@ class Engine {
 
     void set_profiling(bool on) { profiling_ = on; }
     void set_test_wait_ns(uint64_t ns) { test_wait_ns_ = ns; }
+    // Row tiles of long lists in the tensor-core scan: rows per tile (a positive
+    // multiple of 128), 0 for the automatic size, -1 for none.
+    void set_scan_tile_rows(int rows) { scan_tile_rows_ = rows; }
+    int scan_tile_rows(const Index& ix) const;
     m3g_profile last_profile();
 
    private:
@@ -330,6 +335,7 @@ class Engine {
     Workspace ws_;
     std::atomic<bool> profiling_{false};
     uint64_t test_wait_ns_ = 0;  // test hook of the tensor-core scan (0: off)
+    int scan_tile_rows_ = 0;     // set_scan_tile_rows
     m3g_profile prof_{};
     bool prof_pending_ = false;
     int64_t prof_row_bytes_ = 0, prof_dim_ = 0;

@@ -170,7 +170,7 @@ constexpr int SEL_LARGE_NT = 256, SEL_LARGE_CAP = 1024;
 constexpr int SEL_SMALL_P = 128;     // largest P for the small block
 constexpr int SEL_KEYS_SMEM = 8192;  // upper-bound keys cached in shared memory up to this L
 constexpr int SEL_SORT_MAX = 1024;   // largest P whose selection is returned sorted
-constexpr int SEL_OVERLAP_MAX = 256; // above this many candidates, all are rescored
+constexpr int SEL_OVERLAP_MAX = 128; // above this many candidates the overlap test sorts
 constexpr int SEL_STAGE = kExactTileFloats;  // per-warp product tile of the exact rescoring
 constexpr int SEL_FAST_P = 128;      // largest P that takes the pre-filtered threshold path
 constexpr int SEL_KEEP_LO_L = 8192;  // largest L whose lower-bound keys stay beside S0
@@ -533,17 +533,65 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         // other candidate's is ordered, against all others (their exact scores
         // included), by its lower bound; the rest are rescored in the reference's
         // exact arithmetic.  Keys: (score key, id), all distinct.
-        const bool all_exact = cnt > (unsigned)SEL_OVERLAP_MAX;
-        for (int i = threadIdx.x; i < (int)cnt; i += NT) {
-            const uint2 bi = ik[i];
-            bool need = all_exact || bi.x <= kKeyNegInf || bi.y >= kKeyPosInf;
-            for (int j = 0; j < (int)cnt && !need; ++j) {
-                const uint2 bj = ik[j];
-                if (j != i && bj.x <= bi.y && bi.x <= bj.y) need = true;
+        if (cnt <= (unsigned)SEL_OVERLAP_MAX) {
+            // few candidates: every pair of intervals compared
+            for (int i = threadIdx.x; i < (int)cnt; i += NT) {
+                const uint2 bi = ik[i];
+                bool need = bi.x <= kKeyNegInf || bi.y >= kKeyPosInf;
+                for (int j = 0; j < (int)cnt && !need; ++j) {
+                    const uint2 bj = ik[j];
+                    if (j != i && bj.x <= bi.y && bi.x <= bj.y) need = true;
+                }
+                needf[i] = need ? 1 : 0;
             }
+        } else {
+            // many: in the order of the lower bounds (ties by position), a candidate
+            // overlaps an earlier one iff the largest earlier upper bound reaches
+            // its lower bound, and a later one iff the next lower bound is within
+            // its upper bound.  Sort keys and the running maximum use the tile
+            // area (free until the rescoring below).
+            unsigned long long* srt = reinterpret_cast<unsigned long long*>(stage_all);  // CAP
+            uint32_t* hmax = reinterpret_cast<uint32_t*>(srt + CAP);                     // CAP
+            int n2 = 1;
+            while (n2 < (int)cnt) n2 <<= 1;
+            for (int i = threadIdx.x; i < n2; i += NT)
+                srt[i] = i < (int)cnt ? (((unsigned long long)ik[i].x << 32) | (unsigned)i) : ~0ull;
+            __syncthreads();
+            bitonic_sort_u64<NT>(srt, n2);
+            for (int p = threadIdx.x; p < (int)cnt; p += NT)
+                hmax[p] = ik[(uint32_t)(srt[p] & 0xffffffffu)].y;
+            __syncthreads();
+            // inclusive running maximum of the upper bounds (Hillis-Steele)
+            constexpr int PER = CAP / NT;
+            for (int d = 1; d < (int)cnt; d <<= 1) {
+                uint32_t v[PER];
+#pragma unroll
+                for (int u = 0; u < PER; ++u) {
+                    const int p = threadIdx.x + u * NT;
+                    v[u] = 0;
+                    if (p < (int)cnt) v[u] = p >= d ? max(hmax[p], hmax[p - d]) : hmax[p];
+                }
+                __syncthreads();
+#pragma unroll
+                for (int u = 0; u < PER; ++u) {
+                    const int p = threadIdx.x + u * NT;
+                    if (p < (int)cnt) hmax[p] = v[u];
+                }
+                __syncthreads();
+            }
+            for (int p = threadIdx.x; p < (int)cnt; p += NT) {
+                const int i = (int)(srt[p] & 0xffffffffu);
+                const uint2 bi = ik[i];
+                bool need = bi.x <= kKeyNegInf || bi.y >= kKeyPosInf;
+                if (p > 0 && hmax[p - 1] >= bi.x) need = true;
+                if (p + 1 < (int)cnt && (uint32_t)(srt[p + 1] >> 32) <= bi.y) need = true;
+                needf[i] = need ? 1 : 0;
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < (int)cnt; i += NT) {
             const unsigned c = (unsigned)cand[i];
-            needf[i] = need ? 1 : 0;
-            cand[i] = need ? (unsigned long long)c : ((unsigned long long)bi.x << 32) | c;
+            cand[i] = needf[i] ? (unsigned long long)c : ((unsigned long long)ik[i].x << 32) | c;
         }
         __syncthreads();
         // compact the candidates to rescore (exl reuses the interval array)

@@ -174,24 +174,33 @@ __global__ void broadcast_row_kernel(const int32_t* __restrict__ row, int width,
         out[i] = row[i % width];
 }
 
-// Sum of the lengths of the lists a batch probes (for the scan's byte count).
+// Sum of the lengths of the lists a batch probes (for the scan's byte count),
+// the pairs, and the rows the scan's items stream (each list once per group of
+// up to gmax of its queries).
 __global__ void probed_rows_kernel(const int32_t* __restrict__ lcount,
-                                   const int32_t* __restrict__ list_len, int L,
+                                   const int32_t* __restrict__ list_len, int L, int gmax,
                                    unsigned long long* __restrict__ out_rows,
-                                   unsigned long long* __restrict__ out_pairs) {
-    unsigned long long rows = 0, pairs = 0;
+                                   unsigned long long* __restrict__ out_pairs,
+                                   unsigned long long* __restrict__ out_streamed) {
+    unsigned long long rows = 0, pairs = 0, streamed = 0;
     for (int l = blockIdx.x * blockDim.x + threadIdx.x; l < L; l += gridDim.x * blockDim.x) {
-        if (lcount[l] > 0) rows += (unsigned long long)list_len[l];
-        pairs += (unsigned long long)lcount[l];
+        const int c = lcount[l];
+        if (c > 0) {
+            rows += (unsigned long long)list_len[l];
+            streamed += (unsigned long long)list_len[l] * (unsigned long long)((c + gmax - 1) / gmax);
+        }
+        pairs += (unsigned long long)c;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         rows += __shfl_xor_sync(0xffffffffu, rows, o);
         pairs += __shfl_xor_sync(0xffffffffu, pairs, o);
+        streamed += __shfl_xor_sync(0xffffffffu, streamed, o);
     }
     if ((threadIdx.x & 31) == 0) {
         atomicAdd(out_rows, rows);
         atomicAdd(out_pairs, pairs);
+        atomicAdd(out_streamed, streamed);
     }
 }
 
@@ -460,10 +469,11 @@ cudaError_t launch_broadcast_row(const int32_t* row, int width, int64_t nrows, i
     return cudaGetLastError();
 }
 
-cudaError_t launch_probed_rows(const int32_t* lcount, const int32_t* list_len, int L,
+cudaError_t launch_probed_rows(const int32_t* lcount, const int32_t* list_len, int L, int gmax,
                                unsigned long long* out_rows, unsigned long long* out_pairs,
-                               cudaStream_t st) {
-    probed_rows_kernel<<<grid_for(L, 256), 256, 0, st>>>(lcount, list_len, L, out_rows, out_pairs);
+                               unsigned long long* out_streamed, cudaStream_t st) {
+    probed_rows_kernel<<<grid_for(L, 256), 256, 0, st>>>(lcount, list_len, L, gmax, out_rows,
+                                                         out_pairs, out_streamed);
     return cudaGetLastError();
 }
 

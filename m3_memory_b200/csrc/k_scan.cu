@@ -593,82 +593,150 @@ __device__ __forceinline__ int items_of(int c, int gmax) { return (c + gmax - 1)
 constexpr int PLAN_CACHE = 8;  // lists per thread kept in registers (L <= 8192)
 
 // Inclusive block-wide sum of one value per thread (PLAN_THREADS threads).
-__device__ __forceinline__ int32_t plan_block_scan(int32_t v, int32_t* wsum) {
+template <class T>
+__device__ __forceinline__ T plan_block_scan(T v, T* wsum) {
     const int t = threadIdx.x, lane = t & 31, w = t >> 5;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const int32_t u = __shfl_up_sync(0xffffffffu, v, o);
+        const T u = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += u;
     }
     if (lane == 31) wsum[w] = v;
     __syncthreads();
     if (w == 0) {
-        int32_t s = lane < PLAN_THREADS / 32 ? wsum[lane] : 0;
+        T s = lane < PLAN_THREADS / 32 ? wsum[lane] : T(0);
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int32_t u = __shfl_up_sync(0xffffffffu, s, o);
+            const T u = __shfl_up_sync(0xffffffffu, s, o);
             if (lane >= o) s += u;
         }
         if (lane < PLAN_THREADS / 32) wsum[lane] = s;
     }
     __syncthreads();
-    return v + (w > 0 ? wsum[w - 1] : 0);
+    return v + (w > 0 ? wsum[w - 1] : T(0));
+}
+
+// Lists probed by more query groups than this are not tiled: their groups
+// already spread them over the SMs, and run side by side sharing its rows in L2.
+constexpr int TILE_MAX_GROUPS = 2;
+
+// Row tiles a list of len rows with c pairs asks for (1: not tiled).
+__device__ __forceinline__ int tiles_of(int c, int len, int tile_rows, int gmax) {
+    return (tile_rows > 0 && c > 0 && len > tile_rows && items_of(c, gmax) <= TILE_MAX_GROUPS)
+               ? (len + tile_rows - 1) / tile_rows
+               : 1;
+}
+
+// Tile partial lists a tiled list takes (c pairs x nt tiles); 0 when it is not
+// tiled or could never fit the region alone.
+__device__ __forceinline__ int64_t tile_cost(int c, int nt, int tile_cap) {
+    const int64_t n = (int64_t)c * nt;
+    return nt > 1 && n <= (int64_t)tile_cap ? n : 0;
 }
 
 // One block: walks the clusters in list_order, assigns each its pair range and
-// its items (the pairs split into ceil(c / gmax) near-equal groups).  Each
+// its items (the pairs split into ceil(c / gmax) near-equal query groups; a
+// tiled list repeats each group once per row tile).  A list is tiled when its
+// tile partial lists fit the tile region after those of the lists before it in
+// list_order that could fit on their own.  Each
 // thread takes a run of consecutive positions of list_order; up to PLAN_CACHE
 // per thread their loads are issued together and kept in registers.
 __global__ void __launch_bounds__(PLAN_THREADS) plan_items_kernel(
     const int32_t* __restrict__ lcount, const int32_t* __restrict__ order, int L, int gmax,
+    const int32_t* __restrict__ list_len, int tile_rows, int tile_cap,
     int32_t* __restrict__ lstart, ScanItem* __restrict__ items, int32_t* __restrict__ n_items) {
     __shared__ int32_t wp[PLAN_THREADS / 32], wi[PLAN_THREADS / 32];
+    __shared__ int64_t wt[PLAN_THREADS / 32];
     const int t = threadIdx.x;
     const int per = (L + PLAN_THREADS - 1) / PLAN_THREADS;
     const int b = t * per, e = min(L, b + per);
     const bool cached = per <= PLAN_CACHE;
-    int32_t lo[PLAN_CACHE], lc[PLAN_CACHE];
+    const bool tiled = tile_rows > 0 && list_len;
+    int32_t lo[PLAN_CACHE], lc[PLAN_CACHE], ln[PLAN_CACHE];
     int32_t np = 0, ni = 0;
+    int64_t tc = 0;
     if (cached) {
 #pragma unroll
         for (int j = 0; j < PLAN_CACHE; ++j) lo[j] = b + j < e ? order[b + j] : 0;
 #pragma unroll
-        for (int j = 0; j < PLAN_CACHE; ++j) lc[j] = b + j < e ? lcount[lo[j]] : 0;
+        for (int j = 0; j < PLAN_CACHE; ++j) {
+            lc[j] = b + j < e ? lcount[lo[j]] : 0;
+            ln[j] = b + j < e && tiled ? list_len[lo[j]] : 0;
+        }
 #pragma unroll
         for (int j = 0; j < PLAN_CACHE; ++j) {
             np += lc[j];
-            ni += items_of(lc[j], gmax);  // 0 for c = 0
+            tc += tile_cost(lc[j], tiles_of(lc[j], ln[j], tile_rows, gmax), tile_cap);
         }
     } else {
         for (int i = b; i < e; ++i) {
-            const int c = lcount[order[i]];
+            const int l = order[i];
+            const int c = lcount[l];
             np += c;
-            ni += items_of(c, gmax);
+            if (tiled) tc += tile_cost(c, tiles_of(c, list_len[l], tile_rows, gmax), tile_cap);
         }
     }
-    const int32_t pinc = plan_block_scan(np, wp);
-    const int32_t iinc = plan_block_scan(ni, wi);
+    const int32_t pinc = plan_block_scan<int32_t>(np, wp);
+    const int64_t tinc = plan_block_scan<int64_t>(tc, wt);
+    // the lists of this thread that are tiled: their cost ends inside the region
+    int64_t trun = tinc - tc;
+    auto tiles_taken = [&](int c, int len) -> int {
+        const int nt = tiled ? tiles_of(c, len, tile_rows, gmax) : 1;
+        const int64_t cost = tile_cost(c, nt, tile_cap);
+        trun += cost;
+        return (cost > 0 && trun <= (int64_t)tile_cap) ? nt : 1;
+    };
+    int32_t ntk[PLAN_CACHE];
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < PLAN_CACHE; ++j) {
+            ntk[j] = tiles_taken(lc[j], ln[j]);
+            ni += items_of(lc[j], gmax) * ntk[j];  // 0 for c = 0
+        }
+    } else {
+        for (int i = b; i < e; ++i) {
+            const int l = order[i];
+            const int c = lcount[l];
+            ni += items_of(c, gmax) * tiles_taken(c, tiled ? list_len[l] : 0);
+        }
+    }
+    const int32_t iinc = plan_block_scan<int32_t>(ni, wi);
     int32_t pbase = pinc - np, ibase = iinc - ni;
-    auto place = [&](int l, int c) {
+    int64_t tbase = tinc - tc;  // tile partial index of the next tiled list
+    auto place = [&](int l, int c, int len, int nt) {
         lstart[l] = pbase;
         const int n = items_of(c, gmax);
+        const int64_t cost = tiled ? tile_cost(c, tiles_of(c, len, tile_rows, gmax), tile_cap) : 0;
+        // tile-major: the query groups of one tile are neighbours in the work list,
+        // so they run at the same time and share the tile's rows in L2
         int pb = pbase;
         for (int j = 0; j < n; ++j) {
             const int sz = c / n + (j < c % n ? 1 : 0);
-            items[ibase + j] = ScanItem{l, pb, sz, 0};
+            if (nt > 1) {
+                for (int r = 0; r < nt; ++r)
+                    items[ibase + r * n + j] =
+                        ScanItem{l, pb, sz, r * tile_rows, min(tile_rows, len - r * tile_rows),
+                                 (int32_t)(tbase + (int64_t)(pb - pbase) * nt), r, nt};
+            } else {
+                items[ibase + j] = ScanItem{l, pb, sz, 0, -1, -1, 0, 0};
+            }
             pb += sz;
         }
         pbase += c;
-        ibase += n;
+        ibase += n * nt;
+        tbase += cost;
     };
     if (cached) {
 #pragma unroll
         for (int j = 0; j < PLAN_CACHE; ++j)
-            if (b + j < e) place(lo[j], lc[j]);
+            if (b + j < e) place(lo[j], lc[j], ln[j], ntk[j]);
     } else {
+        trun = tinc - tc;
         for (int i = b; i < e; ++i) {
             const int l = order[i];
-            place(l, lcount[l]);
+            const int c = lcount[l];
+            const int len = tiled ? list_len[l] : 0;
+            place(l, c, len, tiles_taken(c, len));
         }
     }
     if (t == PLAN_THREADS - 1) *n_items = iinc;
@@ -698,15 +766,18 @@ cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
                                   const int32_t* list_order, int gmax, int32_t* lcount,
                                   int32_t* lstart, int32_t* lcursor, ScanItem* items,
                                   int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
-                                  cudaStream_t st, const int32_t* skip_len) {
+                                  cudaStream_t st, const int32_t* skip_len,
+                                  const int32_t* list_len, int tile_rows, int tile_cap) {
+    if (tile_rows < 0 || tile_rows % 128 || tile_cap < 0 || (tile_rows > 0 && !list_len))
+        return cudaErrorInvalidValue;
     cudaError_t e;
     if ((e = cudaMemsetAsync(lcount, 0, sizeof(int32_t) * (size_t)L, st)) != cudaSuccess) return e;
     if ((e = cudaMemsetAsync(lcursor, 0, sizeof(int32_t) * (size_t)L, st)) != cudaSuccess) return e;
     const int64_t n = (int64_t)nq * P;
     const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
     if (n > 0) probe_hist_kernel<<<blocks, 256, 0, st>>>(probes, n, L, skip_len, lcount);
-    plan_items_kernel<<<1, PLAN_THREADS, 0, st>>>(lcount, list_order, L, gmax, lstart, items,
-                                                  n_items);
+    plan_items_kernel<<<1, PLAN_THREADS, 0, st>>>(lcount, list_order, L, gmax, list_len,
+                                                  tile_rows, tile_cap, lstart, items, n_items);
     if (n > 0)
         pair_scatter_kernel<<<blocks, 256, 0, st>>>(probes, nq, P, L, skip_len, lstart, lcount,
                                                     lcursor, pair_q, pair_slot);
@@ -780,17 +851,15 @@ __device__ uint32_t radix_select32(F key_of, int64_t n, unsigned rank, unsigned*
 // null, the ids themselves.
 // Exact rescoring (MergeRescore) takes at most this many winners per query.
 constexpr int RS_MAX = 128;
-static_assert(RS_MAX * 33 * 4 <= MCAP * 8, "the staging tile fits in the candidate array");
 
+// With rescore, the winners leave as arena rows (out_ids) in estimate order for
+// rescore_l2_kernel, which writes the final ids and scores.
 __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
     const float* __restrict__ part_score, const int64_t* __restrict__ part_row,
     const int64_t* __restrict__ row_ids, int P, int k, int64_t stride_q, int64_t stride_slot,
     int64_t rstride_q, int64_t rstride_slot, int64_t* __restrict__ out_ids,
-    float* __restrict__ out_scores, int32_t* __restrict__ out_counts, MergeRescore rs,
-    int rescore) {
+    float* __restrict__ out_scores, int32_t* __restrict__ out_counts, int rescore) {
     __shared__ unsigned long long cand[MCAP];
-    __shared__ unsigned long long won[RS_MAX];
-    __shared__ float exact[RS_MAX];
     __shared__ unsigned hist[256];
     __shared__ unsigned shv[4];
     __shared__ unsigned s_tau, s_cnt, s_valid;
@@ -881,92 +950,148 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
         bitonic_u64(cand, n2);
     }
     if (rescore) {
-        // The winners' exact scores (kk <= RS_MAX; thread j sums winner j's row in
-        // index order), then a sort by (exact score, rank by the estimate).  Rows
-        // are staged 32 dims at a time through shared memory (the candidate array,
-        // free once the winners are copied): coalesced 16-byte loads, rows padded
-        // to 33 words so the per-thread reads hit distinct banks.
-        const int j = threadIdx.x;
-        if (j < kk) won[j] = cand[j];
-        __syncthreads();
-        float* tile = reinterpret_cast<float*>(cand);  // [RS_MAX][33]
-        __shared__ float qt[32];
-        __shared__ int64_t wrow[RS_MAX];
-        if (j < kk) wrow[j] = pr[rat((int64_t)(won[j] & 0xffffffffu))];
-        const float* qr = rs.Q + (int64_t)q * rs.ldq;
-        float e = 0.f;
-        for (int d0 = 0; d0 < rs.dim; d0 += 32) {
-            __syncthreads();
-            if (j < 32) qt[j] = d0 + j < rs.dim ? qr[d0 + j] : 0.f;
-            if (rs.bf16_rows) {
-                // 4 x 16 B (8 bf16) per row and chunk
-                for (int t = j; t < kk * 4; t += MRG_BLOCK) {
-                    const int r = t >> 2, c = t & 3;
-                    const __nv_bfloat16* src =
-                        reinterpret_cast<const __nv_bfloat16*>(rs.rows) + wrow[r] * rs.row_ld + d0 + 8 * c;
-                    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                    if (d0 + 8 * c + 8 <= rs.row_ld) {
-                        const uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
-                        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                        for (int h = 0; h < 4; ++h) {
-                            v[2 * h] = __uint_as_float(w[h] << 16);
-                            v[2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
-                        }
-                    }
-#pragma unroll
-                    for (int h = 0; h < 8; ++h) tile[r * 33 + 8 * c + h] = v[h];
-                }
-            } else {
-                // 8 x 16 B (4 fp32) per row and chunk
-                for (int t = j; t < kk * 8; t += MRG_BLOCK) {
-                    const int r = t >> 3, c = t & 7;
-                    const float* src = reinterpret_cast<const float*>(rs.rows) + wrow[r] * rs.row_ld + d0 + 4 * c;
-                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (d0 + 4 * c + 4 <= rs.row_ld) v = __ldg(reinterpret_cast<const float4*>(src));
-                    tile[r * 33 + 4 * c] = v.x;
-                    tile[r * 33 + 4 * c + 1] = v.y;
-                    tile[r * 33 + 4 * c + 2] = v.z;
-                    tile[r * 33 + 4 * c + 3] = v.w;
-                }
-            }
-            __syncthreads();
-            if (j < kk) {
-                const int n = min(32, rs.dim - d0);  // padding dims are never summed
-                for (int i = 0; i < n; ++i) {
-                    const float df = __fsub_rn(qt[i], tile[j * 33 + i]);
-                    e = __fadd_rn(e, __fmul_rn(df, df));
-                }
-            }
+        // hand the winners to rescore_l2_kernel: their arena rows in estimate order
+        // (ties: the merge order), the count in out_counts
+        for (int j = threadIdx.x; j < k; j += MRG_BLOCK) {
+            out_ids[(int64_t)q * k + j] =
+                j < kk ? pr[rat((int64_t)(cand[j] & 0xffffffffu))] : (int64_t)-1;
+            out_scores[(int64_t)q * k + j] = j < kk ? key_float((uint32_t)(cand[j] >> 32)) : INF;
         }
-        if (j < kk) exact[j] = e;
-        __syncthreads();
-        int n2 = 1;
-        while (n2 < kk) n2 <<= 1;
-        if (j < n2) cand[j] = j < kk ? (((unsigned long long)float_key(e) << 32) | (uint32_t)j) : ~0ull;
-        __syncthreads();
-        bitonic_u64(cand, n2);
+        if (threadIdx.x == 0) out_counts[q] = kk;
+        return;
     }
     for (int j = threadIdx.x; j < k; j += MRG_BLOCK) {
         int64_t id = -1;
         float s = INF;
         if (j < kk) {
-            const unsigned long long c = cand[j];
-            if (rescore) {
-                const uint32_t w = (uint32_t)(c & 0xffffffffu);
-                s = exact[w];
-                id = row_ids[pr[rat((int64_t)(won[w] & 0xffffffffu))]];
-            } else {
-                const int64_t i = (int64_t)(c & 0xffffffffu);
-                s = ps[at(i)];
-                const int64_t r = pr[rat(i)];
-                id = row_ids ? row_ids[r] : r;
-            }
+            const int64_t i = (int64_t)(cand[j] & 0xffffffffu);
+            s = ps[at(i)];
+            const int64_t r = pr[rat(i)];
+            id = row_ids ? row_ids[r] : r;
         }
         out_ids[(int64_t)q * k + j] = id;
         out_scores[(int64_t)q * k + j] = s;
     }
     if (threadIdx.x == 0) out_counts[q] = kk;
+}
+}  // namespace
+
+namespace {
+// Exact squared L2 of the winners, in the reference's arithmetic: the sum over
+// i = 0 .. dim-1 of (q_i - x_i)^2 in index order, each step rounded to fp32
+// (Cluster::search_into's distance, AgentMemory/M3/src/cluster.cpp:229-274).
+// One block per query, one thread per winner: the thread streams its row from
+// HBM in 16-byte loads, 128 bytes per batch with the next batch in flight while
+// it sums the current one, against the query staged in shared memory; then the
+// winners are sorted by (exact score, estimate rank).
+constexpr int RS_QCH = 2048;  // query dims staged per round
+
+__device__ __forceinline__ void unpack16(const uint4& u, float* v, bool bf) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    if (bf) {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            v[2 * h] = __uint_as_float(w[h] << 16);
+            v[2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+        }
+    } else {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) v[h] = __uint_as_float(w[h]);
+    }
+}
+
+// Continues e over dims [0, n) of one staged query chunk; src points at the row's
+// first dim of the chunk (16-byte aligned), ng16 = 16-byte groups readable there.
+template <bool BF>
+__device__ __forceinline__ float l2_chunk(const uint4* __restrict__ src, int ng16,
+                                          const float* qs, int n, float e) {
+    constexpr int EPG = BF ? 8 : 4;  // elements per 16-byte group
+    constexpr int U = 8;             // groups per batch (128 bytes)
+    const int G = (n + EPG - 1) / EPG;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    uint4 cur[U], nxt[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) cur[u] = u < G && u < ng16 ? __ldg(src + u) : z;
+    for (int g0 = 0; g0 < G; g0 += U) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int g = g0 + U + u;
+            nxt[u] = g < G && g < ng16 ? __ldg(src + g) : z;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float v[8];
+            unpack16(cur[u], v, BF);
+#pragma unroll
+            for (int h = 0; h < EPG; ++h) {
+                const int i = (g0 + u) * EPG + h;
+                if (i < n) {
+                    const float df = __fsub_rn(qs[i], v[h]);
+                    e = __fadd_rn(e, __fmul_rn(df, df));
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+    }
+    return e;
+}
+
+template <bool BF>
+__global__ void __launch_bounds__(RS_MAX) rescore_l2_kernel(MergeRescore rs,
+                                                           const int64_t* __restrict__ row_ids,
+                                                           int k, int64_t* __restrict__ out_ids,
+                                                           float* __restrict__ out_scores,
+                                                           const int32_t* __restrict__ out_counts) {
+    __shared__ float qs[RS_QCH];
+    __shared__ unsigned long long key[RS_MAX];
+    __shared__ int64_t wrow[RS_MAX];
+    const int q = blockIdx.x, j = threadIdx.x;
+    const int kk = min(out_counts[q], k);
+    const int64_t row = j < kk ? out_ids[(int64_t)q * k + j] : -1;
+    wrow[j] = row;
+    const float* qr = rs.Q + (int64_t)q * rs.ldq;
+    const size_t esz = BF ? 2 : 4;
+    const unsigned char* base = static_cast<const unsigned char*>(rs.rows);
+    float e = 0.f;
+    for (int d0 = 0; d0 < rs.dim; d0 += RS_QCH) {
+        const int n = min(RS_QCH, rs.dim - d0);
+        __syncthreads();
+        for (int i = j; i < n; i += RS_MAX) qs[i] = qr[d0 + i];
+        __syncthreads();
+        if (row >= 0) {
+            const uint4* src = reinterpret_cast<const uint4*>(base + ((size_t)row * rs.row_ld + d0) * esz);
+            const int ng16 = (int)(((rs.row_ld - d0) * (int64_t)esz) / 16);
+            e = l2_chunk<BF>(src, ng16, qs, n, e);
+        }
+    }
+    key[j] = j < kk ? (((unsigned long long)float_key(e) << 32) | (uint32_t)j) : ~0ull;
+    __syncthreads();
+    // bitonic sort of the RS_MAX keys, one per thread
+    for (int s2 = 2; s2 <= RS_MAX; s2 <<= 1)
+        for (int h = s2 >> 1; h > 0; h >>= 1) {
+            const int p = j ^ h;
+            unsigned long long a = key[j], b = key[p];
+            __syncthreads();
+            if (p > j) {
+                if ((a > b) == ((j & s2) == 0)) {
+                    key[j] = b;
+                    key[p] = a;
+                }
+            }
+            __syncthreads();
+        }
+    if (j < k) {
+        int64_t id = -1;
+        float sc = __int_as_float(0x7f800000);
+        if (j < kk) {
+            const unsigned long long c = key[j];
+            sc = key_float((uint32_t)(c >> 32));
+            id = row_ids[wrow[(uint32_t)(c & 0xffffffffu)]];
+        }
+        out_ids[(int64_t)q * k + j] = id;
+        out_scores[(int64_t)q * k + j] = sc;
+    }
 }
 }  // namespace
 
@@ -976,11 +1101,17 @@ cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
                               const MergeRescore* rs) {
     if (nq <= 0) return cudaSuccess;
     if (rs && (k > RS_MAX || !row_ids)) return cudaErrorInvalidValue;
-    const MergeRescore none{};
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(part_score, part_row, row_ids, P, k,
                                                 (int64_t)P * k, k, (int64_t)P * k, k, out_ids,
-                                                out_scores, out_counts, rs ? *rs : none,
-                                                rs ? 1 : 0);
+                                                out_scores, out_counts, rs ? 1 : 0);
+    if (rs) {
+        if (rs->bf16_rows)
+            rescore_l2_kernel<true><<<nq, RS_MAX, 0, st>>>(*rs, row_ids, k, out_ids, out_scores,
+                                                           out_counts);
+        else
+            rescore_l2_kernel<false><<<nq, RS_MAX, 0, st>>>(*rs, row_ids, k, out_ids, out_scores,
+                                                            out_counts);
+    }
     return cudaGetLastError();
 }
 
@@ -1007,7 +1138,7 @@ cudaError_t launch_merge_shards(const float* scores, const int64_t* ids, int nsh
     if (nq <= 0 || k <= 0) return cudaSuccess;
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(scores, ids, nullptr, nshard, k, k,
                                                 (int64_t)nq * k, k, (int64_t)nq * k, out_ids,
-                                                out_scores, out_counts, MergeRescore{}, 0);
+                                                out_scores, out_counts, 0);
     return cudaGetLastError();
 }
 
@@ -1021,7 +1152,7 @@ cudaError_t launch_merge_shards_packed(const unsigned char* packed, int nshard, 
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(
         reinterpret_cast<const float*>(packed), reinterpret_cast<const int64_t*>(packed + ids_offset),
         nullptr, nshard, k, k, shard_bytes / 4, k, shard_bytes / 8, out_ids, out_scores, out_counts,
-        MergeRescore{}, 0);
+        0);
     return cudaGetLastError();
 }
 

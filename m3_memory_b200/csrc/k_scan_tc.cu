@@ -97,11 +97,12 @@ static_assert(QSLOT_BYTES % 1024 == 0, "query tiles stay 1024-byte aligned");
 static_assert(NSPLIT * 32 == QMAX * 8, "a split thread owns 16 bytes of a query chunk");
 
 struct ItemTC {
-    int32_t list;  // -1: no more items
+    int32_t list;     // -1: no more items
     int32_t np;
-    int32_t nrows;
-    int32_t pad;
-    int64_t off;
+    int32_t nrows;    // rows of this item
+    int32_t tile_nt;  // > 0: a row tile (ScanItem)
+    int64_t off;      // arena row of the item's first row
+    int32_t row_begin, tile_out, tile_t, pad;
     int32_t q[QMAX];
     int32_t slot[QMAX];
 };
@@ -186,6 +187,50 @@ struct Geo {
         bpp = HALF_COLS / (2 * nqp);
     }
 };
+
+// Row tiles: merges a (query, probe) pair's nt tile partial lists (at tile
+// partials grp .. grp + nt - 1 of the tile region) by (score, row in the list)
+// into the pair's own partial list `own`; list0 is the arena row of the list's
+// row 0, buf the warp's 32-key buffer.  Called by the last tile to finish, after
+// the atomic count showed every tile's list written.  Kept out of line: it is
+// rare, and one copy serves every query slot of the epilogue.
+template <int KW>
+__device__ __noinline__ void merge_tile_lists(float* part_score, int64_t* part_row, int k,
+                                              int64_t tile_base, int64_t grp, int nt, int64_t own,
+                                              int64_t list0, unsigned long long* buf, int lane) {
+    const float INF = __int_as_float(0x7f800000);
+    __threadfence();
+    RegTopKW<KW> m;
+    for (int t = 0; t < nt; ++t) {
+        const int64_t tb = (tile_base + grp + t) * (int64_t)k;
+#pragma unroll
+        for (int w = 0; w < KW; ++w) {
+            const int e = 32 * w + lane;
+            float sv = INF;
+            int32_t rv = 0;
+            if (e < k) {
+                const int64_t r = __ldcg(part_row + tb + e);
+                if (r >= 0) {
+                    sv = __ldcg(part_score + tb + e);
+                    rv = (int32_t)(r - list0);
+                }
+            }
+            m.push(buf, k, sv, rv, lane);
+        }
+    }
+    if (m.nbuf) m.flush(buf, k, lane);
+    const int64_t ob = own * (int64_t)k;
+#pragma unroll
+    for (int w = 0; w < KW; ++w) {
+        const int e = 32 * w + lane;
+        if (e < k) {
+            const unsigned long long t = m.top[w];
+            const bool v = t != ~0ull;
+            part_score[ob + e] = v ? key_float((uint32_t)(t >> 32)) : INF;
+            part_row[ob + e] = v ? list0 + (int64_t)(uint32_t)(t & 0xffffffffu) : -1;
+        }
+    }
+}
 
 // XB: bf16 rows (else fp32); KW: register top-k width (k <= 32 KW).
 template <bool XB, int KW>
@@ -558,10 +603,12 @@ __global__ void __launch_bounds__(NTHR, 1)
             int nrows = 0;
             int64_t off = 0;
             if (wi.list >= 0) {
-                nrows = a.list_len[wi.list];
-                off = a.list_off[wi.list];
+                const int len = a.list_len[wi.list];
+                nrows = wi.nrows >= 0 ? min(wi.nrows, len - wi.row_begin) : len - wi.row_begin;
+                off = a.list_off[wi.list] + wi.row_begin;
             }
-            if (np < 1 || np > QM || nrows < 0) {
+            if (np < 1 || np > QM || nrows < 0 || wi.row_begin < 0 ||
+                (wi.tile_nt > 0 && (!a.tile_cnt || wi.tile_out < 0 || wi.tile_t >= wi.tile_nt))) {
                 if (leader) {
                     atomicCAS(err, 0, (int)kErrBadItem);
                     inf->list = -1;
@@ -578,6 +625,10 @@ __global__ void __launch_bounds__(NTHR, 1)
                 inf->np = np;
                 inf->nrows = nrows;
                 inf->off = off;
+                inf->tile_nt = wi.tile_nt;
+                inf->row_begin = wi.row_begin;
+                inf->tile_out = wi.tile_out;
+                inf->tile_t = wi.tile_t;
             }
             __syncwarp();
             if (leader) mbar_arrive(&infofull[slot]);
@@ -751,6 +802,7 @@ __global__ void __launch_bounds__(NTHR, 1)
                     }
             }
             // the item's answers: top-k per (query, probe slot)
+            uint32_t last_mask = 0;  // bit j: query slot j finished its pair's last tile
 #pragma unroll
             for (int j = 0; j < QPW; ++j) {
                 const int qi = rsplit ? j : ew + NEPI * j;
@@ -761,7 +813,12 @@ __global__ void __launch_bounds__(NTHR, 1)
                     const unsigned long long kth = rt[j].entry(a.k - 1);
                     if (a.qbound && lane == 0 && kth != ~0ull)
                         atomicMax(&a.qbound[inf->q[qi]], ~(uint32_t)(kth >> 32));
-                    const int64_t base = ((int64_t)inf->q[qi] * a.P + inf->slot[qi]) * a.k;
+                    const int64_t own = (int64_t)inf->q[qi] * a.P + inf->slot[qi];
+                    const int nt = inf->tile_nt;
+                    // a row tile writes to its tile partial list
+                    const int64_t grp = nt > 0 ? (int64_t)inf->tile_out + (int64_t)qi * nt : 0;
+                    const int64_t base =
+                        (nt > 0 ? a.tile_base + grp + inf->tile_t : own) * (int64_t)a.k;
 #pragma unroll
                     for (int w = 0; w < KW; ++w) {
                         const int e = 32 * w + lane;
@@ -773,10 +830,33 @@ __global__ void __launch_bounds__(NTHR, 1)
                                 v ? off + (int64_t)(uint32_t)(t & 0xffffffffu) : -1;
                         }
                     }
+                    if (nt > 0) {
+                        // the pair's last tile to finish (counted after its list is out)
+                        // merges the pair's nt tile lists below
+                        __threadfence();
+                        __syncwarp();
+                        int done = 0;
+                        if (lane == 0) done = atomicAdd(&a.tile_cnt[grp], 1);
+                        if (__shfl_sync(0xffffffffu, done, 0) == nt - 1) last_mask |= 1u << j;
+                    }
                 }
             }
             // the exchange area and key buffers are reused by the next item
             if (rsplit) named_bar_sync(EPI_BAR, NEPI * 32);
+            // Row tiles: the last tile of a pair merges the pair's tile lists into the
+            // pair's own partial list.  Only this warp's key buffer is touched (the
+            // row split's exchange is over, and the other warps start the next item
+            // at a barrier of all four).
+#pragma unroll 1
+            for (int j = 0; j < QPW; ++j) {
+                if (!((last_mask >> j) & 1u)) continue;
+                const int qi = rsplit ? j : ew + NEPI * j;
+                const int nt = inf->tile_nt;
+                merge_tile_lists<KW>(a.part_score, a.part_row, a.k, a.tile_base,
+                                     (int64_t)inf->tile_out + (int64_t)qi * nt, nt,
+                                     (int64_t)inf->q[qi] * a.P + inf->slot[qi],
+                                     off - inf->row_begin, kbuf + qi * 32, lane);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&infoempty[slot]);
         }

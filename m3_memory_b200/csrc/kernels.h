@@ -44,7 +44,16 @@ struct ScanItem {
     int32_t list;        // cluster id
     int32_t pair_begin;  // first (query, probe slot) pair of this item in the pair arrays
     int32_t npairs;      // number of queries in the item (<= gmax)
-    int32_t pad;
+    int32_t row_begin;   // first row of the list the item scans
+    int32_t nrows;       // rows it scans; -1: to the end of the list
+    // Row tiles of a long list (tile_nt > 0): the item is tile tile_t of tile_nt,
+    // its pair i writes its partial top-k to tile partial tile_out + i tile_nt +
+    // tile_t (an index into the tile region of the partial lists, which starts at
+    // ScanArgs::tile_base), and the last tile to finish merges the pair's
+    // tile_nt lists into its own (query, probe slot) partial list.
+    int32_t tile_out;
+    int32_t tile_t;
+    int32_t tile_nt;
 };
 
 // Row boxes of the list arena for the scans: 2-D tensor maps over the arena
@@ -76,6 +85,10 @@ struct ScanArgs {
     // test hook (tensor-core scan): when nonzero, the scheduler first waits this
     // long on a barrier nothing arrives at, records the timeout and ends the scan
     uint64_t test_wait_ns;
+    // row tiles (tensor-core scan): partial index of the tile region and, per
+    // tiled pair, a counter of its finished tiles (zeroed before launch)
+    int64_t tile_base;
+    int32_t* tile_cnt;
 };
 
 int scan_kmax();
@@ -94,12 +107,18 @@ cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, bool bf1
 // Work list: per-list counts of (query, probe) pairs, items, and the pairs
 // grouped by list.  list_order lists the clusters longest first.  With
 // skip_len ([L] rows per list), pairs probing an empty list are left out (their
-// partial lists must then be cleared beforehand).
+// partial lists must then be cleared beforehand).  With tile_rows > 0 (a
+// multiple of 128; the tensor-core scan only) a list longer than tile_rows and
+// probed by at most two query groups is scanned in row tiles of tile_rows, each
+// group once per tile, as long as its tile partial lists fit the tile region of
+// tile_cap lists (longest lists first); list_len gives the rows per list.
 cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
                                   const int32_t* list_order, int gmax, int32_t* lcount,
                                   int32_t* lstart, int32_t* lcursor, ScanItem* items,
                                   int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
-                                  cudaStream_t st, const int32_t* skip_len = nullptr);
+                                  cudaStream_t st, const int32_t* skip_len = nullptr,
+                                  const int32_t* list_len = nullptr, int tile_rows = 0,
+                                  int tile_cap = 0);
 
 // Exact squared-L2 rescoring of a merge's winners: the reference's sum of
 // (q_i - x_i)^2 in index order (AgentMemory/M3/src/base.cpp:12-20) over the

@@ -56,8 +56,8 @@ cudaError_t launch_set_bytes(uint8_t* dst, const int64_t* idx, int64_t n, uint8_
 cudaError_t launch_iota_rows(int32_t* out, int64_t nrows, int width, cudaStream_t st);
 cudaError_t launch_broadcast_row(const int32_t* row, int width, int64_t nrows, int32_t* out,
                                  cudaStream_t st);
-cudaError_t launch_probed_rows(const int32_t* lcount, const int32_t* list_len, int L,
+cudaError_t launch_probed_rows(const int32_t* lcount, const int32_t* list_len, int L, int gmax,
                                unsigned long long* out_rows, unsigned long long* out_pairs,
-                               cudaStream_t st);
+                               unsigned long long* out_streamed, cudaStream_t st);
 
 }  // namespace m3g

@@ -33,6 +33,14 @@ candidates of all ranks are all-gathered and merged into the global top-P by
 single-GPU selection except between centroids whose exact scores tie -- and each
 rank scans the winners it owns (``m3g_search_probes_device``, -1 for the
 others) before the top-k exchange above.
+
+``search_own_batch`` is the serving form, where every rank brings its own batch
+of queries per step: the batches are all-gathered so that every shard sees
+every query, each rank selects the probes of its own batch, the probe lists
+are all-gathered, each rank scans its lists for all batches, and each batch's
+per-shard top-k go back to the batch's rank in one all-to-all of packed records
+for the final merge there.  The work per rank then stays fixed as ranks (and
+batches) are added.
 """
 from __future__ import annotations
 
@@ -85,6 +93,7 @@ class ShardedSearch:
         self.coarse_index_id = coarse_index_id
         self.split_coarse = split_coarse and coarse_index_id is None
         self.rank = rank
+        self.max_probe_cap = max_nprobe
         if self.split_coarse:
             self.nlist = int(engine.info(index_id)[3])
             p = min(max_nprobe, self.nlist)
@@ -202,6 +211,97 @@ class ShardedSearch:
                                                self.out_sc.data_ptr(), self.out_cnt.data_ptr(), s)
         self._mark("topk_exchange")
         return self.out_ids[:nq], self.out_sc[:nq], self.out_cnt[:nq]
+
+    def search_own_batch(self, q_own, nprobe: int):
+        """Top-k over all shards for this rank's own query batch ``q_own`` ([B, dim]
+        fp32, B <= max_q and the same on every rank), ordered after torch's current
+        stream, which waits for the answer.
+
+        Every rank brings its own batch per step: the batches are all-gathered
+        (the queries reach every shard), each rank selects the probes of its own
+        batch over all centroids, the probe lists are all-gathered, every rank
+        scans its own lists for all world * B queries, and the per-shard top-k of
+        each batch go back to the batch's rank -- one all-to-all of packed records
+        (scores, then ids) -- where ``m3g_merge_shards_packed_device`` merges them.
+        Per-rank work stays fixed as ranks are added.  Returns (ids, scores,
+        counts) views of this rank's answer, overwritten by the next call."""
+        import torch
+
+        caller = torch.cuda.current_stream(q_own.device)
+        self.stream.wait_stream(caller)
+        with torch.cuda.stream(self.stream):
+            out = self._search_own_batch(q_own, nprobe)
+        caller.wait_stream(self.stream)
+        return out
+
+    def _own_buffers(self, dim, device):
+        import torch
+
+        if getattr(self, "_own", None) is not None and self._own["dim"] == dim:
+            return self._own
+        nlist = int(self.engine.info(self.index_id)[3])
+        p = min(self.max_probe_cap, nlist)
+        W, B, k = self.world, self.max_q, self.k
+        R = self.record_bytes(B)
+        self._own = dict(
+            dim=dim, nlist=nlist, P=p,
+            q_all=torch.empty((W * B, dim), dtype=torch.float32, device=device),
+            loc=torch.empty((B, p), dtype=torch.int32, device=device),
+            probes=torch.empty((W * B, p), dtype=torch.int32, device=device),
+            ids=torch.empty((W * B, k), dtype=torch.int64, device=device),
+            sc=torch.empty((W * B, k), dtype=torch.float32, device=device),
+            cnt=torch.empty((W * B,), dtype=torch.int32, device=device),
+            send=torch.empty(W * R, dtype=torch.uint8, device=device),
+            recv=torch.empty(W * R, dtype=torch.uint8, device=device))
+        return self._own
+
+    def _search_own_batch(self, q, nprobe: int):
+        import torch
+        import torch.distributed as dist
+
+        B, dim = int(q.shape[0]), int(q.shape[1])
+        if B > self.max_q:
+            raise ValueError(f"batch of {B} queries exceeds max_q={self.max_q}")
+        if not q.is_contiguous():
+            raise ValueError("the query batch must be contiguous")
+        k, W, s = self.k, self.world, self.stream.cuda_stream
+        self._mark("start")
+        if W == 1:
+            self.engine.search_device(self.index_id, q.data_ptr(), B, k, nprobe,
+                                      self.ids.data_ptr(), self.sc.data_ptr(),
+                                      self.cnt.data_ptr(), s)
+            self._mark("search")
+            return self.ids[:B], self.sc[:B], self.cnt[:B]
+        o = self._own_buffers(dim, q.device)
+        P = min(nprobe if nprobe > 0 else o["nlist"], o["nlist"])
+        if P > o["P"]:
+            raise ValueError(f"nprobe {P} exceeds max_nprobe={o['P']}")
+        q_all = o["q_all"][:W * B]
+        dist.all_gather_into_tensor(q_all, q, group=self.group)
+        self._mark("query_exchange")
+        loc = o["loc"].view(-1)[:B * P].view(B, P)
+        self.engine.select_probes_device(self.index_id, q.data_ptr(), B, P, loc.data_ptr(), s)
+        self._mark("coarse")
+        probes = o["probes"].view(-1)[:W * B * P].view(W * B, P)
+        dist.all_gather_into_tensor(probes, loc, group=self.group)
+        self._mark("probe_exchange")
+        ids, sc, cnt = o["ids"][:W * B], o["sc"][:W * B], o["cnt"][:W * B]
+        self.engine.search_probes_device(self.index_id, q_all.data_ptr(), W * B, k,
+                                         probes.data_ptr(), P, ids.data_ptr(), sc.data_ptr(),
+                                         cnt.data_ptr(), s)
+        self._mark("search")
+        # batch r's answers from this shard go to rank r as one record
+        R, off = self.record_bytes(B), self.ids_offset(B)
+        send = o["send"][:W * R].view(W, R)
+        send[:, :B * k * 4].view(torch.float32).copy_(sc.view(W, B * k))
+        send[:, off:off + B * k * 8].view(torch.int64).copy_(ids.view(W, B * k))
+        recv = o["recv"][:W * R]
+        dist.all_to_all_single(recv, o["send"][:W * R], group=self.group)
+        self.engine.merge_shards_packed_device(recv.data_ptr(), W, B, k, R, off,
+                                               self.out_ids.data_ptr(), self.out_sc.data_ptr(),
+                                               self.out_cnt.data_ptr(), s)
+        self._mark("topk_exchange")
+        return self.out_ids[:B], self.out_sc[:B], self.out_cnt[:B]
 
     def _search_split_coarse(self, q, nq, nprobe, s, a_ids, a_sc):
         """Probes of this rank's query slice, all-gathered, then the scan of the

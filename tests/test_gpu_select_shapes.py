@@ -8,7 +8,8 @@ and past 1024 (ids returned unsorted).  The centroid sets cover a clustered
 mixture (close scores: most candidates are rescored), more centroids than the
 shared-memory key caches hold (L = 9000), and near-duplicate centroids whose
 intervals all overlap (S0 and the candidate list overflow into the exact
-fallback)."""
+fallback), and centroids stored twice each, whose intervals overlap in pairs
+among more than 128 candidates (the sorted overlap test)."""
 import numpy as np
 import pytest
 
@@ -21,6 +22,7 @@ CASES = {
     "cos_raw": (2, False, 1500, 130, 32, (1, 32, 127, 300)),
     "cos_norm_wide": (2, True, 9000, 64, 24, (1, 16, 64, 128, 500)),
     "ip_near_duplicates": (1, False, 600, 128, 16, (1, 8, 64, 128, 400)),
+    "l2_duplicate_pairs": (0, False, 1000, 64, 16, (129, 200, 256, 700)),
 }
 
 
@@ -32,6 +34,13 @@ def make_case(name):
         C = (base + 1e-6 * rng.standard_normal((L, d))).astype(np.float32)
         C[::7] = base  # exact duplicates: exact ties, broken by id
         Q = (base + 0.5 * rng.standard_normal((nq, d))).astype(np.float32)
+    elif name == "l2_duplicate_pairs":
+        # every centroid twice (ids 2i and 2i + 1): many overlapping pairs of
+        # intervals among candidates that are otherwise well apart, the case the
+        # sorted overlap test (more than 128 candidates) must flag exactly
+        U = (4.0 * rng.standard_normal((L // 2, d))).astype(np.float32)
+        C = np.repeat(U, 2, axis=0)
+        Q = (U[rng.integers(0, L // 2, nq)] + rng.standard_normal((nq, d))).astype(np.float32)
     else:
         means = rng.standard_normal((16, d)).astype(np.float32)
         C = (means[rng.integers(0, 16, L)] + 0.3 * rng.standard_normal((L, d))).astype(np.float32)

@@ -295,6 +295,10 @@ def test_split_coarse_two_engines_equal_one(cuda_ok):
     compare_search((ids.cpu().numpy(), sc.cpu().numpy(), cnt.cpu().numpy()), want, exact=True)
     assert [n for n, _ in ss.marks] == ["start", "coarse", "probe_exchange", "search"]
     assert all(a.elapsed_time(b) >= 0 for (_, a), (_, b) in zip(ss.marks, ss.marks[1:]))
+    # the serving form on one rank is the plain search of the rank's batch
+    ids, sc, cnt = ShardedSearch(full, 1, k, nq, 1, "cuda").search_own_batch(q, P)
+    torch.cuda.synchronize()
+    compare_search((ids.cpu().numpy(), sc.cpu().numpy(), cnt.cpu().numpy()), want, exact=True)
 
 
 _NCCL_CHILD = r"""
@@ -320,6 +324,15 @@ for name, kw in (("replicated", {}), ("sharded", dict(coarse_index_id=2, owner=o
     torch.cuda.synchronize()
     out[name + "_ids"], out[name + "_sc"], out[name + "_cnt"] = (
         ids.cpu().numpy(), sc.cpu().numpy(), cnt.cpu().numpy())
+B = len(c["Q"]) // world  # serving form: each rank brings its own half of the queries
+ss = ShardedSearch(e, 1, 10, B, world, "cuda", rank=rank)
+ids, sc, cnt = ss.search_own_batch(q[rank * B:(rank + 1) * B].contiguous(), 12)
+torch.cuda.synchronize()
+g = [torch.empty_like(t) for t in (ids, sc, cnt) for _ in range(world)]
+for j, t in enumerate((ids, sc, cnt)):
+    dist.all_gather(g[j * world:(j + 1) * world], t.contiguous())
+out["own_ids"], out["own_sc"], out["own_cnt"] = (
+    torch.cat(g[j * world:(j + 1) * world]).cpu().numpy() for j in range(3))
 if rank == 0:
     np.savez(sys.argv[2], **out)
 dist.barrier()
@@ -360,3 +373,6 @@ def test_sharded_search_over_nccl_two_gpus(cuda_ok, tmp_path):
     for name in ("replicated", "sharded", "split"):
         compare_search((got[name + "_ids"], got[name + "_sc"], got[name + "_cnt"]), full,
                        exact=True)
+    B = len(c["Q"]) // 2  # each rank's own batch, concatenated in rank order
+    compare_search((got["own_ids"], got["own_sc"], got["own_cnt"]),
+                   tuple(a[:2 * B] for a in full), exact=True)

@@ -171,3 +171,87 @@ def test_global_top_p_from_ranks_exact_local_top_p(oracle_mod):
             for i, q in enumerate(c["Q"]):
                 want = oracle_mod.select_nprobe(q, c["C"], metric, norm, P)
                 np.testing.assert_array_equal(top[i], want)
+
+
+def _own_batch_rank_main(rank, world, port, metric, normalized, out):
+    """The serving decomposition of ShardedSearch.search_own_batch with the oracle
+    in place of the engine: every rank brings its own batch, the batches are
+    all-gathered, each rank selects its own batch's probes, the probes are
+    all-gathered, each rank searches its own lists for every query, and each
+    batch's records go back to its rank through one all-to-all for the merge."""
+    sys.path.insert(0, str(ROOT))
+    import torch
+    import torch.distributed as dist
+
+    from m3_memory_b200.sharding import shard_lists
+    from oracle import oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        c = _case()
+        k, P = c["k"], c["nprobe"]
+        B = len(c["Q"]) // world
+        owner = shard_lists(c["sizes"], world)
+        lists = _local_lists(O, c, owner, rank)
+        q_own = torch.from_numpy(np.ascontiguousarray(c["Q"][rank * B:(rank + 1) * B]))
+        q_all = torch.empty((world * B, q_own.shape[1]), dtype=torch.float32)
+        dist.all_gather_into_tensor(q_all, q_own)
+        loc = torch.from_numpy(np.stack([O.select_nprobe(q, c["C"], metric, normalized, P)
+                                         for q in q_own.numpy()]).astype(np.int32))
+        probes = torch.empty((world * B, P), dtype=torch.int32)
+        dist.all_gather_into_tensor(probes, loc)
+        ids = np.full((world * B, k), -1, np.int64)
+        sc = np.full((world * B, k), np.inf, np.float32)
+        for i, q in enumerate(q_all.numpy()):
+            a_ids, a_sc, a_cnt = O.search_on(q[None], lists, probes[i].numpy(), metric,
+                                             normalized, k)
+            ids[i], sc[i] = a_ids[0], a_sc[0]
+        # records of batch r (scores then ids, as bytes) go to rank r
+        rec = [np.concatenate([sc[r * B:(r + 1) * B].reshape(-1).view(np.uint8),
+                               ids[r * B:(r + 1) * B].reshape(-1).view(np.uint8)])
+               for r in range(world)]
+        send = torch.from_numpy(np.concatenate(rec))
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send)
+        R = len(rec[0])
+        got = recv.numpy().reshape(world, R)
+        g_sc = got[:, :B * k * 4].copy().view(np.float32).reshape(world, B, k)
+        g_ids = got[:, B * k * 4:].copy().view(np.int64).reshape(world, B, k)
+        out.put((rank, "ok", O.merge_shards(g_sc, g_ids)))
+    except Exception as ex:  # reported to the parent, which fails the test
+        out.put((rank, "error", repr(ex)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("metric,normalized", [(1, False), (0, False)])
+def test_own_batch_exchange_equals_unsharded(oracle_mod, metric, normalized):
+    """Each rank's merged answer for its own batch equals the unsharded search of
+    that batch (world size 2 over gloo)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_own_batch_rank_main,
+                         args=(r, world, port, metric, normalized, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = [out.get(timeout=120) for _ in range(world)]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    c = _case()
+    B = len(c["Q"]) // world
+    lists = oracle_mod.CsrLists(c["off"], c["X"], c["ids"], c["alive"])
+    for rank, status, merged in res:
+        assert status == "ok", merged
+        want = oracle_mod.search_nprobe(c["Q"][rank * B:(rank + 1) * B], c["C"], lists, metric,
+                                        normalized, c["k"], c["nprobe"])
+        compare_search(merged, want, exact=True)
+    assert all(p.exitcode == 0 for p in procs)
