@@ -616,17 +616,17 @@ def run_ours(args, rank, world, local_rank):
 
     if rank != 0:
         return
-    # our kernels per step: norms, split, coarse GEMM, select, 3 work-list, scan, merge;
-    # N > 1 adds the shard merge; the query-split coarse step a second row-norm pass and
-    # the partial-list clear; the sharded coarse step also the pair scores and the
-    # top-P merge; the own-batch (weak) step: norms, split, coarse GEMM, select for the
-    # rank's batch, then norms, 3 work-list, partial clear, scan, merge for all batches,
-    # and the shard merge
+    # our kernels per step: query prep (norms + split), coarse GEMM, select, 5 work-list
+    # (histogram, gather, scan, place, pair scatter), scan, merge; N > 1 adds the shard
+    # merge; the query-split coarse step a second prep and the partial-list clear; the
+    # sharded coarse step also the pair scores and the top-P merge; the own-batch (weak)
+    # step: prep, coarse GEMM, select for the rank's batch, then prep, 5 work-list,
+    # partial clear, scan, merge for all batches, and the shard merge
     # (the profiled calls add the engine's probed-byte counter, one launch per step, which
     # the timed loop does not run)
     per_step_launches = (launches / args.steps - 1) if launches else (
-        9 if world == 1 else 12 if weak else
-        {"replicated": 10, "split": 12, "sharded": 14}[args.coarse])
+        10 if world == 1 else 13 if weak else
+        {"replicated": 11, "split": 13, "sharded": 15}[args.coarse])
     peak, peak_kind = peaks()
     roofline = None
     if scan_ms:
@@ -910,6 +910,26 @@ def run_config3(args, rank, world, local_rank):
                     "ms_per_launch": statistics.mean(sm),
                     "stage_ms_mean": {k: round(statistics.mean(v), 4) for k, v in stages.items()},
                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
+        # the stages of small batches (device-resident queries, the engine's events; the
+        # kernels then run one by one instead of as a graph)
+        small = {}
+        ids_d = torch.empty((64, K3), dtype=torch.int64, device=dev)
+        sc_d = torch.empty((64, K3), dtype=torch.float32, device=dev)
+        cnt_d = torch.empty((64,), dtype=torch.int32, device=dev)
+        eng.set_profiling(True)
+        for Bs in (1, 64):
+            st_s = {}
+            for i in range(10):
+                eng.search_device(1, Qd[i * Bs].data_ptr(), Bs, K3, C3_NPROBES[0], ids_d.data_ptr(),
+                                  sc_d.data_ptr(), cnt_d.data_ptr())
+                p = eng.last_profile()
+                for key in ("ms_prep", "ms_coarse_gemm", "ms_select", "ms_worklist", "ms_scan",
+                            "ms_merge", "ms_total"):
+                    st_s.setdefault(key[3:], []).append(p[key])
+            small[f"nprobe{C3_NPROBES[0]}_batch{Bs}"] = {
+                k: round(statistics.median(v), 4) for k, v in st_s.items()}
+        eng.set_profiling(False)
+        roofline["small_batch_stage_ms_median"] = small
         if not args.no_cpu_baseline:
             from oracle import oracle as O
 

@@ -180,7 +180,12 @@ class Engine:
             self.h = None
 
     def __del__(self):
-        self.close()
+        # at interpreter exit the module's globals may already be gone: the
+        # process is ending and the driver releases the engine's memory
+        try:
+            self.close()
+        except TypeError:
+            pass
 
     # lifecycle / policies
     def start(self, writers=2, maint=1):

@@ -783,6 +783,8 @@ Engine::~Engine() {
     ws_.pair_q.release();
     ws_.pair_slot.release();
     ws_.items.release();
+    ws_.tile_cnt.release();
+    ws_.plan.release();
     ws_.part_score.release();
     ws_.part_row.release();
     ws_.out_ids.release();
@@ -1578,8 +1580,10 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     const int D = ix.dim;
     cudaEvent_t* ev = w.ev;
     if (profile) M3G_CK(cudaEventRecord(ev[0], st));
-    launch_row_norms(dQ, ldq, nq, D, w.qn.p, w.qn2.p, st);
-    M3G_CK(cudaGetLastError());
+    // the queries' norms and, for the tensor-core coarse GEMM, their split rows
+    const bool split_q = !fixed_probes && P < L && use_tc_gemm();
+    M3G_CK(launch_query_prep(dQ, ldq, nq, D, ix.dpad, gemm_tc_kdim(ix.dpad),
+                             split_q ? w.Q3.p : nullptr, w.qn.p, w.qn2.p, st));
     if (profile) M3G_CK(cudaEventRecord(ev[1], st));
     const int32_t* probes = fixed_probes;
     if (!probes) {
@@ -1587,8 +1591,6 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
             M3G_CK(launch_iota_rows(w.probes.p, nq, P, st));
             if (profile) M3G_CK(cudaEventRecord(ev[2], st));
         } else {
-            if (use_tc_gemm())
-                M3G_CK(launch_split3(dQ, ldq, nq, ix.dpad, gemm_tc_kdim(ix.dpad), w.Q3.p, false, st));
             const float beta = coarse_gemm(dQ, ldq, w.Q3.p, ix.C.p, ix.dpad, ix.C3.p, w.S.p, L,
                                            (int)nq, L, ix.dpad, w.err.p, st);
             if (profile) M3G_CK(cudaEventRecord(ev[2], st));
@@ -1615,7 +1617,8 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     const int64_t tcap = tile_partials(nq, P);
     M3G_CK(launch_build_worklist(probes, (int)nq, P, L, ix.d_list_order.p, gmax, w.lcount.p,
                                  w.lstart.p, w.lcursor.p, w.items.p, w.n_items.p, w.pair_q.p,
-                                 w.pair_slot.p, st, clear_partials ? ix.d_list_len.p : nullptr,
+                                 w.pair_slot.p, w.plan.p, st,
+                                 clear_partials ? ix.d_list_len.p : nullptr,
                                  ix.d_list_len.p, tile_rows, (int)std::min<int64_t>(tcap, INT32_MAX)));
     if (tile_rows > 0) M3G_CK(cudaMemsetAsync(w.tile_cnt.p, 0, sizeof(int32_t) * (size_t)tcap, st));
     if (profile) {
@@ -1674,10 +1677,10 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     M3G_CK(launch_merge_topk(w.part_score.p, w.part_row.p, ix.ids.p, (int)nq, P, k, d_ids, d_scores,
                              d_counts, st, rescore ? &rs : nullptr));
     if (profile) M3G_CK(cudaEventRecord(ev[6], st));
-    // kernels launched: norms, coarse (gemm + select, or iota), 3 work-list
+    // kernels launched: query prep, coarse (gemm + select, or iota), 5 work-list
     // kernels, scan, merge (+ the exact rescoring for L2, + the byte counter when
     // profiling)
-    int launches = 1 + (fixed_probes ? 0 : (P >= L ? 1 : (use_tc_gemm() ? 3 : 2))) + 3 +
+    int launches = 1 + (fixed_probes ? 0 : (P >= L ? 1 : 2)) + 5 +
                    (ix.maps_valid ? 1 : 0) + 1 + (rescore ? 1 : 0);
     if (profile) launches += 1;
     last_launches_ += launches;
@@ -1694,7 +1697,7 @@ std::vector<uintptr_t> Engine::graph_key(const Index& ix, int64_t nq, int k, int
             (uintptr_t)ix.normalized, (uintptr_t)ix.maps_valid, (uintptr_t)nq, (uintptr_t)k,
             (uintptr_t)P, u(w.Q.p), u(w.Q3.p), u(w.S.p), u(w.qn.p), u(w.qn2.p), u(w.probes.p),
             u(w.lcount.p), u(w.lstart.p), u(w.lcursor.p), u(w.items.p), u(w.n_items.p),
-            u(w.item_counter.p), u(w.pair_q.p), u(w.pair_slot.p), u(w.part_score.p),
+            u(w.item_counter.p), u(w.pair_q.p), u(w.pair_slot.p), u(w.plan.p), u(w.part_score.p),
             u(w.part_row.p), u(w.out_ids.p), u(w.out_scores.p), u(w.out_counts.p), u(w.err.p),
             (uintptr_t)use_tc_scan(), (uintptr_t)use_tc_gemm(), (uintptr_t)test_wait_ns_,
             (uintptr_t)(intptr_t)scan_tile_rows(ix), u(w.tile_cnt.p)};
@@ -1742,8 +1745,9 @@ bool Engine::run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t 
         graph_.key = std::move(key);
     } else {
         // the kernels a replay runs, for the caller's accounting
-        last_launches_ += 1 + (P >= ix.nlist() ? 1 : (use_tc_gemm() ? 3 : 2)) + 3 +
-                          (ix.maps_valid ? 1 : 0) + 1;
+        const bool tc = (use_tc_scan() || ix.bf16_rows()) && scan_tc_supported(ix.metric, k);
+        last_launches_ += 1 + (P >= ix.nlist() ? 1 : 2) + 5 + (ix.maps_valid ? 1 : 0) + 1 +
+                          (tc && ix.metric == M3G_L2 && ix.maps_valid ? 1 : 0);
     }
     M3G_CK(cudaGraphLaunch(graph_.exec, st));
     ++graph_launches_;
@@ -1762,7 +1766,8 @@ bool ws_needs_grow(const Workspace& w, const WsSizes& s) {
     const int64_t np = s.nq * s.P, nt = tile_partials(s.nq, s.P);
     return !w.err.p || short_of(w.Q, s.nq * s.dpad) || short_of(w.qn, s.nq) ||
            short_of(w.S, s.nq * s.L) || short_of(w.probes, np) || short_of(w.lcount, s.L) ||
-           short_of(w.lstart, s.L) || short_of(w.lcursor, s.L) || short_of(w.pair_q, np) ||
+           short_of(w.lstart, s.L) || short_of(w.lcursor, s.L) || short_of(w.plan, 6 * s.L) ||
+           short_of(w.pair_q, np) ||
            short_of(w.pair_slot, np) || short_of(w.items, np + nt) || short_of(w.tile_cnt, nt) ||
            short_of(w.part_score, (np + nt) * s.k) || short_of(w.part_row, (np + nt) * s.k) ||
            short_of(w.out_ids, s.nq * s.k) || short_of(w.out_scores, s.nq * s.k) ||
@@ -1786,6 +1791,7 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
     w.lcount.ensure((size_t)s.L);
     w.lstart.ensure((size_t)s.L);
     w.lcursor.ensure((size_t)s.L);
+    w.plan.ensure((size_t)(6 * s.L));
     w.pair_q.ensure((size_t)(s.nq * s.P));
     w.pair_slot.ensure((size_t)(s.nq * s.P));
     const int64_t nt = tile_partials(s.nq, s.P);
@@ -2067,13 +2073,12 @@ void Engine::select_probes(int index_id, const float* Q, int64_t nq, int nprobe,
         if (ix->dpad != ix->dim) M3G_CK(cudaMemsetAsync(ws_.Q.p, 0, (size_t)(m * ix->dpad) * 4, st));
         M3G_CK(cudaMemcpy2DAsync(ws_.Q.p, (size_t)ix->dpad * 4, Q + q0 * ix->dim, (size_t)ix->dim * 4,
                                  (size_t)ix->dim * 4, (size_t)m, cudaMemcpyHostToDevice, st));
-        launch_row_norms(ws_.Q.p, ix->dpad, m, ix->dim, ws_.qn.p, ws_.qn2.p, st);
+        M3G_CK(launch_query_prep(ws_.Q.p, ix->dpad, m, ix->dim, ix->dpad, gemm_tc_kdim(ix->dpad),
+                                 P < L && use_tc_gemm() ? ws_.Q3.p : nullptr, ws_.qn.p,
+                                 ws_.qn2.p, st));
         if (P >= L) {
             M3G_CK(launch_iota_rows(ws_.probes.p, m, P, st));
         } else {
-            if (use_tc_gemm())
-                M3G_CK(launch_split3(ws_.Q.p, ix->dpad, m, ix->dpad, gemm_tc_kdim(ix->dpad),
-                                     ws_.Q3.p, false, st));
             const float beta = coarse_gemm(ws_.Q.p, ix->dpad, ws_.Q3.p, ix->C.p, ix->dpad,
                                            ix->C3.p, ws_.S.p, L, (int)m, L, ix->dpad, ws_.err.p,
                                            st);
@@ -2113,13 +2118,12 @@ void Engine::select_probes_device(int index_id, const float* dQ, int64_t nq, int
         const int64_t m = std::min(ch, nq - q0);
         const float* q = stage_queries(*ix, dQ + q0 * ix->dim, m, st);
         int32_t* out = d_out + q0 * P;
-        launch_row_norms(q, ix->dpad, m, ix->dim, ws_.qn.p, ws_.qn2.p, st);
+        M3G_CK(launch_query_prep(q, ix->dpad, m, ix->dim, ix->dpad, gemm_tc_kdim(ix->dpad),
+                                 P < L && use_tc_gemm() ? ws_.Q3.p : nullptr, ws_.qn.p,
+                                 ws_.qn2.p, st));
         if (P >= L) {
             M3G_CK(launch_iota_rows(out, m, P, st));
         } else {
-            if (use_tc_gemm())
-                M3G_CK(launch_split3(q, ix->dpad, m, ix->dpad, gemm_tc_kdim(ix->dpad), ws_.Q3.p,
-                                     false, st));
             const float beta = coarse_gemm(q, ix->dpad, ws_.Q3.p, ix->C.p, ix->dpad, ix->C3.p,
                                            ws_.S.p, L, (int)m, L, ix->dpad, ws_.err.p, st);
             M3G_CK(launch_select_probes(ws_.S.p, L, q, ix->dpad, ix->C.p, ix->dpad, ws_.qn.p,

@@ -173,6 +173,7 @@ struct Workspace {
     DBuf<__nv_bfloat16> Q3;  // split query operand [hi | hi | lo]
     DBuf<int32_t> probes, lcount, lstart, lcursor, n_items, item_counter, pair_q, pair_slot;
     DBuf<int32_t> tile_cnt;  // finished row tiles per tiled pair (tensor-core scan)
+    DBuf<int32_t> plan;      // work-list planning scratch, 6 per list
     DBuf<ScanItem> items;
     DBuf<float> part_score;
     DBuf<int64_t> part_row;

@@ -172,7 +172,6 @@ constexpr int SEL_KEYS_SMEM = 8192;  // upper-bound keys cached in shared memory
 constexpr int SEL_SORT_MAX = 1024;   // largest P whose selection is returned sorted
 constexpr int SEL_OVERLAP_MAX = 128; // above this many candidates the overlap test sorts
 constexpr int SEL_STAGE = kExactTileFloats;  // per-warp product tile of the exact rescoring
-constexpr int SEL_FAST_P = 128;      // largest P that takes the pre-filtered threshold path
 constexpr int SEL_KEEP_LO_L = 8192;  // largest L whose lower-bound keys stay beside S0
 constexpr int SEL_UNROLL = 8;        // centroids per thread whose bounds load together
 constexpr uint32_t kKeyNegInf = 0x007fffffu;  // float_key(-inf)
@@ -182,7 +181,7 @@ static_assert(SEL_LARGE_CAP >= SEL_SORT_MAX && SEL_SMALL_CAP >= SEL_SMALL_P,
 static_assert(3 * SEL_SMALL_CAP <= (SEL_SMALL_NT / 32) * SEL_STAGE &&
                   3 * SEL_LARGE_CAP <= (SEL_LARGE_NT / 32) * SEL_STAGE,
               "S0 lives in the tile area");
-static_assert(SEL_FAST_P <= 32 * (SEL_SMALL_NT / 32), "each warp offers its ceil(P / warps)-th key");
+static_assert(SEL_SMALL_P <= SEL_SMALL_NT, "the small block's P takes its pre-filtered path");
 
 // 32-bit words of the shared area that holds, in turn, the cached upper-bound
 // keys or the lower-bound keys beside S0, and the per-warp product tiles.
@@ -358,11 +357,16 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
     unsigned cnt = 0;
     // interval of candidate i as keys (lower, upper), beside cand[i]
     uint2* ik = reinterpret_cast<uint2*>(bnd);
-    if (!exact_all && PP <= SEL_FAST_P) {
-        // --- pre-filtered threshold.  Each of the NW warps sorts its threads'
-        // smallest upper-bound keys and offers its ceil(PP/NW)-th smallest; tau0,
-        // the largest offer, has at least NW * ceil(PP/NW) >= PP distinct keys <= it, so
-        // tau0 >= T (the PP-th smallest upper bound of all).  Every centroid with
+    // the pre-filtered threshold serves P up to 32 per warp (each warp offers its
+    // ceil(P / NW)-th key): 128 in the small block, 256 in the large one
+    if (!exact_all && PP <= 32 * NW) {
+        // --- pre-filtered threshold.  Small block: each of the NW warps sorts its
+        // threads' smallest upper-bound keys and offers its ceil(PP/NW)-th smallest;
+        // tau0, the largest offer, has at least NW * ceil(PP/NW) >= PP distinct keys
+        // <= it.  Large block (P up to 256): every thread keeps its TOPT smallest
+        // keys and tau0 is the PP-th smallest of those NT * TOPT keys (a far tighter
+        // threshold than the offers, whose largest is the largest thread minimum).
+        // Either way tau0 >= T (the PP-th smallest upper bound of all).  Every centroid with
         // hi <= T therefore has lo <= tau0, so T is the PP-th smallest upper bound
         // within S0 = {c : lo <= tau0}, and every candidate (lo <= T) is in S0.
         // The lower-bound keys of the first pass are kept when they fit beside S0.
@@ -370,7 +374,11 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         // their loads issued together.
         uint32_t* lkeys = hkeys;
         const bool keep_lo = L <= SEL_KEEP_LO_L;  // the area then holds L + 3 CAP words
-        uint32_t mymin = 0xffffffffu;
+        constexpr int TOPT = NT == SEL_LARGE_NT ? 4 : 1;
+        static_assert(TOPT * NT <= CAP, "the thread minima fit the S0 key array");
+        uint32_t mk[TOPT];  // this thread's TOPT smallest upper-bound keys, ascending
+#pragma unroll
+        for (int j = 0; j < TOPT; ++j) mk[j] = 0xffffffffu;
         for (int c0 = threadIdx.x; c0 < L; c0 += SEL_UNROLL * NT) {
             float sv[SEL_UNROLL], av[SEL_UNROLL], bv[SEL_UNROLL];
 #pragma unroll
@@ -386,16 +394,28 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
                 if (c < L) {
                     float lo, hi;
                     approx_bounds(sv[u], nq, av[u], nq2, bv[u], beta, gamma, metric, nrm, &lo, &hi);
-                    const uint32_t k = float_key(hi);
-                    mymin = k < mymin ? k : mymin;
+                    uint32_t k = float_key(hi);
+#pragma unroll
+                    for (int j = 0; j < TOPT; ++j) {
+                        const uint32_t m = mk[j];
+                        mk[j] = k < m ? k : m;
+                        k = k < m ? m : k;
+                    }
                     if (keep_lo) lkeys[c] = lo != lo ? 0u : float_key(lo);
                 }
             }
         }
-        {
-            const uint32_t sorted = warp_sort_asc_u32(mymin, lane);
+        uint32_t* f_id = hkeys + (keep_lo ? L : 0);  // S0, in the key / tile area
+        uint32_t* f_lo = f_id + CAP;
+        uint32_t* f_hi = f_lo + CAP;
+        if constexpr (TOPT == 1) {
+            const uint32_t sorted = warp_sort_asc_u32(mk[0], lane);
             const uint32_t offer = __shfl_sync(0xffffffffu, sorted, (PP + NW - 1) / NW - 1);
             if (lane == 0) sh.mins[warp] = offer;
+        } else {
+            // the pool of thread minima, in the S0 upper-bound array until S0 fills it
+#pragma unroll
+            for (int j = 0; j < TOPT; ++j) f_hi[threadIdx.x * TOPT + j] = mk[j];
         }
         if (threadIdx.x == 0) {
             sh.count = 0;
@@ -404,10 +424,14 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         }
         __syncthreads();
         uint32_t tau0 = 0;
-        for (int w = 0; w < NW; ++w) tau0 = sh.mins[w] > tau0 ? sh.mins[w] : tau0;
-        uint32_t* f_id = hkeys + (keep_lo ? L : 0);  // S0, in the key / tile area
-        uint32_t* f_lo = f_id + CAP;
-        uint32_t* f_hi = f_lo + CAP;
+        if constexpr (TOPT == 1) {
+            for (int w = 0; w < NW; ++w) tau0 = sh.mins[w] > tau0 ? sh.mins[w] : tau0;
+        } else {
+            // every key of the pool is a distinct centroid's, and the pool holds at
+            // least min(L, NT * TOPT) >= PP real keys (a thread keeps all of its
+            // keys when L <= NT * TOPT), so at least PP centroids have hi <= tau0
+            tau0 = block_radix_select([&](int i) { return f_hi[i]; }, NT * TOPT, (unsigned)PP, sh);
+        }
         auto s0_add = [&](int c, uint32_t lk) {
             if (lk <= tau0) {
                 const unsigned slot = atomicAdd(&sh.count, 1u);
@@ -485,6 +509,10 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         }
         // else S0 overflows: the general path below recomputes every bound
     }
+    // T once the general path has it: the fallback then needs exact scores only for
+    // the centroids whose lower bound is within it
+    bool have_t = false;
+    uint32_t t_all = 0xffffffffu;
     if (!exact_all && !have) {
         if (cache) {
             for (int c = threadIdx.x; c < L; c += NT) {
@@ -506,6 +534,8 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
                     return float_key(hi);
                 },
                 L, (unsigned)PP, sh);
+        have_t = true;
+        t_all = tkey;
         // --- phase B: candidates whose lower bound is <= T (compared as keys,
         // so a NaN bound, key 0xffffffff for hi / mapped low for lo, is kept)
         if (threadIdx.x == 0) sh.count = 0;
@@ -646,10 +676,22 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         return;
     }
 
-    // --- fallback: exact scores for every centroid, selection by (score, id)
+    // --- fallback: exact scores, selection by (score, id).  With T known (more
+    // candidates than the candidate array holds) only the candidates are scored:
+    // every other centroid's exact score is above T, and at least P centroids
+    // (those with an upper bound <= T) score <= T, so +inf in their place changes
+    // nothing among the P smallest.
     __syncthreads();
-    for (int c = threadIdx.x; c < L; c += NT)
-        srow[c] = exact_score(qs, C + (int64_t)c * ldc, D, metric, nrm);
+    for (int c = threadIdx.x; c < L; c += NT) {
+        bool need = true;
+        if (have_t) {
+            float lo, hi;
+            bounds(c, &lo, &hi);
+            need = (lo != lo ? 0u : float_key(lo)) <= t_all;
+        }
+        srow[c] = need ? exact_score(qs, C + (int64_t)c * ldc, D, metric, nrm)
+                       : __int_as_float(0x7f800000);
+    }
     __syncthreads();
     const uint32_t kth =
         block_radix_select([&](int c) { return float_key(srow[c]); }, L, (unsigned)PP, sh);

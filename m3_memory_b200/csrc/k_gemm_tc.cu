@@ -218,7 +218,52 @@ __global__ void split3_kernel(const float* __restrict__ X, int64_t ld, int64_t n
     }
 }
 
+// One block per query row: the fp64 norm of its first d values (nrm_up >= ||x||
+// rounded up, nrm2 ~ ||x||^2) and, with q3, its [hi | hi | lo] bf16 operand row
+// (dims < dpad, zero padded to kp) -- the row norms and the query split in one
+// read of the row.
+__global__ void __launch_bounds__(128) query_prep_kernel(const float* __restrict__ X, int64_t ld,
+                                                         int d, int dpad, int kp,
+                                                         __nv_bfloat16* __restrict__ q3,
+                                                         float* __restrict__ nrm_up,
+                                                         float* __restrict__ nrm2) {
+    __shared__ double part[4];
+    const int64_t row = blockIdx.x;
+    const float* x = X + row * ld;
+    __nv_bfloat16* o = q3 ? q3 + row * (int64_t)kp : nullptr;
+    double acc = 0.0;
+    for (int i = threadIdx.x; i < dpad; i += blockDim.x) {
+        const float xv = x[i];
+        if (i < d) acc = fma((double)xv, (double)xv, acc);
+        if (o) {
+            const __nv_bfloat16 hi = __float2bfloat16_rn(xv);
+            o[i] = hi;
+            o[dpad + i] = hi;
+            o[2 * dpad + i] = __float2bfloat16_rn(xv - __bfloat162float(hi));
+        }
+    }
+    if (o)
+        for (int j = 3 * dpad + threadIdx.x; j < kp; j += blockDim.x) o[j] = __float2bfloat16_rn(0.f);
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const double t = (part[0] + part[1]) + (part[2] + part[3]);
+        if (nrm_up) nrm_up[row] = __double2float_ru(sqrt(t) * (1.0 + 1e-12));
+        if (nrm2) nrm2[row] = (float)t;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_query_prep(const float* X, int64_t ld, int64_t n, int d, int dpad, int kp,
+                              __nv_bfloat16* q3, float* nrm_up, float* nrm2, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (n > INT32_MAX) return cudaErrorInvalidValue;
+    query_prep_kernel<<<(unsigned)n, 128, 0, st>>>(X, ld, d, dpad, kp, q3, nrm_up, nrm2);
+    return cudaGetLastError();
+}
 
 int gemm_tc_kdim(int dpad) { return ((3 * dpad + TC_BK - 1) / TC_BK) * TC_BK; }
 

@@ -590,7 +590,6 @@ constexpr int PLAN_THREADS = 1024;
 
 __device__ __forceinline__ int items_of(int c, int gmax) { return (c + gmax - 1) / gmax; }
 
-constexpr int PLAN_CACHE = 8;  // lists per thread kept in registers (L <= 8192)
 
 // Inclusive block-wide sum of one value per thread (PLAN_THREADS threads).
 template <class T>
@@ -634,112 +633,199 @@ __device__ __forceinline__ int64_t tile_cost(int c, int nt, int tile_cap) {
     return nt > 1 && n <= (int64_t)tile_cap ? n : 0;
 }
 
-// One block: walks the clusters in list_order, assigns each its pair range and
-// its items (the pairs split into ceil(c / gmax) near-equal query groups; a
-// tiled list repeats each group once per row tile).  A list is tiled when its
+// The work list is planned in three steps over the positions of list_order
+// (longest list first): a grid gathers each position's pair count, rows and
+// tile cost; one block scans those arrays into pair, item and tile offsets
+// (deciding which lists are tiled); a grid writes every list's pair start and
+// its items.  A list's pairs split into ceil(c / gmax) near-equal query groups;
+// a tiled list repeats each group once per row tile.  A list is tiled when its
 // tile partial lists fit the tile region after those of the lists before it in
-// list_order that could fit on their own.  Each
-// thread takes a run of consecutive positions of list_order; up to PLAN_CACHE
-// per thread their loads are issued together and kept in registers.
-__global__ void __launch_bounds__(PLAN_THREADS) plan_items_kernel(
-    const int32_t* __restrict__ lcount, const int32_t* __restrict__ order, int L, int gmax,
-    const int32_t* __restrict__ list_len, int tile_rows, int tile_cap,
-    int32_t* __restrict__ lstart, ScanItem* __restrict__ items, int32_t* __restrict__ n_items) {
-    __shared__ int32_t wp[PLAN_THREADS / 32], wi[PLAN_THREADS / 32];
-    __shared__ int64_t wt[PLAN_THREADS / 32];
-    const int t = threadIdx.x;
-    const int per = (L + PLAN_THREADS - 1) / PLAN_THREADS;
-    const int b = t * per, e = min(L, b + per);
-    const bool cached = per <= PLAN_CACHE;
+// list_order that could fit on their own.
+struct PlanArrays {
+    int32_t* c;      // [L] pairs of the list at each position
+    int32_t* len;    // [L] its rows (0 when not tiling)
+    int32_t* cost;   // [L] tile partial lists it asks for, then the tiles it gets
+    int32_t* pair0;  // [L] its first pair
+    int32_t* item0;  // [L] its first item
+    int32_t* tile0;  // [L] its first tile partial list (tiled lists)
+};
+
+__global__ void plan_gather_kernel(const int32_t* __restrict__ lcount,
+                                   const int32_t* __restrict__ order,
+                                   const int32_t* __restrict__ list_len, int L, int gmax,
+                                   int tile_rows, int tile_cap, PlanArrays pa) {
     const bool tiled = tile_rows > 0 && list_len;
-    int32_t lo[PLAN_CACHE], lc[PLAN_CACHE], ln[PLAN_CACHE];
-    int32_t np = 0, ni = 0;
+    for (int pos = blockIdx.x * blockDim.x + threadIdx.x; pos < L; pos += gridDim.x * blockDim.x) {
+        const int l = order[pos];
+        const int c = lcount[l];
+        const int len = tiled ? list_len[l] : 0;
+        pa.c[pos] = c;
+        pa.len[pos] = len;
+        pa.cost[pos] = (int32_t)tile_cost(c, tiles_of(c, len, tile_rows, gmax), tile_cap);
+    }
+}
+
+// Inclusive sum over the lanes of a warp.
+template <class T>
+__device__ __forceinline__ T warp_incl_sum(T v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const T u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    return v;
+}
+
+// Exclusive offsets of the warps' totals (one value per warp in tot), in place.
+template <class T>
+__device__ __forceinline__ void plan_warp_offsets(T* tot, int warp, int lane) {
+    __syncthreads();
+    if (warp == 0) {
+        const T v = lane < PLAN_THREADS / 32 ? tot[lane] : T(0);
+        const T incl = warp_incl_sum(v, lane);
+        if (lane < PLAN_THREADS / 32) tot[lane] = incl - v;
+    }
+    __syncthreads();
+}
+
+// One block.  Warp w takes rows of 32 consecutive positions (lane-contiguous, so
+// every load is coalesced), PLAN_ROWS rows loaded together; prefixes come from
+// warp scans, carried from row to row and offset by the scanned warp totals.
+constexpr int PLAN_ROWS = 8;
+
+__global__ void __launch_bounds__(PLAN_THREADS) plan_scan_kernel(int L, int gmax, int tile_rows,
+                                                                 int tile_cap, PlanArrays pa,
+                                                                 int32_t* __restrict__ n_items) {
+    constexpr int NW = PLAN_THREADS / 32;
+    __shared__ int32_t wp[NW], wi[NW];
+    __shared__ int64_t wt[NW];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rows = (L + 32 * NW - 1) / (32 * NW);  // rows per warp
+    const int base = warp * rows * 32;
+    auto pos_of = [&](int r) { return base + r * 32 + lane; };
+    // pass 1: the warp's pair and tile-cost totals
+    int32_t np = 0;
     int64_t tc = 0;
-    if (cached) {
+    for (int r0 = 0; r0 < rows; r0 += PLAN_ROWS) {
+        int32_t cv[PLAN_ROWS], kv[PLAN_ROWS];
 #pragma unroll
-        for (int j = 0; j < PLAN_CACHE; ++j) lo[j] = b + j < e ? order[b + j] : 0;
-#pragma unroll
-        for (int j = 0; j < PLAN_CACHE; ++j) {
-            lc[j] = b + j < e ? lcount[lo[j]] : 0;
-            ln[j] = b + j < e && tiled ? list_len[lo[j]] : 0;
+        for (int u = 0; u < PLAN_ROWS; ++u) {
+            const int p = pos_of(r0 + u);
+            const bool in = r0 + u < rows && p < L;
+            cv[u] = in ? pa.c[p] : 0;
+            kv[u] = in ? pa.cost[p] : 0;
         }
 #pragma unroll
-        for (int j = 0; j < PLAN_CACHE; ++j) {
-            np += lc[j];
-            tc += tile_cost(lc[j], tiles_of(lc[j], ln[j], tile_rows, gmax), tile_cap);
-        }
-    } else {
-        for (int i = b; i < e; ++i) {
-            const int l = order[i];
-            const int c = lcount[l];
-            np += c;
-            if (tiled) tc += tile_cost(c, tiles_of(c, list_len[l], tile_rows, gmax), tile_cap);
+        for (int u = 0; u < PLAN_ROWS; ++u) {
+            np += cv[u];
+            tc += kv[u];
         }
     }
-    const int32_t pinc = plan_block_scan<int32_t>(np, wp);
-    const int64_t tinc = plan_block_scan<int64_t>(tc, wt);
-    // the lists of this thread that are tiled: their cost ends inside the region
-    int64_t trun = tinc - tc;
-    auto tiles_taken = [&](int c, int len) -> int {
-        const int nt = tiled ? tiles_of(c, len, tile_rows, gmax) : 1;
-        const int64_t cost = tile_cost(c, nt, tile_cap);
-        trun += cost;
-        return (cost > 0 && trun <= (int64_t)tile_cap) ? nt : 1;
-    };
-    int32_t ntk[PLAN_CACHE];
-    if (cached) {
 #pragma unroll
-        for (int j = 0; j < PLAN_CACHE; ++j) {
-            ntk[j] = tiles_taken(lc[j], ln[j]);
-            ni += items_of(lc[j], gmax) * ntk[j];  // 0 for c = 0
+    for (int o = 16; o > 0; o >>= 1) {
+        np += __shfl_xor_sync(0xffffffffu, np, o);
+        tc += __shfl_xor_sync(0xffffffffu, tc, o);
+    }
+    if (lane == 0) {
+        wp[warp] = np;
+        wt[warp] = tc;
+    }
+    plan_warp_offsets(wp, warp, lane);
+    plan_warp_offsets(wt, warp, lane);
+    // pass 2: pair and tile offsets, the tiling decision, the item counts
+    int32_t pcar = wp[warp];
+    int64_t tcar = wt[warp];
+    int32_t ni = 0;
+    for (int r0 = 0; r0 < rows; r0 += PLAN_ROWS) {
+        int32_t cv[PLAN_ROWS], kv[PLAN_ROWS], lv[PLAN_ROWS];
+#pragma unroll
+        for (int u = 0; u < PLAN_ROWS; ++u) {
+            const int p = pos_of(r0 + u);
+            const bool in = r0 + u < rows && p < L;
+            cv[u] = in ? pa.c[p] : 0;
+            kv[u] = in ? pa.cost[p] : 0;
+            lv[u] = in ? pa.len[p] : 0;
         }
-    } else {
-        for (int i = b; i < e; ++i) {
-            const int l = order[i];
-            const int c = lcount[l];
-            ni += items_of(c, gmax) * tiles_taken(c, tiled ? list_len[l] : 0);
+#pragma unroll
+        for (int u = 0; u < PLAN_ROWS; ++u) {
+            const int p = pos_of(r0 + u);
+            const bool in = r0 + u < rows && p < L;
+            const int32_t pin = warp_incl_sum(cv[u], lane);
+            const int64_t tin = warp_incl_sum((int64_t)kv[u], lane);
+            const int64_t tend = tcar + tin;  // tile lists up to and including this list
+            const bool taken = kv[u] > 0 && tend <= (int64_t)tile_cap;
+            const int nt = taken ? tiles_of(cv[u], lv[u], tile_rows, gmax) : 1;
+            if (in) {
+                pa.pair0[p] = pcar + pin - cv[u];
+                pa.tile0[p] = taken ? (int32_t)(tend - kv[u]) : 0;
+                pa.cost[p] = nt;
+            }
+            ni += items_of(cv[u], gmax) * nt;
+            pcar += __shfl_sync(0xffffffffu, pin, 31);
+            tcar += __shfl_sync(0xffffffffu, tin, 31);
         }
     }
-    const int32_t iinc = plan_block_scan<int32_t>(ni, wi);
-    int32_t pbase = pinc - np, ibase = iinc - ni;
-    int64_t tbase = tinc - tc;  // tile partial index of the next tiled list
-    auto place = [&](int l, int c, int len, int nt) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ni += __shfl_xor_sync(0xffffffffu, ni, o);
+    if (lane == 0) wi[warp] = ni;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int32_t total = 0;
+        for (int w = 0; w < NW; ++w) total += wi[w];
+        *n_items = total;
+    }
+    plan_warp_offsets(wi, warp, lane);
+    // pass 3: item offsets
+    int32_t icar = wi[warp];
+    for (int r0 = 0; r0 < rows; r0 += PLAN_ROWS) {
+        int32_t cv[PLAN_ROWS], nv[PLAN_ROWS];
+#pragma unroll
+        for (int u = 0; u < PLAN_ROWS; ++u) {
+            const int p = pos_of(r0 + u);
+            const bool in = r0 + u < rows && p < L;
+            cv[u] = in ? pa.c[p] : 0;
+            nv[u] = in ? pa.cost[p] : 1;
+        }
+#pragma unroll
+        for (int u = 0; u < PLAN_ROWS; ++u) {
+            const int p = pos_of(r0 + u);
+            const int32_t v = items_of(cv[u], gmax) * nv[u];
+            const int32_t inc = warp_incl_sum(v, lane);
+            if (r0 + u < rows && p < L) pa.item0[p] = icar + inc - v;
+            icar += __shfl_sync(0xffffffffu, inc, 31);
+        }
+    }
+}
+
+__global__ void plan_place_kernel(const int32_t* __restrict__ order, int L, int gmax,
+                                  int tile_rows, PlanArrays pa, int32_t* __restrict__ lstart,
+                                  ScanItem* __restrict__ items) {
+    for (int pos = blockIdx.x * blockDim.x + threadIdx.x; pos < L; pos += gridDim.x * blockDim.x) {
+        const int l = order[pos];
+        const int c = pa.c[pos];
+        const int pbase = pa.pair0[pos];
         lstart[l] = pbase;
+        if (c <= 0) continue;
         const int n = items_of(c, gmax);
-        const int64_t cost = tiled ? tile_cost(c, tiles_of(c, len, tile_rows, gmax), tile_cap) : 0;
+        const int nt = pa.cost[pos];
+        const int ibase = pa.item0[pos];
         // tile-major: the query groups of one tile are neighbours in the work list,
         // so they run at the same time and share the tile's rows in L2
         int pb = pbase;
         for (int j = 0; j < n; ++j) {
             const int sz = c / n + (j < c % n ? 1 : 0);
             if (nt > 1) {
+                const int len = pa.len[pos];
+                const int32_t grp0 = pa.tile0[pos] + (pb - pbase) * nt;
                 for (int r = 0; r < nt; ++r)
-                    items[ibase + r * n + j] =
-                        ScanItem{l, pb, sz, r * tile_rows, min(tile_rows, len - r * tile_rows),
-                                 (int32_t)(tbase + (int64_t)(pb - pbase) * nt), r, nt};
+                    items[ibase + r * n + j] = ScanItem{
+                        l, pb, sz, r * tile_rows, min(tile_rows, len - r * tile_rows), grp0, r, nt};
             } else {
                 items[ibase + j] = ScanItem{l, pb, sz, 0, -1, -1, 0, 0};
             }
             pb += sz;
         }
-        pbase += c;
-        ibase += n * nt;
-        tbase += cost;
-    };
-    if (cached) {
-#pragma unroll
-        for (int j = 0; j < PLAN_CACHE; ++j)
-            if (b + j < e) place(lo[j], lc[j], ln[j], ntk[j]);
-    } else {
-        trun = tinc - tc;
-        for (int i = b; i < e; ++i) {
-            const int l = order[i];
-            const int c = lcount[l];
-            const int len = tiled ? list_len[l] : 0;
-            place(l, c, len, tiles_taken(c, len));
-        }
     }
-    if (t == PLAN_THREADS - 1) *n_items = iinc;
 }
 
 __global__ void pair_scatter_kernel(const int32_t* __restrict__ probes, int nq, int P, int L,
@@ -766,9 +852,10 @@ cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
                                   const int32_t* list_order, int gmax, int32_t* lcount,
                                   int32_t* lstart, int32_t* lcursor, ScanItem* items,
                                   int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
-                                  cudaStream_t st, const int32_t* skip_len,
+                                  int32_t* plan, cudaStream_t st, const int32_t* skip_len,
                                   const int32_t* list_len, int tile_rows, int tile_cap) {
-    if (tile_rows < 0 || tile_rows % 128 || tile_cap < 0 || (tile_rows > 0 && !list_len))
+    if (tile_rows < 0 || tile_rows % 128 || tile_cap < 0 || (tile_rows > 0 && !list_len) ||
+        (L > 0 && !plan))
         return cudaErrorInvalidValue;
     cudaError_t e;
     if ((e = cudaMemsetAsync(lcount, 0, sizeof(int32_t) * (size_t)L, st)) != cudaSuccess) return e;
@@ -776,8 +863,17 @@ cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
     const int64_t n = (int64_t)nq * P;
     const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
     if (n > 0) probe_hist_kernel<<<blocks, 256, 0, st>>>(probes, n, L, skip_len, lcount);
-    plan_items_kernel<<<1, PLAN_THREADS, 0, st>>>(lcount, list_order, L, gmax, list_len,
-                                                  tile_rows, tile_cap, lstart, items, n_items);
+    if (L > 0) {
+        const PlanArrays pa{plan, plan + L, plan + 2 * (size_t)L, plan + 3 * (size_t)L,
+                            plan + 4 * (size_t)L, plan + 5 * (size_t)L};
+        const int pg = (int)std::min<int64_t>((L + 255) / 256, 1184);
+        plan_gather_kernel<<<pg, 256, 0, st>>>(lcount, list_order, list_len, L, gmax, tile_rows,
+                                               tile_cap, pa);
+        plan_scan_kernel<<<1, PLAN_THREADS, 0, st>>>(L, gmax, tile_rows, tile_cap, pa, n_items);
+        plan_place_kernel<<<pg, 256, 0, st>>>(list_order, L, gmax, tile_rows, pa, lstart, items);
+    } else if ((e = cudaMemsetAsync(n_items, 0, sizeof(int32_t), st)) != cudaSuccess) {
+        return e;
+    }
     if (n > 0)
         pair_scatter_kernel<<<blocks, 256, 0, st>>>(probes, nq, P, L, skip_len, lstart, lcount,
                                                     lcursor, pair_q, pair_slot);

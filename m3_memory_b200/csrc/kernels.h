@@ -31,6 +31,10 @@ int gemm_tc_box_rows_b();
 int gemm_tc_box_k();
 cudaError_t launch_split3(const float* X, int64_t ld, int64_t n, int dpad, int kp,
                           __nv_bfloat16* out, bool centroid_side, cudaStream_t st);
+// Row norms of n query rows (as launch_row_norms) and, with q3, their query-side
+// split operand rows (as launch_split3), from one read of each row.
+cudaError_t launch_query_prep(const float* X, int64_t ld, int64_t n, int d, int dpad, int kp,
+                              __nv_bfloat16* q3, float* nrm_up, float* nrm2, cudaStream_t st);
 cudaError_t launch_gemm_tc(const CUtensorMap& mapA, const CUtensorMap& mapB, float* S, int64_t lds,
                            int M, int N, int kp, int* err, cudaStream_t st);
 
@@ -112,11 +116,12 @@ cudaError_t launch_list_scan_tc(const RowMaps& maps, const ScanArgs& a, bool bf1
 // probed by at most two query groups is scanned in row tiles of tile_rows, each
 // group once per tile, as long as its tile partial lists fit the tile region of
 // tile_cap lists (longest lists first); list_len gives the rows per list.
+// plan: scratch of 6 L int32.
 cudaError_t launch_build_worklist(const int32_t* probes, int nq, int P, int L,
                                   const int32_t* list_order, int gmax, int32_t* lcount,
                                   int32_t* lstart, int32_t* lcursor, ScanItem* items,
                                   int32_t* n_items, int32_t* pair_q, int32_t* pair_slot,
-                                  cudaStream_t st, const int32_t* skip_len = nullptr,
+                                  int32_t* plan, cudaStream_t st, const int32_t* skip_len = nullptr,
                                   const int32_t* list_len = nullptr, int tile_rows = 0,
                                   int tile_cap = 0);
 
