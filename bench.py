@@ -919,6 +919,7 @@ def run_config3(args, rank, world, local_rank):
         eng.set_profiling(True)
         for Bs in (1, 64):
             st_s = {}
+            torch.cuda.nvtx.range_push(f"small{Bs}")  # ncu --nvtx-include "small1/" selects these
             for i in range(10):
                 eng.search_device(1, Qd[i * Bs].data_ptr(), Bs, K3, C3_NPROBES[0], ids_d.data_ptr(),
                                   sc_d.data_ptr(), cnt_d.data_ptr())
@@ -926,6 +927,7 @@ def run_config3(args, rank, world, local_rank):
                 for key in ("ms_prep", "ms_coarse_gemm", "ms_select", "ms_worklist", "ms_scan",
                             "ms_merge", "ms_total"):
                     st_s.setdefault(key[3:], []).append(p[key])
+            torch.cuda.nvtx.range_pop()
             small[f"nprobe{C3_NPROBES[0]}_batch{Bs}"] = {
                 k: round(statistics.median(v), 4) for k, v in st_s.items()}
         eng.set_profiling(False)

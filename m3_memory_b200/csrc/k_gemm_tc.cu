@@ -221,9 +221,15 @@ __global__ void split3_kernel(const float* __restrict__ X, int64_t ld, int64_t n
 // One block per query row: the fp64 norm of its first d values (nrm_up >= ||x||
 // rounded up, nrm2 ~ ||x||^2) and, with q3, its [hi | hi | lo] bf16 operand row
 // (dims < dpad, zero padded to kp) -- the row norms and the query split in one
-// read of the row.
+// read of the row.  Four dims per thread (16-byte loads, 8-byte stores) when the
+// rows are 16-byte aligned, else one.
+__device__ __forceinline__ uint32_t bf16_pair(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 __global__ void __launch_bounds__(128) query_prep_kernel(const float* __restrict__ X, int64_t ld,
-                                                         int d, int dpad, int kp,
+                                                         int d, int dpad, int kp, int vec,
                                                          __nv_bfloat16* __restrict__ q3,
                                                          float* __restrict__ nrm_up,
                                                          float* __restrict__ nrm2) {
@@ -232,14 +238,34 @@ __global__ void __launch_bounds__(128) query_prep_kernel(const float* __restrict
     const float* x = X + row * ld;
     __nv_bfloat16* o = q3 ? q3 + row * (int64_t)kp : nullptr;
     double acc = 0.0;
-    for (int i = threadIdx.x; i < dpad; i += blockDim.x) {
-        const float xv = x[i];
-        if (i < d) acc = fma((double)xv, (double)xv, acc);
-        if (o) {
-            const __nv_bfloat16 hi = __float2bfloat16_rn(xv);
-            o[i] = hi;
-            o[dpad + i] = hi;
-            o[2 * dpad + i] = __float2bfloat16_rn(xv - __bfloat162float(hi));
+    if (vec) {
+        for (int i = 4 * threadIdx.x; i < dpad; i += 4 * blockDim.x) {
+            const float4 v = *reinterpret_cast<const float4*>(x + i);
+            const float xv[4] = {v.x, v.y, v.z, v.w};
+            float lo[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (i + u < d) acc = fma((double)xv[u], (double)xv[u], acc);
+                lo[u] = xv[u] - __bfloat162float(__float2bfloat16_rn(xv[u]));
+            }
+            if (o) {
+                const uint2 hi = make_uint2(bf16_pair(xv[0], xv[1]), bf16_pair(xv[2], xv[3]));
+                *reinterpret_cast<uint2*>(o + i) = hi;
+                *reinterpret_cast<uint2*>(o + dpad + i) = hi;
+                *reinterpret_cast<uint2*>(o + 2 * dpad + i) =
+                    make_uint2(bf16_pair(lo[0], lo[1]), bf16_pair(lo[2], lo[3]));
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < dpad; i += blockDim.x) {
+            const float xv = x[i];
+            if (i < d) acc = fma((double)xv, (double)xv, acc);
+            if (o) {
+                const __nv_bfloat16 hi = __float2bfloat16_rn(xv);
+                o[i] = hi;
+                o[dpad + i] = hi;
+                o[2 * dpad + i] = __float2bfloat16_rn(xv - __bfloat162float(hi));
+            }
         }
     }
     if (o)
@@ -261,7 +287,13 @@ cudaError_t launch_query_prep(const float* X, int64_t ld, int64_t n, int d, int 
                               __nv_bfloat16* q3, float* nrm_up, float* nrm2, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
     if (n > INT32_MAX) return cudaErrorInvalidValue;
-    query_prep_kernel<<<(unsigned)n, 128, 0, st>>>(X, ld, d, dpad, kp, q3, nrm_up, nrm2);
+    // 16-byte rows: every row start and dpad a multiple of 4 floats (then the
+    // split row's segments start on 8-byte boundaries too, kp being a multiple of 64)
+    const int vec = (ld % 4 == 0 && dpad % 4 == 0 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(q3) & 7u) == 0 && kp % 4 == 0)
+                        ? 1
+                        : 0;
+    query_prep_kernel<<<(unsigned)n, 128, 0, st>>>(X, ld, d, dpad, kp, vec, q3, nrm_up, nrm2);
     return cudaGetLastError();
 }
 
