@@ -631,7 +631,9 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         const int nex = (int)sh.nex;
         float* stage = stage_all + warp * SEL_STAGE;
         for (int r0 = 0; r0 < nex; r0 += NT) {
-            // up to NT candidates per round, G = ceil(n / NW) per warp
+            // up to NT candidates per round, G = ceil(n / NW) per warp: with the blocks
+            // of a batch resident in one wave the kernel's time is a block's latency,
+            // which the shortest per-warp share (and the widest chunks) keeps lowest
             const int n = nex - r0 < NT ? nex - r0 : NT;
             const int G = (n + NW - 1) / NW;
             if (warp * G >= n) continue;  // warp-uniform: nothing for this warp

@@ -1116,13 +1116,24 @@ __device__ __forceinline__ float l2_chunk(const uint4* __restrict__ src, int ng1
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            float v[8];
+            float v[8], qv[8];
             unpack16(cur[u], v, BF);
+            // the group's query values by 16-byte broadcast reads (every lane reads
+            // the same address); values past n are read but never summed
+            const float4* q4 = reinterpret_cast<const float4*>(qs + (g0 + u) * EPG);
+#pragma unroll
+            for (int h4 = 0; h4 < EPG / 4; ++h4) {
+                const float4 a = q4[h4];
+                qv[4 * h4] = a.x;
+                qv[4 * h4 + 1] = a.y;
+                qv[4 * h4 + 2] = a.z;
+                qv[4 * h4 + 3] = a.w;
+            }
 #pragma unroll
             for (int h = 0; h < EPG; ++h) {
                 const int i = (g0 + u) * EPG + h;
                 if (i < n) {
-                    const float df = __fsub_rn(qs[i], v[h]);
+                    const float df = __fsub_rn(qv[h], v[h]);
                     e = __fadd_rn(e, __fmul_rn(df, df));
                 }
             }
@@ -1139,7 +1150,7 @@ __global__ void __launch_bounds__(RS_MAX) rescore_l2_kernel(MergeRescore rs,
                                                            int k, int64_t* __restrict__ out_ids,
                                                            float* __restrict__ out_scores,
                                                            const int32_t* __restrict__ out_counts) {
-    __shared__ float qs[RS_QCH];
+    __shared__ __align__(16) float qs[RS_QCH];
     __shared__ unsigned long long key[RS_MAX];
     __shared__ int64_t wrow[RS_MAX];
     const int q = blockIdx.x, j = threadIdx.x;
