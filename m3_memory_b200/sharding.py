@@ -44,7 +44,34 @@ batches) are added.
 """
 from __future__ import annotations
 
+import datetime
+
 import numpy as np
+
+
+class ShardError(RuntimeError):
+    """An exchange of a sharded search did not complete: a peer rank left, failed
+    or did not join within the limit.  The reference has no multi-GPU path; its
+    writer-thread failures end the process (AgentMemory/M3/src/m3_async.cpp:364)."""
+
+
+def collective(op, timeout_s, what, *args, **kwargs):
+    """Runs one torch.distributed collective.  Without a limit it is enqueued as
+    usual (ordered on the current stream, the host does not wait).  With
+    timeout_s the host waits for it, at most that long, and a peer that does not
+    join (or a transport error) raises ShardError naming the exchange instead of
+    blocking the rank -- the host-side limit on every exchange of the search."""
+    if timeout_s is None:
+        return op(*args, **kwargs)
+    try:
+        work = op(*args, async_op=True, **kwargs)
+        done = work.wait(timeout=datetime.timedelta(seconds=timeout_s))
+    except Exception as ex:  # noqa: BLE001 -- every transport error becomes a ShardError
+        raise ShardError(f"{what}: the exchange did not complete within {timeout_s} s "
+                         f"({type(ex).__name__}: {ex})") from ex
+    if done is False:
+        raise ShardError(f"{what}: the exchange did not complete within {timeout_s} s")
+    return None
 
 
 def torch_dtype(name):
@@ -80,16 +107,22 @@ class ShardedSearch:
     ``engine`` is the rank's ``cabi.Engine`` holding all centroids and the
     lists this rank owns; ``group`` a ``torch.distributed`` process group over
     the ranks (NCCL on GPUs).  Buffers are allocated once for batches of up to
-    ``max_q`` queries.
+    ``max_q`` queries.  With ``timeout_s`` the host waits for every exchange, at
+    most that long, and raises ``ShardError`` when a peer left, failed or did not
+    join (without it the exchanges are only enqueued, and a missing peer holds the
+    rank until the process group's own timeout).
     """
 
     def __init__(self, engine, index_id: int, k: int, max_q: int, world: int, device,
                  group=None, coarse_index_id=None, owner=None, rank: int = 0,
-                 max_nprobe: int = 256, split_coarse: bool = False):
+                 max_nprobe: int = 256, split_coarse: bool = False,
+                 timeout_s: float | None = None):
         import torch
 
         self.engine, self.index_id, self.k, self.world = engine, index_id, k, world
         self.group = group
+        # host-side limit on every exchange (None: enqueue and do not wait)
+        self.timeout_s = timeout_s
         self.coarse_index_id = coarse_index_id
         self.split_coarse = split_coarse and coarse_index_id is None
         self.rank = rank
@@ -205,7 +238,8 @@ class ShardedSearch:
         # one all-gather of the answer records, merged where they land
         R = self.record_bytes(nq)
         g = self.g_rec[:self.world * R]
-        dist.all_gather_into_tensor(g, self.rec[:R], group=self.group)
+        collective(dist.all_gather_into_tensor, self.timeout_s, "top-k exchange", g,
+                   self.rec[:R], group=self.group)
         self.engine.merge_shards_packed_device(g.data_ptr(), self.world, nq, k, R,
                                                self.ids_offset(nq), self.out_ids.data_ptr(),
                                                self.out_sc.data_ptr(), self.out_cnt.data_ptr(), s)
@@ -277,13 +311,15 @@ class ShardedSearch:
         if P > o["P"]:
             raise ValueError(f"nprobe {P} exceeds max_nprobe={o['P']}")
         q_all = o["q_all"][:W * B]
-        dist.all_gather_into_tensor(q_all, q, group=self.group)
+        collective(dist.all_gather_into_tensor, self.timeout_s, "batch exchange", q_all, q,
+                   group=self.group)
         self._mark("query_exchange")
         loc = o["loc"].view(-1)[:B * P].view(B, P)
         self.engine.select_probes_device(self.index_id, q.data_ptr(), B, P, loc.data_ptr(), s)
         self._mark("coarse")
         probes = o["probes"].view(-1)[:W * B * P].view(W * B, P)
-        dist.all_gather_into_tensor(probes, loc, group=self.group)
+        collective(dist.all_gather_into_tensor, self.timeout_s, "probe exchange", probes, loc,
+                   group=self.group)
         self._mark("probe_exchange")
         ids, sc, cnt = o["ids"][:W * B], o["sc"][:W * B], o["cnt"][:W * B]
         self.engine.search_probes_device(self.index_id, q_all.data_ptr(), W * B, k,
@@ -296,7 +332,8 @@ class ShardedSearch:
         send[:, :B * k * 4].view(torch.float32).copy_(sc.view(W, B * k))
         send[:, off:off + B * k * 8].view(torch.int64).copy_(ids.view(W, B * k))
         recv = o["recv"][:W * R]
-        dist.all_to_all_single(recv, o["send"][:W * R], group=self.group)
+        collective(dist.all_to_all_single, self.timeout_s, "top-k exchange", recv,
+                   o["send"][:W * R], group=self.group)
         self.engine.merge_shards_packed_device(recv.data_ptr(), W, B, k, R, off,
                                                self.out_ids.data_ptr(), self.out_sc.data_ptr(),
                                                self.out_cnt.data_ptr(), s)
@@ -325,7 +362,8 @@ class ShardedSearch:
         self._mark("coarse")
         probes = self.sp_all.view(-1)[:self.world * chunk * P].view(self.world * chunk, P)
         if self.world > 1:
-            dist.all_gather_into_tensor(probes, loc, group=self.group)
+            collective(dist.all_gather_into_tensor, self.timeout_s, "probe exchange", probes, loc,
+                       group=self.group)
         else:
             probes.copy_(loc)
         self._mark("probe_exchange")
@@ -361,8 +399,10 @@ class ShardedSearch:
         if self.world > 1:
             g_sc = self.gc_sc.view(-1)[:self.world * nq * P].view(self.world, nq, P)
             g_id = self.gc_id.view(-1)[:self.world * nq * P].view(self.world, nq, P)
-            dist.all_gather_into_tensor(g_sc, cand_sc, group=self.group)
-            dist.all_gather_into_tensor(g_id, cand_id, group=self.group)
+            collective(dist.all_gather_into_tensor, self.timeout_s, "candidate exchange", g_sc,
+                       cand_sc, group=self.group)
+            collective(dist.all_gather_into_tensor, self.timeout_s, "candidate exchange", g_id,
+                       cand_id, group=self.group)
         else:
             g_sc, g_id = cand_sc.unsqueeze(0), cand_id.unsqueeze(0)
         top_id = self.top_id.view(-1)[:nq * P].view(nq, P)

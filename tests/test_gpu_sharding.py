@@ -325,7 +325,7 @@ for name, kw in (("replicated", {}), ("sharded", dict(coarse_index_id=2, owner=o
     out[name + "_ids"], out[name + "_sc"], out[name + "_cnt"] = (
         ids.cpu().numpy(), sc.cpu().numpy(), cnt.cpu().numpy())
 B = len(c["Q"]) // world  # serving form: each rank brings its own half of the queries
-ss = ShardedSearch(e, 1, 10, B, world, "cuda", rank=rank)
+ss = ShardedSearch(e, 1, 10, B, world, "cuda", rank=rank, timeout_s=60.0)  # host-side limit
 ids, sc, cnt = ss.search_own_batch(q[rank * B:(rank + 1) * B].contiguous(), 12)
 torch.cuda.synchronize()
 g = [torch.empty_like(t) for t in (ids, sc, cnt) for _ in range(world)]

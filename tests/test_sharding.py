@@ -255,3 +255,73 @@ def test_own_batch_exchange_equals_unsharded(oracle_mod, metric, normalized):
                                         normalized, c["k"], c["nprobe"])
         compare_search(merged, want, exact=True)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _limit_rank_main(rank, world, port, mode, out):
+    """Rank 0 runs one exchange with a 2 s host-side limit; rank 1 joins
+    ("join"), leaves the job before it ("exit"), or stays but never joins
+    ("stall")."""
+    sys.path.insert(0, str(ROOT))
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from m3_memory_b200.sharding import ShardError, collective
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=6))
+    src = torch.full((4,), float(rank + 1))
+    dst = torch.empty(4 * world)
+    if rank == 1 and mode == "exit":
+        os._exit(0)  # leaves without joining and without a clean shutdown
+    if rank == 1 and mode == "stall":
+        time.sleep(12)
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        collective(dist.all_gather_into_tensor, 2.0, "probe exchange", dst, src)
+        res = ("ok", dst.tolist(), time.monotonic() - t0)
+    except ShardError as ex:
+        res = ("shard_error", str(ex), time.monotonic() - t0)
+    except Exception as ex:  # anything else fails the test
+        res = ("other", repr(ex), time.monotonic() - t0)
+    if rank == 0:
+        out.put(res)
+        out.close()
+        out.join_thread()  # the result is in the pipe before the process ends
+    if res[0] == "ok":
+        dist.destroy_process_group()
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["join", "exit", "stall"])
+def test_exchange_limit_turns_a_missing_peer_into_an_error(mode):
+    """The host-side limit on a sharded search's exchanges (ShardedSearch's
+    timeout_s): with every rank present the exchange completes; a rank that left
+    or never joins makes the waiting rank raise ShardError within the limit (or
+    the process group's 6 s timeout), not block.  gloo ranks on CPU; no GPU."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_limit_rank_main, args=(r, world, port, mode, out))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        status, detail, elapsed = out.get(timeout=60)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    if mode == "join":
+        assert status == "ok", detail
+        assert detail == [1.0] * 4 + [2.0] * 4
+    else:
+        assert status == "shard_error", detail
+        assert "probe exchange" in detail
+        assert elapsed < 15, elapsed
