@@ -152,6 +152,16 @@ bool use_tc_gemm() {
 float coarse_gemm(const float* A, int64_t lda, const __nv_bfloat16* A3, const float* B,
                   int64_t ldb, const __nv_bfloat16* B3, float* S, int64_t lds, int M, int N,
                   int dpad, int* err, cudaStream_t st) {
+    // a few rows: a GEMV over every SM beats the tiled GEMMs (which give one row
+    // tile a few CTAs), with the SIMT GEMM's error bound
+    if (gemv_fits(A, lda, B, ldb, M, dpad)) {
+        int dev = 0, sms = 148;
+        M3G_CK(cudaGetDevice(&dev));
+        M3G_CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        launch_gemv_nt(A, lda, B, ldb, S, lds, M, N, dpad, sms, st);
+        M3G_CK(cudaGetLastError());
+        return sgemm_error_beta(dpad);
+    }
     if (use_tc_gemm()) {
         const int kp = gemm_tc_kdim(dpad);
         CUtensorMap ma, mb;

@@ -157,6 +157,70 @@ void launch_sgemm_nt(const float* A, int64_t lda, const float* B, int64_t ldb, f
 float sgemm_error_beta(int K) { return (float)(K + 2) * 5.9604645e-8f * 1.01f; }
 
 // ---------------------------------------------------------------------------
+// GEMV for a few rows of A (tiny query batches): S[m][n] = sum_k A[m][k] B[n][k]
+// for m < M <= GEMV_MAX_M.  A is staged in shared memory; each warp takes one row
+// of B at a time with 16-byte loads along k, keeps the M dot products per lane
+// and reduces them over the warp.  fp32 FMAs in another order than the GEMM's, so
+// the same bound holds (sgemm_error_beta: any summation order, with or without
+// FMA).  The whole grid streams B once, where the tiled GEMMs give a single
+// row of A a few CTAs.
+// ---------------------------------------------------------------------------
+constexpr int GEMV_MAX_M = 8;
+constexpr int GEMV_SMEM_MAX = 48 * 1024;
+
+__global__ void __launch_bounds__(256) gemv_nt_kernel(const float* __restrict__ A, int64_t lda,
+                                                      const float* __restrict__ B, int64_t ldb,
+                                                      float* __restrict__ S, int64_t lds, int M,
+                                                      int N, int K) {
+    extern __shared__ __align__(16) float as[];  // [M][K]
+    for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
+        const int m = i / K, k = i - m * K;
+        as[i] = A[(int64_t)m * lda + k];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int k4n = K / 4;
+    for (int n = blockIdx.x * nw + warp; n < N; n += gridDim.x * nw) {
+        const float4* b = reinterpret_cast<const float4*>(B + (int64_t)n * ldb);
+        float acc[GEMV_MAX_M];
+#pragma unroll
+        for (int m = 0; m < GEMV_MAX_M; ++m) acc[m] = 0.f;
+        for (int k4 = lane; k4 < k4n; k4 += 32) {
+            const float4 v = __ldg(b + k4);
+#pragma unroll
+            for (int m = 0; m < GEMV_MAX_M; ++m) {
+                if (m < M) {
+                    const float4 a = reinterpret_cast<const float4*>(as + m * K)[k4];
+                    acc[m] = fmaf(a.x, v.x, acc[m]);
+                    acc[m] = fmaf(a.y, v.y, acc[m]);
+                    acc[m] = fmaf(a.z, v.z, acc[m]);
+                    acc[m] = fmaf(a.w, v.w, acc[m]);
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < GEMV_MAX_M; ++m) {
+            float v = acc[m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && m < M) S[(int64_t)m * lds + n] = v;
+        }
+    }
+}
+
+bool gemv_fits(const float* A, int64_t lda, const float* B, int64_t ldb, int M, int K) {
+    return M >= 1 && M <= GEMV_MAX_M && K % 4 == 0 && ldb % 4 == 0 &&
+           (reinterpret_cast<uintptr_t>(B) & 15u) == 0 && (size_t)M * K * 4 <= GEMV_SMEM_MAX;
+}
+
+void launch_gemv_nt(const float* A, int64_t lda, const float* B, int64_t ldb, float* S,
+                    int64_t lds, int M, int N, int K, int num_sms, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return;
+    const int blocks = (int)std::min<int64_t>((N + 7) / 8, (int64_t)num_sms * 8);
+    gemv_nt_kernel<<<blocks, 256, (size_t)M * K * 4, st>>>(A, lda, B, ldb, S, lds, M, N, K);
+}
+
+// ---------------------------------------------------------------------------
 // Exact selection.
 // ---------------------------------------------------------------------------
 namespace {

@@ -15,6 +15,11 @@ void launch_row_norms(const float* X, int64_t ld, int64_t n, int d, float* nrm_u
 void launch_sgemm_nt(const float* A, int64_t lda, const float* B, int64_t ldb, float* S,
                      int64_t lds, int M, int N, int K, cudaStream_t st);
 float sgemm_error_beta(int K);
+// The GEMV form of launch_sgemm_nt for M <= 8 rows of A (the same error bound);
+// gemv_fits tells whether it takes the operands (K and B's rows in 16-byte units).
+bool gemv_fits(const float* A, int64_t lda, const float* B, int64_t ldb, int M, int K);
+void launch_gemv_nt(const float* A, int64_t lda, const float* B, int64_t ldb, float* S,
+                    int64_t lds, int M, int N, int K, int num_sms, cudaStream_t st);
 size_t select_smem_bytes(int L, int D);
 int select_max_dim();
 cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t ldq, const float* C,

@@ -71,3 +71,31 @@ def test_select_matches_oracle(cuda_ok, oracle_mod, name):
                 np.testing.assert_array_equal(got[q], np.sort(got[q]))
             else:
                 np.testing.assert_array_equal(got[q], want, err_msg=f"{name} P={p} q={q}")
+
+
+@pytest.mark.parametrize("metric,normalized,d", [(1, False, 256), (0, False, 1024),
+                                                 (2, False, 2000), (2, True, 96)])
+def test_tiny_batches_select_like_the_oracle(cuda_ok, oracle_mod, metric, normalized, d):
+    """Batches of 1 to 8 queries take the GEMV coarse step (every SM streams the
+    centroids once; the SIMT GEMM's error bound); their selections must be the
+    oracle's, as the larger batches' are.  At dim 2000 eight queries exceed the
+    GEMV's shared-memory stage and take the GEMM, one query the GEMV."""
+    from m3_memory_b200 import cabi
+
+    O = oracle_mod
+    rng = np.random.default_rng(d + metric)
+    L = 1500
+    means = rng.standard_normal((16, d)).astype(np.float32)
+    C = (means[rng.integers(0, 16, L)] + 0.3 * rng.standard_normal((L, d))).astype(np.float32)
+    Q = (means[rng.integers(0, 16, 8)] + 0.3 * rng.standard_normal((8, d))).astype(np.float32)
+    if normalized:
+        C /= np.linalg.norm(C, axis=1, keepdims=True)
+        Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    e = cabi.Engine()
+    e.create_ivf(1, d, metric, normalized, C)
+    for nq in (1, 3, 8):
+        for p in (1, 16, 200):
+            got = e.select_probes(1, Q[:nq], p)
+            for q in range(nq):
+                want = O.select_nprobe(Q[q], C, metric, normalized, p)
+                np.testing.assert_array_equal(got[q], want, err_msg=f"nq={nq} P={p} q={q}")
