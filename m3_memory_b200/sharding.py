@@ -74,6 +74,33 @@ def collective(op, timeout_s, what, *args, **kwargs):
     return None
 
 
+class PendingCollective:
+    """A collective issued now and waited for later, so that independent work can
+    run between: without a limit, finish() makes the current stream wait for it;
+    with timeout_s, finish() waits on the host, at most that long (ShardError)."""
+
+    def __init__(self, op, timeout_s, what, *args, **kwargs):
+        self.timeout_s, self.what = timeout_s, what
+        try:
+            self.work = op(*args, async_op=True, **kwargs)
+        except Exception as ex:  # noqa: BLE001 -- transport errors become ShardErrors
+            raise ShardError(f"{what}: the exchange could not start ({type(ex).__name__}: "
+                             f"{ex})") from ex
+
+    def finish(self):
+        try:
+            if self.timeout_s is None:
+                self.work.wait()
+                return
+            done = self.work.wait(timeout=datetime.timedelta(seconds=self.timeout_s))
+        except Exception as ex:  # noqa: BLE001
+            raise ShardError(f"{self.what}: the exchange did not complete within "
+                             f"{self.timeout_s} s ({type(ex).__name__}: {ex})") from ex
+        if done is False:
+            raise ShardError(f"{self.what}: the exchange did not complete within "
+                             f"{self.timeout_s} s")
+
+
 def torch_dtype(name):
     import torch
 
@@ -311,12 +338,15 @@ class ShardedSearch:
         if P > o["P"]:
             raise ValueError(f"nprobe {P} exceeds max_nprobe={o['P']}")
         q_all = o["q_all"][:W * B]
-        collective(dist.all_gather_into_tensor, self.timeout_s, "batch exchange", q_all, q,
-                   group=self.group)
-        self._mark("query_exchange")
+        # the batches travel while this rank selects its own batch's probes (which
+        # needs only its own queries); the scan waits for both
+        gather = PendingCollective(dist.all_gather_into_tensor, self.timeout_s,
+                                   "batch exchange", q_all, q, group=self.group)
         loc = o["loc"].view(-1)[:B * P].view(B, P)
         self.engine.select_probes_device(self.index_id, q.data_ptr(), B, P, loc.data_ptr(), s)
         self._mark("coarse")
+        gather.finish()
+        self._mark("query_exchange")
         probes = o["probes"].view(-1)[:W * B * P].view(W * B, P)
         collective(dist.all_gather_into_tensor, self.timeout_s, "probe exchange", probes, loc,
                    group=self.group)

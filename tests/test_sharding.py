@@ -267,7 +267,7 @@ def _limit_rank_main(rank, world, port, mode, out):
     import torch
     import torch.distributed as dist
 
-    from m3_memory_b200.sharding import ShardError, collective
+    from m3_memory_b200.sharding import PendingCollective, ShardError, collective
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -275,6 +275,8 @@ def _limit_rank_main(rank, world, port, mode, out):
                             timeout=datetime.timedelta(seconds=6))
     src = torch.full((4,), float(rank + 1))
     dst = torch.empty(4 * world)
+    pending = mode.endswith("_pending")
+    mode = mode.replace("_pending", "")
     if rank == 1 and mode == "exit":
         os._exit(0)  # leaves without joining and without a clean shutdown
     if rank == 1 and mode == "stall":
@@ -282,7 +284,12 @@ def _limit_rank_main(rank, world, port, mode, out):
         os._exit(0)
     t0 = time.monotonic()
     try:
-        collective(dist.all_gather_into_tensor, 2.0, "probe exchange", dst, src)
+        if pending:  # issued first, waited for after other work
+            work = PendingCollective(dist.all_gather_into_tensor, 2.0, "probe exchange", dst, src)
+            time.sleep(0.1)
+            work.finish()
+        else:
+            collective(dist.all_gather_into_tensor, 2.0, "probe exchange", dst, src)
         res = ("ok", dst.tolist(), time.monotonic() - t0)
     except ShardError as ex:
         res = ("shard_error", str(ex), time.monotonic() - t0)
@@ -297,7 +304,7 @@ def _limit_rank_main(rank, world, port, mode, out):
     os._exit(0)
 
 
-@pytest.mark.parametrize("mode", ["join", "exit", "stall"])
+@pytest.mark.parametrize("mode", ["join", "exit", "stall", "join_pending", "exit_pending"])
 def test_exchange_limit_turns_a_missing_peer_into_an_error(mode):
     """The host-side limit on a sharded search's exchanges (ShardedSearch's
     timeout_s): with every rank present the exchange completes; a rank that left
@@ -318,7 +325,7 @@ def test_exchange_limit_turns_a_missing_peer_into_an_error(mode):
             p.join(timeout=30)
             if p.is_alive():
                 p.kill()
-    if mode == "join":
+    if mode.startswith("join"):
         assert status == "ok", detail
         assert detail == [1.0] * 4 + [2.0] * 4
     else:
