@@ -917,18 +917,18 @@ def run_config3(args, rank, world, local_rank):
         sc_d = torch.empty((64, K3), dtype=torch.float32, device=dev)
         cnt_d = torch.empty((64,), dtype=torch.int32, device=dev)
         eng.set_profiling(True)
-        for Bs in (1, 64):
+        for Bs, Ps in ((1, C3_NPROBES[0]), (64, C3_NPROBES[0]), (1, C3_NPROBES[-1])):
             st_s = {}
             torch.cuda.nvtx.range_push(f"small{Bs}")  # ncu --nvtx-include "small1/" selects these
             for i in range(10):
-                eng.search_device(1, Qd[i * Bs].data_ptr(), Bs, K3, C3_NPROBES[0], ids_d.data_ptr(),
+                eng.search_device(1, Qd[i * Bs].data_ptr(), Bs, K3, Ps, ids_d.data_ptr(),
                                   sc_d.data_ptr(), cnt_d.data_ptr())
                 p = eng.last_profile()
                 for key in ("ms_prep", "ms_coarse_gemm", "ms_select", "ms_worklist", "ms_scan",
                             "ms_merge", "ms_total"):
                     st_s.setdefault(key[3:], []).append(p[key])
             torch.cuda.nvtx.range_pop()
-            small[f"nprobe{C3_NPROBES[0]}_batch{Bs}"] = {
+            small[f"nprobe{Ps}_batch{Bs}"] = {
                 k: round(statistics.median(v), 4) for k, v in st_s.items()}
         eng.set_profiling(False)
         roofline["small_batch_stage_ms_median"] = small

@@ -340,8 +340,9 @@ int m3g_set_test_wait_limit(m3g_engine* e, uint64_t ns);
 /* Row tiles of the list scan (tensor-core path): a list longer than `rows` rows
  * is scanned as tiles of `rows` rows, spread over the SMs, each with its own
  * partial top-k, merged per (query, probe) by the last tile to finish.  rows: a
- * positive multiple of 128; 0 (the default) sizes tiles to about 4 MB of rows;
- * -1 scans every list whole.  Answers do not depend on it.  No counterpart in
+ * positive multiple of 128; 0 (the default) sizes tiles to about 4 MB of rows,
+ * or to 128 rows when a batch has fewer (query, probe) pairs than the GPU has
+ * SMs; -1 scans every list whole.  Answers do not depend on it.  No counterpart in
  * the reference (its list loop is serial, m3_index.cpp:426-442). */
 int m3g_set_scan_tile_rows(m3g_engine* e, int rows);
 

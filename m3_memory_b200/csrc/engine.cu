@@ -1558,9 +1558,9 @@ void Engine::set_centroid(int index_id, int cid, const float* c) {
 // ---------------- search pipeline ----------------
 
 namespace {
-constexpr int64_t kMaxChunkQueries = 8192;
+constexpr int64_t kMaxChunkQueries = 32768;
 constexpr int64_t kMaxScoreEntries = int64_t(1) << 26;  // nq * L per chunk
-constexpr int64_t kMaxPartEntries = int64_t(1) << 25;   // nq * P * k per chunk
+constexpr int64_t kMaxPartEntries = int64_t(1) << 27;   // nq * P * k per chunk
 constexpr int64_t kMaxAssignRows = int64_t(1) << 22;    // GEMM grid.y stays < 65536
 // Partial lists of the row-tile region (tensor-core scan): as many as the
 // (query, probe) pairs of a chunk, and at least kMinTilePartials.
@@ -1575,9 +1575,12 @@ float gamma_of(int D) { return (float)(D + 4) * 5.9604645e-8f * 1.01f; }
 // Runs one query chunk whose queries (rows of dQ, stride ldq >= dpad, zero padded)
 // are on the device.  fixed_probes: if non-null, [nq, P] probe lists already on
 // the device (skips the coarse step).  Outputs [nq, k] / [nq] on the device.
-int Engine::scan_tile_rows(const Index& ix) const {
+int Engine::scan_tile_rows(const Index& ix, int64_t pairs) const {
     if (scan_tile_rows_ < 0) return 0;
     if (scan_tile_rows_ > 0) return scan_tile_rows_;
+    // fewer (query, probe) pairs than SMs: the smallest tiles, so the few lists a
+    // small batch probes spread over the SMs
+    if (pairs < num_sms_) return 128;
     const int64_t rows = kAutoTileBytes / std::max<int64_t>(1, ix.row_bytes());
     return (int)std::min<int64_t>(std::max<int64_t>(128, rows & ~int64_t(127)), int64_t(1) << 20);
 }
@@ -1623,7 +1626,7 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     // other ranks own) are not queued
     // long lists are scanned in row tiles (tensor-core scan), so that their rows
     // spread over the SMs
-    const int tile_rows = tc_scan ? scan_tile_rows(ix) : 0;
+    const int tile_rows = tc_scan ? scan_tile_rows(ix, nq * P) : 0;
     const int64_t tcap = tile_partials(nq, P);
     M3G_CK(launch_build_worklist(probes, (int)nq, P, L, ix.d_list_order.p, gmax, w.lcount.p,
                                  w.lstart.p, w.lcursor.p, w.items.p, w.n_items.p, w.pair_q.p,
@@ -1710,7 +1713,7 @@ std::vector<uintptr_t> Engine::graph_key(const Index& ix, int64_t nq, int k, int
             u(w.item_counter.p), u(w.pair_q.p), u(w.pair_slot.p), u(w.plan.p), u(w.part_score.p),
             u(w.part_row.p), u(w.out_ids.p), u(w.out_scores.p), u(w.out_counts.p), u(w.err.p),
             (uintptr_t)use_tc_scan(), (uintptr_t)use_tc_gemm(), (uintptr_t)test_wait_ns_,
-            (uintptr_t)(intptr_t)scan_tile_rows(ix), u(w.tile_cnt.p)};
+            (uintptr_t)(intptr_t)scan_tile_rows(ix, nq * P), u(w.tile_cnt.p)};
 }
 
 // Replays (capturing first when the key changed) run_search on ws_.Q into
@@ -1767,6 +1770,7 @@ bool Engine::run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t 
 namespace {
 struct WsSizes {
     int64_t nq, L, P, k, dpad;
+    bool scores;  // the coarse step's score matrix and split queries are needed
 };
 template <class T>
 bool short_of(const DBuf<T>& b, int64_t n) {
@@ -1775,13 +1779,15 @@ bool short_of(const DBuf<T>& b, int64_t n) {
 bool ws_needs_grow(const Workspace& w, const WsSizes& s) {
     const int64_t np = s.nq * s.P, nt = tile_partials(s.nq, s.P);
     return !w.err.p || short_of(w.Q, s.nq * s.dpad) || short_of(w.qn, s.nq) ||
-           short_of(w.S, s.nq * s.L) || short_of(w.probes, np) || short_of(w.lcount, s.L) ||
+           short_of(w.S, s.scores ? s.nq * s.L : 0) || short_of(w.probes, np) ||
+           short_of(w.lcount, s.L) ||
            short_of(w.lstart, s.L) || short_of(w.lcursor, s.L) || short_of(w.plan, 6 * s.L) ||
            short_of(w.pair_q, np) ||
            short_of(w.pair_slot, np) || short_of(w.items, np + nt) || short_of(w.tile_cnt, nt) ||
            short_of(w.part_score, (np + nt) * s.k) || short_of(w.part_row, (np + nt) * s.k) ||
            short_of(w.out_ids, s.nq * s.k) || short_of(w.out_scores, s.nq * s.k) ||
-           short_of(w.out_counts, s.nq) || short_of(w.Q3, s.nq * gemm_tc_kdim((int)s.dpad)) ||
+           short_of(w.out_counts, s.nq) ||
+           short_of(w.Q3, s.scores ? s.nq * gemm_tc_kdim((int)s.dpad) : 0) ||
            short_of(w.item_counter, 1 + s.nq);
 }
 void ensure_ws(Workspace& w, const WsSizes& s) {
@@ -1796,7 +1802,7 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
     w.Q.ensure((size_t)(s.nq * s.dpad));
     w.qn.ensure((size_t)s.nq);
     w.qn2.ensure((size_t)s.nq);
-    w.S.ensure((size_t)(s.nq * s.L));
+    if (s.scores) w.S.ensure((size_t)(s.nq * s.L));
     w.probes.ensure((size_t)(s.nq * s.P));
     w.lcount.ensure((size_t)s.L);
     w.lstart.ensure((size_t)s.L);
@@ -1812,19 +1818,22 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
     w.out_ids.ensure((size_t)(s.nq * s.k));
     w.out_scores.ensure((size_t)(s.nq * s.k));
     w.out_counts.ensure((size_t)s.nq);
-    w.Q3.ensure((size_t)(s.nq * gemm_tc_kdim((int)s.dpad)));
+    if (s.scores) w.Q3.ensure((size_t)(s.nq * gemm_tc_kdim((int)s.dpad)));
 }
 
-int64_t chunk_queries(int64_t nq, int L, int P, int k) {
+// Queries per chunk of a call.  A list probed by queries of several chunks is
+// streamed once per chunk, so the chunks are as large as the buffers allow; the
+// score matrix's limit applies only to calls that run the coarse step (scores).
+int64_t chunk_queries(int64_t nq, int L, int P, int k, bool scores = true) {
     int64_t c = std::min<int64_t>(nq, kMaxChunkQueries);
-    c = std::min<int64_t>(c, std::max<int64_t>(1, kMaxScoreEntries / std::max(L, 1)));
+    if (scores) c = std::min<int64_t>(c, std::max<int64_t>(1, kMaxScoreEntries / std::max(L, 1)));
     c = std::min<int64_t>(c, std::max<int64_t>(1, kMaxPartEntries / std::max<int64_t>(1, (int64_t)P * k)));
     return std::max<int64_t>(c, 1);
 }
 }  // namespace
 
 void Engine::acquire_ws(cudaStream_t st, int64_t nq, int64_t L, int64_t P, int64_t k,
-                        int64_t dpad) {
+                        int64_t dpad, bool scores) {
     if (!ws_.stream) {
         M3G_CK(cudaStreamCreateWithFlags(&ws_.stream, cudaStreamNonBlocking));
         M3G_CK(cudaEventCreateWithFlags(&ws_.done, cudaEventDisableTiming));
@@ -1840,7 +1849,7 @@ void Engine::acquire_ws(cudaStream_t st, int64_t nq, int64_t L, int64_t P, int64
         M3G_CK(cudaStreamWaitEvent(ws_.stream, ws_.legacy, 0));
         st = ws_.stream;
     }
-    const WsSizes sz{nq, L, P, k, dpad};
+    const WsSizes sz{nq, L, P, k, dpad, scores};
     if (ws_needs_grow(ws_, sz)) {
         M3G_CK(cudaEventSynchronize(ws_.done));
         ensure_ws(ws_, sz);
@@ -2038,9 +2047,9 @@ void Engine::search_on(int index_id, const int32_t* cids, int ncids, const float
         return;
     }
     const int P = (int)keep.size();
-    const int64_t ch = chunk_queries(nq, L, P, k);
+    const int64_t ch = chunk_queries(nq, L, P, k, false);
     std::lock_guard wl(ws_.mu);
-    acquire_ws(nullptr, ch, L, P, k, ix->dpad);
+    acquire_ws(nullptr, ch, L, P, k, ix->dpad, false);
     cudaStream_t st = ws_.stream;
     DBuf<int32_t> row;
     row.alloc((size_t)P);
@@ -2156,9 +2165,9 @@ void Engine::probe_scores_device(int index_id, const float* dQ, int64_t nq,
     if (!dQ || !d_probes || !d_scores) fail(M3G_EINVAL, "probe_scores_device: buffers missing");
     if (ix->dim > select_max_dim()) fail(M3G_EUNSUPPORTED, "probe_scores_device: dim too large");
     const int L = ix->nlist();
-    const int64_t ch = chunk_queries(nq, std::max(L, 1), P, 1);
+    const int64_t ch = chunk_queries(nq, std::max(L, 1), P, 1, false);
     std::lock_guard wl(ws_.mu);
-    acquire_ws(ext, ch, std::max(L, 1), P, 1, ix->dpad);
+    acquire_ws(ext, ch, std::max(L, 1), P, 1, ix->dpad, false);
     cudaStream_t st = ext ? ext : ws_.stream;
     for (int64_t q0 = 0; q0 < nq; q0 += ch) {
         const int64_t m = std::min(ch, nq - q0);
@@ -2185,9 +2194,9 @@ void Engine::search_probes_device(int index_id, const float* dQ, int64_t nq, int
         fail(M3G_EINVAL, "search_probes_device: buffers missing");
     std::shared_lock lk(ix->mu);
     const int L = std::max(ix->nlist(), 1);
-    const int64_t ch = chunk_queries(nq, L, P, k);
+    const int64_t ch = chunk_queries(nq, L, P, k, false);
     std::lock_guard wl(ws_.mu);
-    acquire_ws(ext, ch, L, P, k, ix->dpad);
+    acquire_ws(ext, ch, L, P, k, ix->dpad, false);
     cudaStream_t st = ext ? ext : ws_.stream;
     for (int64_t q0 = 0; q0 < nq; q0 += ch) {
         const int64_t m = std::min(ch, nq - q0);

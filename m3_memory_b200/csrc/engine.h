@@ -282,9 +282,10 @@ class Engine {
     void set_profiling(bool on) { profiling_ = on; }
     void set_test_wait_ns(uint64_t ns) { test_wait_ns_ = ns; }
     // Row tiles of long lists in the tensor-core scan: rows per tile (a positive
-    // multiple of 128), 0 for the automatic size, -1 for none.
+    // multiple of 128), 0 for the automatic size (128 rows when a batch has fewer
+    // (query, probe) pairs than SMs, else about 4 MB of rows), -1 for none.
     void set_scan_tile_rows(int rows) { scan_tile_rows_ = rows; }
-    int scan_tile_rows(const Index& ix) const;
+    int scan_tile_rows(const Index& ix, int64_t pairs) const;
     m3g_profile last_profile();
 
    private:
@@ -310,7 +311,9 @@ class Engine {
                      int64_t n, int32_t* d_out, cudaStream_t st);
     // Creates the workspace stream / events on first use; then orders `st` after
     // the previous user of the workspace (blocking only when buffers must grow).
-    void acquire_ws(cudaStream_t st, int64_t nq, int64_t L, int64_t P, int64_t k, int64_t dpad);
+    // scores: the call runs the coarse step (score matrix and split queries).
+    void acquire_ws(cudaStream_t st, int64_t nq, int64_t L, int64_t P, int64_t k, int64_t dpad,
+                    bool scores = true);
 
     int device_ = 0;
     int num_sms_ = 148;

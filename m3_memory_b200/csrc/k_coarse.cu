@@ -427,9 +427,10 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         // --- pre-filtered threshold.  Small block: each of the NW warps sorts its
         // threads' smallest upper-bound keys and offers its ceil(PP/NW)-th smallest;
         // tau0, the largest offer, has at least NW * ceil(PP/NW) >= PP distinct keys
-        // <= it.  Large block (P up to 256): every thread keeps its TOPT smallest
-        // keys and tau0 is the PP-th smallest of those NT * TOPT keys (a far tighter
-        // threshold than the offers, whose largest is the largest thread minimum).
+        // <= it.  Larger P (over 32 in the small block, every P in the large one):
+        // every thread keeps its TOPT smallest keys (2 / 4) and tau0 is the PP-th
+        // smallest of those NT * TOPT keys (a far tighter threshold than the offers,
+        // whose largest is the largest thread minimum).
         // Either way tau0 >= T (the PP-th smallest upper bound of all).  Every centroid with
         // hi <= T therefore has lo <= tau0, so T is the PP-th smallest upper bound
         // within S0 = {c : lo <= tau0}, and every candidate (lo <= T) is in S0.
@@ -438,7 +439,9 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         // their loads issued together.
         uint32_t* lkeys = hkeys;
         const bool keep_lo = L <= SEL_KEEP_LO_L;  // the area then holds L + 3 CAP words
-        constexpr int TOPT = NT == SEL_LARGE_NT ? 4 : 1;
+        constexpr int TOPT = NT == SEL_LARGE_NT ? 4 : 2;
+        // small P in the small block: the warp offers (cheap, tight enough there)
+        const bool offers = NT != SEL_LARGE_NT && PP <= 32;
         static_assert(TOPT * NT <= CAP, "the thread minima fit the S0 key array");
         uint32_t mk[TOPT];  // this thread's TOPT smallest upper-bound keys, ascending
 #pragma unroll
@@ -472,7 +475,7 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         uint32_t* f_id = hkeys + (keep_lo ? L : 0);  // S0, in the key / tile area
         uint32_t* f_lo = f_id + CAP;
         uint32_t* f_hi = f_lo + CAP;
-        if constexpr (TOPT == 1) {
+        if (offers) {
             const uint32_t sorted = warp_sort_asc_u32(mk[0], lane);
             const uint32_t offer = __shfl_sync(0xffffffffu, sorted, (PP + NW - 1) / NW - 1);
             if (lane == 0) sh.mins[warp] = offer;
@@ -488,7 +491,7 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         }
         __syncthreads();
         uint32_t tau0 = 0;
-        if constexpr (TOPT == 1) {
+        if (offers) {
             for (int w = 0; w < NW; ++w) tau0 = sh.mins[w] > tau0 ? sh.mins[w] : tau0;
         } else {
             // every key of the pool is a distinct centroid's, and the pool holds at

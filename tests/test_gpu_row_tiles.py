@@ -107,12 +107,15 @@ def test_bf16_rows_in_tiles(cuda_ok):
     same(search(cabi, case, 128, storage=cabi.BF16), whole)
 
 
-def test_automatic_tiles_of_a_wide_index(cuda_ok, oracle_mod):
-    """dim 1024 (4 KB rows): the automatic tile is 1024 rows, so the 2600- and
-    4500-row lists are tiled with the default setting."""
+@pytest.mark.parametrize("nq", [24, 64])
+def test_automatic_tiles_of_a_wide_index(cuda_ok, oracle_mod, nq):
+    """dim 1024 (4 KB rows) with the default setting: 64 queries x 3 probes (more
+    pairs than SMs) take tiles of about 4 MB (1024 rows), so the 2600- and
+    4500-row lists are tiled; 24 queries x 3 probes (fewer pairs than SMs) take
+    128-row tiles, so every list longer than that is."""
     from m3_memory_b200 import cabi
 
-    CASES["ip_wide_auto"] = (1, False, 1024, 24, 3, 10)
+    CASES["ip_wide_auto"] = (1, False, 1024, nq, 3, 10)
     try:
         case = make_case("ip_wide_auto", sizes=[2600, 40, 4500, 700, 0, 1100])
     finally:
@@ -122,7 +125,7 @@ def test_automatic_tiles_of_a_wide_index(cuda_ok, oracle_mod):
     lists = oracle_mod.CsrLists(case["off"], case["X"], case["ids"], case["alive"])
     ref = oracle_mod.search_nprobe(case["Q"], case["C"], lists, case["metric"],
                                    case["normalized"], case["k"], case["nprobe"])
-    compare_search(whole, ref)
+    compare_search(whole, ref, min_recall=0.995)
 
 
 def test_tiles_beyond_the_region_scan_whole(cuda_ok):
