@@ -795,8 +795,6 @@ Engine::~Engine() {
     ws_.items.release();
     ws_.tile_cnt.release();
     ws_.plan.release();
-    ws_.part_ids.release();
-    ws_.part_sc.release();
     ws_.part_score.release();
     ws_.part_row.release();
     ws_.out_ids.release();
@@ -1572,50 +1570,6 @@ int64_t tile_partials(int64_t nq, int64_t P) { return std::max(nq * P, kMinTileP
 constexpr int64_t kAutoTileBytes = int64_t(4) << 20;
 
 float gamma_of(int D) { return (float)(D + 4) * 5.9604645e-8f * 1.01f; }
-
-// A tiny batch's selection split over id-ordered parts of the centroids (one block
-// per query and part instead of one per query), for batches of up to
-// kTinySelectRows queries over at least kTinySelectMinL centroids.
-constexpr int kTinySelectRows = 8;
-constexpr int kTinySelectMinL = 4096;
-constexpr int kTinySelectPartLen = 512;
-constexpr int kTinySelectMaxParts = 32;
-constexpr int kTinySelectMaxP = 128;
-constexpr int64_t kTinySelectEntries = int64_t(kTinySelectRows) * kTinySelectMaxParts * kTinySelectMaxP;
-int tiny_select_parts(int64_t m, int L, int P, int dim) {
-    if (m > kTinySelectRows || L < kTinySelectMinL || P > kTinySelectMaxP || P >= L ||
-        dim > select_max_dim())
-        return 1;
-    return std::min(kTinySelectMaxParts, L / kTinySelectPartLen);
-}
-
-// The exact top-P of m queries against the index's centroids from the coarse
-// scores in S (launch_select_probes), split over parts for tiny batches: each
-// part's exact top-P, their exact scores (launch_probe_scores, the reference's
-// arithmetic) and a merge by (score, id) -- the same P ids in the same order.
-// Returns the kernels launched.
-int select_probes_into(Workspace& w, const Index& ix, const float* q, int64_t ldq, int64_t m,
-                       int P, float beta, int32_t* out, cudaStream_t st) {
-    const int L = ix.nlist();
-    const int nrm = ix.normalized ? 1 : 0;
-    const int parts = tiny_select_parts(m, L, P, ix.dim);
-    if (parts <= 1) {
-        M3G_CK(launch_select_probes(w.S.p, L, q, ldq, ix.C.p, ix.dpad, w.qn.p, w.qn2.p, ix.cn.p,
-                                    ix.cn2.p, (int)m, L, ix.dim, ix.metric, nrm, beta,
-                                    gamma_of(ix.dim), P, 0, out, st));
-        return 1;
-    }
-    const int part_len = (L + parts - 1) / parts;
-    const int G = (L + part_len - 1) / part_len;
-    const int n = G * P;
-    M3G_CK(launch_select_probes(w.S.p, L, q, ldq, ix.C.p, ix.dpad, w.qn.p, w.qn2.p, ix.cn.p,
-                                ix.cn2.p, (int)m, L, ix.dim, ix.metric, nrm, beta,
-                                gamma_of(ix.dim), P, 0, w.part_ids.p, st, parts));
-    M3G_CK(launch_probe_scores(q, ldq, ix.C.p, ix.dpad, L, w.part_ids.p, m, n, ix.dim, ix.metric,
-                               nrm, w.part_sc.p, st));
-    M3G_CK(launch_merge_parts(w.part_sc.p, w.part_ids.p, (int)m, n, P, out, st));
-    return 3;
-}
 }  // namespace
 
 // Runs one query chunk whose queries (rows of dQ, stride ldq >= dpad, zero padded)
@@ -1645,7 +1599,6 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
                              split_q ? w.Q3.p : nullptr, w.qn.p, w.qn2.p, st));
     if (profile) M3G_CK(cudaEventRecord(ev[1], st));
     const int32_t* probes = fixed_probes;
-    int sel_launches = 1;
     if (!probes) {
         if (P >= L) {
             M3G_CK(launch_iota_rows(w.probes.p, nq, P, st));
@@ -1654,7 +1607,9 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
             const float beta = coarse_gemm(dQ, ldq, w.Q3.p, ix.C.p, ix.dpad, ix.C3.p, w.S.p, L,
                                            (int)nq, L, ix.dpad, w.err.p, st);
             if (profile) M3G_CK(cudaEventRecord(ev[2], st));
-            sel_launches = select_probes_into(w, ix, dQ, ldq, nq, P, beta, w.probes.p, st);
+            M3G_CK(launch_select_probes(w.S.p, L, dQ, ldq, ix.C.p, ix.dpad, w.qn.p, w.qn2.p, ix.cn.p,
+                                        ix.cn2.p, (int)nq, L, D, ix.metric, ix.normalized ? 1 : 0,
+                                        beta, gamma_of(D), P, 0, w.probes.p, st));
         }
         probes = w.probes.p;
     } else if (profile) {
@@ -1738,7 +1693,7 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
     // kernels launched: query prep, coarse (gemm + select, or iota), 5 work-list
     // kernels, scan, merge (+ the exact rescoring for L2, + the byte counter when
     // profiling)
-    int launches = 1 + (fixed_probes ? 0 : (P >= L ? 1 : 1 + sel_launches)) + 5 +
+    int launches = 1 + (fixed_probes ? 0 : (P >= L ? 1 : 2)) + 5 +
                    (ix.maps_valid ? 1 : 0) + 1 + (rescore ? 1 : 0);
     if (profile) launches += 1;
     last_launches_ += launches;
@@ -1804,8 +1759,7 @@ bool Engine::run_search_graph(Index& ix, int64_t nq, int k, int P, cudaStream_t 
     } else {
         // the kernels a replay runs, for the caller's accounting
         const bool tc = (use_tc_scan() || ix.bf16_rows()) && scan_tc_supported(ix.metric, k);
-        last_launches_ += 1 + (P >= ix.nlist() ? 1 : (tiny_select_parts(nq, ix.nlist(), P, ix.dim) > 1 ? 4 : 2)) +
-                          5 + (ix.maps_valid ? 1 : 0) + 1 +
+        last_launches_ += 1 + (P >= ix.nlist() ? 1 : 2) + 5 + (ix.maps_valid ? 1 : 0) + 1 +
                           (tc && ix.metric == M3G_L2 && ix.maps_valid ? 1 : 0);
     }
     M3G_CK(cudaGraphLaunch(graph_.exec, st));
@@ -1834,7 +1788,6 @@ bool ws_needs_grow(const Workspace& w, const WsSizes& s) {
            short_of(w.out_ids, s.nq * s.k) || short_of(w.out_scores, s.nq * s.k) ||
            short_of(w.out_counts, s.nq) ||
            short_of(w.Q3, s.scores ? s.nq * gemm_tc_kdim((int)s.dpad) : 0) ||
-           short_of(w.part_ids, s.scores ? kTinySelectEntries : 0) ||
            short_of(w.item_counter, 1 + s.nq);
 }
 void ensure_ws(Workspace& w, const WsSizes& s) {
@@ -1865,11 +1818,7 @@ void ensure_ws(Workspace& w, const WsSizes& s) {
     w.out_ids.ensure((size_t)(s.nq * s.k));
     w.out_scores.ensure((size_t)(s.nq * s.k));
     w.out_counts.ensure((size_t)s.nq);
-    if (s.scores) {
-        w.Q3.ensure((size_t)(s.nq * gemm_tc_kdim((int)s.dpad)));
-        w.part_ids.ensure((size_t)kTinySelectEntries);
-        w.part_sc.ensure((size_t)kTinySelectEntries);
-    }
+    if (s.scores) w.Q3.ensure((size_t)(s.nq * gemm_tc_kdim((int)s.dpad)));
 }
 
 // Queries per chunk of a call.  A list probed by queries of several chunks is
@@ -2152,7 +2101,10 @@ void Engine::select_probes(int index_id, const float* Q, int64_t nq, int nprobe,
             const float beta = coarse_gemm(ws_.Q.p, ix->dpad, ws_.Q3.p, ix->C.p, ix->dpad,
                                            ix->C3.p, ws_.S.p, L, (int)m, L, ix->dpad, ws_.err.p,
                                            st);
-            select_probes_into(ws_, *ix, ws_.Q.p, ix->dpad, m, P, beta, ws_.probes.p, st);
+            M3G_CK(launch_select_probes(ws_.S.p, L, ws_.Q.p, ix->dpad, ix->C.p, ix->dpad, ws_.qn.p,
+                                        ws_.qn2.p, ix->cn.p, ix->cn2.p, (int)m, L, ix->dim,
+                                        ix->metric, ix->normalized ? 1 : 0, beta,
+                                        gamma_of(ix->dim), P, 0, ws_.probes.p, st));
         }
         M3G_CK(cudaMemcpyAsync(out + q0 * P, ws_.probes.p, (size_t)(m * P) * 4, cudaMemcpyDeviceToHost, st));
     }
@@ -2193,7 +2145,10 @@ void Engine::select_probes_device(int index_id, const float* dQ, int64_t nq, int
         } else {
             const float beta = coarse_gemm(q, ix->dpad, ws_.Q3.p, ix->C.p, ix->dpad, ix->C3.p,
                                            ws_.S.p, L, (int)m, L, ix->dpad, ws_.err.p, st);
-            select_probes_into(ws_, *ix, q, ix->dpad, m, P, beta, out, st);
+            M3G_CK(launch_select_probes(ws_.S.p, L, q, ix->dpad, ix->C.p, ix->dpad, ws_.qn.p,
+                                        ws_.qn2.p, ix->cn.p, ix->cn2.p, (int)m, L, ix->dim,
+                                        ix->metric, ix->normalized ? 1 : 0, beta,
+                                        gamma_of(ix->dim), P, 0, out, st));
         }
     }
     M3G_CK(cudaEventRecord(ws_.done, st));

@@ -174,8 +174,6 @@ struct Workspace {
     DBuf<int32_t> probes, lcount, lstart, lcursor, n_items, item_counter, pair_q, pair_slot;
     DBuf<int32_t> tile_cnt;  // finished row tiles per tiled pair (tensor-core scan)
     DBuf<int32_t> plan;      // work-list planning scratch, 6 per list
-    DBuf<int32_t> part_ids;  // a tiny batch's selection split over parts: the parts' ids
-    DBuf<float> part_sc;     // and their exact scores
     DBuf<ScanItem> items;
     DBuf<float> part_score;
     DBuf<int64_t> part_row;

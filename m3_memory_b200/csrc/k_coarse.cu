@@ -387,21 +387,12 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
     float* __restrict__ S, int64_t lds, const float* __restrict__ Q, int64_t ldq,
     const float* __restrict__ C, int64_t ldc, const float* __restrict__ qn,
     const float* __restrict__ qn2, const float* __restrict__ cn, const float* __restrict__ cn2,
-    int L_all, int D, int metric, int normalized, float beta, float gamma, int P, int nan_is_none,
-    int32_t* __restrict__ probes, int part_len) {
+    int L, int D, int metric, int normalized, float beta, float gamma, int P, int nan_is_none,
+    int32_t* __restrict__ probes) {
     extern __shared__ __align__(16) unsigned char sel_smem[];
     __shared__ SelShared<NT> sh;
     constexpr int NW = NT / 32;
     const int q = blockIdx.x;
-    // with part_len, block (q, y) selects among centroids [y part_len, (y + 1) part_len)
-    // and writes their ids (global) to row q * gridDim.y + y of probes
-    const int part = blockIdx.y;
-    const int c0 = part_len > 0 ? part * part_len : 0;
-    const int L = part_len > 0 ? min(part_len, L_all - c0) : L_all;
-    C += (int64_t)c0 * ldc;
-    cn += c0;
-    cn2 += c0;
-    int32_t* pout = probes + ((int64_t)q * gridDim.y + part) * P;
     float* qs = reinterpret_cast<float*>(sel_smem);                               // D floats
     unsigned long long* cand = reinterpret_cast<unsigned long long*>(qs + ((D + 3) & ~3));  // CAP
     float2* bnd = reinterpret_cast<float2*>(cand + CAP);                     // CAP
@@ -416,7 +407,7 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
 
     const float* qrow = Q + (int64_t)q * ldq;
     for (int i = threadIdx.x; i < D; i += NT) qs[i] = qrow[i];
-    float* srow = S + (int64_t)q * lds + c0;
+    float* srow = S + (int64_t)q * lds;
     const float nq = qn[q], nq2 = qn2[q];
     const bool nrm = normalized != 0;
     if (threadIdx.x == 0) sh.nex = 0;  // read after later barriers on every path
@@ -425,7 +416,6 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         approx_bounds(srow[c], nq, cn[c], nq2, cn2[c], beta, gamma, metric, nrm, lo, hi);
     };
     const int PP = P < L ? P : L;
-    for (int j = PP + threadIdx.x; j < P; j += NT) pout[j] = -1;  // a part shorter than P
     bool exact_all = PP > SEL_SORT_MAX;
     bool have = false;  // candidates in cand[0, cnt)
     unsigned cnt = 0;
@@ -736,7 +726,7 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
                 if (r < (unsigned)PP) {
                     int32_t id = (int32_t)(kk & 0xffffffffu);
                     if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
-                    pout[r] = id >= 0 ? id + c0 : id;
+                    probes[(int64_t)q * P + r] = id;
                 }
             }
             return;
@@ -750,7 +740,7 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
             const unsigned long long kk = cand[j];
             int32_t id = (int32_t)(kk & 0xffffffffu);
             if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
-            pout[j] = id >= 0 ? id + c0 : id;
+            probes[(int64_t)q * P + j] = id;
         }
         return;
     }
@@ -800,7 +790,7 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
             if (sorted)
                 cand[out_pos + off] = ((unsigned long long)k << 32) | (unsigned)c;
             else
-                pout[out_pos + off] = c + c0;
+                probes[(int64_t)q * P + out_pos + off] = c;
         }
         out_pos += take_tot;
         ties_taken += tie_tot;
@@ -816,7 +806,7 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
             const unsigned long long kk = cand[j];
             int32_t id = (int32_t)(kk & 0xffffffffu);
             if (nan_is_none && (uint32_t)(kk >> 32) == 0xffffffffu) id = -1;
-            pout[j] = id >= 0 ? id + c0 : id;
+            probes[(int64_t)q * P + j] = id;
         }
     }
 }
@@ -893,78 +883,21 @@ cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t 
                                  int64_t ldc, const float* qn, const float* qn2, const float* cn,
                                  const float* cn2, int nq, int L, int D, int metric,
                                  int normalized, float beta, float gamma, int P, int nan_is_none,
-                                 int32_t* probes, cudaStream_t st, int parts) {
+                                 int32_t* probes, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
-    // parts > 1: the centroids in id-ordered parts of part_len, one block per (query,
-    // part), P ids per part (probes holds nq x parts x P)
-    const int part_len = parts > 1 ? (L + parts - 1) / parts : 0;
-    const int G = parts > 1 ? (L + part_len - 1) / part_len : 1;
-    const int Lb = parts > 1 ? part_len : L;  // centroids of the largest block
     auto run = [&](auto kernel, int nt, size_t smem) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
-        kernel<<<dim3((unsigned)nq, (unsigned)G), nt, smem, st>>>(
-            S, lds, Q, ldq, C, ldc, qn, qn2, cn, cn2, L, D, metric, normalized, beta, gamma, P,
-            nan_is_none, probes, part_len);
+        kernel<<<nq, nt, smem, st>>>(S, lds, Q, ldq, C, ldc, qn, qn2, cn, cn2, L, D, metric,
+                                     normalized, beta, gamma, P, nan_is_none, probes);
         return cudaGetLastError();
     };
-    if ((P < Lb ? P : Lb) <= SEL_SMALL_P)
+    if ((P < L ? P : L) <= SEL_SMALL_P)
         return run(select_probes_kernel<SEL_SMALL_NT, SEL_SMALL_CAP, SEL_SMALL_MINB>, SEL_SMALL_NT,
-                   select_smem_bytes_t<SEL_SMALL_NT, SEL_SMALL_CAP>(Lb, D));
+                   select_smem_bytes_t<SEL_SMALL_NT, SEL_SMALL_CAP>(L, D));
     return run(select_probes_kernel<SEL_LARGE_NT, SEL_LARGE_CAP, 3>, SEL_LARGE_NT,
-               select_smem_bytes_t<SEL_LARGE_NT, SEL_LARGE_CAP>(Lb, D));
-}
-
-namespace {
-constexpr int MP_BLOCK = 256;
-constexpr int MP_CAP = 4096;  // candidates per query (parts x P)
-
-// Per query, the P smallest of its n candidates by (exact score, position); the
-// positions run part by part, each part's ids ascending by (score, id), so the
-// order is (score, id) -- the selection's own order.  Empty slots (id < 0) last.
-__global__ void __launch_bounds__(MP_BLOCK) merge_parts_kernel(const float* __restrict__ scores,
-                                                               const int32_t* __restrict__ ids,
-                                                               int n, int P,
-                                                               int32_t* __restrict__ probes) {
-    __shared__ unsigned long long key[MP_CAP];
-    const int q = blockIdx.x;
-    int n2 = 1;
-    while (n2 < n) n2 <<= 1;
-    for (int i = threadIdx.x; i < n2; i += MP_BLOCK) {
-        unsigned long long k = ~0ull;
-        if (i < n && ids[(int64_t)q * n + i] >= 0)
-            k = ((unsigned long long)float_key(scores[(int64_t)q * n + i]) << 32) | (uint32_t)i;
-        key[i] = k;
-    }
-    __syncthreads();
-    for (int s2 = 2; s2 <= n2; s2 <<= 1)
-        for (int h = s2 >> 1; h > 0; h >>= 1) {
-            for (int i = threadIdx.x; i < n2; i += MP_BLOCK) {
-                const int p = i ^ h;
-                if (p > i) {
-                    const unsigned long long a = key[i], b = key[p];
-                    if ((a > b) == ((i & s2) == 0)) {
-                        key[i] = b;
-                        key[p] = a;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    for (int j = threadIdx.x; j < P; j += MP_BLOCK) {
-        const unsigned long long k = key[j];
-        probes[(int64_t)q * P + j] = k == ~0ull ? -1 : ids[(int64_t)q * n + (uint32_t)(k & 0xffffffffu)];
-    }
-}
-}  // namespace
-
-cudaError_t launch_merge_parts(const float* scores, const int32_t* ids, int nq, int n, int P,
-                               int32_t* probes, cudaStream_t st) {
-    if (nq <= 0) return cudaSuccess;
-    if (n > MP_CAP || P > n) return cudaErrorInvalidValue;
-    merge_parts_kernel<<<nq, MP_BLOCK, 0, st>>>(scores, ids, n, P, probes);
-    return cudaGetLastError();
+               select_smem_bytes_t<SEL_LARGE_NT, SEL_LARGE_CAP>(L, D));
 }
 
 }  // namespace m3g

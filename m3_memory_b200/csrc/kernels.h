@@ -26,13 +26,7 @@ cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t 
                                  int64_t ldc, const float* qn, const float* qn2, const float* cn,
                                  const float* cn2, int nq, int L, int D, int metric,
                                  int normalized, float beta, float gamma, int P, int nan_is_none,
-                                 int32_t* probes, cudaStream_t st, int parts = 1);
-// The P smallest of each query's n candidates (ids [nq, n], exact scores [nq, n],
-// n <= 4096) by (score, position) into probes [nq, P]: the merge of a selection
-// split into id-ordered parts (launch_select_probes with parts > 1, then
-// launch_probe_scores of the parts' ids).
-cudaError_t launch_merge_parts(const float* scores, const int32_t* ids, int nq, int n, int P,
-                               int32_t* probes, cudaStream_t st);
+                                 int32_t* probes, cudaStream_t st);
 
 // ---- coarse GEMM on the tensor cores (k_gemm_tc.cu) ----
 int gemm_tc_kdim(int dpad);            // K' of the split operands (3 dpad, padded to 64)

@@ -99,3 +99,35 @@ def test_tiny_batches_select_like_the_oracle(cuda_ok, oracle_mod, metric, normal
             for q in range(nq):
                 want = O.select_nprobe(Q[q], C, metric, normalized, p)
                 np.testing.assert_array_equal(got[q], want, err_msg=f"nq={nq} P={p} q={q}")
+
+
+@pytest.mark.parametrize("metric,normalized,d", [(1, False, 128), (0, False, 96),
+                                                 (2, False, 64), (2, True, 200)])
+def test_tiny_batches_over_many_centroids(cuda_ok, oracle_mod, metric, normalized, d):
+    """1 to 8 queries over 5000 centroids (the GEMV coarse step) select exactly
+    the oracle's P ids, with exact duplicate centroids far apart in id (ties broken
+    by the lower id) and P from 1 to 128; a batch of 12 (the GEMM coarse step, a
+    different error bound and candidate set) agrees with them."""
+    from m3_memory_b200 import cabi
+
+    O = oracle_mod
+    rng = np.random.default_rng(7 * d + metric)
+    L = 5000
+    means = rng.standard_normal((24, d)).astype(np.float32)
+    C = (means[rng.integers(0, 24, L)] + 0.3 * rng.standard_normal((L, d))).astype(np.float32)
+    C[[100, 700, 1300, 4999]] = C[5]  # exact duplicates in several parts
+    Q = (means[rng.integers(0, 24, 12)] + 0.3 * rng.standard_normal((12, d))).astype(np.float32)
+    Q[0] = C[5]
+    if normalized:
+        C /= np.linalg.norm(C, axis=1, keepdims=True)
+        Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    e = cabi.Engine()
+    e.create_ivf(1, d, metric, normalized, C)
+    for p in (1, 8, 100, 128):
+        big = e.select_probes(1, Q, p)
+        for nq in (1, 5, 8):
+            got = e.select_probes(1, Q[:nq], p)
+            np.testing.assert_array_equal(got, big[:nq], err_msg=f"nq={nq} P={p}")
+            for q in range(nq):
+                want = O.select_nprobe(Q[q], C, metric, normalized, p)
+                np.testing.assert_array_equal(got[q], want, err_msg=f"nq={nq} P={p} q={q}")
