@@ -720,14 +720,14 @@ def run_ours(args, rank, world, local_rank):
                         "steps in flight on alternating streams (sync_call_value: one blocking "
                         "m3g_search per step)" if world == 1
                 else "per GPU: H2D of its own batch + NCCL all-gather of the batches + "
-                     "m3g_select_probes_device (own batch) + NCCL all-gather of the probes + "
+                     "m3g_select_probe_sets_device (own batch) + NCCL all-gather of the probes + "
                      "m3g_search_probes_device (all batches, own lists) + NCCL all-to-all of "
                      "the packed top-k records + m3g_merge_shards_packed_device + D2H of its "
                      "batch's answer, two steps in flight on alternating streams "
                      "(sync_call_value: one step at a time); bytes per GPU" if weak
                 else ("H2D + m3g_search_device + NCCL all-gather + m3g_merge_shards_device + D2H"
                       if args.coarse == "replicated" else
-                      "H2D + m3g_select_probes_device (this rank's query slice) + NCCL all-gather "
+                      "H2D + m3g_select_probe_sets_device (this rank's query slice) + NCCL all-gather "
                       "of the probes + m3g_search_probes_device + NCCL all-gather + "
                       "m3g_merge_shards_device + D2H" if args.coarse == "split" else
                       "H2D + m3g_select_probes_device + m3g_probe_scores_device (own centroids) + "

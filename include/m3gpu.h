@@ -292,6 +292,10 @@ int m3g_merge_shards_packed_device(m3g_engine* e, const void* d_packed, int nsha
  *
  * m3g_select_probes_device: m3g_select_probes on device queries [nq, dim],
  * writing [nq, min(nprobe, nlist)] cluster ids ascending by exact score.
+ * m3g_select_probe_sets_device: the same sets of cluster ids, each row in an
+ * order of the engine's choosing (the same for the same inputs) -- the form the
+ * list scan consumes, and cheaper: only the centroids whose place in or out of
+ * the top nprobe the GEMM's error bound leaves open are rescored exactly.
  * m3g_probe_scores_device: the exact unified score (unified_score,
  * base.h:22-31, in the reference's fp32 arithmetic) of each pair
  * (query q, centroid d_probes[q, j]), [nq, nprobe]; +inf for ids out of range.
@@ -300,6 +304,8 @@ int m3g_merge_shards_packed_device(m3g_engine* e, const void* d_packed, int nsha
  * the slot); outputs as m3g_search_device. */
 int m3g_select_probes_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
                              int nprobe, int32_t* d_out_probes, void* stream);
+int m3g_select_probe_sets_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
+                                 int nprobe, int32_t* d_out_probes, void* stream);
 int m3g_probe_scores_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
                             const int32_t* d_probes, int nprobe, float* d_out_scores,
                             void* stream);

@@ -99,6 +99,7 @@ SIGNATURES = {
     "m3g_split_cluster": (_i32, [_vp, _i32, _i32, _i32, _u64, _pi32]),
     "m3g_merge_shards_device": (_i32, [_vp, _vp, _vp, _i32, _i64, _i32, _vp, _vp, _vp, _vp]),
     "m3g_select_probes_device": (_i32, [_vp, _i32, _vp, _i64, _i32, _vp, _vp]),
+    "m3g_select_probe_sets_device": (_i32, [_vp, _i32, _vp, _i64, _i32, _vp, _vp]),
     "m3g_probe_scores_device": (_i32, [_vp, _i32, _vp, _i64, _vp, _i32, _vp, _vp]),
     "m3g_search_probes_device": (_i32, [_vp, _i32, _vp, _i64, _i32, _vp, _i32, _vp, _vp, _vp,
                                         _vp]),
@@ -438,6 +439,13 @@ class Engine:
         check(lib().m3g_select_probes_device(self.h, index_id, ct.c_void_p(q_ptr), nq, nprobe,
                                              ct.c_void_p(out_ptr),
                                              ct.c_void_p(stream) if stream else None))
+
+    def select_probe_sets_device(self, index_id, q_ptr, nq, nprobe, out_ptr, stream=None):
+        """As select_probes_device, each row's ids in an order of the engine's
+        choosing: the sets a list scan needs, at less cost."""
+        check(lib().m3g_select_probe_sets_device(self.h, index_id, ct.c_void_p(q_ptr), nq,
+                                                 nprobe, ct.c_void_p(out_ptr),
+                                                 ct.c_void_p(stream) if stream else None))
 
     def probe_scores_device(self, index_id, q_ptr, nq, probes_ptr, nprobe, out_ptr,
                             stream=None):

@@ -464,6 +464,16 @@ int m3g_select_probes_device(m3g_engine* e, int index_id, const float* d_queries
     });
 }
 
+int m3g_select_probe_sets_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
+                                 int nprobe, int32_t* d_out_probes, void* stream) {
+    M3G_ENGINE_OR_FAIL(e);
+    return guarded([&] {
+        if (nq < 0) m3g::fail(M3G_EINVAL, "select_probe_sets_device: nq < 0");
+        e->eng.select_probes_device(index_id, d_queries, nq, nprobe, d_out_probes,
+                                    static_cast<cudaStream_t>(stream), true);
+    });
+}
+
 int m3g_probe_scores_device(m3g_engine* e, int index_id, const float* d_queries, int64_t nq,
                             const int32_t* d_probes, int nprobe, float* d_out_scores,
                             void* stream) {

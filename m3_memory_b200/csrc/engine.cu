@@ -1609,7 +1609,7 @@ void Engine::run_search(Index& ix, const float* dQ, int64_t ldq, int64_t nq, int
             if (profile) M3G_CK(cudaEventRecord(ev[2], st));
             M3G_CK(launch_select_probes(w.S.p, L, dQ, ldq, ix.C.p, ix.dpad, w.qn.p, w.qn2.p, ix.cn.p,
                                         ix.cn2.p, (int)nq, L, D, ix.metric, ix.normalized ? 1 : 0,
-                                        beta, gamma_of(D), P, 0, w.probes.p, st));
+                                        beta, gamma_of(D), P, kSelectSetOnly, w.probes.p, st));
         }
         probes = w.probes.p;
     } else if (profile) {
@@ -2121,7 +2121,7 @@ const float* Engine::stage_queries(const Index& ix, const float* dQ, int64_t m, 
 }
 
 void Engine::select_probes_device(int index_id, const float* dQ, int64_t nq, int nprobe,
-                                  int32_t* d_out, cudaStream_t ext) {
+                                  int32_t* d_out, cudaStream_t ext, bool set_only) {
     auto ix = get(index_id, "select_probes_device");
     DeviceGuard g(device_);
     std::shared_lock lk(ix->mu);
@@ -2148,7 +2148,8 @@ void Engine::select_probes_device(int index_id, const float* dQ, int64_t nq, int
             M3G_CK(launch_select_probes(ws_.S.p, L, q, ix->dpad, ix->C.p, ix->dpad, ws_.qn.p,
                                         ws_.qn2.p, ix->cn.p, ix->cn2.p, (int)m, L, ix->dim,
                                         ix->metric, ix->normalized ? 1 : 0, beta,
-                                        gamma_of(ix->dim), P, 0, out, st));
+                                        gamma_of(ix->dim), P, set_only ? kSelectSetOnly : 0, out,
+                                        st));
         }
     }
     M3G_CK(cudaEventRecord(ws_.done, st));

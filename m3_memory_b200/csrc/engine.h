@@ -237,9 +237,11 @@ class Engine {
     // Device-pointer pieces of a list-sharded search whose coarse step is sharded
     // too: the selection over this index's centroids, the exact scores of given
     // (query, centroid) pairs, and a search over caller-given probes (-1: none).
-    // Enqueued on ext_stream (null: the engine's stream, waited for).
+    // Enqueued on ext_stream (null: the engine's stream, waited for).  set_only:
+    // each row holds the selected set in no particular order (cheaper: only the
+    // centroids near the P-th place are rescored).
     void select_probes_device(int index_id, const float* dQ, int64_t nq, int nprobe,
-                              int32_t* d_out, cudaStream_t ext_stream);
+                              int32_t* d_out, cudaStream_t ext_stream, bool set_only = false);
     void probe_scores_device(int index_id, const float* dQ, int64_t nq, const int32_t* d_probes,
                              int P, float* d_scores, cudaStream_t ext_stream);
     void search_probes_device(int index_id, const float* dQ, int64_t nq, int k,

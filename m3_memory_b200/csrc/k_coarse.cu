@@ -261,7 +261,7 @@ template <int NT>
 struct SelShared {
     unsigned hist[256];
     unsigned mins[NT / 32];
-    unsigned prefix, remain, count, count2, m_less, tie_need, tkey, nex, wtot[NT / 32];
+    unsigned prefix, remain, count, count2, m_less, tie_need, tkey, nex, nin, wtot[NT / 32];
 };
 
 // Finds the rank-th smallest (1-based) of the keys produced by key_of(c),
@@ -381,13 +381,16 @@ __device__ void bitonic_sort_u64(unsigned long long* a, int n) {
 // One block per query.  S holds the approximate inner products (overwritten
 // with exact scores on the fallback path).  Writes P cluster ids per query into
 // probes (ascending by exact score when P <= 1024, else in ascending id order),
-// or -1 for the nearest-cluster form (P == 1, nan_is_none) when every score is NaN.
+// or -1 for the nearest-cluster form (P == 1, kSelectNanIsNone) when every score
+// is NaN.  With kSelectSetOnly the row holds the same set of ids in an order of
+// the kernel's choosing (deterministic), and only the candidates whose
+// membership the intervals leave open are rescored exactly.
 template <int NT, int CAP, int MINB>
 __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
     float* __restrict__ S, int64_t lds, const float* __restrict__ Q, int64_t ldq,
     const float* __restrict__ C, int64_t ldc, const float* __restrict__ qn,
     const float* __restrict__ qn2, const float* __restrict__ cn, const float* __restrict__ cn2,
-    int L, int D, int metric, int normalized, float beta, float gamma, int P, int nan_is_none,
+    int L, int D, int metric, int normalized, float beta, float gamma, int P, int flags,
     int32_t* __restrict__ probes) {
     extern __shared__ __align__(16) unsigned char sel_smem[];
     __shared__ SelShared<NT> sh;
@@ -404,13 +407,18 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
     float* stage_all = reinterpret_cast<float*>(hkeys);
     const bool cache = L <= SEL_KEYS_SMEM;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool nan_is_none = (flags & kSelectNanIsNone) != 0;
+    const bool set_only = (flags & kSelectSetOnly) != 0;
 
     const float* qrow = Q + (int64_t)q * ldq;
     for (int i = threadIdx.x; i < D; i += NT) qs[i] = qrow[i];
     float* srow = S + (int64_t)q * lds;
     const float nq = qn[q], nq2 = qn2[q];
     const bool nrm = normalized != 0;
-    if (threadIdx.x == 0) sh.nex = 0;  // read after later barriers on every path
+    if (threadIdx.x == 0) {  // read after later barriers on every path
+        sh.nex = 0;
+        sh.nin = 0;
+    }
 
     auto bounds = [&](int c, float* lo, float* hi) {
         approx_bounds(srow[c], nq, cn[c], nq2, cn2[c], beta, gamma, metric, nrm, lo, hi);
@@ -630,7 +638,50 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         // other candidate's is ordered, against all others (their exact scores
         // included), by its lower bound; the rest are rescored in the reference's
         // exact arithmetic.  Keys: (score key, id), all distinct.
-        if (cnt <= (unsigned)SEL_OVERLAP_MAX) {
+        //
+        // Set mode needs only membership.  Candidate i is in for certain when
+        // fewer than PP others can precede it (lower bound <= its upper bound):
+        // then its upper bound is <= T, so no non-candidate (lower bound > T) can.
+        // It is out for certain when PP others precede it for certain (upper
+        // bound < its lower bound).  Only the rest are rescored (needf 1; 0 in,
+        // 2 out), and the in-for-certain ones are ordered by their lower bounds.
+        constexpr int PER = CAP / NT;  // candidates per thread in the pairwise loops
+        static_assert(CAP % NT == 0, "whole candidates per thread");
+        const bool set_mode = set_only && !nan_is_none;
+        if (set_mode) {
+            uint2 bi[PER];
+            unsigned maybe_before[PER], surely_before[PER];
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                const int i = threadIdx.x + u * NT;
+                bi[u] = i < (int)cnt ? ik[i] : make_uint2(0u, 0u);
+                maybe_before[u] = 0;
+                surely_before[u] = 0;
+            }
+            for (int j = 0; j < (int)cnt; ++j) {
+                const uint2 bj = ik[j];
+#pragma unroll
+                for (int u = 0; u < PER; ++u) {
+                    maybe_before[u] += bj.x <= bi[u].y ? 1u : 0u;
+                    surely_before[u] += bj.y < bi[u].x ? 1u : 0u;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                const int i = threadIdx.x + u * NT;
+                if (i >= (int)cnt) continue;
+                // the loop counted the candidate against itself too
+                const unsigned mb = maybe_before[u] - (bi[u].x <= bi[u].y ? 1u : 0u);
+                const unsigned sb = surely_before[u] - (bi[u].y < bi[u].x ? 1u : 0u);
+                unsigned char st = 1;
+                if (bi[u].x > kKeyNegInf && bi[u].y < kKeyPosInf) {
+                    if (mb < (unsigned)PP) st = 0;
+                    else if (sb >= (unsigned)PP) st = 2;
+                }
+                if (st == 0) atomicAdd(&sh.nin, 1u);
+                needf[i] = st;
+            }
+        } else if (cnt <= (unsigned)SEL_OVERLAP_MAX) {
             // few candidates: every pair of intervals compared
             for (int i = threadIdx.x; i < (int)cnt; i += NT) {
                 const uint2 bi = ik[i];
@@ -659,7 +710,6 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
                 hmax[p] = ik[(uint32_t)(srt[p] & 0xffffffffu)].y;
             __syncthreads();
             // inclusive running maximum of the upper bounds (Hillis-Steele)
-            constexpr int PER = CAP / NT;
             for (int d = 1; d < (int)cnt; d <<= 1) {
                 uint32_t v[PER];
 #pragma unroll
@@ -688,12 +738,12 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         __syncthreads();
         for (int i = threadIdx.x; i < (int)cnt; i += NT) {
             const unsigned c = (unsigned)cand[i];
-            cand[i] = needf[i] ? (unsigned long long)c : ((unsigned long long)ik[i].x << 32) | c;
+            cand[i] = needf[i] == 1 ? (unsigned long long)c : ((unsigned long long)ik[i].x << 32) | c;
         }
         __syncthreads();
         // compact the candidates to rescore (exl reuses the interval array)
         for (int i = threadIdx.x; i < (int)cnt; i += NT)
-            if (needf[i]) exl[atomicAdd(&sh.nex, 1u)] = i;
+            if (needf[i] == 1) exl[atomicAdd(&sh.nex, 1u)] = i;
         __syncthreads();
         const int nex = (int)sh.nex;
         float* stage = stage_all + warp * SEL_STAGE;
@@ -717,6 +767,35 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
             if (idx >= 0) cand[idx] = ((unsigned long long)float_key(r) << 32) | (unsigned)c;
         }
         __syncthreads();
+        if (set_mode) {
+            // positions: the nin in-for-certain ids by (lower-bound key, id), then
+            // the best PP - nin rescored ones by (exact key, id)
+            const unsigned nin = sh.nin;
+            unsigned long long kk[PER];
+            unsigned char st[PER];
+            unsigned r[PER];
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                const int i = threadIdx.x + u * NT;
+                st[u] = i < (int)cnt ? needf[i] : 2;
+                kk[u] = i < (int)cnt ? cand[i] : 0ull;
+                r[u] = 0;
+            }
+            for (int j = 0; j < (int)cnt; ++j) {
+                const unsigned char sj = needf[j];
+                const unsigned long long kj = cand[j];
+#pragma unroll
+                for (int u = 0; u < PER; ++u) r[u] += (sj == st[u] && kj < kk[u]) ? 1u : 0u;
+            }
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                if (st[u] == 2) continue;
+                const unsigned pos = st[u] == 0 ? r[u] : nin + r[u];
+                if (pos < (unsigned)PP)
+                    probes[(int64_t)q * P + pos] = (int32_t)(kk[u] & 0xffffffffu);
+            }
+            return;
+        }
         if (cnt <= (unsigned)NT) {
             // output position = rank among the candidates (cnt >= PP)
             if (threadIdx.x < cnt) {
@@ -882,7 +961,7 @@ cudaError_t launch_probe_scores(const float* Q, int64_t ldq, const float* C, int
 cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t ldq, const float* C,
                                  int64_t ldc, const float* qn, const float* qn2, const float* cn,
                                  const float* cn2, int nq, int L, int D, int metric,
-                                 int normalized, float beta, float gamma, int P, int nan_is_none,
+                                 int normalized, float beta, float gamma, int P, int flags,
                                  int32_t* probes, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
     auto run = [&](auto kernel, int nt, size_t smem) {
@@ -890,7 +969,7 @@ cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t 
                                              (int)smem);
         if (e != cudaSuccess) return e;
         kernel<<<nq, nt, smem, st>>>(S, lds, Q, ldq, C, ldc, qn, qn2, cn, cn2, L, D, metric,
-                                     normalized, beta, gamma, P, nan_is_none, probes);
+                                     normalized, beta, gamma, P, flags, probes);
         return cudaGetLastError();
     };
     if ((P < L ? P : L) <= SEL_SMALL_P)

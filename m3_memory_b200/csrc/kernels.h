@@ -22,10 +22,13 @@ void launch_gemv_nt(const float* A, int64_t lda, const float* B, int64_t ldb, fl
                     int64_t lds, int M, int N, int K, int num_sms, cudaStream_t st);
 size_t select_smem_bytes(int L, int D);
 int select_max_dim();
+// flags of launch_select_probes
+constexpr int kSelectNanIsNone = 1;  // P == 1: -1 where every score is NaN
+constexpr int kSelectSetOnly = 2;    // each row holds the top-P set in no particular order
 cudaError_t launch_select_probes(float* S, int64_t lds, const float* Q, int64_t ldq, const float* C,
                                  int64_t ldc, const float* qn, const float* qn2, const float* cn,
                                  const float* cn2, int nq, int L, int D, int metric,
-                                 int normalized, float beta, float gamma, int P, int nan_is_none,
+                                 int normalized, float beta, float gamma, int P, int flags,
                                  int32_t* probes, cudaStream_t st);
 
 // ---- coarse GEMM on the tensor cores (k_gemm_tc.cu) ----

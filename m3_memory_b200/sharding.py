@@ -16,8 +16,9 @@ reads the gathered records in place (``m3g_merge_shards_packed_device``).
 
 With ``split_coarse=True`` the coarse step is split by query instead of being
 repeated: rank r selects the probes of its slice of the batch (queries
-r * ceil(Q / world) ..) over all centroids (``m3g_select_probes_device``, the
-same exact selection), the ``[Q, P]`` probe lists are all-gathered (Q * P * 4
+r * ceil(Q / world) ..) over all centroids (``m3g_select_probe_sets_device``: the
+same exact selection, each row's order left to the engine), the ``[Q, P]`` probe
+lists are all-gathered (Q * P * 4
 bytes), and every rank scans its own lists for the whole batch
 (``m3g_search_probes_device``; lists it does not own hold no rows here) before
 the top-k exchange above.  The coarse work per rank then shrinks with the
@@ -343,7 +344,8 @@ class ShardedSearch:
         gather = PendingCollective(dist.all_gather_into_tensor, self.timeout_s,
                                    "batch exchange", q_all, q, group=self.group)
         loc = o["loc"].view(-1)[:B * P].view(B, P)
-        self.engine.select_probes_device(self.index_id, q.data_ptr(), B, P, loc.data_ptr(), s)
+        self.engine.select_probe_sets_device(self.index_id, q.data_ptr(), B, P, loc.data_ptr(),
+                                             s)
         self._mark("coarse")
         gather.finish()
         self._mark("query_exchange")
@@ -385,8 +387,8 @@ class ShardedSearch:
         loc = self.sp_loc.view(-1)[:chunk * P].view(chunk, P)
         if nloc > 0:
             row = q.stride(0) * q.element_size()
-            self.engine.select_probes_device(self.index_id, q.data_ptr() + q0 * row, nloc, P,
-                                             loc.data_ptr(), s)
+            self.engine.select_probe_sets_device(self.index_id, q.data_ptr() + q0 * row, nloc,
+                                                 P, loc.data_ptr(), s)
         if nloc < chunk:
             loc[nloc:].fill_(-1)
         self._mark("coarse")

@@ -9,7 +9,8 @@ mixture (close scores: most candidates are rescored), more centroids than the
 shared-memory key caches hold (L = 9000), and near-duplicate centroids whose
 intervals all overlap (S0 and the candidate list overflow into the exact
 fallback), and centroids stored twice each, whose intervals overlap in pairs
-among more than 128 candidates (the sorted overlap test)."""
+among more than 128 candidates (the sorted overlap test).  The same cases run
+through the set form of the selection (membership only)."""
 import numpy as np
 import pytest
 
@@ -71,6 +72,38 @@ def test_select_matches_oracle(cuda_ok, oracle_mod, name):
                 np.testing.assert_array_equal(got[q], np.sort(got[q]))
             else:
                 np.testing.assert_array_equal(got[q], want, err_msg=f"{name} P={p} q={q}")
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_probe_sets_match_oracle(cuda_ok, oracle_mod, name):
+    """m3g_select_probe_sets_device (the form the search's scan consumes: only
+    the centroids near the P-th place are rescored) returns, per query, exactly
+    the oracle's selected set, without repeats, and the same rows on a second
+    call.  Batches of 1 and 5 take the GEMV coarse step, the full batch the GEMM."""
+    import torch
+
+    from m3_memory_b200 import cabi
+
+    O = oracle_mod
+    metric, normalized, C, Q = make_case(name)
+    e = cabi.Engine()
+    e.create_ivf(1, C.shape[1], metric, normalized, C)
+    for p in CASES[name][5]:
+        pp = min(p, len(C))
+        want = [np.sort(O.select_nprobe(Q[q], C, metric, normalized, p)) for q in range(len(Q))]
+        for nq in sorted({1, 5, len(Q)}):
+            dq = torch.from_numpy(np.ascontiguousarray(Q[:nq])).cuda()
+            out = torch.full((nq, pp), -7, dtype=torch.int32, device="cuda")
+            e.select_probe_sets_device(1, dq.data_ptr(), nq, p, out.data_ptr())
+            torch.cuda.synchronize()
+            got = out.cpu().numpy()
+            again = torch.full_like(out, -7)
+            e.select_probe_sets_device(1, dq.data_ptr(), nq, p, again.data_ptr())
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(again.cpu().numpy(), got, err_msg=f"{name} P={p}")
+            for q in range(nq):
+                np.testing.assert_array_equal(np.sort(got[q]), want[q],
+                                              err_msg=f"{name} P={p} nq={nq} q={q}")
 
 
 @pytest.mark.parametrize("metric,normalized,d", [(1, False, 256), (0, False, 1024),
