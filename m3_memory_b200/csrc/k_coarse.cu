@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -649,38 +650,46 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         static_assert(CAP % NT == 0, "whole candidates per thread");
         const bool set_mode = set_only && !nan_is_none;
         if (set_mode) {
-            uint2 bi[PER];
-            unsigned maybe_before[PER], surely_before[PER];
+            // PX candidates per thread (1 when they fit one per thread: the warps
+            // past the last candidate then skip the loop)
+            auto classify = [&](auto px) {
+                constexpr int PX = decltype(px)::value;
+                if ((int)threadIdx.x >= (int)cnt) return;
+                uint2 bi[PX];
+                unsigned maybe_before[PX], surely_before[PX];
 #pragma unroll
-            for (int u = 0; u < PER; ++u) {
-                const int i = threadIdx.x + u * NT;
-                bi[u] = i < (int)cnt ? ik[i] : make_uint2(0u, 0u);
-                maybe_before[u] = 0;
-                surely_before[u] = 0;
-            }
-            for (int j = 0; j < (int)cnt; ++j) {
-                const uint2 bj = ik[j];
-#pragma unroll
-                for (int u = 0; u < PER; ++u) {
-                    maybe_before[u] += bj.x <= bi[u].y ? 1u : 0u;
-                    surely_before[u] += bj.y < bi[u].x ? 1u : 0u;
+                for (int u = 0; u < PX; ++u) {
+                    const int i = threadIdx.x + u * NT;
+                    bi[u] = i < (int)cnt ? ik[i] : make_uint2(0u, 0u);
+                    maybe_before[u] = 0;
+                    surely_before[u] = 0;
                 }
-            }
+                for (int j = 0; j < (int)cnt; ++j) {
+                    const uint2 bj = ik[j];
 #pragma unroll
-            for (int u = 0; u < PER; ++u) {
-                const int i = threadIdx.x + u * NT;
-                if (i >= (int)cnt) continue;
-                // the loop counted the candidate against itself too
-                const unsigned mb = maybe_before[u] - (bi[u].x <= bi[u].y ? 1u : 0u);
-                const unsigned sb = surely_before[u] - (bi[u].y < bi[u].x ? 1u : 0u);
-                unsigned char st = 1;
-                if (bi[u].x > kKeyNegInf && bi[u].y < kKeyPosInf) {
-                    if (mb < (unsigned)PP) st = 0;
-                    else if (sb >= (unsigned)PP) st = 2;
+                    for (int u = 0; u < PX; ++u) {
+                        maybe_before[u] += bj.x <= bi[u].y ? 1u : 0u;
+                        surely_before[u] += bj.y < bi[u].x ? 1u : 0u;
+                    }
                 }
-                if (st == 0) atomicAdd(&sh.nin, 1u);
-                needf[i] = st;
-            }
+#pragma unroll
+                for (int u = 0; u < PX; ++u) {
+                    const int i = threadIdx.x + u * NT;
+                    if (i >= (int)cnt) continue;
+                    // the loop counted the candidate against itself too
+                    const unsigned mb = maybe_before[u] - (bi[u].x <= bi[u].y ? 1u : 0u);
+                    const unsigned sb = surely_before[u] - (bi[u].y < bi[u].x ? 1u : 0u);
+                    unsigned char st = 1;
+                    if (bi[u].x > kKeyNegInf && bi[u].y < kKeyPosInf) {
+                        if (mb < (unsigned)PP) st = 0;
+                        else if (sb >= (unsigned)PP) st = 2;
+                    }
+                    if (st == 0) atomicAdd(&sh.nin, 1u);
+                    needf[i] = st;
+                }
+            };
+            if (cnt <= (unsigned)NT) classify(std::integral_constant<int, 1>{});
+            else classify(std::integral_constant<int, PER>{});
         } else if (cnt <= (unsigned)SEL_OVERLAP_MAX) {
             // few candidates: every pair of intervals compared
             for (int i = threadIdx.x; i < (int)cnt; i += NT) {
@@ -748,11 +757,15 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
         const int nex = (int)sh.nex;
         float* stage = stage_all + warp * SEL_STAGE;
         for (int r0 = 0; r0 < nex; r0 += NT) {
-            // up to NT candidates per round, G = ceil(n / NW) per warp: with the blocks
-            // of a batch resident in one wave the kernel's time is a block's latency,
-            // which the shortest per-warp share (and the widest chunks) keeps lowest
+            // up to NT candidates per round, G per warp.  With the blocks of a batch
+            // resident in one wave the kernel's time is a block's latency, which
+            // the shortest per-warp share and the widest chunks keep lowest; a
+            // warp's time is set by its chunk width, not by how many of its lanes
+            // hold candidates, so a warp takes up to 8 (the widest chunks) before
+            // the next takes any, and the idle warps leave the SM's issue slots to
+            // the blocks beside it.  More than 8 per warp: ceil(n / NW) each.
             const int n = nex - r0 < NT ? nex - r0 : NT;
-            const int G = (n + NW - 1) / NW;
+            const int G = min(n, max(8, (n + NW - 1) / NW));
             if (warp * G >= n) continue;  // warp-uniform: nothing for this warp
             const int i = warp * G + lane;
             const int idx = (lane < G && i < n) ? exl[r0 + i] : -1;
@@ -771,29 +784,35 @@ __global__ void __launch_bounds__(NT, MINB) select_probes_kernel(
             // positions: the nin in-for-certain ids by (lower-bound key, id), then
             // the best PP - nin rescored ones by (exact key, id)
             const unsigned nin = sh.nin;
-            unsigned long long kk[PER];
-            unsigned char st[PER];
-            unsigned r[PER];
+            auto place = [&](auto px) {
+                constexpr int PX = decltype(px)::value;
+                if ((int)threadIdx.x >= (int)cnt) return;
+                unsigned long long kk[PX];
+                unsigned char st[PX];
+                unsigned r[PX];
 #pragma unroll
-            for (int u = 0; u < PER; ++u) {
-                const int i = threadIdx.x + u * NT;
-                st[u] = i < (int)cnt ? needf[i] : 2;
-                kk[u] = i < (int)cnt ? cand[i] : 0ull;
-                r[u] = 0;
-            }
-            for (int j = 0; j < (int)cnt; ++j) {
-                const unsigned char sj = needf[j];
-                const unsigned long long kj = cand[j];
+                for (int u = 0; u < PX; ++u) {
+                    const int i = threadIdx.x + u * NT;
+                    st[u] = i < (int)cnt ? needf[i] : 2;
+                    kk[u] = i < (int)cnt ? cand[i] : 0ull;
+                    r[u] = 0;
+                }
+                for (int j = 0; j < (int)cnt; ++j) {
+                    const unsigned char sj = needf[j];
+                    const unsigned long long kj = cand[j];
 #pragma unroll
-                for (int u = 0; u < PER; ++u) r[u] += (sj == st[u] && kj < kk[u]) ? 1u : 0u;
-            }
+                    for (int u = 0; u < PX; ++u) r[u] += (sj == st[u] && kj < kk[u]) ? 1u : 0u;
+                }
 #pragma unroll
-            for (int u = 0; u < PER; ++u) {
-                if (st[u] == 2) continue;
-                const unsigned pos = st[u] == 0 ? r[u] : nin + r[u];
-                if (pos < (unsigned)PP)
-                    probes[(int64_t)q * P + pos] = (int32_t)(kk[u] & 0xffffffffu);
-            }
+                for (int u = 0; u < PX; ++u) {
+                    if (st[u] == 2) continue;
+                    const unsigned pos = st[u] == 0 ? r[u] : nin + r[u];
+                    if (pos < (unsigned)PP)
+                        probes[(int64_t)q * P + pos] = (int32_t)(kk[u] & 0xffffffffu);
+                }
+            };
+            if (cnt <= (unsigned)NT) place(std::integral_constant<int, 1>{});
+            else place(std::integral_constant<int, PER>{});
             return;
         }
         if (cnt <= (unsigned)NT) {
