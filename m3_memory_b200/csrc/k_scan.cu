@@ -1070,6 +1070,96 @@ __global__ void __launch_bounds__(MRG_BLOCK) merge_topk_kernel(
     }
     if (threadIdx.x == 0) out_counts[q] = kk;
 }
+
+// The same merge, one warp per query, for k <= 32 and at most 32 MWL candidates
+// per query (the batch shapes of the searches: P k = 320 at P = 32, k = 10):
+// the same cut at tau and the same (score, slot, j) order, with the candidates
+// in registers and the k winners taken by k rounds of a warp minimum instead of
+// a block-wide sort; the winners' ids are then fetched by k lanes at once.
+constexpr int MWL = 16;        // candidates per lane
+constexpr int MW_WARPS = 8;    // queries per block
+
+__global__ void __launch_bounds__(MW_WARPS * 32) merge_topk_warp_kernel(
+    const float* __restrict__ part_score, const int64_t* __restrict__ part_row,
+    const int64_t* __restrict__ row_ids, int nq, int P, int k, int64_t stride_q,
+    int64_t stride_slot, int64_t rstride_q, int64_t rstride_slot, int64_t* __restrict__ out_ids,
+    float* __restrict__ out_scores, int32_t* __restrict__ out_counts) {
+    __shared__ uint32_t sel[MW_WARPS][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * MW_WARPS + warp;
+    if (q >= nq) return;  // warp-uniform
+    const int n = P * k;  // <= 32 MWL (checked by the launcher)
+    const float* ps = part_score + (int64_t)q * stride_q;
+    const int64_t* pr = part_row + (int64_t)q * rstride_q;
+    const float INF = __int_as_float(0x7f800000);
+    float tau = INF;
+    for (int sl = lane; sl < P; sl += 32) {
+        const float last = ps[(int64_t)sl * stride_slot + k - 1];
+        if (score_valid(last)) tau = fminf(tau, last);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tau = fminf(tau, __shfl_xor_sync(0xffffffffu, tau, o));
+    unsigned long long key[MWL];
+    unsigned nvalid = 0;
+#pragma unroll
+    for (int u = 0; u < MWL; ++u) {
+        const int i = lane + 32 * u;
+        key[u] = ~0ull;
+        if (i < n) {
+            const float sv = ps[(int64_t)(i / k) * stride_slot + (i % k)];
+            if (score_valid(sv)) {
+                ++nvalid;
+                if (sv <= tau) key[u] = ((unsigned long long)float_key(sv) << 32) | (uint32_t)i;
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) nvalid += __shfl_xor_sync(0xffffffffu, nvalid, o);
+    int kk = (int)((unsigned)k < nvalid ? (unsigned)k : nvalid);
+    // k rounds: the warp's smallest key leaves its lane (keys are distinct).  At
+    // least kk candidates are <= tau (a full list's k entries are); should the
+    // lists break that, the answer stops at the candidates there are
+    unsigned long long m = ~0ull;
+#pragma unroll
+    for (int u = 0; u < MWL; ++u) m = key[u] < m ? key[u] : m;
+    for (int r = 0; r < kk; ++r) {
+        unsigned long long w = m;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, w, o);
+            w = t < w ? t : w;
+        }
+        if (w == ~0ull) {  // warp-uniform
+            kk = r;
+            break;
+        }
+        if (m == w) {
+            sel[warp][r] = (uint32_t)(w & 0xffffffffu);
+            m = ~0ull;
+#pragma unroll
+            for (int u = 0; u < MWL; ++u) {
+                if (key[u] == w) key[u] = ~0ull;
+                m = key[u] < m ? key[u] : m;
+            }
+        }
+    }
+    __syncwarp();
+    if (lane < k) {
+        int64_t id = -1;
+        float sv = INF;
+        if (lane < kk) {
+            const int i = (int)sel[warp][lane];
+            sv = ps[(int64_t)(i / k) * stride_slot + (i % k)];
+            const int64_t row = pr[(int64_t)(i / k) * rstride_slot + (i % k)];
+            id = row_ids ? row_ids[row] : row;
+        }
+        out_ids[(int64_t)q * k + lane] = id;
+        out_scores[(int64_t)q * k + lane] = sv;
+    }
+    if (lane == 0) out_counts[q] = kk;
+}
+
+bool merge_fits_warp(int P, int k) { return k >= 1 && k <= 32 && (int64_t)P * k <= 32 * MWL; }
 }  // namespace
 
 namespace {
@@ -1208,6 +1298,12 @@ cudaError_t launch_merge_topk(const float* part_score, const int64_t* part_row,
                               const MergeRescore* rs) {
     if (nq <= 0) return cudaSuccess;
     if (rs && (k > RS_MAX || !row_ids)) return cudaErrorInvalidValue;
+    if (!rs && merge_fits_warp(P, k)) {
+        merge_topk_warp_kernel<<<(nq + MW_WARPS - 1) / MW_WARPS, MW_WARPS * 32, 0, st>>>(
+            part_score, part_row, row_ids, nq, P, k, (int64_t)P * k, k, (int64_t)P * k, k,
+            out_ids, out_scores, out_counts);
+        return cudaGetLastError();
+    }
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(part_score, part_row, row_ids, P, k,
                                                 (int64_t)P * k, k, (int64_t)P * k, k, out_ids,
                                                 out_scores, out_counts, rs ? 1 : 0);
@@ -1243,6 +1339,12 @@ cudaError_t launch_merge_shards(const float* scores, const int64_t* ids, int nsh
                                 int64_t* out_ids, float* out_scores, int32_t* out_counts,
                                 cudaStream_t st) {
     if (nq <= 0 || k <= 0) return cudaSuccess;
+    if (merge_fits_warp(nshard, k)) {
+        merge_topk_warp_kernel<<<(nq + MW_WARPS - 1) / MW_WARPS, MW_WARPS * 32, 0, st>>>(
+            scores, ids, nullptr, nq, nshard, k, k, (int64_t)nq * k, k, (int64_t)nq * k, out_ids,
+            out_scores, out_counts);
+        return cudaGetLastError();
+    }
     merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(scores, ids, nullptr, nshard, k, k,
                                                 (int64_t)nq * k, k, (int64_t)nq * k, out_ids,
                                                 out_scores, out_counts, 0);
@@ -1256,10 +1358,16 @@ cudaError_t launch_merge_shards_packed(const unsigned char* packed, int nshard, 
     if (shard_bytes % 8 || ids_offset % 8 || (reinterpret_cast<uintptr_t>(packed) & 7) ||
         ids_offset < (int64_t)nq * k * 4 || shard_bytes < ids_offset + (int64_t)nq * k * 8)
         return cudaErrorInvalidValue;
-    merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(
-        reinterpret_cast<const float*>(packed), reinterpret_cast<const int64_t*>(packed + ids_offset),
-        nullptr, nshard, k, k, shard_bytes / 4, k, shard_bytes / 8, out_ids, out_scores, out_counts,
-        0);
+    const float* sc = reinterpret_cast<const float*>(packed);
+    const int64_t* ids = reinterpret_cast<const int64_t*>(packed + ids_offset);
+    if (merge_fits_warp(nshard, k)) {
+        merge_topk_warp_kernel<<<(nq + MW_WARPS - 1) / MW_WARPS, MW_WARPS * 32, 0, st>>>(
+            sc, ids, nullptr, nq, nshard, k, k, shard_bytes / 4, k, shard_bytes / 8, out_ids,
+            out_scores, out_counts);
+        return cudaGetLastError();
+    }
+    merge_topk_kernel<<<nq, MRG_BLOCK, 0, st>>>(sc, ids, nullptr, nshard, k, k, shard_bytes / 4, k,
+                                                shard_bytes / 8, out_ids, out_scores, out_counts, 0);
     return cudaGetLastError();
 }
 
