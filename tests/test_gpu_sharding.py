@@ -29,7 +29,10 @@ def _merge_device(cabi, torch, sc, ids):
     return o_ids.cpu().numpy(), o_sc.cpu().numpy(), o_cnt.cpu().numpy()
 
 
-@pytest.mark.parametrize("ns,nq,k", [(2, 50, 10), (8, 33, 7), (3, 5, 1), (4, 9, 64)])
+# (16, 20, 32): 512 candidates per query, the most the warp-per-query merge takes;
+# (17, 20, 32) and k = 64 take the block merge
+@pytest.mark.parametrize("ns,nq,k", [(2, 50, 10), (8, 33, 7), (3, 5, 1), (4, 9, 64),
+                                     (16, 20, 32), (17, 20, 32)])
 def test_merge_kernel_matches_rule(cuda_ok, oracle_mod, ns, nq, k):
     import torch
 
