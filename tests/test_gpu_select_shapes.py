@@ -24,6 +24,9 @@ CASES = {
     "cos_norm_wide": (2, True, 9000, 64, 24, (1, 16, 64, 128, 500)),
     "ip_near_duplicates": (1, False, 600, 128, 16, (1, 8, 64, 128, 400)),
     "l2_duplicate_pairs": (0, False, 1000, 64, 16, (129, 200, 256, 700)),
+    # centroid norms from 0.14 to 7.4: the first pass's uniform norm bound (the
+    # largest norm) is far wider than most centroids' own
+    "ip_varied_norms": (1, False, 2048, 256, 32, (1, 8, 32, 128, 256)),
 }
 
 
@@ -46,6 +49,8 @@ def make_case(name):
         means = rng.standard_normal((16, d)).astype(np.float32)
         C = (means[rng.integers(0, 16, L)] + 0.3 * rng.standard_normal((L, d))).astype(np.float32)
         Q = (means[rng.integers(0, 16, nq)] + 0.3 * rng.standard_normal((nq, d))).astype(np.float32)
+    if name == "ip_varied_norms":
+        C *= np.exp(rng.uniform(-2.0, 2.0, (L, 1))).astype(np.float32)
     if normalized:
         C /= np.linalg.norm(C, axis=1, keepdims=True)
         Q /= np.linalg.norm(Q, axis=1, keepdims=True)
@@ -164,3 +169,47 @@ def test_tiny_batches_over_many_centroids(cuda_ok, oracle_mod, metric, normalize
             for q in range(nq):
                 want = O.select_nprobe(Q[q], C, metric, normalized, p)
                 np.testing.assert_array_equal(got[q], want, err_msg=f"nq={nq} P={p} q={q}")
+
+
+@pytest.mark.parametrize("metric,normalized", [(1, False), (2, True)])
+def test_select_after_centroid_updates(cuda_ok, oracle_mod, metric, normalized):
+    """The selection's uniform norm bound follows set_centroid and add_cluster:
+    a centroid moved far out (the new largest norm), one shrunk, and a new
+    cluster, then both selection forms against the oracle on the updated
+    centroids (for normalised cosine the new rows are unit vectors)."""
+    import torch
+
+    from m3_memory_b200 import cabi
+
+    O = oracle_mod
+    rng = np.random.default_rng(7 + metric)
+    L, d, nq, P = 600, 128, 24, 16
+    means = rng.standard_normal((8, d)).astype(np.float32)
+    C = (means[rng.integers(0, 8, L)] + 0.3 * rng.standard_normal((L, d))).astype(np.float32)
+    Q = (means[rng.integers(0, 8, nq)] + 0.3 * rng.standard_normal((nq, d))).astype(np.float32)
+    if normalized:
+        C /= np.linalg.norm(C, axis=1, keepdims=True)
+        Q /= np.linalg.norm(Q, axis=1, keepdims=True)
+    e = cabi.Engine()
+    e.create_ivf(1, d, metric, normalized, C)
+    e.select_probes(1, Q, P)
+    big = (Q[0] * (1.0 if normalized else 9.0)).astype(np.float32)
+    small = (C[5] * (1.0 if normalized else 0.05)).astype(np.float32)
+    extra = (Q[3] + 0.01 * rng.standard_normal(d)).astype(np.float32)
+    if normalized:
+        extra /= np.linalg.norm(extra)
+    e.set_centroid(1, 17, big)
+    e.set_centroid(1, 5, small)
+    e.add_cluster(1, extra)
+    C2 = np.concatenate([C, extra[None]]).astype(np.float32)
+    C2[17], C2[5] = big, small
+    got = e.select_probes(1, Q, P)
+    dq = torch.from_numpy(np.ascontiguousarray(Q)).cuda()
+    out = torch.full((nq, P), -7, dtype=torch.int32, device="cuda")
+    e.select_probe_sets_device(1, dq.data_ptr(), nq, P, out.data_ptr())
+    torch.cuda.synchronize()
+    sets = out.cpu().numpy()
+    for q in range(nq):
+        want = O.select_nprobe(Q[q], C2, metric, normalized, P)
+        np.testing.assert_array_equal(got[q], want, err_msg=f"q={q}")
+        np.testing.assert_array_equal(np.sort(sets[q]), np.sort(want), err_msg=f"set q={q}")
