@@ -511,6 +511,7 @@ def run_ours(args, rank, world, local_rank):
     h_cnt = torch.empty((BATCH,), dtype=torch.int32).pin_memory()
     scan_ms, scan_bytes, launches = [], [], 0
     stage_ms = {}
+    stage_by_rank = None  # N > 1: every rank's phase means
     if world == 1:
         lib = cabi.lib()
 
@@ -647,6 +648,13 @@ def run_ours(args, rank, world, local_rank):
             for (_, ea), (name, eb) in zip(m, m[1:]):
                 stage_ms.setdefault("ms_" + name, []).append(ea.elapsed_time(eb))
             stage_ms.setdefault("ms_total", []).append(m[0][1].elapsed_time(m[-1][1]))
+        # every rank's phase means, gathered (the slowest rank's scan sets the step)
+        names = sorted(stage_ms)
+        mine = torch.tensor([statistics.mean(stage_ms[k]) for k in names], device=dev)
+        every = torch.empty((world, len(names)), device=dev)
+        dist.all_gather_into_tensor(every, mine)
+        stage_by_rank = {k[3:]: [round(float(x), 4) for x in every[:, j].tolist()]
+                         for j, k in enumerate(names)}
     e2e_qps = per_step * args.steps / e2e_s
     e2e_sync_qps = per_step * args.steps / e2e_sync_s
 
@@ -700,6 +708,7 @@ def run_ours(args, rank, world, local_rank):
         "recall_at_10": recall,
         "recall_sweep": {str(k): v for k, v in sweep.items()},
         "stage_ms_mean": {k[3:]: round(statistics.mean(v), 4) for k, v in stage_ms.items()},
+        "stage_ms_by_rank": stage_by_rank,
         "parallelism": ("1 GPU" if world == 1 else
                         f"lists sharded over {world} GPUs; every GPU brings its own batch of "
                         f"{BATCH} queries per step (batches all-gathered, probes of each batch "
